@@ -1,0 +1,341 @@
+"""Benchmark of the MoE FFN hot path (vireo moe_ffn) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+Workloads (synthetic, seeded):
+  cfg1_moe_decode   config 1: OLMoE-1B-7B-shaped MoE layer, Q8_0 experts,
+                    64 experts top-8, batch-1 decode (default)
+  qwen3_moe_decode  the MoE layer of config 3: Qwen3-30B-A3B-shaped, Q4_K
+                    gate/up, Q6_K down, 128 experts top-8 renormalised
+
+A step is T decode tokens, each one batch-1 pass of a token through an MoE
+layer (router -> top-k -> gate/up/SwiGLU -> down -> combine).  Tokens rotate
+over NL device copies of the layer so the same weights are not re-read out
+of L2 between tokens (reuse distance NL x bytes/token > 126 MB L2).
+
+Decode does not shard (batch 1): with --gpus N every rank runs its own
+replica ("replicas only", weak scaling); value = all ranks' tokens / max
+rank time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from vireo_b200 import synth as S  # noqa: E402
+
+WORKLOADS = {
+    "cfg1_moe_decode": dict(spec=S.olmoe_q8_layer, seed=1234, config=1,
+                            desc="OLMoE-1B-7B-shaped MoE layer, Q8_0, 64 experts top-8, batch-1 decode"),
+    "qwen3_moe_decode": dict(spec=S.qwen3_layer, seed=1234, config=3,
+                             desc="Qwen3-30B-A3B-shaped MoE layer, Q4_K gate/up + Q6_K down, 128 experts "
+                                  "top-8 renorm, batch-1 decode"),
+}
+L2_BYTES = 126 * 1024 * 1024
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def traffic_per_launch(workload):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu
+    summary, if one exists for this workload."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f).get(workload)
+    except Exception:
+        return None
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, index):
+        self.index, self.proc, self.path = index, None, f"/tmp/vireo_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait()
+            self.f.close()
+
+    def summary(self):
+        try:
+            rows = [l.split(",") for l in open(self.path).read().strip().splitlines()]
+        except Exception:
+            return None
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [c.strip() for c in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_reference_rate(layer, toks, seconds, threads, warm=4):
+    """The reference's own moe_ffn (compiled from its sources, oracle/_ref)
+    on this host: tokens/s over a bounded sample of about ``seconds``."""
+    from oracle import oracle as O
+    O.build(ref=False)
+    kind = "reference" if O.ref_available() else "port"
+    impl = O.RefMoe(layer) if kind == "reference" else O.PortMoe(layer)
+    if kind == "reference":
+        O.ref().ref_set_threads(threads)
+    else:
+        O.port().orc_set_threads(threads)
+    impl(toks[:warm])  # first touches load every expert the sample needs
+    n, t0 = 0, time.perf_counter()
+    while True:
+        i = n % len(toks)
+        impl(toks[i:i + 1])
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds and n >= 8:
+            break
+    if kind == "reference":
+        impl.close()
+    return n / el, n, el, kind
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_reference(args, spec_w):
+    """--impl reference: the reference CPU path on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    spec = spec_w["spec"]()
+    layer = S.MoeLayer(spec, spec_w["seed"])
+    toks, _ = S.routed_tokens(layer, 256, spec_w["seed"])
+    th = host_threads()
+    from oracle import oracle as O
+    O.build(ref=False)
+    kind = "reference" if O.ref_available() else "port"
+    impl = O.RefMoe(layer) if kind == "reference" else O.PortMoe(layer)
+    (O.ref().ref_set_threads if kind == "reference" else O.port().orc_set_threads)(th)
+    per_step = 16
+    impl(toks[:8])
+    for i in range(args.warmup):
+        impl(toks[(i * per_step) % 240:(i * per_step) % 240 + per_step])
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        j = (i * per_step) % 240
+        impl(toks[j:j + per_step])
+    el = time.perf_counter() - t0
+    tps = args.steps * per_step / el
+    line = {"metric": "moe_decode_tok_per_s", "value": tps, "unit": "tok/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded GGUF blocks, random-init)",
+            "config": {"workload": args.workload, "desc": spec_w["desc"], "tokens_per_step": per_step},
+            "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": th, "kind": kind,
+                             "sample": f"{args.steps} steps x {per_step} tokens, OMP threads={th}"},
+            "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=40)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="cfg1_moe_decode", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--tokens", type=int, default=1000, help="decode tokens per step")
+    ap.add_argument("--copies", type=int, default=8, help="layer copies rotated per token")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        return run_reference(args, wl)
+
+    import torch
+    import vireo_b200 as V
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    V.check(V.lib().vireo_device_init(local), "vireo_device_init")
+
+    spec = wl["spec"]()
+    layer = S.MoeLayer(spec, wl["seed"])
+    T = args.tokens
+    toks, _ = S.routed_tokens(layer, min(T, 1000), wl["seed"])
+    NL = max(1, args.copies)
+    per_tok = spec.bytes_per_token()
+    assert NL * per_tok > L2_BYTES or NL * spec.expert_bytes * spec.n_experts > 4 * L2_BYTES
+
+    layers = [V.MoeLayer(layer, local)]
+    for _ in range(NL - 1):  # identical bytes at different addresses: no L2 reuse across tokens
+        layers.append(V.MoeLayer(layer, local))
+    dev = torch.device("cuda", local)
+    hb = torch.from_numpy(toks).to(dev)
+    nt = hb.shape[0]
+    x = torch.zeros_like(hb)
+    stream = torch.cuda.Stream(dev)
+    sp = stream.cuda_stream
+
+    ffn = V.lib().gguf_moe_ffn
+    d_bytes = 4 * spec.dim
+    calls = [(layers[i % NL].h, hb.data_ptr() + (i % nt) * d_bytes, x.data_ptr() + (i % nt) * d_bytes, 1,
+              None, None, sp) for i in range(T)]
+
+    def step():
+        for a in calls:
+            if ffn(*a):
+                raise RuntimeError("gguf_moe_ffn failed")
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    for m in layers[:1]:
+        m.sync(sp)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        torch.cuda.synchronize(dev)
+        e0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(args.steps):
+                step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    st = layers[0].sync(sp)
+    t_sec = ms / 1e3
+    if world > 1:
+        tt = torch.tensor([t_sec], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        t_sec = float(tt.item())
+    tokens_all = args.steps * T * world
+    value = tokens_all / t_sec
+    launches = args.steps * T
+
+    # end to end through the host C-ABI call (pinned host buffers, copies in
+    # the timed region), per-token round trips as a decode loop makes them
+    e2e = None
+    n_e2e = min(200, T)
+    hb_h = torch.from_numpy(toks[:n_e2e].copy()).pin_memory()
+    x_h = torch.zeros_like(hb_h).pin_memory()
+    ids_h = torch.zeros((n_e2e, spec.n_used), dtype=torch.int32).pin_memory()
+    w_h = torch.zeros((n_e2e, spec.n_used), dtype=torch.float32).pin_memory()
+    L = V.lib()
+
+    fh = L.gguf_moe_ffn_host
+    hcalls = [(layers[i % NL].h, hb_h[i].data_ptr(), x_h[i].data_ptr(), 1, ids_h[i].data_ptr(),
+               w_h[i].data_ptr()) for i in range(n_e2e)]
+
+    def e2e_step():
+        for a in hcalls:
+            if fh(*a):
+                raise RuntimeError("gguf_moe_ffn_host failed")
+
+    for _ in range(2):
+        e2e_step()
+    t0 = time.perf_counter()
+    e2e_iters = max(3, args.steps // 4)
+    for _ in range(e2e_iters):
+        e2e_step()
+    el = time.perf_counter() - t0
+    e2e_tps = e2e_iters * n_e2e / el
+    if world > 1:
+        tt = torch.tensor([el], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        e2e_tps = e2e_iters * n_e2e * world / float(tt.item())
+    d = spec.dim
+    e2e = {"value": e2e_tps, "unit": "tok/s", "h2d_bytes_per_step": T * 2 * 4 * d,
+           "d2h_bytes_per_step": T * (4 * d + 8 * spec.n_used),
+           "note": "gguf_moe_ffn_host per token, pinned host buffers"}
+
+    peak, peak_kind = peaks()
+    per_launch_s = t_sec / launches if world == 1 else ms / 1e3 / launches
+    achieved = per_tok / per_launch_s / 1e9
+    tr = traffic_per_launch(args.workload)
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": tr, "peak_kind": peak_kind, "algorithmic_bytes_per_launch": per_tok,
+                "kernel": "moe_decode_kernel (one launch per token)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        th = host_threads()
+        rate, n, el, kind = cpu_reference_rate(layer, toks, args.cpu_seconds, th)
+        cpu = {"value": rate, "unit": "tok/s", "cores": th, "kind": kind,
+               "sample": f"{n} tokens of the same workload in {el:.1f} s, OMP threads={th}"}
+
+    if rank == 0:
+        line = {"metric": "moe_decode_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_sec / args.steps * 1e3,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded GGUF blocks, random-init weights)",
+                "config": {"workload": args.workload, "desc": wl["desc"], "baseline_config": wl["config"],
+                           "tokens_per_step": T, "batch": 1, "parallelism": f"replicas x{world}",
+                           "l2": f"{NL} layer copies rotated per token (reuse distance "
+                                 f"{NL * per_tok / 2**20:.0f} MiB > 126 MiB L2)",
+                           "bytes_per_token": per_tok},
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
+                "clocks": clk.summary(), "hbm_gbs": achieved}
+        print(json.dumps(line), flush=True)
+    for m in layers:
+        m.close()
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,72 @@
+/* vireo-b200: the MoE FFN block on B200 (sm_100a).
+ *
+ * The reference computes the MoE FFN in moe_ffn (vireo src/gguf_run.c:185-214),
+ * a static function inside its model runner: router matvec (:187), softmax
+ * (:181-182), greedy top-k with ties to the lowest expert id (:190-191),
+ * optional renormalisation (:192), and per selected expert gate/up matvec,
+ * SwiGLU and down matvec with a rank-ordered weighted combine (:198-213),
+ * adding the result into the residual x.  This header exports that block
+ * as a C-ABI call so a host model loop can replace the body of moe_ffn with
+ * one gguf_moe_ffn call per layer.
+ *
+ * One decode token runs as one persistent cooperative kernel: router,
+ * top-k, gate/up + SwiGLU and down + combine, with the expert weights
+ * streamed raw (GGUF blocks, no repacking) from HBM. */
+#ifndef VIREO_GGUF_MOE_H
+#define VIREO_GGUF_MOE_H
+#include <stdint.h>
+
+#include "gguf.h"
+#include "vireo_status.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* One MoE layer.  Mirrors the reference Model/Layer fields moe_ffn reads:
+ * dim, ffn_exp, n_experts, n_used, topk_renorm (src/gguf_run.c:154) and the
+ * tensors ffn_gate_inp / ffn_{gate,up,down}_exps (src/gguf_run.c:312-315).
+ * All pointers are DEVICE pointers.  The expert tensors are the 3-D GGUF
+ * tensors with the expert index outermost: expert e of gate_exps starts at
+ * gate_exps + e * (gate_nbytes / n_experts), as gguf_run.c:326-331 slices
+ * them. */
+typedef struct {
+    int dim, ffn_exp, n_experts, n_used, topk_renorm;
+    uint32_t router_type, gate_type, up_type, down_type;
+    const void *router;
+    const void *gate_exps, *up_exps, *down_exps;
+    uint64_t gate_nbytes, up_nbytes, down_nbytes;
+} gguf_moe_desc;
+
+typedef struct gguf_moe gguf_moe;
+
+/* Validates the layer, picks the kernel and allocates its device scratch.
+ * Fast path: router F32; gate/up (same type) and down in Q8_0/Q4_K/Q6_K;
+ * dim % 512 == 0; ffn_exp % 256 == 0; n_experts <= 256; n_used <= 64. */
+int gguf_moe_create(const gguf_moe_desc *desc, gguf_moe **out);
+
+/* n_tok independent tokens through the layer, one after another (decode).
+ * hb: [n_tok][dim] normalised hidden; x: [n_tok][dim] residual, updated in
+ * place (x += MoE(hb)); ids / wts: [n_tok][n_used] selected experts in rank
+ * order and their gate weights, or NULL.  Device pointers, stream-ordered,
+ * no host synchronisation; device-side failures surface in gguf_moe_sync. */
+int gguf_moe_ffn(gguf_moe *m, const float *hb, float *x, int n_tok, int32_t *ids, float *wts, void *stream);
+
+/* Same with HOST buffers: copies in, runs, copies out, synchronises. */
+int gguf_moe_ffn_host(gguf_moe *m, const float *hb, float *x, int n_tok, int32_t *ids, float *wts);
+
+/* Waits for the layer's work on stream and returns its device status. */
+int gguf_moe_sync(gguf_moe *m, void *stream);
+
+/* Point expert e's gate/up/down weights at arbitrary device addresses
+ * (arrays of n_experts pointers; a NULL array keeps the current pointers).
+ * Used when an ExpertStore owns the expert slabs. */
+int gguf_moe_set_expert_ptrs(gguf_moe *m, const void *const *gate, const void *const *up,
+                             const void *const *down);
+
+void gguf_moe_destroy(gguf_moe *m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

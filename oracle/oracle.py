@@ -1,0 +1,207 @@
+"""ctypes access to the parity checkers (test infrastructure only).
+
+* ``port()``  — oracle/_build/liboracle.so, the CPU restatement in
+  vireo_oracle.c (each function there cites the reference file:line).
+* ``ref()``   — oracle/_ref/libvireo_ref.so, the reference's own sources
+  compiled from the reference tree plus ref_harness.c (absent if the
+  reference was never available to build it).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU legs may use this
+module; the product library never loads either file.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PORT_SO = os.path.join(HERE, "_build", "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libvireo_ref.so")
+
+_f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
+
+
+def build(ref: bool = True) -> None:
+    """Compile the checkers (the reference library only when its sources exist)."""
+    targets = ["port"] + (["ref"] if ref else [])
+    subprocess.run(["make", "-s", "-C", HERE] + targets, check=True,
+                   env={**os.environ, "OCC": os.environ.get("ORACLE_CC", "gcc")})
+
+
+class OrcMoeLayer(C.Structure):
+    _fields_ = [("dim", C.c_int), ("ffn_exp", C.c_int), ("n_experts", C.c_int),
+                ("n_used", C.c_int), ("topk_renorm", C.c_int),
+                ("router_type", C.c_uint32), ("gate_type", C.c_uint32),
+                ("up_type", C.c_uint32), ("down_type", C.c_uint32),
+                ("router", C.c_void_p), ("gate", C.c_void_p), ("up", C.c_void_p),
+                ("down", C.c_void_p),
+                ("gate_nbytes", C.c_uint64), ("up_nbytes", C.c_uint64),
+                ("down_nbytes", C.c_uint64)]
+
+
+class ExpertStats(C.Structure):
+    """Mirror of ExpertStats (reference src/expert_store.h:22-25)."""
+    _fields_ = [(n, C.c_uint64) for n in ("requests", "hits", "misses", "bytes_read",
+                                          "resident_bytes", "capacity_bytes",
+                                          "experts_resident")]
+
+
+_port = None
+_ref = None
+
+
+def port():
+    global _port
+    if _port is None:
+        if not os.path.exists(PORT_SO):
+            build(ref=False)
+        lib = C.CDLL(PORT_SO)
+        lib.orc_f16_to_f32.argtypes = [C.c_uint16]
+        lib.orc_f16_to_f32.restype = C.c_float
+        lib.orc_dequant_row.argtypes = [C.c_uint32, _u8p, _f32p, C.c_int]
+        lib.orc_dequant_row.restype = C.c_int
+        lib.orc_matmul.argtypes = [_f32p, _f32p, C.c_uint32, _u8p, C.c_int, C.c_int]
+        lib.orc_matmul.restype = C.c_int
+        lib.orc_moe_ffn.argtypes = [C.POINTER(OrcMoeLayer), _f32p, _f32p, _i32p, _f32p, C.c_void_p]
+        lib.orc_moe_ffn.restype = C.c_int
+        lib.orc_moe_ffn_batch.argtypes = [C.POINTER(OrcMoeLayer), C.c_int, _f32p, _f32p, _i32p, _f32p]
+        lib.orc_moe_ffn_batch.restype = C.c_int
+        lib.orc_set_threads.argtypes = [C.c_int]
+        lib.orc_max_threads.restype = C.c_int
+        _port = lib
+    return _port
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_SO)
+
+
+def ref():
+    global _ref
+    if _ref is None:
+        if not os.path.exists(REF_SO):
+            raise FileNotFoundError(REF_SO + " (reference library not built)")
+        lib = C.CDLL(REF_SO)
+        lib.gguf_f16_to_f32.argtypes = [C.c_uint16]
+        lib.gguf_f16_to_f32.restype = C.c_float
+        lib.gguf_dequant_row.argtypes = [C.c_uint32, _u8p, _f32p, C.c_int]
+        lib.gguf_dequant_row.restype = None
+        lib.ref_matmul.argtypes = [_f32p, _f32p, C.c_uint32, _u8p, C.c_int, C.c_int]
+        lib.ref_matmul.restype = None
+        lib.ref_moe_create.argtypes = [C.c_int] * 5 + [C.c_uint32, C.c_void_p, C.c_uint64] * 4 + [C.c_uint64]
+        lib.ref_moe_create.restype = C.c_void_p
+        lib.ref_moe_ffn.argtypes = [C.c_void_p, _f32p, _f32p, _i32p, _f32p]
+        lib.ref_moe_ffn.restype = C.c_int
+        lib.ref_moe_ffn_batch.argtypes = [C.c_void_p, C.c_int, _f32p, _f32p, _i32p, _f32p]
+        lib.ref_moe_ffn_batch.restype = C.c_int
+        lib.ref_moe_stats.argtypes = [C.c_void_p, C.POINTER(ExpertStats)]
+        lib.ref_moe_destroy.argtypes = [C.c_void_p]
+        lib.ref_set_threads.argtypes = [C.c_int]
+        lib.ref_max_threads.restype = C.c_int
+        _ref = lib
+    return _ref
+
+
+# ---------------------------------------------------------------------------
+# convenience wrappers over numpy arrays
+# ---------------------------------------------------------------------------
+
+def _u8(a) -> np.ndarray:
+    return np.ascontiguousarray(a).view(np.uint8).reshape(-1)
+
+
+def dequant_row(ggml_type: int, src, n: int, lib=None) -> np.ndarray:
+    lib = lib or port()
+    out = np.zeros(n, dtype=np.float32)
+    if lib is _ref:
+        lib.gguf_dequant_row(ggml_type, _u8(src), out, n)
+    else:
+        lib.orc_dequant_row(ggml_type, _u8(src), out, n)
+    return out
+
+
+def matmul(ggml_type: int, w, x, n: int, d: int, lib=None) -> np.ndarray:
+    lib = lib or port()
+    y = np.zeros(d, dtype=np.float32)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    if lib is _ref:
+        lib.ref_matmul(y, x, ggml_type, _u8(w), n, d)
+    else:
+        lib.orc_matmul(y, x, ggml_type, _u8(w), n, d)
+    return y
+
+
+class PortMoe:
+    """The restated moe_ffn over a synth.MoeLayer (arrays kept alive here)."""
+
+    def __init__(self, layer):
+        s = layer.spec
+        self.layer = layer
+        self._keep = [_u8(layer.router), _u8(layer.gate), _u8(layer.up), _u8(layer.down)]
+        self.desc = OrcMoeLayer(s.dim, s.ffn_exp, s.n_experts, s.n_used, s.topk_renorm,
+                                s.router_type, s.gate_type, s.up_type, s.down_type,
+                                self._keep[0].ctypes.data, self._keep[1].ctypes.data,
+                                self._keep[2].ctypes.data, self._keep[3].ctypes.data,
+                                self._keep[1].nbytes, self._keep[2].nbytes, self._keep[3].nbytes)
+
+    def __call__(self, hb, x=None):
+        """Returns (x_out, ids, wts) for a batch of independent tokens."""
+        s = self.layer.spec
+        hb = np.ascontiguousarray(hb, dtype=np.float32).reshape(-1, s.dim)
+        n = hb.shape[0]
+        x = np.zeros_like(hb) if x is None else np.array(x, dtype=np.float32).reshape(n, s.dim)
+        k = min(s.n_used, 64)
+        ids = np.zeros((n, k), dtype=np.int32)
+        wts = np.zeros((n, k), dtype=np.float32)
+        port().orc_moe_ffn_batch(C.byref(self.desc), n, hb.reshape(-1), x.reshape(-1),
+                                 ids.reshape(-1), wts.reshape(-1))
+        return x, ids, wts
+
+
+class RefMoe:
+    """The reference's own moe_ffn (through ref_harness.c) over a synth.MoeLayer."""
+
+    def __init__(self, layer, cap_bytes: int = 0):
+        s = layer.spec
+        self.layer = layer
+        self._keep = [_u8(layer.router), _u8(layer.gate), _u8(layer.up), _u8(layer.down)]
+        r = self._keep
+        self.h = ref().ref_moe_create(s.dim, s.ffn_exp, s.n_experts, s.n_used, s.topk_renorm,
+                                      s.router_type, r[0].ctypes.data, r[0].nbytes,
+                                      s.gate_type, r[1].ctypes.data, r[1].nbytes,
+                                      s.up_type, r[2].ctypes.data, r[2].nbytes,
+                                      s.down_type, r[3].ctypes.data, r[3].nbytes, cap_bytes)
+        if not self.h:
+            raise RuntimeError("ref_moe_create failed")
+
+    def __call__(self, hb, x=None):
+        s = self.layer.spec
+        hb = np.ascontiguousarray(hb, dtype=np.float32).reshape(-1, s.dim)
+        n = hb.shape[0]
+        x = np.zeros_like(hb) if x is None else np.array(x, dtype=np.float32).reshape(n, s.dim)
+        k = min(s.n_used, 64)
+        ids = np.zeros((n, k), dtype=np.int32)
+        wts = np.zeros((n, k), dtype=np.float32)
+        ref().ref_moe_ffn_batch(self.h, n, hb.reshape(-1), x.reshape(-1), ids.reshape(-1), wts.reshape(-1))
+        return x, ids, wts
+
+    def stats(self) -> ExpertStats:
+        st = ExpertStats()
+        ref().ref_moe_stats(self.h, C.byref(st))
+        return st
+
+    def close(self):
+        if self.h:
+            ref().ref_moe_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

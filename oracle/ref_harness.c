@@ -1,0 +1,176 @@
+/* ref_harness.c — drives the reference's own CPU MoE path.
+ *
+ * TEST INFRASTRUCTURE ONLY (checker and CPU baseline; never product code).
+ * Compiled by oracle/Makefile together with the reference's unmodified
+ * sources (src/gguf.c, src/gguf_compute.c, src/expert_store.c and the KV
+ * sources gguf_run.c links against) into oracle/_ref/libvireo_ref.so.
+ *
+ * The reference's MoE block, moe_ffn (src/gguf_run.c:185-214), is a static
+ * function, so this file includes src/gguf_run.c with its main() renamed and
+ * calls moe_ffn directly on a Model whose MoE fields are filled here.  The
+ * expert weights are written to an anonymous file and registered with the
+ * reference ExpertStore exactly as gguf_run.c:325-331 does (expert e of each
+ * 3-D tensor at base + e * (nbytes / n_experts)), so every lookup, pread and
+ * eviction is the reference's own.  expert_store_lookup is routed through a
+ * recording hook (same signature, forwards to the real function) so the
+ * selected expert ids can be read back in rank order.
+ */
+#define _GNU_SOURCE
+#define main vireo_gguf_main
+#define expert_store_lookup ref_hook_lookup
+#include "gguf_run.c"
+#undef expert_store_lookup
+#undef main
+
+#include <sys/mman.h>
+#include <unistd.h>
+
+int expert_store_lookup(ExpertStore *s, int layer, int expert, ExpertView *view);
+
+static int g_rec_ids[64];
+static int g_rec_n;
+
+int ref_hook_lookup(ExpertStore *s, int layer, int expert, ExpertView *view) {
+    if (g_rec_n < 64) g_rec_ids[g_rec_n] = expert;
+    g_rec_n++;
+    return expert_store_lookup(s, layer, expert, view);
+}
+
+typedef struct {
+    Model m;
+    gguf_ctx g;
+    Layer ly;
+    gguf_tensor router, gate, up, down;
+    int fd;
+    void *anchor;
+} RefMoe;
+
+void ref_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
+int ref_max_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
+
+static int write_all(int fd, const void *p, uint64_t n, uint64_t off) {
+    const uint8_t *b = (const uint8_t *)p;
+    while (n) {
+        ssize_t w = pwrite(fd, b, n > (1u << 30) ? (1u << 30) : n, (off_t)off);
+        if (w <= 0) return -1;
+        b += w; n -= (uint64_t)w; off += (uint64_t)w;
+    }
+    return 0;
+}
+
+/* One MoE layer (layer index 0) with the given tensors.  cap_bytes is the
+ * ExpertStore budget (0 = unbounded), as VIREO_EXPERT_CAP_MB sets it. */
+RefMoe *ref_moe_create(int dim, int ffn_exp, int n_experts, int n_used, int renorm,
+                       uint32_t router_type, const void *router, uint64_t router_nbytes,
+                       uint32_t gate_type, const void *gate, uint64_t gate_nbytes,
+                       uint32_t up_type, const void *up, uint64_t up_nbytes,
+                       uint32_t down_type, const void *down, uint64_t down_nbytes,
+                       uint64_t cap_bytes) {
+    RefMoe *r = (RefMoe *)calloc(1, sizeof(RefMoe));
+    if (!r) return NULL;
+    r->fd = memfd_create("vireo_ref_experts", 0);
+    if (r->fd < 0) { free(r); return NULL; }
+    uint64_t off_g = 0, off_u = gate_nbytes, off_d = gate_nbytes + up_nbytes;
+    if (write_all(r->fd, gate, gate_nbytes, off_g) || write_all(r->fd, up, up_nbytes, off_u) ||
+        write_all(r->fd, down, down_nbytes, off_d)) {
+        close(r->fd); free(r); return NULL;
+    }
+    /* tensors: data pointers only feed the (unused) base-offset arithmetic in
+     * moe_ffn; expert bytes come from the ExpertStore. */
+    r->anchor = malloc(16);
+    r->g.map = r->anchor;
+    r->router.data = router; r->router.ggml_type = router_type; r->router.nbytes = router_nbytes;
+    r->gate.data = r->anchor; r->gate.ggml_type = gate_type; r->gate.nbytes = gate_nbytes;
+    r->up.data = r->anchor; r->up.ggml_type = up_type; r->up.nbytes = up_nbytes;
+    r->down.data = r->anchor; r->down.ggml_type = down_type; r->down.nbytes = down_nbytes;
+    r->ly.router = &r->router; r->ly.gate_exps = &r->gate; r->ly.up_exps = &r->up; r->ly.down_exps = &r->down;
+    Model *m = &r->m;
+    m->g = &r->g;
+    m->L = &r->ly;
+    m->n_layers = 1;
+    m->dim = dim; m->ffn_exp = ffn_exp; m->n_experts = n_experts; m->n_used = n_used;
+    m->topk_renorm = renorm; m->is_moe = 1; m->exp_type = gate_type;
+    m->rlog = (float *)malloc(sizeof(float) * (size_t)n_experts);
+    m->gbuf = (float *)malloc(sizeof(float) * (size_t)ffn_exp);
+    m->ubuf = (float *)malloc(sizeof(float) * (size_t)ffn_exp);
+    m->dbuf = (float *)malloc(sizeof(float) * (size_t)dim);
+    m->moe_acc = (float *)malloc(sizeof(float) * (size_t)dim);
+    m->es = expert_store_create(r->fd, cap_bytes, 1, n_experts);
+    uint32_t gs = (uint32_t)(gate_nbytes / (uint64_t)n_experts);
+    uint32_t us = (uint32_t)(up_nbytes / (uint64_t)n_experts);
+    uint32_t ds = (uint32_t)(down_nbytes / (uint64_t)n_experts);
+    for (int e = 0; e < n_experts; e++) {
+        ExpertSlices sl = {off_g + (uint64_t)e * gs, off_u + (uint64_t)e * us, off_d + (uint64_t)e * ds,
+                           gs, us, ds};
+        expert_store_register(m->es, 0, e, &sl);
+    }
+    return r;
+}
+
+/* Runs the reference moe_ffn for one token.  hb: normalised hidden [dim]
+ * (not modified by the reference); x: residual [dim] in/out.  ids/wts get
+ * the experts the reference looked up, in rank order, and their gate
+ * weights (softmax probabilities, renormalised as moe_ffn does when
+ * topk_renorm is set).  Returns the number of experts looked up. */
+int ref_moe_ffn(RefMoe *r, const float *hb, float *x, int32_t *ids, float *wts) {
+    Model *m = &r->m;
+    float *hcopy = (float *)malloc(sizeof(float) * (size_t)m->dim);
+    memcpy(hcopy, hb, sizeof(float) * (size_t)m->dim);
+    m->x = x;
+    g_rec_n = 0;
+    moe_ffn(m, 0, hcopy);
+    free(hcopy);
+    int n = g_rec_n < 64 ? g_rec_n : 64;
+    if (ids) for (int t = 0; t < n; t++) ids[t] = g_rec_ids[t];
+    if (wts) {
+        /* after moe_ffn, m->rlog holds the softmax probabilities */
+        float ws = 0.0f;
+        for (int t = 0; t < n; t++) { wts[t] = m->rlog[g_rec_ids[t]]; ws = ws + wts[t]; }
+        if (m->topk_renorm && ws > 0) for (int t = 0; t < n; t++) wts[t] = wts[t] / ws;
+    }
+    return n;
+}
+
+/* n_tok independent tokens through the layer, one moe_ffn call each. */
+int ref_moe_ffn_batch(RefMoe *r, int n_tok, const float *hb, float *x, int32_t *ids, float *wts) {
+    int k = r->m.n_used < 64 ? r->m.n_used : 64;
+    for (int t = 0; t < n_tok; t++)
+        ref_moe_ffn(r, hb + (size_t)t * r->m.dim, x + (size_t)t * r->m.dim,
+                    ids ? ids + (size_t)t * k : NULL, wts ? wts + (size_t)t * k : NULL);
+    return k;
+}
+
+void ref_moe_stats(RefMoe *r, ExpertStats *st) { expert_store_stats(r->m.es, st); }
+
+void ref_moe_destroy(RefMoe *r) {
+    if (!r) return;
+    Model *m = &r->m;
+    expert_store_destroy(m->es);
+    free(m->rlog); free(m->gbuf); free(m->ubuf); free(m->dbuf); free(m->moe_acc);
+    free(r->anchor);
+    close(r->fd);
+    free(r);
+}
+
+/* gguf_matmul on a bare tensor (type + data), as moe_ffn builds them
+ * (gguf_run.c:202-204). */
+void ref_matmul(float *y, const float *x, uint32_t type, const void *data, int n, int d) {
+    gguf_tensor t;
+    memset(&t, 0, sizeof(t));
+    t.data = data;
+    t.ggml_type = type;
+    gguf_matmul(y, x, &t, n, d);
+}

@@ -1,0 +1,207 @@
+"""vireo-b200: vireo's MoE FFN hot path, B200-native (sm_100a).
+
+The product is the C-ABI shared library ``libvireo_b200.so`` built from
+``csrc/`` (headers in ``include/``).  This package loads it with ctypes and
+mirrors the reference interface for Python callers:
+
+* ``gguf_matmul`` / ``gguf_dequant_row`` / ``gguf_f16_to_f32`` — the three
+  functions of the reference's gguf_compute.h (vireo src/gguf_compute.h:8-10);
+* ``MoeLayer`` — the MoE FFN block (reference moe_ffn, src/gguf_run.c:185-214)
+  behind ``gguf_moe_*``.
+
+There is no fallback: if the library is missing or no CUDA device is
+present, calls raise.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libvireo_b200.so")
+
+VIREO_OK = 0
+STATUS = {0: "ok", -1: "invalid argument", -2: "CUDA runtime error", -3: "unsupported tensor type or shape",
+          -4: "device wait timed out", -5: "out of memory", -6: "I/O error", -7: "no CUDA device"}
+
+
+class VireoError(RuntimeError):
+    def __init__(self, status: int, what: str = ""):
+        super().__init__(f"{what}: {STATUS.get(status, status)} ({status})")
+        self.status = status
+
+
+def build(jobs: int = 8) -> str:
+    """Compile libvireo_b200.so for sm_100a (nvcc cross-compiles without a GPU)."""
+    subprocess.run(["make", "-s", "-C", HERE, f"-j{jobs}"], check=True)
+    return LIB_PATH
+
+
+class GgufTensor(C.Structure):
+    """gguf_tensor (reference src/gguf.h:36-45), ABI-identical."""
+    _fields_ = [("name_ptr", C.c_char_p), ("name_len", C.c_uint64), ("n_dims", C.c_uint32),
+                ("dims", C.c_uint64 * 4), ("ggml_type", C.c_uint32), ("offset", C.c_uint64),
+                ("data", C.c_void_p), ("n_elems", C.c_uint64), ("nbytes", C.c_uint64)]
+
+
+class GgufMoeDesc(C.Structure):
+    _fields_ = [("dim", C.c_int), ("ffn_exp", C.c_int), ("n_experts", C.c_int), ("n_used", C.c_int),
+                ("topk_renorm", C.c_int), ("router_type", C.c_uint32), ("gate_type", C.c_uint32),
+                ("up_type", C.c_uint32), ("down_type", C.c_uint32), ("router", C.c_void_p),
+                ("gate_exps", C.c_void_p), ("up_exps", C.c_void_p), ("down_exps", C.c_void_p),
+                ("gate_nbytes", C.c_uint64), ("up_nbytes", C.c_uint64), ("down_nbytes", C.c_uint64)]
+
+
+_lib = None
+
+
+def lib():
+    """The loaded C-ABI library (raises if it was never built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(f"{LIB_PATH} is missing: run vireo_b200.build() (no CPU fallback exists)")
+        L = C.CDLL(LIB_PATH)
+        L.gguf_f16_to_f32.argtypes = [C.c_uint16]
+        L.gguf_f16_to_f32.restype = C.c_float
+        L.gguf_dequant_row.argtypes = [C.c_uint32, C.c_void_p, C.c_void_p, C.c_int]
+        L.gguf_dequant_row.restype = None
+        L.gguf_matmul.argtypes = [C.c_void_p, C.c_void_p, C.POINTER(GgufTensor), C.c_int, C.c_int]
+        L.gguf_matmul.restype = None
+        L.vireo_last_error.restype = C.c_int
+        L.vireo_status_string.argtypes = [C.c_int]
+        L.vireo_status_string.restype = C.c_char_p
+        L.vireo_device_init.argtypes = [C.c_int]
+        L.gguf_matmul_dev.argtypes = [C.c_void_p, C.c_void_p, C.POINTER(GgufTensor), C.c_int, C.c_int, C.c_void_p]
+        L.gguf_dequant_row_dev.argtypes = [C.c_uint32, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]
+        L.gguf_weights_register.argtypes = [C.c_void_p, C.c_uint64]
+        L.gguf_weights_unregister.argtypes = [C.c_void_p]
+        L.vireo_sync.argtypes = [C.c_void_p]
+        L.gguf_moe_create.argtypes = [C.POINTER(GgufMoeDesc), C.POINTER(C.c_void_p)]
+        L.gguf_moe_ffn.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]
+        L.gguf_moe_ffn_host.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
+        L.gguf_moe_sync.argtypes = [C.c_void_p, C.c_void_p]
+        L.gguf_moe_set_expert_ptrs.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
+        L.gguf_moe_destroy.argtypes = [C.c_void_p]
+        L.gguf_moe_destroy.restype = None
+        _lib = L
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    if status != VIREO_OK:
+        raise VireoError(status, what)
+
+
+def _ptr(a) -> int:
+    """Address of a numpy array or torch tensor."""
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data
+    return a.data_ptr()
+
+
+# ---------------------------------------------------------------------------
+# gguf_compute.h mirror
+# ---------------------------------------------------------------------------
+
+def gguf_f16_to_f32(h: int) -> float:
+    return lib().gguf_f16_to_f32(h)
+
+
+def gguf_dequant_row(ggml_type: int, src, n: int, out=None):
+    """Reference gguf_dequant_row; src/out numpy (host) or torch CUDA tensors."""
+    if out is None:
+        out = np.zeros(n, dtype=np.float32)
+    lib().gguf_dequant_row(ggml_type, _ptr(src), _ptr(out), n)
+    check(lib().vireo_last_error(), "gguf_dequant_row")
+    return out
+
+
+def make_tensor(ggml_type: int, data) -> GgufTensor:
+    t = GgufTensor()
+    t.ggml_type = ggml_type
+    t.data = _ptr(data)
+    return t
+
+
+def gguf_matmul(ggml_type: int, w, x, n: int, d: int, y=None):
+    """Reference gguf_matmul: y[d] = W[d x n] . x[n] (host or device buffers)."""
+    if y is None:
+        y = np.zeros(d, dtype=np.float32)
+    t = make_tensor(ggml_type, w)
+    lib().gguf_matmul(_ptr(y), _ptr(x), C.byref(t), n, d)
+    check(lib().vireo_last_error(), "gguf_matmul")
+    return y
+
+
+def gguf_matmul_dev(ggml_type: int, w, x, n: int, d: int, y, stream=None) -> None:
+    t = make_tensor(ggml_type, w)
+    check(lib().gguf_matmul_dev(_ptr(y), _ptr(x), C.byref(t), n, d, stream), "gguf_matmul_dev")
+
+
+def sync(stream=None) -> None:
+    check(lib().vireo_sync(stream), "vireo_sync")
+
+
+# ---------------------------------------------------------------------------
+# MoE block (gguf_moe.h)
+# ---------------------------------------------------------------------------
+
+class MoeLayer:
+    """One MoE FFN layer resident in HBM, evaluated by gguf_moe_ffn.
+
+    ``layer`` is a ``vireo_b200.synth.MoeLayer`` or any object with ``spec``
+    (dim, ffn_exp, n_experts, n_used, topk_renorm, *_type) and raw GGUF byte
+    arrays ``router``, ``gate``, ``up``, ``down`` (experts outermost).
+    Device memory is held in torch tensors (plumbing only)."""
+
+    def __init__(self, layer, device: int = 0):
+        import torch
+        s = layer.spec
+        self.spec = s
+        self.device = torch.device("cuda", device)
+        up = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.uint8).reshape(-1)).to(self.device)
+        self.router, self.gate, self.up, self.down = up(layer.router), up(layer.gate), up(layer.up), up(layer.down)
+        self.desc = GgufMoeDesc(s.dim, s.ffn_exp, s.n_experts, s.n_used, s.topk_renorm, s.router_type,
+                                s.gate_type, s.up_type, s.down_type, self.router.data_ptr(),
+                                self.gate.data_ptr(), self.up.data_ptr(), self.down.data_ptr(),
+                                self.gate.numel(), self.up.numel(), self.down.numel())
+        h = C.c_void_p()
+        check(lib().gguf_moe_create(C.byref(self.desc), C.byref(h)), "gguf_moe_create")
+        self.h = h
+
+    def ffn(self, hb, x, ids=None, wts=None, stream=None) -> None:
+        """Device tensors: hb/x [n_tok, dim] fp32 (x updated), ids/wts [n_tok, n_used]."""
+        n = hb.shape[0] if hb.dim() > 1 else 1
+        check(lib().gguf_moe_ffn(self.h, hb.data_ptr(), x.data_ptr(), n,
+                                 ids.data_ptr() if ids is not None else None,
+                                 wts.data_ptr() if wts is not None else None, stream), "gguf_moe_ffn")
+
+    def sync(self, stream=None) -> None:
+        check(lib().gguf_moe_sync(self.h, stream), "gguf_moe_sync")
+
+    def ffn_host(self, hb: np.ndarray, x: np.ndarray | None = None):
+        """Host buffers through gguf_moe_ffn_host; returns (x_out, ids, wts)."""
+        s = self.spec
+        hb = np.ascontiguousarray(hb, dtype=np.float32).reshape(-1, s.dim)
+        n = hb.shape[0]
+        x = np.zeros_like(hb) if x is None else np.array(x, dtype=np.float32).reshape(n, s.dim)
+        ids = np.zeros((n, s.n_used), dtype=np.int32)
+        wts = np.zeros((n, s.n_used), dtype=np.float32)
+        check(lib().gguf_moe_ffn_host(self.h, hb.ctypes.data, x.ctypes.data, n, ids.ctypes.data, wts.ctypes.data),
+              "gguf_moe_ffn_host")
+        return x, ids, wts
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            lib().gguf_moe_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,580 @@
+// C-ABI layer: the reference's gguf_compute.h functions, their device
+// variants, and the MoE block (gguf_moe.h).  Host code only; kernels live
+// in decode_kernels.cu / generic_kernels.cu.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <mutex>
+#include <unordered_set>
+#include <vector>
+
+#include "gguf_compute.h"
+#include "gguf_moe.h"
+#include "moe_decode.cuh"
+#include "vireo_internal.h"
+
+namespace vireo {
+
+static thread_local int t_last = VIREO_OK;
+void set_last_error(int code) { t_last = code; }
+int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return VIREO_OK;
+  if (e == cudaErrorMemoryAllocation) return VIREO_ERR_NOMEM;
+  if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) return VIREO_ERR_NODEV;
+  return VIREO_ERR_CUDA;
+}
+
+static std::mutex g_init_mu;
+static Ctx* g_ctx = nullptr;
+static int g_req_device = -1;
+
+Ctx* ctx_get(int* status) {
+  std::lock_guard<std::mutex> lk(g_init_mu);
+  if (g_ctx) {
+    *status = VIREO_OK;
+    return g_ctx;
+  }
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    *status = VIREO_ERR_NODEV;
+    return nullptr;
+  }
+  Ctx* c = new Ctx();
+  int dev = g_req_device;
+  if (dev < 0 && cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+  cudaError_t e = cudaSetDevice(dev);
+  cudaDeviceProp prop;
+  if (e == cudaSuccess) e = cudaGetDeviceProperties(&prop, dev);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaMalloc(&c->d_err, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, sizeof(int));
+  if (e != cudaSuccess) {
+    *status = cuda_status(e);
+    delete c;
+    return nullptr;
+  }
+  c->device = dev;
+  c->num_sms = prop.multiProcessorCount;
+  c->smem_optin = (uint32_t)prop.sharedMemPerBlockOptin;
+  g_ctx = c;
+  *status = VIREO_OK;
+  return c;
+}
+
+void* ctx_scratch(Ctx* c, size_t bytes) {
+  if (bytes <= c->scratch_bytes) return c->scratch;
+  if (c->scratch) cudaFree(c->scratch);
+  c->scratch = nullptr;
+  c->scratch_bytes = 0;
+  size_t want = bytes + bytes / 4;
+  if (cudaMalloc(&c->scratch, want) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  c->scratch_bytes = want;
+  return c->scratch;
+}
+
+static std::mutex g_attr_mu;
+static std::unordered_set<const void*> g_attr_done;
+// dynamic shared memory available to the decode kernels: the opt-in limit
+// minus room for their static shared memory
+static uint32_t dyn_smem_limit(const Ctx* c) { return c->smem_optin - 1024u; }
+
+static int ensure_smem_attr(const Ctx* c, const void* fn) {
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  if (g_attr_done.count(fn)) return VIREO_OK;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn_smem_limit(c));
+  if (e != cudaSuccess) return cuda_status(e);
+  g_attr_done.insert(fn);
+  return VIREO_OK;
+}
+
+int gemv_dev(Ctx* c, uint32_t type, const void* w, const float* x, float* y, int n, int d, cudaStream_t s) {
+  if (n <= 0 || d < 0) return VIREO_ERR_ARG;
+  if (d == 0) return VIREO_OK;
+  if (fast_format(type) && n % kSegElems == 0 && d % 16 == 0 && ((uintptr_t)w % 16) == 0) {
+    GemvParams p;
+    memset(&p, 0, sizeof(p));
+    if (stage_geom(type, n, &p.sg) == VIREO_OK) {
+      p.W = (const uint8_t*)w;
+      p.x = x;
+      p.y = y;
+      p.n = n;
+      p.d = d;
+      p.err = c->d_err;
+      const uint32_t smem = gemv_layout(&p, dyn_smem_limit(c));
+      if (smem) {
+        const void* fn = gemv_kernel_for(type);
+        int st = ensure_smem_attr(c, fn);
+        if (st) return st;
+        int grid = std::min(c->num_sms, d / 16);
+        void* args[] = {&p};
+        return cuda_status(cudaLaunchKernel(fn, dim3(grid), dim3(kDecodeThreads), args, smem, s));
+      }
+    }
+  }
+  return launch_gemv_generic(type, w, x, y, n, d, s);
+}
+
+static bool is_device_ptr(const void* p) {
+  if (!p) return false;
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+static const void* registered_dev(Ctx* c, const void* host, uint64_t bytes) {
+  const uint8_t* h = (const uint8_t*)host;
+  for (auto& r : c->ranges)
+    if (h >= r.host && h + bytes <= r.host + r.bytes) return r.dev + (h - r.host);
+  return nullptr;
+}
+
+static int read_status(Ctx* c, cudaStream_t s) {
+  int st = cuda_status(cudaStreamSynchronize(s));
+  if (st) return st;
+  int herr = 0;
+  st = cuda_status(cudaMemcpy(&herr, c->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (st) return st;
+  if (herr) {
+    cudaMemset(c->d_err, 0, sizeof(int));
+    return herr;
+  }
+  return VIREO_OK;
+}
+
+static size_t up256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+}  // namespace vireo
+
+using namespace vireo;
+
+extern "C" {
+
+int vireo_last_error(void) { return t_last; }
+
+const char* vireo_status_string(int s) {
+  switch (s) {
+    case VIREO_OK: return "ok";
+    case VIREO_ERR_ARG: return "invalid argument";
+    case VIREO_ERR_CUDA: return "CUDA runtime error";
+    case VIREO_ERR_UNSUPPORTED: return "unsupported tensor type or shape";
+    case VIREO_ERR_TIMEOUT: return "device wait timed out";
+    case VIREO_ERR_NOMEM: return "out of memory";
+    case VIREO_ERR_IO: return "I/O error";
+    case VIREO_ERR_NODEV: return "no CUDA device";
+    default: return "unknown status";
+  }
+}
+
+int vireo_device_init(int device) {
+  {
+    std::lock_guard<std::mutex> lk(g_init_mu);
+    if (g_ctx) return g_ctx->device == device ? VIREO_OK : VIREO_ERR_ARG;
+    g_req_device = device;
+  }
+  int st;
+  Ctx* c = ctx_get(&st);
+  return c ? VIREO_OK : st;
+}
+
+float gguf_f16_to_f32(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h >> 15) << 31;
+  const uint32_t e = (h >> 10) & 31u, m = h & 1023u;
+  uint32_t bits;
+  if (e == 31u) {
+    bits = sign | 0x7f800000u | (m << 13);
+  } else if (e == 0u) {
+    float f = (float)m * 0x1p-24f;  // subnormal or zero: exact
+    memcpy(&bits, &f, 4);
+    bits |= sign;
+  } else {
+    bits = sign | ((e + 112u) << 23) | (m << 13);
+  }
+  float f;
+  memcpy(&f, &bits, 4);
+  return f;
+}
+
+int vireo_sync(void* stream) {
+  int st;
+  Ctx* c = ctx_get(&st);
+  if (!c) return st;
+  return read_status(c, stream ? (cudaStream_t)stream : c->stream);
+}
+
+int gguf_matmul_dev(float* y, const float* x, const gguf_tensor* w, int n, int d, void* stream) {
+  int st;
+  Ctx* c = ctx_get(&st);
+  if (!c) return st;
+  if (!w || !y || !x || !w->data) return VIREO_ERR_ARG;
+  return gemv_dev(c, w->ggml_type, w->data, x, y, n, d, stream ? (cudaStream_t)stream : c->stream);
+}
+
+int gguf_dequant_row_dev(uint32_t type, const void* src, float* dst, int n, void* stream) {
+  int st;
+  Ctx* c = ctx_get(&st);
+  if (!c) return st;
+  return launch_dequant(type, src, dst, n, stream ? (cudaStream_t)stream : c->stream);
+}
+
+void gguf_dequant_row(uint32_t type, const void* src, float* dst, int n) {
+  int st;
+  Ctx* c = ctx_get(&st);
+  if (!c) {
+    set_last_error(st);
+    return;
+  }
+  int be, bb;
+  if (type_block(type, &be, &bb) || n < 0 || n % be) {
+    set_last_error(VIREO_ERR_UNSUPPORTED);
+    return;
+  }
+  std::lock_guard<std::mutex> lk(c->mu);
+  const size_t sb = (size_t)row_bytes(type, n), db = (size_t)n * 4;
+  const bool sdev = is_device_ptr(src), ddev = is_device_ptr(dst);
+  const void* s = sdev ? src : registered_dev(c, src, sb);
+  uint8_t* scr = (uint8_t*)ctx_scratch(c, up256(sb) + up256(db));
+  if (!scr) {
+    set_last_error(VIREO_ERR_NOMEM);
+    return;
+  }
+  if (!s) {
+    if ((st = cuda_status(cudaMemcpyAsync(scr, src, sb, cudaMemcpyHostToDevice, c->stream)))) {
+      set_last_error(st);
+      return;
+    }
+    s = scr;
+  }
+  float* dd = ddev ? dst : (float*)(scr + up256(sb));
+  st = launch_dequant(type, s, dd, n, c->stream);
+  if (!st && !ddev) st = cuda_status(cudaMemcpyAsync(dst, dd, db, cudaMemcpyDeviceToHost, c->stream));
+  if (!st) st = read_status(c, c->stream);
+  set_last_error(st);
+}
+
+void gguf_matmul(float* y, const float* x, const gguf_tensor* w, int n, int d) {
+  int st;
+  Ctx* c = ctx_get(&st);
+  if (!c) {
+    set_last_error(st);
+    return;
+  }
+  if (!w || !w->data || !x || !y || n <= 0 || d < 0) {
+    set_last_error(VIREO_ERR_ARG);
+    return;
+  }
+  int be, bb;
+  if (type_block(w->ggml_type, &be, &bb) || n % be) {
+    set_last_error(VIREO_ERR_UNSUPPORTED);
+    return;
+  }
+  std::lock_guard<std::mutex> lk(c->mu);
+  const size_t wb = (size_t)row_bytes(w->ggml_type, n) * (size_t)d, xb = (size_t)n * 4, yb = (size_t)d * 4;
+  const bool wdev = is_device_ptr(w->data), xdev = is_device_ptr(x), ydev = is_device_ptr(y);
+  const void* wd = wdev ? w->data : registered_dev(c, w->data, wb);
+  const size_t need = (wd ? 0 : up256(wb)) + up256(xb) + up256(yb);
+  uint8_t* scr = (uint8_t*)ctx_scratch(c, need);
+  if (!scr) {
+    set_last_error(VIREO_ERR_NOMEM);
+    return;
+  }
+  size_t off = 0;
+  if (!wd) {
+    if ((st = cuda_status(cudaMemcpyAsync(scr, w->data, wb, cudaMemcpyHostToDevice, c->stream)))) {
+      set_last_error(st);
+      return;
+    }
+    wd = scr;
+    off = up256(wb);
+  }
+  const float* xd = x;
+  if (!xdev) {
+    float* xs = (float*)(scr + off);
+    off += up256(xb);
+    if ((st = cuda_status(cudaMemcpyAsync(xs, x, xb, cudaMemcpyHostToDevice, c->stream)))) {
+      set_last_error(st);
+      return;
+    }
+    xd = xs;
+  }
+  float* yd = ydev ? y : (float*)(scr + off);
+  st = gemv_dev(c, w->ggml_type, wd, xd, yd, n, d, c->stream);
+  if (!st && !ydev) st = cuda_status(cudaMemcpyAsync(y, yd, yb, cudaMemcpyDeviceToHost, c->stream));
+  if (!st) st = read_status(c, c->stream);
+  set_last_error(st);
+}
+
+int gguf_weights_register(const void* host, uint64_t nbytes) {
+  int st;
+  Ctx* c = ctx_get(&st);
+  if (!c) return st;
+  if (!host || !nbytes) return VIREO_ERR_ARG;
+  std::lock_guard<std::mutex> lk(c->mu);
+  HostRange r;
+  r.host = (const uint8_t*)host;
+  r.bytes = nbytes;
+  r.dev = nullptr;
+  if ((st = cuda_status(cudaMalloc(&r.dev, nbytes)))) return st;
+  if ((st = cuda_status(cudaMemcpy(r.dev, host, nbytes, cudaMemcpyHostToDevice)))) {
+    cudaFree(r.dev);
+    return st;
+  }
+  c->ranges.push_back(r);
+  return VIREO_OK;
+}
+
+int gguf_weights_unregister(const void* host) {
+  int st;
+  Ctx* c = ctx_get(&st);
+  if (!c) return st;
+  std::lock_guard<std::mutex> lk(c->mu);
+  for (size_t i = 0; i < c->ranges.size(); i++) {
+    if (c->ranges[i].host == host) {
+      cudaStreamSynchronize(c->stream);
+      cudaFree(c->ranges[i].dev);
+      c->ranges.erase(c->ranges.begin() + (long)i);
+      return VIREO_OK;
+    }
+  }
+  return VIREO_ERR_ARG;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// MoE block
+// ---------------------------------------------------------------------------
+struct gguf_moe {
+  gguf_moe_desc desc;
+  MoeDecodeParams prm;
+  const void* kernel = nullptr;
+  uint32_t smem = 0;
+  int grid = 0;
+  const uint8_t** d_exp_tab = nullptr;
+  std::vector<const uint8_t*> h_exp_tab;
+  void* scratch = nullptr;
+  size_t scratch_bytes = 0;
+  float* d_io = nullptr;  // host-API staging: hb, x
+  int32_t* d_ids = nullptr;
+  float* d_wts = nullptr;
+  int io_cap = 0;
+  cudaStream_t stream = nullptr;
+};
+
+static int moe_reset_scratch(gguf_moe* m, cudaStream_t s) {
+  return cuda_status(cudaMemsetAsync(m->scratch, 0, m->scratch_bytes, s));
+}
+
+extern "C" {
+
+int gguf_moe_create(const gguf_moe_desc* desc, gguf_moe** out) {
+  int st;
+  Ctx* c = ctx_get(&st);
+  if (!c) return st;
+  if (!desc || !out) return VIREO_ERR_ARG;
+  *out = nullptr;
+  const gguf_moe_desc& D = *desc;
+  if (D.dim <= 0 || D.ffn_exp <= 0 || D.n_experts <= 0 || D.n_used <= 0 || D.n_used > D.n_experts ||
+      !D.router || !D.gate_exps || !D.up_exps || !D.down_exps)
+    return VIREO_ERR_ARG;
+  if (D.router_type != T_F32 || D.gate_type != D.up_type || !fast_format(D.gate_type) ||
+      !fast_format(D.down_type) || D.dim % kRouterChunk || D.ffn_exp % kSegElems || D.n_experts > 256 ||
+      D.n_used > kMaxTopK)
+    return VIREO_ERR_UNSUPPORTED;
+  const uint64_t gsl = (uint64_t)D.ffn_exp * row_bytes(D.gate_type, D.dim);
+  const uint64_t dsl = (uint64_t)D.dim * row_bytes(D.down_type, D.ffn_exp);
+  if (D.gate_nbytes < gsl * D.n_experts || D.up_nbytes < gsl * D.n_experts || D.down_nbytes < dsl * D.n_experts)
+    return VIREO_ERR_ARG;
+  const uint64_t gstep = D.gate_nbytes / D.n_experts, ustep = D.up_nbytes / D.n_experts,
+                 dstep = D.down_nbytes / D.n_experts;
+  if (((uintptr_t)D.router | (uintptr_t)D.gate_exps | (uintptr_t)D.up_exps | (uintptr_t)D.down_exps) % 16 ||
+      gstep % 16 || ustep % 16 || dstep % 16)
+    return VIREO_ERR_UNSUPPORTED;
+
+  gguf_moe* m = new gguf_moe();
+  m->desc = D;
+  MoeDecodeParams& p = m->prm;
+  memset(&p, 0, sizeof(p));
+  p.d = D.dim;
+  p.fe = D.ffn_exp;
+  p.ne = D.n_experts;
+  p.k = D.n_used;
+  p.renorm = D.topk_renorm;
+  p.router = (const float*)D.router;
+  if ((st = stage_geom(D.gate_type, D.dim, &p.sg_gu)) || (st = stage_geom(D.down_type, D.ffn_exp, &p.sg_d))) {
+    delete m;
+    return st;
+  }
+  m->smem = moe_decode_layout(&p, dyn_smem_limit(c));
+  m->kernel = moe_decode_kernel_for(D.gate_type, D.down_type);
+  if (!m->smem || !m->kernel) {
+    delete m;
+    return VIREO_ERR_UNSUPPORTED;
+  }
+  if ((st = ensure_smem_attr(c, m->kernel))) {
+    delete m;
+    return st;
+  }
+  int per_sm = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, m->kernel, kDecodeThreads, m->smem);
+  if (e != cudaSuccess || per_sm < 1) {
+    delete m;
+    return e != cudaSuccess ? cuda_status(e) : VIREO_ERR_UNSUPPORTED;
+  }
+  m->grid = c->num_sms;
+
+  // scratch: logit partials, h, y, tile counters, grid barrier, status
+  const size_t n_lp = (size_t)(D.dim / kRouterChunk) * D.n_experts, n_h = (size_t)D.n_used * D.ffn_exp,
+               n_y = (size_t)D.n_used * D.dim, n_tc = (size_t)D.dim / 16;
+  size_t off = 0;
+  const size_t o_lp = off;
+  off = up256(off + n_lp * 4);
+  const size_t o_h = off;
+  off = up256(off + n_h * 4);
+  const size_t o_y = off;
+  off = up256(off + n_y * 4);
+  const size_t o_tc = off;
+  off = up256(off + n_tc * 4);
+  const size_t o_gs = off;
+  off = up256(off + sizeof(GridSync));
+  const size_t o_err = off;
+  off = up256(off + sizeof(int));
+  m->scratch_bytes = off;
+  if ((st = cuda_status(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking))) ||
+      (st = cuda_status(cudaMalloc(&m->scratch, off))) ||
+      (st = cuda_status(cudaMemset(m->scratch, 0, off)))) {
+    gguf_moe_destroy(m);
+    return st;
+  }
+  uint8_t* sb = (uint8_t*)m->scratch;
+  p.s.logit_part = (float*)(sb + o_lp);
+  p.s.hbuf = (float*)(sb + o_h);
+  p.s.ybuf = (float*)(sb + o_y);
+  p.s.tile_cnt = (unsigned int*)(sb + o_tc);
+  p.s.gsync = (GridSync*)(sb + o_gs);
+  p.s.err = (int*)(sb + o_err);
+
+  m->h_exp_tab.resize((size_t)3 * D.n_experts);
+  for (int ex = 0; ex < D.n_experts; ex++) {
+    m->h_exp_tab[3 * ex + 0] = (const uint8_t*)D.gate_exps + (uint64_t)ex * gstep;
+    m->h_exp_tab[3 * ex + 1] = (const uint8_t*)D.up_exps + (uint64_t)ex * ustep;
+    m->h_exp_tab[3 * ex + 2] = (const uint8_t*)D.down_exps + (uint64_t)ex * dstep;
+  }
+  if ((st = cuda_status(cudaMalloc(&m->d_exp_tab, sizeof(void*) * m->h_exp_tab.size()))) ||
+      (st = cuda_status(cudaMemcpy(m->d_exp_tab, m->h_exp_tab.data(), sizeof(void*) * m->h_exp_tab.size(),
+                                   cudaMemcpyHostToDevice)))) {
+    gguf_moe_destroy(m);
+    return st;
+  }
+  p.exp_tab = m->d_exp_tab;
+  *out = m;
+  return VIREO_OK;
+}
+
+int gguf_moe_ffn(gguf_moe* m, const float* hb, float* x, int n_tok, int32_t* ids, float* wts, void* stream) {
+  if (!m || !hb || !x || n_tok < 0) return VIREO_ERR_ARG;
+  if (((uintptr_t)hb % 16) || ((size_t)m->prm.d * 4) % 16) return VIREO_ERR_ARG;
+  cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
+  MoeDecodeParams p = m->prm;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(m->grid);
+  cfg.blockDim = dim3(kDecodeThreads);
+  cfg.dynamicSmemBytes = m->smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  for (int i = 0; i < n_tok; i++) {
+    p.hb = hb + (size_t)i * p.d;
+    p.x = x + (size_t)i * p.d;
+    p.ids_out = ids ? ids + (size_t)i * p.k : nullptr;
+    p.wts_out = wts ? wts + (size_t)i * p.k : nullptr;
+    void* args[] = {&p};
+    int st = cuda_status(cudaLaunchKernelExC(&cfg, m->kernel, args));
+    if (st) return st;
+  }
+  return VIREO_OK;
+}
+
+int gguf_moe_sync(gguf_moe* m, void* stream) {
+  if (!m) return VIREO_ERR_ARG;
+  cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
+  int st = cuda_status(cudaStreamSynchronize(s));
+  if (st) return st;
+  int herr = 0;
+  if ((st = cuda_status(cudaMemcpy(&herr, m->prm.s.err, sizeof(int), cudaMemcpyDeviceToHost)))) return st;
+  if (herr) {
+    moe_reset_scratch(m, s);
+    cudaStreamSynchronize(s);
+    return herr;
+  }
+  return VIREO_OK;
+}
+
+int gguf_moe_ffn_host(gguf_moe* m, const float* hb, float* x, int n_tok, int32_t* ids, float* wts) {
+  if (!m || !hb || !x || n_tok < 0) return VIREO_ERR_ARG;
+  if (n_tok == 0) return VIREO_OK;
+  const size_t d = (size_t)m->prm.d, k = (size_t)m->prm.k;
+  int st;
+  if (n_tok > m->io_cap) {
+    cudaFree(m->d_io);
+    cudaFree(m->d_ids);
+    cudaFree(m->d_wts);
+    m->d_io = nullptr;
+    m->d_ids = nullptr;
+    m->d_wts = nullptr;
+    m->io_cap = 0;
+    if ((st = cuda_status(cudaMalloc(&m->d_io, 2 * d * n_tok * 4))) ||
+        (st = cuda_status(cudaMalloc(&m->d_ids, k * n_tok * 4))) ||
+        (st = cuda_status(cudaMalloc(&m->d_wts, k * n_tok * 4))))
+      return st;
+    m->io_cap = n_tok;
+  }
+  float* dh = m->d_io;
+  float* dx = m->d_io + d * n_tok;
+  cudaStream_t s = m->stream;
+  if ((st = cuda_status(cudaMemcpyAsync(dh, hb, d * n_tok * 4, cudaMemcpyHostToDevice, s))) ||
+      (st = cuda_status(cudaMemcpyAsync(dx, x, d * n_tok * 4, cudaMemcpyHostToDevice, s))))
+    return st;
+  if ((st = gguf_moe_ffn(m, dh, dx, n_tok, m->d_ids, m->d_wts, s))) return st;
+  if ((st = cuda_status(cudaMemcpyAsync(x, dx, d * n_tok * 4, cudaMemcpyDeviceToHost, s)))) return st;
+  if (ids && (st = cuda_status(cudaMemcpyAsync(ids, m->d_ids, k * n_tok * 4, cudaMemcpyDeviceToHost, s)))) return st;
+  if (wts && (st = cuda_status(cudaMemcpyAsync(wts, m->d_wts, k * n_tok * 4, cudaMemcpyDeviceToHost, s)))) return st;
+  return gguf_moe_sync(m, s);
+}
+
+int gguf_moe_set_expert_ptrs(gguf_moe* m, const void* const* gate, const void* const* up, const void* const* down) {
+  if (!m) return VIREO_ERR_ARG;
+  for (int ex = 0; ex < m->desc.n_experts; ex++) {
+    if (gate) m->h_exp_tab[3 * ex + 0] = (const uint8_t*)gate[ex];
+    if (up) m->h_exp_tab[3 * ex + 1] = (const uint8_t*)up[ex];
+    if (down) m->h_exp_tab[3 * ex + 2] = (const uint8_t*)down[ex];
+  }
+  for (auto* ptr : m->h_exp_tab)
+    if (((uintptr_t)ptr) % 16) return VIREO_ERR_ARG;
+  return cuda_status(cudaMemcpy(m->d_exp_tab, m->h_exp_tab.data(), sizeof(void*) * m->h_exp_tab.size(),
+                                cudaMemcpyHostToDevice));
+}
+
+void gguf_moe_destroy(gguf_moe* m) {
+  if (!m) return;
+  if (m->stream) cudaStreamSynchronize(m->stream);
+  cudaFree(m->scratch);
+  cudaFree(m->d_exp_tab);
+  cudaFree(m->d_io);
+  cudaFree(m->d_ids);
+  cudaFree(m->d_wts);
+  if (m->stream) cudaStreamDestroy(m->stream);
+  delete m;
+}
+
+}  // extern "C"

@@ -1,0 +1,76 @@
+// Internal declarations shared by the CUDA sources and the C-ABI layer.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+#include <mutex>
+#include <vector>
+
+#include "vireo_status.h"
+
+namespace vireo {
+
+struct StageGeom;
+struct MoeDecodeParams;
+
+// elements / bytes per block for the types this library reads (GGUF wire
+// sizes, vireo src/gguf.c:27-38); 0 on success
+inline int type_block(uint32_t t, int* be, int* bb) {
+  switch (t) {
+    case 0: *be = 1; *bb = 4; return 0;      // F32
+    case 1: *be = 1; *bb = 2; return 0;      // F16
+    case 6: *be = 32; *bb = 22; return 0;    // Q5_0
+    case 8: *be = 32; *bb = 34; return 0;    // Q8_0
+    case 12: *be = 256; *bb = 144; return 0; // Q4_K
+    case 14: *be = 256; *bb = 210; return 0; // Q6_K
+    default: return -1;
+  }
+}
+inline uint64_t row_bytes(uint32_t t, int n) {
+  int be, bb;
+  if (type_block(t, &be, &bb)) return 0;
+  return (uint64_t)(n / be) * (uint64_t)bb;
+}
+
+struct GemvParams;
+
+bool fast_format(uint32_t type);
+int stage_geom(uint32_t type, int K, StageGeom* sg);
+const void* moe_decode_kernel_for(uint32_t gtype, uint32_t dtype);
+uint32_t moe_decode_layout(MoeDecodeParams* p, uint32_t smem_limit);
+const void* gemv_kernel_for(uint32_t type);
+uint32_t gemv_layout(GemvParams* p, uint32_t smem_limit);
+
+// generic kernels (any supported type/shape), generic_kernels.cu
+int launch_dequant(uint32_t type, const void* src, float* dst, int n, cudaStream_t s);
+int launch_gemv_generic(uint32_t type, const void* w, const float* x, float* y, int n, int d, cudaStream_t s);
+
+// process-wide device context
+struct HostRange {
+  const uint8_t* host;
+  uint64_t bytes;
+  uint8_t* dev;
+};
+
+struct Ctx {
+  int device = -1;
+  int num_sms = 0;
+  uint32_t smem_optin = 0;
+  cudaStream_t stream = nullptr;
+  int* d_err = nullptr;   // device status word for stand-alone calls
+  void* scratch = nullptr;
+  size_t scratch_bytes = 0;
+  std::vector<HostRange> ranges;
+  std::mutex mu;
+};
+
+Ctx* ctx_get(int* status);
+void set_last_error(int code);
+int cuda_status(cudaError_t e);
+void* ctx_scratch(Ctx* c, size_t bytes);  // grows, caller holds c->mu
+
+// device-pointer GEMV with the fast path when possible
+int gemv_dev(Ctx* c, uint32_t type, const void* w, const float* x, float* y, int n, int d, cudaStream_t s);
+
+}  // namespace vireo
