@@ -49,7 +49,10 @@ int gguf_moe_create(const gguf_moe_desc *desc, gguf_moe **out);
  * hb: [n_tok][dim] normalised hidden; x: [n_tok][dim] residual, updated in
  * place (x += MoE(hb)); ids / wts: [n_tok][n_used] selected experts in rank
  * order and their gate weights, or NULL.  Device pointers, stream-ordered,
- * no host synchronisation; device-side failures surface in gguf_moe_sync. */
+ * no host synchronisation; device-side failures surface in gguf_moe_sync.
+ * Each token is one kernel launched with programmatic dependent launch: it
+ * may read the router weights before the preceding kernel on the stream has
+ * finished, so router weights must not be written by that kernel. */
 int gguf_moe_ffn(gguf_moe *m, const float *hb, float *x, int n_tok, int32_t *ids, float *wts, void *stream);
 
 /* Same with HOST buffers: copies in, runs, copies out, synchronises. */
@@ -63,6 +66,18 @@ int gguf_moe_sync(gguf_moe *m, void *stream);
  * Used when an ExpertStore owns the expert slabs. */
 int gguf_moe_set_expert_ptrs(gguf_moe *m, const void *const *gate, const void *const *up,
                              const void *const *down);
+
+/* Phase tracing (diagnostics): when dev_buf is non-NULL, every later
+ * launch writes 72 %globaltimer stamps (ns) per CTA into dev_buf
+ * [gguf_moe_grid(m)][72]: kernel start, router partials written, all
+ * partials visible, routing done, own gate/up units done, all gate/up units
+ * done, down tables built, down units done (consumer side); first gate/up
+ * issue, first down issue, last issue, copies drained (producer side);
+ * then (stage ready, unit done) pairs for the CTA's first 24 units and 8
+ * spare stamps.  The buffer must hold the full 72 stamps per CTA.  NULL
+ * turns tracing off. */
+int gguf_moe_set_trace(gguf_moe *m, unsigned long long *dev_buf);
+int gguf_moe_grid(const gguf_moe *m);
 
 void gguf_moe_destroy(gguf_moe *m);
 

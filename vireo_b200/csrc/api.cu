@@ -110,9 +110,18 @@ int gemv_dev(Ctx* c, uint32_t type, const void* w, const float* x, float* y, int
         const void* fn = gemv_kernel_for(type);
         int st = ensure_smem_attr(c, fn);
         if (st) return st;
-        int grid = std::min(c->num_sms, d / 16);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(std::min(c->num_sms, d / 16));
+        cfg.blockDim = dim3(kDecodeThreads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
         void* args[] = {&p};
-        return cuda_status(cudaLaunchKernel(fn, dim3(grid), dim3(kDecodeThreads), args, smem, s));
+        return cuda_status(cudaLaunchKernelExC(&cfg, fn, args));
       }
     }
   }
@@ -365,6 +374,7 @@ struct gguf_moe {
   int32_t* d_ids = nullptr;
   float* d_wts = nullptr;
   int io_cap = 0;
+  bool pdl = true;
   cudaStream_t stream = nullptr;
 };
 
@@ -385,7 +395,8 @@ int gguf_moe_create(const gguf_moe_desc* desc, gguf_moe** out) {
       !D.router || !D.gate_exps || !D.up_exps || !D.down_exps)
     return VIREO_ERR_ARG;
   if (D.router_type != T_F32 || D.gate_type != D.up_type || !fast_format(D.gate_type) ||
-      !fast_format(D.down_type) || D.dim % kRouterChunk || D.ffn_exp % kSegElems || D.n_experts > 256 ||
+      !fast_format(D.down_type) || D.dim % kRouterChunk || D.dim > 8 * kRouterChunk || D.ffn_exp % kSegElems ||
+      D.n_experts > 256 || D.ffn_exp % (32 * kConsumerWarps) || D.n_used * D.ffn_exp > 32 * 32 * kConsumerWarps ||
       D.n_used > kMaxTopK)
     return VIREO_ERR_UNSUPPORTED;
   const uint64_t gsl = (uint64_t)D.ffn_exp * row_bytes(D.gate_type, D.dim);
@@ -412,7 +423,7 @@ int gguf_moe_create(const gguf_moe_desc* desc, gguf_moe** out) {
     delete m;
     return st;
   }
-  m->smem = moe_decode_layout(&p, dyn_smem_limit(c));
+  m->smem = moe_decode_layout(&p, dyn_smem_limit(c), c->num_sms);
   m->kernel = moe_decode_kernel_for(D.gate_type, D.down_type);
   if (!m->smem || !m->kernel) {
     delete m;
@@ -430,20 +441,16 @@ int gguf_moe_create(const gguf_moe_desc* desc, gguf_moe** out) {
   }
   m->grid = c->num_sms;
 
-  // scratch: logit partials, h, y, tile counters, grid barrier, status
-  const size_t n_lp = (size_t)(D.dim / kRouterChunk) * D.n_experts, n_h = (size_t)D.n_used * D.ffn_exp,
-               n_y = (size_t)D.n_used * D.dim, n_tc = (size_t)D.dim / 16;
+  // scratch: logit partials, h, per-launch sync words, status
+  p.hsx_count = (uint32_t)(D.ffn_exp / (D.down_type == T_Q6_K ? 16 : 32));
+  const size_t n_lp = (size_t)(D.dim / kRouterChunk) * D.n_experts, n_h = (size_t)D.n_used * D.ffn_exp;
   size_t off = 0;
   const size_t o_lp = off;
   off = up256(off + n_lp * 4);
   const size_t o_h = off;
   off = up256(off + n_h * 4);
-  const size_t o_y = off;
-  off = up256(off + n_y * 4);
-  const size_t o_tc = off;
-  off = up256(off + n_tc * 4);
-  const size_t o_gs = off;
-  off = up256(off + sizeof(GridSync));
+  const size_t o_sy = off;
+  off = up256(off + sizeof(MoeSync));
   const size_t o_err = off;
   off = up256(off + sizeof(int));
   m->scratch_bytes = off;
@@ -456,9 +463,7 @@ int gguf_moe_create(const gguf_moe_desc* desc, gguf_moe** out) {
   uint8_t* sb = (uint8_t*)m->scratch;
   p.s.logit_part = (float*)(sb + o_lp);
   p.s.hbuf = (float*)(sb + o_h);
-  p.s.ybuf = (float*)(sb + o_y);
-  p.s.tile_cnt = (unsigned int*)(sb + o_tc);
-  p.s.gsync = (GridSync*)(sb + o_gs);
+  p.s.sync = (MoeSync*)(sb + o_sy);
   p.s.err = (int*)(sb + o_err);
 
   m->h_exp_tab.resize((size_t)3 * D.n_experts);
@@ -488,18 +493,32 @@ int gguf_moe_ffn(gguf_moe* m, const float* hb, float* x, int n_tok, int32_t* ids
   cfg.blockDim = dim3(kDecodeThreads);
   cfg.dynamicSmemBytes = m->smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  // cooperative: every CTA must be resident (CTAs wait on one another's
+  // flags); programmatic serialization: the next token's kernel may begin
+  // its weight-only prologue while this one drains (griddepcontrol.wait in
+  // the kernel orders everything that reads the previous kernel's output)
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = m->pdl ? 2 : 1;
   for (int i = 0; i < n_tok; i++) {
     p.hb = hb + (size_t)i * p.d;
     p.x = x + (size_t)i * p.d;
     p.ids_out = ids ? ids + (size_t)i * p.k : nullptr;
     p.wts_out = wts ? wts + (size_t)i * p.k : nullptr;
     void* args[] = {&p};
-    int st = cuda_status(cudaLaunchKernelExC(&cfg, m->kernel, args));
+    cudaError_t e = cudaLaunchKernelExC(&cfg, m->kernel, args);
+    if (e != cudaSuccess && m->pdl) {
+      // this driver refuses cooperative + programmatic launches: drop PDL
+      cudaGetLastError();
+      m->pdl = false;
+      cfg.numAttrs = 1;
+      e = cudaLaunchKernelExC(&cfg, m->kernel, args);
+    }
+    int st = cuda_status(e);
     if (st) return st;
   }
   return VIREO_OK;
@@ -564,6 +583,14 @@ int gguf_moe_set_expert_ptrs(gguf_moe* m, const void* const* gate, const void* c
   return cuda_status(cudaMemcpy(m->d_exp_tab, m->h_exp_tab.data(), sizeof(void*) * m->h_exp_tab.size(),
                                 cudaMemcpyHostToDevice));
 }
+
+int gguf_moe_set_trace(gguf_moe* m, unsigned long long* dev_buf) {
+  if (!m) return VIREO_ERR_ARG;
+  m->prm.trace = dev_buf;
+  return VIREO_OK;
+}
+
+int gguf_moe_grid(const gguf_moe* m) { return m ? m->grid : 0; }
 
 void gguf_moe_destroy(gguf_moe* m) {
   if (!m) return;

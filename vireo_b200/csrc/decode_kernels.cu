@@ -13,14 +13,17 @@ namespace vireo {
 struct Ctl {
   int abort;
   int nvalid;
-  int t_lo;
   float xinv;
   int ids[kMaxTopK];
   float wts[kMaxTopK];
   float hinv[kMaxTopK];
+  int tile_cnt[2];  // down units finished per tile buffer
+  float hamax[kMaxTopK];  // this CTA's max |h| per expert slot
 };
 
-__device__ const int kNeverAbort = 0;
+VDEV void trace(const MoeDecodeParams& p, int slot) {
+  if (p.trace) p.trace[blockIdx.x * kTraceSlots + slot] = now_ns();
+}
 
 VDEV void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
@@ -34,13 +37,36 @@ VDEV void do_abort(Ctl* c, int* err, int code) {
 // the partial/counter protocol intact
 template <class S>
 VDEV bool consume(const uint8_t* stage, const StageGeom& sg, int v, int nseg, int w, const uint8_t* btab,
-                  const float* sx, float* part, int* ucnt, const LaneCtx& L, float* val, bool active) {
-  return consume_unit<S>(stage, sg, v, active ? nseg : 0, kConsumerWarps, w, btab, sx, part, ucnt, L, val);
+                  const float* sx, float* part, int* ucnt, const LaneCtx& L, float* val, bool active, BFrag& bf) {
+  return consume_unit<S>(stage, sg, v, active ? nseg : 0, kConsumerWarps, w, btab, sx, part, ucnt, L, val, bf);
+}
+
+// Warp-collective stage wait: lane 0 waits (bounded), the result and the
+// completed phase are shared with the warp.  False when aborted or timed out
+// (the timeout is recorded).
+VDEV bool warp_wait(uint64_t* bar, uint32_t par, Ctl* ctl, int* err) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) {
+    ok = (!aborted(ctl) && mbar_wait(bar, par, &ctl->abort)) ? 1 : 0;
+    if (!ok && !aborted(ctl)) do_abort(ctl, err, VIREO_ERR_TIMEOUT);
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
 }
 
 // ---------------------------------------------------------------------------
 // MoE decode kernel
 // ---------------------------------------------------------------------------
+
+// Cooperative (block-wide among nthr threads starting at thread 0) load of
+// n floats from global into shared memory with 16-byte loads.
+VDEV void stage_vec(const float* g, float* s, int n, int tid, int nthr, bool bypass_l1) {
+  const float4* g4 = reinterpret_cast<const float4*>(g);
+  float4* s4 = reinterpret_cast<float4*>(s);
+  for (int i = tid; i < n / 4; i += nthr) s4[i] = bypass_l1 ? __ldcg(g4 + i) : __ldg(g4 + i);
+}
+
 template <class SG, class SD>
 __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __grid_constant__ MoeDecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -50,289 +76,391 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __g
   Ctl* ctl = reinterpret_cast<Ctl*>(smem + p.off_ctl);
   float* part = reinterpret_cast<float*>(smem + p.off_part);
   int* ucnt = reinterpret_cast<int*>(smem + p.off_ucnt);
+  int* unit_of = reinterpret_cast<int*>(smem + p.off_unit);  // unit carried by each stage
+  float* ytile = reinterpret_cast<float*>(smem + p.off_ytile); // [2][k][16] expert rows of a tile
   uint8_t* xtab = smem + p.off_xtab;
   float* xsx = reinterpret_cast<float*>(smem + p.off_xsx);
   uint8_t* htab = smem + p.off_htab;
   float* hsx = reinterpret_cast<float*>(smem + p.off_hsx);
+  float* stg = reinterpret_cast<float*>(smem + p.off_stg);  // x staging
   uint8_t* stages = smem + p.off_stage;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int W = kConsumerWarps;
+  constexpr int NC = W * 32;  // consumer threads
   const int G = gridDim.x, cta = blockIdx.x;
   const int d = p.d, fe = p.fe, ne = p.ne, k = p.k, S = p.nstages;
+  MoeSync* sy = p.s.sync;
 
   if (threadIdx.x == 0) {
+    trace(p, kTrStart);
     for (int s = 0; s < S; s++) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], kProducerThreads + 1);  // every producer's copies + the unit id
       mbar_init(&empty[s], W);
     }
     ctl->abort = 0;
+    ctl->tile_cnt[0] = ctl->tile_cnt[1] = 0;
+    for (int t = 0; t < kMaxTopK; t++) ctl->hamax[t] = 0.f;
     mbar_fence_init();
   }
   for (int i = threadIdx.x; i < S; i += blockDim.x) ucnt[i] = 0;
-  __syncthreads();
+  // the next token's kernel may start its own prologue as SMs free up
+  pdl_launch_dependents();
 
-  // ---- phase R: router partial dot products -------------------------------
-  if (warp < W) {
+  // ---- phase R: router partial dot products --------------------------------
+  // Router rows are weights (independent of the previous kernel): their loads
+  // are issued before waiting on the previous kernel in the stream.
+  {
     const int nchunk = d / kRouterChunk;
-    const int gw = cta * W + warp, nw = G * W;
-    for (int task = gw; task < ne * nchunk; task += nw) {
-      const int e = task / nchunk, c = task - e * nchunk;
+    const int ntask = ne * nchunk, nw = G * (int)(blockDim.x / 32);
+    const int gw = warp * G + cta;  // spread tasks over all CTAs first
+    float4 r0[4], r1[4];
+    const bool has0 = gw < ntask, has1 = gw + nw < ntask;
+    if (has0) {
+      const int e = gw / nchunk, c = gw - e * nchunk;
       const float4* row = reinterpret_cast<const float4*>(p.router + (size_t)e * d + (size_t)c * kRouterChunk);
-      const float4* xv = reinterpret_cast<const float4*>(p.hb + (size_t)c * kRouterChunk);
-      float4 r[4], xx[4];
 #pragma unroll
-      for (int i = 0; i < 4; i++) {
-        r[i] = __ldg(row + lane + 32 * i);
-        xx[i] = __ldg(xv + lane + 32 * i);
+      for (int i = 0; i < 4; i++) r0[i] = __ldg(row + lane + 32 * i);
+    }
+    if (has1) {
+      const int t1 = gw + nw, e = t1 / nchunk, c = t1 - e * nchunk;
+      const float4* row = reinterpret_cast<const float4*>(p.router + (size_t)e * d + (size_t)c * kRouterChunk);
+#pragma unroll
+      for (int i = 0; i < 4; i++) r1[i] = __ldg(row + lane + 32 * i);
+    }
+    pdl_wait();
+    stage_vec(p.hb, stg, d, threadIdx.x, blockDim.x, false);
+    for (int task = gw, it = 0; task < ntask; task += nw, it++) {
+      const int e = task / nchunk, c = task - e * nchunk;
+      float4 r[4];
+      if (it == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) r[i] = r0[i];
+      } else if (it == 1) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) r[i] = r1[i];
+      } else {
+        const float4* row = reinterpret_cast<const float4*>(p.router + (size_t)e * d + (size_t)c * kRouterChunk);
+#pragma unroll
+        for (int i = 0; i < 4; i++) r[i] = __ldg(row + lane + 32 * i);
       }
+      const float4* xv = reinterpret_cast<const float4*>(p.hb + (size_t)c * kRouterChunk);
       float s = 0.f;
 #pragma unroll
       for (int i = 0; i < 4; i++) {
-        s = fmaf(r[i].x, xx[i].x, s);
-        s = fmaf(r[i].y, xx[i].y, s);
-        s = fmaf(r[i].z, xx[i].z, s);
-        s = fmaf(r[i].w, xx[i].w, s);
+        const float4 xx = __ldg(xv + lane + 32 * i);
+        s = fmaf(r[i].x, xx.x, s);
+        s = fmaf(r[i].y, xx.y, s);
+        s = fmaf(r[i].z, xx.z, s);
+        s = fmaf(r[i].w, xx.w, s);
       }
 #pragma unroll
       for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
       if (lane == 0) p.s.logit_part[(size_t)c * ne + e] = s;
     }
-  }
-
-  // ---- x table (every CTA builds its own) ---------------------------------
-  {
-    float m = 0.f;
-    for (int i = threadIdx.x; i < d; i += blockDim.x) m = fmaxf(m, fabsf(__ldg(p.hb + i)));
-#pragma unroll
-    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) red[warp] = m;
     __syncthreads();
+    // every CTA has written its router partials once router_arrive == G
     if (threadIdx.x == 0) {
-      float mm = 0.f;
-      for (int i = 0; i < (int)(blockDim.x / 32); i++) mm = fmaxf(mm, red[i]);
-      const float sc = pow2_scale(mm);
-      red[kDecodeThreads / 32] = sc;
-      ctl->xinv = 1.f / sc;
+      trace(p, kTrRouterDone);
+      red_add_release_gpu(&sy->router_arrive.v, 1u);
+    }
+    // x table while the other CTAs finish their router partials
+    {
+      float m = 0.f;
+      for (int i = threadIdx.x; i < d; i += blockDim.x) m = fmaxf(m, fabsf(stg[i]));
+#pragma unroll
+      for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (lane == 0) red[warp] = m;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        float mm = 0.f;
+        for (int i = 0; i < (int)(blockDim.x / 32); i++) mm = fmaxf(mm, red[i]);
+        const float sc = pow2_scale(mm);
+        red[kDecodeThreads / 32] = sc;
+        ctl->xinv = 1.f / sc;
+      }
+      __syncthreads();
+      build_btab<SG>(stg, d, red[kDecodeThreads / 32], xtab, xsx, threadIdx.x, blockDim.x, false);
+    }
+    if (threadIdx.x == 0) {
+      if (!wait_geq(&sy->router_arrive.v, (unsigned)G, p.s.err)) ctl->abort = 1;
+      trace(p, kTrPartials);
     }
     __syncthreads();
-    build_btab<SG>(p.hb, d, red[kDecodeThreads / 32], xtab, xsx, threadIdx.x, blockDim.x, false);
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    if (!grid_barrier(p.s.gsync, (unsigned)G, p.s.err)) ctl->abort = 1;
-  }
-  __syncthreads();
-
-  // ---- softmax + greedy top-k (every CTA, warp 0) ------------------------
-  if (warp == 0 && !aborted(ctl)) {
-    const int nchunk = d / kRouterChunk;
-    float v[8];
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-      const int e = lane + 32 * i;
-      float s = -INFINITY;
+    // ---- softmax + top-k in every CTA (no second hop) ----------------------
+    // logits l[e] = sum of the chunk partials in chunk order; p = softmax(l);
+    // expert e takes rank r = #{j : p_j > p_e, or p_j == p_e and j < e}, the
+    // position the reference's greedy strict-'>' selection gives it
+    // (gguf_run.c:190-191); ranks < k are the selection.  NaN never ranks.
+    float* pr = reinterpret_cast<float*>(htab);  // probabilities (htab idle until the down phase)
+    if (!aborted(ctl)) {
+      float lv = -INFINITY;
+      const int e = threadIdx.x;
       if (e < ne) {
-        s = 0.f;
-        for (int c = 0; c < nchunk; c++) s += __ldcg(p.s.logit_part + (size_t)c * ne + e);
+        float part_c[8];
+#pragma unroll
+        for (int c = 0; c < 8; c++) part_c[c] = (c < nchunk) ? __ldcg(p.s.logit_part + (size_t)c * ne + e) : 0.f;
+        lv = 0.f;
+#pragma unroll
+        for (int c = 0; c < 8; c++)
+          if (c < nchunk) lv += part_c[c];
       }
-      v[i] = s;
-    }
-    float mx = -INFINITY;
+      float m = lv;
 #pragma unroll
-    for (int i = 0; i < 8; i++) mx = fmaxf(mx, v[i]);
+      for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (lane == 0) red[warp] = m;
+      __syncthreads();
+      float mx = -INFINITY;
+      for (int i = 0; i < (int)(blockDim.x / 32); i++) mx = fmaxf(mx, red[i]);
+      const float ex = (e < ne) ? expf(lv - mx) : 0.f;
+      float sm = ex;
 #pragma unroll
-    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float sum = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-      const int e = lane + 32 * i;
-      v[i] = (e < ne) ? expf(v[i] - mx) : 0.f;
-      sum += v[i];
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-#pragma unroll
-    for (int i = 0; i < 8; i++) v[i] = v[i] / sum;
-    uint32_t used = 0;
-    for (int t = 0; t < k; t++) {
-      float bv = -1.f;
-      int bi = -1;
-#pragma unroll
-      for (int i = 0; i < 8; i++) {
-        const int e = lane + 32 * i;
-        if (e < ne && !((used >> i) & 1u) && v[i] > bv) {
-          bv = v[i];
-          bi = e;
+      for (int o = 16; o; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+      __syncthreads();
+      if (lane == 0) red[warp] = sm;
+      __syncthreads();
+      float sum = 0.f;
+      for (int i = 0; i < (int)(blockDim.x / 32); i++) sum += red[i];
+      const float pe = ex / sum;
+      if (e < ne) pr[e] = pe;
+      __syncthreads();
+      if (e < ne && !isnan(pe)) {
+        int rank = 0;
+        const float4* pr4 = reinterpret_cast<const float4*>(pr);
+#pragma unroll 4
+        for (int j4 = 0; j4 < ne / 4; j4++) {
+          const float4 q = pr4[j4];
+          const int j = 4 * j4;
+          rank += (q.x > pe) || (q.x == pe && j < e);
+          rank += (q.y > pe) || (q.y == pe && j + 1 < e);
+          rank += (q.z > pe) || (q.z == pe && j + 2 < e);
+          rank += (q.w > pe) || (q.w == pe && j + 3 < e);
+        }
+        for (int j = ne & ~3; j < ne; j++) {
+          const float pj = pr[j];
+          rank += (pj > pe) || (pj == pe && j < e);
+        }
+        if (rank < k) {
+          ctl->ids[rank] = e;
+          ctl->wts[rank] = pe;
         }
       }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi >= 0 && (bi < 0 || oi < bi))) {
-          bv = ov;
-          bi = oi;
+      // fewer than k selectable experts (NaN probabilities): unused slots
+      const int nsel = __syncthreads_count(e < ne && !isnan(pe));
+      if (threadIdx.x == 0) {
+        for (int t = nsel; t < k; t++) {
+          ctl->ids[t] = -1;
+          ctl->wts[t] = -1.f;
         }
-      }
-      if (bi >= 0 && (bi & 31) == lane) used |= 1u << (bi >> 5);
-      if (lane == 0) {
-        ctl->ids[t] = bi;
-        ctl->wts[t] = bv;
-      }
-    }
-    __syncwarp();
-    if (lane == 0) {
-      int nv = 0;
-      float ws = 0.f;
-      for (int t = 0; t < k; t++) {
-        ws = ws + ctl->wts[t];
-        nv += ctl->ids[t] >= 0;
-      }
-      if (p.renorm && ws > 0.f)
-        for (int t = 0; t < k; t++) ctl->wts[t] = ctl->wts[t] / ws;
-      ctl->nvalid = nv;
-      if (cta == 0) {
+        float ws = 0.f;
+        int nv = 0;
         for (int t = 0; t < k; t++) {
-          if (p.ids_out) p.ids_out[t] = ctl->ids[t];
-          if (p.wts_out) p.wts_out[t] = ctl->wts[t];
+          ws = ws + ctl->wts[t];
+          nv += ctl->ids[t] >= 0;
         }
+        if (p.renorm && ws > 0.f)
+          for (int t = 0; t < k; t++) ctl->wts[t] = ctl->wts[t] / ws;
+        ctl->nvalid = nv;
+        if (cta == 0) {
+          for (int t = 0; t < k; t++) {
+            if (p.ids_out) p.ids_out[t] = ctl->ids[t];
+            if (p.wts_out) p.wts_out[t] = ctl->wts[t];
+          }
+        }
+        trace(p, kTrRouted);
       }
     }
+    __syncthreads();
   }
-  __syncthreads();
 
-  // ---- units ---------------------------------------------------------------
-  const int rgG = fe / 8, rgD = d / 16;
-  const int UG = k * rgG, UD = k * rgD;
+  const int rgG = fe / 8, UG = k * rgG, ntile = d / 16;
   const int g0 = (int)((long long)cta * UG / G), g1 = (int)((long long)(cta + 1) * UG / G);
-  const int d0 = (int)((long long)cta * UD / G), d1 = (int)((long long)(cta + 1) * UD / G);
-  const int nG = g1 - g0, nD = d1 - d0, nU = nG + nD;
-  const int nsegG = d / kSegElems, nsegD = fe / kSegElems;
+  const int my_tiles = (cta < ntile) ? (ntile - 1 - cta) / G + 1 : 0;
 
-  if (warp == W) {
-    // ---- producer -----------------------------------------------------------
-    if (lane == 0) {
-      int issued = 0;
-      for (int v = 0; v < nU; v++) {
-        if (aborted(ctl)) break;
-        const int slot = v % S;
-        const uint32_t par = ((uint32_t)(v / S) & 1u) ^ 1u;
-        if (!mbar_wait(&empty[slot], par, &ctl->abort)) {
-          do_abort(ctl, p.s.err, VIREO_ERR_TIMEOUT);
-          break;
-        }
-        uint8_t* stage = stages + (size_t)slot * p.stage_bytes;
-        if (v < nG) {
-          const int u = g0 + v, t = u / rgG, rg = u - t * rgG;
-          const int e = ctl->ids[t];
-          if (e < 0) {
-            mbar_arrive(&full[slot]);
-          } else {
-            const uint8_t* gsrc = p.exp_tab[3 * e + 0] + (size_t)(8 * rg) * p.sg_gu.rb;
-            const uint8_t* usrc = p.exp_tab[3 * e + 1] + (size_t)(8 * rg) * p.sg_gu.rb;
-            issue_unit(stage, &full[slot], gsrc, usrc, p.sg_gu);
-          }
-        } else {
-          const int u = d0 + (v - nG), t = u / rgD, rg = u - t * rgD;
-          const int e = ctl->ids[t];
-          if (e < 0) {
-            mbar_arrive(&full[slot]);
-          } else {
-            const uint8_t* src = p.exp_tab[3 * e + 2] + (size_t)(16 * rg) * p.sg_d.rb;
-            issue_unit(stage, &full[slot], src, src + 8 * (size_t)p.sg_d.rb, p.sg_d);
-          }
-        }
-        issued = v + 1;
+  if (warp >= W) {
+    // ---- producers: 16-byte cp.async copies ---------------------------------
+    const int ptid = threadIdx.x - NC;
+    int v = 0;
+    // gate/up units: a contiguous range per CTA
+    if (ptid == 0) trace(p, kTrProdFirst);
+    for (int u = g0; u < g1; u++) {
+      const int slot = v % S;
+      if (!warp_wait(&empty[slot], ((uint32_t)(v / S) & 1u) ^ 1u, ctl, p.s.err)) break;
+      const int t = u / rgG, rg = u - t * rgG;
+      const int e = ctl->ids[t];
+      const uint8_t* gsrc = e < 0 ? nullptr : p.exp_tab[3 * e + 0] + (size_t)(8 * rg) * p.sg_gu.rb;
+      const uint8_t* usrc = e < 0 ? nullptr : p.exp_tab[3 * e + 1] + (size_t)(8 * rg) * p.sg_gu.rb;
+      issue_unit(stages + (size_t)slot * p.stage_bytes, &full[slot], gsrc, usrc, p.sg_gu, ptid, kProducerThreads);
+      if (ptid == 0) {
+        unit_of[slot] = u;
+        mbar_arrive(&full[slot]);
       }
-      // drain: every copy this CTA issued must land before the CTA exits
-      for (int v = (issued > S ? issued - S : 0); v < issued; v++)
-        mbar_wait(&full[v % S], (uint32_t)(v / S) & 1u, &kNeverAbort);
+      v++;
     }
+    // end-of-gate/up marker
+    {
+      const int slot = v % S;
+      if (warp_wait(&empty[slot], ((uint32_t)(v / S) & 1u) ^ 1u, ctl, p.s.err)) {
+        cp_async_arrive(&full[slot]);
+        if (ptid == 0) {
+          unit_of[slot] = -1;
+          mbar_arrive(&full[slot]);
+        }
+      }
+      v++;
+    }
+    // down units: every expert slot of each of this CTA's 16-row tiles
+    if (ptid == 0) trace(p, kTrProdFirstD);
+    for (int i = 0; i < my_tiles && !aborted(ctl); i++) {
+      const int tile = cta + i * G;
+      for (int t = 0; t < k; t++) {
+        const int slot = v % S;
+        if (!warp_wait(&empty[slot], ((uint32_t)(v / S) & 1u) ^ 1u, ctl, p.s.err)) break;
+        const int e = ctl->ids[t];
+        const uint8_t* src = e < 0 ? nullptr : p.exp_tab[3 * e + 2] + (size_t)(16 * tile) * p.sg_d.rb;
+        issue_unit(stages + (size_t)slot * p.stage_bytes, &full[slot], src, src ? src + 8 * (size_t)p.sg_d.rb : nullptr,
+                   p.sg_d, ptid, kProducerThreads);
+        if (ptid == 0) {
+          unit_of[slot] = tile * k + t;
+          mbar_arrive(&full[slot]);
+        }
+        v++;
+      }
+    }
+    if (ptid == 0) trace(p, kTrProdLast);
+    cp_async_wait_all();  // no copy may still target this CTA's shared memory at exit
+    if (ptid == 0) trace(p, kTrProdDrained);
     return;
   }
 
   // ---- consumers -------------------------------------------------------------
   const LaneCtx L = lane_ctx();
-  for (int v = 0; v < nG; v++) {
+  BFrag bf;
+  bf.reset();
+  int v = 0;
+  for (;; v++) {
     const int slot = v % S;
-    bool ok = !aborted(ctl) && mbar_wait(&full[slot], (uint32_t)(v / S) & 1u, &ctl->abort);
-    if (!ok && !aborted(ctl)) do_abort(ctl, p.s.err, VIREO_ERR_TIMEOUT);
-    const int u = g0 + v, t = u / rgG, rg = u - t * rgG;
-    const bool active = ok && ctl->ids[t] >= 0;
+    const bool ok = warp_wait(&full[slot], (uint32_t)(v / S) & 1u, ctl, p.s.err);
+    const int u = ok ? unit_of[slot] : -1;
+    if (u < 0) {  // end-of-gate/up marker (or abort)
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+      v++;
+      break;
+    }
+    if (threadIdx.x == 0 && v < kTrUnits) trace(p, kTrUnitBase + 2 * v);
+    const int t = u / rgG, rg = u - t * rgG;
+    const bool active = ctl->ids[t] >= 0;
     float val = 0.f;
-    const bool last = consume<SG>(stages + (size_t)slot * p.stage_bytes, p.sg_gu, v, nsegG, warp, xtab, xsx,
-                                  part + slot * W * 16, &ucnt[slot], L, &val, active);
+    const bool last = consume<SG>(stages + (size_t)slot * p.stage_bytes, p.sg_gu, v, p.d / kSegElems, warp, xtab,
+                                  xsx, part + slot * p.part_stride, &ucnt[slot], L, &val, active, bf);
     if (last) {
       const float up = __shfl_sync(0xffffffffu, val, (lane + 8) & 31);
+      float hv = 0.f;
       if (active && lane < 8) {
         const float gg = val * ctl->xinv, uu = up * ctl->xinv;
         const float sl = gg / (1.0f + expf(-gg));
-        p.s.hbuf[(size_t)t * fe + 8 * rg + lane] = sl * uu;
+        hv = sl * uu;
+        p.s.hbuf[(size_t)t * fe + 8 * rg + lane] = hv;
       }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);
-  }
-
-  // ---- phase boundary: every h row of every expert is written --------------
-  named_bar(1, W * 32);
-  if (threadIdx.x == 0 && !aborted(ctl)) {
-    if (!grid_barrier(p.s.gsync, (unsigned)G, p.s.err)) ctl->abort = 1;
-  }
-  named_bar(1, W * 32);
-  const int t_lo = (nD > 0) ? d0 / rgD : 0;
-  const int t_hi = (nD > 0) ? (d1 - 1) / rgD : -1;
-  if (!aborted(ctl)) {
-    for (int t = t_lo + warp; t <= t_hi; t += W) {
-      if (ctl->ids[t] < 0) continue;
-      const float* hv = p.s.hbuf + (size_t)t * fe;
-      float m = 0.f;
-      for (int i = lane; i < fe; i += 32) m = fmaxf(m, fabsf(__ldcg(hv + i)));
+      float am = fabsf(hv);
 #pragma unroll
-      for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      const float sc = pow2_scale(m);
-      if (lane == 0) ctl->hinv[t] = 1.f / sc;
-      build_btab<SD>(hv, fe, sc, htab + (size_t)(t - t_lo) * p.htab_bytes, hsx + (size_t)(t - t_lo) * (fe / 32),
-                     lane, 32, true);
-    }
-  }
-  named_bar(1, W * 32);
-
-  for (int v = nG; v < nU; v++) {
-    const int slot = v % S;
-    bool ok = !aborted(ctl) && mbar_wait(&full[slot], (uint32_t)(v / S) & 1u, &ctl->abort);
-    if (!ok && !aborted(ctl)) do_abort(ctl, p.s.err, VIREO_ERR_TIMEOUT);
-    const int u = d0 + (v - nG), t = u / rgD, rg = u - t * rgD;
-    const bool active = ok && ctl->ids[t] >= 0;
-    float val = 0.f;
-    const bool last = consume<SD>(stages + (size_t)slot * p.stage_bytes, p.sg_d, v, nsegD, warp,
-                                  htab + (size_t)(t - t_lo) * p.htab_bytes, hsx + (size_t)(t - t_lo) * (fe / 32),
-                                  part + slot * W * 16, &ucnt[slot], L, &val, active);
-    if (last && active) {
-      if (lane < 16) p.s.ybuf[(size_t)t * d + 16 * rg + lane] = val * ctl->hinv[t];
-      __syncwarp();
-      unsigned int old = 0;
-      if (lane == 0) {
-        __threadfence();
-        old = atomicAdd(&p.s.tile_cnt[rg], 1u);
-        __threadfence();
-      }
-      old = __shfl_sync(0xffffffffu, old, 0);
-      if ((int)old == ctl->nvalid - 1) {
-        __syncwarp();
-        if (lane < 16) {
-          const int r = 16 * rg + lane;
-          float acc = 0.f;
-          for (int tt = 0; tt < k; tt++)
-            if (ctl->ids[tt] >= 0) acc = __fadd_rn(acc, __fmul_rn(ctl->wts[tt], __ldcg(p.s.ybuf + (size_t)tt * d + r)));
-          p.x[r] = __fadd_rn(p.x[r], acc);
-        }
-        if (lane == 0) atomicExch(&p.s.tile_cnt[rg], 0u);
-      }
+      for (int o = 4; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+      if (lane == 0 && active) atomicMax(reinterpret_cast<unsigned int*>(&ctl->hamax[t]), __float_as_uint(am));
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
+    if (threadIdx.x == 0 && v < kTrUnits) trace(p, kTrUnitBase + 2 * v + 1);
+  }
+  // publish this CTA's gate/up results: one max per expert slot, one count
+  named_bar(1, NC);
+  if (threadIdx.x < k && ctl->hamax[threadIdx.x] > 0.f)
+    atomicMax(&sy->h_amax.v + threadIdx.x, __float_as_uint(ctl->hamax[threadIdx.x]));
+  named_bar(1, NC);
+  if (threadIdx.x == 0) {
+    trace(p, kTrGDone);
+    __threadfence();
+    red_add_release_gpu(&sy->g_done.v, (unsigned)(g1 - g0));
+  }
+
+  if (my_tiles > 0) {
+    // ---- every h row written: build the k down-projection B tables ----------
+    if (threadIdx.x == 0) {
+      if (!aborted(ctl) && !wait_geq(&sy->g_done.v, (unsigned)UG, p.s.err)) ctl->abort = 1;
+      trace(p, kTrGAll);
+    }
+    named_bar(1, NC);
+    if (!aborted(ctl)) {
+      float* hscale = stg;  // x staging is free by now
+      if (threadIdx.x < k) {
+        const float am = __uint_as_float(__ldcg(&sy->h_amax.v + threadIdx.x));
+        hscale[threadIdx.x] = pow2_scale(am);
+        ctl->hinv[threadIdx.x] = 1.f / hscale[threadIdx.x];
+      }
+      named_bar(1, NC);
+      if (threadIdx.x == 0) trace(p, kTrDbg + 0);
+      build_btab_experts<SD>(p.s.hbuf, k, fe, hscale, htab, p.htab_bytes, hsx, p.hsx_count, threadIdx.x, NC,
+                             [] { named_bar(1, NC); });
+      if (threadIdx.x == 0) trace(p, kTrDbg + 1);
+    }
+    named_bar(1, NC);
+    if (threadIdx.x == 0) trace(p, kTrHtab);
+
+    // ---- down units: tile-major, combined in this CTA ------------------------
+    for (int i = 0; i < my_tiles; i++) {
+      const int tb = i & 1;
+      for (int t = 0; t < k; t++, v++) {
+        const int slot = v % S;
+        const bool ok = warp_wait(&full[slot], (uint32_t)(v / S) & 1u, ctl, p.s.err);
+        if (threadIdx.x == 0 && v < kTrUnits) trace(p, kTrUnitBase + 2 * v);
+        const int tile = cta + i * G;
+        const bool active = ok && ctl->ids[t] >= 0;
+        float val = 0.f;
+        const bool last = consume<SD>(stages + (size_t)slot * p.stage_bytes, p.sg_d, v, fe / kSegElems, warp,
+                                      htab + (size_t)t * p.htab_bytes, hsx + (size_t)t * p.hsx_count,
+                                      part + slot * p.part_stride, &ucnt[slot], L, &val, active, bf);
+        if (last) {
+          if (lane < 16) ytile[(tb * k + t) * 16 + lane] = active ? val * ctl->hinv[t] : 0.f;
+          __syncwarp();
+          int done = 0;
+          if (lane == 0) {
+            __threadfence_block();
+            done = (atomicAdd(&ctl->tile_cnt[tb], 1) == k - 1);
+          }
+          done = __shfl_sync(0xffffffffu, done, 0);
+          if (done) {
+            __threadfence_block();
+            if (lane < 16 && ok) {
+              // the reference's combine order: acc = sum over rank t of w_t * y_t, then x += acc
+              const int r = 16 * tile + lane;
+              float acc = 0.f;
+              for (int tt = 0; tt < k; tt++)
+                if (ctl->ids[tt] >= 0)
+                  acc = __fadd_rn(acc, __fmul_rn(ctl->wts[tt], ((volatile float*)ytile)[(tb * k + tt) * 16 + lane]));
+              p.x[r] = __fadd_rn(p.x[r], acc);
+            }
+            __syncwarp();
+            if (lane == 0) ctl->tile_cnt[tb] = 0;
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (threadIdx.x == 0 && v < kTrUnits) trace(p, kTrUnitBase + 2 * v + 1);
+      }
+    }
+  }
+  if (threadIdx.x == 0) trace(p, kTrDDone);
+
+  // ---- launch exit: the last CTA out resets the per-launch words -------------
+  named_bar(1, NC);
+  if (threadIdx.x == 0) {
+    if (atom_add_acq_rel_gpu(&sy->exit_cnt.v, 1u) == (unsigned)G - 1u) {
+      sy->router_arrive.v = 0u;
+      sy->g_done.v = 0u;
+      for (int t = 0; t < k; t++) (&sy->h_amax.v)[t] = 0u;
+      __threadfence();
+      sy->exit_cnt.v = 0u;
+    }
   }
 }
 
@@ -353,11 +481,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) gemv_kernel(const __grid_co
   uint8_t* stages = smem + p.off_stage;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int W = kConsumerWarps;
+  constexpr int NC = W * 32;
   const int S = p.nstages;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; s++) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], kProducerThreads);
       mbar_init(&empty[s], W);
     }
     ctl->abort = 0;
@@ -367,54 +496,53 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) gemv_kernel(const __grid_co
   const int U = p.d / 16;
   const int u0 = (int)((long long)blockIdx.x * U / gridDim.x), u1 = (int)((long long)(blockIdx.x + 1) * U / gridDim.x);
   const int nU = u1 - u0, nseg = p.n / kSegElems;
+  pdl_launch_dependents();
+  pdl_wait();
   __syncthreads();
 
-  if (warp == W) {
-    if (lane == 0) {
-      int issued = 0;
-      for (int v = 0; v < nU; v++) {
-        if (aborted(ctl)) break;
-        const int slot = v % S;
-        if (!mbar_wait(&empty[slot], (((uint32_t)(v / S)) & 1u) ^ 1u, &ctl->abort)) {
-          do_abort(ctl, p.err, VIREO_ERR_TIMEOUT);
-          break;
-        }
-        const uint8_t* src = p.W + (size_t)(16 * (u0 + v)) * p.sg.rb;
-        issue_unit(stages + (size_t)slot * p.stage_bytes, &full[slot], src, src + 8 * (size_t)p.sg.rb, p.sg);
-        issued = v + 1;
-      }
-      for (int v = (issued > S ? issued - S : 0); v < issued; v++)
-        mbar_wait(&full[v % S], (uint32_t)(v / S) & 1u, &kNeverAbort);
+  if (warp >= W) {
+    const int ptid = threadIdx.x - NC;
+    for (int v = 0; v < nU; v++) {
+      const int slot = v % S;
+      if (!warp_wait(&empty[slot], (((uint32_t)(v / S)) & 1u) ^ 1u, ctl, p.err)) break;
+      const uint8_t* src = p.W + (size_t)(16 * (u0 + v)) * p.sg.rb;
+      issue_unit(stages + (size_t)slot * p.stage_bytes, &full[slot], src, src + 8 * (size_t)p.sg.rb, p.sg, ptid,
+                 kProducerThreads);
     }
+    cp_async_wait_all();
     return;
   }
-  // x table (consumers only; the producer already streams weights)
+  // x table (consumers only; the producers already stream weights)
   {
+    float* xs = reinterpret_cast<float*>(smem + p.off_stg);
+    if (((uintptr_t)p.x & 15) == 0 && (p.n & 3) == 0) {
+      stage_vec(p.x, xs, p.n, threadIdx.x, NC, false);
+    } else {
+      for (int i = threadIdx.x; i < p.n; i += NC) xs[i] = __ldg(p.x + i);
+    }
+    named_bar(1, NC);
     float m = 0.f;
-    for (int i = threadIdx.x; i < p.n; i += W * 32) m = fmaxf(m, fabsf(__ldg(p.x + i)));
+    for (int i = threadIdx.x; i < p.n; i += NC) m = fmaxf(m, fabsf(xs[i]));
 #pragma unroll
     for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if (lane == 0) red[warp] = m;
-    named_bar(1, W * 32);
-    if (threadIdx.x == 0) {
-      float mm = 0.f;
-      for (int i = 0; i < W; i++) mm = fmaxf(mm, red[i]);
-      const float sc = pow2_scale(mm);
-      red[W] = sc;
-      ctl->xinv = 1.f / sc;
-    }
-    named_bar(1, W * 32);
-    build_btab<SF>(p.x, p.n, red[W], xtab, xsx, threadIdx.x, W * 32, false);
-    named_bar(1, W * 32);
+    named_bar(1, NC);
+    float mm = 0.f;
+    for (int i = 0; i < W; i++) mm = fmaxf(mm, red[i]);
+    const float sc = pow2_scale(mm);
+    if (threadIdx.x == 0) ctl->xinv = 1.f / sc;
+    build_btab<SF>(xs, p.n, sc, xtab, xsx, threadIdx.x, NC, false);
+    named_bar(1, NC);
   }
   const LaneCtx L = lane_ctx();
+  BFrag bf;
+  bf.reset();
   for (int v = 0; v < nU; v++) {
     const int slot = v % S;
-    bool ok = !aborted(ctl) && mbar_wait(&full[slot], (uint32_t)(v / S) & 1u, &ctl->abort);
-    if (!ok && !aborted(ctl)) do_abort(ctl, p.err, VIREO_ERR_TIMEOUT);
+    const bool ok = warp_wait(&full[slot], (uint32_t)(v / S) & 1u, ctl, p.err);
     float val = 0.f;
     const bool last = consume<SF>(stages + (size_t)slot * p.stage_bytes, p.sg, v, nseg, warp, xtab, xsx,
-                                  part + slot * W * 16, &ucnt[slot], L, &val, ok);
+                                  part + slot * p.part_stride, &ucnt[slot], L, &val, ok, bf);
     if (last && ok && lane < 16) p.y[16 * (u0 + v) + lane] = val * ctl->xinv;
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
@@ -449,6 +577,12 @@ int stage_geom(uint32_t type, int K, StageGeom* sg) {
   sg->G = G;
   sg->gstride = gbytes + pad;
   sg->hstride = (8u / G) * sg->gstride;
+  // multiply-shift division by gbytes, verified exact over the half's range
+  const uint64_t magic = ((1ull << 32) + gbytes - 1) / gbytes;
+  if (magic > 0xFFFFFFFFull) return VIREO_ERR_UNSUPPORTED;
+  sg->gmagic = (uint32_t)magic;
+  for (uint32_t b = 0; b < 8u * rb; b += 16u)
+    if ((uint32_t)(((uint64_t)b * sg->gmagic) >> 32) != b / gbytes) return VIREO_ERR_UNSUPPORTED;
   return VIREO_OK;
 }
 
@@ -476,27 +610,37 @@ const void* moe_decode_kernel_for(uint32_t gtype, uint32_t dtype) {
 
 // Shared-memory layout for the MoE kernel; picks the deepest stage ring that
 // fits.  Returns the dynamic shared-memory bytes (0 if nothing fits).
-uint32_t moe_decode_layout(MoeDecodeParams* p, uint32_t smem_limit) {
+uint32_t moe_decode_layout(MoeDecodeParams* p, uint32_t smem_limit, int grid) {
+  (void)grid;
   const int W = kConsumerWarps;
   const uint32_t stage = up_to(std::max(2u * p->sg_gu.hstride, 2u * p->sg_d.hstride), 128u);
   p->stage_bytes = stage;
   p->htab_bytes = (uint32_t)(4 * p->fe);
+  const uint32_t htab_region = std::max((uint32_t)p->k * p->htab_bytes, (uint32_t)(4 * p->ne));
+  const uint32_t stg_bytes = (uint32_t)std::max(4 * p->d, 4 * p->k);
+  p->part_stride = (uint32_t)std::max(W, std::max(p->d, p->fe) / kSegElems) * 16u;
   for (int S = kMaxStages; S >= 2; S--) {
     uint32_t off = 2u * kMaxStages * 8u;
     p->off_ctl = off;
     off = up_to(off + (uint32_t)sizeof(Ctl), 16);
     p->off_part = off;
-    off = up_to(off + (uint32_t)(S * W * 16 * 4), 16);
+    off = up_to(off + (uint32_t)S * p->part_stride * 4u, 16);
     p->off_ucnt = off;
     off = up_to(off + (uint32_t)(S * 4), 16);
+    p->off_unit = off;
+    off = up_to(off + (uint32_t)(S * 4), 16);
+    p->off_ytile = off;
+    off = up_to(off + (uint32_t)(2 * p->k * 16 * 4), 16);
     p->off_xtab = off;
     off = up_to(off + (uint32_t)(4 * p->d), 16);
     p->off_xsx = off;
-    off = up_to(off + (uint32_t)(p->d / 32 * 4), 16);
+    off = up_to(off + (uint32_t)(p->d / 16 * 4), 16);
     p->off_htab = off;
-    off = up_to(off + (uint32_t)p->k * p->htab_bytes, 16);
+    off = up_to(off + htab_region, 16);
     p->off_hsx = off;
-    off = up_to(off + (uint32_t)(p->k * (p->fe / 32) * 4), 128);
+    off = up_to(off + (uint32_t)(p->k * (p->fe / 16) * 4), 16);
+    p->off_stg = off;
+    off = up_to(off + stg_bytes, 128);
     p->off_stage = off;
     off += (uint32_t)S * stage + 16;
     if (off <= smem_limit) {
@@ -518,18 +662,21 @@ uint32_t gemv_layout(GemvParams* p, uint32_t smem_limit) {
   const int W = kConsumerWarps;
   const uint32_t stage = up_to(2u * p->sg.hstride, 128u);
   p->stage_bytes = stage;
+  p->part_stride = (uint32_t)std::max(W, p->n / kSegElems) * 16u;
   for (int S = kMaxStages; S >= 2; S--) {
     uint32_t off = 2u * kMaxStages * 8u;
     p->off_ctl = off;
     off = up_to(off + (uint32_t)sizeof(Ctl), 16);
     p->off_part = off;
-    off = up_to(off + (uint32_t)(S * W * 16 * 4), 16);
+    off = up_to(off + (uint32_t)S * p->part_stride * 4u, 16);
     p->off_ucnt = off;
     off = up_to(off + (uint32_t)(S * 4), 16);
     p->off_xtab = off;
     off = up_to(off + (uint32_t)(4 * p->n), 16);
     p->off_xsx = off;
-    off = up_to(off + (uint32_t)(p->n / 32 * 4), 128);
+    off = up_to(off + (uint32_t)(p->n / 16 * 4), 16);
+    p->off_stg = off;
+    off = up_to(off + (uint32_t)(4 * p->n), 128);
     p->off_stage = off;
     off += (uint32_t)S * stage + 16;
     if (off <= smem_limit) {

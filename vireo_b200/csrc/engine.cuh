@@ -28,9 +28,10 @@ constexpr int kMaxStages = 16;
 
 struct StageGeom {
   uint32_t rb;       // bytes per weight row
-  uint32_t G;        // rows per bulk copy (1, 2, 4 or 8)
+  uint32_t G;        // rows per copy group (1, 2, 4 or 8)
   uint32_t gstride;  // smem bytes between copy groups inside a half
   uint32_t hstride;  // smem bytes from half 0 to half 1
+  uint32_t gmagic;   // floor(b / (G * rb)) == (b * gmagic) >> 32 for b < 8 * rb
 };
 
 VDEV const uint8_t* stage_row(const uint8_t* stage, const StageGeom& sg, int r) {
@@ -38,14 +39,30 @@ VDEV const uint8_t* stage_row(const uint8_t* stage, const StageGeom& sg, int r) 
   return stage + h * sg.hstride + (r8 / (int)sg.G) * sg.gstride + (r8 % (int)sg.G) * sg.rb;
 }
 
-// Producer side: one thread issues the copies of a unit into a stage.
+// Producer side: nprod threads (ptid = 0..nprod-1) copy a unit into a stage
+// in 16-byte pieces and each arrives on the stage's full barrier (expected
+// count nprod) once its pieces have landed.  A null src0 issues nothing
+// (the unit is skipped) but still arrives.
+// Each half (8 rows, contiguous in global memory) is walked as one flat
+// byte range so that consecutive lanes copy consecutive 16-byte pieces; the
+// destination of a piece is its copy group's padded slot, found with a
+// multiply-shift division.
 VDEV void issue_unit(uint8_t* stage, uint64_t* full, const uint8_t* src0, const uint8_t* src1,
-                     const StageGeom& sg) {
-  mbar_arrive_expect_tx(full, 16u * sg.rb);
-  const uint32_t groups = 8u / sg.G, gbytes = sg.G * sg.rb;
-  for (uint32_t j = 0; j < groups; j++) bulk_g2s(stage + j * sg.gstride, src0 + j * gbytes, gbytes, full);
-  for (uint32_t j = 0; j < groups; j++)
-    bulk_g2s(stage + sg.hstride + j * sg.gstride, src1 + j * gbytes, gbytes, full);
+                     const StageGeom& sg, int ptid, int nprod) {
+  if (src0) {
+    const uint32_t gbytes = sg.G * sg.rb;  // bytes per copy group (multiple of 16)
+    const uint32_t hbytes = 8u * sg.rb;
+#pragma unroll
+    for (uint32_t h = 0; h < 2; h++) {
+      const uint8_t* hs = h ? src1 : src0;
+      uint8_t* hd = stage + h * sg.hstride;
+      for (uint32_t b = 16u * (uint32_t)ptid; b < hbytes; b += 16u * (uint32_t)nprod) {
+        const uint32_t j = __umulhi(b, sg.gmagic);
+        cp_async16(hd + j * sg.gstride + (b - j * gbytes), hs + b);
+      }
+    }
+  }
+  cp_async_arrive(full);
 }
 
 struct LaneCtx {
@@ -80,78 +97,76 @@ VDEV uint32_t h2_splat(float v) {
 // 16 bytes from a 2-byte-aligned shared address, as four words.
 VDEV void ld16u(const uint8_t* p, uint32_t (&w)[4]) {
   uint32_t a = smem_addr(p);
-  uint32_t a4 = a & ~3u, sh = (a & 2u) << 3;
-  uint32_t x0, x1, x2, x3, x4;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(x0) : "r"(a4));
-  asm volatile("ld.shared.u32 %0, [%1+4];" : "=r"(x1) : "r"(a4));
-  asm volatile("ld.shared.u32 %0, [%1+8];" : "=r"(x2) : "r"(a4));
-  asm volatile("ld.shared.u32 %0, [%1+12];" : "=r"(x3) : "r"(a4));
-  asm volatile("ld.shared.u32 %0, [%1+16];" : "=r"(x4) : "r"(a4));
+  uint32_t sh = (a & 2u) << 3;
+  const uint32_t* q = reinterpret_cast<const uint32_t*>(p - (a & 3u));
+  const uint32_t x0 = q[0], x1 = q[1], x2 = q[2], x3 = q[3], x4 = q[4];
   w[0] = __funnelshift_r(x0, x1, sh);
   w[1] = __funnelshift_r(x1, x2, sh);
   w[2] = __funnelshift_r(x2, x3, sh);
   w[3] = __funnelshift_r(x3, x4, sh);
 }
-VDEV int lds_s8(const void* p) {
-  int v;
-  asm volatile("ld.shared.s8 %0, [%1];" : "=r"(v) : "r"(smem_addr(p)));
-  return v;
-}
-VDEV uint32_t lds_u16(const void* p) {
-  uint32_t v;
-  asm volatile("ld.shared.u16 %0, [%1];" : "=r"(v) : "r"(smem_addr(p)));
-  return v;
-}
+VDEV int lds_s8(const void* p) { return *reinterpret_cast<const int8_t*>(p); }
+VDEV uint32_t lds_u16(const void* p) { return *reinterpret_cast<const uint16_t*>(p); }
+
+// ---------------------------------------------------------------------------
+// B fragments of one segment held in registers (16 steps x 2 regs); a warp
+// that meets the same segment of the same table again (consecutive units
+// whose segment index lands on the same warp) skips the reload.
+// ---------------------------------------------------------------------------
+struct BFrag {
+  uint32_t b[16][2];
+  const uint8_t* key;
+  VDEV void reset() { key = nullptr; }
+  VDEV void get(const uint8_t* segtab, const LaneCtx& L) {
+    if (segtab == key) return;
+    key = segtab;
+#pragma unroll
+    for (int s = 0; s < 16; s++) {
+      const uint2 v = lds64(segtab + s * kStepBytesB + L.boff);
+      b[s][0] = L.bon ? v.x : 0u;
+      b[s][1] = L.bon ? v.y : 0u;
+    }
+  }
+};
 
 // ---------------------------------------------------------------------------
 // Segment kernels: accumulate one 256-value segment of rows g (r0) and g+8
-// (r1) into this lane's fp32 totals.  btab: the segment's B table
-// (16 steps x 64 B); sx: the segment's 8 sub-block sums (Q4_K only).
+// (r1) into this lane's fp32 totals.  B: the segment's fragments; sx: the
+// segment's 8 sub-block sums (Q4_K only).  Each kernel runs two independent
+// accumulator chains so consecutive tensor-core ops do not wait on each
+// other.
 // ---------------------------------------------------------------------------
 struct SegQ8 : Q8 {
-  VDEV static void run(const uint8_t* r0, const uint8_t* r1, const uint8_t* btab, const float* sx,
-                       const LaneCtx& L, float& tot0, float& tot1) {
-    (void)sx;
+  VDEV static void run(const uint8_t* r0, const uint8_t* r1, const BFrag& B, const float* sx, const LaneCtx& L,
+                       float& tot0, float& tot1) {
     const uint8_t* p0 = r0 + 68 * L.t;
     const uint8_t* p1 = r1 + 68 * L.t;
     const uint32_t w0a = lds32(p0), w8a = lds32(p0 + 32), w0b = lds32(p1), w8b = lds32(p1 + 32);
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    float ca[4] = {0.f, 0.f, 0.f, 0.f}, cb[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int s = 0; s < 8; s++) {
-      uint32_t wa = (s < 7) ? lds32(p0 + 4 + 4 * s) : byte_perm(w0a, w8a, 0x5432u);
-      uint32_t wb = (s < 7) ? lds32(p1 + 4 + 4 * s) : byte_perm(w0b, w8b, 0x5432u);
-      uint32_t a[4];
+      // block A (steps 0..7) and block B (steps 8..15) interleaved
+      const uint32_t wa = (s < 7) ? lds32(p0 + 4 + 4 * s) : byte_perm(w0a, w8a, 0x5432u);
+      const uint32_t wb = (s < 7) ? lds32(p1 + 4 + 4 * s) : byte_perm(w0b, w8b, 0x5432u);
+      const uint32_t xa = lds32(p0 + 36 + 4 * s), xb = lds32(p1 + 36 + 4 * s);
+      uint32_t a[4], e[4];
       conv(wa, a[0], a[2]);
       conv(wb, a[1], a[3]);
-#pragma unroll
-      for (int i = 0; i < 4; i++) a[i] = h2_sub(a[i], kBias);
-      uint32_t b0, b1;
-      bload(btab, s, L, b0, b1);
-      mma_16816(c, a, b0, b1);
+      conv(xa, e[0], e[2]);
+      conv(xb, e[1], e[3]);
+      mma_16816(ca, a, B.b[s][0], B.b[s][1]);
+      mma_16816(cb, e, B.b[8 + s][0], B.b[8 + s][1]);
     }
-    tot0 += h_lo(w0a) * (c[0] + c[1]);
-    tot1 += h_lo(w0b) * (c[2] + c[3]);
-    c[0] = c[1] = c[2] = c[3] = 0.f;
-#pragma unroll
-    for (int s = 0; s < 8; s++) {
-      uint32_t wa = lds32(p0 + 36 + 4 * s), wb = lds32(p1 + 36 + 4 * s);
-      uint32_t a[4];
-      conv(wa, a[0], a[2]);
-      conv(wb, a[1], a[3]);
-#pragma unroll
-      for (int i = 0; i < 4; i++) a[i] = h2_sub(a[i], kBias);
-      uint32_t b0, b1;
-      bload(btab, 8 + s, L, b0, b1);
-      mma_16816(c, a, b0, b1);
-    }
-    tot0 += h_hi(w8a) * (c[0] + c[1]);
-    tot1 += h_hi(w8b) * (c[2] + c[3]);
+    // the halves hold 1152 + q: remove 1152 * (sum of x over the block)
+    const float oa = kOffset * sx[2 * L.t], ob = kOffset * sx[2 * L.t + 1];
+    tot0 += h_lo(w0a) * ((ca[0] + ca[1]) - oa) + h_hi(w8a) * ((cb[0] + cb[1]) - ob);
+    tot1 += h_lo(w0b) * ((ca[2] + ca[3]) - oa) + h_hi(w8b) * ((cb[2] + cb[3]) - ob);
   }
 };
 
 struct SegQ4K : Q4K {
-  VDEV static void run(const uint8_t* r0, const uint8_t* r1, const uint8_t* btab, const float* sx,
-                       const LaneCtx& L, float& tot0, float& tot1) {
+  VDEV static void run(const uint8_t* r0, const uint8_t* r1, const BFrag& B, const float* sx, const LaneCtx& L,
+                       float& tot0, float& tot1) {
     const uint4 hd0 = lds128(r0), hd1 = lds128(r1);
     const int j0 = 2 * L.t, j1 = 2 * L.t + 1;
     uint32_t sc00, mn00, sc01, mn01, sc10, mn10, sc11, mn11;
@@ -169,65 +184,70 @@ struct SegQ4K : Q4K {
     const uint4 qb0 = lds128(r1 + 16 + 32 * L.t), qb1 = lds128(r1 + 32 + 32 * L.t);
     const uint32_t wa[8] = {qa0.x, qa0.y, qa0.z, qa0.w, qa1.x, qa1.y, qa1.z, qa1.w};
     const uint32_t wb[8] = {qb0.x, qb0.y, qb0.z, qb0.w, qb1.x, qb1.y, qb1.z, qb1.w};
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    float cl[4] = {0.f, 0.f, 0.f, 0.f}, ch[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int i = 0; i < 8; i++) {
-      uint32_t a[4], t02, t13, b0, b1;
+      uint32_t a[4], e[4], t02, t13;
       conv_lo(wa[i], t02, t13);
       a[0] = h2_fma(t02, SL0, CL0);
       a[2] = h2_fma(t13, SL0, CL0);
       conv_lo(wb[i], t02, t13);
       a[1] = h2_fma(t02, SL1, CL1);
       a[3] = h2_fma(t13, SL1, CL1);
-      bload(btab, 2 * i, L, b0, b1);
-      mma_16816(c, a, b0, b1);
       conv_hi(wa[i], t02, t13);
-      a[0] = h2_fma(t02, SH0, CH0);
-      a[2] = h2_fma(t13, SH0, CH0);
+      e[0] = h2_fma(t02, SH0, CH0);
+      e[2] = h2_fma(t13, SH0, CH0);
       conv_hi(wb[i], t02, t13);
-      a[1] = h2_fma(t02, SH1, CH1);
-      a[3] = h2_fma(t13, SH1, CH1);
-      bload(btab, 2 * i + 1, L, b0, b1);
-      mma_16816(c, a, b0, b1);
+      e[1] = h2_fma(t02, SH1, CH1);
+      e[3] = h2_fma(t13, SH1, CH1);
+      mma_16816(cl, a, B.b[2 * i][0], B.b[2 * i][1]);
+      mma_16816(ch, e, B.b[2 * i + 1][0], B.b[2 * i + 1][1]);
     }
     const float sxa = sx[j0], sxb = sx[j1];
     const float mt0 = (float)mn00 * sxa + (float)mn01 * sxb;
     const float mt1 = (float)mn10 * sxa + (float)mn11 * sxb;
-    tot0 += h_lo(hd0.x) * (c[0] + c[1]) - h_hi(hd0.x) * mt0;
-    tot1 += h_lo(hd1.x) * (c[2] + c[3]) - h_hi(hd1.x) * mt1;
+    tot0 += h_lo(hd0.x) * ((cl[0] + cl[1]) + (ch[0] + ch[1])) - h_hi(hd0.x) * mt0;
+    tot1 += h_lo(hd1.x) * ((cl[2] + cl[3]) + (ch[2] + ch[3])) - h_hi(hd1.x) * mt1;
   }
 };
 
 struct SegQ6K : Q6K {
-  VDEV static void run(const uint8_t* r0, const uint8_t* r1, const uint8_t* btab, const float* sx,
-                       const LaneCtx& L, float& tot0, float& tot1) {
-    (void)sx;
+  VDEV static void run(const uint8_t* r0, const uint8_t* r1, const BFrag& B, const float* sx, const LaneCtx& L,
+                       float& tot0, float& tot1) {
     const float d0 = __half2float(__ushort_as_half((unsigned short)lds_u16(r0 + 208)));
     const float d1 = __half2float(__ushort_as_half((unsigned short)lds_u16(r1 + 208)));
     const int qlo = 32 * (L.t & 1);
 #pragma unroll
-    for (int m = 0; m < 4; m++) {
-      const int h = m >> 1, l0 = 16 * (m & 1);
-      uint32_t la[4], ha[4], lb[4], hb[4];
-      ld16u(r0 + 64 * h + qlo + l0, la);
-      ld16u(r0 + 128 + 32 * h + l0, ha);
-      ld16u(r1 + 64 * h + qlo + l0, lb);
-      ld16u(r1 + 128 + 32 * h + l0, hb);
-      float c[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int mp = 0; mp < 4; mp += 2) {
+      // macro-steps mp (l0 = 0) and mp + 1 (l0 = 16) of half h in two chains
+      const int h = mp >> 1;
+      uint32_t la[8], ha[8], lb[8], hb[8];
+      ld16u(r0 + 64 * h + qlo, *reinterpret_cast<uint32_t(*)[4]>(la));
+      ld16u(r0 + 64 * h + qlo + 16, *reinterpret_cast<uint32_t(*)[4]>(la + 4));
+      ld16u(r0 + 128 + 32 * h, *reinterpret_cast<uint32_t(*)[4]>(ha));
+      ld16u(r0 + 128 + 32 * h + 16, *reinterpret_cast<uint32_t(*)[4]>(ha + 4));
+      ld16u(r1 + 64 * h + qlo, *reinterpret_cast<uint32_t(*)[4]>(lb));
+      ld16u(r1 + 64 * h + qlo + 16, *reinterpret_cast<uint32_t(*)[4]>(lb + 4));
+      ld16u(r1 + 128 + 32 * h, *reinterpret_cast<uint32_t(*)[4]>(hb));
+      ld16u(r1 + 128 + 32 * h + 16, *reinterpret_cast<uint32_t(*)[4]>(hb + 4));
+      float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int s = 0; s < 4; s++) {
-        uint32_t a[4], b0, b1;
+        uint32_t a[4], e[4];
         conv(six(la[s], ha[s], L.t), a[0], a[2]);
         conv(six(lb[s], hb[s], L.t), a[1], a[3]);
-#pragma unroll
-        for (int i = 0; i < 4; i++) a[i] = h2_sub(a[i], kBias);
-        bload(btab, 4 * m + s, L, b0, b1);
-        mma_16816(c, a, b0, b1);
+        conv(six(la[4 + s], ha[4 + s], L.t), e[0], e[2]);
+        conv(six(lb[4 + s], hb[4 + s], L.t), e[1], e[3]);
+        mma_16816(c0, a, B.b[4 * mp + s][0], B.b[4 * mp + s][1]);
+        mma_16816(c1, e, B.b[4 * mp + 4 + s][0], B.b[4 * mp + 4 + s][1]);
       }
-      const int sidx = 192 + 8 * h + 2 * L.t + (m & 1);
-      const float s0 = (float)lds_s8(r0 + sidx), s1 = (float)lds_s8(r1 + sidx);
-      tot0 += (d0 * s0) * (c[0] + c[1]);
-      tot1 += (d1 * s1) * (c[2] + c[3]);
+      const int gi = 8 * h + 2 * L.t;  // scale group of chain 0 (chain 1: gi + 1)
+      const float s00 = (float)lds_s8(r0 + 192 + gi), s01 = (float)lds_s8(r0 + 193 + gi);
+      const float s10 = (float)lds_s8(r1 + 192 + gi), s11 = (float)lds_s8(r1 + 193 + gi);
+      // the halves hold 1024 + z = (z - 32) + 1056: remove 1056 * group sum
+      const float o0 = kOffset * sx[gi], o1 = kOffset * sx[gi + 1];
+      tot0 += (d0 * s00) * ((c0[0] + c0[1]) - o0) + (d0 * s01) * ((c1[0] + c1[1]) - o1);
+      tot1 += (d1 * s10) * ((c0[2] + c0[3]) - o0) + (d1 * s11) * ((c1[2] + c1[3]) - o1);
     }
   }
 };
@@ -248,6 +268,24 @@ VDEV float pow2_scale(float amax) {
   return ldexpf(1.f, e);
 }
 
+// Sums of (x_hi + x_lo) of scale * v over consecutive groups of GS (16 or
+// 32) values; warp-cooperative, tid/nthr whole warps.
+template <int GS>
+VDEV void group_sums(const float* v, int K, float scale, float* sx, int tid, int nthr, bool from_global) {
+  const int lane = tid & 31, nw = nthr >> 5;
+  constexpr int GPW = 32 / GS;  // groups per warp pass
+  for (int g0 = (tid >> 5) * GPW; g0 < K / GS; g0 += nw * GPW) {
+    const int idx = g0 * GS + lane;
+    float x = 0.f;
+    if (idx < K) x = (from_global ? __ldcg(v + idx) : v[idx]) * scale;
+    const float hi = __half2float(__float2half_rn(x));
+    float s = hi + __half2float(__float2half_rn(x - hi));
+#pragma unroll
+    for (int o = GS / 2; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((lane % GS) == 0 && g0 + lane / GS < K / GS) sx[g0 + lane / GS] = s;
+  }
+}
+
 // Block-cooperative (threads tid in [0, nthr)).  v may be global or shared.
 template <class F>
 VDEV void build_btab(const float* v, int K, float scale, uint8_t* tab, float* sx, int tid, int nthr,
@@ -263,40 +301,106 @@ VDEV void build_btab(const float* v, int K, float scale, uint8_t* tab, float* sx
     *reinterpret_cast<__half*>(dst) = hi;
     *reinterpret_cast<__half*>(dst + 8) = lo;
   }
-  if (F::kNeedsSubSums) {
-    for (int i = tid; i < K / 32; i += nthr) {
-      float s = 0.f;
-      for (int l = 0; l < 32; l++) s += (from_global ? __ldcg(v + 32 * i + l) : v[32 * i + l]) * scale;
-      sx[i] = s;
+  // sums of the scaled x over each group of F::kSumGroup values (the offset
+  // and min corrections), each the fp32 sum of x_hi + x_lo; one group per
+  // warp (or half-warp) with consecutive lanes on consecutive values
+  group_sums<F::kSumGroup>(v, K, scale, sx, tid, nthr, from_global);
+}
+
+// B tables of k vectors at once (the k experts' SwiGLU outputs h, fp32 in
+// global memory, fe values each; scale[t] the power-of-two scale of vector
+// t).  Block-cooperative over nthr threads (whole warps, fe % nthr == 0).
+// The h rows are first copied with coalesced 16-byte loads into the table
+// area itself (k * 4 * fe bytes, the same size as the tables), the group
+// sums are taken there warp-cooperatively, every thread then gathers the
+// values of its table slots into registers, and after a barrier the f16
+// hi/lo pairs are written over the staging copy.  bar(): the caller's
+// barrier over the same nthr threads.
+template <class F, class Bar>
+VDEV void build_btab_experts(const float* hbuf, int k, int fe, const float* scale, uint8_t* tabs, uint32_t tab_bytes,
+                             float* sxs, uint32_t sx_count, int tid, int nthr, Bar bar) {
+  float* raw = reinterpret_cast<float*>(tabs);
+  {
+    const float4* src = reinterpret_cast<const float4*>(hbuf);
+    float4* dst = reinterpret_cast<float4*>(raw);
+    const int n4 = k * fe / 4;
+    for (int i0 = tid; i0 < n4; i0 += 8 * nthr) {
+      float4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; j++)
+        if (i0 + j * nthr < n4) v[j] = __ldcg(src + i0 + j * nthr);
+#pragma unroll
+      for (int j = 0; j < 8; j++)
+        if (i0 + j * nthr < n4) dst[i0 + j * nthr] = v[j];
+    }
+  }
+  bar();
+  for (int t = 0; t < k; t++)
+    group_sums<F::kSumGroup>(raw + (size_t)t * fe, fe, scale[t], sxs + (size_t)t * sx_count, tid, nthr, false);
+  // gather the values of this thread's slots (slot i of expert t holds
+  // element seg*256 + elem(step, tt, jq) of that expert)
+  const int fq = fe / nthr, nj = k * fq;
+  constexpr int kMaxSlots = 32;
+  float xv[kMaxSlots];
+  uint32_t off[kMaxSlots];
+  {
+    int t = 0, rem = 0;
+#pragma unroll
+    for (int j = 0; j < kMaxSlots; j++) {
+      if (j < nj) {
+        const int i = rem * nthr + tid;
+        const int seg = i >> 8, r8 = i & 255, step = r8 >> 4, tt = (r8 >> 2) & 3, jq = r8 & 3;
+        const int e = seg * kSegElems + F::elem(step, tt, jq);
+        xv[j] = raw[(size_t)t * fe + e] * scale[t];
+        off[j] = (uint32_t)t * tab_bytes + seg * (16 * kStepBytesB) + step * kStepBytesB + tt * 16 + jq * 2;
+        if (++rem == fq) {
+          rem = 0;
+          ++t;
+        }
+      }
+    }
+  }
+  bar();
+#pragma unroll
+  for (int j = 0; j < kMaxSlots; j++) {
+    if (j < nj) {
+      const __half hi = __float2half_rn(xv[j]);
+      const __half lo = __float2half_rn(xv[j] - __half2float(hi));
+      *reinterpret_cast<__half*>(tabs + off[j]) = hi;
+      *reinterpret_cast<__half*>(tabs + off[j] + 8) = lo;
     }
   }
 }
 
 // ---------------------------------------------------------------------------
-// Consumer side of one unit for warp w: run this warp's segments, reduce
-// over the 4 lanes of a row, publish the 16-row partial, and return true in
-// the warp that completes the unit (which then owns the epilogue with the
-// summed rows in lanes 0..15 via *row_val).
+// Consumer side of one unit for warp w: run this warp's segments, reduce each
+// over the 4 lanes of a row, publish one 16-row partial per segment, and
+// return true in the warp that completes the unit, which sums the segment
+// partials in segment order (so the result does not depend on which warp
+// computed which segment) into *row_val (lanes 0..15).
+// part: [max(nseg, W)][16] floats for this stage.
 // ---------------------------------------------------------------------------
 template <class S>
 VDEV bool consume_unit(const uint8_t* stage, const StageGeom& sg, int v, int nseg, int W, int w,
-                       const uint8_t* btab, const float* sx, float* part /*[W][16]*/, int* ucnt,
-                       const LaneCtx& L, float* row_val) {
+                       const uint8_t* btab, const float* sx, float* part, int* ucnt, const LaneCtx& L,
+                       float* row_val, BFrag& bf) {
   const uint8_t* r0 = stage_row(stage, sg, L.g);
   const uint8_t* r1 = stage_row(stage, sg, L.g + 8);
-  float tot0 = 0.f, tot1 = 0.f;
   int first = (w - (v * nseg) % W) % W;
   if (first < 0) first += W;
-  for (int seg = first; seg < nseg; seg += W)
-    S::run(r0 + seg * S::kSegBytes, r1 + seg * S::kSegBytes, btab + seg * (16 * kStepBytesB), sx + seg * 8,
-           L, tot0, tot1);
-  tot0 += __shfl_xor_sync(0xffffffffu, tot0, 1);
-  tot1 += __shfl_xor_sync(0xffffffffu, tot1, 1);
-  tot0 += __shfl_xor_sync(0xffffffffu, tot0, 2);
-  tot1 += __shfl_xor_sync(0xffffffffu, tot1, 2);
-  if (L.t == 0) {
-    part[w * 16 + L.g] = tot0;
-    part[w * 16 + L.g + 8] = tot1;
+  for (int seg = first; seg < nseg; seg += W) {
+    float tot0 = 0.f, tot1 = 0.f;
+    bf.get(btab + seg * (16 * kStepBytesB), L);
+    S::run(r0 + seg * S::kSegBytes, r1 + seg * S::kSegBytes, bf, sx + seg * (kSegElems / S::kSumGroup), L, tot0,
+           tot1);
+    tot0 += __shfl_xor_sync(0xffffffffu, tot0, 1);
+    tot1 += __shfl_xor_sync(0xffffffffu, tot1, 1);
+    tot0 += __shfl_xor_sync(0xffffffffu, tot0, 2);
+    tot1 += __shfl_xor_sync(0xffffffffu, tot1, 2);
+    if (L.t == 0) {
+      part[seg * 16 + L.g] = tot0;
+      part[seg * 16 + L.g + 8] = tot1;
+    }
   }
   __syncwarp();
   int last = 0;
@@ -309,7 +413,7 @@ VDEV bool consume_unit(const uint8_t* stage, const StageGeom& sg, int v, int nse
     __threadfence_block();
     float acc = 0.f;
     if (L.lane < 16)
-      for (int ww = 0; ww < W; ww++) acc += ((volatile float*)part)[ww * 16 + L.lane];
+      for (int seg = 0; seg < nseg; seg++) acc += ((volatile float*)part)[seg * 16 + L.lane];
     *row_val = acc;
     __syncwarp();
     if (L.lane == 0) *ucnt = 0;

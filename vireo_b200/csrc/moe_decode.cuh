@@ -25,16 +25,31 @@
 namespace vireo {
 
 constexpr int kConsumerWarps = 8;
-constexpr int kDecodeThreads = 32 * (kConsumerWarps + 1);
+constexpr int kProducerWarps = 4;  // issue the 16-byte cp.async weight copies
+constexpr int kProducerThreads = 32 * kProducerWarps;
+constexpr int kDecodeThreads = 32 * (kConsumerWarps + kProducerWarps);
 constexpr int kRouterChunk = 512;
 constexpr int kMaxTopK = 64;
 
+// Per-launch synchronisation words in device scratch.  All start at zero;
+// the last CTA to leave a launch puts them back to zero.
+// Each word sits on its own 256-byte line: words that many CTAs update must
+// not share an L2 line, or their atomics queue behind one another.
+struct alignas(256) SyncWord {
+  unsigned int v;
+  unsigned int pad[63];
+};
+struct MoeSync {
+  SyncWord router_arrive;  // CTAs done with their router partials
+  SyncWord g_done;         // gate/up units finished (added once per CTA)
+  SyncWord exit_cnt;       // CTAs done with the launch
+  SyncWord h_amax;         // [kMaxTopK] max |h| per expert slot (float bits), one atomic per CTA and slot
+};
+
 struct MoeScratch {
-  float* logit_part;       // [d/512][ne]
-  float* hbuf;             // [k][fe]
-  float* ybuf;             // [k][d]
-  unsigned int* tile_cnt;  // [d/16]
-  GridSync* gsync;
+  float* logit_part;  // [d/512][ne]
+  float* hbuf;        // [k][fe]
+  MoeSync* sync;
   int* err;
 };
 
@@ -51,8 +66,20 @@ struct MoeDecodeParams {
   uint32_t stage_bytes;
   int nstages;
   // shared-memory offsets (bytes)
-  uint32_t off_part, off_ucnt, off_ctl, off_xtab, off_xsx, off_htab, off_hsx, off_stage;
+  uint32_t off_part, off_ucnt, off_unit, off_ytile, off_ctl, off_xtab, off_xsx, off_htab, off_hsx, off_stg,
+      off_stage;
   uint32_t htab_bytes;  // per expert table bytes
+  uint32_t hsx_count;   // per expert group sums
+  uint32_t part_stride; // floats of segment partials per stage
+  unsigned long long* trace;  // optional: kTraceSlots %globaltimer stamps per CTA
+};
+
+// phase trace slots (per CTA): consumer thread 0 and producer thread 0
+enum TraceSlot {
+  kTrStart = 0, kTrRouterDone, kTrPartials, kTrRouted, kTrGDone, kTrGAll, kTrHtab, kTrDDone,
+  kTrProdFirst, kTrProdFirstD, kTrProdLast, kTrProdDrained,
+  kTrUnitBase = 16,  // per-unit stamps for the first kTrUnits units: ready, done
+  kTrUnits = 24, kTrDbg = 64, kTraceSlots = 72
 };
 
 struct GemvParams {
@@ -63,7 +90,8 @@ struct GemvParams {
   StageGeom sg;
   uint32_t stage_bytes;
   int nstages;
-  uint32_t off_part, off_ucnt, off_ctl, off_xtab, off_xsx, off_stage;
+  uint32_t off_part, off_ucnt, off_ctl, off_xtab, off_xsx, off_stg, off_stage;
+  uint32_t part_stride;
   int* err;
 };
 

@@ -45,6 +45,25 @@ constexpr int kStepBytesB = 64; // B table bytes per k16 step: [t][hi,lo][4 x f1
 VHD int kperm(int j) { return (j == 0) ? 0 : (j == 1) ? 2 : (j == 2) ? 1 : 3; }
 
 // ---- portable bit helpers (host versions for the self-test) --------------
+// 3-input bitwise function with lookup table lut (a, b, c <-> 0xF0, 0xCC, 0xAA)
+#ifdef __CUDA_ARCH__
+template <uint32_t LUT>
+__device__ __forceinline__ uint32_t lop3t(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, %4;" : "=r"(d) : "r"(a), "r"(b), "r"(c), "n"(LUT));
+  return d;
+}
+#else
+template <uint32_t LUT>
+inline uint32_t lop3t(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d = 0;
+  for (int i = 0; i < 32; i++) {
+    uint32_t idx = (((a >> i) & 1u) << 2) | (((b >> i) & 1u) << 1) | ((c >> i) & 1u);
+    d |= ((LUT >> idx) & 1u) << i;
+  }
+  return d;
+}
+#endif
 VHD uint32_t byte_perm(uint32_t a, uint32_t b, uint32_t s) {
 #ifdef __CUDA_ARCH__
   return __byte_perm(a, b, s);
@@ -69,21 +88,22 @@ VHD uint32_t byte_perm(uint32_t a, uint32_t b, uint32_t s) {
 struct Q8 {
   static constexpr uint32_t kType = T_Q8_0;
   static constexpr int kSegBytes = 272, kSteps = 16;
-  static constexpr bool kNeedsSubSums = false;
+  static constexpr int kSumGroup = 32;  // x sums per block (offset correction)
   VHD static int elem(int step, int t, int j) {
     int base = 64 * t;
     if (step < 7) return base + 2 + 4 * step + kperm(j);
     if (step == 7) return base + ((j == 0) ? 0 : (j == 1) ? 30 : (j == 2) ? 1 : 31);
     return base + 32 + 4 * (step - 8) + kperm(j);
   }
-  // int8 x4 -> (f16x2 of bytes 0,2 ; f16x2 of bytes 1,3), exact
+  // int8 x4 -> (f16x2 of bytes 0,2 ; f16x2 of bytes 1,3) holding 1152 + q,
+  // exact.  One lop3 per pair: the sign bit of each byte is flipped (q+128
+  // as an unsigned byte), the other byte of each half becomes 0x64; bit
+  // classes per (b, c): (0,0) keep, (1,0) flip, (1,1) one, (0,1) zero.
   VHD static void conv(uint32_t w, uint32_t& h02, uint32_t& h13) {
-    uint32_t u = w ^ 0x80808080u;  // int8 -> int8 + 128 (unsigned byte)
-    h02 = (u & 0x00FF00FFu) | 0x64006400u;
-    h13 = ((u >> 8) & 0x00FF00FFu) | 0x64006400u;
-    // caller subtracts 1152 (0x6480) from both halves
+    h02 = lop3t<0x9C>(w, 0x64806480u, 0xFF00FF00u);
+    h13 = lop3t<0x9C>(w >> 8, 0x64806480u, 0xFF00FF00u);
   }
-  static constexpr uint32_t kBias = 0x64806480u;  // 1024 + 128
+  static constexpr float kOffset = 1152.f;  // removed with the block sum of x
 };
 
 // ---- Q4_K: 144-byte super-blocks, segment = 1 super-block ---------------
@@ -96,7 +116,7 @@ struct Q8 {
 struct Q4K {
   static constexpr uint32_t kType = T_Q4_K;
   static constexpr int kSegBytes = 144, kSteps = 16;
-  static constexpr bool kNeedsSubSums = true;  // sum of x over each 32-value sub-block
+  static constexpr int kSumGroup = 32;  // x sums per sub-block (min term)
   VHD static int elem(int step, int t, int j) { return 64 * t + 32 * (step & 1) + 4 * (step >> 1) + kperm(j); }
   // low nibbles: halves 1024 + q (bytes 0,2) and (bytes 1,3)
   VHD static void conv_lo(uint32_t w, uint32_t& h02, uint32_t& h13) {
@@ -131,7 +151,7 @@ struct Q4K {
 struct Q6K {
   static constexpr uint32_t kType = T_Q6_K;
   static constexpr int kSegBytes = 210, kSteps = 16;
-  static constexpr bool kNeedsSubSums = false;
+  static constexpr int kSumGroup = 16;  // x sums per scale group (offset correction)
   VHD static int elem(int step, int t, int j) {
     int m = step >> 2, s = step & 3;
     return 128 * (m >> 1) + 32 * t + 16 * (m & 1) + 4 * s + kperm(j);
@@ -142,12 +162,13 @@ struct Q6K {
     uint32_t hi = ((qh >> (2u * (uint32_t)t)) & 0x03030303u) << 4;
     return lo | hi;
   }
+  // halves 1024 + z (z = the 6-bit value); value = z - 32, so the offset
+  // removed with the group sum of x is 1056
   VHD static void conv(uint32_t z, uint32_t& h02, uint32_t& h13) {
     h02 = (z & 0x00FF00FFu) | 0x64006400u;
     h13 = byte_perm(z, 0x64646464u, 0x4341u);
-    // caller subtracts 1056 (0x6420) = 1024 + 32 from both halves
   }
-  static constexpr uint32_t kBias = 0x64206420u;
+  static constexpr float kOffset = 1056.f;
 };
 
 }  // namespace vireo

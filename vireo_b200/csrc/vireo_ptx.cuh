@@ -47,18 +47,36 @@ VDEV bool mbar_test(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait that lets the hardware suspend the thread for up to hint_ns
+VDEV bool mbar_test_suspend(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
 // Waits for the phase with the given parity to complete.  Gives up (false)
 // when the time limit passes or *abort becomes non-zero.
 VDEV bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort) {
   if (mbar_test(bar, parity)) return true;
   uint64_t t0 = now_ns();
-  for (uint32_t it = 0;; ++it) {
-    if (mbar_test(bar, parity)) return true;
-    if ((it & 63) == 63) {
-      if (*abort) return false;
-      if (now_ns() - t0 > kWaitLimitNs) return false;
-    }
+  for (;;) {
+    if (mbar_test_suspend(bar, parity, 20000u)) return true;
+    if (*abort) return false;
+    if (now_ns() - t0 > kWaitLimitNs) return false;
   }
+}
+// warp-collective wait: lane 0 waits, the warp then proceeds together (the
+// __syncwarp orders the other lanes' later shared-memory reads after the
+// completed phase).  Returns the same result in every lane.
+VDEV bool mbar_wait_warp(uint64_t* bar, uint32_t parity, const volatile int* abort) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
 }
 
 // ---- 1-D bulk copy global -> shared (TMA engine), completes on mbarrier ---
@@ -71,9 +89,27 @@ VDEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
       : "memory");
 }
 
+// ---- 16-byte asynchronous copies global -> shared (LSU path) --------------
+VDEV void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+// arrive on bar once every cp.async this thread issued so far has landed
+// (the barrier's expected count includes this arrival)
+VDEV void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+VDEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// ---- programmatic dependent launch ---------------------------------------
+// wait until the preceding kernel in the stream has completed and its
+// memory is visible (no-op when launched without the PDL attribute)
+VDEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// allow the next kernel in the stream to begin launching
+VDEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---- tensor core: D = A(16x16 f16) * B(16x8 f16) + C, fp32 accumulate ----
 VDEV void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -93,29 +129,51 @@ VDEV uint32_t h2_fma(uint32_t a, uint32_t b, uint32_t c) {
 }
 
 // ---- shared-memory loads --------------------------------------------------
-VDEV uint32_t lds32(const void* p) {
-  uint32_t v;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_addr(p)));
-  return v;
-}
-VDEV uint4 lds128(const void* p) {
-  uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(smem_addr(p)));
-  return v;
-}
-VDEV uint2 lds64(const void* p) {
-  uint2 v;
-  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(smem_addr(p)));
-  return v;
-}
+// Plain C++ loads (not asm volatile) so the compiler may schedule them ahead
+// of their use; they stay ordered after the mbarrier waits, which clobber
+// memory.  Pointers are derived from the kernel's shared arrays, so these
+// compile to shared-memory loads.
+VDEV uint32_t lds32(const void* p) { return *reinterpret_cast<const uint32_t*>(p); }
+VDEV uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
+VDEV uint2 lds64(const void* p) { return *reinterpret_cast<const uint2*>(p); }
 
 // ---- global loads that bypass L1 (data written by other CTAs) ------------
 VDEV uint32_t ld_acquire_gpu(const unsigned int* p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+
+VDEV void st_release_gpu(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+VDEV unsigned int atom_add_acq_rel_gpu(unsigned int* p, unsigned int v) {
+  unsigned int old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+VDEV void red_add_release_gpu(unsigned int* p, unsigned int v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// L2 prefetch of a 16-byte-aligned span (size a multiple of 16)
+VDEV void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Waits until *p >= target (acquire).  One thread per CTA polls.  Returns
+// false on timeout (recorded in *err) or when *err is already set.
+VDEV bool wait_geq(unsigned int* p, unsigned int target, int* err) {
+  if (ld_acquire_gpu(p) >= target) return true;
+  uint64_t t0 = now_ns();
+  for (;;) {
+    __nanosleep(32);
+    if (ld_acquire_gpu(p) >= target) return true;
+    if (*(volatile int*)err) return false;
+    if (now_ns() - t0 > kWaitLimitNs) {
+      atomicCAS(err, 0, VIREO_ERR_TIMEOUT);
+      return false;
+    }
+  }
 }
 
 // ---- grid-wide barrier (one thread per CTA calls it) ---------------------
