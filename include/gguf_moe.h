@@ -81,6 +81,21 @@ int gguf_moe_grid(const gguf_moe *m);
 
 void gguf_moe_destroy(gguf_moe *m);
 
+/* No counterpart in the reference: an extension for callers that may not
+ * allocate device memory.  Same computation and arguments as gguf_moe_ffn,
+ * with the layer given by its descriptor (device pointers, the rules of
+ * gguf_moe_create) instead of a handle.  Allocates nothing: the kernel's
+ * scratch is a fixed 64 KiB device array in the library, enough for every
+ * shape gguf_moe_create accepts; a shape needing more returns
+ * VIREO_ERR_NOMEM.  The first call on a device sets that device up (takes
+ * the array's address, zeroes it) and must come before any stream capture.
+ * Every call zeroes the launch's sync and status words first.  The call
+ * synchronises stream (NULL = the legacy default stream) and returns the
+ * kernel's status.  All calls on one device share the array: calls that
+ * overlap on the GPU race. */
+int gguf_moe_ffn_noalloc(const gguf_moe_desc *desc, const float *hb, float *x, int n_tok, int32_t *ids,
+                         float *wts, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -86,6 +86,8 @@ def lib():
         L.gguf_moe_sync.argtypes = [C.c_void_p, C.c_void_p]
         L.gguf_moe_set_expert_ptrs.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
         L.gguf_moe_destroy.argtypes = [C.c_void_p]
+        L.gguf_moe_ffn_noalloc.argtypes = [C.POINTER(GgufMoeDesc), C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
+                                           C.c_void_p, C.c_void_p]
         L.gguf_moe_destroy.restype = None
         _lib = L
     return _lib
