@@ -67,6 +67,23 @@ VDEV void stage_vec(const float* g, float* s, int n, int tid, int nthr, bool byp
   for (int i = tid; i < n / 4; i += nthr) s4[i] = bypass_l1 ? __ldcg(g4 + i) : __ldg(g4 + i);
 }
 
+// As stage_vec with L2-only loads (data other CTAs wrote) and 8 loads in
+// flight per thread.
+VDEV void stage_vec_cg8(const float* g, float* s, int n, int tid, int nthr) {
+  const float4* g4 = reinterpret_cast<const float4*>(g);
+  float4* s4 = reinterpret_cast<float4*>(s);
+  const int n4 = n / 4;
+  for (int i0 = tid; i0 < n4; i0 += 8 * nthr) {
+    float4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+      if (i0 + j * nthr < n4) v[j] = __ldcg(g4 + i0 + j * nthr);
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+      if (i0 + j * nthr < n4) s4[i0 + j * nthr] = v[j];
+  }
+}
+
 template <class SG, class SD>
 __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __grid_constant__ MoeDecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -180,7 +197,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __g
         ctl->xinv = 1.f / sc;
       }
       __syncthreads();
-      build_btab<SG>(stg, d, red[kDecodeThreads / 32], xtab, xsx, threadIdx.x, blockDim.x, false);
+      build_tables<SG>(stg, xtab, xsx, d / kSegElems, d / kSegElems, &red[kDecodeThreads / 32], warp,
+                       (int)(blockDim.x / 32), lane);
     }
     if (threadIdx.x == 0) {
       if (!wait_geq(&sy->router_arrive.v, (unsigned)G, p.s.err)) ctl->abort = 1;
@@ -399,8 +417,13 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __g
       }
       named_bar(1, NC);
       if (threadIdx.x == 0) trace(p, kTrDbg + 0);
-      build_btab_experts<SD>(p.s.hbuf, k, fe, hscale, htab, p.htab_bytes, hsx, p.hsx_count, threadIdx.x, NC,
-                             [] { named_bar(1, NC); });
+      // h rows (written by other CTAs) into the table area with coalesced
+      // 16-byte loads, then the tables built in place
+      stage_vec_cg8(p.s.hbuf, reinterpret_cast<float*>(htab), k * fe, threadIdx.x, NC);
+      named_bar(1, NC);
+      if (threadIdx.x == 0) trace(p, kTrDbg + 2);
+      build_tables<SD>(reinterpret_cast<const float*>(htab), htab, hsx, k * fe / kSegElems, fe / kSegElems, hscale,
+                       warp, W, lane);
       if (threadIdx.x == 0) trace(p, kTrDbg + 1);
     }
     named_bar(1, NC);
@@ -531,7 +554,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) gemv_kernel(const __grid_co
     for (int i = 0; i < W; i++) mm = fmaxf(mm, red[i]);
     const float sc = pow2_scale(mm);
     if (threadIdx.x == 0) ctl->xinv = 1.f / sc;
-    build_btab<SF>(xs, p.n, sc, xtab, xsx, threadIdx.x, NC, false);
+    const float scv = sc;
+    build_tables<SF>(xs, xtab, xsx, p.n / kSegElems, p.n / kSegElems, &scv, warp, W, lane);
     named_bar(1, NC);
   }
   const LaneCtx L = lane_ctx();

@@ -268,107 +268,58 @@ VDEV float pow2_scale(float amax) {
   return ldexpf(1.f, e);
 }
 
-// Sums of (x_hi + x_lo) of scale * v over consecutive groups of GS (16 or
-// 32) values; warp-cooperative, tid/nthr whole warps.
-template <int GS>
-VDEV void group_sums(const float* v, int K, float scale, float* sx, int tid, int nthr, bool from_global) {
-  const int lane = tid & 31, nw = nthr >> 5;
-  constexpr int GPW = 32 / GS;  // groups per warp pass
-  for (int g0 = (tid >> 5) * GPW; g0 < K / GS; g0 += nw * GPW) {
-    const int idx = g0 * GS + lane;
-    float x = 0.f;
-    if (idx < K) x = (from_global ? __ldcg(v + idx) : v[idx]) * scale;
-    const float hi = __half2float(__float2half_rn(x));
-    float s = hi + __half2float(__float2half_rn(x - hi));
-#pragma unroll
-    for (int o = GS / 2; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if ((lane % GS) == 0 && g0 + lane / GS < K / GS) sx[g0 + lane / GS] = s;
-  }
-}
-
-// Block-cooperative (threads tid in [0, nthr)).  v may be global or shared.
+// B tables of 256-value segments, one warp per segment.  Segment i of the
+// source is the fp32 values src[256 i, 256 i + 256), scaled by
+// scales[i / segs_per_vec] (a power of two); its table is the 1 KB at
+// dst + 1024 i: 16 steps x 4 threads x 16 bytes, the 16-byte chunk c =
+// 4 step + t holding f16 hi[4] then f16 lo[4] of elements F::elem(step, t,
+// j), j = 0..3.  Its group sums sx[i * 256/GS + g] are the fp32 sums of
+// hi + lo over the natural groups of GS = F::kSumGroup values (Q8_0 and
+// Q4_K: 32, Q6_K: 16), the offset / min corrections of the segment kernels.
+// Every read of a segment precedes every write to it (warp-synchronous), so
+// dst may alias src: 4 bytes of table per value, the same footprint.
 template <class F>
-VDEV void build_btab(const float* v, int K, float scale, uint8_t* tab, float* sx, int tid, int nthr,
-                     bool from_global) {
-  for (int idx = tid; idx < K; idx += nthr) {
-    const int seg = idx >> 8, rem = idx & 255;
-    const int step = rem >> 4, t = (rem >> 2) & 3, j = rem & 3;
-    const int e = seg * kSegElems + F::elem(step, t, j);
-    const float x = (from_global ? __ldcg(v + e) : v[e]) * scale;
-    const __half hi = __float2half_rn(x);
-    const __half lo = __float2half_rn(x - __half2float(hi));
-    uint8_t* dst = tab + seg * (16 * kStepBytesB) + step * kStepBytesB + t * 16 + j * 2;
-    *reinterpret_cast<__half*>(dst) = hi;
-    *reinterpret_cast<__half*>(dst + 8) = lo;
-  }
-  // sums of the scaled x over each group of F::kSumGroup values (the offset
-  // and min corrections), each the fp32 sum of x_hi + x_lo; one group per
-  // warp (or half-warp) with consecutive lanes on consecutive values
-  group_sums<F::kSumGroup>(v, K, scale, sx, tid, nthr, from_global);
-}
-
-// B tables of k vectors at once (the k experts' SwiGLU outputs h, fp32 in
-// global memory, fe values each; scale[t] the power-of-two scale of vector
-// t).  Block-cooperative over nthr threads (whole warps, fe % nthr == 0).
-// The h rows are first copied with coalesced 16-byte loads into the table
-// area itself (k * 4 * fe bytes, the same size as the tables), the group
-// sums are taken there warp-cooperatively, every thread then gathers the
-// values of its table slots into registers, and after a barrier the f16
-// hi/lo pairs are written over the staging copy.  bar(): the caller's
-// barrier over the same nthr threads.
-template <class F, class Bar>
-VDEV void build_btab_experts(const float* hbuf, int k, int fe, const float* scale, uint8_t* tabs, uint32_t tab_bytes,
-                             float* sxs, uint32_t sx_count, int tid, int nthr, Bar bar) {
-  float* raw = reinterpret_cast<float*>(tabs);
-  {
-    const float4* src = reinterpret_cast<const float4*>(hbuf);
-    float4* dst = reinterpret_cast<float4*>(raw);
-    const int n4 = k * fe / 4;
-    for (int i0 = tid; i0 < n4; i0 += 8 * nthr) {
-      float4 v[8];
+VDEV void build_tables(const float* src, uint8_t* dst, float* sx, int nseg, int segs_per_vec, const float* scales,
+                       int warp, int nwarps, int lane) {
+  constexpr int GS = F::kSumGroup;
+#pragma unroll 1
+  for (int i = warp; i < nseg; i += nwarps) {
+    const float sc = scales[i / segs_per_vec];
+    const float* v = src + (size_t)i * kSegElems;
+    // group sums: lane l holds the natural values [8 l, 8 l + 8)
+    const float4 a = *reinterpret_cast<const float4*>(v + 8 * lane);
+    const float4 b = *reinterpret_cast<const float4*>(v + 8 * lane + 4);
+    const float nat[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    float s = 0.f;
 #pragma unroll
-      for (int j = 0; j < 8; j++)
-        if (i0 + j * nthr < n4) v[j] = __ldcg(src + i0 + j * nthr);
-#pragma unroll
-      for (int j = 0; j < 8; j++)
-        if (i0 + j * nthr < n4) dst[i0 + j * nthr] = v[j];
+    for (int q = 0; q < 8; q++) {
+      const float x = nat[q] * sc;
+      const float hi = __half2float(__float2half_rn(x));
+      s += hi + __half2float(__float2half_rn(x - hi));
     }
-  }
-  bar();
-  for (int t = 0; t < k; t++)
-    group_sums<F::kSumGroup>(raw + (size_t)t * fe, fe, scale[t], sxs + (size_t)t * sx_count, tid, nthr, false);
-  // gather the values of this thread's slots (slot i of expert t holds
-  // element seg*256 + elem(step, tt, jq) of that expert)
-  const int fq = fe / nthr, nj = k * fq;
-  constexpr int kMaxSlots = 32;
-  float xv[kMaxSlots];
-  uint32_t off[kMaxSlots];
-  {
-    int t = 0, rem = 0;
 #pragma unroll
-    for (int j = 0; j < kMaxSlots; j++) {
-      if (j < nj) {
-        const int i = rem * nthr + tid;
-        const int seg = i >> 8, r8 = i & 255, step = r8 >> 4, tt = (r8 >> 2) & 3, jq = r8 & 3;
-        const int e = seg * kSegElems + F::elem(step, tt, jq);
-        xv[j] = raw[(size_t)t * fe + e] * scale[t];
-        off[j] = (uint32_t)t * tab_bytes + seg * (16 * kStepBytesB) + step * kStepBytesB + tt * 16 + jq * 2;
-        if (++rem == fq) {
-          rem = 0;
-          ++t;
-        }
+    for (int o = 1; o < GS / 8; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    // table chunks c = lane and lane + 32
+    uint4 out[2];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const int c = lane + 32 * h, step = c >> 2, t = c & 3;
+      uint32_t hv[4], lv[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float x = v[F::elem(step, t, j)] * sc;
+        const __half hh = __float2half_rn(x);
+        hv[j] = __half_as_ushort(hh);
+        lv[j] = __half_as_ushort(__float2half_rn(x - __half2float(hh)));
       }
+      out[h] = make_uint4(hv[0] | (hv[1] << 16), hv[2] | (hv[3] << 16), lv[0] | (lv[1] << 16), lv[2] | (lv[3] << 16));
     }
-  }
-  bar();
-#pragma unroll
-  for (int j = 0; j < kMaxSlots; j++) {
-    if (j < nj) {
-      const __half hi = __float2half_rn(xv[j]);
-      const __half lo = __float2half_rn(xv[j] - __half2float(hi));
-      *reinterpret_cast<__half*>(tabs + off[j]) = hi;
-      *reinterpret_cast<__half*>(tabs + off[j] + 8) = lo;
-    }
+    __syncwarp();
+    if ((lane & (GS / 8 - 1)) == 0) sx[(size_t)i * (kSegElems / GS) + lane / (GS / 8)] = s;
+    uint4* d4 = reinterpret_cast<uint4*>(dst + (size_t)i * (16 * kStepBytesB));
+    d4[lane] = out[0];
+    d4[lane + 32] = out[1];
+    __syncwarp();
   }
 }
 
@@ -388,6 +339,7 @@ VDEV bool consume_unit(const uint8_t* stage, const StageGeom& sg, int v, int nse
   const uint8_t* r1 = stage_row(stage, sg, L.g + 8);
   int first = (w - (v * nseg) % W) % W;
   if (first < 0) first += W;
+#pragma unroll 1
   for (int seg = first; seg < nseg; seg += W) {
     float tot0 = 0.f, tot1 = 0.f;
     bf.get(btab + seg * (16 * kStepBytesB), L);
