@@ -5,8 +5,12 @@ the bit-exact CPU restatement (oracle/), run on the same seeded inputs.
 
 Tolerances (the north star's bar):
 * dequantisation and expert ids: bit-exact;
-* mat-vec and MoE-layer outputs: max |got - ref| / max |ref| <= 2e-3 per
-  output vector, with fp32 accumulation (the kernels land near 1e-6).
+* MoE-layer outputs: max |got - ref| / max |ref| <= 2e-3 per output vector;
+* mat-vec outputs: the same measure <= MM_TOL = 1e-4.  The kernels multiply
+  the exact quantised weights by activations carried as two int8 digits per
+  value under one fp32 scale per 32 values (|error| <= max|x| / 64516 of the
+  group), with exact integer accumulation and fp32 block sums: about 2e-5 on
+  random inputs.
 """
 import numpy as np
 import pytest
@@ -17,6 +21,7 @@ from vireo_b200 import synth as S
 pytestmark = pytest.mark.gpu
 
 TOL = 2e-3
+MM_TOL = 1e-4
 TYPES = [S.GGML_F32, S.GGML_F16, S.GGML_Q8_0, S.GGML_Q5_0, S.GGML_Q4_K, S.GGML_Q6_K]
 
 
@@ -63,7 +68,7 @@ def test_matmul_golden(V, golden, t):
         n, d = int(n), int(d)
         w, x, y = golden[k], golden[k[:-1] + "x"], golden[k[:-1] + "y"]
         got = V.gguf_matmul(t, w, x, n, d)
-        assert rel_err(got, y) < 1e-5, (k, rel_err(got, y))
+        assert rel_err(got, y) < MM_TOL, (k, rel_err(got, y))
 
 
 SHAPES = [(S.GGML_Q8_0, 2048, 1024), (S.GGML_Q8_0, 1024, 2048), (S.GGML_Q4_K, 2048, 768),
@@ -83,7 +88,7 @@ def test_matmul_shapes_device(V, t, n, d):
     V.gguf_matmul_dev(t, wd, xd, n, d, yd)
     V.sync()
     got = yd.cpu().numpy()
-    assert rel_err(got, ref) < 1e-5, rel_err(got, ref)
+    assert rel_err(got, ref) < MM_TOL, rel_err(got, ref)
     # host-pointer entry gives the same numbers
     assert np.array_equal(V.gguf_matmul(t, w, x, n, d), got)
 
@@ -97,7 +102,7 @@ def test_matmul_registered_weights(V):
     V.check(lib.gguf_weights_register(w.ctypes.data, w.nbytes), "register")
     try:
         got = V.gguf_matmul(t, w[S.row_bytes(t, n) * 16:], x, n, d - 16)
-        assert rel_err(got, ref[16:]) < 1e-5
+        assert rel_err(got, ref[16:]) < MM_TOL
     finally:
         V.check(lib.gguf_weights_unregister(w.ctypes.data), "unregister")
 

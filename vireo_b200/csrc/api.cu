@@ -396,7 +396,7 @@ int gguf_moe_create(const gguf_moe_desc* desc, gguf_moe** out) {
     return VIREO_ERR_ARG;
   if (D.router_type != T_F32 || D.gate_type != D.up_type || !fast_format(D.gate_type) ||
       !fast_format(D.down_type) || D.dim % kRouterChunk || D.dim > 8 * kRouterChunk || D.ffn_exp % kSegElems ||
-      D.n_experts > 256 || D.ffn_exp % (32 * kConsumerWarps) || D.n_used * D.ffn_exp > 32 * 32 * kConsumerWarps ||
+      D.n_experts > 256 || D.n_used * D.ffn_exp > kMaxHValues ||
       D.n_used > kMaxTopK)
     return VIREO_ERR_UNSUPPORTED;
   const uint64_t gsl = (uint64_t)D.ffn_exp * row_bytes(D.gate_type, D.dim);
@@ -442,7 +442,7 @@ int gguf_moe_create(const gguf_moe_desc* desc, gguf_moe** out) {
   m->grid = c->num_sms;
 
   // scratch: logit partials, h, per-launch sync words, status
-  p.hsx_count = (uint32_t)(D.ffn_exp / (D.down_type == T_Q6_K ? 16 : 32));
+  p.hsx_count = (uint32_t)(D.ffn_exp / kSegElems * kMeta);
   const size_t n_lp = (size_t)(D.dim / kRouterChunk) * D.n_experts, n_h = (size_t)D.n_used * D.ffn_exp;
   size_t off = 0;
   const size_t o_lp = off;

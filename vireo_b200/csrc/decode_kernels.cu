@@ -12,13 +12,10 @@ namespace vireo {
 
 struct Ctl {
   int abort;
-  int nvalid;
-  float xinv;
+  float wsum;  // renorm denominator
   int ids[kMaxTopK];
   float wts[kMaxTopK];
-  float hinv[kMaxTopK];
   int tile_cnt[2];  // down units finished per tile buffer
-  float hamax[kMaxTopK];  // this CTA's max |h| per expert slot
 };
 
 VDEV void trace(const MoeDecodeParams& p, int slot) {
@@ -88,12 +85,16 @@ template <class SG, class SD>
 __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __grid_constant__ MoeDecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float red[kDecodeThreads / 32 + 1];
+  // gate/up ring (S stages) and down ring (SD slots over the same memory)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kMaxStages;
+  uint64_t* full_d = empty + kMaxStages;
+  uint64_t* empty_d = full_d + kMaxStages;
   Ctl* ctl = reinterpret_cast<Ctl*>(smem + p.off_ctl);
   float* part = reinterpret_cast<float*>(smem + p.off_part);
+  float* part_d = reinterpret_cast<float*>(smem + p.off_part_d);
   int* ucnt = reinterpret_cast<int*>(smem + p.off_ucnt);
-  int* unit_of = reinterpret_cast<int*>(smem + p.off_unit);  // unit carried by each stage
+  int* ucnt_d = ucnt + kMaxStages;
   float* ytile = reinterpret_cast<float*>(smem + p.off_ytile); // [2][k][16] expert rows of a tile
   uint8_t* xtab = smem + p.off_xtab;
   float* xsx = reinterpret_cast<float*>(smem + p.off_xsx);
@@ -106,21 +107,24 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __g
   constexpr int W = kConsumerWarps;
   constexpr int NC = W * 32;  // consumer threads
   const int G = gridDim.x, cta = blockIdx.x;
-  const int d = p.d, fe = p.fe, ne = p.ne, k = p.k, S = p.nstages;
+  const int d = p.d, fe = p.fe, ne = p.ne, k = p.k, S = p.nstages, SD_ = p.nstages_d;
   MoeSync* sy = p.s.sync;
 
   if (threadIdx.x == 0) {
     trace(p, kTrStart);
     for (int s = 0; s < S; s++) {
-      mbar_init(&full[s], kProducerThreads + 1);  // every producer's copies + the unit id
+      mbar_init(&full[s], kProducerThreads);  // every producer's copies
       mbar_init(&empty[s], W);
+    }
+    for (int s = 0; s < SD_; s++) {
+      mbar_init(&full_d[s], kProducerThreads);
+      mbar_init(&empty_d[s], W);
     }
     ctl->abort = 0;
     ctl->tile_cnt[0] = ctl->tile_cnt[1] = 0;
-    for (int t = 0; t < kMaxTopK; t++) ctl->hamax[t] = 0.f;
     mbar_fence_init();
   }
-  for (int i = threadIdx.x; i < S; i += blockDim.x) ucnt[i] = 0;
+  for (int i = threadIdx.x; i < 2 * kMaxStages; i += blockDim.x) ucnt[i] = 0;
   // the next token's kernel may start its own prologue as SMs free up
   pdl_launch_dependents();
 
@@ -182,24 +186,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __g
       red_add_release_gpu(&sy->router_arrive.v, 1u);
     }
     // x table while the other CTAs finish their router partials
-    {
-      float m = 0.f;
-      for (int i = threadIdx.x; i < d; i += blockDim.x) m = fmaxf(m, fabsf(stg[i]));
-#pragma unroll
-      for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      if (lane == 0) red[warp] = m;
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        float mm = 0.f;
-        for (int i = 0; i < (int)(blockDim.x / 32); i++) mm = fmaxf(mm, red[i]);
-        const float sc = pow2_scale(mm);
-        red[kDecodeThreads / 32] = sc;
-        ctl->xinv = 1.f / sc;
-      }
-      __syncthreads();
-      build_tables<SG>(stg, xtab, xsx, d / kSegElems, d / kSegElems, &red[kDecodeThreads / 32], warp,
-                       (int)(blockDim.x / 32), lane);
-    }
+    build_tables<SG>(stg, xtab, xsx, d / kSegElems, warp, (int)(blockDim.x / 32), lane);
     if (threadIdx.x == 0) {
       if (!wait_geq(&sy->router_arrive.v, (unsigned)G, p.s.err)) ctl->abort = 1;
       trace(p, kTrPartials);
@@ -264,29 +251,33 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __g
         }
       }
       // fewer than k selectable experts (NaN probabilities): unused slots
+      // hold id -1, weight -1 as in the reference's scan
       const int nsel = __syncthreads_count(e < ne && !isnan(pe));
-      if (threadIdx.x == 0) {
-        for (int t = nsel; t < k; t++) {
-          ctl->ids[t] = -1;
-          ctl->wts[t] = -1.f;
-        }
-        float ws = 0.f;
-        int nv = 0;
-        for (int t = 0; t < k; t++) {
-          ws = ws + ctl->wts[t];
-          nv += ctl->ids[t] >= 0;
-        }
-        if (p.renorm && ws > 0.f)
-          for (int t = 0; t < k; t++) ctl->wts[t] = ctl->wts[t] / ws;
-        ctl->nvalid = nv;
-        if (cta == 0) {
-          for (int t = 0; t < k; t++) {
-            if (p.ids_out) p.ids_out[t] = ctl->ids[t];
-            if (p.wts_out) p.wts_out[t] = ctl->wts[t];
-          }
-        }
-        trace(p, kTrRouted);
+      const int t = threadIdx.x;
+      if (t < k && t >= nsel) {
+        ctl->ids[t] = -1;
+        ctl->wts[t] = -1.f;
       }
+      __syncthreads();
+      if (t == 0) {
+        // renorm denominator: the sequential rank-order sum (gguf_run.c:192)
+        float ws = 0.f;
+#pragma unroll 1
+        for (int j = 0; j < k; j++) ws = ws + ctl->wts[j];
+        ctl->wsum = ws;
+      }
+      __syncthreads();
+      if (t < k) {
+        const float ws = ctl->wsum;
+        float w = ctl->wts[t];
+        if (p.renorm && ws > 0.f) w = w / ws;
+        ctl->wts[t] = w;
+        if (cta == 0) {
+          if (p.ids_out) p.ids_out[t] = ctl->ids[t];
+          if (p.wts_out) p.wts_out[t] = w;
+        }
+      }
+      if (t == 0) trace(p, kTrRouted);
     }
     __syncthreads();
   }
@@ -295,55 +286,42 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __g
   const int g0 = (int)((long long)cta * UG / G), g1 = (int)((long long)(cta + 1) * UG / G);
   const int my_tiles = (cta < ntile) ? (ntile - 1 - cta) / G + 1 : 0;
 
+  const int nG = g1 - g0, nD = my_tiles * k;
   if (warp >= W) {
     // ---- producers: 16-byte cp.async copies ---------------------------------
     const int ptid = threadIdx.x - NC;
-    int v = 0;
     // gate/up units: a contiguous range per CTA
     if (ptid == 0) trace(p, kTrProdFirst);
-    for (int u = g0; u < g1; u++) {
+    for (int v = 0; v < nG; v++) {
       const int slot = v % S;
       if (!warp_wait(&empty[slot], ((uint32_t)(v / S) & 1u) ^ 1u, ctl, p.s.err)) break;
-      const int t = u / rgG, rg = u - t * rgG;
+      const int u = g0 + v, t = u / rgG, rg = u - t * rgG;
       const int e = ctl->ids[t];
       const uint8_t* gsrc = e < 0 ? nullptr : p.exp_tab[3 * e + 0] + (size_t)(8 * rg) * p.sg_gu.rb;
       const uint8_t* usrc = e < 0 ? nullptr : p.exp_tab[3 * e + 1] + (size_t)(8 * rg) * p.sg_gu.rb;
       issue_unit(stages + (size_t)slot * p.stage_bytes, &full[slot], gsrc, usrc, p.sg_gu, ptid, kProducerThreads);
-      if (ptid == 0) {
-        unit_of[slot] = u;
-        mbar_arrive(&full[slot]);
-      }
-      v++;
     }
-    // end-of-gate/up marker
-    {
-      const int slot = v % S;
-      if (warp_wait(&empty[slot], ((uint32_t)(v / S) & 1u) ^ 1u, ctl, p.s.err)) {
-        cp_async_arrive(&full[slot]);
-        if (ptid == 0) {
-          unit_of[slot] = -1;
-          mbar_arrive(&full[slot]);
-        }
-      }
-      v++;
-    }
-    // down units: every expert slot of each of this CTA's 16-row tiles
+    // down units: every expert slot of each of this CTA's 16-row tiles, in
+    // the down ring.  A slot's first use waits for the last release of every
+    // gate/up stage it overlaps (the down weights do not depend on h, so
+    // they stream in while gate/up is still being consumed).
     if (ptid == 0) trace(p, kTrProdFirstD);
-    for (int i = 0; i < my_tiles && !aborted(ctl); i++) {
-      const int tile = cta + i * G;
-      for (int t = 0; t < k; t++) {
-        const int slot = v % S;
-        if (!warp_wait(&empty[slot], ((uint32_t)(v / S) & 1u) ^ 1u, ctl, p.s.err)) break;
-        const int e = ctl->ids[t];
-        const uint8_t* src = e < 0 ? nullptr : p.exp_tab[3 * e + 2] + (size_t)(16 * tile) * p.sg_d.rb;
-        issue_unit(stages + (size_t)slot * p.stage_bytes, &full[slot], src, src ? src + 8 * (size_t)p.sg_d.rb : nullptr,
-                   p.sg_d, ptid, kProducerThreads);
-        if (ptid == 0) {
-          unit_of[slot] = tile * k + t;
-          mbar_arrive(&full[slot]);
-        }
-        v++;
+    for (int j = 0; j < nD && !aborted(ctl); j++) {
+      const int slot = j % SD_;
+      bool ok = true;
+      if (j < SD_) {
+        const uint32_t lo = (uint32_t)slot * p.dslot_bytes, hi = lo + p.dslot_bytes - 1u;
+        for (int st = (int)(lo / p.stage_bytes); ok && st <= (int)(hi / p.stage_bytes) && st < nG; st++)
+          ok = warp_wait(&empty[st], (uint32_t)((nG - 1 - st) / S) & 1u, ctl, p.s.err);
+      } else {
+        ok = warp_wait(&empty_d[slot], ((uint32_t)(j / SD_) & 1u) ^ 1u, ctl, p.s.err);
       }
+      if (!ok) break;
+      const int i = j / k, t = j - i * k, tile = cta + i * G;
+      const int e = ctl->ids[t];
+      const uint8_t* src = e < 0 ? nullptr : p.exp_tab[3 * e + 2] + (size_t)(16 * tile) * p.sg_d.rb;
+      issue_unit(stages + (size_t)slot * p.dslot_bytes, &full_d[slot], src, src ? src + 8 * (size_t)p.sg_d.rb : nullptr,
+                 p.sg_d, ptid, kProducerThreads);
     }
     if (ptid == 0) trace(p, kTrProdLast);
     cp_async_wait_all();  // no copy may still target this CTA's shared memory at exit
@@ -355,17 +333,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __g
   const LaneCtx L = lane_ctx();
   BFrag bf;
   bf.reset();
-  int v = 0;
-  for (;; v++) {
+  for (int v = 0; v < nG; v++) {
     const int slot = v % S;
-    const bool ok = warp_wait(&full[slot], (uint32_t)(v / S) & 1u, ctl, p.s.err);
-    const int u = ok ? unit_of[slot] : -1;
-    if (u < 0) {  // end-of-gate/up marker (or abort)
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[slot]);
-      v++;
-      break;
-    }
+    if (!warp_wait(&full[slot], (uint32_t)(v / S) & 1u, ctl, p.s.err)) break;
+    const int u = g0 + v;
     if (threadIdx.x == 0 && v < kTrUnits) trace(p, kTrUnitBase + 2 * v);
     const int t = u / rgG, rg = u - t * rgG;
     const bool active = ctl->ids[t] >= 0;
@@ -376,24 +347,16 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __g
       const float up = __shfl_sync(0xffffffffu, val, (lane + 8) & 31);
       float hv = 0.f;
       if (active && lane < 8) {
-        const float gg = val * ctl->xinv, uu = up * ctl->xinv;
-        const float sl = gg / (1.0f + expf(-gg));
-        hv = sl * uu;
+        // the reference's SwiGLU, gguf_run.c:206
+        hv = (val / (1.0f + expf(-val))) * up;
         p.s.hbuf[(size_t)t * fe + 8 * rg + lane] = hv;
       }
-      float am = fabsf(hv);
-#pragma unroll
-      for (int o = 4; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-      if (lane == 0 && active) atomicMax(reinterpret_cast<unsigned int*>(&ctl->hamax[t]), __float_as_uint(am));
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
     if (threadIdx.x == 0 && v < kTrUnits) trace(p, kTrUnitBase + 2 * v + 1);
   }
-  // publish this CTA's gate/up results: one max per expert slot, one count
-  named_bar(1, NC);
-  if (threadIdx.x < k && ctl->hamax[threadIdx.x] > 0.f)
-    atomicMax(&sy->h_amax.v + threadIdx.x, __float_as_uint(ctl->hamax[threadIdx.x]));
+  // publish this CTA's gate/up results (h rows in scratch): one count
   named_bar(1, NC);
   if (threadIdx.x == 0) {
     trace(p, kTrGDone);
@@ -409,41 +372,33 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __g
     }
     named_bar(1, NC);
     if (!aborted(ctl)) {
-      float* hscale = stg;  // x staging is free by now
-      if (threadIdx.x < k) {
-        const float am = __uint_as_float(__ldcg(&sy->h_amax.v + threadIdx.x));
-        hscale[threadIdx.x] = pow2_scale(am);
-        ctl->hinv[threadIdx.x] = 1.f / hscale[threadIdx.x];
-      }
-      named_bar(1, NC);
       if (threadIdx.x == 0) trace(p, kTrDbg + 0);
       // h rows (written by other CTAs) into the table area with coalesced
       // 16-byte loads, then the tables built in place
       stage_vec_cg8(p.s.hbuf, reinterpret_cast<float*>(htab), k * fe, threadIdx.x, NC);
       named_bar(1, NC);
       if (threadIdx.x == 0) trace(p, kTrDbg + 2);
-      build_tables<SD>(reinterpret_cast<const float*>(htab), htab, hsx, k * fe / kSegElems, fe / kSegElems, hscale,
-                       warp, W, lane);
+      build_tables<SD>(reinterpret_cast<const float*>(htab), htab, hsx, k * fe / kSegElems, warp, W, lane);
       if (threadIdx.x == 0) trace(p, kTrDbg + 1);
     }
     named_bar(1, NC);
     if (threadIdx.x == 0) trace(p, kTrHtab);
 
     // ---- down units: tile-major, combined in this CTA ------------------------
-    for (int i = 0; i < my_tiles; i++) {
+    for (int i = 0, j = 0; i < my_tiles; i++) {
       const int tb = i & 1;
-      for (int t = 0; t < k; t++, v++) {
-        const int slot = v % S;
-        const bool ok = warp_wait(&full[slot], (uint32_t)(v / S) & 1u, ctl, p.s.err);
-        if (threadIdx.x == 0 && v < kTrUnits) trace(p, kTrUnitBase + 2 * v);
+      for (int t = 0; t < k; t++, j++) {
+        const int slot = j % SD_;
+        const bool ok = warp_wait(&full_d[slot], (uint32_t)(j / SD_) & 1u, ctl, p.s.err);
+        if (threadIdx.x == 0 && nG + j < kTrUnits) trace(p, kTrUnitBase + 2 * (nG + j));
         const int tile = cta + i * G;
         const bool active = ok && ctl->ids[t] >= 0;
         float val = 0.f;
-        const bool last = consume<SD>(stages + (size_t)slot * p.stage_bytes, p.sg_d, v, fe / kSegElems, warp,
+        const bool last = consume<SD>(stages + (size_t)slot * p.dslot_bytes, p.sg_d, j, fe / kSegElems, warp,
                                       htab + (size_t)t * p.htab_bytes, hsx + (size_t)t * p.hsx_count,
-                                      part + slot * p.part_stride, &ucnt[slot], L, &val, active, bf);
+                                      part_d + slot * p.part_stride, &ucnt_d[slot], L, &val, active, bf);
         if (last) {
-          if (lane < 16) ytile[(tb * k + t) * 16 + lane] = active ? val * ctl->hinv[t] : 0.f;
+          if (lane < 16) ytile[(tb * k + t) * 16 + lane] = active ? val : 0.f;
           __syncwarp();
           int done = 0;
           if (lane == 0) {
@@ -467,8 +422,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __g
           }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
-        if (threadIdx.x == 0 && v < kTrUnits) trace(p, kTrUnitBase + 2 * v + 1);
+        if (lane == 0) mbar_arrive(&empty_d[slot]);
+        if (threadIdx.x == 0 && nG + j < kTrUnits) trace(p, kTrUnitBase + 2 * (nG + j) + 1);
       }
     }
   }
@@ -480,7 +435,6 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __g
     if (atom_add_acq_rel_gpu(&sy->exit_cnt.v, 1u) == (unsigned)G - 1u) {
       sy->router_arrive.v = 0u;
       sy->g_done.v = 0u;
-      for (int t = 0; t < k; t++) (&sy->h_amax.v)[t] = 0u;
       __threadfence();
       sy->exit_cnt.v = 0u;
     }
@@ -493,7 +447,6 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __g
 template <class SF>
 __global__ void __launch_bounds__(kDecodeThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ float red[kDecodeThreads / 32 + 1];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kMaxStages;
   Ctl* ctl = reinterpret_cast<Ctl*>(smem + p.off_ctl);
@@ -544,18 +497,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) gemv_kernel(const __grid_co
       for (int i = threadIdx.x; i < p.n; i += NC) xs[i] = __ldg(p.x + i);
     }
     named_bar(1, NC);
-    float m = 0.f;
-    for (int i = threadIdx.x; i < p.n; i += NC) m = fmaxf(m, fabsf(xs[i]));
-#pragma unroll
-    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) red[warp] = m;
-    named_bar(1, NC);
-    float mm = 0.f;
-    for (int i = 0; i < W; i++) mm = fmaxf(mm, red[i]);
-    const float sc = pow2_scale(mm);
-    if (threadIdx.x == 0) ctl->xinv = 1.f / sc;
-    const float scv = sc;
-    build_tables<SF>(xs, xtab, xsx, p.n / kSegElems, p.n / kSegElems, &scv, warp, W, lane);
+    build_tables<SF>(xs, xtab, xsx, p.n / kSegElems, warp, W, lane);
     named_bar(1, NC);
   }
   const LaneCtx L = lane_ctx();
@@ -567,7 +509,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) gemv_kernel(const __grid_co
     float val = 0.f;
     const bool last = consume<SF>(stages + (size_t)slot * p.stage_bytes, p.sg, v, nseg, warp, xtab, xsx,
                                   part + slot * p.part_stride, &ucnt[slot], L, &val, ok, bf);
-    if (last && ok && lane < 16) p.y[16 * (u0 + v) + lane] = val * ctl->xinv;
+    if (last && ok && lane < 16) p.y[16 * (u0 + v) + lane] = val;
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
   }
@@ -638,37 +580,41 @@ uint32_t moe_decode_layout(MoeDecodeParams* p, uint32_t smem_limit, int grid) {
   (void)grid;
   const int W = kConsumerWarps;
   const uint32_t stage = up_to(std::max(2u * p->sg_gu.hstride, 2u * p->sg_d.hstride), 128u);
+  const uint32_t dslot = up_to(2u * p->sg_d.hstride, 128u);
   p->stage_bytes = stage;
+  p->dslot_bytes = dslot;
   p->htab_bytes = (uint32_t)(4 * p->fe);
   const uint32_t htab_region = std::max((uint32_t)p->k * p->htab_bytes, (uint32_t)(4 * p->ne));
   const uint32_t stg_bytes = (uint32_t)std::max(4 * p->d, 4 * p->k);
   p->part_stride = (uint32_t)std::max(W, std::max(p->d, p->fe) / kSegElems) * 16u;
   for (int S = kMaxStages; S >= 2; S--) {
-    uint32_t off = 2u * kMaxStages * 8u;
+    const int SD = (int)std::min<uint32_t>((uint32_t)kMaxStages, (uint32_t)S * stage / dslot);
+    uint32_t off = 4u * kMaxStages * 8u;  // full/empty barriers of both rings
     p->off_ctl = off;
     off = up_to(off + (uint32_t)sizeof(Ctl), 16);
     p->off_part = off;
     off = up_to(off + (uint32_t)S * p->part_stride * 4u, 16);
+    p->off_part_d = off;
+    off = up_to(off + (uint32_t)SD * p->part_stride * 4u, 16);
     p->off_ucnt = off;
-    off = up_to(off + (uint32_t)(S * 4), 16);
-    p->off_unit = off;
-    off = up_to(off + (uint32_t)(S * 4), 16);
+    off = up_to(off + (uint32_t)(2 * kMaxStages * 4), 16);
     p->off_ytile = off;
     off = up_to(off + (uint32_t)(2 * p->k * 16 * 4), 16);
     p->off_xtab = off;
     off = up_to(off + (uint32_t)(4 * p->d), 16);
     p->off_xsx = off;
-    off = up_to(off + (uint32_t)(p->d / 16 * 4), 16);
+    off = up_to(off + (uint32_t)(p->d / kSegElems * kMeta * 4), 16);
     p->off_htab = off;
     off = up_to(off + htab_region, 16);
     p->off_hsx = off;
-    off = up_to(off + (uint32_t)(p->k * (p->fe / 16) * 4), 16);
+    off = up_to(off + (uint32_t)(p->k * (p->fe / kSegElems) * kMeta * 4), 16);
     p->off_stg = off;
     off = up_to(off + stg_bytes, 128);
     p->off_stage = off;
     off += (uint32_t)S * stage + 16;
-    if (off <= smem_limit) {
+    if (off <= smem_limit && SD >= 1) {
       p->nstages = S;
+      p->nstages_d = SD;
       return off;
     }
   }
@@ -698,7 +644,7 @@ uint32_t gemv_layout(GemvParams* p, uint32_t smem_limit) {
     p->off_xtab = off;
     off = up_to(off + (uint32_t)(4 * p->n), 16);
     p->off_xsx = off;
-    off = up_to(off + (uint32_t)(p->n / 16 * 4), 16);
+    off = up_to(off + (uint32_t)(p->n / kSegElems * kMeta * 4), 16);
     p->off_stg = off;
     off = up_to(off + (uint32_t)(4 * p->n), 128);
     p->off_stage = off;

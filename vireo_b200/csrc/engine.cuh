@@ -52,7 +52,7 @@ VDEV void issue_unit(uint8_t* stage, uint64_t* full, const uint8_t* src0, const 
   if (src0) {
     const uint32_t gbytes = sg.G * sg.rb;  // bytes per copy group (multiple of 16)
     const uint32_t hbytes = 8u * sg.rb;
-#pragma unroll
+#pragma unroll 1
     for (uint32_t h = 0; h < 2; h++) {
       const uint8_t* hs = h ? src1 : src0;
       uint8_t* hd = stage + h * sg.hstride;
@@ -109,19 +109,19 @@ VDEV int lds_s8(const void* p) { return *reinterpret_cast<const int8_t*>(p); }
 VDEV uint32_t lds_u16(const void* p) { return *reinterpret_cast<const uint16_t*>(p); }
 
 // ---------------------------------------------------------------------------
-// B fragments of one segment held in registers (16 steps x 2 regs); a warp
+// B fragments of one segment held in registers (8 steps x 2 regs); a warp
 // that meets the same segment of the same table again (consecutive units
 // whose segment index lands on the same warp) skips the reload.
 // ---------------------------------------------------------------------------
 struct BFrag {
-  uint32_t b[16][2];
+  uint32_t b[kSegSteps][2];
   const uint8_t* key;
   VDEV void reset() { key = nullptr; }
   VDEV void get(const uint8_t* segtab, const LaneCtx& L) {
     if (segtab == key) return;
     key = segtab;
 #pragma unroll
-    for (int s = 0; s < 16; s++) {
+    for (int s = 0; s < kSegSteps; s++) {
       const uint2 v = lds64(segtab + s * kStepBytesB + L.boff);
       b[s][0] = L.bon ? v.x : 0u;
       b[s][1] = L.bon ? v.y : 0u;
@@ -129,196 +129,219 @@ struct BFrag {
   }
 };
 
+constexpr float kInv254 = 1.0f / 254.0f;
+// s * (d1-dot + d2-dot / 254) for one C column pair
+VDEV float dig(int c0, int c1) { return (float)c0 + (float)c1 * kInv254; }
+
 // ---------------------------------------------------------------------------
 // Segment kernels: accumulate one 256-value segment of rows g (r0) and g+8
-// (r1) into this lane's fp32 totals.  B: the segment's fragments; sx: the
-// segment's 8 sub-block sums (Q4_K only).  Each kernel runs two independent
-// accumulator chains so consecutive tensor-core ops do not wait on each
-// other.
+// (r1) into this lane's fp32 totals.  B: the segment's fragments; meta: the
+// segment's activation metadata (kMeta floats).  Independent scale groups
+// run as independent accumulator chains.
 // ---------------------------------------------------------------------------
 struct SegQ8 : Q8 {
-  VDEV static void run(const uint8_t* r0, const uint8_t* r1, const BFrag& B, const float* sx, const LaneCtx& L,
+  VDEV static void run(const uint8_t* r0, const uint8_t* r1, const BFrag& B, const float* meta, const LaneCtx& L,
                        float& tot0, float& tot1) {
     const uint8_t* p0 = r0 + 68 * L.t;
     const uint8_t* p1 = r1 + 68 * L.t;
-    const uint32_t w0a = lds32(p0), w8a = lds32(p0 + 32), w0b = lds32(p1), w8b = lds32(p1 + 32);
-    float ca[4] = {0.f, 0.f, 0.f, 0.f}, cb[4] = {0.f, 0.f, 0.f, 0.f};
+    uint32_t wa[17], wb[17];
 #pragma unroll
-    for (int s = 0; s < 8; s++) {
-      // block A (steps 0..7) and block B (steps 8..15) interleaved
-      const uint32_t wa = (s < 7) ? lds32(p0 + 4 + 4 * s) : byte_perm(w0a, w8a, 0x5432u);
-      const uint32_t wb = (s < 7) ? lds32(p1 + 4 + 4 * s) : byte_perm(w0b, w8b, 0x5432u);
-      const uint32_t xa = lds32(p0 + 36 + 4 * s), xb = lds32(p1 + 36 + 4 * s);
-      uint32_t a[4], e[4];
-      conv(wa, a[0], a[2]);
-      conv(wb, a[1], a[3]);
-      conv(xa, e[0], e[2]);
-      conv(xb, e[1], e[3]);
-      mma_16816(ca, a, B.b[s][0], B.b[s][1]);
-      mma_16816(cb, e, B.b[8 + s][0], B.b[8 + s][1]);
+    for (int i = 0; i < 17; i++) {
+      wa[i] = lds32(p0 + 4 * i);
+      wb[i] = lds32(p1 + 4 * i);
     }
-    // the halves hold 1152 + q: remove 1152 * (sum of x over the block)
-    const float oa = kOffset * sx[2 * L.t], ob = kOffset * sx[2 * L.t + 1];
-    tot0 += h_lo(w0a) * ((ca[0] + ca[1]) - oa) + h_hi(w8a) * ((cb[0] + cb[1]) - ob);
-    tot1 += h_lo(w0b) * ((ca[2] + ca[3]) - oa) + h_hi(w8b) * ((cb[2] + cb[3]) - ob);
+    int ca[4], cb[4];
+#pragma unroll
+    for (int m = 0; m < 4; m++) {
+      uint32_t a[4], e[4];
+      a[0] = wa[1 + 2 * m];
+      a[1] = wb[1 + 2 * m];
+      a[2] = (m < 3) ? wa[2 + 2 * m] : byte_perm(wa[0], wa[8], 0x5432u);
+      a[3] = (m < 3) ? wb[2 + 2 * m] : byte_perm(wb[0], wb[8], 0x5432u);
+      e[0] = wa[9 + 2 * m];
+      e[1] = wb[9 + 2 * m];
+      e[2] = wa[10 + 2 * m];
+      e[3] = wb[10 + 2 * m];
+      if (m == 0) {
+        imma_s8_z(ca, a, B.b[0][0], B.b[0][1]);
+        imma_s8_z(cb, e, B.b[4][0], B.b[4][1]);
+      } else {
+        imma_s8(ca, a, B.b[m][0], B.b[m][1]);
+        imma_s8(cb, e, B.b[4 + m][0], B.b[4 + m][1]);
+      }
+    }
+    const float sA = meta[2 * L.t], sB = meta[2 * L.t + 1];
+    tot0 += h_lo(wa[0]) * sA * dig(ca[0], ca[1]) + h_hi(wa[8]) * sB * dig(cb[0], cb[1]);
+    tot1 += h_lo(wb[0]) * sA * dig(ca[2], ca[3]) + h_hi(wb[8]) * sB * dig(cb[2], cb[3]);
   }
 };
 
 struct SegQ4K : Q4K {
-  VDEV static void run(const uint8_t* r0, const uint8_t* r1, const BFrag& B, const float* sx, const LaneCtx& L,
+  VDEV static void run(const uint8_t* r0, const uint8_t* r1, const BFrag& B, const float* meta, const LaneCtx& L,
                        float& tot0, float& tot1) {
     const uint4 hd0 = lds128(r0), hd1 = lds128(r1);
+    const uint4 qa0 = lds128(r0 + 16 + 32 * L.t), qa1 = lds128(r0 + 32 + 32 * L.t);
+    const uint4 qb0 = lds128(r1 + 16 + 32 * L.t), qb1 = lds128(r1 + 32 + 32 * L.t);
+    const uint32_t wa[8] = {qa0.x, qa0.y, qa0.z, qa0.w, qa1.x, qa1.y, qa1.z, qa1.w};
+    const uint32_t wb[8] = {qb0.x, qb0.y, qb0.z, qb0.w, qb1.x, qb1.y, qb1.z, qb1.w};
+    int cl[4], ch[4];
+#pragma unroll
+    for (int m = 0; m < 4; m++) {
+      uint32_t a[4], e[4];
+      a[0] = wa[2 * m] & 0x0F0F0F0Fu;
+      a[1] = wb[2 * m] & 0x0F0F0F0Fu;
+      a[2] = wa[2 * m + 1] & 0x0F0F0F0Fu;
+      a[3] = wb[2 * m + 1] & 0x0F0F0F0Fu;
+      e[0] = wa[2 * m] & 0xF0F0F0F0u;
+      e[1] = wb[2 * m] & 0xF0F0F0F0u;
+      e[2] = wa[2 * m + 1] & 0xF0F0F0F0u;
+      e[3] = wb[2 * m + 1] & 0xF0F0F0F0u;
+      if (m == 0) {
+        imma_u8_z(cl, a, B.b[0][0], B.b[0][1]);
+        imma_u8_z(ch, e, B.b[4][0], B.b[4][1]);
+      } else {
+        imma_u8(cl, a, B.b[m][0], B.b[m][1]);
+        imma_u8(ch, e, B.b[4 + m][0], B.b[4 + m][1]);
+      }
+    }
     const int j0 = 2 * L.t, j1 = 2 * L.t + 1;
     uint32_t sc00, mn00, sc01, mn01, sc10, mn10, sc11, mn11;
     scale_min(hd0.y, hd0.z, hd0.w, j0, sc00, mn00);
     scale_min(hd0.y, hd0.z, hd0.w, j1, sc01, mn01);
     scale_min(hd1.y, hd1.z, hd1.w, j0, sc10, mn10);
     scale_min(hd1.y, hd1.z, hd1.w, j1, sc11, mn11);
-    // low nibbles (sub-block 2t): A = sc*(1024+q) - 1024*sc ; high nibbles
-    // (sub-block 2t+1, stored as 1024+16q): A = (sc/16)*(1024+16q) - 64*sc
-    const uint32_t SL0 = h2_splat((float)sc00), CL0 = h2_splat(-1024.f * (float)sc00);
-    const uint32_t SH0 = h2_splat((float)sc01 * 0.0625f), CH0 = h2_splat(-64.f * (float)sc01);
-    const uint32_t SL1 = h2_splat((float)sc10), CL1 = h2_splat(-1024.f * (float)sc10);
-    const uint32_t SH1 = h2_splat((float)sc11 * 0.0625f), CH1 = h2_splat(-64.f * (float)sc11);
-    const uint4 qa0 = lds128(r0 + 16 + 32 * L.t), qa1 = lds128(r0 + 32 + 32 * L.t);
-    const uint4 qb0 = lds128(r1 + 16 + 32 * L.t), qb1 = lds128(r1 + 32 + 32 * L.t);
-    const uint32_t wa[8] = {qa0.x, qa0.y, qa0.z, qa0.w, qa1.x, qa1.y, qa1.z, qa1.w};
-    const uint32_t wb[8] = {qb0.x, qb0.y, qb0.z, qb0.w, qb1.x, qb1.y, qb1.z, qb1.w};
-    float cl[4] = {0.f, 0.f, 0.f, 0.f}, ch[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-      uint32_t a[4], e[4], t02, t13;
-      conv_lo(wa[i], t02, t13);
-      a[0] = h2_fma(t02, SL0, CL0);
-      a[2] = h2_fma(t13, SL0, CL0);
-      conv_lo(wb[i], t02, t13);
-      a[1] = h2_fma(t02, SL1, CL1);
-      a[3] = h2_fma(t13, SL1, CL1);
-      conv_hi(wa[i], t02, t13);
-      e[0] = h2_fma(t02, SH0, CH0);
-      e[2] = h2_fma(t13, SH0, CH0);
-      conv_hi(wb[i], t02, t13);
-      e[1] = h2_fma(t02, SH1, CH1);
-      e[3] = h2_fma(t13, SH1, CH1);
-      mma_16816(cl, a, B.b[2 * i][0], B.b[2 * i][1]);
-      mma_16816(ch, e, B.b[2 * i + 1][0], B.b[2 * i + 1][1]);
-    }
-    const float sxa = sx[j0], sxb = sx[j1];
-    const float mt0 = (float)mn00 * sxa + (float)mn01 * sxb;
-    const float mt1 = (float)mn10 * sxa + (float)mn11 * sxb;
-    tot0 += h_lo(hd0.x) * ((cl[0] + cl[1]) + (ch[0] + ch[1])) - h_hi(hd0.x) * mt0;
-    tot1 += h_lo(hd1.x) * ((cl[2] + cl[3]) + (ch[2] + ch[3])) - h_hi(hd1.x) * mt1;
+    const float s0 = meta[j0], s1 = meta[j1] * 0.0625f;  // high nibbles were 16 q
+    const float S0 = meta[8 + j0], S1 = meta[8 + j1];
+    tot0 += h_lo(hd0.x) * ((float)sc00 * s0 * dig(cl[0], cl[1]) + (float)sc01 * s1 * dig(ch[0], ch[1])) -
+            h_hi(hd0.x) * ((float)mn00 * S0 + (float)mn01 * S1);
+    tot1 += h_lo(hd1.x) * ((float)sc10 * s0 * dig(cl[2], cl[3]) + (float)sc11 * s1 * dig(ch[2], ch[3])) -
+            h_hi(hd1.x) * ((float)mn10 * S0 + (float)mn11 * S1);
   }
 };
 
 struct SegQ6K : Q6K {
-  VDEV static void run(const uint8_t* r0, const uint8_t* r1, const BFrag& B, const float* sx, const LaneCtx& L,
+  VDEV static void run(const uint8_t* r0, const uint8_t* r1, const BFrag& B, const float* meta, const LaneCtx& L,
                        float& tot0, float& tot1) {
     const float d0 = __half2float(__ushort_as_half((unsigned short)lds_u16(r0 + 208)));
     const float d1 = __half2float(__ushort_as_half((unsigned short)lds_u16(r1 + 208)));
     const int qlo = 32 * (L.t & 1);
 #pragma unroll
-    for (int mp = 0; mp < 4; mp += 2) {
-      // macro-steps mp (l0 = 0) and mp + 1 (l0 = 16) of half h in two chains
-      const int h = mp >> 1;
-      uint32_t la[8], ha[8], lb[8], hb[8];
-      ld16u(r0 + 64 * h + qlo, *reinterpret_cast<uint32_t(*)[4]>(la));
-      ld16u(r0 + 64 * h + qlo + 16, *reinterpret_cast<uint32_t(*)[4]>(la + 4));
-      ld16u(r0 + 128 + 32 * h, *reinterpret_cast<uint32_t(*)[4]>(ha));
-      ld16u(r0 + 128 + 32 * h + 16, *reinterpret_cast<uint32_t(*)[4]>(ha + 4));
-      ld16u(r1 + 64 * h + qlo, *reinterpret_cast<uint32_t(*)[4]>(lb));
-      ld16u(r1 + 64 * h + qlo + 16, *reinterpret_cast<uint32_t(*)[4]>(lb + 4));
-      ld16u(r1 + 128 + 32 * h, *reinterpret_cast<uint32_t(*)[4]>(hb));
-      ld16u(r1 + 128 + 32 * h + 16, *reinterpret_cast<uint32_t(*)[4]>(hb + 4));
-      float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int s = 0; s < 4; s++) {
-        uint32_t a[4], e[4];
-        conv(six(la[s], ha[s], L.t), a[0], a[2]);
-        conv(six(lb[s], hb[s], L.t), a[1], a[3]);
-        conv(six(la[4 + s], ha[4 + s], L.t), e[0], e[2]);
-        conv(six(lb[4 + s], hb[4 + s], L.t), e[1], e[3]);
-        mma_16816(c0, a, B.b[4 * mp + s][0], B.b[4 * mp + s][1]);
-        mma_16816(c1, e, B.b[4 * mp + 4 + s][0], B.b[4 * mp + 4 + s][1]);
-      }
-      const int gi = 8 * h + 2 * L.t;  // scale group of chain 0 (chain 1: gi + 1)
-      const float s00 = (float)lds_s8(r0 + 192 + gi), s01 = (float)lds_s8(r0 + 193 + gi);
-      const float s10 = (float)lds_s8(r1 + 192 + gi), s11 = (float)lds_s8(r1 + 193 + gi);
-      // the halves hold 1024 + z = (z - 32) + 1056: remove 1056 * group sum
-      const float o0 = kOffset * sx[gi], o1 = kOffset * sx[gi + 1];
-      tot0 += (d0 * s00) * ((c0[0] + c0[1]) - o0) + (d0 * s01) * ((c1[0] + c1[1]) - o1);
-      tot1 += (d1 * s10) * ((c0[2] + c0[3]) - o0) + (d1 * s11) * ((c1[2] + c1[3]) - o1);
+    for (int q = 0; q < 4; q++) {
+      // scale group q: half h = q >> 1, l0 = 16 (q & 1); steps 2q, 2q + 1
+      const int h = q >> 1, l0 = 16 * (q & 1);
+      uint32_t la[4], ha[4], lb[4], hb[4];
+      ld16u(r0 + 64 * h + qlo + l0, la);
+      ld16u(r0 + 128 + 32 * h + l0, ha);
+      ld16u(r1 + 64 * h + qlo + l0, lb);
+      ld16u(r1 + 128 + 32 * h + l0, hb);
+      uint32_t a[4], e[4];
+      a[0] = six(la[0], ha[0], L.t);
+      a[1] = six(lb[0], hb[0], L.t);
+      a[2] = six(la[1], ha[1], L.t);
+      a[3] = six(lb[1], hb[1], L.t);
+      e[0] = six(la[2], ha[2], L.t);
+      e[1] = six(lb[2], hb[2], L.t);
+      e[2] = six(la[3], ha[3], L.t);
+      e[3] = six(lb[3], hb[3], L.t);
+      int c[4];
+      imma_u8_z(c, a, B.b[2 * q][0], B.b[2 * q][1]);
+      imma_u8(c, e, B.b[2 * q + 1][0], B.b[2 * q + 1][1]);
+      const int gi = 8 * h + 2 * L.t + (q & 1);  // scale index = 16-group index
+      const float xs = meta[4 * h + L.t], S16 = 32.f * meta[16 + gi];
+      tot0 += d0 * (float)lds_s8(r0 + 192 + gi) * (xs * dig(c[0], c[1]) - S16);
+      tot1 += d1 * (float)lds_s8(r1 + 192 + gi) * (xs * dig(c[2], c[3]) - S16);
     }
   }
 };
 
 // ---------------------------------------------------------------------------
-// B tables: an fp32 vector v[K] scaled by a power of two (so that max|v|
-// lands in [2^14, 2^15) and the f16 split neither overflows nor flushes),
-// split into x_hi + x_lo and laid out in each format's k order.
-// ---------------------------------------------------------------------------
-
-// power-of-two scale for a vector whose max magnitude is amax
-VDEV float pow2_scale(float amax) {
-  if (!(amax > 0.f) || !isfinite(amax)) return 1.f;
-  int ex;
-  frexpf(amax, &ex);  // amax in [2^(ex-1), 2^ex)
-  int e = 15 - ex;
-  e = e > 100 ? 100 : (e < -100 ? -100 : e);
-  return ldexpf(1.f, e);
-}
-
 // B tables of 256-value segments, one warp per segment.  Segment i of the
-// source is the fp32 values src[256 i, 256 i + 256), scaled by
-// scales[i / segs_per_vec] (a power of two); its table is the 1 KB at
-// dst + 1024 i: 16 steps x 4 threads x 16 bytes, the 16-byte chunk c =
-// 4 step + t holding f16 hi[4] then f16 lo[4] of elements F::elem(step, t,
-// j), j = 0..3.  Its group sums sx[i * 256/GS + g] are the fp32 sums of
-// hi + lo over the natural groups of GS = F::kSumGroup values (Q8_0 and
-// Q4_K: 32, Q6_K: 16), the offset / min corrections of the segment kernels.
+// source is the fp32 values src[256 i, 256 i + 256).  Its table is the first
+// 512 bytes of dst + kSegTabBytes i: step m, thread t, digit c at byte
+// 64 m + 16 t + 8 c: the digits of elements F::elem(m, t, r, j) for r = 0, 1
+// and j = 0..3.  Its metadata meta[kMeta i ..] holds, per natural 32-value
+// group q, the scale s_q = max|x| / 127 and the sum of x~ = s (d1 + d2/254),
+// and the same sums per 16-value group.  A group holding inf or NaN gets a
+// NaN scale, so that its dot products come out NaN as the reference's do.
 // Every read of a segment precedes every write to it (warp-synchronous), so
-// dst may alias src: 4 bytes of table per value, the same footprint.
+// dst may alias src (the same 1 KB footprint per segment).
+// ---------------------------------------------------------------------------
 template <class F>
-VDEV void build_tables(const float* src, uint8_t* dst, float* sx, int nseg, int segs_per_vec, const float* scales,
-                       int warp, int nwarps, int lane) {
-  constexpr int GS = F::kSumGroup;
+VDEV void build_tables(const float* src, uint8_t* dst, float* meta, int nseg, int warp, int nwarps, int lane) {
 #pragma unroll 1
   for (int i = warp; i < nseg; i += nwarps) {
-    const float sc = scales[i / segs_per_vec];
     const float* v = src + (size_t)i * kSegElems;
-    // group sums: lane l holds the natural values [8 l, 8 l + 8)
-    const float4 a = *reinterpret_cast<const float4*>(v + 8 * lane);
-    const float4 b = *reinterpret_cast<const float4*>(v + 8 * lane + 4);
-    const float nat[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    float s = 0.f;
+    uint8_t* tab = dst + (size_t)i * kSegTabBytes;
+    // lane l holds the natural values [8 l, 8 l + 8): 32-group l / 4
+    const float4 a4 = *reinterpret_cast<const float4*>(v + 8 * lane);
+    const float4 b4 = *reinterpret_cast<const float4*>(v + 8 * lane + 4);
+    const float x[8] = {a4.x, a4.y, a4.z, a4.w, b4.x, b4.y, b4.z, b4.w};
+    float mx = 0.f;
+    bool bad = false;
 #pragma unroll
     for (int q = 0; q < 8; q++) {
-      const float x = nat[q] * sc;
-      const float hi = __half2float(__float2half_rn(x));
-      s += hi + __half2float(__float2half_rn(x - hi));
+      mx = fmaxf(mx, fabsf(x[q]));
+      bad |= !(fabsf(x[q]) <= 3.402823466e38f);
     }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    bad = __shfl_xor_sync(0xffffffffu, (int)bad, 1) | __shfl_xor_sync(0xffffffffu, (int)bad, 2) | bad;
+    const float sc = bad ? __int_as_float(0x7fc00000) : mx * (1.0f / 127.0f);
+    const float inv = (mx > 0.f && !bad) ? 127.0f / mx : 0.f;
+    uint32_t lo1 = 0, hi1 = 0, lo2 = 0, hi2 = 0;
+    int s1 = 0, s2 = 0;
 #pragma unroll
-    for (int o = 1; o < GS / 8; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    // table chunks c = lane and lane + 32
-    uint4 out[2];
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-      const int c = lane + 32 * h, step = c >> 2, t = c & 3;
-      uint32_t hv[4], lv[4];
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const float x = v[F::elem(step, t, j)] * sc;
-        const __half hh = __float2half_rn(x);
-        hv[j] = __half_as_ushort(hh);
-        lv[j] = __half_as_ushort(__float2half_rn(x - __half2float(hh)));
+    for (int q = 0; q < 8; q++) {
+      const float y = x[q] * inv;
+      const float r1 = fminf(fmaxf(rintf(y), -127.f), 127.f);
+      const float r2 = fminf(fmaxf(rintf((y - r1) * 254.f), -127.f), 127.f);
+      const int i1 = (int)r1, i2 = (int)r2;
+      s1 += i1;
+      s2 += i2;
+      const uint32_t b1 = (uint32_t)(i1 & 0xFF), b2 = (uint32_t)(i2 & 0xFF);
+      if (q < 4) {
+        lo1 |= b1 << (8 * q);
+        lo2 |= b2 << (8 * q);
+      } else {
+        hi1 |= b1 << (8 * (q - 4));
+        hi2 |= b2 << (8 * (q - 4));
       }
-      out[h] = make_uint4(hv[0] | (hv[1] << 16), hv[2] | (hv[3] << 16), lv[0] | (lv[1] << 16), lv[2] | (lv[3] << 16));
+    }
+    // sums of x~ per 16-group (lane pairs) and per 32-group (lane quads)
+    s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+    s2 += __shfl_xor_sync(0xffffffffu, s2, 1);
+    const float sum16 = sc * ((float)s1 + (float)s2 * kInv254);
+    const int t1 = s1 + __shfl_xor_sync(0xffffffffu, s1, 2), t2 = s2 + __shfl_xor_sync(0xffffffffu, s2, 2);
+    const float sum32 = sc * ((float)t1 + (float)t2 * kInv254);
+    __syncwarp();  // every lane holds its values: the segment may be overwritten
+    // natural-order digits in the scratch half: d1 at +512, d2 at +768
+    *reinterpret_cast<uint2*>(tab + 512 + 8 * lane) = make_uint2(lo1, hi1);
+    *reinterpret_cast<uint2*>(tab + 768 + 8 * lane) = make_uint2(lo2, hi2);
+    if ((lane & 3) == 0) {
+      meta[(size_t)i * kMeta + lane / 4] = sc;
+      meta[(size_t)i * kMeta + 8 + lane / 4] = sum32;
+    }
+    if ((lane & 1) == 0) meta[(size_t)i * kMeta + 16 + lane / 2] = sum16;
+    __syncwarp();
+    // table chunks ch = lane, lane + 32: step m = ch >> 3, thread t = (ch >> 1) & 3, digit c = ch & 1
+    uint2 out[2];
+#pragma unroll
+    for (int hh = 0; hh < 2; hh++) {
+      const int ch = lane + 32 * hh, m = ch >> 3, t = (ch >> 1) & 3, c = ch & 1;
+      const uint8_t* nat = tab + 512 + 256 * c;
+      uint32_t w[2];
+#pragma unroll
+      for (int r = 0; r < 2; r++) {
+        uint32_t acc = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc |= (uint32_t)nat[F::elem(m, t, r, j)] << (8 * j);
+        w[r] = acc;
+      }
+      out[hh] = make_uint2(w[0], w[1]);
     }
     __syncwarp();
-    if ((lane & (GS / 8 - 1)) == 0) sx[(size_t)i * (kSegElems / GS) + lane / (GS / 8)] = s;
-    uint4* d4 = reinterpret_cast<uint4*>(dst + (size_t)i * (16 * kStepBytesB));
-    d4[lane] = out[0];
-    d4[lane + 32] = out[1];
+    reinterpret_cast<uint2*>(tab)[lane] = out[0];
+    reinterpret_cast<uint2*>(tab)[lane + 32] = out[1];
     __syncwarp();
   }
 }
@@ -333,7 +356,7 @@ VDEV void build_tables(const float* src, uint8_t* dst, float* sx, int nseg, int 
 // ---------------------------------------------------------------------------
 template <class S>
 VDEV bool consume_unit(const uint8_t* stage, const StageGeom& sg, int v, int nseg, int W, int w,
-                       const uint8_t* btab, const float* sx, float* part, int* ucnt, const LaneCtx& L,
+                       const uint8_t* btab, const float* meta, float* part, int* ucnt, const LaneCtx& L,
                        float* row_val, BFrag& bf) {
   const uint8_t* r0 = stage_row(stage, sg, L.g);
   const uint8_t* r1 = stage_row(stage, sg, L.g + 8);
@@ -342,9 +365,8 @@ VDEV bool consume_unit(const uint8_t* stage, const StageGeom& sg, int v, int nse
 #pragma unroll 1
   for (int seg = first; seg < nseg; seg += W) {
     float tot0 = 0.f, tot1 = 0.f;
-    bf.get(btab + seg * (16 * kStepBytesB), L);
-    S::run(r0 + seg * S::kSegBytes, r1 + seg * S::kSegBytes, bf, sx + seg * (kSegElems / S::kSumGroup), L, tot0,
-           tot1);
+    bf.get(btab + seg * kSegTabBytes, L);
+    S::run(r0 + seg * S::kSegBytes, r1 + seg * S::kSegBytes, bf, meta + seg * kMeta, L, tot0, tot1);
     tot0 += __shfl_xor_sync(0xffffffffu, tot0, 1);
     tot1 += __shfl_xor_sync(0xffffffffu, tot1, 1);
     tot0 += __shfl_xor_sync(0xffffffffu, tot0, 2);

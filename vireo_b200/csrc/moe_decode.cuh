@@ -17,6 +17,9 @@
 //   D  units (expert slot t, 16 rows of the down matrix); epilogue writes the
 //      expert's rows and the last of the k experts to finish a 16-row tile
 //      combines them in rank order into the residual.
+// The weight stages form two rings over one shared-memory area: gate/up
+// units in stages sized for them, down units in (usually smaller) slots of
+// their own, so that more down units are in flight during gate/up.
 #pragma once
 #include <stdint.h>
 
@@ -24,12 +27,13 @@
 
 namespace vireo {
 
-constexpr int kConsumerWarps = 8;
+constexpr int kConsumerWarps = 12;
 constexpr int kProducerWarps = 4;  // issue the 16-byte cp.async weight copies
 constexpr int kProducerThreads = 32 * kProducerWarps;
 constexpr int kDecodeThreads = 32 * (kConsumerWarps + kProducerWarps);
 constexpr int kRouterChunk = 512;
 constexpr int kMaxTopK = 64;
+constexpr int kMaxHValues = 8192;  // n_used * ffn_exp: h scratch and the down tables in shared memory
 
 // Per-launch synchronisation words in device scratch.  All start at zero;
 // the last CTA to leave a launch puts them back to zero.
@@ -43,7 +47,6 @@ struct MoeSync {
   SyncWord router_arrive;  // CTAs done with their router partials
   SyncWord g_done;         // gate/up units finished (added once per CTA)
   SyncWord exit_cnt;       // CTAs done with the launch
-  SyncWord h_amax;         // [kMaxTopK] max |h| per expert slot (float bits), one atomic per CTA and slot
 };
 
 struct MoeScratch {
@@ -63,13 +66,15 @@ struct MoeDecodeParams {
   float* wts_out;                    // [k] or null
   MoeScratch s;
   StageGeom sg_gu, sg_d;
-  uint32_t stage_bytes;
+  uint32_t stage_bytes;  // gate/up ring: nstages stages of stage_bytes
   int nstages;
+  uint32_t dslot_bytes;  // down ring: nstages_d slots of dslot_bytes over the same memory
+  int nstages_d;
   // shared-memory offsets (bytes)
-  uint32_t off_part, off_ucnt, off_unit, off_ytile, off_ctl, off_xtab, off_xsx, off_htab, off_hsx, off_stg,
+  uint32_t off_part, off_part_d, off_ucnt, off_ytile, off_ctl, off_xtab, off_xsx, off_htab, off_hsx, off_stg,
       off_stage;
   uint32_t htab_bytes;  // per expert table bytes
-  uint32_t hsx_count;   // per expert group sums
+  uint32_t hsx_count;   // activation metadata floats per expert table
   uint32_t part_stride; // floats of segment partials per stage
   unsigned long long* trace;  // optional: kTraceSlots %globaltimer stamps per CTA
 };

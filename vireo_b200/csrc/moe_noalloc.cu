@@ -31,7 +31,7 @@
 namespace vireo {
 namespace {
 
-// sync words (1 KiB) + status (256 B) + expert table (<= 6 KiB for 256
+// sync words (768 B) + status (256 B) + expert table (<= 6 KiB for 256
 // experts) + router partials (<= 8 KiB) + h (<= 32 KiB): 64 KiB covers every
 // shape gguf_moe_create accepts
 constexpr size_t kNoAllocScratchBytes = 64 * 1024;
@@ -94,7 +94,7 @@ extern "C" int gguf_moe_ffn_noalloc(const gguf_moe_desc* desc, const float* hb, 
     return fail(VIREO_ERR_ARG);
   if (D.router_type != T_F32 || D.gate_type != D.up_type || !fast_format(D.gate_type) ||
       !fast_format(D.down_type) || D.dim % kRouterChunk || D.dim > 8 * kRouterChunk || D.ffn_exp % kSegElems ||
-      D.n_experts > 256 || D.ffn_exp % (32 * kConsumerWarps) || D.n_used * D.ffn_exp > 32 * 32 * kConsumerWarps ||
+      D.n_experts > 256 || D.n_used * D.ffn_exp > kMaxHValues ||
       D.n_used > kMaxTopK)
     return fail(VIREO_ERR_UNSUPPORTED);
   const uint64_t gsl = (uint64_t)D.ffn_exp * row_bytes(D.gate_type, D.dim);
@@ -143,7 +143,7 @@ extern "C" int gguf_moe_ffn_noalloc(const gguf_moe_desc* desc, const float* hb, 
   if ((st = cuda_status(
            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S->smem_limit))))
     return fail(st);
-  p.hsx_count = (uint32_t)(D.ffn_exp / (D.down_type == T_Q6_K ? 16 : 32));
+  p.hsx_count = (uint32_t)(D.ffn_exp / kSegElems * kMeta);
   uint8_t* sb = S->scratch;
   p.s.sync = (MoeSync*)(sb + o_sy);
   p.s.err = (int*)(sb + o_err);

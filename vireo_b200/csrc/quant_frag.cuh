@@ -1,29 +1,27 @@
-// GGUF block formats -> tensor-core fragments.
+// GGUF block formats -> integer tensor-core fragments.
 //
-// The decode GEMV multiplies a 16-row weight tile by one activation vector
-// with mma.sync.m16n8k16 (f16 in, f32 accumulate).  Weights are the A
-// operand, dequantised in registers straight from the raw GGUF bytes the
-// TMA engine staged in shared memory; the activation vector is the B
-// operand, split into an f16 high part and an f16 residual so that x is
-// carried to ~22 bits (x_hi + x_lo), well inside the fp32-accumulate budget.
+// The decode GEMV multiplies 16-row weight tiles by one activation vector
+// with mma.sync.m16n8k32 (int8 x int8 -> int32).  Weights are the A operand,
+// read straight from the raw GGUF bytes staged in shared memory: Q8_0 quants
+// as s8, Q4_K nibbles and Q6_K 6-bit values as u8, only masked in place.
+// The activation vector is the B operand: for each natural 32-value group a
+// scale s = max|x| / 127 and two int8 digits per value, x ~ s (d1 + d2/254)
+// (|error| <= s / 508, about 1.6e-5 of the group's largest value).
 //
-// Fragment layout of m16n8k16 (lane = 4*g + t): A rows g and g+8 at k-slots
-// {2t, 2t+1, 2t+8, 2t+9}; B column g at the same k-slots; C row g / g+8 at
-// columns 2t, 2t+1.  The k order inside a step is free as long as A and B
-// agree, so every format chooses the order that keeps a thread's weights in
-// one aligned 32-bit word: k-slots (2t, 2t+1, 2t+8, 2t+9) <- bytes
-// (0, 2, 1, 3) of that word ("kPerm").
+// Fragment layout of m16n8k32 (lane = 4 g + t): A registers {row g, k 4t..
+// 4t+3}, {row g+8, same k}, {row g, k 16+4t..}, {row g+8, k 16+4t..}; B
+// registers {k 4t.., column g}, {k 16+4t.., column g}; C {row g: columns 2t,
+// 2t+1}, {row g+8: columns 2t, 2t+1}.  The order of k inside a step is free
+// as long as A and B agree, so each format maps thread t's k-slots to 8 of
+// its OWN values (all in one scale group).  "Column trick": B column 2t
+// holds d1 and column 2t+1 holds d2, only at thread t's k-slots, so lane
+// (g, t) ends a run of steps holding in C[2t], C[2t+1] the exact integer
+// dot products over the values it supplied, and applies its own block
+// scales in fp32.
 //
-// "Column trick": B column 2t holds x_hi and column 2t+1 holds x_lo only at
-// thread t's own k-slots (zero elsewhere), so after a run of steps lane
-// (g, t) holds in C[2t] + C[2t+1] the dot product over exactly the weights
-// thread t supplied.  Each thread can therefore follow its own scale group
-// (Q8_0 block, Q6_K 16-value group) and apply that scale in fp32.
-//
-// Integer-valued dequantisation is exact in f16: 0x6400 | u is 1024 + u, so
-// a byte or nibble placed in the low mantissa bits and a subtraction (or an
-// FMA whose exact result is an integer below 2048) recovers the quant value
-// (or scale * quant for Q4_K, whose 6-bit scale times 4-bit quant is < 2048).
+// A segment is 256 consecutive values of a row: 8 steps of k32, thread t
+// supplying 64 values.  F::elem(m, t, r, j) is the segment value behind step
+// m, thread t, register r (0: k 4t+j, 1: k 16+4t+j), byte j.
 //
 // Reference block layouts: vireo src/gguf_compute.c:38-42 (structs),
 // :45-51 (Q4_K scale/min packing), :52-66 (Q4_K), :83-103 (Q6_K).
@@ -40,9 +38,13 @@ namespace vireo {
 
 enum : uint32_t { T_F32 = 0, T_F16 = 1, T_Q5_0 = 6, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14 };
 
-constexpr int kSegElems = 256;  // every fast-path format works in 256-value segments
-constexpr int kStepBytesB = 64; // B table bytes per k16 step: [t][hi,lo][4 x f16]
-VHD int kperm(int j) { return (j == 0) ? 0 : (j == 1) ? 2 : (j == 2) ? 1 : 3; }
+constexpr int kSegElems = 256;   // every fast-path format works in 256-value segments
+constexpr int kSegSteps = 8;     // k32 tensor-core steps per segment
+constexpr int kStepBytesB = 64;  // B table bytes per step: [t][digit][2 regs x 4 x int8]
+constexpr int kSegTabBytes = 1024;  // B table stride per segment (512 used, 512 build scratch)
+constexpr int kMeta = 32;        // floats of per-segment activation metadata:
+                                 // [0,8) scale of each 32-group, [8,16) sum of x~ per
+                                 // 32-group, [16,32) sum of x~ per 16-group
 
 // ---- portable bit helpers (host versions for the self-test) --------------
 // 3-input bitwise function with lookup table lut (a, b, c <-> 0xF0, 0xCC, 0xAA)
@@ -80,54 +82,34 @@ VHD uint32_t byte_perm(uint32_t a, uint32_t b, uint32_t s) {
 
 // ---- Q8_0: 34-byte blocks (f16 d, 32 x int8), segment = 8 blocks --------
 // Thread t owns the block pair (2t, 2t+1) = bytes [68t, 68t+68) of the
-// segment, a 4-byte-aligned span of 17 words W0..W16:
-//   W0 = [dA, dA, q0, q1], W1..W7 = q2..q29, W8 = [q30, q31, dB, dB],
-//   W9..W16 = block B's 32 quants.
-// Steps 0..6 use W1..W7, step 7 uses [q0,q1,q30,q31] = prmt(W0, W8), steps
-// 8..15 use W9..W16.  After step 7 and step 15 the block's d scales C.
+// segment, 17 aligned words: W0 = [dA dA q0 q1], W1..W7 = q2..q29,
+// W8 = [q30 q31 dB dB], W9..W16 = block B's 32 quants.  Steps 0..3 cover
+// block A with (W1, W2), (W3, W4), (W5, W6), (W7, [q0 q1 q30 q31] = prmt(W0,
+// W8)); steps 4..7 cover block B with (W9, W10) .. (W15, W16).  The quants
+// are the s8 A operand as they are.
 struct Q8 {
   static constexpr uint32_t kType = T_Q8_0;
-  static constexpr int kSegBytes = 272, kSteps = 16;
-  static constexpr int kSumGroup = 32;  // x sums per block (offset correction)
-  VHD static int elem(int step, int t, int j) {
-    int base = 64 * t;
-    if (step < 7) return base + 2 + 4 * step + kperm(j);
-    if (step == 7) return base + ((j == 0) ? 0 : (j == 1) ? 30 : (j == 2) ? 1 : 31);
-    return base + 32 + 4 * (step - 8) + kperm(j);
+  static constexpr int kSegBytes = 272;
+  VHD static int elem(int m, int t, int r, int j) {
+    const int base = 64 * t;
+    if (m >= 4) return base + 32 + 8 * (m - 4) + 4 * r + j;
+    if (m < 3 || r == 0) return base + 4 * (1 + 2 * m + r) - 2 + j;
+    return base + (j < 2 ? j : 28 + j);
   }
-  // int8 x4 -> (f16x2 of bytes 0,2 ; f16x2 of bytes 1,3) holding 1152 + q,
-  // exact.  One lop3 per pair: the sign bit of each byte is flipped (q+128
-  // as an unsigned byte), the other byte of each half becomes 0x64; bit
-  // classes per (b, c): (0,0) keep, (1,0) flip, (1,1) one, (0,1) zero.
-  VHD static void conv(uint32_t w, uint32_t& h02, uint32_t& h13) {
-    h02 = lop3t<0x9C>(w, 0x64806480u, 0xFF00FF00u);
-    h13 = lop3t<0x9C>(w >> 8, 0x64806480u, 0xFF00FF00u);
-  }
-  static constexpr float kOffset = 1152.f;  // removed with the block sum of x
 };
 
 // ---- Q4_K: 144-byte super-blocks, segment = 1 super-block ---------------
-// Thread t owns the 64-value chunk t: bytes qs[32t, 32t+32) (two 16-byte
-// aligned loads); low nibbles are sub-block 2t, high nibbles sub-block
-// 2t+1.  Step 2i uses the low nibbles of word i, step 2i+1 the high ones.
-// The 6-bit sub-block scale is folded into A (sc*q <= 945, exact in f16);
-// the super-block d and the min term -dmin*m_j*sum(x over sub-block j) are
-// applied in fp32 once per segment.
+// Thread t owns the 64-value chunk t: the 32 bytes qs[32t, 32t+32) as words
+// w0..w7; byte l's low nibble is value 64t + l (sub-block 2t), its high
+// nibble value 64t + 32 + l (sub-block 2t+1).  Steps 0..3: low nibbles of
+// (w[2m], w[2m+1]) (w & 0x0F0F0F0F, u8 q); steps 4..7: high nibbles of
+// (w[2m-8], w[2m-7]) as u8 16q (w & 0xF0F0F0F0, the 1/16 goes to the
+// scale).  Value = d sc_j q - dmin m_j; the min term is applied with the
+// group sum of x.
 struct Q4K {
   static constexpr uint32_t kType = T_Q4_K;
-  static constexpr int kSegBytes = 144, kSteps = 16;
-  static constexpr int kSumGroup = 32;  // x sums per sub-block (min term)
-  VHD static int elem(int step, int t, int j) { return 64 * t + 32 * (step & 1) + 4 * (step >> 1) + kperm(j); }
-  // low nibbles: halves 1024 + q (bytes 0,2) and (bytes 1,3)
-  VHD static void conv_lo(uint32_t w, uint32_t& h02, uint32_t& h13) {
-    h02 = (w & 0x000F000Fu) | 0x64006400u;
-    h13 = ((w >> 8) & 0x000F000Fu) | 0x64006400u;
-  }
-  // high nibbles: halves 1024 + 16*q
-  VHD static void conv_hi(uint32_t w, uint32_t& h02, uint32_t& h13) {
-    h02 = (w & 0x00F000F0u) | 0x64006400u;
-    h13 = ((w >> 8) & 0x00F000F0u) | 0x64006400u;
-  }
+  static constexpr int kSegBytes = 144;
+  VHD static int elem(int m, int t, int r, int j) { return 64 * t + (m >= 4 ? 32 : 0) + 8 * (m & 3) + 4 * r + j; }
   // 6-bit (scale, min) of sub-block j from the 12 packed bytes held in
   // three little-endian words S0 = bytes 0..3, S1 = 4..7, S2 = 8..11.
   VHD static void scale_min(uint32_t S0, uint32_t S1, uint32_t S2, int j, uint32_t& sc, uint32_t& mn) {
@@ -141,20 +123,19 @@ struct Q4K {
 };
 
 // ---- Q6_K: 210-byte super-blocks, segment = 1 super-block ---------------
-// Four macro-steps m (half h = m>>1, l0 = 16*(m&1)), four steps each.  In a
-// macro-step thread t follows stream t of half h: values 128h + 32t + l0 +
-// (0..15), whose low 4 bits are the low (t<2) or high (t>=2) nibble of
-// ql[64h + 32*(t&1) + l] and whose top 2 bits are bits (2t, 2t+1) of
-// qh[32h + l]; one int8 scale (index 8h + 2t + l0/16) covers all 16.
-// Super-blocks are only 2-byte aligned in general (210 = 2 mod 4), so
-// words are read with a funnel shift.
+// Thread t follows stream t of each half h (reference q1..q4): value 128h +
+// 32t + l has its low 4 bits in the low (t < 2) or high (t >= 2) nibble of
+// ql[64h + 32(t&1) + l] and its top 2 bits in bits (2t, 2t+1) of
+// qh[32h + l]; int8 scale sc[8h + 2t + l/16].  Step m: h = m >> 2, l = 16
+// ((m >> 1) & 1) + 8 (m & 1) + 4r + j, so each pair of steps is one 16-value
+// scale group.  z = the 6-bit value as u8; value = d sc (z - 32), the 32 is
+// removed with the 16-group sum of x.  Super-blocks are only 2-byte aligned
+// in general (210 = 2 mod 4): words are read with a funnel shift.
 struct Q6K {
   static constexpr uint32_t kType = T_Q6_K;
-  static constexpr int kSegBytes = 210, kSteps = 16;
-  static constexpr int kSumGroup = 16;  // x sums per scale group (offset correction)
-  VHD static int elem(int step, int t, int j) {
-    int m = step >> 2, s = step & 3;
-    return 128 * (m >> 1) + 32 * t + 16 * (m & 1) + 4 * s + kperm(j);
+  static constexpr int kSegBytes = 210;
+  VHD static int elem(int m, int t, int r, int j) {
+    return 128 * (m >> 2) + 32 * t + 16 * ((m >> 1) & 1) + 8 * (m & 1) + 4 * r + j;
   }
   // 4 six-bit values of stream t from a ql word and a qh word
   VHD static uint32_t six(uint32_t ql, uint32_t qh, int t) {
@@ -162,13 +143,6 @@ struct Q6K {
     uint32_t hi = ((qh >> (2u * (uint32_t)t)) & 0x03030303u) << 4;
     return lo | hi;
   }
-  // halves 1024 + z (z = the 6-bit value); value = z - 32, so the offset
-  // removed with the group sum of x is 1056
-  VHD static void conv(uint32_t z, uint32_t& h02, uint32_t& h13) {
-    h02 = (z & 0x00FF00FFu) | 0x64006400u;
-    h13 = byte_perm(z, 0x64646464u, 0x4341u);
-  }
-  static constexpr float kOffset = 1056.f;
 };
 
 }  // namespace vireo
