@@ -28,7 +28,7 @@ _u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
 
 def build(ref: bool = True) -> None:
     """Compile the checkers (the reference library only when its sources exist)."""
-    targets = ["port"] + (["ref"] if ref else [])
+    targets = ["port"] + (["ref", "ref_store_test"] if ref else [])
     subprocess.run(["make", "-s", "-C", HERE] + targets, check=True,
                    env={**os.environ, "OCC": os.environ.get("ORACLE_CC", "gcc")})
 

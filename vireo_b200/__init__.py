@@ -55,6 +55,24 @@ class GgufMoeDesc(C.Structure):
                 ("gate_nbytes", C.c_uint64), ("up_nbytes", C.c_uint64), ("down_nbytes", C.c_uint64)]
 
 
+class ExpertStats(C.Structure):
+    _fields_ = [(n, C.c_uint64) for n in ("requests", "hits", "misses", "bytes_read", "resident_bytes",
+                                          "capacity_bytes", "experts_resident")]
+
+
+class ExpertSlices(C.Structure):
+    _fields_ = [("gate_off", C.c_uint64), ("up_off", C.c_uint64), ("down_off", C.c_uint64),
+                ("gate_bytes", C.c_uint32), ("up_bytes", C.c_uint32), ("down_bytes", C.c_uint32)]
+
+
+class ExpertView(C.Structure):
+    _fields_ = [("gate", C.c_void_p), ("up", C.c_void_p), ("down", C.c_void_p), ("slot", C.c_void_p)]
+
+
+class ExpertStatsExt(C.Structure):
+    _fields_ = [(n, C.c_uint64) for n in ("h2d_bytes", "copies", "evictions", "over_budget_loads")]
+
+
 _lib = None
 
 
@@ -89,6 +107,24 @@ def lib():
         L.gguf_moe_ffn_noalloc.argtypes = [C.POINTER(GgufMoeDesc), C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
                                            C.c_void_p, C.c_void_p]
         L.gguf_moe_destroy.restype = None
+        # ExpertStore (include/expert_store.h)
+        L.expert_store_create.argtypes = [C.c_int, C.c_uint64, C.c_int, C.c_int]
+        L.expert_store_create.restype = C.c_void_p
+        L.expert_store_create_host.argtypes = [C.c_void_p, C.c_uint64, C.c_uint64, C.c_int, C.c_int]
+        L.expert_store_create_host.restype = C.c_void_p
+        L.expert_store_register.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(ExpertSlices)]
+        L.expert_store_register.restype = None
+        L.expert_store_lookup.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(ExpertView)]
+        L.expert_store_lookup_async.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(ExpertView), C.c_void_p]
+        L.expert_store_release.argtypes = [C.c_void_p, C.POINTER(ExpertView)]
+        L.expert_store_release.restype = None
+        L.expert_store_release_after.argtypes = [C.c_void_p, C.POINTER(ExpertView), C.c_void_p]
+        L.expert_store_stats.argtypes = [C.c_void_p, C.POINTER(ExpertStats)]
+        L.expert_store_stats.restype = None
+        L.expert_store_stats_ext.argtypes = [C.c_void_p, C.POINTER(ExpertStatsExt)]
+        L.expert_store_stats_ext.restype = None
+        L.expert_store_destroy.argtypes = [C.c_void_p]
+        L.expert_store_destroy.restype = None
         _lib = L
     return _lib
 
