@@ -17,6 +17,7 @@
 #include <stdint.h>
 
 #include "gguf.h"
+#include "expert_store.h"
 #include "vireo_status.h"
 
 #ifdef __cplusplus
@@ -54,6 +55,29 @@ int gguf_moe_create(const gguf_moe_desc *desc, gguf_moe **out);
  * may read the router weights before the preceding kernel on the stream has
  * finished, so router weights must not be written by that kernel. */
 int gguf_moe_ffn(gguf_moe *m, const float *hb, float *x, int n_tok, int32_t *ids, float *wts, void *stream);
+
+/* No counterpart in the reference (its moe_ffn always routes with the
+ * router, gguf_run.c:187-192): n_tok tokens through the layer with the route
+ * given by the caller instead of the router -- a routing-override hook.
+ * ids / wts: HOST arrays [n_tok][n_used], rank-order expert ids (-1 = unused
+ * slot) and the gate weights the combine uses (final: no softmax, no
+ * renormalisation); expert_ptrs: HOST array [n_tok][n_used][3] of DEVICE
+ * addresses of each selected expert's gate, up and down slices (16-byte
+ * aligned; NULL = unused slot).  The arrays are read during the call (each
+ * token's route travels in its launch), so they may be reused at once.
+ * hb / x as in gguf_moe_ffn; stream-ordered. */
+int gguf_moe_ffn_routed(gguf_moe *m, const float *hb, float *x, int n_tok, const int32_t *ids, const float *wts,
+                        const void *const *expert_ptrs, void *stream);
+
+/* The reference's per-expert ExpertStore use in moe_ffn (gguf_run.c:199-210:
+ * lookup, compute, release) for one token whose route is given on the host
+ * (ids / wts: HOST arrays [n_used], as gguf_moe_ffn_routed): each selected
+ * expert of `layer` is looked up asynchronously (misses are copied to the
+ * device on the store's copy stream and `stream` waits for them), the routed
+ * kernel runs on `stream`, and the leases end when it completes.  An expert
+ * whose lookup fails is skipped, as the reference does. */
+int gguf_moe_ffn_store(gguf_moe *m, ExpertStore *store, int layer, const float *hb, float *x, const int32_t *ids,
+                       const float *wts, void *stream);
 
 /* Same with HOST buffers: copies in, runs, copies out, synchronises. */
 int gguf_moe_ffn_host(gguf_moe *m, const float *hb, float *x, int n_tok, int32_t *ids, float *wts);

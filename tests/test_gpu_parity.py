@@ -163,3 +163,116 @@ def test_moe_unsupported_layer_is_rejected(V):
     with pytest.raises(V.VireoError) as ei:
         V.MoeLayer(L)
     assert ei.value.status == -3
+
+
+def expert_out(L, e, x):
+    """One expert's FFN output on the CPU oracle: down(silu(gate x) * up x)
+    (gguf_run.c:202-208), each mat-vec by the restated gguf_matmul."""
+    s = L.spec
+    sl = lambda a, n: a.view(np.uint8).ravel()[e * (a.nbytes // s.n_experts):(e + 1) * (a.nbytes // s.n_experts)]
+    g = O.matmul(s.gate_type, sl(L.gate, 0), x, s.dim, s.ffn_exp)
+    u = O.matmul(s.up_type, sl(L.up, 0), x, s.dim, s.ffn_exp)
+    h = (g / (np.float32(1) + np.exp(-g)) * u).astype(np.float32)
+    return O.matmul(s.down_type, sl(L.down, 0), h, s.ffn_exp, s.dim)
+
+
+def expert_ptrs(L, m, ids):
+    """Device addresses [n][k][3] of the selected experts' slices (experts outermost)."""
+    s = L.spec
+    gs, us, ds = m.gate.numel() // s.n_experts, m.up.numel() // s.n_experts, m.down.numel() // s.n_experts
+    out = np.zeros(ids.shape + (3,), dtype=np.uint64)
+    for idx, e in np.ndenumerate(ids):
+        if e >= 0:
+            out[idx] = (m.gate.data_ptr() + int(e) * gs, m.up.data_ptr() + int(e) * us, m.down.data_ptr() + int(e) * ds)
+    return out
+
+
+@pytest.mark.parametrize("name", ["cfg1_olmoe_q8", "qwen3"])
+def test_moe_routed_matches_router(V, golden, name):
+    """The routing-override entry (gguf_moe_ffn_routed) given the router's own
+    selection reproduces the router path bit for bit; a different selection
+    matches the CPU oracle run with that selection."""
+    import torch
+    L = golden_layer(golden, name)
+    n = 6
+    toks, _ = S.routed_tokens(L, n, 91)
+    x0 = (S.normal(91, 3, toks.size) * 0.3).astype(np.float32).reshape(toks.shape)
+    m = V.MoeLayer(L)
+    k = L.spec.n_used
+    hb, xa = torch.from_numpy(toks).cuda(), torch.from_numpy(x0.copy()).cuda()
+    ids = torch.zeros((n, k), dtype=torch.int32, device="cuda")
+    wts = torch.zeros((n, k), dtype=torch.float32, device="cuda")
+    m.ffn(hb, xa, ids, wts)
+    m.sync()
+    hid, hwt = ids.cpu().numpy(), wts.cpu().numpy()
+    ptrs = expert_ptrs(L, m, hid)
+    xb = torch.from_numpy(x0.copy()).cuda()
+    V.check(V.lib().gguf_moe_ffn_routed(m.h, hb.data_ptr(), xb.data_ptr(), n, hid.ctypes.data, hwt.ctypes.data,
+                                        ptrs.ctypes.data, None), "gguf_moe_ffn_routed")
+    m.sync()
+    assert torch.equal(xa, xb)
+    # an arbitrary route (reversed expert order, one unused slot) against the oracle's experts
+    rid = hid[:, ::-1].copy()
+    rid[:, -1] = -1
+    rwt = np.linspace(0.05, 0.3, k, dtype=np.float32)[None, :].repeat(n, 0)
+    xc = torch.from_numpy(x0.copy()).cuda()
+    rptrs = expert_ptrs(L, m, rid)  # named: the library reads it during the call
+    V.check(V.lib().gguf_moe_ffn_routed(m.h, hb.data_ptr(), xc.data_ptr(), n, rid.ctypes.data, rwt.ctypes.data,
+                                        rptrs.ctypes.data, None), "gguf_moe_ffn_routed")
+    m.sync()
+    got = xc.cpu().numpy()
+    for i in range(n):
+        ref = x0[i].astype(np.float64).copy()
+        for t in range(k):
+            if rid[i, t] >= 0:
+                ref += float(rwt[i, t]) * expert_out(L, int(rid[i, t]), toks[i]).astype(np.float64)
+        e = rel_err(got[i] - x0[i], ref - x0[i])
+        assert e < TOL, (i, e)
+    m.close()
+
+
+def test_moe_store_backed_matches_routed(V, golden):
+    """gguf_moe_ffn_store: experts leased from an ExpertStore over a host image
+    of the layer (budget of 12 experts for 8 per token, so lookups miss and
+    evict) give the same bits as the routed entry with the layer's own device
+    tensors, and the budget holds once each token's leases have ended."""
+    import ctypes as C
+    import torch
+    L = golden_layer(golden, "qwen3")
+    s = L.spec
+    n = 5
+    toks, _ = S.routed_tokens(L, n, 17)
+    x0 = (S.normal(17, 2, toks.size) * 0.3).astype(np.float32).reshape(toks.shape)
+    m = V.MoeLayer(L)
+    lib = V.lib()
+    image = np.concatenate([L.gate.view(np.uint8).ravel(), L.up.view(np.uint8).ravel(), L.down.view(np.uint8).ravel()])
+    G, U = L.gate.nbytes, L.up.nbytes
+    gs, us, ds = G // s.n_experts, U // s.n_experts, L.down.nbytes // s.n_experts
+    store = lib.expert_store_create_host(image.ctypes.data, image.nbytes, 12 * (gs + us + ds), 1, s.n_experts)
+    assert store
+    try:
+        for e in range(s.n_experts):
+            sl = V.ExpertSlices(e * gs, G + e * us, G + U + e * ds, gs, us, ds)
+            lib.expert_store_register(store, 0, e, C.byref(sl))
+        rng = np.random.default_rng(5)
+        rid = np.stack([rng.choice(s.n_experts, s.n_used, replace=False) for _ in range(n)]).astype(np.int32)
+        rwt = rng.uniform(0.05, 0.3, (n, s.n_used)).astype(np.float32)
+        hb = torch.from_numpy(toks).cuda()
+        xa, xb = torch.from_numpy(x0.copy()).cuda(), torch.from_numpy(x0.copy()).cuda()
+        stream = torch.cuda.current_stream().cuda_stream
+        for i in range(n):
+            V.check(lib.gguf_moe_ffn_store(m.h, store, 0, hb[i].data_ptr(), xa[i].data_ptr(),
+                                           rid[i].ctypes.data, rwt[i].ctypes.data, C.c_void_p(stream)),
+                    "gguf_moe_ffn_store")
+            torch.cuda.synchronize()  # this token's leases end before the next lookups
+        rptrs = expert_ptrs(L, m, rid)  # named: the library reads it during the call
+        V.check(lib.gguf_moe_ffn_routed(m.h, hb.data_ptr(), xb.data_ptr(), n, rid.ctypes.data, rwt.ctypes.data,
+                                        rptrs.ctypes.data, C.c_void_p(stream)), "routed")
+        torch.cuda.synchronize()
+        assert torch.equal(xa, xb)
+        st = V.ExpertStats()
+        lib.expert_store_stats(store, C.byref(st))
+        assert st.requests == n * s.n_used and st.misses > 12 and st.resident_bytes <= st.capacity_bytes
+    finally:
+        lib.expert_store_destroy(store)
+        m.close()

@@ -107,6 +107,10 @@ def lib():
         L.gguf_moe_ffn_noalloc.argtypes = [C.POINTER(GgufMoeDesc), C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
                                            C.c_void_p, C.c_void_p]
         L.gguf_moe_destroy.restype = None
+        L.gguf_moe_ffn_routed.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
+                                          C.c_void_p, C.c_void_p]
+        L.gguf_moe_ffn_store.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                         C.c_void_p, C.c_void_p]
         # ExpertStore (include/expert_store.h)
         L.expert_store_create.argtypes = [C.c_int, C.c_uint64, C.c_int, C.c_int]
         L.expert_store_create.restype = C.c_void_p

@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "gguf_compute.h"
+#include "expert_store.h"
 #include "gguf_moe.h"
 #include "moe_decode.cuh"
 #include "vireo_internal.h"
@@ -364,6 +365,7 @@ struct gguf_moe {
   gguf_moe_desc desc;
   MoeDecodeParams prm;
   const void* kernel = nullptr;
+  const void* rkernel = nullptr;  // routed variant (caller's route, no router phase)
   uint32_t smem = 0;
   int grid = 0;
   const uint8_t** d_exp_tab = nullptr;
@@ -425,11 +427,12 @@ int gguf_moe_create(const gguf_moe_desc* desc, gguf_moe** out) {
   }
   m->smem = moe_decode_layout(&p, dyn_smem_limit(c), c->num_sms);
   m->kernel = moe_decode_kernel_for(D.gate_type, D.down_type);
-  if (!m->smem || !m->kernel) {
+  m->rkernel = moe_decode_kernel_for(D.gate_type, D.down_type, true);
+  if (!m->smem || !m->kernel || !m->rkernel) {
     delete m;
     return VIREO_ERR_UNSUPPORTED;
   }
-  if ((st = ensure_smem_attr(c, m->kernel))) {
+  if ((st = ensure_smem_attr(c, m->kernel)) || (st = ensure_smem_attr(c, m->rkernel))) {
     delete m;
     return st;
   }
@@ -483,20 +486,17 @@ int gguf_moe_create(const gguf_moe_desc* desc, gguf_moe** out) {
   return VIREO_OK;
 }
 
-int gguf_moe_ffn(gguf_moe* m, const float* hb, float* x, int n_tok, int32_t* ids, float* wts, void* stream) {
-  if (!m || !hb || !x || n_tok < 0) return VIREO_ERR_ARG;
-  if (((uintptr_t)hb % 16) || ((size_t)m->prm.d * 4) % 16) return VIREO_ERR_ARG;
-  cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
-  MoeDecodeParams p = m->prm;
+// One launch of the decode kernel (or its routed variant) for one token:
+// cooperative (every CTA resident: CTAs wait on one another's flags) and with
+// programmatic serialization, so that the next token's kernel may begin its
+// weight-only prologue while this one drains (griddepcontrol.wait in the
+// kernel orders everything that reads the previous kernel's output).
+static int moe_launch(gguf_moe* m, const void* kernel, void** args, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(m->grid);
   cfg.blockDim = dim3(kDecodeThreads);
   cfg.dynamicSmemBytes = m->smem;
   cfg.stream = s;
-  // cooperative: every CTA must be resident (CTAs wait on one another's
-  // flags); programmatic serialization: the next token's kernel may begin
-  // its weight-only prologue while this one drains (griddepcontrol.wait in
-  // the kernel orders everything that reads the previous kernel's output)
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
@@ -504,24 +504,90 @@ int gguf_moe_ffn(gguf_moe* m, const float* hb, float* x, int n_tok, int32_t* ids
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = m->pdl ? 2 : 1;
+  cudaError_t e = cudaLaunchKernelExC(&cfg, kernel, args);
+  if (e != cudaSuccess && m->pdl) {
+    // this driver refuses cooperative + programmatic launches: drop PDL
+    cudaGetLastError();
+    m->pdl = false;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelExC(&cfg, kernel, args);
+  }
+  return cuda_status(e);
+}
+
+int gguf_moe_ffn(gguf_moe* m, const float* hb, float* x, int n_tok, int32_t* ids, float* wts, void* stream) {
+  if (!m || !hb || !x || n_tok < 0) return VIREO_ERR_ARG;
+  if (((uintptr_t)hb % 16) || ((size_t)m->prm.d * 4) % 16) return VIREO_ERR_ARG;
+  cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
+  MoeDecodeParams p = m->prm;
   for (int i = 0; i < n_tok; i++) {
     p.hb = hb + (size_t)i * p.d;
     p.x = x + (size_t)i * p.d;
     p.ids_out = ids ? ids + (size_t)i * p.k : nullptr;
     p.wts_out = wts ? wts + (size_t)i * p.k : nullptr;
     void* args[] = {&p};
-    cudaError_t e = cudaLaunchKernelExC(&cfg, m->kernel, args);
-    if (e != cudaSuccess && m->pdl) {
-      // this driver refuses cooperative + programmatic launches: drop PDL
-      cudaGetLastError();
-      m->pdl = false;
-      cfg.numAttrs = 1;
-      e = cudaLaunchKernelExC(&cfg, m->kernel, args);
-    }
-    int st = cuda_status(e);
+    int st = moe_launch(m, m->kernel, args, s);
     if (st) return st;
   }
   return VIREO_OK;
+}
+
+int gguf_moe_ffn_routed(gguf_moe* m, const float* hb, float* x, int n_tok, const int32_t* ids, const float* wts,
+                        const void* const* expert_ptrs, void* stream) {
+  if (!m || !hb || !x || n_tok < 0 || (n_tok && (!ids || !wts || !expert_ptrs))) return VIREO_ERR_ARG;
+  if (((uintptr_t)hb % 16) || ((size_t)m->prm.d * 4) % 16) return VIREO_ERR_ARG;
+  cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
+  MoeDecodeParams p = m->prm;
+  const int k = p.k;
+  MoeRoute r;
+  memset(&r, 0, sizeof(r));
+  for (int i = 0; i < n_tok; i++) {
+    for (int t = 0; t < k; t++) {
+      const int32_t e = ids[(size_t)i * k + t];
+      const void* const* pt = expert_ptrs + ((size_t)i * k + t) * 3;
+      const bool on = e >= 0 && e < p.ne && pt[0] && pt[1] && pt[2];
+      if (on && (((uintptr_t)pt[0] | (uintptr_t)pt[1] | (uintptr_t)pt[2]) % 16)) return VIREO_ERR_UNSUPPORTED;
+      r.ids[t] = on ? e : -1;
+      r.wts[t] = on ? wts[(size_t)i * k + t] : -1.f;
+      for (int j = 0; j < 3; j++) r.ptr[t][j] = on ? (const uint8_t*)pt[j] : nullptr;
+    }
+    p.hb = hb + (size_t)i * p.d;
+    p.x = x + (size_t)i * p.d;
+    p.ids_out = nullptr;
+    p.wts_out = nullptr;
+    void* args[] = {&p, &r};
+    int st = moe_launch(m, m->rkernel, args, s);
+    if (st) return st;
+  }
+  return VIREO_OK;
+}
+
+int gguf_moe_ffn_store(gguf_moe* m, ExpertStore* store, int layer, const float* hb, float* x, const int32_t* ids,
+                       const float* wts, void* stream) {
+  if (!m || !store || !ids || !wts) return VIREO_ERR_ARG;
+  cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
+  const int k = m->prm.k;
+  ExpertView views[kMaxTopK];
+  const void* ptrs[kMaxTopK * 3];
+  int32_t rid[kMaxTopK];
+  memset(views, 0, sizeof(views));
+  memset(ptrs, 0, sizeof(ptrs));
+  memset(rid, 0, sizeof(rid));
+  int st = VIREO_OK;
+  for (int t = 0; t < k; t++) {
+    rid[t] = ids[t];
+    if (ids[t] < 0 || expert_store_lookup_async(store, layer, ids[t], &views[t], s) != 0) {
+      rid[t] = -1;  // the reference skips an expert whose lookup fails (gguf_run.c:201)
+      memset(&views[t], 0, sizeof(views[t]));
+    }
+    ptrs[3 * t + 0] = views[t].gate;
+    ptrs[3 * t + 1] = views[t].up;
+    ptrs[3 * t + 2] = views[t].down;
+  }
+  st = gguf_moe_ffn_routed(m, hb, x, 1, rid, wts, ptrs, s);
+  for (int t = 0; t < k; t++)
+    if (views[t].slot) expert_store_release_after(store, &views[t], s);
+  return st;
 }
 
 int gguf_moe_sync(gguf_moe* m, void* stream) {

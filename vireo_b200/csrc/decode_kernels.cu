@@ -81,8 +81,10 @@ VDEV void stage_vec_cg8(const float* g, float* s, int n, int tid, int nthr) {
   }
 }
 
-template <class SG, class SD>
-__global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __grid_constant__ MoeDecodeParams p) {
+// The decode kernel body.  ROUTED: the route comes from the caller (rt) and
+// the router phase is skipped; otherwise every CTA computes it.
+template <class SG, class SD, bool ROUTED>
+__device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const MoeRoute* rt) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float red[kDecodeThreads / 32 + 1];
   // gate/up ring (S stages) and down ring (SD slots over the same memory)
@@ -128,6 +130,23 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __g
   // the next token's kernel may start its own prologue as SMs free up
   pdl_launch_dependents();
 
+  if constexpr (ROUTED) {
+    // ---- caller's route: x tables and the selection, no router phase --------
+    pdl_wait();
+    stage_vec(p.hb, stg, d, threadIdx.x, blockDim.x, false);
+    if (threadIdx.x < k) {
+      ctl->ids[threadIdx.x] = rt->ids[threadIdx.x];
+      ctl->wts[threadIdx.x] = rt->wts[threadIdx.x];
+      if (cta == 0) {
+        if (p.ids_out) p.ids_out[threadIdx.x] = rt->ids[threadIdx.x];
+        if (p.wts_out) p.wts_out[threadIdx.x] = rt->wts[threadIdx.x];
+      }
+    }
+    __syncthreads();
+    build_tables<SG>(stg, xtab, xsx, d / kSegElems, warp, (int)(blockDim.x / 32), lane);
+    __syncthreads();
+    if (threadIdx.x == 0) trace(p, kTrRouted);
+  } else {
   // ---- phase R: router partial dot products --------------------------------
   // Router rows are weights (independent of the previous kernel): their loads
   // are issued before waiting on the previous kernel in the stream.
@@ -281,6 +300,17 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __g
     }
     __syncthreads();
   }
+  }
+
+  // device address of slice `which` (0 gate, 1 up, 2 down) of expert slot t
+  auto expert_ptr = [&](int t, int which) -> const uint8_t* {
+    if constexpr (ROUTED) {
+      return ctl->ids[t] < 0 ? nullptr : rt->ptr[t][which];
+    } else {
+      const int e = ctl->ids[t];
+      return e < 0 ? nullptr : p.exp_tab[3 * e + which];
+    }
+  };
 
   const int rgG = fe / 8, UG = k * rgG, ntile = d / 16;
   const int g0 = (int)((long long)cta * UG / G), g1 = (int)((long long)(cta + 1) * UG / G);
@@ -296,9 +326,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __g
       const int slot = v % S;
       if (!warp_wait(&empty[slot], ((uint32_t)(v / S) & 1u) ^ 1u, ctl, p.s.err)) break;
       const int u = g0 + v, t = u / rgG, rg = u - t * rgG;
-      const int e = ctl->ids[t];
-      const uint8_t* gsrc = e < 0 ? nullptr : p.exp_tab[3 * e + 0] + (size_t)(8 * rg) * p.sg_gu.rb;
-      const uint8_t* usrc = e < 0 ? nullptr : p.exp_tab[3 * e + 1] + (size_t)(8 * rg) * p.sg_gu.rb;
+      const uint8_t* gb = expert_ptr(t, 0);
+      const uint8_t* ub = expert_ptr(t, 1);
+      const uint8_t* gsrc = gb ? gb + (size_t)(8 * rg) * p.sg_gu.rb : nullptr;
+      const uint8_t* usrc = ub ? ub + (size_t)(8 * rg) * p.sg_gu.rb : nullptr;
       issue_unit(stages + (size_t)slot * p.stage_bytes, &full[slot], gsrc, usrc, p.sg_gu, ptid, kProducerThreads);
     }
     // down units: every expert slot of each of this CTA's 16-row tiles, in
@@ -318,8 +349,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __g
       }
       if (!ok) break;
       const int i = j / k, t = j - i * k, tile = cta + i * G;
-      const int e = ctl->ids[t];
-      const uint8_t* src = e < 0 ? nullptr : p.exp_tab[3 * e + 2] + (size_t)(16 * tile) * p.sg_d.rb;
+      const uint8_t* db = expert_ptr(t, 2);
+      const uint8_t* src = db ? db + (size_t)(16 * tile) * p.sg_d.rb : nullptr;
       issue_unit(stages + (size_t)slot * p.dslot_bytes, &full_d[slot], src, src ? src + 8 * (size_t)p.sg_d.rb : nullptr,
                  p.sg_d, ptid, kProducerThreads);
     }
@@ -441,6 +472,17 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __g
   }
 }
 
+template <class SG, class SD>
+__global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const __grid_constant__ MoeDecodeParams p) {
+  moe_decode_body<SG, SD, false>(p, nullptr);
+}
+
+template <class SG, class SD>
+__global__ void __launch_bounds__(kDecodeThreads, 1)
+    moe_routed_kernel(const __grid_constant__ MoeDecodeParams p, const __grid_constant__ MoeRoute r) {
+  moe_decode_body<SG, SD, true>(p, &r);
+}
+
 // ---------------------------------------------------------------------------
 // Stand-alone GEMV: y[d] = W[d x n] . x[n]  (fast formats, d % 16 == 0)
 // ---------------------------------------------------------------------------
@@ -555,22 +597,23 @@ int stage_geom(uint32_t type, int K, StageGeom* sg) {
 static uint32_t up_to(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
 template <class SG, class SD>
-static const void* moe_kernel_ptr() {
-  return reinterpret_cast<const void*>(&moe_decode_kernel<SG, SD>);
+static const void* moe_kernel_ptr(bool routed) {
+  return routed ? reinterpret_cast<const void*>(&moe_routed_kernel<SG, SD>)
+                : reinterpret_cast<const void*>(&moe_decode_kernel<SG, SD>);
 }
 
 template <class SG>
-static const void* moe_kernel_for(uint32_t dtype) {
-  if (dtype == T_Q8_0) return moe_kernel_ptr<SG, SegQ8>();
-  if (dtype == T_Q4_K) return moe_kernel_ptr<SG, SegQ4K>();
-  if (dtype == T_Q6_K) return moe_kernel_ptr<SG, SegQ6K>();
+static const void* moe_kernel_for(uint32_t dtype, bool routed) {
+  if (dtype == T_Q8_0) return moe_kernel_ptr<SG, SegQ8>(routed);
+  if (dtype == T_Q4_K) return moe_kernel_ptr<SG, SegQ4K>(routed);
+  if (dtype == T_Q6_K) return moe_kernel_ptr<SG, SegQ6K>(routed);
   return nullptr;
 }
 
-const void* moe_decode_kernel_for(uint32_t gtype, uint32_t dtype) {
-  if (gtype == T_Q8_0) return moe_kernel_for<SegQ8>(dtype);
-  if (gtype == T_Q4_K) return moe_kernel_for<SegQ4K>(dtype);
-  if (gtype == T_Q6_K) return moe_kernel_for<SegQ6K>(dtype);
+const void* moe_decode_kernel_for(uint32_t gtype, uint32_t dtype, bool routed) {
+  if (gtype == T_Q8_0) return moe_kernel_for<SegQ8>(dtype, routed);
+  if (gtype == T_Q4_K) return moe_kernel_for<SegQ4K>(dtype, routed);
+  if (gtype == T_Q6_K) return moe_kernel_for<SegQ6K>(dtype, routed);
   return nullptr;
 }
 

@@ -79,6 +79,16 @@ struct MoeDecodeParams {
   unsigned long long* trace;  // optional: kTraceSlots %globaltimer stamps per CTA
 };
 
+// A route given by the caller (routed launches, no router phase): rank-order
+// expert ids (-1 = unused slot), gate weights as used in the combine, and the
+// device addresses of each selected expert's gate, up and down slices.
+// Passed by value as a kernel parameter (2 KB).
+struct MoeRoute {
+  int ids[kMaxTopK];
+  float wts[kMaxTopK];
+  const uint8_t* ptr[kMaxTopK][3];
+};
+
 // phase trace slots (per CTA): consumer thread 0 and producer thread 0
 enum TraceSlot {
   kTrStart = 0, kTrRouterDone, kTrPartials, kTrRouted, kTrGDone, kTrGAll, kTrHtab, kTrDDone,

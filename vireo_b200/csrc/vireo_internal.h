@@ -37,7 +37,7 @@ struct GemvParams;
 
 bool fast_format(uint32_t type);
 int stage_geom(uint32_t type, int K, StageGeom* sg);
-const void* moe_decode_kernel_for(uint32_t gtype, uint32_t dtype);
+const void* moe_decode_kernel_for(uint32_t gtype, uint32_t dtype, bool routed = false);
 uint32_t moe_decode_layout(MoeDecodeParams* p, uint32_t smem_limit, int grid);
 const void* gemv_kernel_for(uint32_t type);
 uint32_t gemv_layout(GemvParams* p, uint32_t smem_limit);
