@@ -79,6 +79,21 @@ int gguf_moe_ffn_routed(gguf_moe *m, const float *hb, float *x, int n_tok, const
 int gguf_moe_ffn_store(gguf_moe *m, ExpertStore *store, int layer, const float *hb, float *x, const int32_t *ids,
                        const float *wts, void *stream);
 
+/* Batched (prefill) MoE FFN: n_tok tokens at once, the same function as
+ * gguf_moe_ffn per token (the reference's moe_ffn, gguf_run.c:185-214), as
+ * grouped GEMMs over the experts on the tensor cores.  hb_bf16: DEVICE
+ * [n_tok][dim] bf16 hidden vectors; x: DEVICE [n_tok][dim] fp32 residual,
+ * updated in place; router_bias: DEVICE [n_experts] added to the router
+ * logits before the softmax, or NULL (the reference has none); ids / wts:
+ * DEVICE [n_tok][n_used] selection out, or NULL.  Stream-ordered; device
+ * failures surface in gguf_moe_sync.  Supported: router F32, gate/up Q4_K,
+ * down Q6_K, dim % 256 == 0, ffn_exp % 256 == 0, n_experts <= 128,
+ * n_used <= 8; other layers return VIREO_ERR_UNSUPPORTED.  Activations and
+ * dequantised weights are f16 with fp32 accumulation: hidden values must lie
+ * within f16 range. */
+int gguf_moe_prefill(gguf_moe *m, const void *hb_bf16, float *x, int n_tok, const float *router_bias, int32_t *ids,
+                     float *wts, void *stream);
+
 /* Same with HOST buffers: copies in, runs, copies out, synchronises. */
 int gguf_moe_ffn_host(gguf_moe *m, const float *hb, float *x, int n_tok, int32_t *ids, float *wts);
 

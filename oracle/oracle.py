@@ -71,6 +71,9 @@ def port():
         lib.orc_moe_ffn.restype = C.c_int
         lib.orc_moe_ffn_batch.argtypes = [C.POINTER(OrcMoeLayer), C.c_int, _f32p, _f32p, _i32p, _f32p]
         lib.orc_moe_ffn_batch.restype = C.c_int
+        lib.orc_moe_ffn_batch_bias.argtypes = [C.POINTER(OrcMoeLayer), C.c_int, _f32p, _f32p, _i32p, _f32p,
+                                               C.c_void_p]
+        lib.orc_moe_ffn_batch_bias.restype = C.c_int
         lib.orc_set_threads.argtypes = [C.c_int]
         lib.orc_max_threads.restype = C.c_int
         _port = lib
@@ -149,8 +152,10 @@ class PortMoe:
                                 self._keep[2].ctypes.data, self._keep[3].ctypes.data,
                                 self._keep[1].nbytes, self._keep[2].nbytes, self._keep[3].nbytes)
 
-    def __call__(self, hb, x=None):
-        """Returns (x_out, ids, wts) for a batch of independent tokens."""
+    def __call__(self, hb, x=None, bias=None):
+        """Returns (x_out, ids, wts) for a batch of independent tokens; bias
+        (optional, [n_experts]) is added to the router logits before the
+        softmax (the restated function with bias=None is the reference's)."""
         s = self.layer.spec
         hb = np.ascontiguousarray(hb, dtype=np.float32).reshape(-1, s.dim)
         n = hb.shape[0]
@@ -158,8 +163,13 @@ class PortMoe:
         k = min(s.n_used, 64)
         ids = np.zeros((n, k), dtype=np.int32)
         wts = np.zeros((n, k), dtype=np.float32)
-        port().orc_moe_ffn_batch(C.byref(self.desc), n, hb.reshape(-1), x.reshape(-1),
-                                 ids.reshape(-1), wts.reshape(-1))
+        if bias is None:
+            port().orc_moe_ffn_batch(C.byref(self.desc), n, hb.reshape(-1), x.reshape(-1),
+                                     ids.reshape(-1), wts.reshape(-1))
+        else:
+            b = np.ascontiguousarray(bias, dtype=np.float32)
+            port().orc_moe_ffn_batch_bias(C.byref(self.desc), n, hb.reshape(-1), x.reshape(-1),
+                                          ids.reshape(-1), wts.reshape(-1), b.ctypes.data)
         return x, ids, wts
 
 

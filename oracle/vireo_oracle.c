@@ -285,8 +285,18 @@ static void softmax_inplace(float *v, int n) {
  * the selected experts in rank order and their gate weights (after renorm).
  * probs (optional, [n_experts]) receives the softmax probabilities.
  * Returns the number of experts used (min(n_used, 64)). */
+int orc_moe_ffn_bias(const orc_moe_layer *L, const float *hb, float *x, int32_t *ids, float *wts,
+                     float *probs, const float *bias);
 int orc_moe_ffn(const orc_moe_layer *L, const float *hb, float *x, int32_t *ids, float *wts,
                 float *probs) {
+    return orc_moe_ffn_bias(L, hb, x, ids, wts, probs, NULL);
+}
+
+/* The same with a per-expert bias added to the router logits before the
+ * softmax (the imbalanced-routing configuration adds it in its harness; the
+ * reference has no bias, and bias == NULL is exactly orc_moe_ffn). */
+int orc_moe_ffn_bias(const orc_moe_layer *L, const float *hb, float *x, int32_t *ids, float *wts,
+                     float *probs, const float *bias) {
     int d = L->dim, fe = L->ffn_exp, ne = L->n_experts, k = L->n_used;
     int kk = k < 64 ? k : 64;
     float *rl = (float *)malloc(sizeof(float) * (size_t)ne);
@@ -297,6 +307,7 @@ int orc_moe_ffn(const orc_moe_layer *L, const float *hb, float *x, int32_t *ids,
     int idx[64];
     float w[64];
     orc_matmul(rl, hb, L->router_type, L->router, d, ne);
+    if (bias) for (int e = 0; e < ne; e++) rl[e] = rl[e] + bias[e];
     softmax_inplace(rl, ne);
     if (probs) memcpy(probs, rl, sizeof(float) * (size_t)ne);
     /* greedy top-k: k passes of a strict '>' argmax over the unused experts,
@@ -349,5 +360,21 @@ int orc_moe_ffn_batch(const orc_moe_layer *L, int n_tok, const float *hb, float 
     for (int t = 0; t < n_tok; t++)
         orc_moe_ffn(L, hb + (size_t)t * L->dim, x + (size_t)t * L->dim,
                     ids ? ids + (size_t)t * kk : NULL, wts ? wts + (size_t)t * kk : NULL, NULL);
+    return kk;
+}
+
+/* orc_moe_ffn_batch with a router bias (NULL = none); tokens in parallel
+ * (each token's computation is independent and sequential in itself, so the
+ * results do not depend on the thread count). */
+int orc_moe_ffn_batch_bias(const orc_moe_layer *L, int n_tok, const float *hb, float *x,
+                           int32_t *ids, float *wts, const float *bias) {
+    int kk = L->n_used < 64 ? L->n_used : 64;
+    int saved = orc_max_threads();
+    orc_set_threads(1);  /* one thread per token below; no nested parallel mat-vecs */
+    #pragma omp parallel for schedule(dynamic, 1) num_threads(saved)
+    for (int t = 0; t < n_tok; t++)
+        orc_moe_ffn_bias(L, hb + (size_t)t * L->dim, x + (size_t)t * L->dim,
+                         ids ? ids + (size_t)t * kk : NULL, wts ? wts + (size_t)t * kk : NULL, NULL, bias);
+    orc_set_threads(saved);
     return kk;
 }

@@ -111,6 +111,8 @@ def lib():
                                           C.c_void_p, C.c_void_p]
         L.gguf_moe_ffn_store.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                          C.c_void_p, C.c_void_p]
+        L.gguf_moe_prefill.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
+                                       C.c_void_p, C.c_void_p]
         # ExpertStore (include/expert_store.h)
         L.expert_store_create.argtypes = [C.c_int, C.c_uint64, C.c_int, C.c_int]
         L.expert_store_create.restype = C.c_void_p

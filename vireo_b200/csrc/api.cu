@@ -378,6 +378,8 @@ struct gguf_moe {
   int io_cap = 0;
   bool pdl = true;
   cudaStream_t stream = nullptr;
+  PrefillScratch pre;  // batched path, grown on demand
+  int num_sms = 0;
 };
 
 static int moe_reset_scratch(gguf_moe* m, cudaStream_t s) {
@@ -443,6 +445,7 @@ int gguf_moe_create(const gguf_moe_desc* desc, gguf_moe** out) {
     return e != cudaSuccess ? cuda_status(e) : VIREO_ERR_UNSUPPORTED;
   }
   m->grid = c->num_sms;
+  m->num_sms = c->num_sms;
 
   // scratch: logit partials, h, per-launch sync words, status
   p.hsx_count = (uint32_t)(D.ffn_exp / kSegElems * kMeta);
@@ -590,6 +593,27 @@ int gguf_moe_ffn_store(gguf_moe* m, ExpertStore* store, int layer, const float* 
   return st;
 }
 
+int gguf_moe_prefill(gguf_moe* m, const void* hb_bf16, float* x, int n_tok, const float* router_bias, int32_t* ids,
+                     float* wts, void* stream) {
+  if (!m || n_tok < 0 || (n_tok && (!hb_bf16 || !x))) return VIREO_ERR_ARG;
+  const gguf_moe_desc& D = m->desc;
+  if (!prefill_supported(D.dim, D.ffn_exp, D.n_experts, D.n_used, D.router_type, D.gate_type, D.up_type,
+                         D.down_type))
+    return VIREO_ERR_UNSUPPORTED;
+  if (((uintptr_t)hb_bf16 | (uintptr_t)x) % 16) return VIREO_ERR_ARG;
+  if (n_tok == 0) return VIREO_OK;
+  cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
+  PrefillLayer L;
+  L.d = D.dim;
+  L.fe = D.ffn_exp;
+  L.ne = D.n_experts;
+  L.k = D.n_used;
+  L.renorm = D.topk_renorm;
+  L.router = (const float*)D.router;
+  L.exp_tab = m->d_exp_tab;
+  return prefill_run(L, &m->pre, hb_bf16, x, n_tok, router_bias, ids, wts, m->prm.s.err, m->num_sms, s);
+}
+
 int gguf_moe_sync(gguf_moe* m, void* stream) {
   if (!m) return VIREO_ERR_ARG;
   cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
@@ -661,6 +685,7 @@ int gguf_moe_grid(const gguf_moe* m) { return m ? m->grid : 0; }
 void gguf_moe_destroy(gguf_moe* m) {
   if (!m) return;
   if (m->stream) cudaStreamSynchronize(m->stream);
+  prefill_scratch_free(&m->pre);
   cudaFree(m->scratch);
   cudaFree(m->d_exp_tab);
   cudaFree(m->d_io);

@@ -1,5 +1,6 @@
 // Internal declarations shared by the CUDA sources and the C-ABI layer.
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -41,6 +42,34 @@ const void* moe_decode_kernel_for(uint32_t gtype, uint32_t dtype, bool routed = 
 uint32_t moe_decode_layout(MoeDecodeParams* p, uint32_t smem_limit, int grid);
 const void* gemv_kernel_for(uint32_t type);
 uint32_t gemv_layout(GemvParams* p, uint32_t smem_limit);
+
+// batched (prefill) MoE FFN, prefill.cu
+struct PrefillLayer {
+  int d, fe, ne, k, renorm;
+  const float* router;             // [ne][d] fp32
+  const uint8_t* const* exp_tab;   // device [ne][3]: gate, up, down
+};
+struct PrefillScratch {
+  __half* xa = nullptr;
+  int32_t* ids = nullptr;
+  float* wts = nullptr;
+  int* counts = nullptr;
+  int* cursor = nullptr;
+  struct PTile* tiles = nullptr;
+  int* n_mtiles = nullptr;
+  int* rowpos = nullptr;
+  float* wrow = nullptr;
+  __half* xg = nullptr;
+  __half* hg = nullptr;
+  float* y = nullptr;
+  __half* r2 = nullptr;
+  size_t c_xa = 0, c_ids = 0, c_wts = 0, c_counts = 0, c_cursor = 0, c_tiles = 0, c_n_mtiles = 0, c_rowpos = 0,
+         c_wrow = 0, c_xg = 0, c_hg = 0, c_y = 0, c_r2 = 0;
+};
+int prefill_supported(int d, int fe, int ne, int k, uint32_t rt, uint32_t gt, uint32_t ut, uint32_t dt);
+int prefill_run(const PrefillLayer& L, PrefillScratch* S, const void* hb_bf16, float* x, int T, const float* bias,
+                int32_t* ids_out, float* wts_out, int* d_err, int num_sms, cudaStream_t st);
+void prefill_scratch_free(PrefillScratch* s);
 
 // generic kernels (any supported type/shape), generic_kernels.cu
 int launch_dequant(uint32_t type, const void* src, float* dst, int n, cudaStream_t s);
