@@ -663,6 +663,7 @@ int gguf_moe_ffn_host(gguf_moe* m, const float* hb, float* x, int n_tok, int32_t
 
 int gguf_moe_set_expert_ptrs(gguf_moe* m, const void* const* gate, const void* const* up, const void* const* down) {
   if (!m) return VIREO_ERR_ARG;
+  m->pre.minmat_ok = false;  // the batched path's min block follows the gate/up bytes
   for (int ex = 0; ex < m->desc.n_experts; ex++) {
     if (gate) m->h_exp_tab[3 * ex + 0] = (const uint8_t*)gate[ex];
     if (up) m->h_exp_tab[3 * ex + 1] = (const uint8_t*)up[ex];

@@ -43,6 +43,8 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "engine.cuh"
 #include "moe_decode.cuh"
 #include "umma.cuh"
@@ -53,12 +55,16 @@ namespace vireo {
 constexpr int kPM = 128;   // activation rows per tile
 constexpr int kPN = 256;   // weight rows per tile
 constexpr int kPK = 64;    // K per stage
-constexpr int kPStages = 4;
+constexpr int kPStages = 3;
 constexpr int kPThreads = 512;
 constexpr int kDqWarp0 = 4, kDqWarps = 8, kEpiWarp0 = 12;
 constexpr int kPTopK = 8;  // prefill top-k limit (held in registers)
 constexpr uint32_t kPStageA = kPM * kPK * 2, kPStageB = kPN * kPK * 2;
-constexpr uint32_t kPSmem = 1024 + kPStages * (kPStageA + kPStageB);
+// raw weight chunks of one stage (the repacked layouts, 256 rows each):
+// gate/up 48 B per row (Q4_K header + the stage's 32 quant bytes), down 80 B
+// per row (64 six-bit values as bytes z + 96, then 4 f16 scales d sc)
+constexpr uint32_t kPRawGU = kPN * 48, kPRawDN = kPN * 80, kPStageR = kPRawDN;
+constexpr uint32_t kPSmem = 1024 + kPStages * (kPStageA + kPStageB + kPStageR);
 
 enum PMode { P_ROUTER = 0, P_GATEUP = 1, P_DOWN = 2 };
 
@@ -74,6 +80,7 @@ struct PrefillParams {
   const int* n_mtiles;  // device (gate/up, down)
   const PTile* tiles;   // device
   const uint8_t* const* exp_tab;
+  const uint8_t* pack;   // repacked weight chunks of this GEMM
   uint32_t rb_gu, rb_d;  // row bytes of gate/up (Q4_K, d) and down (Q6_K, fe) rows
   // router
   const float* bias;
@@ -103,111 +110,80 @@ VDEV bool pwait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
   return false;
 }
 
-// ---- Q4_K row -> 64 f16 of one K stage (gate/up B tiles) -------------------
-// Values of chunk c of super-block sb, in the xa column order: positions
-// 0..31 the low nibbles of qs[32c ..], 32..63 the high nibbles, each group of
-// 4 ordered (0 2 1 3).  Value = round(d sc_j q); the -dmin m_j term is the
-// min block.
-VDEV void dq_q4k_stage(const uint8_t* rowp, int kt, int nkd, int d, uint8_t* tile, int r) {
-  uint4 out[8];
-  if (kt < nkd) {
-    const uint8_t* sbp = rowp + (kt >> 2) * 144;
-    const int c = kt & 3;
-    const uint4 hd = __ldg(reinterpret_cast<const uint4*>(sbp));
-    const uint4 qa = __ldg(reinterpret_cast<const uint4*>(sbp + 16 + 32 * c));
-    const uint4 qb = __ldg(reinterpret_cast<const uint4*>(sbp + 32 + 32 * c));
-    const float dd = h_lo(hd.x);
-    uint32_t sc0, m0, sc1, m1;
-    Q4K::scale_min(hd.y, hd.z, hd.w, 2 * c, sc0, m0);
-    Q4K::scale_min(hd.y, hd.z, hd.w, 2 * c + 1, sc1, m1);
-    const float a0f = dd * (float)sc0, a1f = dd * (float)sc1 * 0.0625f;  // high nibbles come as 16 q
-    const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-    const bool fast = fabsf(a0f) < 32.f && fabsf(a1f) < 32.f;  // 1024 a exact in f16
-    const __half2 A0 = __float2half2_rn(a0f), A1 = __float2half2_rn(a1f);
-    const __half2 C0 = __hmul2(A0, __float2half2_rn(-1024.f)), C1 = __hmul2(A1, __float2half2_rn(-1024.f));
-    const __half2 K1024 = __float2half2_rn(1024.f);
+// ---- Q4_K chunk row -> 64 f16 of one K stage (gate/up B tiles) -------------
+// Stage kt (< d / 64) = chunk c = kt & 3 of super-block kt >> 2.  Positions
+// 0..31 are the low nibbles of qs[32c ..], 32..63 the high nibbles, each
+// group of 4 ordered (0 2 1 3), as xa's columns.  Value = round(d sc_j q);
+// the -dmin m_j terms come from the min-block stages (minmat, by TMA).
+struct Q4Raw {
+  uint4 hd, qa, qb;  // super-block header, the stage's 32 quant bytes
+};
+
+VDEV void conv_q4k(const Q4Raw& R, int kt, uint8_t* tile, int r) {
+  const int c = kt & 3;
+  const float dd = h_lo(R.hd.x);
+  uint32_t sc0, m0, sc1, m1;
+  Q4K::scale_min(R.hd.y, R.hd.z, R.hd.w, 2 * c, sc0, m0);
+  Q4K::scale_min(R.hd.y, R.hd.z, R.hd.w, 2 * c + 1, sc1, m1);
+  const float a0f = dd * (float)sc0, a1f = dd * (float)sc1 * 0.0625f;  // high nibbles come as 16 q
+  const uint32_t w[8] = {R.qa.x, R.qa.y, R.qa.z, R.qa.w, R.qb.x, R.qb.y, R.qb.z, R.qb.w};
+  const bool fast = fabsf(a0f) < 32.f && fabsf(a1f) < 32.f;  // 1024 a exact in f16
+  const __half2 A0 = __float2half2_rn(a0f), A1 = __float2half2_rn(a1f);
+  const __half2 C0 = __hmul2(A0, __float2half2_rn(-1024.f)), C1 = __hmul2(A1, __float2half2_rn(-1024.f));
+  const __half2 K1024 = __float2half2_rn(1024.f);
+  uint8_t* rowt = tile + r * 128;
+  const int sw = r & 7;
+  if (fast) {
 #pragma unroll
     for (int ch = 0; ch < 8; ch++) {
       const uint32_t msk = ch < 4 ? 0x000F000Fu : 0x00F000F0u;
       const __half2 A = ch < 4 ? A0 : A1, C = ch < 4 ? C0 : C1;
       const uint32_t w0 = w[2 * (ch & 3)], w1 = w[2 * (ch & 3) + 1];
+      const uint32_t h0 = h2u(__hfma2(u2h((w0 & msk) | 0x64006400u), A, C));
+      const uint32_t h1 = h2u(__hfma2(u2h(((w0 >> 8) & msk) | 0x64006400u), A, C));
+      const uint32_t h2 = h2u(__hfma2(u2h((w1 & msk) | 0x64006400u), A, C));
+      const uint32_t h3 = h2u(__hfma2(u2h(((w1 >> 8) & msk) | 0x64006400u), A, C));
+      *reinterpret_cast<uint4*>(rowt + ((ch ^ sw) << 4)) = make_uint4(h0, h1, h2, h3);
+    }
+  } else {
+#pragma unroll
+    for (int ch = 0; ch < 8; ch++) {
+      const uint32_t msk = ch < 4 ? 0x000F000Fu : 0x00F000F0u;
+      const __half2 A = ch < 4 ? A0 : A1;
+      const uint32_t w0 = w[2 * (ch & 3)], w1 = w[2 * (ch & 3) + 1];
       const uint32_t u[4] = {(w0 & msk) | 0x64006400u, ((w0 >> 8) & msk) | 0x64006400u, (w1 & msk) | 0x64006400u,
                              ((w1 >> 8) & msk) | 0x64006400u};
       uint32_t h[4];
 #pragma unroll
-      for (int i = 0; i < 4; i++)
-        h[i] = fast ? h2u(__hfma2(u2h(u[i]), A, C)) : h2u(__hmul2(__hsub2(u2h(u[i]), K1024), A));
-      out[ch] = make_uint4(h[0], h[1], h[2], h[3]);
-    }
-  } else {
-    // min block: column j (natural order) = -round(dmin m_j) of sub-block j
-    const int jb = (kt - nkd) * 64;
-#pragma unroll
-    for (int ch = 0; ch < 8; ch++) {
-      const int j0 = jb + 8 * ch, sb = j0 >> 3;
-      uint32_t h[4] = {0u, 0u, 0u, 0u};
-      if (sb < d / 256) {
-        const uint4 hd = __ldg(reinterpret_cast<const uint4*>(rowp + sb * 144));
-        const float dm = h_hi(hd.x);
-        float v[8];
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-          uint32_t sc, mn;
-          Q4K::scale_min(hd.y, hd.z, hd.w, i, sc, mn);
-          v[i] = -(dm * (float)mn);
-        }
-#pragma unroll
-        for (int i = 0; i < 4; i++) h[i] = h2u(__floats2half2_rn(v[2 * i], v[2 * i + 1]));
-      }
-      out[ch] = make_uint4(h[0], h[1], h[2], h[3]);
+      for (int i = 0; i < 4; i++) h[i] = h2u(__hmul2(__hsub2(u2h(u[i]), K1024), A));
+      *reinterpret_cast<uint4*>(rowt + ((ch ^ sw) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
     }
   }
-#pragma unroll
-  for (int ch = 0; ch < 8; ch++)
-    *reinterpret_cast<uint4*>(tile + r * 128 + ((ch ^ (r & 7)) << 4)) = out[ch];
 }
 
-// n 32-bit words from a 2-byte-aligned global address (one extra word read)
-template <int N>
-VDEV void ldg_words_u16(const uint8_t* p, uint32_t (&w)[N]) {
-  const uint32_t mis = (uint32_t)((uintptr_t)p & 3u);
-  const uint32_t* q = reinterpret_cast<const uint32_t*>(p - mis);
-  uint32_t raw[N + 1];
-#pragma unroll
-  for (int i = 0; i <= N; i++) raw[i] = __ldg(q + i);
-#pragma unroll
-  for (int i = 0; i < N; i++) w[i] = __funnelshift_r(raw[i], raw[i + 1], 8 * mis);
-}
-
-// ---- Q6_K row -> 64 f16 of one K stage (down B tiles) ----------------------
-// Stage kt = quarter q of super-block sb: half h = q >> 1; positions 0..31
-// stream s0 = 2 (q & 1), 32..63 stream s0 + 1 (values 64 q + l, 64 q + 32 + l
-// of the super-block), groups of 4 ordered (0 2 1 3).  Value = round(d sc
-// (z - 32)) with (1024 + z) - 1056 exact.
-VDEV void dq_q6k_stage(const uint8_t* rowp, int kt, uint8_t* tile, int r) {
-  const uint8_t* sbp = rowp + (kt >> 2) * 210;
-  const int q = kt & 3, h = q >> 1, hi = q & 1, s0 = 2 * hi;
-  uint32_t ql[16], qh[8];
-  ldg_words_u16<16>(sbp + 64 * h, ql);
-  ldg_words_u16<8>(sbp + 128 + 32 * h, qh);
-  const float dd = __half2float(__ushort_as_half(
-      (unsigned short)((uint32_t)__ldg(sbp + 208) | ((uint32_t)__ldg(sbp + 209) << 8))));
-  const int8_t* sc = reinterpret_cast<const int8_t*>(sbp + 192 + 8 * h);
-  const __half2 K1056 = __float2half2_rn(1056.f);
+// ---- repacked Q6_K chunk row (shared memory) -> 64 f16 of one stage --------
+// bytes 0..63: z + 96 of the stage's 64 values in natural order (z the 6-bit
+// quant); bytes 64..71: f16 d sc of the four 16-value groups.  Value =
+// ((1024 + z + 96) - 1152) * d sc, the subtraction exact.
+VDEV void conv_dn(const uint8_t* raw, uint8_t* tile, int r) {
+  const uint4 v0 = *reinterpret_cast<const uint4*>(raw), v1 = *reinterpret_cast<const uint4*>(raw + 16);
+  const uint4 v2 = *reinterpret_cast<const uint4*>(raw + 32), v3 = *reinterpret_cast<const uint4*>(raw + 48);
+  const uint2 sc = *reinterpret_cast<const uint2*>(raw + 64);
+  const uint32_t w[16] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w, v2.x, v2.y, v2.z, v2.w, v3.x, v3.y, v3.z, v3.w};
+  const __half2 K1152 = __float2half2_rn(1152.f);
+  uint8_t* rowt = tile + r * 128;
+  const int sw = r & 7;
 #pragma unroll
   for (int ch = 0; ch < 8; ch++) {
-    const int s = s0 + (ch >> 2), l0 = 8 * (ch & 3);
-    const __half2 A = __float2half2_rn(dd * (float)__ldg(sc + 2 * s + (l0 >> 4)));
-    uint32_t hv[4];
-#pragma unroll
-    for (int i = 0; i < 2; i++) {
-      const uint32_t qlw = ql[(s & 1) * 8 + (l0 >> 2) + i], qhw = qh[(l0 >> 2) + i];
-      const uint32_t z = ((qlw >> (4 * hi)) & 0x0F0F0F0Fu) | (((qhw >> (2 * s)) & 0x03030303u) << 4);
-      const uint32_t u0 = (z & 0x00FF00FFu) | 0x64006400u, u1 = ((z >> 8) & 0x00FF00FFu) | 0x64006400u;
-      hv[2 * i] = h2u(__hmul2(__hsub2(u2h(u0), K1056), A));
-      hv[2 * i + 1] = h2u(__hmul2(__hsub2(u2h(u1), K1056), A));
-    }
-    *reinterpret_cast<uint4*>(tile + r * 128 + ((ch ^ (r & 7)) << 4)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+    const uint32_t sw2 = (ch >> 1) < 2 ? sc.x : sc.y;
+    const uint32_t a16 = ((ch >> 1) & 1) ? (sw2 >> 16) : (sw2 & 0xFFFFu);
+    const __half2 A = u2h(a16 | (a16 << 16));
+    const uint32_t w0 = w[2 * ch], w1 = w[2 * ch + 1];
+    const uint32_t h0 = h2u(__hmul2(__hsub2(u2h((w0 & 0x00FF00FFu) | 0x64006400u), K1152), A));
+    const uint32_t h1 = h2u(__hmul2(__hsub2(u2h(((w0 >> 8) & 0x00FF00FFu) | 0x64006400u), K1152), A));
+    const uint32_t h2 = h2u(__hmul2(__hsub2(u2h((w1 & 0x00FF00FFu) | 0x64006400u), K1152), A));
+    const uint32_t h3 = h2u(__hmul2(__hsub2(u2h(((w1 >> 8) & 0x00FF00FFu) | 0x64006400u), K1152), A));
+    *reinterpret_cast<uint4*>(rowt + ((ch ^ sw) << 4)) = make_uint4(h0, h1, h2, h3);
   }
 }
 
@@ -219,7 +195,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
   uint8_t* sm = reinterpret_cast<uint8_t*>(((uintptr_t)praw + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = sm;
   uint8_t* sB = sm + kPStages * kPStageA;
-  __shared__ uint64_t full[kPStages], empty[kPStages], tfull[2], tempty[2], drain;
+  uint8_t* sR = sB + kPStages * kPStageB;
+  __shared__ uint64_t full[kPStages], empty[kPStages], rawfull[kPStages], tfull[2], tempty[2], drain;
   __shared__ uint32_t tbase;
   __shared__ int n_items_s;
   __shared__ volatile int abort_s;
@@ -229,6 +206,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     for (int s = 0; s < kPStages; s++) {
       mbar_init(&full[s], MODE == P_ROUTER ? 1u : 1u + kDqWarps);
       mbar_init(&empty[s], 1);
+      mbar_init(&rawfull[s], 1);
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(&tfull[b], 1);
@@ -266,9 +244,28 @@ __global__ void __launch_bounds__(kPThreads, 1)
         for (int kt = 0; kt < p.nk; kt++, g++) {
           const int s = (int)(g % kPStages);
           if (g >= (uint32_t)kPStages && !pwait(&empty[s], ((g / kPStages) - 1) & 1, &abort_s, p.err)) break;
-          mbar_arrive_expect_tx(&full[s], kPStageA + (MODE == P_ROUTER ? kPStageB : 0u));
+          // B by TMA: the router's split weights; the gate/up min-block stages
+          // (rows e * 2fe + f of minmat: gate rows, then up rows)
+          const bool bt = MODE == P_ROUTER || (MODE == P_GATEUP && kt >= p.d / kPK);
+          mbar_arrive_expect_tx(&full[s], kPStageA + (bt ? kPStageB : 0u));
           tma_load_2d(sA + s * kPStageA, &tmA, kt * kPK, t.row0, &full[s]);
-          if constexpr (MODE == P_ROUTER) tma_load_2d(sB + s * kPStageB, &tmB, kt * kPK, 0, &full[s]);
+          if constexpr (MODE == P_ROUTER) {
+            tma_load_2d(sB + s * kPStageB, &tmB, kt * kPK, 0, &full[s]);
+          } else {
+            const int nt = item % p.n_ntiles;
+            if (MODE == P_GATEUP && bt) {
+              const int y0 = t.e * 2 * p.fe + nt * 128, x0 = (kt - p.d / kPK) * kPK;
+              tma_load_2d(sB + s * kPStageB, &tmB, x0, y0, &full[s]);
+              tma_load_2d(sB + s * kPStageB + kPStageB / 2, &tmB, x0, y0 + p.fe, &full[s]);
+            } else {
+              // the stage's raw weight chunk: one bulk copy (the dequant warps convert it)
+              const uint32_t cb = MODE == P_GATEUP ? kPRawGU : kPRawDN;
+              const int nkm = MODE == P_GATEUP ? p.d / kPK : p.nk;
+              const uint8_t* src = p.pack + ((size_t)(t.e * p.n_ntiles + nt) * nkm + kt) * cb;
+              mbar_arrive_expect_tx(&rawfull[s], cb);
+              bulk_g2s(sR + s * kPStageR, src, cb, &rawfull[s]);
+            }
+          }
         }
       }
       // the loads of the last stages land before the CTA may exit
@@ -312,37 +309,48 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
   } else if (warp >= kDqWarp0 && warp < kDqWarp0 + kDqWarps) {
     if constexpr (MODE != P_ROUTER) {
-      // ---- weight tiles: GGUF blocks -> swizzled f16 in shared memory --------
+      // ---- weight tiles: repacked raw chunks -> swizzled f16 in shared memory --
+      // Each thread owns one tile row.  A stage's raw chunk arrives by bulk
+      // copy (rawfull); the thread converts its row into the B tile and the
+      // warp arrives on full.  The gate/up min-block stages come by TMA: the
+      // warps only arrive once the stage's previous use is over.
       const int r = threadIdx.x - 32 * kDqWarp0;  // tile row 0..255
+      const int nkd = MODE == P_GATEUP ? p.d / kPK : p.nk;  // stages with a raw chunk
+      uint32_t rawpar = 0;  // rawfull phase parity per stage (bit s)
       uint32_t g = 0;
-      for (int item = blockIdx.x; item < n_items && !abort_s; item += gridDim.x) {
-        const int mt = item / p.n_ntiles, nt = item - mt * p.n_ntiles;
-        const PTile t = tile_of(mt);
-        const uint8_t* rowp;
-        if constexpr (MODE == P_GATEUP) {
-          const int f = nt * 128 + (r & 127);
-          rowp = p.exp_tab[3 * t.e + (r < 128 ? 0 : 1)] + (size_t)f * p.rb_gu;
-        } else {
-          rowp = p.exp_tab[3 * t.e + 2] + (size_t)(nt * kPN + r) * p.rb_d;
-        }
-        bool ok = true;
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < n_items && !abort_s; item += gridDim.x) {
         for (int kt = 0; kt < p.nk; kt++, g++) {
           const int s = (int)(g % kPStages);
           int w_ok = 1;
-          if (g >= (uint32_t)kPStages && lane == 0) w_ok = pwait(&empty[s], ((g / kPStages) - 1) & 1, &abort_s, p.err);
+          if (kt < nkd) {
+            if (lane == 0) w_ok = pwait(&rawfull[s], (rawpar >> s) & 1u, &abort_s, p.err);
+            rawpar ^= 1u << s;
+          } else if (g >= (uint32_t)kPStages && lane == 0) {
+            w_ok = pwait(&empty[s], ((g / kPStages) - 1) & 1, &abort_s, p.err);
+          }
           w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
           if (!w_ok) {
             ok = false;
             break;
           }
-          uint8_t* tile = sB + s * kPStageB;
-          if constexpr (MODE == P_GATEUP) dq_q4k_stage(rowp, kt, p.d / kPK, p.d, tile, r);
-          else dq_q6k_stage(rowp, kt, tile, r);
-          fence_proxy_async();
+          if (kt < nkd) {
+            uint8_t* tile = sB + s * kPStageB;
+            if constexpr (MODE == P_GATEUP) {
+              const uint8_t* raw = sR + s * kPStageR + r * 48;
+              Q4Raw q;
+              q.hd = *reinterpret_cast<const uint4*>(raw);
+              q.qa = *reinterpret_cast<const uint4*>(raw + 16);
+              q.qb = *reinterpret_cast<const uint4*>(raw + 32);
+              conv_q4k(q, kt, tile, r);
+            } else {
+              conv_dn(sR + s * kPStageR + r * 80, tile, r);
+            }
+            fence_proxy_async();
+          }
           __syncwarp();
           if (lane == 0) mbar_arrive(&full[s]);
         }
-        if (!ok) break;
       }
     }
   } else if (warp >= kEpiWarp0) {
@@ -451,7 +459,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
 #pragma unroll
             for (int i = 0; i < 4; i++) {
               const float g = __uint_as_float(vg[4 * j4 + i]), u = __uint_as_float(vu[4 * j4 + i]);
-              hv[i] = (g / (1.0f + expf(-g))) * u;
+              // fast exp and divide: h is rounded to f16 (2^-11) right after
+              hv[i] = __fdividef(g, 1.0f + __expf(-g)) * u;
             }
             // positions (0 2 1 3) within the group of 4
             hp[2 * j4] = h2u(__floats2half2_rn(hv[0], hv[2]));
@@ -531,6 +540,83 @@ __global__ void prefill_router_split(const float* R, __half* R2, int ne, int d) 
     }
     R2[(size_t)row * d + j] = __float2half_rn(v);
   }
+}
+
+// ---- Q4_K min block: minmat[e * 2fe + row][j] = -round(dmin m_j) of
+// sub-block j of gate row (row < fe) or up row (row - fe) of expert e;
+// columns d/32 .. Km zero ----------------------------------------------------
+__global__ void prefill_minmat(const uint8_t* const* exp_tab, int d, int fe, int Km, uint32_t rb, __half* out) {
+  const int row = blockIdx.x, e = row / (2 * fe), rr = row - e * 2 * fe;
+  const uint8_t* rowp = exp_tab[3 * e + (rr < fe ? 0 : 1)] + (size_t)(rr < fe ? rr : rr - fe) * rb;
+  for (int j = threadIdx.x; j < Km; j += blockDim.x) {
+    float v = 0.f;
+    if (j < d / 32) {
+      const uint32_t* hp = reinterpret_cast<const uint32_t*>(rowp + (j >> 3) * 144);
+      uint32_t sc, mn;
+      Q4K::scale_min(__ldg(hp + 1), __ldg(hp + 2), __ldg(hp + 3), j & 7, sc, mn);
+      v = -(h_hi(__ldg(hp)) * (float)mn);
+    }
+    out[(size_t)row * Km + j] = __float2half_rn(v);
+  }
+}
+
+// ---- repacking (once per layer): the raw bytes of each (expert, n-tile,
+// stage) in one contiguous chunk, rows in tile order -------------------------
+// gate/up: chunk (e * fe/128 + nt) * d/64 + kt, row r < 128 gate row nt 128 + r,
+// r >= 128 up row nt 128 + r - 128: the Q4_K header and quant bytes 32c.. of
+// super-block kt / 4 (c = kt % 4)
+__global__ void prefill_pack_gu(const uint8_t* const* exp_tab, int d, int fe, uint32_t rb, uint8_t* out) {
+  const int nkd = d / kPK, ntl = fe / 128;
+  const int b = blockIdx.x, kt = b % nkd, ent = b / nkd, nt = ent % ntl, e = ent / ntl, r = threadIdx.x;
+  const uint8_t* sbp =
+      exp_tab[3 * e + (r < 128 ? 0 : 1)] + (size_t)(nt * 128 + (r & 127)) * rb + (size_t)(kt >> 2) * 144;
+  const int c = kt & 3;
+  uint4* dst = reinterpret_cast<uint4*>(out + (size_t)b * kPRawGU + r * 48);
+  dst[0] = __ldg(reinterpret_cast<const uint4*>(sbp));
+  dst[1] = __ldg(reinterpret_cast<const uint4*>(sbp + 16 + 32 * c));
+  dst[2] = __ldg(reinterpret_cast<const uint4*>(sbp + 32 + 32 * c));
+}
+
+// down: chunk (e * d/256 + nt) * fe/64 + kt, row r = down row nt 256 + r: the
+// stage's 64 values (quarter q = kt % 4 of super-block kt / 4: streams
+// 2 (q & 1) and 2 (q & 1) + 1 of half q / 2, vireo gguf_compute.c:88-99) as
+// bytes z + 96 in natural order, then f16 d sc of the four 16-value groups
+__global__ void prefill_pack_dn(const uint8_t* const* exp_tab, int d, int fe, uint32_t rb, uint8_t* out) {
+  const int nkf = fe / kPK, ntl = d / kPN;
+  const int b = blockIdx.x, kt = b % nkf, ent = b / nkf, nt = ent % ntl, e = ent / ntl, r = threadIdx.x;
+  const uint8_t* sbp = exp_tab[3 * e + 2] + (size_t)(nt * kPN + r) * rb + (size_t)(kt >> 2) * 210;
+  const int q = kt & 3, h = q >> 1, s0 = 2 * (q & 1);
+  uint8_t* dst = out + (size_t)b * kPRawDN + r * 80;
+  uint32_t words[16];
+#pragma unroll
+  for (int i = 0; i < 16; i++) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int v = 4 * i + j, st = s0 + (v >> 5), l = v & 31;
+      const uint32_t lo = (__ldg(sbp + 64 * h + 32 * (st & 1) + l) >> (4 * (st >> 1))) & 15u;
+      const uint32_t hi = (__ldg(sbp + 128 + 32 * h + l) >> (2 * st)) & 3u;
+      w |= ((lo | (hi << 4)) + 96u) << (8 * j);
+    }
+    words[i] = w;
+  }
+  const float dd = __half2float(__ushort_as_half((unsigned short)(__ldg(sbp + 208) | (__ldg(sbp + 209) << 8))));
+  uint32_t scw[2];
+#pragma unroll
+  for (int g2 = 0; g2 < 2; g2++) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      const int grp = 2 * g2 + j, st = s0 + (grp >> 1);
+      const int8_t sc = (int8_t)__ldg(sbp + 192 + 8 * h + 2 * st + (grp & 1));
+      w |= (uint32_t)__half_as_ushort(__float2half_rn(dd * (float)sc)) << (16 * j);
+    }
+    scw[g2] = w;
+  }
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; i++) d4[i] = make_uint4(words[4 * i], words[4 * i + 1], words[4 * i + 2], words[4 * i + 3]);
+  d4[4] = make_uint4(scw[0], scw[1], 0u, 0u);
 }
 
 // ---- scan: padded row ranges, the tile table, placement cursors ------------
@@ -642,7 +728,7 @@ int prefill_supported(int d, int fe, int ne, int k, uint32_t rt, uint32_t gt, ui
 void prefill_scratch_free(PrefillScratch* s) {
   for (void* p : {(void*)s->xa, (void*)s->ids, (void*)s->wts, (void*)s->counts, (void*)s->cursor, (void*)s->tiles,
                   (void*)s->n_mtiles, (void*)s->rowpos, (void*)s->wrow, (void*)s->xg, (void*)s->hg, (void*)s->y,
-                  (void*)s->r2})
+                  (void*)s->r2, (void*)s->minmat, (void*)s->gu_pack, (void*)s->dn_pack})
     if (p) cudaFree(p);
   *s = PrefillScratch();
 }
@@ -679,9 +765,24 @@ int prefill_run(const PrefillLayer& L, PrefillScratch* S, const void* hb, float*
     if ((rc = grow((void**)&S->r2, &S->c_r2, (size_t)256 * d * 2))) return rc;
     prefill_router_split<<<256, 256, 0, st>>>(L.router, (__half*)S->r2, ne, d);
   }
-  CUtensorMap mA_r, mB_r, mA_gu, mA_d;
+  const int Km = Kx - d;
+  if (!S->minmat_ok) {
+    // per layer, once (again after the expert pointers change): the min block
+    // and the repacked weight chunks the GEMMs stream
+    const size_t n_gu = (size_t)ne * (fe / 128) * (d / kPK), n_dn = (size_t)ne * (d / kPN) * (fe / kPK);
+    if ((rc = grow((void**)&S->minmat, &S->c_minmat, (size_t)ne * 2 * fe * Km * 2)) ||
+        (rc = grow((void**)&S->gu_pack, &S->c_gu_pack, n_gu * kPRawGU)) ||
+        (rc = grow((void**)&S->dn_pack, &S->c_dn_pack, n_dn * kPRawDN)))
+      return rc;
+    prefill_minmat<<<ne * 2 * fe, 64, 0, st>>>(L.exp_tab, d, fe, Km, (uint32_t)(d / 256 * 144), S->minmat);
+    prefill_pack_gu<<<(unsigned)n_gu, kPN, 0, st>>>(L.exp_tab, d, fe, (uint32_t)(d / 256 * 144), S->gu_pack);
+    prefill_pack_dn<<<(unsigned)n_dn, kPN, 0, st>>>(L.exp_tab, d, fe, (uint32_t)(fe / 256 * 210), S->dn_pack);
+    S->minmat_ok = true;
+  }
+  CUtensorMap mA_r, mB_r, mA_gu, mA_d, mM;
   if ((rc = make_map(&mA_r, S->xa, T, Kx, kPM)) || (rc = make_map(&mB_r, S->r2, 256, d, kPN)) ||
-      (rc = make_map(&mA_gu, S->xg, rows, Kx, kPM)) || (rc = make_map(&mA_d, S->hg, rows, fe, kPM)))
+      (rc = make_map(&mA_gu, S->xg, rows, Kx, kPM)) || (rc = make_map(&mA_d, S->hg, rows, fe, kPM)) ||
+      (rc = make_map(&mM, S->minmat, (uint64_t)ne * 2 * fe, Km, 128)))
     return rc;
   static std::once_flag attr_once;
   std::call_once(attr_once, [] {
@@ -724,10 +825,12 @@ int prefill_run(const PrefillLayer& L, PrefillScratch* S, const void* hb, float*
   // gate/up + SwiGLU
   p.nk = Kx / kPK;
   p.n_ntiles = fe / 128;
-  prefill_gemm<P_GATEUP><<<num_sms, kPThreads, kPSmem, st>>>(mA_gu, mA_gu, p);
+  p.pack = S->gu_pack;
+  prefill_gemm<P_GATEUP><<<num_sms, kPThreads, kPSmem, st>>>(mA_gu, mM, p);
   // down, scaled by the routing weight
   p.nk = fe / kPK;
   p.n_ntiles = d / kPN;
+  p.pack = S->dn_pack;
   prefill_gemm<P_DOWN><<<num_sms, kPThreads, kPSmem, st>>>(mA_d, mA_d, p);
   prefill_combine<<<T, 256, 0, st>>>(S->rowpos, S->y, x, T, k, d);
   if (ids_out && cudaMemcpyAsync(ids_out, S->ids, pairs * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)

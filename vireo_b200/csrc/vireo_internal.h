@@ -63,8 +63,12 @@ struct PrefillScratch {
   __half* hg = nullptr;
   float* y = nullptr;
   __half* r2 = nullptr;
+  __half* minmat = nullptr;  // Q4_K min block of every gate/up row (depends on the expert pointers)
+  uint8_t* gu_pack = nullptr;  // repacked gate/up and down weight chunks (likewise)
+  uint8_t* dn_pack = nullptr;
+  bool minmat_ok = false;
   size_t c_xa = 0, c_ids = 0, c_wts = 0, c_counts = 0, c_cursor = 0, c_tiles = 0, c_n_mtiles = 0, c_rowpos = 0,
-         c_wrow = 0, c_xg = 0, c_hg = 0, c_y = 0, c_r2 = 0;
+         c_wrow = 0, c_xg = 0, c_hg = 0, c_y = 0, c_r2 = 0, c_minmat = 0, c_gu_pack = 0, c_dn_pack = 0;
 };
 int prefill_supported(int d, int fe, int ne, int k, uint32_t rt, uint32_t gt, uint32_t ut, uint32_t dt);
 int prefill_run(const PrefillLayer& L, PrefillScratch* S, const void* hb_bf16, float* x, int T, const float* bias,
