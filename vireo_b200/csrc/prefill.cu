@@ -55,7 +55,6 @@ namespace vireo {
 constexpr int kPM = 128;   // activation rows per tile
 constexpr int kPN = 256;   // weight rows per tile
 constexpr int kPK = 64;    // K per stage
-constexpr int kPStages = 3;
 constexpr int kPThreads = 512;
 constexpr int kDqWarp0 = 4, kDqWarps = 8, kEpiWarp0 = 12;
 constexpr int kPTopK = 8;  // prefill top-k limit (held in registers)
@@ -63,8 +62,25 @@ constexpr uint32_t kPStageA = kPM * kPK * 2, kPStageB = kPN * kPK * 2;
 // raw weight chunks of one stage (the repacked layouts, 256 rows each):
 // gate/up 48 B per row (Q4_K header + the stage's 32 quant bytes), down 80 B
 // per row (64 six-bit values as bytes z + 96, then 4 f16 scales d sc)
-constexpr uint32_t kPRawGU = kPN * 48, kPRawDN = kPN * 80, kPStageR = kPRawDN;
-constexpr uint32_t kPSmem = 1024 + kPStages * (kPStageA + kPStageB + kPStageR);
+constexpr uint32_t kPRawGU = kPN * 48, kPRawDN = kPN * 80;
+
+// Three rings per GEMM: activation tiles (TMA, freed by the MMA), raw weight
+// chunks (bulk copy, freed by the dequant warps) and converted weight tiles
+// (written by the dequant warps, freed by the MMA).  The first two run
+// several stages ahead of the MMA so their latency is hidden; only a few
+// 32 KB converted tiles need to be resident.
+template <int MODE>
+struct PRing {
+  static constexpr int NA = MODE == 2 ? 3 : 4;                 // activation stages
+  static constexpr int NB = 3;                                 // converted weight stages
+  static constexpr int NR = MODE == 1 ? 4 : (MODE == 2 ? 3 : 1);  // raw chunk stages
+  static constexpr uint32_t RB = MODE == 2 ? kPRawDN : kPRawGU;   // raw chunk bytes
+  static constexpr uint32_t OFF_B = NA * kPStageA;
+  static constexpr uint32_t OFF_R = OFF_B + NB * kPStageB;
+  static constexpr uint32_t BYTES = OFF_R + (MODE == 0 ? 0u : NR * RB);
+};
+constexpr uint32_t cmax(uint32_t a, uint32_t b) { return a > b ? a : b; }
+constexpr uint32_t kPSmem = 1024 + cmax(PRing<0>::BYTES, cmax(PRing<1>::BYTES, PRing<2>::BYTES));
 
 enum PMode { P_ROUTER = 0, P_GATEUP = 1, P_DOWN = 2 };
 
@@ -193,20 +209,30 @@ __global__ void __launch_bounds__(kPThreads, 1)
                  const __grid_constant__ PrefillParams p) {
   extern __shared__ __align__(1024) uint8_t praw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>(((uintptr_t)praw + 1023) & ~(uintptr_t)1023);
+  using RG = PRing<MODE>;
+  constexpr int NA = RG::NA, NB = RG::NB, NR = RG::NR;
   uint8_t* sA = sm;
-  uint8_t* sB = sm + kPStages * kPStageA;
-  uint8_t* sR = sB + kPStages * kPStageB;
-  __shared__ uint64_t full[kPStages], empty[kPStages], rawfull[kPStages], tfull[2], tempty[2], drain;
+  uint8_t* sB = sm + RG::OFF_B;
+  uint8_t* sR = sm + RG::OFF_R;
+  __shared__ uint64_t fullA[NA], emptyA[NA], fullB[NB], emptyB[NB], rawfull[NR], rawempty[NR];
+  __shared__ uint64_t tfull[2], tempty[2], drain;
   __shared__ uint32_t tbase;
   __shared__ int n_items_s;
   __shared__ volatile int abort_s;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kPStages; s++) {
-      mbar_init(&full[s], MODE == P_ROUTER ? 1u : 1u + kDqWarps);
-      mbar_init(&empty[s], 1);
-      mbar_init(&rawfull[s], 1);
+    for (int i = 0; i < NA; i++) {
+      mbar_init(&fullA[i], 1);
+      mbar_init(&emptyA[i], 1);
+    }
+    for (int i = 0; i < NB; i++) {
+      mbar_init(&fullB[i], MODE == P_ROUTER ? 1u : (uint32_t)kDqWarps);
+      mbar_init(&emptyB[i], 1);
+    }
+    for (int i = 0; i < NR; i++) {
+      mbar_init(&rawfull[i], 1);
+      mbar_init(&rawempty[i], kDqWarps);
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(&tfull[b], 1);
@@ -223,6 +249,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
   tc_fence_after();
   const uint32_t tmem = tbase;
   const int n_items = n_items_s;
+  const int nkd = MODE == P_GATEUP ? p.d / kPK : p.nk;  // stages with a raw chunk (all but the min block)
   auto tile_of = [&](int mt) -> PTile {
     if constexpr (MODE == P_ROUTER) {
       PTile t;
@@ -237,42 +264,43 @@ __global__ void __launch_bounds__(kPThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---- TMA producer ------------------------------------------------------
-      uint32_t g = 0;
-      for (int item = blockIdx.x; item < n_items && !abort_s; item += gridDim.x) {
+      // ---- producer: activation tiles (TMA) and raw weight chunks (bulk) ----
+      uint32_t g = 0, rg = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < n_items && !abort_s; item += gridDim.x) {
         const PTile t = tile_of(item / p.n_ntiles);
+        const int nt = item % p.n_ntiles;
         for (int kt = 0; kt < p.nk; kt++, g++) {
-          const int s = (int)(g % kPStages);
-          if (g >= (uint32_t)kPStages && !pwait(&empty[s], ((g / kPStages) - 1) & 1, &abort_s, p.err)) break;
-          // B by TMA: the router's split weights; the gate/up min-block stages
-          // (rows e * 2fe + f of minmat: gate rows, then up rows)
-          const bool bt = MODE == P_ROUTER || (MODE == P_GATEUP && kt >= p.d / kPK);
-          mbar_arrive_expect_tx(&full[s], kPStageA + (bt ? kPStageB : 0u));
-          tma_load_2d(sA + s * kPStageA, &tmA, kt * kPK, t.row0, &full[s]);
+          // every wait of the stage comes before any of its copies is issued,
+          // so an abort leaves no copy untracked by the drain below
+          const int a = (int)(g % NA), b = (int)(g % NB), sl = (int)(rg % NR);
+          const bool raw = MODE != P_ROUTER && kt < nkd;
+          if ((g >= (uint32_t)NA && !pwait(&emptyA[a], ((g / NA) - 1) & 1, &abort_s, p.err)) ||
+              (MODE == P_ROUTER && g >= (uint32_t)NB && !pwait(&emptyB[b], ((g / NB) - 1) & 1, &abort_s, p.err)) ||
+              (raw && rg >= (uint32_t)NR && !pwait(&rawempty[sl], ((rg / NR) - 1) & 1, &abort_s, p.err))) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&fullA[a], kPStageA);
+          tma_load_2d(sA + a * kPStageA, &tmA, kt * kPK, t.row0, &fullA[a]);
           if constexpr (MODE == P_ROUTER) {
-            tma_load_2d(sB + s * kPStageB, &tmB, kt * kPK, 0, &full[s]);
-          } else {
-            const int nt = item % p.n_ntiles;
-            if (MODE == P_GATEUP && bt) {
-              const int y0 = t.e * 2 * p.fe + nt * 128, x0 = (kt - p.d / kPK) * kPK;
-              tma_load_2d(sB + s * kPStageB, &tmB, x0, y0, &full[s]);
-              tma_load_2d(sB + s * kPStageB + kPStageB / 2, &tmB, x0, y0 + p.fe, &full[s]);
-            } else {
-              // the stage's raw weight chunk: one bulk copy (the dequant warps convert it)
-              const uint32_t cb = MODE == P_GATEUP ? kPRawGU : kPRawDN;
-              const int nkm = MODE == P_GATEUP ? p.d / kPK : p.nk;
-              const uint8_t* src = p.pack + ((size_t)(t.e * p.n_ntiles + nt) * nkm + kt) * cb;
-              mbar_arrive_expect_tx(&rawfull[s], cb);
-              bulk_g2s(sR + s * kPStageR, src, cb, &rawfull[s]);
-            }
+            mbar_arrive_expect_tx(&fullB[b], kPStageB);
+            tma_load_2d(sB + b * kPStageB, &tmB, kt * kPK, 0, &fullB[b]);
+          } else if (raw) {
+            const uint8_t* src = p.pack + ((size_t)(t.e * p.n_ntiles + nt) * nkd + kt) * RG::RB;
+            mbar_arrive_expect_tx(&rawfull[sl], RG::RB);
+            bulk_g2s(sR + sl * RG::RB, src, RG::RB, &rawfull[sl]);
+            rg++;
           }
         }
       }
-      // the loads of the last stages land before the CTA may exit
-      for (uint32_t j = g > (uint32_t)kPStages ? g - kPStages : 0; j < g; j++) {
-        volatile int never = 0;
-        mbar_wait(&full[j % kPStages], (j / kPStages) & 1, &never);
-      }
+      // the copies this thread issued land before the CTA may exit
+      volatile int never = 0;
+      for (uint32_t j = g > (uint32_t)NA ? g - NA : 0; j < g; j++) mbar_wait(&fullA[j % NA], (j / NA) & 1, &never);
+      if (MODE == P_ROUTER)
+        for (uint32_t j = g > (uint32_t)NB ? g - NB : 0; j < g; j++) mbar_wait(&fullB[j % NB], (j / NB) & 1, &never);
+      for (uint32_t j = rg > (uint32_t)NR ? rg - NR : 0; j < rg; j++)
+        mbar_wait(&rawfull[j % NR], (j / NR) & 1, &never);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -281,26 +309,27 @@ __global__ void __launch_bounds__(kPThreads, 1)
       uint32_t g = 0;
       int it = 0;
       for (int item = blockIdx.x; item < n_items && !abort_s; item += gridDim.x, it++) {
-        const int b = it & 1;
-        if (it >= 2 && !pwait(&tempty[b], ((it >> 1) - 1) & 1, &abort_s, p.err)) break;
+        const int b2 = it & 1;
+        if (it >= 2 && !pwait(&tempty[b2], ((it >> 1) - 1) & 1, &abort_s, p.err)) break;
         tc_fence_after();
-        const uint32_t dt = tmem + (uint32_t)(b * kPN);
+        const uint32_t dt = tmem + (uint32_t)(b2 * kPN);
         bool ok = true;
         for (int kt = 0; kt < p.nk; kt++, g++) {
-          const int s = (int)(g % kPStages);
-          if (!pwait(&full[s], (g / kPStages) & 1, &abort_s, p.err)) {
+          const int a = (int)(g % NA), b = (int)(g % NB);
+          if (!pwait(&fullA[a], (g / NA) & 1, &abort_s, p.err) || !pwait(&fullB[b], (g / NB) & 1, &abort_s, p.err)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t da = umma_desc_sw128(sA + s * kPStageA), db = umma_desc_sw128(sB + s * kPStageB);
+          const uint64_t da = umma_desc_sw128(sA + a * kPStageA), db = umma_desc_sw128(sB + b * kPStageB);
 #pragma unroll
           for (int kk = 0; kk < kPK / 16; kk++)
             umma_f16_ss(dt, da + 2 * kk, db + 2 * kk, idesc, (kt | kk) != 0 ? 1u : 0u);
-          umma_commit(&empty[s]);
+          umma_commit(&emptyA[a]);
+          umma_commit(&emptyB[b]);
         }
         if (!ok) break;
-        umma_commit(&tfull[b]);
+        umma_commit(&tfull[b2]);
       }
       // every MMA issued here is complete before TMEM may be released
       umma_commit(&drain);
@@ -309,48 +338,70 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
   } else if (warp >= kDqWarp0 && warp < kDqWarp0 + kDqWarps) {
     if constexpr (MODE != P_ROUTER) {
-      // ---- weight tiles: repacked raw chunks -> swizzled f16 in shared memory --
-      // Each thread owns one tile row.  A stage's raw chunk arrives by bulk
-      // copy (rawfull); the thread converts its row into the B tile and the
-      // warp arrives on full.  The gate/up min-block stages come by TMA: the
-      // warps only arrive once the stage's previous use is over.
+      // ---- weight tiles: raw chunks -> swizzled f16 in shared memory ----------
+      // Each thread owns one tile row: it waits for the stage's converted-tile
+      // slot to be free (emptyB) and its raw chunk to land (rawfull), converts
+      // its row, frees the raw slot (rawempty) and the warp arrives on fullB.
+      // A gate/up min-block stage is loaded into the slot by TMA instead (one
+      // lane of the first dequant warp; its arrive.expect_tx is that warp's
+      // arrival).
       const int r = threadIdx.x - 32 * kDqWarp0;  // tile row 0..255
-      const int nkd = MODE == P_GATEUP ? p.d / kPK : p.nk;  // stages with a raw chunk
-      uint32_t rawpar = 0;  // rawfull phase parity per stage (bit s)
-      uint32_t g = 0;
+      uint32_t g = 0, rg = 0;
       bool ok = true;
       for (int item = blockIdx.x; ok && item < n_items && !abort_s; item += gridDim.x) {
+        const PTile t = tile_of(item / p.n_ntiles);
+        const int nt = item % p.n_ntiles;
         for (int kt = 0; kt < p.nk; kt++, g++) {
-          const int s = (int)(g % kPStages);
+          const int b = (int)(g % NB);
           int w_ok = 1;
-          if (kt < nkd) {
-            if (lane == 0) w_ok = pwait(&rawfull[s], (rawpar >> s) & 1u, &abort_s, p.err);
-            rawpar ^= 1u << s;
-          } else if (g >= (uint32_t)kPStages && lane == 0) {
-            w_ok = pwait(&empty[s], ((g / kPStages) - 1) & 1, &abort_s, p.err);
-          }
+          if (lane == 0 && g >= (uint32_t)NB) w_ok = pwait(&emptyB[b], ((g / NB) - 1) & 1, &abort_s, p.err);
+          const bool is_raw = kt < nkd;
+          const int sl = (int)(rg % NR);
+          if (lane == 0 && w_ok && is_raw) w_ok = pwait(&rawfull[sl], (rg / NR) & 1, &abort_s, p.err);
           w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
           if (!w_ok) {
             ok = false;
             break;
           }
-          if (kt < nkd) {
-            uint8_t* tile = sB + s * kPStageB;
+          uint8_t* tile = sB + b * kPStageB;
+          if (is_raw) {
             if constexpr (MODE == P_GATEUP) {
-              const uint8_t* raw = sR + s * kPStageR + r * 48;
+              const uint8_t* raw = sR + sl * RG::RB + r * 48;
               Q4Raw q;
               q.hd = *reinterpret_cast<const uint4*>(raw);
               q.qa = *reinterpret_cast<const uint4*>(raw + 16);
               q.qb = *reinterpret_cast<const uint4*>(raw + 32);
               conv_q4k(q, kt, tile, r);
             } else {
-              conv_dn(sR + s * kPStageR + r * 80, tile, r);
+              conv_dn(sR + sl * RG::RB + r * 80, tile, r);
             }
             fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+              mbar_arrive(&rawempty[sl]);
+              mbar_arrive(&fullB[b]);
+            }
+            rg++;
+          } else if constexpr (MODE == P_GATEUP) {
+            if (lane == 0) {
+              if (warp == kDqWarp0) {
+                const int y0 = t.e * 2 * p.fe + nt * 128, x0 = (kt - nkd) * kPK;
+                mbar_arrive_expect_tx(&fullB[b], kPStageB);
+                tma_load_2d(tile, &tmB, x0, y0, &fullB[b]);
+                tma_load_2d(tile + kPStageB / 2, &tmB, x0, y0 + p.fe, &fullB[b]);
+              } else {
+                mbar_arrive(&fullB[b]);
+              }
+            }
           }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&full[s]);
         }
+      }
+      // a min-block load issued here lands before the CTA may exit (stage j
+      // of this loop is stage j % nk of its tile)
+      if (warp == kDqWarp0 && lane == 0 && MODE == P_GATEUP) {
+        volatile int never = 0;
+        for (uint32_t j = g > (uint32_t)NB ? g - NB : 0; j < g; j++)
+          if ((int)(j % (uint32_t)p.nk) >= nkd) mbar_wait(&fullB[j % NB], (j / NB) & 1, &never);
       }
     }
   } else if (warp >= kEpiWarp0) {
