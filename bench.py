@@ -352,9 +352,13 @@ def main():
 
 
 def run_prefill(args, wl):
-    """Config 4: one MoE layer over 8192 tokens at once (gguf_moe_prefill:
-    router GEMM + top-k, expert dispatch, Q4_K gate/up and Q6_K down grouped
-    GEMMs on the tcgen05 tensor cores, combine).  A step is the whole batch."""
+    """Config 4: one MoE layer over 8192 tokens at once.  One GPU:
+    gguf_moe_prefill (router GEMM + top-k, expert dispatch, Q4_K gate/up and
+    Q6_K down grouped GEMMs on the tcgen05 tensor cores, combine).  N GPUs:
+    gguf_moe_prefill_ep, expert parallel: each rank routes 8192/N of the
+    tokens, experts are placed on ranks by expected load (the router bias),
+    and the rows go to their experts' ranks and back as NCCL all-to-alls.
+    A step is the whole 8192-token batch (strong scaling)."""
     import ctypes as C
     import torch
     import vireo_b200 as V
@@ -373,24 +377,38 @@ def run_prefill(args, wl):
     spec = wl["spec"]()
     layer = S.MoeLayer(spec, wl["seed"])
     T, d = PREFILL_TOKENS, spec.dim
+    if T % world:
+        raise SystemExit(f"{T} tokens do not split over {world} ranks")
+    Tl = T // world
     dev = torch.device("cuda", local)
-    x_bf = torch.from_numpy(S.normal(wl["seed"], 41, T * d).astype(np.float32).reshape(T, d)).to(torch.bfloat16)
-    bias = torch.from_numpy((S.normal(wl["seed"], 42, spec.n_experts) * 0.5).astype(np.float32)).to(dev)
+    x_all = torch.from_numpy(S.normal(wl["seed"], 41, T * d).astype(np.float32).reshape(T, d)).to(torch.bfloat16)
+    x_bf = x_all[rank * Tl:(rank + 1) * Tl].contiguous()
+    bias_np = (S.normal(wl["seed"], 42, spec.n_experts) * 0.5).astype(np.float32)
+    bias = torch.from_numpy(bias_np).to(dev)
     hb = x_bf.to(dev)
-    x = torch.zeros((T, d), dtype=torch.float32, device=dev)
-    ids = torch.empty((T, spec.n_used), dtype=torch.int32, device=dev)
-    wts = torch.empty((T, spec.n_used), dtype=torch.float32, device=dev)
-    m = V.MoeLayer(layer, local)
+    x = torch.zeros((Tl, d), dtype=torch.float32, device=dev)
+    ids = torch.empty((Tl, spec.n_used), dtype=torch.int32, device=dev)
+    wts = torch.empty((Tl, spec.n_used), dtype=torch.float32, device=dev)
     stream = torch.cuda.Stream(dev)
     sp = C.c_void_p(stream.cuda_stream)
-    fn = L.gguf_moe_prefill
+    if world > 1:
+        owner = V.ep_place(np.exp(bias_np.astype(np.float64)), world)
+        uid = [V.ep_unique_id() if rank == 0 else None]
+        torch.distributed.broadcast_object_list(uid, src=0)
+        ep = V.MoeLayerEP(layer, owner, rank, world, uid[0], local)
+        fn, handle, sync, launches = L.gguf_moe_prefill_ep, ep.h, L.gguf_moe_ep_sync, 10
+        what = "gguf_moe_prefill_ep"
+    else:
+        m = V.MoeLayer(layer, local)
+        fn, handle, sync, launches = L.gguf_moe_prefill, m.h, L.gguf_moe_sync, 7
+        what = "gguf_moe_prefill"
 
     def step(hb_p, x_p):
-        V.check(fn(m.h, hb_p, x_p, T, bias.data_ptr(), ids.data_ptr(), wts.data_ptr(), sp), "gguf_moe_prefill")
+        V.check(fn(handle, hb_p, x_p, Tl, bias.data_ptr(), ids.data_ptr(), wts.data_ptr(), sp), what)
 
     for _ in range(args.warmup):
         step(hb.data_ptr(), x.data_ptr())
-    V.check(L.gguf_moe_sync(m.h, sp), "gguf_moe_sync")
+    V.check(sync(handle, sp), "sync")
     if world > 1:
         torch.distributed.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -401,18 +419,20 @@ def run_prefill(args, wl):
             step(hb.data_ptr(), x.data_ptr())
         e1.record(stream)
         torch.cuda.synchronize(dev)
-    V.check(L.gguf_moe_sync(m.h, sp), "gguf_moe_sync")
+    V.check(sync(handle, sp), "sync")
     t_sec = e0.elapsed_time(e1) / 1e3
     if world > 1:
         tt = torch.tensor([t_sec], device=dev)
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
         t_sec = float(tt.item())
-    value = args.steps * T * world / t_sec
+    value = args.steps * T / t_sec
 
     # end to end: hidden states and residual from pinned host memory, residual back
     hb_h = x_bf.pin_memory()
-    x_h = torch.zeros((T, d), dtype=torch.float32).pin_memory()
+    x_h = torch.zeros((Tl, d), dtype=torch.float32).pin_memory()
     n_e2e = max(3, args.steps // 4)
+    if world > 1:
+        torch.distributed.barrier()
     torch.cuda.synchronize(dev)
     t0 = time.perf_counter()
     for _ in range(n_e2e):
@@ -423,7 +443,12 @@ def run_prefill(args, wl):
         with torch.cuda.stream(stream):
             x_h.copy_(x, non_blocking=True)
         stream.synchronize()
-    e2e_tps = n_e2e * T * world / (time.perf_counter() - t0)
+    el = time.perf_counter() - t0
+    if world > 1:
+        tt = torch.tensor([el], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        el = float(tt.item())
+    e2e_tps = n_e2e * T / el
 
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -431,7 +456,7 @@ def run_prefill(args, wl):
         peak, peak_kind = float(pk["bf16_tflops_sustained"]), "measured (bf16 sustained)"
     except Exception:
         peak, peak_kind = 1400.0, "fallback (sustained)"
-    achieved = PREFILL_FLOPS * args.steps / t_sec / 1e12
+    achieved = PREFILL_FLOPS * args.steps / t_sec / 1e12 / world  # per GPU, against one GPU's peak
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         th = host_threads()
@@ -443,24 +468,28 @@ def run_prefill(args, wl):
     if rank == 0:
         line = {"metric": "moe_prefill_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_sec / args.steps * 1e3,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
                 "data": "synthetic (seeded GGUF blocks, random-init weights, N(0,1) bf16 tokens)",
                 "config": {"workload": args.workload, "desc": wl["desc"], "baseline_config": wl["config"],
-                           "tokens_per_step": T, "parallelism": f"replicas x{world}",
+                           "tokens_per_step": T, "tokens_per_rank": Tl,
+                           "parallelism": f"ep{world}" if world > 1 else "single GPU",
                            "l2": "391 MB of expert weights + 34 MB of tokens per step, above the 126 MB L2"},
                 "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                              "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
                              "algorithmic_flops_per_step": PREFILL_FLOPS,
-                             "kernel": "whole step (router, dispatch, gate/up, down, combine)"},
+                             "kernel": "whole step per GPU (router, dispatch, gate/up, down, combine"
+                                       + (", all-to-alls)" if world > 1 else ")")},
                 "cpu_baseline": cpu,
                 "e2e": {"value": e2e_tps, "unit": "tok/s", "h2d_bytes_per_step": T * d * (2 + 4),
                         "d2h_bytes_per_step": T * d * 4,
-                        "note": "bf16 tokens + fp32 residual in from pinned host, residual out"},
-                "gpu_launches": 7 * args.steps, "clocks": clk.summary()}
+                        "note": "bf16 tokens + fp32 residual in from pinned host, residual out (all ranks)"},
+                "gpu_launches": launches * args.steps, "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
-    m.close()
     if world > 1:
+        ep.close()
         torch.distributed.destroy_process_group()
+    else:
+        m.close()
 
 
 def zipf_routes(n_tok, n_layers, ne, k, seed):

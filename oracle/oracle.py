@@ -74,6 +74,8 @@ def port():
         lib.orc_moe_ffn_batch_bias.argtypes = [C.POINTER(OrcMoeLayer), C.c_int, _f32p, _f32p, _i32p, _f32p,
                                                C.c_void_p]
         lib.orc_moe_ffn_batch_bias.restype = C.c_int
+        lib.orc_expert_ffn.argtypes = [C.POINTER(OrcMoeLayer), C.c_int, _f32p, _f32p]
+        lib.orc_expert_ffn.restype = C.c_int
         lib.orc_set_threads.argtypes = [C.c_int]
         lib.orc_max_threads.restype = C.c_int
         _port = lib
@@ -171,6 +173,17 @@ class PortMoe:
             port().orc_moe_ffn_batch_bias(C.byref(self.desc), n, hb.reshape(-1), x.reshape(-1),
                                           ids.reshape(-1), wts.reshape(-1), b.ctypes.data)
         return x, ids, wts
+
+
+    def expert(self, e: int, hb) -> np.ndarray:
+        """One expert's FFN output (before the gate weight) for one token:
+        the body of the reference's per-expert loop, gguf_run.c:202-208."""
+        s = self.layer.spec
+        hb = np.ascontiguousarray(hb, dtype=np.float32).reshape(s.dim)
+        out = np.zeros(s.dim, dtype=np.float32)
+        if port().orc_expert_ffn(C.byref(self.desc), int(e), hb, out):
+            raise ValueError(f"bad expert id {e}")
+        return out
 
 
 class RefMoe:

@@ -280,6 +280,35 @@ static void softmax_inplace(float *v, int n) {
     for (int i = 0; i < n; i++) v[i] = v[i] / s;
 }
 
+/* One expert's FFN for one token (gguf_run.c:202-208): gate and up mat-vecs,
+ * SwiGLU h = g / (1 + expf(-g)) * u, down mat-vec into dn [dim].  g and u
+ * are [ffn_exp] work buffers (g ends holding h). */
+static void expert_ffn(const orc_moe_layer *L, int e, const float *hb, float *g, float *u, float *dn) {
+    int d = L->dim, fe = L->ffn_exp, ne = L->n_experts;
+    uint64_t gs = L->gate_nbytes / (uint64_t)ne, us = L->up_nbytes / (uint64_t)ne,
+             ds = L->down_nbytes / (uint64_t)ne;
+    orc_matmul(g, hb, L->gate_type, (const uint8_t *)L->gate + (uint64_t)e * gs, d, fe);
+    orc_matmul(u, hb, L->up_type, (const uint8_t *)L->up + (uint64_t)e * us, d, fe);
+    for (int i = 0; i < fe; i++) {
+        float gi = g[i];
+        float den = 1.0f + expf(-gi);
+        float s = gi / den;
+        g[i] = s * u[i];
+    }
+    orc_matmul(dn, g, L->down_type, (const uint8_t *)L->down + (uint64_t)e * ds, fe, d);
+}
+
+/* expert_ffn for callers (the expert-parallel dataflow tests run one expert
+ * at a time on the rank that holds it); returns -1 for a bad expert id. */
+int orc_expert_ffn(const orc_moe_layer *L, int e, const float *hb, float *dn) {
+    if (e < 0 || e >= L->n_experts) return -1;
+    float *g = (float *)malloc(sizeof(float) * (size_t)L->ffn_exp);
+    float *u = (float *)malloc(sizeof(float) * (size_t)L->ffn_exp);
+    expert_ffn(L, e, hb, g, u, dn);
+    free(g); free(u);
+    return 0;
+}
+
 /* One token through the MoE FFN.  hb: normalised hidden [dim]; x: residual
  * [dim], updated in place (x += sum_t w_t * expert_t(hb)).  ids/wts receive
  * the selected experts in rank order and their gate weights (after renorm).
@@ -328,20 +357,10 @@ int orc_moe_ffn_bias(const orc_moe_layer *L, const float *hb, float *x, int32_t 
         for (int t = 0; t < kk; t++) ws = ws + w[t];
         if (ws > 0) for (int t = 0; t < kk; t++) w[t] = w[t] / ws;
     }
-    uint64_t gs = L->gate_nbytes / (uint64_t)ne, us = L->up_nbytes / (uint64_t)ne,
-             ds = L->down_nbytes / (uint64_t)ne;
     for (int t = 0; t < kk; t++) {
         int e = idx[t];
         if (e < 0) continue;
-        orc_matmul(g, hb, L->gate_type, (const uint8_t *)L->gate + (uint64_t)e * gs, d, fe);
-        orc_matmul(u, hb, L->up_type, (const uint8_t *)L->up + (uint64_t)e * us, d, fe);
-        for (int i = 0; i < fe; i++) {
-            float gi = g[i];
-            float den = 1.0f + expf(-gi);
-            float s = gi / den;
-            g[i] = s * u[i];
-        }
-        orc_matmul(dn, g, L->down_type, (const uint8_t *)L->down + (uint64_t)e * ds, fe, d);
+        expert_ffn(L, e, hb, g, u, dn);
         for (int i = 0; i < d; i++) { float t2 = w[t] * dn[i]; acc[i] = acc[i] + t2; }
     }
     for (int i = 0; i < d; i++) x[i] = x[i] + acc[i];

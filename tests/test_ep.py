@@ -1,0 +1,138 @@
+"""Expert-parallel batched MoE FFN (gguf_moe_prefill_ep) on the GPU, through
+the C-ABI.  The expert-parallel result must be bit-identical to
+gguf_moe_prefill on one GPU over the same tokens (same GEMM arithmetic per
+row, same combine order), and within the oracle tolerance of the CPU
+restatement of the reference's moe_ffn.
+
+world 1 runs in this process (the whole dispatch / return path over an NCCL
+communicator of one rank); world 2 runs as two spawned processes and is
+skipped on a box with fewer than two GPUs.
+"""
+import os
+import time
+
+import numpy as np
+import pytest
+
+from vireo_b200 import synth as S
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3
+
+
+def _case(seed):
+    spec = S.MoeLayerSpec(1024, 512, 32, 8, 1, S.GGML_Q4_K, S.GGML_Q4_K, S.GGML_Q6_K)
+    L = S.MoeLayer(spec, seed)
+    T = 300
+    toks = S.normal(seed, 31, T * spec.dim).astype(np.float32).reshape(T, spec.dim)
+    x0 = (S.normal(seed, 32, toks.size) * 0.5).astype(np.float32).reshape(toks.shape)
+    bias = (S.normal(seed, 33, spec.n_experts) * 0.5).astype(np.float32)
+    return spec, L, toks, x0, bias
+
+
+def _single_gpu(L, toks, x0, bias, device=0):
+    import torch
+    import vireo_b200 as V
+    m = V.MoeLayer(L, device)
+    try:
+        dev = torch.device("cuda", device)
+        hb = torch.from_numpy(toks).to(dev).to(torch.bfloat16)
+        x = torch.from_numpy(x0.copy()).to(dev)
+        ids = torch.zeros((toks.shape[0], L.spec.n_used), dtype=torch.int32, device=dev)
+        wts = torch.zeros((toks.shape[0], L.spec.n_used), dtype=torch.float32, device=dev)
+        b = torch.from_numpy(bias).to(dev)
+        V.check(V.lib().gguf_moe_prefill(m.h, hb.data_ptr(), x.data_ptr(), toks.shape[0], b.data_ptr(),
+                                         ids.data_ptr(), wts.data_ptr(), None), "gguf_moe_prefill")
+        m.sync()
+        return x.cpu().numpy(), ids.cpu().numpy(), wts.cpu().numpy()
+    finally:
+        m.close()
+
+
+def _ep_run(L, toks, x0, bias, owner, rank, world, uid, device):
+    import torch
+    import vireo_b200 as V
+    dev = torch.device("cuda", device)
+    ep = V.MoeLayerEP(L, owner, rank, world, uid, device)
+    try:
+        hb = torch.from_numpy(toks).to(dev).to(torch.bfloat16)
+        x = torch.from_numpy(x0.copy()).to(dev)
+        n = toks.shape[0]
+        ids = torch.full((max(n, 1), L.spec.n_used), -7, dtype=torch.int32, device=dev)
+        wts = torch.zeros((max(n, 1), L.spec.n_used), dtype=torch.float32, device=dev)
+        b = torch.from_numpy(bias).to(dev)
+        outs = []
+        for _ in range(2):  # twice: buffers reused, results repeat
+            xx = x.clone()
+            ep.prefill(hb, xx, b, ids, wts)
+            ep.sync()
+            outs.append((xx.cpu().numpy(), ids.cpu().numpy()[:n], wts.cpu().numpy()[:n]))
+        return outs
+    finally:
+        ep.close()
+
+
+def test_ep_world1_matches_single_gpu_bits():
+    import torch
+    import vireo_b200 as V
+    assert torch.cuda.is_available()
+    from oracle import oracle as O
+    spec, L, toks, x0, bias = _case(71)
+    ref = _single_gpu(L, toks, x0, bias)
+    owner = np.zeros(spec.n_experts, dtype=np.int32)
+    outs = _ep_run(L, toks, x0, bias, owner, 0, 1, V.ep_unique_id(), 0)
+    for x, ids, wts in outs:
+        assert np.array_equal(ids, ref[1])
+        assert np.array_equal(wts.view(np.uint32), ref[2].view(np.uint32))
+        assert np.array_equal(x.view(np.uint32), ref[0].view(np.uint32)), np.abs(x - ref[0]).max()
+    # and the CPU restatement of the reference, within tolerance (bf16-rounded inputs)
+    hb = torch.from_numpy(toks).to(torch.bfloat16).float().numpy()
+    rx, rids, _ = O.PortMoe(L)(hb[:40], x0[:40], bias)
+    agree = (rids == ref[1][:40]).all(axis=1)
+    for i in np.flatnonzero(agree):
+        d = outs[0][0][i] - x0[i]
+        r = rx[i] - x0[i]
+        assert np.abs(d - r).max() / np.abs(r).max() < TOL
+
+
+def _rank_main(rank, world, tmp, split):
+    """Spawned rank of the world-2 test."""
+    import torch
+    import vireo_b200 as V
+    torch.cuda.set_device(rank)
+    spec, L, toks, x0, bias = _case(72)
+    idf = os.path.join(tmp, "uid.bin")
+    if rank == 0:
+        with open(idf + ".tmp", "wb") as f:
+            f.write(V.ep_unique_id())
+        os.replace(idf + ".tmp", idf)
+    t0 = time.time()
+    while not os.path.exists(idf):
+        if time.time() - t0 > 60:
+            raise TimeoutError("no unique id")
+        time.sleep(0.05)
+    with open(idf, "rb") as f:
+        uid = f.read()
+    owner = V.ep_place(np.exp(bias.astype(np.float64)), world)
+    lo, hi = split[rank], split[rank + 1]
+    outs = _ep_run(L, toks[lo:hi], x0[lo:hi], bias, owner, rank, world, uid, rank)
+    np.save(os.path.join(tmp, f"x{rank}.npy"), np.stack([o[0] for o in outs]) if hi > lo else np.zeros((2, 0, spec.dim)))
+    np.save(os.path.join(tmp, f"ids{rank}.npy"), outs[0][1])
+
+
+@pytest.mark.parametrize("split", [(0, 150, 300), (0, 300, 300)])
+def test_ep_world2_matches_single_gpu_bits(tmp_path, split):
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    mp.start_processes(_rank_main, args=(2, str(tmp_path), split), nprocs=2, join=True, start_method="spawn")
+    spec, L, toks, x0, bias = _case(72)
+    ref = _single_gpu(L, toks, x0, bias)
+    for r in range(2):
+        lo, hi = split[r], split[r + 1]
+        xs = np.load(tmp_path / f"x{r}.npy")
+        for x in xs:
+            assert np.array_equal(x.view(np.uint32), ref[0][lo:hi].view(np.uint32)), (r, np.abs(x - ref[0][lo:hi]).max())
+        assert np.array_equal(np.load(tmp_path / f"ids{r}.npy"), ref[1][lo:hi])

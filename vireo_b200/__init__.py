@@ -113,6 +113,20 @@ def lib():
                                          C.c_void_p, C.c_void_p]
         L.gguf_moe_prefill.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
                                        C.c_void_p, C.c_void_p]
+        # expert parallelism (include/gguf_moe.h)
+        L.gguf_moe_ep_unique_id.argtypes = [C.c_void_p]
+        L.gguf_moe_ep_place.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+        L.gguf_moe_ep_offsets.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                          C.c_void_p]
+        L.gguf_moe_ep_create.argtypes = [C.POINTER(GgufMoeDesc), C.c_void_p, C.c_int, C.c_int, C.c_void_p,
+                                         C.POINTER(C.c_void_p)]
+        L.gguf_moe_prefill_ep.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
+                                          C.c_void_p, C.c_void_p]
+        L.gguf_moe_ep_sync.argtypes = [C.c_void_p, C.c_void_p]
+        L.gguf_moe_ep_layer.argtypes = [C.c_void_p]
+        L.gguf_moe_ep_layer.restype = C.c_void_p
+        L.gguf_moe_ep_destroy.argtypes = [C.c_void_p]
+        L.gguf_moe_ep_destroy.restype = None
         # ExpertStore (include/expert_store.h)
         L.expert_store_create.argtypes = [C.c_int, C.c_uint64, C.c_int, C.c_int]
         L.expert_store_create.restype = C.c_void_p
@@ -249,3 +263,67 @@ class MoeLayer:
             self.close()
         except Exception:
             pass
+
+
+def ep_place(expected_load, world: int) -> np.ndarray:
+    """gguf_moe_ep_place: expert -> rank by expected load (host only)."""
+    load = np.ascontiguousarray(expected_load, dtype=np.float64)
+    owner = np.zeros(load.size, dtype=np.int32)
+    check(lib().gguf_moe_ep_place(load.ctypes.data, load.size, world, owner.ctypes.data), "gguf_moe_ep_place")
+    return owner
+
+
+def ep_offsets(counts, rank: int):
+    """gguf_moe_ep_offsets over a [world][world] count matrix (host only):
+    (send_off, recv_off, recv_cnt, recv_total)."""
+    c = np.ascontiguousarray(counts, dtype=np.int32)
+    w = c.shape[0]
+    so, ro, rc = (np.zeros(w, dtype=np.int32) for _ in range(3))
+    tot = C.c_int32()
+    check(lib().gguf_moe_ep_offsets(c.ctypes.data, w, rank, so.ctypes.data, ro.ctypes.data, rc.ctypes.data,
+                                    C.byref(tot)), "gguf_moe_ep_offsets")
+    return so, ro, rc, int(tot.value)
+
+
+def ep_unique_id() -> bytes:
+    buf = C.create_string_buffer(128)
+    check(lib().gguf_moe_ep_unique_id(buf), "gguf_moe_ep_unique_id")
+    return buf.raw
+
+
+class MoeLayerEP:
+    """One rank's share of an expert-parallel MoE layer (gguf_moe_ep_*).
+    Every rank constructs it with the same owner table and unique id."""
+
+    def __init__(self, layer, owner, rank: int, world: int, uid: bytes, device: int = 0):
+        import torch
+        s = layer.spec
+        self.spec = s
+        dev = torch.device("cuda", device)
+        up = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.uint8).reshape(-1)).to(dev)
+        self._keep = [up(layer.router), up(layer.gate), up(layer.up), up(layer.down)]
+        r, g, u, dn = self._keep
+        self.desc = GgufMoeDesc(s.dim, s.ffn_exp, s.n_experts, s.n_used, s.topk_renorm, s.router_type,
+                                s.gate_type, s.up_type, s.down_type, r.data_ptr(), g.data_ptr(), u.data_ptr(),
+                                dn.data_ptr(), g.numel(), u.numel(), dn.numel())
+        self.owner = np.ascontiguousarray(owner, dtype=np.int32)
+        buf = C.create_string_buffer(uid, 128)
+        h = C.c_void_p()
+        check(lib().gguf_moe_ep_create(C.byref(self.desc), self.owner.ctypes.data, rank, world, buf, C.byref(h)),
+              "gguf_moe_ep_create")
+        self.h = h
+
+    def prefill(self, hb_bf16, x, bias=None, ids=None, wts=None, stream=None) -> None:
+        n = hb_bf16.shape[0]
+        check(lib().gguf_moe_prefill_ep(self.h, hb_bf16.data_ptr(), x.data_ptr(), n,
+                                        bias.data_ptr() if bias is not None else None,
+                                        ids.data_ptr() if ids is not None else None,
+                                        wts.data_ptr() if wts is not None else None, stream), "gguf_moe_prefill_ep")
+
+    def sync(self, stream=None) -> None:
+        check(lib().gguf_moe_ep_sync(self.h, stream), "gguf_moe_ep_sync")
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            lib().gguf_moe_ep_destroy(self.h)
+            self.h = None

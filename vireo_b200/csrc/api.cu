@@ -13,6 +13,7 @@
 #include "expert_store.h"
 #include "gguf_moe.h"
 #include "moe_decode.cuh"
+#include "moe_view.h"
 #include "vireo_internal.h"
 
 namespace vireo {
@@ -382,6 +383,17 @@ struct gguf_moe {
   int num_sms = 0;
 };
 
+int vireo::moe_view(gguf_moe* m, MoeView* v) {
+  if (!m || !v) return VIREO_ERR_ARG;
+  v->desc = &m->desc;
+  v->exp_tab = m->d_exp_tab;
+  v->pre = &m->pre;
+  v->err = m->prm.s.err;
+  v->num_sms = m->num_sms;
+  v->stream = m->stream;
+  return VIREO_OK;
+}
+
 static int moe_reset_scratch(gguf_moe* m, cudaStream_t s) {
   return cuda_status(cudaMemsetAsync(m->scratch, 0, m->scratch_bytes, s));
 }
@@ -489,30 +501,33 @@ int gguf_moe_create(const gguf_moe_desc* desc, gguf_moe** out) {
   return VIREO_OK;
 }
 
-// One launch of the decode kernel (or its routed variant) for one token:
-// cooperative (every CTA resident: CTAs wait on one another's flags) and with
-// programmatic serialization, so that the next token's kernel may begin its
-// weight-only prologue while this one drains (griddepcontrol.wait in the
-// kernel orders everything that reads the previous kernel's output).
+// One launch of the decode kernel (or its routed variant) for one token,
+// with programmatic stream serialization: the next token's CTAs take SMs as
+// this launch's CTAs leave and run their weight-only prologue (barrier set-up,
+// router rows) before griddepcontrol.wait, which orders everything that reads
+// the previous kernel's output.  The launch is not marked cooperative (the
+// driver refuses cooperative + programmatic launches), so co-residency of the
+// grid's CTAs, which wait on one another's flags, rests on the grid being one
+// CTA per SM with occupancy >= 1 (checked at create) and on nothing else
+// holding the SMs; every such wait is bounded, so a launch that shares the
+// GPU with another kernel that holds SMs ends with VIREO_ERR_TIMEOUT instead
+// of hanging.
 static int moe_launch(gguf_moe* m, const void* kernel, void** args, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(m->grid);
   cfg.blockDim = dim3(kDecodeThreads);
   cfg.dynamicSmemBytes = m->smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = m->pdl ? 2 : 1;
+  cfg.numAttrs = m->pdl ? 1 : 0;
   cudaError_t e = cudaLaunchKernelExC(&cfg, kernel, args);
   if (e != cudaSuccess && m->pdl) {
-    // this driver refuses cooperative + programmatic launches: drop PDL
     cudaGetLastError();
     m->pdl = false;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 0;
     e = cudaLaunchKernelExC(&cfg, kernel, args);
   }
   return cuda_status(e);

@@ -596,8 +596,10 @@ __global__ void prefill_router_split(const float* R, __half* R2, int ne, int d) 
 // ---- Q4_K min block: minmat[e * 2fe + row][j] = -round(dmin m_j) of
 // sub-block j of gate row (row < fe) or up row (row - fe) of expert e;
 // columns d/32 .. Km zero ----------------------------------------------------
-__global__ void prefill_minmat(const uint8_t* const* exp_tab, int d, int fe, int Km, uint32_t rb, __half* out) {
+__global__ void prefill_minmat(const uint8_t* const* exp_tab, const int* own, int d, int fe, int Km, uint32_t rb,
+                               __half* out) {
   const int row = blockIdx.x, e = row / (2 * fe), rr = row - e * 2 * fe;
+  if (own && !own[e]) return;  // expert held by another rank: its bytes are never read
   const uint8_t* rowp = exp_tab[3 * e + (rr < fe ? 0 : 1)] + (size_t)(rr < fe ? rr : rr - fe) * rb;
   for (int j = threadIdx.x; j < Km; j += blockDim.x) {
     float v = 0.f;
@@ -616,9 +618,11 @@ __global__ void prefill_minmat(const uint8_t* const* exp_tab, int d, int fe, int
 // gate/up: chunk (e * fe/128 + nt) * d/64 + kt, row r < 128 gate row nt 128 + r,
 // r >= 128 up row nt 128 + r - 128: the Q4_K header and quant bytes 32c.. of
 // super-block kt / 4 (c = kt % 4)
-__global__ void prefill_pack_gu(const uint8_t* const* exp_tab, int d, int fe, uint32_t rb, uint8_t* out) {
+__global__ void prefill_pack_gu(const uint8_t* const* exp_tab, const int* own, int d, int fe, uint32_t rb,
+                                uint8_t* out) {
   const int nkd = d / kPK, ntl = fe / 128;
   const int b = blockIdx.x, kt = b % nkd, ent = b / nkd, nt = ent % ntl, e = ent / ntl, r = threadIdx.x;
+  if (own && !own[e]) return;
   const uint8_t* sbp =
       exp_tab[3 * e + (r < 128 ? 0 : 1)] + (size_t)(nt * 128 + (r & 127)) * rb + (size_t)(kt >> 2) * 144;
   const int c = kt & 3;
@@ -632,9 +636,11 @@ __global__ void prefill_pack_gu(const uint8_t* const* exp_tab, int d, int fe, ui
 // stage's 64 values (quarter q = kt % 4 of super-block kt / 4: streams
 // 2 (q & 1) and 2 (q & 1) + 1 of half q / 2, vireo gguf_compute.c:88-99) as
 // bytes z + 96 in natural order, then f16 d sc of the four 16-value groups
-__global__ void prefill_pack_dn(const uint8_t* const* exp_tab, int d, int fe, uint32_t rb, uint8_t* out) {
+__global__ void prefill_pack_dn(const uint8_t* const* exp_tab, const int* own, int d, int fe, uint32_t rb,
+                                uint8_t* out) {
   const int nkf = fe / kPK, ntl = d / kPN;
   const int b = blockIdx.x, kt = b % nkf, ent = b / nkf, nt = ent % ntl, e = ent / ntl, r = threadIdx.x;
+  if (own && !own[e]) return;
   const uint8_t* sbp = exp_tab[3 * e + 2] + (size_t)(nt * kPN + r) * rb + (size_t)(kt >> 2) * 210;
   const int q = kt & 3, h = q >> 1, s0 = 2 * (q & 1);
   uint8_t* dst = out + (size_t)b * kPRawDN + r * 80;
@@ -785,6 +791,7 @@ void prefill_scratch_free(PrefillScratch* s) {
 }
 
 static int grow(void** p, size_t* cap, size_t bytes) {
+  bytes = std::max<size_t>(bytes, 256);
   if (*cap >= bytes && *p) return VIREO_OK;
   if (*p) cudaFree(*p);
   *p = nullptr;
@@ -797,63 +804,31 @@ static int grow(void** p, size_t* cap, size_t bytes) {
   return VIREO_OK;
 }
 
-int prefill_run(const PrefillLayer& L, PrefillScratch* S, const void* hb, float* x, int T, const float* bias,
-                int32_t* ids_out, float* wts_out, int* d_err, int num_sms, cudaStream_t st) {
-  const int d = L.d, fe = L.fe, ne = L.ne, k = L.k;
-  const int Kx = d + ((d / 32 + 63) / 64) * 64;
-  const size_t pairs = (size_t)T * k, rows = ((pairs + (size_t)ne * (kPM - 1)) + kPM - 1) / kPM * kPM;
-  const size_t max_mtiles = rows / kPM + 1;
-  int rc;
-  if ((rc = grow((void**)&S->xa, &S->c_xa, (size_t)T * Kx * 2)) || (rc = grow((void**)&S->ids, &S->c_ids, pairs * 4)) ||
-      (rc = grow((void**)&S->wts, &S->c_wts, pairs * 4)) || (rc = grow((void**)&S->counts, &S->c_counts, 256 * 4)) ||
-      (rc = grow((void**)&S->cursor, &S->c_cursor, 256 * 4)) ||
-      (rc = grow((void**)&S->tiles, &S->c_tiles, max_mtiles * sizeof(PTile))) ||
-      (rc = grow((void**)&S->n_mtiles, &S->c_n_mtiles, 16)) || (rc = grow((void**)&S->rowpos, &S->c_rowpos, pairs * 4)) ||
-      (rc = grow((void**)&S->wrow, &S->c_wrow, rows * 4)) || (rc = grow((void**)&S->xg, &S->c_xg, rows * Kx * 2)) ||
-      (rc = grow((void**)&S->hg, &S->c_hg, rows * fe * 2)) || (rc = grow((void**)&S->y, &S->c_y, rows * d * 4)))
-    return rc;
-  if (!S->r2) {
-    if ((rc = grow((void**)&S->r2, &S->c_r2, (size_t)256 * d * 2))) return rc;
-    prefill_router_split<<<256, 256, 0, st>>>(L.router, (__half*)S->r2, ne, d);
-  }
-  const int Km = Kx - d;
-  if (!S->minmat_ok) {
-    // per layer, once (again after the expert pointers change): the min block
-    // and the repacked weight chunks the GEMMs stream
-    const size_t n_gu = (size_t)ne * (fe / 128) * (d / kPK), n_dn = (size_t)ne * (d / kPN) * (fe / kPK);
-    if ((rc = grow((void**)&S->minmat, &S->c_minmat, (size_t)ne * 2 * fe * Km * 2)) ||
-        (rc = grow((void**)&S->gu_pack, &S->c_gu_pack, n_gu * kPRawGU)) ||
-        (rc = grow((void**)&S->dn_pack, &S->c_dn_pack, n_dn * kPRawDN)))
-      return rc;
-    prefill_minmat<<<ne * 2 * fe, 64, 0, st>>>(L.exp_tab, d, fe, Km, (uint32_t)(d / 256 * 144), S->minmat);
-    prefill_pack_gu<<<(unsigned)n_gu, kPN, 0, st>>>(L.exp_tab, d, fe, (uint32_t)(d / 256 * 144), S->gu_pack);
-    prefill_pack_dn<<<(unsigned)n_dn, kPN, 0, st>>>(L.exp_tab, d, fe, (uint32_t)(fe / 256 * 210), S->dn_pack);
-    S->minmat_ok = true;
-  }
-  CUtensorMap mA_r, mB_r, mA_gu, mA_d, mM;
-  if ((rc = make_map(&mA_r, S->xa, T, Kx, kPM)) || (rc = make_map(&mB_r, S->r2, 256, d, kPN)) ||
-      (rc = make_map(&mA_gu, S->xg, rows, Kx, kPM)) || (rc = make_map(&mA_d, S->hg, rows, fe, kPM)) ||
-      (rc = make_map(&mM, S->minmat, (uint64_t)ne * 2 * fe, Km, 128)))
-    return rc;
+int prefill_kx(int d) { return d + ((d / 32 + 63) / 64) * 64; }
+int prefill_tile_rows() { return kPM; }
+
+static void set_attrs_once() {
   static std::once_flag attr_once;
   std::call_once(attr_once, [] {
     cudaFuncSetAttribute(prefill_gemm<P_ROUTER>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPSmem);
     cudaFuncSetAttribute(prefill_gemm<P_GATEUP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPSmem);
     cudaFuncSetAttribute(prefill_gemm<P_DOWN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPSmem);
   });
+}
+
+static PrefillParams base_params(const PrefillLayer& L, PrefillScratch* S, int T, int* d_err) {
   PrefillParams p;
   memset(&p, 0, sizeof(p));
   p.T = T;
-  p.d = d;
-  p.fe = fe;
-  p.ne = ne;
-  p.k = k;
+  p.d = L.d;
+  p.fe = L.fe;
+  p.ne = L.ne;
+  p.k = L.k;
   p.renorm = L.renorm;
-  p.Kx = Kx;
+  p.Kx = prefill_kx(L.d);
   p.exp_tab = L.exp_tab;
-  p.rb_gu = (uint32_t)(d / 256 * 144);
-  p.rb_d = (uint32_t)(fe / 256 * 210);
-  p.bias = bias;
+  p.rb_gu = (uint32_t)(L.d / 256 * 144);
+  p.rb_d = (uint32_t)(L.fe / 256 * 210);
   p.ids = S->ids;
   p.wts = S->wts;
   p.counts = S->counts;
@@ -863,16 +838,85 @@ int prefill_run(const PrefillLayer& L, PrefillScratch* S, const void* hb, float*
   p.wrow = S->wrow;
   p.y = S->y;
   p.err = d_err;
+  return p;
+}
 
+int prefill_prepare(const PrefillLayer& L, PrefillScratch* S, cudaStream_t st) {
+  const int d = L.d, fe = L.fe, ne = L.ne;
+  int rc;
+  if (!S->r2) {
+    if ((rc = grow((void**)&S->r2, &S->c_r2, (size_t)256 * d * 2))) return rc;
+    prefill_router_split<<<256, 256, 0, st>>>(L.router, (__half*)S->r2, ne, d);
+  }
+  const int Km = prefill_kx(d) - d;
+  if (!S->minmat_ok) {
+    // per layer, once (again after the expert pointers change): the min block
+    // and the repacked weight chunks the GEMMs stream, for the experts this
+    // handle computes (L.own; all when null)
+    const size_t n_gu = (size_t)ne * (fe / 128) * (d / kPK), n_dn = (size_t)ne * (d / kPN) * (fe / kPK);
+    if ((rc = grow((void**)&S->minmat, &S->c_minmat, (size_t)ne * 2 * fe * Km * 2)) ||
+        (rc = grow((void**)&S->gu_pack, &S->c_gu_pack, n_gu * kPRawGU)) ||
+        (rc = grow((void**)&S->dn_pack, &S->c_dn_pack, n_dn * kPRawDN)))
+      return rc;
+    prefill_minmat<<<ne * 2 * fe, 64, 0, st>>>(L.exp_tab, L.own, d, fe, Km, (uint32_t)(d / 256 * 144), S->minmat);
+    prefill_pack_gu<<<(unsigned)n_gu, kPN, 0, st>>>(L.exp_tab, L.own, d, fe, (uint32_t)(d / 256 * 144), S->gu_pack);
+    prefill_pack_dn<<<(unsigned)n_dn, kPN, 0, st>>>(L.exp_tab, L.own, d, fe, (uint32_t)(fe / 256 * 210), S->dn_pack);
+    S->minmat_ok = true;
+  }
+  return cuda_status(cudaGetLastError());
+}
+
+int prefill_route(const PrefillLayer& L, PrefillScratch* S, const void* hb, int T, const float* bias, int* d_err,
+                  int num_sms, cudaStream_t st) {
+  const int d = L.d, k = L.k, Kx = prefill_kx(d);
+  const size_t pairs = (size_t)T * k;
+  int rc;
+  if ((rc = grow((void**)&S->xa, &S->c_xa, (size_t)T * Kx * 2)) || (rc = grow((void**)&S->ids, &S->c_ids, pairs * 4)) ||
+      (rc = grow((void**)&S->wts, &S->c_wts, pairs * 4)) || (rc = grow((void**)&S->counts, &S->c_counts, 256 * 4)) ||
+      (rc = grow((void**)&S->cursor, &S->c_cursor, 256 * 4)) || (rc = grow((void**)&S->n_mtiles, &S->c_n_mtiles, 16)))
+    return rc;
+  if ((rc = prefill_prepare(L, S, st))) return rc;
+  CUtensorMap mA_r, mB_r;
+  if ((rc = make_map(&mA_r, S->xa, T, Kx, kPM)) || (rc = make_map(&mB_r, S->r2, 256, d, kPN))) return rc;
+  set_attrs_once();
+  PrefillParams p = base_params(L, S, T, d_err);
+  p.bias = bias;
   if (cudaMemsetAsync(S->counts, 0, 256 * 4, st) != cudaSuccess) return cuda_status(cudaGetLastError());
   prefill_prep<<<T, 256, 0, st>>>((const __nv_bfloat16*)hb, (__half*)S->xa, T, d, Kx);
-  // router
   p.nk = d / kPK;
   p.n_ntiles = 1;
   prefill_gemm<P_ROUTER><<<std::min(num_sms, (T + kPM - 1) / kPM), kPThreads, kPSmem, st>>>(mA_r, mB_r, p);
-  prefill_scan<<<1, 256, 0, st>>>(S->counts, ne, S->cursor, S->tiles, S->n_mtiles);
-  prefill_place<<<(unsigned)((pairs + 7) / 8), 256, 0, st>>>(S->ids, S->wts, (const __half*)S->xa, T, k, Kx,
-                                                              S->cursor, S->rowpos, S->wrow, (__half*)S->xg);
+  return cuda_status(cudaGetLastError());
+}
+
+size_t prefill_row_capacity(size_t pairs, int ne) { return ((pairs + (size_t)ne * (kPM - 1)) + kPM - 1) / kPM * kPM; }
+
+int prefill_grow_rows(const PrefillLayer& L, PrefillScratch* S, size_t rows) {
+  const int Kx = prefill_kx(L.d);
+  rows = std::max<size_t>(rows, kPM);
+  const size_t max_mtiles = rows / kPM + 1;
+  int rc;
+  if ((rc = grow((void**)&S->tiles, &S->c_tiles, max_mtiles * sizeof(PTile))) ||
+      (rc = grow((void**)&S->wrow, &S->c_wrow, rows * 4)) || (rc = grow((void**)&S->xg, &S->c_xg, rows * Kx * 2)) ||
+      (rc = grow((void**)&S->hg, &S->c_hg, rows * L.fe * 2)) || (rc = grow((void**)&S->y, &S->c_y, rows * L.d * 4)))
+    return rc;
+  return VIREO_OK;
+}
+
+void prefill_scan_launch(const int* counts, int ne, PrefillScratch* S, cudaStream_t st) {
+  prefill_scan<<<1, 256, 0, st>>>(counts, ne, S->cursor, S->tiles, S->n_mtiles);
+}
+
+int prefill_experts(const PrefillLayer& L, PrefillScratch* S, size_t rows, int* d_err, int num_sms, cudaStream_t st) {
+  const int d = L.d, fe = L.fe, ne = L.ne, Kx = prefill_kx(d), Km = Kx - d;
+  rows = std::max<size_t>(rows, kPM);
+  CUtensorMap mA_gu, mA_d, mM;
+  int rc;
+  if ((rc = make_map(&mA_gu, S->xg, rows, Kx, kPM)) || (rc = make_map(&mA_d, S->hg, rows, fe, kPM)) ||
+      (rc = make_map(&mM, S->minmat, (uint64_t)ne * 2 * fe, Km, 128)))
+    return rc;
+  set_attrs_once();
+  PrefillParams p = base_params(L, S, 0, d_err);
   // gate/up + SwiGLU
   p.nk = Kx / kPK;
   p.n_ntiles = fe / 128;
@@ -883,6 +927,20 @@ int prefill_run(const PrefillLayer& L, PrefillScratch* S, const void* hb, float*
   p.n_ntiles = d / kPN;
   p.pack = S->dn_pack;
   prefill_gemm<P_DOWN><<<num_sms, kPThreads, kPSmem, st>>>(mA_d, mA_d, p);
+  return cuda_status(cudaGetLastError());
+}
+
+int prefill_run(const PrefillLayer& L, PrefillScratch* S, const void* hb, float* x, int T, const float* bias,
+                int32_t* ids_out, float* wts_out, int* d_err, int num_sms, cudaStream_t st) {
+  const int d = L.d, ne = L.ne, k = L.k, Kx = prefill_kx(d);
+  const size_t pairs = (size_t)T * k, rows = prefill_row_capacity(pairs, ne);
+  int rc;
+  if ((rc = prefill_route(L, S, hb, T, bias, d_err, num_sms, st))) return rc;
+  if ((rc = grow((void**)&S->rowpos, &S->c_rowpos, pairs * 4)) || (rc = prefill_grow_rows(L, S, rows))) return rc;
+  prefill_scan_launch(S->counts, ne, S, st);
+  prefill_place<<<(unsigned)((pairs + 7) / 8), 256, 0, st>>>(S->ids, S->wts, (const __half*)S->xa, T, k, Kx,
+                                                              S->cursor, S->rowpos, S->wrow, (__half*)S->xg);
+  if ((rc = prefill_experts(L, S, rows, d_err, num_sms, st))) return rc;
   prefill_combine<<<T, 256, 0, st>>>(S->rowpos, S->y, x, T, k, d);
   if (ids_out && cudaMemcpyAsync(ids_out, S->ids, pairs * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
     return cuda_status(cudaGetLastError());

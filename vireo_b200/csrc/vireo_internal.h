@@ -48,6 +48,7 @@ struct PrefillLayer {
   int d, fe, ne, k, renorm;
   const float* router;             // [ne][d] fp32
   const uint8_t* const* exp_tab;   // device [ne][3]: gate, up, down
+  const int* own = nullptr;        // device [ne]: experts this handle computes (null = all)
 };
 struct PrefillScratch {
   __half* xa = nullptr;
@@ -74,6 +75,16 @@ int prefill_supported(int d, int fe, int ne, int k, uint32_t rt, uint32_t gt, ui
 int prefill_run(const PrefillLayer& L, PrefillScratch* S, const void* hb_bf16, float* x, int T, const float* bias,
                 int32_t* ids_out, float* wts_out, int* d_err, int num_sms, cudaStream_t st);
 void prefill_scratch_free(PrefillScratch* s);
+// pieces of prefill_run, shared with the expert-parallel path (ep.cu)
+int prefill_kx(int d);
+int prefill_prepare(const PrefillLayer& L, PrefillScratch* S, cudaStream_t st);
+int prefill_route(const PrefillLayer& L, PrefillScratch* S, const void* hb, int T, const float* bias, int* d_err,
+                  int num_sms, cudaStream_t st);
+size_t prefill_row_capacity(size_t pairs, int ne);
+int prefill_grow_rows(const PrefillLayer& L, PrefillScratch* S, size_t rows);
+void prefill_scan_launch(const int* counts, int ne, PrefillScratch* S, cudaStream_t st);
+int prefill_experts(const PrefillLayer& L, PrefillScratch* S, size_t rows, int* d_err, int num_sms, cudaStream_t st);
+int prefill_tile_rows();  // rows per activation tile (row ranges per expert are padded to it)
 
 // generic kernels (any supported type/shape), generic_kernels.cu
 int launch_dequant(uint32_t type, const void* src, float* dst, int n, cudaStream_t s);
