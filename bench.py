@@ -357,7 +357,8 @@ def run_prefill(args, wl):
     Q6_K down grouped GEMMs on the tcgen05 tensor cores, combine).  N GPUs:
     gguf_moe_prefill_ep, expert parallel: each rank routes 8192/N of the
     tokens, experts are placed on ranks by expected load (the router bias),
-    and the rows go to their experts' ranks and back as NCCL all-to-alls.
+    and the kernels store the rows into their experts' ranks and the outputs
+    back over NVLink peer memory.
     A step is the whole 8192-token batch (strong scaling)."""
     import ctypes as C
     import torch
@@ -395,8 +396,8 @@ def run_prefill(args, wl):
         owner = V.ep_place(np.exp(bias_np.astype(np.float64)), world)
         uid = [V.ep_unique_id() if rank == 0 else None]
         torch.distributed.broadcast_object_list(uid, src=0)
-        ep = V.MoeLayerEP(layer, owner, rank, world, uid[0], local)
-        fn, handle, sync, launches = L.gguf_moe_prefill_ep, ep.h, L.gguf_moe_ep_sync, 10
+        ep = V.MoeLayerEP(layer, owner, rank, world, uid[0], Tl, local)
+        fn, handle, sync, launches = L.gguf_moe_prefill_ep, ep.h, L.gguf_moe_ep_sync, 9
         what = "gguf_moe_prefill_ep"
     else:
         m = V.MoeLayer(layer, local)
@@ -478,7 +479,7 @@ def run_prefill(args, wl):
                              "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
                              "algorithmic_flops_per_step": PREFILL_FLOPS,
                              "kernel": "whole step per GPU (router, dispatch, gate/up, down, combine"
-                                       + (", all-to-alls)" if world > 1 else ")")},
+                                       + (", peer-memory dispatch and return)" if world > 1 else ")")},
                 "cpu_baseline": cpu,
                 "e2e": {"value": e2e_tps, "unit": "tok/s", "h2d_bytes_per_step": T * d * (2 + 4),
                         "d2h_bytes_per_step": T * d * 4,

@@ -122,11 +122,15 @@ void gguf_moe_destroy(gguf_moe *m);
 
 /* ---- Expert parallelism (no counterpart in the reference, which runs on one
  * host): the batched MoE FFN of gguf_moe_prefill spread over the GPUs of one
- * node, one process per GPU.  Each rank holds a slice of the tokens and the
- * experts placed on it (owner[e] == rank); the tokens' rows go to their
- * experts' ranks and the outputs come back, each as one NCCL all-to-all.  The
- * result on every rank is bit-identical to gguf_moe_prefill on one GPU over
- * the same tokens.  NCCL is loaded at run time (libnccl.so.2). */
+ * node, one process per GPU.  Each rank routes its own slice of the tokens
+ * and computes the experts placed on it (owner[e] == rank).  The kernels move
+ * the rows themselves over NVLink peer memory (CUDA IPC mappings of every
+ * rank's buffers): each (token, slot) row is stored straight into its
+ * expert's GEMM operand on the owning rank, and the down GEMM stores each
+ * output row straight back into the source rank's return buffer.  NCCL (run
+ * time loaded, libnccl.so.2) carries only the per-expert counts and two
+ * barriers per call.  The result on every rank is bit-identical to
+ * gguf_moe_prefill on one GPU over the same tokens. */
 typedef struct gguf_moe_ep gguf_moe_ep;
 
 /* An NCCL unique id (128 bytes) for gguf_moe_ep_create: rank 0 makes it and
@@ -138,30 +142,36 @@ int gguf_moe_ep_unique_id(void *id128);
  * n_experts / world experts.  owner: [n_experts] out. */
 int gguf_moe_ep_place(const double *expected_load, int n_experts, int world, int32_t *owner);
 
-/* Host only.  Offsets of one all-to-all: counts[src * world + dst] rows;
- * send_off / recv_off / recv_cnt: [world] out for `rank`; recv_total: out,
- * or NULL. */
-int gguf_moe_ep_offsets(const int32_t *counts, int world, int rank, int32_t *send_off, int32_t *recv_off,
-                        int32_t *recv_cnt, int32_t *recv_total);
+/* Host only.  Where `rank`'s rows land: counts[src * n_experts + e] = pairs
+ * rank src routes to expert e.  Each owner lays out its experts' row ranges
+ * in expert order, each range padded to the GEMM tile (128 rows), and within
+ * an expert's range the sources in rank order.  dst_off: [n_experts] out,
+ * the first row of `rank`'s pairs in expert e's range on owner[e];
+ * rows_here: out (or NULL), the rows `rank` receives. */
+int gguf_moe_ep_rows(const int32_t *counts, const int32_t *owner, int n_experts, int world, int rank,
+                     int32_t *dst_off, int32_t *rows_here);
 
-/* Collective (every rank calls it with the same id, owner and world; the
- * current CUDA device is this rank's GPU).  desc: the layer as for
- * gguf_moe_create; only the slices of the experts this rank owns are read.
- * Supported layers: those of gguf_moe_prefill. */
-int gguf_moe_ep_create(const gguf_moe_desc *desc, const int32_t *owner, int rank, int world, const void *id128,
-                       gguf_moe_ep **out);
+/* Collective (every rank calls it with the same id, owner, world and
+ * max_tokens; the current CUDA device is this rank's GPU; world <= 8).
+ * desc: the layer as for gguf_moe_create; only the slices of the experts
+ * this rank owns are read.  max_tokens: the most local tokens a call may
+ * pass (sizes the exchange buffers).  Supported layers: those of
+ * gguf_moe_prefill with n_experts <= 128. */
+int gguf_moe_ep_create(const gguf_moe_desc *desc, const int32_t *owner, int rank, int world, int max_tokens,
+                       const void *id128, gguf_moe_ep **out);
 
-/* Collective.  n_tok local tokens (may differ between ranks, may be 0):
- * arguments as gguf_moe_prefill, DEVICE pointers.  Reads the count matrix to
- * the host once per call (a bounded wait); device failures surface in
- * gguf_moe_ep_sync.  A peer that stops answering ends the call with
- * VIREO_ERR_TIMEOUT and leaves the handle unusable. */
+/* Collective.  n_tok local tokens (may differ between ranks, may be 0, at
+ * most max_tokens): arguments as gguf_moe_prefill, DEVICE pointers.
+ * Stream-ordered with no host synchronisation (the row layout is computed on
+ * the device from the all-gathered counts); device failures surface in
+ * gguf_moe_ep_sync, whose wait is bounded: a peer that stops answering ends
+ * it with VIREO_ERR_TIMEOUT and leaves the handle unusable. */
 int gguf_moe_prefill_ep(gguf_moe_ep *ep, const void *hb_bf16, float *x, int n_tok, const float *router_bias,
                         int32_t *ids, float *wts, void *stream);
 int gguf_moe_ep_sync(gguf_moe_ep *ep, void *stream);
 /* The rank's layer handle (owned by ep; valid until gguf_moe_ep_destroy). */
 gguf_moe *gguf_moe_ep_layer(gguf_moe_ep *ep);
-/* Collective (destroys the communicator). */
+/* Collective (unmaps the peers' buffers, destroys the communicator). */
 void gguf_moe_ep_destroy(gguf_moe_ep *ep);
 
 /* No counterpart in the reference: an extension for callers that may not

@@ -50,11 +50,11 @@ def _single_gpu(L, toks, x0, bias, device=0):
         m.close()
 
 
-def _ep_run(L, toks, x0, bias, owner, rank, world, uid, device):
+def _ep_run(L, toks, x0, bias, owner, rank, world, uid, device, max_tokens):
     import torch
     import vireo_b200 as V
     dev = torch.device("cuda", device)
-    ep = V.MoeLayerEP(L, owner, rank, world, uid, device)
+    ep = V.MoeLayerEP(L, owner, rank, world, uid, max_tokens, device)
     try:
         hb = torch.from_numpy(toks).to(dev).to(torch.bfloat16)
         x = torch.from_numpy(x0.copy()).to(dev)
@@ -81,7 +81,7 @@ def test_ep_world1_matches_single_gpu_bits():
     spec, L, toks, x0, bias = _case(71)
     ref = _single_gpu(L, toks, x0, bias)
     owner = np.zeros(spec.n_experts, dtype=np.int32)
-    outs = _ep_run(L, toks, x0, bias, owner, 0, 1, V.ep_unique_id(), 0)
+    outs = _ep_run(L, toks, x0, bias, owner, 0, 1, V.ep_unique_id(), 0, toks.shape[0])
     for x, ids, wts in outs:
         assert np.array_equal(ids, ref[1])
         assert np.array_equal(wts.view(np.uint32), ref[2].view(np.uint32))
@@ -116,8 +116,8 @@ def _rank_main(rank, world, tmp, split):
         uid = f.read()
     owner = V.ep_place(np.exp(bias.astype(np.float64)), world)
     lo, hi = split[rank], split[rank + 1]
-    outs = _ep_run(L, toks[lo:hi], x0[lo:hi], bias, owner, rank, world, uid, rank)
-    np.save(os.path.join(tmp, f"x{rank}.npy"), np.stack([o[0] for o in outs]) if hi > lo else np.zeros((2, 0, spec.dim)))
+    outs = _ep_run(L, toks[lo:hi], x0[lo:hi], bias, owner, rank, world, uid, rank, toks.shape[0])
+    np.save(os.path.join(tmp, f"x{rank}.npy"), np.stack([o[0] for o in outs]) if hi > lo else np.zeros((2, 0, spec.dim), dtype=np.float32))
     np.save(os.path.join(tmp, f"ids{rank}.npy"), outs[0][1])
 
 
@@ -127,7 +127,14 @@ def test_ep_world2_matches_single_gpu_bits(tmp_path, split):
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    mp.start_processes(_rank_main, args=(2, str(tmp_path), split), nprocs=2, join=True, start_method="spawn")
+    ctx = mp.start_processes(_rank_main, args=(2, str(tmp_path), split), nprocs=2, join=False, start_method="spawn")
+    deadline = time.time() + 180
+    while not ctx.join(timeout=5):
+        if time.time() > deadline:
+            for pr in ctx.processes:
+                if pr.is_alive():
+                    pr.terminate()
+            pytest.fail("expert-parallel ranks did not finish in 180 s")
     spec, L, toks, x0, bias = _case(72)
     ref = _single_gpu(L, toks, x0, bias)
     for r in range(2):

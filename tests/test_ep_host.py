@@ -1,13 +1,15 @@
 """Expert parallelism on the host, no GPU: the library's placement and
-all-to-all offset functions (gguf_moe_ep_place, gguf_moe_ep_offsets), and
-the expert-parallel dataflow of gguf_moe_prefill_ep run end to end as two
-gloo ranks on CPU with the CPU oracle as the expert math.
+row-layout functions (gguf_moe_ep_place, gguf_moe_ep_rows), and the
+expert-parallel dataflow of gguf_moe_prefill_ep run end to end as two gloo
+ranks on CPU with the CPU oracle as the expert math.
 
 The dataflow test follows the device path step by step: each rank routes its
-own tokens, sends every (token, slot) row to the rank that owns the slot's
-expert (counts all-gathered, offsets from gguf_moe_ep_offsets), the owner
-computes w * expert(x), the rows come back, and each token is combined in
-rank order.  The result must equal the single-process restatement of the
+own tokens and counts pairs per expert, the counts are all-gathered, every
+(token, slot) row goes to the row gguf_moe_ep_rows assigns it in its expert's
+range on the owning rank (gloo stands in for the peer stores), the owner
+finds each row's expert from that layout alone and computes w * expert(x),
+the rows return to (source rank, pair), and each token is combined in rank
+order.  The result must equal the single-process restatement of the
 reference's moe_ffn bit for bit (same float32 operations in the same order).
 """
 import datetime
@@ -46,19 +48,44 @@ def test_place_balances_load_and_counts():
         V.ep_place(np.ones(4), 0)
 
 
-def test_offsets_match_a_prefix_sum():
+def test_rows_layout_matches_the_owner_scan():
+    """dst_off from gguf_moe_ep_rows against the owner's layout written out
+    directly: experts in index order, each range padded to 128 rows, sources
+    in rank order inside a range."""
     import vireo_b200 as V
     rng = np.random.default_rng(5)
-    for world in (1, 2, 5, 8):
-        cnt = rng.integers(0, 50, size=(world, world)).astype(np.int32)
+    for world, ne in [(1, 8), (2, 16), (3, 10), (8, 128)]:
+        cnt = rng.integers(0, 300, size=(world, ne)).astype(np.int32)
+        cnt[:, rng.integers(0, ne)] = 0  # an expert nobody routes to
+        owner = V.ep_place(rng.exponential(size=ne), world)
+        base = {}
+        for q in range(world):
+            b = 0
+            for e in range(ne):
+                if owner[e] == q:
+                    base[e] = b
+                    b += -(-int(cnt[:, e].sum()) // 128) * 128
         for r in range(world):
-            so, ro, rc, tot = V.ep_offsets(cnt, r)
-            assert np.array_equal(so, np.concatenate([[0], np.cumsum(cnt[r])[:-1]]))
-            assert np.array_equal(rc, cnt[:, r])
-            assert np.array_equal(ro, np.concatenate([[0], np.cumsum(cnt[:, r])[:-1]]))
-            assert tot == cnt[:, r].sum()
+            off, here = V.ep_rows(cnt, owner, r)
+            for e in range(ne):
+                assert off[e] == base[e] + cnt[:r, e].sum(), (world, r, e)
+            assert here == sum(int(cnt[:, e].sum()) for e in range(ne) if owner[e] == r)
     with pytest.raises(V.VireoError):
-        V.ep_offsets(-np.ones((2, 2), dtype=np.int32), 0)
+        V.ep_rows(-np.ones((2, 4), dtype=np.int32), np.zeros(4, dtype=np.int32), 0)
+
+
+def off_rows(counts, owner, rank, e, row):
+    """True when `row` lies in expert e's range on its owner `rank` (the
+    layout gguf_moe_ep_rows describes)."""
+    b = 0
+    for e2 in range(counts.shape[1]):
+        if owner[e2] != rank:
+            continue
+        n = int(counts[:, e2].sum())
+        if e2 == e:
+            return b <= row < b + n
+        b += -(-n // 128) * 128
+    return False
 
 
 def _ep_rank(rank, world, port, seed, n_tok, out_dir):
@@ -83,43 +110,60 @@ def _ep_rank(rank, world, port, seed, n_tok, out_dir):
         T = mine.shape[0]
         # every rank places the experts the same way (a fixed synthetic load)
         owner = V.ep_place(np.arange(ne, 0, -1, dtype=np.float64) ** 1.5, world)
-        # route the local tokens
+        # route the local tokens; per expert, the local count and each pair's index
         _, ids, wts = P(mine)
-        dest = owner[ids.reshape(-1)]
-        sendcnt = np.bincount(dest, minlength=world).astype(np.int32)
-        allc = [torch.zeros(world, dtype=torch.int32) for _ in range(world)]
-        dist.all_gather(allc, torch.from_numpy(sendcnt))
-        counts = torch.stack(allc).numpy()
-        so, ro, rc, R = V.ep_offsets(counts, rank)
-        # dispatch rows: [hidden | expert | weight], grouped by destination in pair order
-        send = np.zeros((int(sendcnt.sum()), d + 2), dtype=np.float32)
+        flat = ids.reshape(-1)
         pos = np.zeros(T * k, dtype=np.int64)
-        fill = so.astype(np.int64).copy()
+        cnt = np.zeros(ne, dtype=np.int32)
         for p in range(T * k):
-            q = dest[p]
-            pos[p] = fill[q]
-            fill[q] += 1
-            send[pos[p], :d] = mine[p // k]
-            send[pos[p], d] = ids.reshape(-1)[p]
-            send[pos[p], d + 1] = wts.reshape(-1)[p]
-        recv = torch.zeros((R, d + 2), dtype=torch.float32)
-        dist.all_to_all_single(recv, torch.from_numpy(send), [int(c) for c in rc], [int(c) for c in sendcnt])
+            pos[p] = cnt[flat[p]]
+            cnt[flat[p]] += 1
+        allc = [torch.zeros(ne, dtype=torch.int32) for _ in range(world)]
+        dist.all_gather(allc, torch.from_numpy(cnt))
+        counts = torch.stack(allc).numpy()
+        off, here = V.ep_rows(counts, owner, rank)
+        # dispatch: each pair's row goes to row off[e] + pos of its expert's
+        # owner (the peer stores of the device path, carried here by gloo)
+        dest = owner[flat]
+        sendcnt = np.bincount(dest, minlength=world)
+        recvcnt = np.array([counts[q][owner == rank].sum() for q in range(world)])
+        order = np.argsort(dest, kind="stable")
+        send = np.zeros((T * k, d + 4), dtype=np.float32)  # [hidden | dest row | weight | pair | expert]
+        for j, p in enumerate(order):
+            send[j, :d] = mine[p // k]
+            send[j, d] = off[flat[p]] + pos[p]
+            send[j, d + 1] = wts.reshape(-1)[p]
+            send[j, d + 2] = p
+            send[j, d + 3] = flat[p]
+        recv = torch.zeros((int(recvcnt.sum()), d + 4), dtype=torch.float32)
+        dist.all_to_all_single(recv, torch.from_numpy(send), [int(c) for c in recvcnt], [int(c) for c in sendcnt])
         recv = recv.numpy()
-        # the experts held here: y = w * expert(x)
-        ysend = np.zeros((R, d), dtype=np.float32)
-        for i in range(R):
-            e = int(recv[i, d])
-            assert owner[e] == rank, (e, owner[e], rank)
-            ysend[i] = np.float32(recv[i, d + 1]) * P.expert(e, recv[i, :d])
-        yret = torch.zeros((send.shape[0], d), dtype=torch.float32)
-        dist.all_to_all_single(yret, torch.from_numpy(ysend), [int(c) for c in sendcnt], [int(c) for c in rc])
-        yret = yret.numpy()
+        # the owner's operand rows: every received row lands on its own row
+        rows = np.full((max(int(recv[:, d].max()) + 1 if len(recv) else 0, 1),), -1, dtype=np.int64)
+        for i in range(len(recv)):
+            assert rows[int(recv[i, d])] == -1  # no two pairs share a row
+            rows[int(recv[i, d])] = i
+        assert here == len(recv)
+        # the experts held here: y = w * expert(x), returned to (source rank, pair)
+        yback = np.zeros((len(recv), d), dtype=np.float32)
+        for i in range(len(recv)):
+            r0 = int(recv[i, d])
+            held = [e2 for e2 in range(ne) if owner[e2] == rank and off_rows(counts, owner, rank, e2, r0)]
+            assert held == [int(recv[i, d + 3])], (held, recv[i, d + 3])  # the layout alone names the expert
+            yback[i] = np.float32(recv[i, d + 1]) * P.expert(held[0], recv[i, :d])
+        ret = np.concatenate([yback, recv[:, d + 2:d + 3]], axis=1)
+        got = torch.zeros((T * k, d + 1), dtype=torch.float32)
+        dist.all_to_all_single(got, torch.from_numpy(ret), [int(c) for c in sendcnt], [int(c) for c in recvcnt])
+        got = got.numpy()
+        yret = np.zeros((T * k, d), dtype=np.float32)
+        for j in range(T * k):
+            yret[int(got[j, d])] = got[j, :d]
         # combine in rank order, then the residual add
         x = xm.copy()
         for t in range(T):
             acc = np.zeros(d, dtype=np.float32)
             for i in range(k):
-                acc = acc + yret[pos[t * k + i]]
+                acc = acc + yret[t * k + i]
             x[t] = x[t] + acc
         ref, _, _ = P(mine, xm)
         np.save(os.path.join(out_dir, f"rank{rank}.npy"), np.stack([x, ref]))

@@ -116,9 +116,8 @@ def lib():
         # expert parallelism (include/gguf_moe.h)
         L.gguf_moe_ep_unique_id.argtypes = [C.c_void_p]
         L.gguf_moe_ep_place.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p]
-        L.gguf_moe_ep_offsets.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
-                                          C.c_void_p]
-        L.gguf_moe_ep_create.argtypes = [C.POINTER(GgufMoeDesc), C.c_void_p, C.c_int, C.c_int, C.c_void_p,
+        L.gguf_moe_ep_rows.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+        L.gguf_moe_ep_create.argtypes = [C.POINTER(GgufMoeDesc), C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                          C.POINTER(C.c_void_p)]
         L.gguf_moe_prefill_ep.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
                                           C.c_void_p, C.c_void_p]
@@ -273,16 +272,17 @@ def ep_place(expected_load, world: int) -> np.ndarray:
     return owner
 
 
-def ep_offsets(counts, rank: int):
-    """gguf_moe_ep_offsets over a [world][world] count matrix (host only):
-    (send_off, recv_off, recv_cnt, recv_total)."""
+def ep_rows(counts, owner, rank: int):
+    """gguf_moe_ep_rows (host only): (dst_off [n_experts], rows_here) for
+    `rank` given the [world][n_experts] pair counts and the placement."""
     c = np.ascontiguousarray(counts, dtype=np.int32)
-    w = c.shape[0]
-    so, ro, rc = (np.zeros(w, dtype=np.int32) for _ in range(3))
-    tot = C.c_int32()
-    check(lib().gguf_moe_ep_offsets(c.ctypes.data, w, rank, so.ctypes.data, ro.ctypes.data, rc.ctypes.data,
-                                    C.byref(tot)), "gguf_moe_ep_offsets")
-    return so, ro, rc, int(tot.value)
+    o = np.ascontiguousarray(owner, dtype=np.int32)
+    world, ne = c.shape
+    off = np.zeros(ne, dtype=np.int32)
+    here = C.c_int32()
+    check(lib().gguf_moe_ep_rows(c.ctypes.data, o.ctypes.data, ne, world, rank, off.ctypes.data, C.byref(here)),
+          "gguf_moe_ep_rows")
+    return off, int(here.value)
 
 
 def ep_unique_id() -> bytes:
@@ -295,7 +295,7 @@ class MoeLayerEP:
     """One rank's share of an expert-parallel MoE layer (gguf_moe_ep_*).
     Every rank constructs it with the same owner table and unique id."""
 
-    def __init__(self, layer, owner, rank: int, world: int, uid: bytes, device: int = 0):
+    def __init__(self, layer, owner, rank: int, world: int, uid: bytes, max_tokens: int, device: int = 0):
         import torch
         s = layer.spec
         self.spec = s
@@ -309,8 +309,8 @@ class MoeLayerEP:
         self.owner = np.ascontiguousarray(owner, dtype=np.int32)
         buf = C.create_string_buffer(uid, 128)
         h = C.c_void_p()
-        check(lib().gguf_moe_ep_create(C.byref(self.desc), self.owner.ctypes.data, rank, world, buf, C.byref(h)),
-              "gguf_moe_ep_create")
+        check(lib().gguf_moe_ep_create(C.byref(self.desc), self.owner.ctypes.data, rank, world, max_tokens, buf,
+                                       C.byref(h)), "gguf_moe_ep_create")
         self.h = h
 
     def prefill(self, hb_bf16, x, bias=None, ids=None, wts=None, stream=None) -> None:

@@ -3,30 +3,44 @@
 // The reference has no batched path and no distribution at all (moe_ffn,
 // vireo src/gguf_run.c:185-214, runs one token at a time on the host).  This
 // file spreads the batched path of prefill.cu over G ranks, one process per
-// GPU: rank r holds its own slice of the tokens and computes the experts
-// placed on it; the tokens' rows travel to the experts and the expert outputs
-// travel back, each as one NCCL all-to-all over NVLink.
+// GPU: rank r routes its own slice of the tokens and computes the experts
+// placed on it.  The exchange is done by the kernels themselves over NVLink
+// peer memory (CUDA IPC mappings of every rank's buffers), not by a copy
+// collective:
 //
-// One call, rank r, T local tokens, k slots each (pairs = T k):
-//   route     prep + router GEMM + top-k on the local tokens (prefill.cu)
-//   count     pair -> owning rank of its expert; per-destination counts; an
-//             all-gather of the counts gives every rank the full [G][G]
-//             matrix (one host read per call: NCCL needs the sizes)
-//   dispatch  each pair's activation row (f16, Kx columns) with a 16-byte tail
-//             {expert, gate weight} is packed by destination and sent
-//   experts   received rows are grouped by (local) expert and run through the
-//             tcgen05 gate/up and down GEMMs of prefill.cu
-//   return    output rows go back to their source ranks in arrival order
-//   combine   x[t] += sum over rank order of the returned rows (the reference's
-//             combine order, gguf_run.c:209, 213)
-// Every output row is computed by the same GEMM arithmetic as on one GPU, and
-// the combine order is the same, so the result is bit-identical to
-// gguf_moe_prefill on one GPU.
+//   route     prep + router GEMM + top-k on the local tokens (prefill.cu);
+//             per expert, the local pair count and each pair's index in it
+//   count     all-gather of the [ne] counts (NCCL, 512 bytes per rank): every
+//             rank knows the [G][ne] matrix and computes from it, on the
+//             device, where each of its pairs lands in its expert's row range
+//             on the owning rank (the ranges are laid out as prefill_scan lays
+//             them out); no host synchronisation anywhere in a call
+//   dispatch  one warp per (token, slot) pair writes the token's activation
+//             row, the gate weight and the pair's origin straight into the
+//             owning rank's GEMM operand (peer stores), then a barrier
+//   experts   the owner runs the tcgen05 gate/up and down GEMMs of prefill.cu
+//             over its rows; the down GEMM's epilogue stores each output row
+//             into the SOURCE rank's return buffer over NVLink, tile by tile
+//             while the next tiles' MMAs run (one kernel: GEMM + return)
+//   combine   after a barrier, x[t] += sum over rank order of the returned
+//             rows (the reference's combine order, gguf_run.c:209, 213)
+// Every output row comes from the same GEMM arithmetic as on one GPU and the
+// combine order is the same, so the result is bit-identical to
+// gguf_moe_prefill on one GPU over the same tokens.
 //
-// NCCL is loaded at run time (dlopen of libnccl.so.2; in a process that has
-// already loaded it, e.g. through PyTorch, that copy is used).  Host-side
-// waits on the stream are bounded: a peer that stops answering ends the call
-// with VIREO_ERR_TIMEOUT and aborts the communicator.
+// Ordering across ranks: every rank's writes into a peer's buffers are
+// followed by a system-scope fence and the end of the kernel, then an NCCL
+// all-reduce of one word on the stream (the barrier); the peer reads only
+// after its own copy of that barrier.  A buffer a peer writes in call n + 1
+// was last read in call n before this rank's count all-gather of call n + 1,
+// which the writer waits for.
+//
+// NCCL (counts, barriers, IPC handle exchange) is loaded at run time (dlopen
+// of libnccl.so.2; in a process that already loaded it, e.g. through PyTorch,
+// that copy is used).  Host-side waits on the stream (gguf_moe_ep_sync, set-up)
+// are bounded: a peer that stops answering ends them with VIREO_ERR_TIMEOUT and aborts the
+// communicator.  Peer memory is only ever written with ordinary
+// loads and stores; no bulk or tensor copy engine touches it.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <dlfcn.h>
@@ -46,8 +60,9 @@
 
 namespace vireo {
 
-constexpr int kEpMaxWorld = 64;
-constexpr int kEpTailHalves = 8;  // 16-byte row tail: expert id, gate weight, 2 spare words
+constexpr int kEpMaxWorld = 8;    // one node
+constexpr int kEpMaxExperts = 128;
+constexpr int kEpMaxTopK = 8;    // the batched path's top-k limit
 constexpr double kEpWaitSeconds = 60.0;
 
 // ---- NCCL entry points, resolved once ---------------------------------------
@@ -57,11 +72,8 @@ struct NcclApi {
   decltype(&ncclCommDestroy) commDestroy = nullptr;
   decltype(&ncclCommAbort) commAbort = nullptr;
   decltype(&ncclCommGetAsyncError) getAsyncError = nullptr;
-  decltype(&ncclGroupStart) groupStart = nullptr;
-  decltype(&ncclGroupEnd) groupEnd = nullptr;
-  decltype(&ncclSend) send = nullptr;
-  decltype(&ncclRecv) recv = nullptr;
   decltype(&ncclAllGather) allGather = nullptr;
+  decltype(&ncclAllReduce) allReduce = nullptr;
   bool ok = false;
 };
 
@@ -78,116 +90,121 @@ static const NcclApi& nccl() {
     VIREO_NCCL_SYM(commDestroy, "ncclCommDestroy");
     VIREO_NCCL_SYM(commAbort, "ncclCommAbort");
     VIREO_NCCL_SYM(getAsyncError, "ncclCommGetAsyncError");
-    VIREO_NCCL_SYM(groupStart, "ncclGroupStart");
-    VIREO_NCCL_SYM(groupEnd, "ncclGroupEnd");
-    VIREO_NCCL_SYM(send, "ncclSend");
-    VIREO_NCCL_SYM(recv, "ncclRecv");
     VIREO_NCCL_SYM(allGather, "ncclAllGather");
+    VIREO_NCCL_SYM(allReduce, "ncclAllReduce");
 #undef VIREO_NCCL_SYM
     api.ok = api.getUniqueId && api.commInitRank && api.commDestroy && api.commAbort && api.getAsyncError &&
-             api.groupStart && api.groupEnd && api.send && api.recv && api.allGather;
+             api.allGather && api.allReduce;
   });
   return api;
 }
 
-struct EpOffsets {
-  int off[kEpMaxWorld];
+// where this rank's pairs go: every rank's operand buffers and, per expert,
+// the first row this rank's pairs take in that expert's range on its owner
+struct EpDispatch {
+  __half* xg[kEpMaxWorld];
+  float* wrow[kEpMaxWorld];
+  int* ysrc[kEpMaxWorld];
+  const int* dst_off;  // [ne], device (ep_layout)
+  int rows_cap;        // rows of every rank's operand buffers
 };
 
 // ---- kernels ------------------------------------------------------------------
-// pair -> destination rank and its index among that rank's rows
-__global__ void ep_route(const int32_t* ids, const int32_t* owner, int pairs, int* sendcnt, int* pdest, int* ppos) {
+// per expert: the local pair count and each pair's index among them
+__global__ void ep_count(const int32_t* ids, int pairs, int* cnt, int* pos) {
   const int p = blockIdx.x * blockDim.x + threadIdx.x;
   if (p >= pairs) return;
   const int e = ids[p];
-  int dst = -1, pos = -1;
-  if (e >= 0) {
-    dst = owner[e];
-    pos = atomicAdd(&sendcnt[dst], 1);
-  }
-  pdest[p] = dst;
-  ppos[p] = pos;
+  pos[p] = e >= 0 ? atomicAdd(&cnt[e], 1) : -1;
 }
 
-// dispatch rows: the token's activation row + {expert, weight} tail; one warp per pair
-__global__ void ep_pack(const __half* xa, const int32_t* ids, const float* wts, const int* pdest, const int* ppos,
-                        int pairs, int k, int Kx, const __grid_constant__ EpOffsets so, __half* sendbuf) {
-  const int p = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (p >= pairs) return;
-  const int dst = pdest[p];
-  if (dst < 0) return;
-  const int rs = Kx + kEpTailHalves;
-  __half* row = sendbuf + (size_t)(so.off[dst] + ppos[p]) * rs;
-  const uint4* s4 = reinterpret_cast<const uint4*>(xa + (size_t)(p / k) * Kx);
-  uint4* d4 = reinterpret_cast<uint4*>(row);
-  for (int i = lane; i < Kx / 8; i += 32) d4[i] = s4[i];
-  if (lane == 0) {
-    int32_t* tail = reinterpret_cast<int32_t*>(row + Kx);
-    tail[0] = ids[p];
-    tail[1] = __float_as_int(wts[p]);
-    tail[2] = 0;
-    tail[3] = 0;
-  }
-}
-
-// received rows per local expert; a row whose expert is not held here is
-// counted nowhere and flagged
-__global__ void ep_hist(const __half* recvbuf, int R, int Kx, int ne, const int* own, int* counts, int* err) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= R) return;
-  const int e = reinterpret_cast<const int32_t*>(recvbuf + (size_t)i * (Kx + kEpTailHalves) + Kx)[0];
-  if (e < 0 || e >= ne || !own[e]) {
-    atomicCAS(err, 0, VIREO_ERR_ARG);
-    return;
-  }
-  atomicAdd(&counts[e], 1);
-}
-
-// received row i -> a row of its expert's range (prefill_scan's cursors)
-__global__ void ep_place(const __half* recvbuf, int R, int Kx, int ne, const int* own, int* cursor, int* rrow,
-                         float* wrow, __half* xg) {
-  const int i = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (i >= R) return;
-  const __half* row = recvbuf + (size_t)i * (Kx + kEpTailHalves);
-  const int32_t* tail = reinterpret_cast<const int32_t*>(row + Kx);
-  const int e = tail[0];
-  int pos = -1;
-  if (lane == 0) {
-    if (e >= 0 && e < ne && own[e]) {
-      pos = atomicAdd(&cursor[e], 1);
-      wrow[pos] = __int_as_float(tail[1]);
+// The row layout of every owner (gguf_moe_ep_rows on the device): experts in
+// index order, each range padded to the GEMM tile, sources in rank order
+// inside a range.  dst_off[e]: the first row of this rank's pairs in expert
+// e's range on owner[e]; totals[e]: rows expert e receives if held here, else
+// 0 (the counts prefill_scan lays out).  One block, thread e per expert.
+__global__ void ep_layout(const int* cntall, const int32_t* owner, int G, int ne, int rank, int tile, int* dst_off,
+                          int* totals) {
+  __shared__ int tot[kEpMaxExperts], before[kEpMaxExperts];
+  const int e = threadIdx.x;
+  if (e < ne) {
+    int n = 0, b = 0;
+    for (int q = 0; q < G; q++) {
+      const int c = cntall[q * ne + e];
+      if (q < rank) b += c;
+      n += c;
     }
-    rrow[i] = pos;
+    tot[e] = n;
+    before[e] = b;
   }
-  pos = __shfl_sync(0xffffffffu, pos, 0);
-  if (pos < 0) return;
-  const uint4* s4 = reinterpret_cast<const uint4*>(row);
-  uint4* d4 = reinterpret_cast<uint4*>(xg + (size_t)pos * Kx);
-  for (int c = lane; c < Kx / 8; c += 32) d4[c] = s4[c];
+  __syncthreads();
+  if (e == 0) {
+    int next[kEpMaxWorld];
+    for (int q = 0; q < G; q++) next[q] = 0;
+    for (int i = 0; i < ne; i++) {
+      const int q = owner[i];
+      dst_off[i] = next[q] + before[i];
+      next[q] += (tot[i] + tile - 1) / tile * tile;
+      totals[i] = q == rank ? tot[i] : 0;
+    }
+  }
 }
 
-// output rows in arrival order (the order their sources expect them back)
-__global__ void ep_gather(const float* y, const int* rrow, int R, int d, float* ysend) {
-  const int i = blockIdx.x;
-  if (i >= R) return;
-  const int r = rrow[i];
-  const float4* s = reinterpret_cast<const float4*>(y + (size_t)(r < 0 ? 0 : r) * d);
-  float4* o = reinterpret_cast<float4*>(ysend + (size_t)i * d);
-  for (int c = threadIdx.x; c < d / 4; c += blockDim.x) o[c] = r < 0 ? make_float4(0.f, 0.f, 0.f, 0.f) : s[c];
+// one warp per (token, slot) pair: the token's activation row, the gate
+// weight and the pair's origin, stored into the owner's operand buffers
+__global__ void ep_dispatch(const __half* xa, const int32_t* ids, const float* wts, const int32_t* owner,
+                            const int* pos, int pairs, int k, int Kx, int rank, const __grid_constant__ EpDispatch D,
+                            int* err) {
+  const int p = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (p < pairs) {
+    const int e = ids[p];
+    const int q = e >= 0 ? owner[e] : 0, row = e >= 0 ? D.dst_off[e] + pos[p] : -1;
+    if (e >= 0 && row >= D.rows_cap) {
+      if (lane == 0) atomicCAS(err, 0, VIREO_ERR_ARG);  // inconsistent counts: never write past a buffer
+    } else if (e >= 0) {
+      const uint4* s4 = reinterpret_cast<const uint4*>(xa + (size_t)(p / k) * Kx);
+      uint4* d4 = reinterpret_cast<uint4*>(D.xg[q] + (size_t)row * Kx);
+      for (int i = lane; i < Kx / 8; i += 32) d4[i] = s4[i];
+      if (lane == 0) {
+        D.wrow[q][row] = wts[p];
+        D.ysrc[q][row] = (rank << 24) | p;
+      }
+    }
+  }
+  __threadfence_system();
 }
 
-// x[t] += sum over rank order of the returned rows (prefill_combine's order)
-__global__ void ep_combine(const int* pdest, const int* ppos, const __grid_constant__ EpOffsets so, const float* yret,
-                           float* x, int T, int k, int d) {
+// x[t] += sum over rank order of the returned rows (prefill_combine's order),
+// four columns per thread; the slots' loads are issued together
+__global__ void ep_combine(const int32_t* ids, const float* yret, float* x, int T, int k, int d) {
   const int t = blockIdx.x;
   if (t >= T) return;
-  for (int c = threadIdx.x; c < d; c += blockDim.x) {
-    float acc = 0.f;
-    for (int i = 0; i < k; i++) {
-      const int dst = pdest[(size_t)t * k + i];
-      if (dst >= 0) acc = __fadd_rn(acc, yret[(size_t)(so.off[dst] + ppos[(size_t)t * k + i]) * d + c]);
-    }
-    x[(size_t)t * d + c] = __fadd_rn(x[(size_t)t * d + c], acc);
+  bool on[kEpMaxTopK];
+#pragma unroll
+  for (int i = 0; i < kEpMaxTopK; i++) on[i] = i < k && ids[(size_t)t * k + i] >= 0;
+  const int d4 = d / 4;
+  const float4* y4 = reinterpret_cast<const float4*>(yret) + (size_t)t * k * d4;
+  float4* x4 = reinterpret_cast<float4*>(x) + (size_t)t * d4;
+  for (int c = threadIdx.x; c < d4; c += blockDim.x) {
+    float4 v[kEpMaxTopK];
+#pragma unroll
+    for (int i = 0; i < kEpMaxTopK; i++)
+      if (on[i]) v[i] = __ldcs(y4 + (size_t)i * d4 + c);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < kEpMaxTopK; i++)
+      if (on[i]) {
+        acc.x = __fadd_rn(acc.x, v[i].x);
+        acc.y = __fadd_rn(acc.y, v[i].y);
+        acc.z = __fadd_rn(acc.z, v[i].z);
+        acc.w = __fadd_rn(acc.w, v[i].w);
+      }
+    float4 xv = x4[c];
+    xv.x = __fadd_rn(xv.x, acc.x);
+    xv.y = __fadd_rn(xv.y, acc.y);
+    xv.z = __fadd_rn(xv.z, acc.z);
+    xv.w = __fadd_rn(xv.w, acc.w);
+    x4[c] = xv;
   }
 }
 
@@ -197,39 +214,31 @@ using namespace vireo;
 
 struct gguf_moe_ep {
   gguf_moe* m = nullptr;
-  int rank = 0, world = 1, device = 0;
+  int rank = 0, world = 1, max_tok = 0, ne = 0;
   ncclComm_t comm = nullptr;
   bool broken = false;
   std::vector<int32_t> owner;
   int32_t* d_owner = nullptr;
   int* d_own = nullptr;
-  int* d_sendcnt = nullptr;  // [world]
-  int* d_cntmat = nullptr;   // [world][world], row = source rank
-  int* h_cntmat = nullptr;   // pinned
-  int* d_rcounts = nullptr;  // [ne] received rows per expert
-  int* d_pdest = nullptr;
-  int* d_ppos = nullptr;
-  int* d_rrow = nullptr;
-  __half* sendbuf = nullptr;
-  __half* recvbuf = nullptr;
-  float* ysend = nullptr;
-  float* yret = nullptr;
-  size_t c_pairs = 0, c_recv = 0;
+  int* d_cnt = nullptr;     // [ne] local pairs per expert
+  int* d_cntall = nullptr;  // [G][ne]
+  int* d_totals = nullptr;  // [ne]
+  int* d_dstoff = nullptr;  // [ne]
+  int* d_pos = nullptr;     // [max_tok * k]
+  int* d_bar = nullptr;     // barrier word
+  // this rank's exported buffers (peers write them)
+  size_t rows_cap = 0;
+  __half* xg = nullptr;     // [rows_cap][Kx]
+  float* wrow = nullptr;    // [rows_cap]
+  int* ysrc = nullptr;      // [rows_cap]
+  float* yret = nullptr;    // [max_tok * k][d]
+  // every rank's buffers as mapped here (own entry = the local pointer)
+  __half* p_xg[kEpMaxWorld] = {};
+  float* p_wrow[kEpMaxWorld] = {};
+  int* p_ysrc[kEpMaxWorld] = {};
+  float* p_yret[kEpMaxWorld] = {};
+  bool mapped[kEpMaxWorld] = {};
 };
-
-static int ep_grow(void** p, size_t* cap, size_t n, size_t bytes_each) {
-  n = std::max<size_t>(n, 1);
-  if (*p && *cap >= n) return VIREO_OK;
-  if (*p) cudaFree(*p);
-  *p = nullptr;
-  *cap = 0;
-  if (cudaMalloc(p, n * bytes_each) != cudaSuccess) {
-    cudaGetLastError();
-    return VIREO_ERR_NOMEM;
-  }
-  *cap = n;
-  return VIREO_OK;
-}
 
 static double now_s() {
   timespec ts;
@@ -237,31 +246,41 @@ static double now_s() {
   return ts.tv_sec + 1e-9 * ts.tv_nsec;
 }
 
+static void ep_abort(gguf_moe_ep* ep) {
+  if (ep->comm) nccl().commAbort(ep->comm);
+  ep->comm = nullptr;
+  ep->broken = true;
+}
+
 // Waits for the stream with a wall-clock bound, watching the communicator
-// for asynchronous errors; on either failure the communicator is aborted.
+// for asynchronous errors; on any failure the communicator is aborted.
 static int ep_wait(gguf_moe_ep* ep, cudaStream_t s) {
   const NcclApi& N = nccl();
   const double t0 = now_s();
   for (;;) {
     cudaError_t e = cudaStreamQuery(s);
     if (e == cudaSuccess) return VIREO_OK;
-    if (e != cudaErrorNotReady) return cuda_status(e);
+    if (e != cudaErrorNotReady) {
+      ep_abort(ep);
+      return cuda_status(e);
+    }
     ncclResult_t ae = ncclSuccess;
     if (N.getAsyncError(ep->comm, &ae) != ncclSuccess || (ae != ncclSuccess && ae != ncclInProgress)) {
-      N.commAbort(ep->comm);
-      ep->comm = nullptr;
-      ep->broken = true;
+      ep_abort(ep);
       return VIREO_ERR_CUDA;
     }
     if (now_s() - t0 > kEpWaitSeconds) {
-      N.commAbort(ep->comm);
-      ep->comm = nullptr;
-      ep->broken = true;
+      ep_abort(ep);
       return VIREO_ERR_TIMEOUT;
     }
     struct timespec ts = {0, 20000};
     nanosleep(&ts, nullptr);
   }
+}
+
+static int ep_barrier(gguf_moe_ep* ep, cudaStream_t s) {
+  return nccl().allReduce(ep->d_bar, ep->d_bar, 1, ncclInt32, ncclSum, ep->comm, s) == ncclSuccess ? VIREO_OK
+                                                                                                   : VIREO_ERR_CUDA;
 }
 
 extern "C" {
@@ -277,7 +296,7 @@ int gguf_moe_ep_unique_id(void* id128) {
 }
 
 int gguf_moe_ep_place(const double* expected_load, int n_experts, int world, int32_t* owner) {
-  if (!expected_load || !owner || n_experts < 1 || world < 1 || world > kEpMaxWorld) return VIREO_ERR_ARG;
+  if (!expected_load || !owner || n_experts < 1 || world < 1 || world > 64) return VIREO_ERR_ARG;
   // heaviest expert first onto the least-loaded rank that still has room;
   // every rank holds ceil or floor of n_experts / world experts
   std::vector<int> order(n_experts);
@@ -302,37 +321,47 @@ int gguf_moe_ep_place(const double* expected_load, int n_experts, int world, int
   return VIREO_OK;
 }
 
-int gguf_moe_ep_offsets(const int32_t* counts, int world, int rank, int32_t* send_off, int32_t* recv_off,
-                        int32_t* recv_cnt, int32_t* recv_total) {
-  if (!counts || world < 1 || world > kEpMaxWorld || rank < 0 || rank >= world || !send_off || !recv_off ||
-      !recv_cnt)
+int gguf_moe_ep_rows(const int32_t* counts, const int32_t* owner, int n_experts, int world, int rank,
+                     int32_t* dst_off, int32_t* rows_here) {
+  if (!counts || !owner || !dst_off || n_experts < 1 || world < 1 || world > 64 || rank < 0 || rank >= world)
     return VIREO_ERR_ARG;
-  int64_t so = 0, ro = 0;
-  for (int q = 0; q < world; q++) {
-    const int32_t sc = counts[(size_t)rank * world + q], rc = counts[(size_t)q * world + rank];
-    if (sc < 0 || rc < 0) return VIREO_ERR_ARG;
-    send_off[q] = (int32_t)so;
-    recv_off[q] = (int32_t)ro;
-    recv_cnt[q] = rc;
-    so += sc;
-    ro += rc;
+  const int tile = prefill_tile_rows();
+  std::vector<int64_t> next(world, 0);  // running base of each owner's ranges
+  int64_t here = 0;
+  for (int e = 0; e < n_experts; e++) {
+    const int q = owner[e];
+    if (q < 0 || q >= world) return VIREO_ERR_ARG;
+    int64_t total = 0, before = 0;
+    for (int s = 0; s < world; s++) {
+      const int32_t c = counts[(size_t)s * n_experts + e];
+      if (c < 0) return VIREO_ERR_ARG;
+      if (s < rank) before += c;
+      total += c;
+    }
+    dst_off[e] = (int32_t)(next[q] + before);
+    next[q] += (total + tile - 1) / tile * tile;
+    if (q == rank) here += total;
   }
-  if (so > INT32_MAX || ro > INT32_MAX) return VIREO_ERR_ARG;
-  if (recv_total) *recv_total = (int32_t)ro;
+  for (int q = 0; q < world; q++)
+    if (next[q] > INT32_MAX) return VIREO_ERR_ARG;
+  if (rows_here) *rows_here = (int32_t)here;
   return VIREO_OK;
 }
 
 void gguf_moe_ep_destroy(gguf_moe_ep* ep);
 
-int gguf_moe_ep_create(const gguf_moe_desc* desc, const int32_t* owner, int rank, int world, const void* id128,
-                       gguf_moe_ep** out) {
-  if (!desc || !owner || !id128 || !out || world < 1 || world > kEpMaxWorld || rank < 0 || rank >= world)
+int gguf_moe_ep_create(const gguf_moe_desc* desc, const int32_t* owner, int rank, int world, int max_tokens,
+                       const void* id128, gguf_moe_ep** out) {
+  if (!desc || !owner || !id128 || !out || world < 1 || world > kEpMaxWorld || rank < 0 || rank >= world ||
+      max_tokens < 1)
     return VIREO_ERR_ARG;
   *out = nullptr;
-  const int ne = desc->n_experts;
-  if (!prefill_supported(desc->dim, desc->ffn_exp, ne, desc->n_used, desc->router_type, desc->gate_type,
-                         desc->up_type, desc->down_type))
+  const int ne = desc->n_experts, k = desc->n_used, d = desc->dim;
+  if (!prefill_supported(d, desc->ffn_exp, ne, k, desc->router_type, desc->gate_type, desc->up_type,
+                         desc->down_type) ||
+      ne > kEpMaxExperts)
     return VIREO_ERR_UNSUPPORTED;
+  if ((int64_t)max_tokens * k >= (1 << 24)) return VIREO_ERR_ARG;  // pair ids travel in 24 bits
   for (int e = 0; e < ne; e++)
     if (owner[e] < 0 || owner[e] >= world) return VIREO_ERR_ARG;
   const NcclApi& N = nccl();
@@ -340,20 +369,30 @@ int gguf_moe_ep_create(const gguf_moe_desc* desc, const int32_t* owner, int rank
   gguf_moe_ep* ep = new gguf_moe_ep();
   ep->rank = rank;
   ep->world = world;
+  ep->max_tok = max_tokens;
+  ep->ne = ne;
   ep->owner.assign(owner, owner + ne);
   int st;
   if ((st = gguf_moe_create(desc, &ep->m))) {
     delete ep;
     return st;
   }
-  cudaGetDevice(&ep->device);
   std::vector<int> own(ne);
   for (int e = 0; e < ne; e++) own[e] = owner[e] == rank;
+  const int Kx = prefill_kx(d);
+  const size_t pairs_cap = (size_t)max_tokens * k;
+  // the most rows any rank can receive: every pair of every rank
+  ep->rows_cap = prefill_row_capacity(pairs_cap * world, ne);
   if ((st = cuda_status(cudaMalloc(&ep->d_owner, ne * 4))) || (st = cuda_status(cudaMalloc(&ep->d_own, ne * 4))) ||
-      (st = cuda_status(cudaMalloc(&ep->d_sendcnt, kEpMaxWorld * 4))) ||
-      (st = cuda_status(cudaMalloc(&ep->d_cntmat, kEpMaxWorld * kEpMaxWorld * 4))) ||
-      (st = cuda_status(cudaMalloc(&ep->d_rcounts, 256 * 4))) ||
-      (st = cuda_status(cudaMallocHost(&ep->h_cntmat, kEpMaxWorld * kEpMaxWorld * 4))) ||
+      (st = cuda_status(cudaMalloc(&ep->d_cnt, ne * 4))) ||
+      (st = cuda_status(cudaMalloc(&ep->d_cntall, (size_t)world * ne * 4))) ||
+      (st = cuda_status(cudaMalloc(&ep->d_totals, ne * 4))) || (st = cuda_status(cudaMalloc(&ep->d_dstoff, ne * 4))) ||
+      (st = cuda_status(cudaMalloc(&ep->d_pos, pairs_cap * 4))) || (st = cuda_status(cudaMalloc(&ep->d_bar, 16))) ||
+      (st = cuda_status(cudaMalloc(&ep->xg, ep->rows_cap * Kx * 2))) ||
+      (st = cuda_status(cudaMalloc(&ep->wrow, ep->rows_cap * 4))) ||
+      (st = cuda_status(cudaMalloc(&ep->ysrc, ep->rows_cap * 4))) ||
+      (st = cuda_status(cudaMalloc(&ep->yret, pairs_cap * d * 4))) ||
+      (st = cuda_status(cudaMemset(ep->d_bar, 0, 16))) ||
       (st = cuda_status(cudaMemcpy(ep->d_owner, owner, ne * 4, cudaMemcpyHostToDevice))) ||
       (st = cuda_status(cudaMemcpy(ep->d_own, own.data(), ne * 4, cudaMemcpyHostToDevice)))) {
     gguf_moe_ep_destroy(ep);
@@ -366,6 +405,58 @@ int gguf_moe_ep_create(const gguf_moe_desc* desc, const int32_t* owner, int rank
     gguf_moe_ep_destroy(ep);
     return VIREO_ERR_CUDA;
   }
+  // exchange the IPC handles of the four exported buffers, with max_tokens:
+  // every rank must size its buffers alike (a peer writes up to its own
+  // max_tokens * n_used rows into them)
+  struct {
+    cudaIpcMemHandle_t h[4];
+    int64_t max_tok, pad;
+  } mine;
+  static_assert(sizeof(mine) % 16 == 0, "exchange record");
+  mine.max_tok = max_tokens;
+  mine.pad = 0;
+  void* bufs[4] = {ep->xg, ep->wrow, ep->ysrc, ep->yret};
+  for (int i = 0; i < 4; i++)
+    if ((st = cuda_status(cudaIpcGetMemHandle(&mine.h[i], bufs[i])))) {
+      gguf_moe_ep_destroy(ep);
+      return st;
+    }
+  std::vector<decltype(mine)> all((size_t)world);
+  void *d_mine = nullptr, *d_all = nullptr;
+  cudaStream_t s0 = nullptr;
+  st = cuda_status(cudaStreamCreateWithFlags(&s0, cudaStreamNonBlocking));
+  if (!st) st = cuda_status(cudaMalloc(&d_mine, sizeof(mine)));
+  if (!st) st = cuda_status(cudaMalloc(&d_all, sizeof(mine) * world));
+  if (!st) st = cuda_status(cudaMemcpy(d_mine, &mine, sizeof(mine), cudaMemcpyHostToDevice));
+  if (!st && N.allGather(d_mine, d_all, sizeof(mine), ncclUint8, ep->comm, s0) != ncclSuccess) st = VIREO_ERR_CUDA;
+  if (!st) st = ep_wait(ep, s0);
+  if (!st) st = cuda_status(cudaMemcpy(all.data(), d_all, sizeof(mine) * world, cudaMemcpyDeviceToHost));
+  if (d_mine) cudaFree(d_mine);
+  if (d_all) cudaFree(d_all);
+  if (s0) cudaStreamDestroy(s0);
+  for (int q = 0; q < world && !st; q++)
+    if (all[q].max_tok != max_tokens) st = VIREO_ERR_ARG;
+  for (int q = 0; q < world && !st; q++) {
+    if (q == rank) {
+      ep->p_xg[q] = ep->xg;
+      ep->p_wrow[q] = ep->wrow;
+      ep->p_ysrc[q] = ep->ysrc;
+      ep->p_yret[q] = ep->yret;
+      continue;
+    }
+    void* ptr[4] = {};
+    for (int i = 0; i < 4 && !st; i++)
+      st = cuda_status(cudaIpcOpenMemHandle(&ptr[i], all[q].h[i], cudaIpcMemLazyEnablePeerAccess));
+    ep->p_xg[q] = (__half*)ptr[0];
+    ep->p_wrow[q] = (float*)ptr[1];
+    ep->p_ysrc[q] = (int*)ptr[2];
+    ep->p_yret[q] = (float*)ptr[3];
+    ep->mapped[q] = true;
+  }
+  if (st) {
+    gguf_moe_ep_destroy(ep);
+    return st;
+  }
   *out = ep;
   return VIREO_OK;
 }
@@ -374,6 +465,7 @@ int gguf_moe_prefill_ep(gguf_moe_ep* ep, const void* hb_bf16, float* x, int n_to
                         int32_t* ids_out, float* wts_out, void* stream) {
   if (!ep || n_tok < 0 || (n_tok && (!hb_bf16 || !x))) return VIREO_ERR_ARG;
   if (ep->broken || !ep->comm) return VIREO_ERR_CUDA;
+  if (n_tok > ep->max_tok) return VIREO_ERR_ARG;
   if (((uintptr_t)hb_bf16 | (uintptr_t)x) % 16) return VIREO_ERR_ARG;
   MoeView v;
   int rc;
@@ -382,7 +474,7 @@ int gguf_moe_prefill_ep(gguf_moe_ep* ep, const void* hb_bf16, float* x, int n_to
   const NcclApi& N = nccl();
   cudaStream_t s = stream ? (cudaStream_t)stream : v.stream;
   const int G = ep->world, r = ep->rank, d = D.dim, k = D.n_used, ne = D.n_experts;
-  const int Kx = prefill_kx(d), rs = Kx + kEpTailHalves;
+  const int Kx = prefill_kx(d);
   const size_t pairs = (size_t)n_tok * k;
   PrefillLayer L;
   L.d = d;
@@ -395,80 +487,42 @@ int gguf_moe_prefill_ep(gguf_moe_ep* ep, const void* hb_bf16, float* x, int n_to
   L.own = ep->d_own;
   PrefillScratch* S = v.pre;
 
-  if (ep->c_pairs < pairs || !ep->d_pdest) {
-    size_t c = 0;
-    for (void** p : {(void**)&ep->d_pdest, (void**)&ep->d_ppos, (void**)&ep->sendbuf, (void**)&ep->yret})
-      if (*p) cudaFree(*p), *p = nullptr;
-    ep->c_pairs = 0;
-    if ((rc = ep_grow((void**)&ep->d_pdest, &c, pairs, 4)) || (rc = ep_grow((void**)&ep->d_ppos, &c, pairs, 4)) ||
-        (rc = ep_grow((void**)&ep->sendbuf, &c, pairs, (size_t)rs * 2)) ||
-        (rc = ep_grow((void**)&ep->yret, &c, pairs, (size_t)d * 4)))
-      return rc;
-    ep->c_pairs = std::max<size_t>(pairs, 1);
-  }
-  // route the local tokens (this handle's router; only its own experts are packed)
+  // route the local tokens (only this rank's experts are packed)
   if (n_tok > 0 && (rc = prefill_route(L, S, hb_bf16, n_tok, router_bias, v.err, v.num_sms, s))) return rc;
   if (n_tok == 0 && (rc = prefill_prepare(L, S, s))) return rc;
-  if ((rc = cuda_status(cudaMemsetAsync(ep->d_sendcnt, 0, G * 4, s)))) return rc;
-  if (pairs) ep_route<<<(unsigned)((pairs + 255) / 256), 256, 0, s>>>(S->ids, ep->d_owner, (int)pairs, ep->d_sendcnt,
-                                                                      ep->d_pdest, ep->d_ppos);
-  // the [G][G] count matrix on every rank, then on the host
-  if (N.allGather(ep->d_sendcnt, ep->d_cntmat, (size_t)G, ncclInt32, ep->comm, s) != ncclSuccess) return VIREO_ERR_CUDA;
-  if ((rc = cuda_status(cudaMemcpyAsync(ep->h_cntmat, ep->d_cntmat, (size_t)G * G * 4, cudaMemcpyDeviceToHost, s))) ||
-      (rc = ep_wait(ep, s)))
-    return rc;
-  int32_t soff[kEpMaxWorld], roff[kEpMaxWorld], rcnt[kEpMaxWorld], R = 0;
-  if ((rc = gguf_moe_ep_offsets(ep->h_cntmat, G, r, soff, roff, rcnt, &R))) return rc;
-  EpOffsets so;
-  memset(&so, 0, sizeof(so));
-  for (int q = 0; q < G; q++) so.off[q] = soff[q];
-  // receive side buffers and the GEMM rows
-  if (ep->c_recv < (size_t)R || !ep->recvbuf) {
-    size_t c = 0;
-    for (void** p : {(void**)&ep->recvbuf, (void**)&ep->ysend, (void**)&ep->d_rrow})
-      if (*p) cudaFree(*p), *p = nullptr;
-    ep->c_recv = 0;
-    if ((rc = ep_grow((void**)&ep->recvbuf, &c, R, (size_t)rs * 2)) ||
-        (rc = ep_grow((void**)&ep->ysend, &c, R, (size_t)d * 4)) || (rc = ep_grow((void**)&ep->d_rrow, &c, R, 4)))
-      return rc;
-    ep->c_recv = std::max<size_t>(R, 1);
+  if ((rc = cuda_status(cudaMemsetAsync(ep->d_cnt, 0, ne * 4, s)))) return rc;
+  if (pairs) ep_count<<<(unsigned)((pairs + 255) / 256), 256, 0, s>>>(S->ids, (int)pairs, ep->d_cnt, ep->d_pos);
+  // the [G][ne] count matrix on every rank; the row layout from it, on the device
+  if (N.allGather(ep->d_cnt, ep->d_cntall, (size_t)ne, ncclInt32, ep->comm, s) != ncclSuccess) return VIREO_ERR_CUDA;
+  ep_layout<<<1, kEpMaxExperts, 0, s>>>(ep->d_cntall, ep->d_owner, G, ne, r, prefill_tile_rows(), ep->d_dstoff,
+                                        ep->d_totals);
+  EpDispatch Dp;
+  memset(&Dp, 0, sizeof(Dp));
+  for (int q = 0; q < G; q++) {
+    Dp.xg[q] = ep->p_xg[q];
+    Dp.wrow[q] = ep->p_wrow[q];
+    Dp.ysrc[q] = ep->p_ysrc[q];
   }
-  const size_t rows = prefill_row_capacity((size_t)R, ne);
-  if ((rc = prefill_grow_rows(L, S, rows))) return rc;
-  // dispatch
+  Dp.dst_off = ep->d_dstoff;
+  Dp.rows_cap = (int)ep->rows_cap;
+  // the GEMMs of this rank run on the exported operand buffers, sized for the
+  // most rows any call can bring (no host read of the counts)
+  S->xg = ep->xg;
+  S->wrow = ep->wrow;
+  S->c_xg = ep->rows_cap * Kx * 2;
+  S->c_wrow = ep->rows_cap * 4;
+  const size_t rows = ep->rows_cap;
+  if ((rc = prefill_grow_rows(L, S, rows, false))) return rc;  // outputs go to the sources, not S->y
+  // dispatch straight into the owners' operands, then every rank's rows are in place
   if (pairs)
-    ep_pack<<<(unsigned)((pairs + 7) / 8), 256, 0, s>>>(S->xa, S->ids, S->wts, ep->d_pdest, ep->d_ppos, (int)pairs, k,
-                                                        Kx, so, ep->sendbuf);
-  const size_t rb = (size_t)rs * 2;
-  if (N.groupStart() != ncclSuccess) return VIREO_ERR_CUDA;
-  for (int q = 0; q < G; q++) {
-    const int sc = ep->h_cntmat[r * G + q];
-    if (sc > 0 && N.send((const uint8_t*)ep->sendbuf + soff[q] * rb, sc * rb, ncclUint8, q, ep->comm, s) != ncclSuccess)
-      return N.groupEnd(), VIREO_ERR_CUDA;
-    if (rcnt[q] > 0 && N.recv((uint8_t*)ep->recvbuf + roff[q] * rb, rcnt[q] * rb, ncclUint8, q, ep->comm, s) != ncclSuccess)
-      return N.groupEnd(), VIREO_ERR_CUDA;
-  }
-  if (N.groupEnd() != ncclSuccess) return VIREO_ERR_CUDA;
-  // experts held here
-  if ((rc = cuda_status(cudaMemsetAsync(ep->d_rcounts, 0, 256 * 4, s)))) return rc;
-  if (R > 0) ep_hist<<<(R + 255) / 256, 256, 0, s>>>(ep->recvbuf, R, Kx, ne, ep->d_own, ep->d_rcounts, v.err);
-  prefill_scan_launch(ep->d_rcounts, ne, S, s);
-  if (R > 0)
-    ep_place<<<(R + 7) / 8, 256, 0, s>>>(ep->recvbuf, R, Kx, ne, ep->d_own, S->cursor, ep->d_rrow, S->wrow, S->xg);
-  if ((rc = prefill_experts(L, S, rows, v.err, v.num_sms, s))) return rc;
-  if (R > 0) ep_gather<<<R, 256, 0, s>>>(S->y, ep->d_rrow, R, d, ep->ysend);
-  // return the output rows to their sources
-  const size_t yb = (size_t)d * 4;
-  if (N.groupStart() != ncclSuccess) return VIREO_ERR_CUDA;
-  for (int q = 0; q < G; q++) {
-    const int sc = ep->h_cntmat[r * G + q];
-    if (rcnt[q] > 0 && N.send((const uint8_t*)ep->ysend + roff[q] * yb, rcnt[q] * yb, ncclUint8, q, ep->comm, s) != ncclSuccess)
-      return N.groupEnd(), VIREO_ERR_CUDA;
-    if (sc > 0 && N.recv((uint8_t*)ep->yret + soff[q] * yb, sc * yb, ncclUint8, q, ep->comm, s) != ncclSuccess)
-      return N.groupEnd(), VIREO_ERR_CUDA;
-  }
-  if (N.groupEnd() != ncclSuccess) return VIREO_ERR_CUDA;
-  if (n_tok > 0) ep_combine<<<n_tok, 256, 0, s>>>(ep->d_pdest, ep->d_ppos, so, ep->yret, x, n_tok, k, d);
+    ep_dispatch<<<(unsigned)((pairs + 7) / 8), 256, 0, s>>>(S->xa, S->ids, S->wts, ep->d_owner, ep->d_pos,
+                                                             (int)pairs, k, Kx, r, Dp, v.err);
+  if ((rc = ep_barrier(ep, s))) return rc;
+  // the experts held here; the down GEMM returns each row to its source rank
+  prefill_scan_launch(ep->d_totals, ne, S, s);
+  if ((rc = prefill_experts(L, S, rows, v.err, v.num_sms, s, ep->ysrc, ep->p_yret, G))) return rc;
+  if ((rc = ep_barrier(ep, s))) return rc;
+  if (n_tok > 0) ep_combine<<<n_tok, 256, 0, s>>>(S->ids, ep->yret, x, n_tok, k, d);
   if (ids_out && pairs && cudaMemcpyAsync(ids_out, S->ids, pairs * 4, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
     return cuda_status(cudaGetLastError());
   if (wts_out && pairs && cudaMemcpyAsync(wts_out, S->wts, pairs * 4, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
@@ -491,17 +545,34 @@ gguf_moe* gguf_moe_ep_layer(gguf_moe_ep* ep) { return ep ? ep->m : nullptr; }
 
 void gguf_moe_ep_destroy(gguf_moe_ep* ep) {
   if (!ep) return;
+  const bool clean = cudaDeviceSynchronize() == cudaSuccess;
+  for (int q = 0; q < kEpMaxWorld; q++)
+    if (ep->mapped[q])
+      for (void* p : {(void*)ep->p_xg[q], (void*)ep->p_wrow[q], (void*)ep->p_ysrc[q], (void*)ep->p_yret[q]})
+        if (p) cudaIpcCloseMemHandle(p);
   if (ep->comm) {
+    // the peers unmap this rank's buffers before any of them is freed: one
+    // last barrier when the device is clean; after a fault the communicator
+    // is aborted instead, which does not wait for peers
     const NcclApi& N = nccl();
-    cudaDeviceSynchronize();
-    N.commDestroy(ep->comm);
+    if (clean && ep_barrier(ep, nullptr) == VIREO_OK && cudaDeviceSynchronize() == cudaSuccess)
+      N.commDestroy(ep->comm);
+    else
+      N.commAbort(ep->comm);
   }
-  for (void* p : {(void*)ep->d_owner, (void*)ep->d_own, (void*)ep->d_sendcnt, (void*)ep->d_cntmat,
-                  (void*)ep->d_rcounts, (void*)ep->d_pdest, (void*)ep->d_ppos, (void*)ep->d_rrow, (void*)ep->sendbuf,
-                  (void*)ep->recvbuf, (void*)ep->ysend, (void*)ep->yret})
+  if (ep->m) {
+    // the layer's batched scratch points at this handle's buffers: detach them
+    MoeView v;
+    if (!moe_view(ep->m, &v)) {
+      if (v.pre->xg == ep->xg) v.pre->xg = nullptr, v.pre->c_xg = 0;
+      if (v.pre->wrow == ep->wrow) v.pre->wrow = nullptr, v.pre->c_wrow = 0;
+    }
+    gguf_moe_destroy(ep->m);
+  }
+  for (void* p : {(void*)ep->d_owner, (void*)ep->d_own, (void*)ep->d_cnt, (void*)ep->d_cntall, (void*)ep->d_totals, (void*)ep->d_dstoff,
+                  (void*)ep->d_pos, (void*)ep->d_bar, (void*)ep->xg, (void*)ep->wrow, (void*)ep->ysrc,
+                  (void*)ep->yret})
     if (p) cudaFree(p);
-  if (ep->h_cntmat) cudaFreeHost(ep->h_cntmat);
-  if (ep->m) gguf_moe_destroy(ep->m);
   delete ep;
 }
 

@@ -58,6 +58,7 @@ constexpr int kPK = 64;    // K per stage
 constexpr int kPThreads = 512;
 constexpr int kDqWarp0 = 4, kDqWarps = 8, kEpiWarp0 = 12;
 constexpr int kPTopK = 8;  // prefill top-k limit (held in registers)
+constexpr int kPMaxPeers = 8;  // expert-parallel ranks (one node)
 constexpr uint32_t kPStageA = kPM * kPK * 2, kPStageB = kPN * kPK * 2;
 // raw weight chunks of one stage (the repacked layouts, 256 rows each):
 // gate/up 48 B per row (Q4_K header + the stage's 32 quant bytes), down 80 B
@@ -80,7 +81,13 @@ struct PRing {
   static constexpr uint32_t BYTES = OFF_R + (MODE == 0 ? 0u : NR * RB);
 };
 constexpr uint32_t cmax(uint32_t a, uint32_t b) { return a > b ? a : b; }
-constexpr uint32_t kPSmem = 1024 + cmax(PRing<0>::BYTES, cmax(PRing<1>::BYTES, PRing<2>::BYTES));
+// the down GEMM's epilogue stages each warp's 32 x 32 output block here
+// (row stride 33 floats) when its rows return to other ranks
+constexpr uint32_t kPEpiStage = 4 * 32 * 33 * 4;
+template <int MODE>
+constexpr uint32_t psmem() {
+  return 1024 + PRing<MODE>::BYTES + (MODE == 2 ? kPEpiStage : 0u);
+}
 
 enum PMode { P_ROUTER = 0, P_GATEUP = 1, P_DOWN = 2 };
 
@@ -108,6 +115,11 @@ struct PrefillParams {
   // down
   const float* wrow;
   float* y;  // [rows][d]
+  // expert-parallel return (ep.cu): when ysrc is set, row r's output goes to
+  // rank ysrc[r] >> 24's buffer ypeer[rank], row ysrc[r] & 0xFFFFFF, instead
+  // of y (peer memory: the NVLink write overlaps the next tile's MMAs)
+  const int* ysrc;
+  float* ypeer[kPMaxPeers];
   int* err;
 };
 
@@ -527,6 +539,36 @@ __global__ void __launch_bounds__(kPThreads, 1)
         // y = w * (H W_down^T), fp32
         const int n0 = nt * kPN;
         const float w = valid ? p.wrow[row] : 0.f;
+        if (p.ysrc) {
+          // expert-parallel return: each row goes to its source rank's buffer
+          // (peer memory over NVLink).  A thread holds one row, so the warp's
+          // 32 rows are staged per 32-column chunk in shared memory and stored
+          // row by row, 8 lanes per row: every store is a whole 128-byte line.
+          float* stg = reinterpret_cast<float*>(sm + RG::BYTES) + q * (32 * 33);
+          unsigned long long dst = 0;
+          if (valid) {
+            const int src = p.ysrc[row];
+            dst = reinterpret_cast<unsigned long long>(p.ypeer[src >> 24] + (size_t)(src & 0xFFFFFF) * p.d + n0);
+          }
+#pragma unroll 1
+          for (int c = 0; c < kPN; c += 32) {
+            uint32_t v[32];
+            tmem_ld32(ta + c, v);
+#pragma unroll
+            for (int j = 0; j < 32; j++) stg[lane * 33 + j] = __uint_as_float(v[j]) * w;
+            __syncwarp();
+#pragma unroll
+            for (int pass = 0; pass < 8; pass++) {
+              const int rr = 4 * pass + (lane >> 3), c4 = lane & 7;
+              const unsigned long long drow = __shfl_sync(0xffffffffu, dst, rr);
+              if (drow) {
+                const float* sr = stg + rr * 33 + 4 * c4;
+                reinterpret_cast<float4*>(drow)[(c >> 2) + c4] = make_float4(sr[0], sr[1], sr[2], sr[3]);
+              }
+            }
+            __syncwarp();
+          }
+        } else {
 #pragma unroll 1
         for (int c = 0; c < kPN; c += 32) {
           uint32_t v[32];
@@ -539,12 +581,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
                                    __uint_as_float(v[4 * i + 2]) * w, __uint_as_float(v[4 * i + 3]) * w);
           }
         }
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
     }
   }
+  if (MODE == P_DOWN && p.ysrc) __threadfence_system();  // peer rows written before the kernel ends
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, 512);
@@ -729,16 +773,37 @@ __global__ void prefill_place(const int32_t* ids, const float* wts, const __half
 }
 
 // ---- combine: x[t] += sum over rank of y(t, slot) (gguf_run.c:209, 213) ----
+// four columns per thread; the slots' rows are loaded together, then summed
+// in rank order
 __global__ void prefill_combine(const int* rowpos, const float* y, float* x, int T, int k, int d) {
   const int t = blockIdx.x;
   if (t >= T) return;
-  for (int c = threadIdx.x; c < d; c += blockDim.x) {
-    float acc = 0.f;
-    for (int i = 0; i < k; i++) {
-      const int r = rowpos[(size_t)t * k + i];
-      if (r >= 0) acc = __fadd_rn(acc, y[(size_t)r * d + c]);
-    }
-    x[(size_t)t * d + c] = __fadd_rn(x[(size_t)t * d + c], acc);
+  int rp[kPTopK];
+#pragma unroll
+  for (int i = 0; i < kPTopK; i++) rp[i] = i < k ? rowpos[(size_t)t * k + i] : -1;
+  const int d4 = d / 4;
+  const float4* y4 = reinterpret_cast<const float4*>(y);
+  float4* x4 = reinterpret_cast<float4*>(x) + (size_t)t * d4;
+  for (int c = threadIdx.x; c < d4; c += blockDim.x) {
+    float4 v[kPTopK];
+#pragma unroll
+    for (int i = 0; i < kPTopK; i++)
+      if (rp[i] >= 0) v[i] = __ldcs(y4 + (size_t)rp[i] * d4 + c);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < kPTopK; i++)
+      if (rp[i] >= 0) {
+        acc.x = __fadd_rn(acc.x, v[i].x);
+        acc.y = __fadd_rn(acc.y, v[i].y);
+        acc.z = __fadd_rn(acc.z, v[i].z);
+        acc.w = __fadd_rn(acc.w, v[i].w);
+      }
+    float4 xv = x4[c];
+    xv.x = __fadd_rn(xv.x, acc.x);
+    xv.y = __fadd_rn(xv.y, acc.y);
+    xv.z = __fadd_rn(xv.z, acc.z);
+    xv.w = __fadd_rn(xv.w, acc.w);
+    x4[c] = xv;
   }
 }
 
@@ -810,9 +875,9 @@ int prefill_tile_rows() { return kPM; }
 static void set_attrs_once() {
   static std::once_flag attr_once;
   std::call_once(attr_once, [] {
-    cudaFuncSetAttribute(prefill_gemm<P_ROUTER>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPSmem);
-    cudaFuncSetAttribute(prefill_gemm<P_GATEUP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPSmem);
-    cudaFuncSetAttribute(prefill_gemm<P_DOWN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPSmem);
+    cudaFuncSetAttribute(prefill_gemm<P_ROUTER>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem<P_ROUTER>());
+    cudaFuncSetAttribute(prefill_gemm<P_GATEUP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem<P_GATEUP>());
+    cudaFuncSetAttribute(prefill_gemm<P_DOWN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem<P_DOWN>());
   });
 }
 
@@ -885,20 +950,23 @@ int prefill_route(const PrefillLayer& L, PrefillScratch* S, const void* hb, int 
   prefill_prep<<<T, 256, 0, st>>>((const __nv_bfloat16*)hb, (__half*)S->xa, T, d, Kx);
   p.nk = d / kPK;
   p.n_ntiles = 1;
-  prefill_gemm<P_ROUTER><<<std::min(num_sms, (T + kPM - 1) / kPM), kPThreads, kPSmem, st>>>(mA_r, mB_r, p);
+  prefill_gemm<P_ROUTER><<<std::min(num_sms, (T + kPM - 1) / kPM), kPThreads, psmem<P_ROUTER>(), st>>>(mA_r, mB_r, p);
   return cuda_status(cudaGetLastError());
 }
 
 size_t prefill_row_capacity(size_t pairs, int ne) { return ((pairs + (size_t)ne * (kPM - 1)) + kPM - 1) / kPM * kPM; }
 
-int prefill_grow_rows(const PrefillLayer& L, PrefillScratch* S, size_t rows) {
+int prefill_grow_rows(const PrefillLayer& L, PrefillScratch* S, size_t rows, bool need_y) {
   const int Kx = prefill_kx(L.d);
   rows = std::max<size_t>(rows, kPM);
   const size_t max_mtiles = rows / kPM + 1;
   int rc;
-  if ((rc = grow((void**)&S->tiles, &S->c_tiles, max_mtiles * sizeof(PTile))) ||
+  if ((rc = grow((void**)&S->counts, &S->c_counts, 256 * 4)) || (rc = grow((void**)&S->cursor, &S->c_cursor, 256 * 4)) ||
+      (rc = grow((void**)&S->n_mtiles, &S->c_n_mtiles, 16)) ||
+      (rc = grow((void**)&S->tiles, &S->c_tiles, max_mtiles * sizeof(PTile))) ||
       (rc = grow((void**)&S->wrow, &S->c_wrow, rows * 4)) || (rc = grow((void**)&S->xg, &S->c_xg, rows * Kx * 2)) ||
-      (rc = grow((void**)&S->hg, &S->c_hg, rows * L.fe * 2)) || (rc = grow((void**)&S->y, &S->c_y, rows * L.d * 4)))
+      (rc = grow((void**)&S->hg, &S->c_hg, rows * L.fe * 2)) ||
+      (need_y && (rc = grow((void**)&S->y, &S->c_y, rows * L.d * 4))))
     return rc;
   return VIREO_OK;
 }
@@ -907,7 +975,9 @@ void prefill_scan_launch(const int* counts, int ne, PrefillScratch* S, cudaStrea
   prefill_scan<<<1, 256, 0, st>>>(counts, ne, S->cursor, S->tiles, S->n_mtiles);
 }
 
-int prefill_experts(const PrefillLayer& L, PrefillScratch* S, size_t rows, int* d_err, int num_sms, cudaStream_t st) {
+int prefill_experts(const PrefillLayer& L, PrefillScratch* S, size_t rows, int* d_err, int num_sms, cudaStream_t st,
+                    const int* ysrc, float* const* ypeer, int npeers) {
+  if (npeers > kPMaxPeers) return VIREO_ERR_ARG;
   const int d = L.d, fe = L.fe, ne = L.ne, Kx = prefill_kx(d), Km = Kx - d;
   rows = std::max<size_t>(rows, kPM);
   CUtensorMap mA_gu, mA_d, mM;
@@ -921,12 +991,14 @@ int prefill_experts(const PrefillLayer& L, PrefillScratch* S, size_t rows, int* 
   p.nk = Kx / kPK;
   p.n_ntiles = fe / 128;
   p.pack = S->gu_pack;
-  prefill_gemm<P_GATEUP><<<num_sms, kPThreads, kPSmem, st>>>(mA_gu, mM, p);
+  prefill_gemm<P_GATEUP><<<num_sms, kPThreads, psmem<P_GATEUP>(), st>>>(mA_gu, mM, p);
   // down, scaled by the routing weight
   p.nk = fe / kPK;
   p.n_ntiles = d / kPN;
   p.pack = S->dn_pack;
-  prefill_gemm<P_DOWN><<<num_sms, kPThreads, kPSmem, st>>>(mA_d, mA_d, p);
+  p.ysrc = ysrc;
+  for (int i = 0; i < npeers; i++) p.ypeer[i] = ypeer[i];
+  prefill_gemm<P_DOWN><<<num_sms, kPThreads, psmem<P_DOWN>(), st>>>(mA_d, mA_d, p);
   return cuda_status(cudaGetLastError());
 }
 
@@ -936,11 +1008,11 @@ int prefill_run(const PrefillLayer& L, PrefillScratch* S, const void* hb, float*
   const size_t pairs = (size_t)T * k, rows = prefill_row_capacity(pairs, ne);
   int rc;
   if ((rc = prefill_route(L, S, hb, T, bias, d_err, num_sms, st))) return rc;
-  if ((rc = grow((void**)&S->rowpos, &S->c_rowpos, pairs * 4)) || (rc = prefill_grow_rows(L, S, rows))) return rc;
+  if ((rc = grow((void**)&S->rowpos, &S->c_rowpos, pairs * 4)) || (rc = prefill_grow_rows(L, S, rows, true))) return rc;
   prefill_scan_launch(S->counts, ne, S, st);
   prefill_place<<<(unsigned)((pairs + 7) / 8), 256, 0, st>>>(S->ids, S->wts, (const __half*)S->xa, T, k, Kx,
                                                               S->cursor, S->rowpos, S->wrow, (__half*)S->xg);
-  if ((rc = prefill_experts(L, S, rows, d_err, num_sms, st))) return rc;
+  if ((rc = prefill_experts(L, S, rows, d_err, num_sms, st, nullptr, nullptr, 0))) return rc;
   prefill_combine<<<T, 256, 0, st>>>(S->rowpos, S->y, x, T, k, d);
   if (ids_out && cudaMemcpyAsync(ids_out, S->ids, pairs * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
     return cuda_status(cudaGetLastError());

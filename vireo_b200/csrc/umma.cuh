@@ -72,7 +72,7 @@ VDEV void tmem_ld32(uint32_t addr, uint32_t (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// 2-D tiled TMA load (no multicast) completing on bar; x (innermost, in
+// 2-D tiled TMA load (one CTA, this GPU's memory) completing on bar; x (innermost, in
 // elements) must be a multiple of 16 bytes' worth of elements
 VDEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
