@@ -125,28 +125,26 @@ __global__ void ep_count(const int32_t* ids, int pairs, int* cnt, int* pos) {
 // 0 (the counts prefill_scan lays out).  One block, thread e per expert.
 __global__ void ep_layout(const int* cntall, const int32_t* owner, int G, int ne, int rank, int tile, int* dst_off,
                           int* totals) {
-  __shared__ int tot[kEpMaxExperts], before[kEpMaxExperts];
+  __shared__ int pad[kEpMaxExperts], own_s[kEpMaxExperts];
   const int e = threadIdx.x;
+  int n = 0, b = 0, q = 0;
   if (e < ne) {
-    int n = 0, b = 0;
-    for (int q = 0; q < G; q++) {
-      const int c = cntall[q * ne + e];
-      if (q < rank) b += c;
+    for (int s = 0; s < G; s++) {
+      const int c = cntall[s * ne + e];
+      if (s < rank) b += c;
       n += c;
     }
-    tot[e] = n;
-    before[e] = b;
+    q = owner[e];
+    pad[e] = (n + tile - 1) / tile * tile;
+    own_s[e] = q;
   }
   __syncthreads();
-  if (e == 0) {
-    int next[kEpMaxWorld];
-    for (int q = 0; q < G; q++) next[q] = 0;
-    for (int i = 0; i < ne; i++) {
-      const int q = owner[i];
-      dst_off[i] = next[q] + before[i];
-      next[q] += (tot[i] + tile - 1) / tile * tile;
-      totals[i] = q == rank ? tot[i] : 0;
-    }
+  if (e < ne) {
+    int base = 0;  // padded ranges of the experts before e on the same owner
+    for (int i = 0; i < e; i++)
+      if (own_s[i] == q) base += pad[i];
+    dst_off[e] = base + b;
+    totals[e] = q == rank ? n : 0;
   }
 }
 
