@@ -202,6 +202,9 @@ def main():
     ap.add_argument("--copies", type=int, default=8, help="layer copies rotated per token")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--timeline", default=None,
+                    help="prefill only: after the timed steps, record 3 more steps under the CUDA activity "
+                         "profiler and write each rank's kernel timeline to TIMELINE.rank<r>.txt (not timed)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     wl = WORKLOADS[args.workload]
@@ -428,6 +431,9 @@ def run_prefill(args, wl):
         t_sec = float(tt.item())
     value = args.steps * T / t_sec
 
+    if args.timeline:
+        write_timeline(args.timeline, rank, lambda: step(hb.data_ptr(), x.data_ptr()), 3)
+
     # end to end: hidden states and residual from pinned host memory, residual back
     hb_h = x_bf.pin_memory()
     x_h = torch.zeros((Tl, d), dtype=torch.float32).pin_memory()
@@ -491,6 +497,30 @@ def run_prefill(args, wl):
         torch.distributed.destroy_process_group()
     else:
         m.close()
+
+
+def write_timeline(path, rank, step, n):
+    """Kernel timeline of n steps from the CUDA activity profiler (CUPTI via
+    torch.profiler): start offset, duration and name of every kernel, memcpy
+    and memset on this rank's GPU, one line each, to path.rank<r>.txt."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(n):
+            step()
+        torch.cuda.synchronize()
+    raw = f"{path}.rank{rank}.json"
+    prof.export_chrome_trace(raw)
+    with open(raw) as f:
+        ev = [e for e in json.load(f)["traceEvents"] if e.get("cat") in ("kernel", "gpu_memcpy", "gpu_memset")]
+    os.remove(raw)
+    ev.sort(key=lambda e: e["ts"])
+    t0 = ev[0]["ts"] if ev else 0
+    with open(f"{path}.rank{rank}.txt", "w") as f:
+        f.write("# start_us duration_us kernel\n")
+        for e in ev:
+            f.write(f"{e['ts'] - t0:10.1f} {e['dur']:9.1f}  {e['name'][:100]}\n")
 
 
 def zipf_routes(n_tok, n_layers, ne, k, seed):
