@@ -70,11 +70,30 @@ constexpr uint32_t kPRawGU = kPN * 48, kPRawDN = kPN * 80;
 // (written by the dequant warps, freed by the MMA).  The first two run
 // several stages ahead of the MMA so their latency is hidden; only a few
 // 32 KB converted tiles need to be resident.
+#ifndef VIREO_P_NA_GU
+#define VIREO_P_NA_GU 4
+#endif
+#ifndef VIREO_P_NB_GU
+#define VIREO_P_NB_GU 3
+#endif
+#ifndef VIREO_P_NR_GU
+#define VIREO_P_NR_GU 4
+#endif
+#ifndef VIREO_P_NA_DN
+#define VIREO_P_NA_DN 3
+#endif
+#ifndef VIREO_P_NB_DN
+#define VIREO_P_NB_DN 3
+#endif
+#ifndef VIREO_P_NR_DN
+#define VIREO_P_NR_DN 3
+#endif
 template <int MODE>
 struct PRing {
-  static constexpr int NA = MODE == 2 ? 3 : 4;                 // activation stages
-  static constexpr int NB = 3;                                 // converted weight stages
-  static constexpr int NR = MODE == 1 ? 4 : (MODE == 2 ? 3 : 1);  // raw chunk stages
+  // activation stages, converted weight stages, raw chunk stages
+  static constexpr int NA = MODE == 2 ? VIREO_P_NA_DN : (MODE == 1 ? VIREO_P_NA_GU : 4);
+  static constexpr int NB = MODE == 2 ? VIREO_P_NB_DN : (MODE == 1 ? VIREO_P_NB_GU : 3);
+  static constexpr int NR = MODE == 1 ? VIREO_P_NR_GU : (MODE == 2 ? VIREO_P_NR_DN : 1);
   static constexpr uint32_t RB = MODE == 2 ? kPRawDN : kPRawGU;   // raw chunk bytes
   static constexpr uint32_t OFF_B = NA * kPStageA;
   static constexpr uint32_t OFF_R = OFF_B + NB * kPStageB;
@@ -88,6 +107,8 @@ template <int MODE>
 constexpr uint32_t psmem() {
   return 1024 + PRing<MODE>::BYTES + (MODE == 2 ? kPEpiStage : 0u);
 }
+static_assert(psmem<0>() <= 227 * 1024 && psmem<1>() <= 227 * 1024 && psmem<2>() <= 227 * 1024,
+              "prefill rings exceed the shared memory of one CTA");
 
 enum PMode { P_ROUTER = 0, P_GATEUP = 1, P_DOWN = 2 };
 
@@ -276,20 +297,17 @@ __global__ void __launch_bounds__(kPThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---- producer: activation tiles (TMA) and raw weight chunks (bulk) ----
-      uint32_t g = 0, rg = 0;
+      // ---- producer: activation tiles (TMA; the router's weight tiles too) ---
+      uint32_t g = 0;
       bool ok = true;
       for (int item = blockIdx.x; ok && item < n_items && !abort_s; item += gridDim.x) {
         const PTile t = tile_of(item / p.n_ntiles);
-        const int nt = item % p.n_ntiles;
         for (int kt = 0; kt < p.nk; kt++, g++) {
           // every wait of the stage comes before any of its copies is issued,
           // so an abort leaves no copy untracked by the drain below
-          const int a = (int)(g % NA), b = (int)(g % NB), sl = (int)(rg % NR);
-          const bool raw = MODE != P_ROUTER && kt < nkd;
+          const int a = (int)(g % NA), b = (int)(g % NB);
           if ((g >= (uint32_t)NA && !pwait(&emptyA[a], ((g / NA) - 1) & 1, &abort_s, p.err)) ||
-              (MODE == P_ROUTER && g >= (uint32_t)NB && !pwait(&emptyB[b], ((g / NB) - 1) & 1, &abort_s, p.err)) ||
-              (raw && rg >= (uint32_t)NR && !pwait(&rawempty[sl], ((rg / NR) - 1) & 1, &abort_s, p.err))) {
+              (MODE == P_ROUTER && g >= (uint32_t)NB && !pwait(&emptyB[b], ((g / NB) - 1) & 1, &abort_s, p.err))) {
             ok = false;
             break;
           }
@@ -298,11 +316,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
           if constexpr (MODE == P_ROUTER) {
             mbar_arrive_expect_tx(&fullB[b], kPStageB);
             tma_load_2d(sB + b * kPStageB, &tmB, kt * kPK, 0, &fullB[b]);
-          } else if (raw) {
-            const uint8_t* src = p.pack + ((size_t)(t.e * p.n_ntiles + nt) * nkd + kt) * RG::RB;
-            mbar_arrive_expect_tx(&rawfull[sl], RG::RB);
-            bulk_g2s(sR + sl * RG::RB, src, RG::RB, &rawfull[sl]);
-            rg++;
           }
         }
       }
@@ -311,8 +324,32 @@ __global__ void __launch_bounds__(kPThreads, 1)
       for (uint32_t j = g > (uint32_t)NA ? g - NA : 0; j < g; j++) mbar_wait(&fullA[j % NA], (j / NA) & 1, &never);
       if (MODE == P_ROUTER)
         for (uint32_t j = g > (uint32_t)NB ? g - NB : 0; j < g; j++) mbar_wait(&fullB[j % NB], (j / NB) & 1, &never);
-      for (uint32_t j = rg > (uint32_t)NR ? rg - NR : 0; j < rg; j++)
-        mbar_wait(&rawfull[j % NR], (j / NR) & 1, &never);
+    }
+  } else if (warp == 2) {
+    if constexpr (MODE != P_ROUTER) {
+      if (lane == 0) {
+        // ---- producer: raw weight chunks (bulk copies), paced only by the
+        // dequantisation warps, so the chunk ring runs ahead of the MMAs -----
+        uint32_t rg = 0;
+        bool ok = true;
+        for (int item = blockIdx.x; ok && item < n_items && !abort_s; item += gridDim.x) {
+          const PTile t = tile_of(item / p.n_ntiles);
+          const int nt = item % p.n_ntiles;
+          for (int kt = 0; kt < nkd; kt++, rg++) {
+            const int sl = (int)(rg % NR);
+            if (rg >= (uint32_t)NR && !pwait(&rawempty[sl], ((rg / NR) - 1) & 1, &abort_s, p.err)) {
+              ok = false;
+              break;
+            }
+            const uint8_t* src = p.pack + ((size_t)(t.e * p.n_ntiles + nt) * nkd + kt) * RG::RB;
+            mbar_arrive_expect_tx(&rawfull[sl], RG::RB);
+            bulk_g2s(sR + sl * RG::RB, src, RG::RB, &rawfull[sl]);
+          }
+        }
+        volatile int never = 0;
+        for (uint32_t j = rg > (uint32_t)NR ? rg - NR : 0; j < rg; j++)
+          mbar_wait(&rawfull[j % NR], (j / NR) & 1, &never);
+      }
     }
   } else if (warp == 1) {
     if (lane == 0) {
