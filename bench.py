@@ -43,6 +43,14 @@ WORKLOADS = {
     "qwen3_prefill": dict(spec=S.qwen3_layer, seed=1234, config=4,
                           desc="Qwen3-30B-A3B-shaped MoE layer, 8192 bf16 tokens, router logits + per-expert bias "
                                "N(0,0.5), Q4_K gate/up + Q6_K down, 128 experts top-8 renorm, batched prefill"),
+    "olmoe_decoder": dict(spec=S.olmoe_decoder, seed=1234, config=2, prompt=4096, gen=256,
+                          desc="OLMoE-1B-7B-shaped decoder (16 layers, 16 heads x 128, vocab 50304, 64 experts "
+                               "top-8, Q4_K attention and gate/up, Q6_K down and LM head), 4096-token seeded "
+                               "prompt then greedy batch-1 decode"),
+    "qwen3_decoder": dict(spec=S.qwen3_decoder, seed=1234, config=3, prompt=8192, gen=256,
+                          desc="Qwen3-30B-A3B-shaped decoder (48 layers, 32 q / 4 kv heads x 128, vocab 151936, "
+                               "128 experts top-8 renorm, Q4_K attention and gate/up, Q6_K down and LM head), "
+                               "8192-token context then greedy batch-1 decode"),
     "qwen3_cached_decode": dict(spec=S.qwen3_layer, seed=1234, config=5,
                                 desc="Qwen3-30B-A3B-shaped 48-layer MoE stack, experts in pinned host memory "
                                      "behind a 4 GiB device ExpertStore, Zipf(1.1) routing, batch-1 decode"),
@@ -202,6 +210,7 @@ def main():
     ap.add_argument("--copies", type=int, default=8, help="layer copies rotated per token")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prompt", type=int, default=None, help="decoder workloads: prompt tokens (default: the config's)")
     ap.add_argument("--timeline", default=None,
                     help="prefill only: after the timed steps, record 3 more steps under the CUDA activity "
                          "profiler and write each rank's kernel timeline to TIMELINE.rank<r>.txt (not timed)")
@@ -214,6 +223,8 @@ def main():
         return run_cached(args, wl)
     if args.workload == "qwen3_prefill":
         return run_prefill(args, wl)
+    if args.workload in ("olmoe_decoder", "qwen3_decoder"):
+        return run_decoder(args, wl)
 
     import torch
     import vireo_b200 as V
@@ -497,6 +508,156 @@ def run_prefill(args, wl):
         torch.distributed.destroy_process_group()
     else:
         m.close()
+
+
+def cpu_decoder_rate(dec, seconds, threads):
+    """The reference's own forward() (oracle/_ref, its dense KV store and
+    ExpertStore) over 1- and 2-layer slices of the same decoder at short
+    context; seconds per token for the full layer count by a linear fit
+    (a + b L: the LM head and embedding plus L layers)."""
+    from oracle import oracle as O
+    if not O.ref_available():
+        return None
+    O.ref().ref_set_threads(threads)
+    per = {}
+    for nl in (1, 2):
+        sub = S.Decoder.__new__(S.Decoder)
+        sub.spec = S.DecoderSpec(nl, dec.spec.dim, dec.spec.n_heads, dec.spec.n_kv_heads, dec.spec.head_size,
+                                 dec.spec.vocab, dec.spec.moe, dec.spec.qk_norm, dec.spec.attn_type,
+                                 dec.spec.embd_type, dec.spec.lm_type, dec.spec.eps, dec.spec.rope_base)
+        sub.seed, sub.tok_embd, sub.out_norm, sub.lm_head = dec.seed, dec.tok_embd, dec.out_norm, dec.lm_head
+        sub.layers = dec.layers[:nl]
+        R = O.RefDecoder(sub)
+        try:
+            R.step(1, 0, True)
+            n, t0 = 0, time.perf_counter()
+            while time.perf_counter() - t0 < seconds / 2 and n < 64:
+                R.step((7 * n + 3) % dec.spec.vocab, n + 1, True)
+                n += 1
+            per[nl] = (time.perf_counter() - t0) / n
+        finally:
+            R.close()
+    b = per[2] - per[1]
+    a = per[1] - b
+    full = a + b * dec.spec.n_layers
+    return full, per
+
+
+def run_decoder(args, wl):
+    """Configs 2 and 3: whole decode steps (gguf_decoder_step_dev: every
+    layer's attention and MoE block, the final norm, the LM head and the
+    greedy argmax on the device; each step's token is the previous step's
+    argmax, read on the device).  The prompt is fed first (seeded ids, no LM
+    head, as the reference's prompt steps); a step of the timed region is
+    one generated token."""
+    import torch
+    import vireo_b200 as V
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    L = V.lib()
+    V.check(L.vireo_device_init(local), "vireo_device_init")
+    spec = wl["spec"]()
+    P, gen = (wl["prompt"] if args.prompt is None else args.prompt), max(args.steps, 1)
+    dec = S.Decoder(spec, wl["seed"], n_distinct_layers=1)
+    dev = torch.device("cuda", local)
+    G = V.Decoder(dec, max_ctx=P + gen + args.warmup + 40, kv_f16=True, device=local)
+    stream = torch.cuda.Stream(dev)
+    sp = stream.cuda_stream
+    prompt = (S.u64(wl["seed"], 55, P) % np.uint64(spec.vocab)).astype(np.int64)
+    tok = torch.zeros(1, dtype=torch.int32, device=dev)
+    t0 = time.perf_counter()
+    for pos in range(P):
+        G.step(int(prompt[pos]), pos, stream=sp)
+    G.sync(sp)
+    prompt_s = time.perf_counter() - t0
+    pos = P
+    with torch.cuda.stream(stream):
+        tok.fill_(int(prompt[-1]))
+    for _ in range(args.warmup):
+        G.step_dev(tok, pos, next=tok, stream=sp)
+        pos += 1
+    G.sync(sp)
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx0 = pos
+    with Clocks(local) as clk:
+        torch.cuda.synchronize(dev)
+        e0.record(stream)
+        for _ in range(gen):
+            G.step_dev(tok, pos, next=tok, stream=sp)
+            pos += 1
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    G.sync(sp)
+    t_sec = e0.elapsed_time(e1) / 1e3
+    if world > 1:
+        tt = torch.tensor([t_sec], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        t_sec = float(tt.item())
+    value = gen * world / t_sec
+    # end to end: the host API with a host token per step and the next token
+    # read back to the host every step
+    n_e2e = min(gen, 32)
+    nxt = torch.zeros(1, dtype=torch.int32, device=dev)
+    host_tok = int(tok.item())
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        G.step(host_tok, pos, next=nxt, stream=sp)
+        pos += 1
+        stream.synchronize()
+        host_tok = int(nxt.item())
+    e2e_tps = n_e2e * world / (time.perf_counter() - t0)
+    G.sync(sp)
+
+    avg_ctx = ctx0 + gen / 2
+    wbytes = spec.weight_bytes_per_token()
+    kvb = spec.kv_bytes_per_position(2) * avg_ctx
+    per_tok = wbytes + kvb
+    peak, peak_kind = peaks()
+    achieved = per_tok * gen / t_sec / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        th = host_threads()
+        r = cpu_decoder_rate(dec, args.cpu_seconds, th)
+        if r:
+            full, per = r
+            cpu = {"value": 1.0 / full, "unit": "tok/s", "cores": th, "kind": "reference",
+                   "sample": f"the reference's forward() on 1- and 2-layer slices of this decoder at context "
+                             f"<= 64 ({per[1] * 1e3:.1f} / {per[2] * 1e3:.1f} ms per token), linear in the layer "
+                             f"count to {spec.n_layers} layers; long-context attention not included; "
+                             f"OMP threads={th}"}
+    if rank == 0:
+        line = {"metric": "decoder_decode_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": world,
+                "steps": gen, "warmup": args.warmup, "ms_per_step": t_sec / gen * 1e3,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded GGUF blocks, random-init weights, seeded prompt ids, greedy decode)",
+                "config": {"workload": args.workload, "desc": wl["desc"], "baseline_config": wl["config"],
+                           "layers": spec.n_layers, "prompt_tokens": P, "context_at_timed_start": ctx0,
+                           "kv_cache": "f16", "batch": 1, "parallelism": f"replicas x{world}",
+                           "prompt_seconds": prompt_s,
+                           "l2": "every layer's weights at distinct addresses; 2 GB of weights per token"},
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                             "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
+                             "algorithmic_bytes_per_step": per_tok,
+                             "weight_bytes_per_token": wbytes, "kv_bytes_per_token": kvb,
+                             "kernel": "whole decode step (all layers, LM head, argmax)"},
+                "cpu_baseline": cpu,
+                "e2e": {"value": e2e_tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4,
+                        "note": "gguf_decoder_step with a host token id per step, next token read back"},
+                "gpu_launches": gen * (1 + 10 * spec.n_layers + 3), "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    G.close()
+    if world > 1:
+        torch.distributed.destroy_process_group()
 
 
 def write_timeline(path, rank, step, n):

@@ -108,6 +108,12 @@ def ref():
         lib.ref_moe_destroy.argtypes = [C.c_void_p]
         lib.ref_set_threads.argtypes = [C.c_int]
         lib.ref_max_threads.restype = C.c_int
+        lib.ref_decoder_create.argtypes = [C.c_int] * 6 + [C.c_float, C.c_float] + [C.c_int] * 4 + [C.c_void_p] * 4
+        lib.ref_decoder_create.restype = C.c_void_p
+        lib.ref_decoder_forward.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+        lib.ref_decoder_forward.restype = C.c_int
+        lib.ref_decoder_destroy.argtypes = [C.c_void_p]
+        lib.ref_decoder_destroy.restype = None
         _ref = lib
     return _ref
 
@@ -184,6 +190,70 @@ class PortMoe:
         if port().orc_expert_ffn(C.byref(self.desc), int(e), hb, out):
             raise ValueError(f"bad expert id {e}")
         return out
+
+
+class RefTensorIn(C.Structure):
+    _fields_ = [("type", C.c_uint32), ("data", C.c_void_p), ("nbytes", C.c_uint64), ("dim0", C.c_uint64)]
+
+
+class RefDecoder:
+    """The reference's own forward() (gguf_run.c:216-252, through
+    ref_harness.c) over a synth.Decoder: its dense KV store and its
+    ExpertStore, one decode step per call."""
+
+    def __init__(self, dec):
+        s = dec.spec
+        m = s.moe
+        self.dec = dec
+        keep = []
+
+        def t(ggml_type, arr, dim0):
+            if arr is None:
+                return RefTensorIn(0, None, 0, 0)
+            a = _u8(arr)
+            keep.append(a)
+            return RefTensorIn(ggml_type, a.ctypes.data, a.nbytes, dim0)
+
+        F32 = 0
+        tok = t(s.embd_type, dec.tok_embd, s.dim)
+        on = t(F32, dec.out_norm, s.dim)
+        lm = t(s.lm_type, dec.lm_head, s.dim)
+        rows = []
+        for ly in dec.layers:
+            qn = s.head_size if s.qk_norm == "head" else s.q_dim
+            kn = s.head_size if s.qk_norm == "head" else s.kv_dim
+            rows += [t(F32, ly.attn_norm, s.dim), t(s.attn_type, ly.wq, s.dim), t(s.attn_type, ly.wk, s.dim),
+                     t(s.attn_type, ly.wv, s.dim), t(s.attn_type, ly.wo, s.q_dim), t(F32, ly.ffn_norm, s.dim),
+                     t(F32, ly.q_norm, qn), t(F32, ly.k_norm, kn), t(m.router_type, ly.moe.router, s.dim),
+                     t(m.gate_type, ly.moe.gate, s.dim), t(m.up_type, ly.moe.up, s.dim),
+                     t(m.down_type, ly.moe.down, m.ffn_exp)]
+        arr = (RefTensorIn * len(rows))(*rows)
+        self._keep = (keep, tok, on, lm, arr)
+        self.h = ref().ref_decoder_create(s.n_layers, s.dim, s.n_heads, s.n_kv_heads, s.head_size, s.vocab, s.eps,
+                                          s.rope_base, m.n_experts, m.n_used, m.ffn_exp, m.topk_renorm,
+                                          C.byref(tok), C.byref(on), C.byref(lm), arr)
+        if not self.h:
+            raise RuntimeError("ref_decoder_create failed")
+
+    def step(self, token: int, pos: int, want_logits: bool = True):
+        """(logits or None, residual x, argmax or -1)"""
+        s = self.dec.spec
+        lg = np.zeros(s.vocab, dtype=np.float32)
+        x = np.zeros(s.dim, dtype=np.float32)
+        a = ref().ref_decoder_forward(self.h, int(token), int(pos), int(want_logits), lg.ctypes.data,
+                                      x.ctypes.data)
+        return (lg if want_logits else None), x, a
+
+    def close(self):
+        if getattr(self, "h", None):
+            ref().ref_decoder_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class RefMoe:

@@ -174,3 +174,124 @@ void ref_matmul(float *y, const float *x, uint32_t type, const void *data, int n
     t.ggml_type = type;
     gguf_matmul(y, x, &t, n, d);
 }
+
+/* ---- whole decode steps: the reference's forward() (gguf_run.c:216-252) ----
+ * A Model built here from caller-owned tensors (the fields main() fills from
+ * GGUF metadata, gguf_run.c:276-293, 297-333), with the reference's dense KV
+ * store (exact attention, src/kvstore_dense.c) and its ExpertStore over an
+ * anonymous file holding every layer's experts. */
+typedef struct {
+    uint32_t type;
+    const void *data;
+    uint64_t nbytes;
+    uint64_t dim0;
+} RefTensorIn;
+
+enum { RT_ATTN_NORM, RT_WQ, RT_WK, RT_WV, RT_WO, RT_FFN_NORM, RT_Q_NORM, RT_K_NORM, RT_ROUTER, RT_GATE, RT_UP,
+       RT_DOWN, RT_N };
+
+typedef struct {
+    Model m;
+    gguf_ctx g;
+    gguf_tensor tok_embd, out_norm, lm_head;
+    gguf_tensor *lt;  /* [n_layers][RT_N] */
+    int fd;
+    void *anchor;
+} RefDec;
+
+static void ref_tensor(gguf_tensor *t, const RefTensorIn *in) {
+    memset(t, 0, sizeof(*t));
+    t->data = in->data;
+    t->ggml_type = in->type;
+    t->nbytes = in->nbytes;
+    t->dims[0] = in->dim0;
+    t->n_dims = 1;
+}
+
+RefDec *ref_decoder_create(int n_layers, int dim, int n_heads, int n_kv_heads, int head_size, int vocab, float eps,
+                           float rope_base, int n_experts, int n_used, int ffn_exp, int topk_renorm,
+                           const RefTensorIn *tok_embd, const RefTensorIn *out_norm, const RefTensorIn *lm_head,
+                           const RefTensorIn *layers) {
+    RefDec *r = (RefDec *)calloc(1, sizeof(RefDec));
+    if (!r) return NULL;
+    r->fd = memfd_create("vireo_ref_decoder_experts", 0);
+    if (r->fd < 0) { free(r); return NULL; }
+    r->anchor = malloc(16);
+    r->g.map = r->anchor;
+    r->lt = (gguf_tensor *)calloc((size_t)n_layers * RT_N, sizeof(gguf_tensor));
+    Model *m = &r->m;
+    m->g = &r->g;
+    m->n_layers = n_layers; m->dim = dim; m->n_heads = n_heads; m->n_kv_heads = n_kv_heads;
+    m->head_size = head_size; m->vocab = vocab; m->eps = eps; m->rope_base = rope_base; m->ffn = ffn_exp;
+    m->is_moe = 1; m->n_experts = n_experts; m->n_used = n_used; m->ffn_exp = ffn_exp; m->topk_renorm = topk_renorm;
+    ref_tensor(&r->tok_embd, tok_embd);
+    ref_tensor(&r->out_norm, out_norm);
+    ref_tensor(&r->lm_head, lm_head);
+    m->tok_embd = &r->tok_embd; m->out_norm = &r->out_norm; m->lm_head = &r->lm_head;
+    m->L = (Layer *)calloc((size_t)n_layers, sizeof(Layer));
+    uint64_t off = 0;
+    m->es = expert_store_create(r->fd, 0, n_layers, n_experts);
+    for (int l = 0; l < n_layers; l++) {
+        gguf_tensor *t = r->lt + (size_t)l * RT_N;
+        const RefTensorIn *in = layers + (size_t)l * RT_N;
+        for (int i = 0; i < RT_N; i++) ref_tensor(&t[i], &in[i]);
+        Layer *ly = &m->L[l];
+        ly->attn_norm = &t[RT_ATTN_NORM]; ly->wq = &t[RT_WQ]; ly->wk = &t[RT_WK]; ly->wv = &t[RT_WV];
+        ly->wo = &t[RT_WO]; ly->ffn_norm = &t[RT_FFN_NORM];
+        ly->q_norm = in[RT_Q_NORM].data ? &t[RT_Q_NORM] : NULL;
+        ly->k_norm = in[RT_K_NORM].data ? &t[RT_K_NORM] : NULL;
+        ly->router = &t[RT_ROUTER];
+        /* expert tensors: bytes come from the ExpertStore; data only feeds
+         * the (unused) base-offset arithmetic in moe_ffn */
+        uint64_t og = off, ou = og + in[RT_GATE].nbytes, od = ou + in[RT_UP].nbytes;
+        if (write_all(r->fd, in[RT_GATE].data, in[RT_GATE].nbytes, og) ||
+            write_all(r->fd, in[RT_UP].data, in[RT_UP].nbytes, ou) ||
+            write_all(r->fd, in[RT_DOWN].data, in[RT_DOWN].nbytes, od))
+            return NULL;
+        off = od + in[RT_DOWN].nbytes;
+        t[RT_GATE].data = r->anchor; t[RT_UP].data = r->anchor; t[RT_DOWN].data = r->anchor;
+        ly->gate_exps = &t[RT_GATE]; ly->up_exps = &t[RT_UP]; ly->down_exps = &t[RT_DOWN];
+        uint32_t gs = (uint32_t)(in[RT_GATE].nbytes / (uint64_t)n_experts);
+        uint32_t us = (uint32_t)(in[RT_UP].nbytes / (uint64_t)n_experts);
+        uint32_t ds = (uint32_t)(in[RT_DOWN].nbytes / (uint64_t)n_experts);
+        for (int e = 0; e < n_experts; e++) {
+            ExpertSlices sl = {og + (uint64_t)e * gs, ou + (uint64_t)e * us, od + (uint64_t)e * ds, gs, us, ds};
+            expert_store_register(m->es, l, e, &sl);
+        }
+    }
+    m->exp_type = r->lt[RT_GATE].ggml_type;
+    KVConfig cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.n_layers = n_layers * n_kv_heads;
+    cfg.kv_dim = head_size;
+    m->kv = kvstore_dense_create(cfg);
+    m->x = malloc(dim * 4); m->xb = malloc(dim * 4);
+    m->q = malloc((size_t)n_heads * head_size * 4); m->k = malloc((size_t)n_kv_heads * head_size * 4);
+    m->v = malloc((size_t)n_kv_heads * head_size * 4); m->att_out = malloc((size_t)n_heads * head_size * 4);
+    m->logits = malloc((size_t)vocab * 4);
+    m->rlog = malloc((size_t)n_experts * 4); m->gbuf = malloc((size_t)ffn_exp * 4);
+    m->ubuf = malloc((size_t)ffn_exp * 4); m->dbuf = malloc((size_t)dim * 4); m->moe_acc = malloc((size_t)dim * 4);
+    return r;
+}
+
+/* forward(m, token, pos, want_logits); logits_out [vocab] (when want_logits)
+ * and x_out [dim] (the residual stream) may be NULL. */
+int ref_decoder_forward(RefDec *r, int token, int pos, int want_logits, float *logits_out, float *x_out) {
+    Model *m = &r->m;
+    float *lg = forward(m, token, pos, want_logits);
+    if (lg && logits_out) memcpy(logits_out, lg, sizeof(float) * (size_t)m->vocab);
+    if (x_out) memcpy(x_out, m->x, sizeof(float) * (size_t)m->dim);
+    return lg ? argmax(lg, m->vocab) : -1;
+}
+
+void ref_decoder_destroy(RefDec *r) {
+    if (!r) return;
+    Model *m = &r->m;
+    kv_destroy(m->kv);
+    expert_store_destroy(m->es);
+    free(m->x); free(m->xb); free(m->q); free(m->k); free(m->v); free(m->att_out); free(m->logits);
+    free(m->rlog); free(m->gbuf); free(m->ubuf); free(m->dbuf); free(m->moe_acc);
+    free(m->L); free(r->lt); free(r->anchor);
+    close(r->fd);
+    free(r);
+}

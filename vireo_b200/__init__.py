@@ -327,3 +327,137 @@ class MoeLayerEP:
         if getattr(self, "h", None):
             lib().gguf_moe_ep_destroy(self.h)
             self.h = None
+
+
+class GgufDecoderDesc(C.Structure):
+    _fields_ = [("n_layers", C.c_int), ("dim", C.c_int), ("n_heads", C.c_int), ("n_kv_heads", C.c_int),
+                ("head_size", C.c_int), ("vocab", C.c_int), ("eps", C.c_float), ("rope_base", C.c_float),
+                ("max_ctx", C.c_int), ("kv_f16", C.c_int), ("tok_embd_type", C.c_uint32), ("tok_embd", C.c_void_p),
+                ("out_norm", C.c_void_p), ("lm_head_type", C.c_uint32), ("lm_head", C.c_void_p)]
+
+
+class GgufDecoderLayer(C.Structure):
+    _fields_ = [("attn_norm", C.c_void_p), ("ffn_norm", C.c_void_p), ("wq_type", C.c_uint32),
+                ("wk_type", C.c_uint32), ("wv_type", C.c_uint32), ("wo_type", C.c_uint32), ("wq", C.c_void_p),
+                ("wk", C.c_void_p), ("wv", C.c_void_p), ("wo", C.c_void_p), ("bq", C.c_void_p), ("bk", C.c_void_p),
+                ("bv", C.c_void_p), ("q_norm", C.c_void_p), ("k_norm", C.c_void_p), ("q_norm_len", C.c_int),
+                ("k_norm_len", C.c_int), ("moe", C.c_void_p)]
+
+
+def _decoder_api(L):
+    if getattr(L, "_decoder_api", False):
+        return
+    L.gguf_decoder_create.argtypes = [C.POINTER(GgufDecoderDesc), C.c_void_p, C.POINTER(C.c_void_p)]
+    L.gguf_decoder_step.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]
+    L.gguf_decoder_step_dev.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]
+    L.gguf_decoder_hidden.argtypes = [C.c_void_p]
+    L.gguf_decoder_hidden.restype = C.c_void_p
+    L.gguf_decoder_sync.argtypes = [C.c_void_p, C.c_void_p]
+    L.gguf_decoder_destroy.argtypes = [C.c_void_p]
+    L.gguf_decoder_destroy.restype = None
+    L._decoder_api = True
+
+
+class Decoder:
+    """A whole MoE decoder on the device (gguf_decoder_*): the reference's
+    forward() (src/gguf_run.c:216-252) one step per call.  ``dec`` is a
+    ``vireo_b200.synth.Decoder`` (or any object with the same fields).  Each
+    layer gets its own device copy of its tensors, also when the generated
+    layers repeat, so no step reads another layer's bytes out of L2."""
+
+    def __init__(self, dec, max_ctx: int, kv_f16: bool = True, device: int = 0):
+        import torch
+        L = lib()
+        _decoder_api(L)
+        s = dec.spec
+        self.spec = s
+        dev = torch.device("cuda", device)
+        self.device = dev
+        uploaded = {}
+
+        def up(a):
+            """a device copy per call (distinct addresses), uploaded once per host array"""
+            if a is None:
+                return None
+            key = id(a)
+            if key not in uploaded:
+                uploaded[key] = torch.from_numpy(np.ascontiguousarray(a).view(np.uint8).reshape(-1)).to(dev)
+                return uploaded[key]
+            return uploaded[key].clone()
+
+        self._keep = []
+        keep = self._keep.append
+        ptr = lambda t: t.data_ptr() if t is not None else None
+        tok, on, lm = up(dec.tok_embd), up(dec.out_norm), up(dec.lm_head)
+        keep(tok), keep(on), keep(lm)
+        self.desc = GgufDecoderDesc(s.n_layers, s.dim, s.n_heads, s.n_kv_heads, s.head_size, s.vocab, s.eps,
+                                    s.rope_base, max_ctx, int(kv_f16), s.embd_type, ptr(tok), ptr(on), s.lm_type,
+                                    ptr(lm))
+        self.moe = []
+        rows = []
+        for ly in dec.layers:
+            t = [up(a) for a in (ly.attn_norm, ly.ffn_norm, ly.wq, ly.wk, ly.wv, ly.wo, ly.q_norm, ly.k_norm)]
+            for x in t:
+                keep(x)
+            m = _DeviceMoe(ly.moe, up)
+            self.moe.append(m)
+            qn = s.head_size if s.qk_norm == "head" else s.q_dim
+            kn = s.head_size if s.qk_norm == "head" else s.kv_dim
+            rows.append(GgufDecoderLayer(ptr(t[0]), ptr(t[1]), s.attn_type, s.attn_type, s.attn_type, s.attn_type,
+                                         ptr(t[2]), ptr(t[3]), ptr(t[4]), ptr(t[5]), None, None, None, ptr(t[6]),
+                                         ptr(t[7]), qn if t[6] is not None else 0, kn if t[7] is not None else 0,
+                                         m.h))
+        self.layers = (GgufDecoderLayer * len(rows))(*rows)
+        h = C.c_void_p()
+        check(L.gguf_decoder_create(C.byref(self.desc), self.layers, C.byref(h)), "gguf_decoder_create")
+        self.h = h
+
+    def step(self, token: int, pos: int, logits=None, next=None, stream=None) -> None:
+        """Device tensors logits [vocab] fp32 / next [1] int32, or None."""
+        check(lib().gguf_decoder_step(self.h, int(token), int(pos), logits.data_ptr() if logits is not None else None,
+                                      next.data_ptr() if next is not None else None, stream), "gguf_decoder_step")
+
+    def step_dev(self, token, pos: int, logits=None, next=None, stream=None) -> None:
+        """token: device int32 tensor [1] (e.g. the previous step's next)."""
+        check(lib().gguf_decoder_step_dev(self.h, token.data_ptr(), int(pos),
+                                          logits.data_ptr() if logits is not None else None,
+                                          next.data_ptr() if next is not None else None, stream),
+              "gguf_decoder_step_dev")
+
+    def sync(self, stream=None) -> None:
+        check(lib().gguf_decoder_sync(self.h, stream), "gguf_decoder_sync")
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            lib().gguf_decoder_destroy(self.h)
+            self.h = None
+        for m in getattr(self, "moe", []):
+            m.close()
+        self.moe = []
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class _DeviceMoe:
+    """A gguf_moe handle over device copies made by `up` (Decoder's uploader)."""
+
+    def __init__(self, layer, up):
+        s = layer.spec
+        self.spec = s
+        self.router, self.gate, self.up, self.down = up(layer.router), up(layer.gate), up(layer.up), up(layer.down)
+        self.desc = GgufMoeDesc(s.dim, s.ffn_exp, s.n_experts, s.n_used, s.topk_renorm, s.router_type,
+                                s.gate_type, s.up_type, s.down_type, self.router.data_ptr(),
+                                self.gate.data_ptr(), self.up.data_ptr(), self.down.data_ptr(),
+                                self.gate.numel(), self.up.numel(), self.down.numel())
+        h = C.c_void_p()
+        check(lib().gguf_moe_create(C.byref(self.desc), C.byref(h)), "gguf_moe_create")
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().gguf_moe_destroy(self.h)
+            self.h = None

@@ -1,0 +1,454 @@
+// The decoder forward pass around the MoE block (include/gguf_decoder.h):
+// one decode step of the reference's forward() (vireo src/gguf_run.c:216-252)
+// on the device.  The projections and the LM head run on the quantised
+// mat-vec engine of gguf_matmul_dev; the MoE block is gguf_moe_ffn; this file
+// adds the small kernels in between: RMSNorm (fused with the residual add),
+// the q/k post-processing (bias, QK norm, NEOX RoPE, KV append), exact
+// attention over the KV cache (split over position chunks, merged with the
+// online-softmax rule of the reference's KV store) and the greedy argmax.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <vector>
+
+#include "gguf_decoder.h"
+#include "vireo_internal.h"
+#include "vireo_ptx.cuh"
+
+namespace vireo {
+
+constexpr int kDecThreads = 1024;
+constexpr int kAttnChunk = 256;  // cached positions per attention CTA
+constexpr int kAttnWarps = 4;
+constexpr int kMaxHeadSize = 256;
+
+VDEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// block-wide sum, every thread gets the total (blockDim.x a multiple of 32)
+VDEV float block_sum(float v, float* red) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < nw; i++) t += red[i];
+  return t;
+}
+
+// x (+)= y, then out = x * (1 / sqrt(mean(x^2) + eps)) * w  (rmsnorm,
+// gguf_run.c:161-165; with y the residual add of gguf_run.c:237 first)
+__global__ void __launch_bounds__(kDecThreads) dec_rmsnorm(float* x, const float* y, const float* w, float* out, int n,
+                                                           float eps) {
+  __shared__ float red[32];
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float v = x[i];
+    if (y) {
+      v = v + y[i];
+      x[i] = v;
+    }
+    ss += v * v;
+  }
+  ss = block_sum(ss, red);
+  const float r = 1.0f / sqrtf(ss / (float)n + eps);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = x[i] * r * w[i];
+}
+
+struct AttnPrepParams {
+  float *q, *k, *v;
+  const float *bq, *bk, *bv;
+  const float *qn, *kn;
+  int qn_len, kn_len;
+  int nh, nkv, hs, pos, max_ctx, f16;
+  float eps, base;
+  void *kc, *vc;  // this layer's caches, [nkv][max_ctx][hs]
+};
+
+// RMSNorm of `nv` heads of hs values in place, per head (len == hs) or over
+// the whole vector (len == nv hs); the caller syncs before and after
+VDEV void qk_norm(float* v, int nv, int hs, const float* w, int len, float eps, float* red) {
+  if (len == hs) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int h = warp; h < nv; h += nw) {
+      float* p = v + (size_t)h * hs;
+      float ss = 0.f;
+      for (int i = lane; i < hs; i += 32) ss += p[i] * p[i];
+      ss = warp_sum(ss);
+      const float r = 1.0f / sqrtf(ss / (float)hs + eps);
+      for (int i = lane; i < hs; i += 32) p[i] = p[i] * r * w[i];
+    }
+  } else {
+    const int n = nv * hs;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ss += v[i] * v[i];
+    ss = block_sum(ss, red);
+    const float r = 1.0f / sqrtf(ss / (float)n + eps);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) v[i] = v[i] * r * w[i];
+  }
+}
+
+// bias (gguf_run.c:223-225), QK norm (:226-229), NEOX RoPE (:230-231,
+// rope_neox :168-173) and the KV append (:232-233), one CTA
+__global__ void __launch_bounds__(kDecThreads) dec_attn_prep(const __grid_constant__ AttnPrepParams p) {
+  __shared__ float red[32];
+  const int nq = p.nh * p.hs, nk = p.nkv * p.hs;
+  for (int i = threadIdx.x; i < nq; i += blockDim.x)
+    if (p.bq) p.q[i] = p.q[i] + p.bq[i];
+  for (int i = threadIdx.x; i < nk; i += blockDim.x) {
+    if (p.bk) p.k[i] = p.k[i] + p.bk[i];
+    if (p.bv) p.v[i] = p.v[i] + p.bv[i];
+  }
+  __syncthreads();
+  if (p.qn) qk_norm(p.q, p.nh, p.hs, p.qn, p.qn_len, p.eps, red);
+  __syncthreads();
+  if (p.kn) qk_norm(p.k, p.nkv, p.hs, p.kn, p.kn_len, p.eps, red);
+  __syncthreads();
+  const int half = p.hs / 2, pairs = (p.nh + p.nkv) * half;
+  for (int idx = threadIdx.x; idx < pairs; idx += blockDim.x) {
+    const int h = idx / half, j = idx - h * half;
+    float* v = h < p.nh ? p.q + (size_t)h * p.hs : p.k + (size_t)(h - p.nh) * p.hs;
+    const float freq = powf(p.base, -2.0f * j / p.hs);
+    const float a = (float)p.pos * freq;
+    const float c = cosf(a), s = sinf(a);
+    const float x0 = v[j], x1 = v[j + half];
+    v[j] = x0 * c - x1 * s;
+    v[j + half] = x0 * s + x1 * c;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < nk; i += blockDim.x) {
+    const int kh = i / p.hs, e = i - kh * p.hs;
+    const size_t at = ((size_t)kh * p.max_ctx + p.pos) * p.hs + e;
+    if (p.f16) {
+      reinterpret_cast<__half*>(p.kc)[at] = __float2half_rn(p.k[i]);
+      reinterpret_cast<__half*>(p.vc)[at] = __float2half_rn(p.v[i]);
+    } else {
+      reinterpret_cast<float*>(p.kc)[at] = p.k[i];
+      reinterpret_cast<float*>(p.vc)[at] = p.v[i];
+    }
+  }
+}
+
+struct AttnParams {
+  const float* q;
+  const void *kc, *vc;
+  int nh, nkv, hs, npos, max_ctx, nchunk;
+  float scale;
+  float* part;  // [nh][nchunk][hs + 2]: acc, m, l
+};
+
+VDEV float kv_load(const float* p, size_t i) { return p[i]; }
+VDEV float kv_load(const __half* p, size_t i) { return __half2float(p[i]); }
+
+// One (position chunk, q head): the reference's online softmax step
+// (kvstore.h:90-98) over the chunk's positions, split over 4 warps, then the
+// warps' states merged; the chunk's state goes to part.
+template <class KT>
+__global__ void __launch_bounds__(32 * kAttnWarps) dec_attn_partial(const __grid_constant__ AttnParams p) {
+  __shared__ float sm_m[kAttnWarps], sm_l[kAttnWarps];
+  __shared__ float sm_acc[kAttnWarps][kMaxHeadSize];
+  const int c = blockIdx.x, h = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kh = h / (p.nh / p.nkv), nr = p.hs / 32;
+  const KT* kb = reinterpret_cast<const KT*>(p.kc) + (size_t)kh * p.max_ctx * p.hs;
+  const KT* vb = reinterpret_cast<const KT*>(p.vc) + (size_t)kh * p.max_ctx * p.hs;
+  float q[kMaxHeadSize / 32], acc[kMaxHeadSize / 32];
+#pragma unroll
+  for (int r = 0; r < kMaxHeadSize / 32; r++) {
+    q[r] = r < nr ? p.q[(size_t)h * p.hs + lane + 32 * r] : 0.f;
+    acc[r] = 0.f;
+  }
+  float m = -INFINITY, l = 0.f;
+  const int t0 = c * kAttnChunk, t1 = min(t0 + kAttnChunk, p.npos);
+  for (int t = t0 + warp; t < t1; t += kAttnWarps) {
+    const size_t row = (size_t)t * p.hs;
+    float s = 0.f;
+#pragma unroll
+    for (int r = 0; r < kMaxHeadSize / 32; r++)
+      if (r < nr) s += q[r] * kv_load(kb, row + lane + 32 * r);
+    s = warp_sum(s) * p.scale;
+    const float nm = s > m ? s : m;
+    const float cf = expf(m - nm), pe = expf(s - nm);
+    l = l * cf + pe;
+#pragma unroll
+    for (int r = 0; r < kMaxHeadSize / 32; r++)
+      if (r < nr) acc[r] = acc[r] * cf + pe * kv_load(vb, row + lane + 32 * r);
+    m = nm;
+  }
+  if (lane == 0) {
+    sm_m[warp] = m;
+    sm_l[warp] = l;
+  }
+#pragma unroll
+  for (int r = 0; r < kMaxHeadSize / 32; r++)
+    if (r < nr) sm_acc[warp][lane + 32 * r] = acc[r];
+  __syncthreads();
+  float M = -INFINITY;
+  for (int w = 0; w < kAttnWarps; w++) M = fmaxf(M, sm_m[w]);
+  float* out = p.part + ((size_t)h * p.nchunk + c) * (p.hs + 2);
+  for (int i = threadIdx.x; i < p.hs; i += blockDim.x) {
+    float a = 0.f;
+    for (int w = 0; w < kAttnWarps; w++)
+      if (sm_m[w] > -INFINITY) a += sm_acc[w][i] * expf(sm_m[w] - M);
+    out[i] = a;
+  }
+  if (threadIdx.x == 0) {
+    float L = 0.f;
+    for (int w = 0; w < kAttnWarps; w++)
+      if (sm_m[w] > -INFINITY) L += sm_l[w] * expf(sm_m[w] - M);
+    out[p.hs] = M;
+    out[p.hs + 1] = L;
+  }
+}
+
+// the chunks' states merged; out = acc / l (kv_softmax_finish, kvstore.h:99-101)
+__global__ void dec_attn_combine(const __grid_constant__ AttnParams p, float* out) {
+  const int h = blockIdx.x;
+  const float* base = p.part + (size_t)h * p.nchunk * (p.hs + 2);
+  float M = -INFINITY;
+  for (int c = 0; c < p.nchunk; c++) M = fmaxf(M, base[(size_t)c * (p.hs + 2) + p.hs]);
+  for (int i = threadIdx.x; i < p.hs; i += blockDim.x) {
+    float a = 0.f, L = 0.f;
+    for (int c = 0; c < p.nchunk; c++) {
+      const float* pc = base + (size_t)c * (p.hs + 2);
+      if (pc[p.hs] > -INFINITY) {
+        const float f = expf(pc[p.hs] - M);
+        a += pc[i] * f;
+        L += pc[p.hs + 1] * f;
+      }
+    }
+    out[(size_t)h * p.hs + i] = L > 0.f ? a * (1.0f / L) : 0.f;
+  }
+}
+
+// greedy argmax (gguf_run.c:253): strict '>' from index 0, so the lowest id
+// wins ties and a NaN never wins
+__global__ void __launch_bounds__(kDecThreads) dec_argmax(const float* v, int n, int32_t* out) {
+  __shared__ float bv_s[32];
+  __shared__ int bi_s[32];
+  float bv = -INFINITY;
+  int bi = -1;
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    if (v[i] > bv || (bi < 0 && v[i] == bv)) {
+      bv = v[i];
+      bi = i;
+    }
+  // (value desc, index asc), empty (bi < 0) last
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    bv_s[warp] = bv;
+    bi_s[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = -INFINITY;
+    int ix = -1;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++)
+      if (bi_s[w] >= 0 && (ix < 0 || bv_s[w] > b || (bv_s[w] == b && bi_s[w] < ix))) {
+        b = bv_s[w];
+        ix = bi_s[w];
+      }
+    // the reference starts from v[0]: when v[0] is NaN nothing beats it
+    *out = (ix < 0 || isnan(v[0])) ? 0 : ix;
+  }
+}
+
+}  // namespace vireo
+
+using namespace vireo;
+
+struct gguf_decoder {
+  gguf_decoder_desc d;
+  std::vector<gguf_decoder_layer> L;
+  Ctx* c = nullptr;
+  float *x = nullptr, *xb = nullptr, *y = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr,
+        *part = nullptr, *logits = nullptr;
+  void *kc = nullptr, *vc = nullptr;
+  size_t layer_kv = 0;  // elements of one layer's K (or V) cache
+  int max_chunk = 0;
+};
+
+extern "C" {
+
+void gguf_decoder_destroy(gguf_decoder* dec) {
+  if (!dec) return;
+  for (void* p : {(void*)dec->x, (void*)dec->xb, (void*)dec->y, (void*)dec->q, (void*)dec->k, (void*)dec->v,
+                  (void*)dec->att, (void*)dec->part, (void*)dec->logits, dec->kc, dec->vc})
+    if (p) cudaFree(p);
+  delete dec;
+}
+
+int gguf_decoder_create(const gguf_decoder_desc* desc, const gguf_decoder_layer* layers, gguf_decoder** out) {
+  if (!desc || !layers || !out) return VIREO_ERR_ARG;
+  *out = nullptr;
+  int st;
+  Ctx* c = ctx_get(&st);
+  if (!c) return st;
+  const gguf_decoder_desc& D = *desc;
+  if (D.n_layers < 1 || D.dim < 1 || D.dim > 16384 || D.n_heads < 1 || D.n_kv_heads < 1 ||
+      D.n_heads % D.n_kv_heads || D.head_size < 32 || D.head_size % 32 || D.head_size > kMaxHeadSize ||
+      D.vocab < 1 || D.max_ctx < 1 || !D.tok_embd || !D.out_norm || !D.lm_head)
+    return VIREO_ERR_ARG;
+  int be, bb;
+  if (type_block(D.tok_embd_type, &be, &bb) || D.dim % be || type_block(D.lm_head_type, &be, &bb) || D.dim % be)
+    return VIREO_ERR_UNSUPPORTED;
+  const int nq = D.n_heads * D.head_size, nk = D.n_kv_heads * D.head_size;
+  for (int l = 0; l < D.n_layers; l++) {
+    const gguf_decoder_layer& y = layers[l];
+    if (!y.attn_norm || !y.ffn_norm || !y.wq || !y.wk || !y.wv || !y.wo || !y.moe) return VIREO_ERR_ARG;
+    if ((y.q_norm && y.q_norm_len != D.head_size && y.q_norm_len != nq) ||
+        (y.k_norm && y.k_norm_len != D.head_size && y.k_norm_len != nk))
+      return VIREO_ERR_ARG;
+    for (uint32_t t : {y.wq_type, y.wk_type, y.wv_type})
+      if (type_block(t, &be, &bb) || D.dim % be) return VIREO_ERR_UNSUPPORTED;
+    if (type_block(y.wo_type, &be, &bb) || nq % be) return VIREO_ERR_UNSUPPORTED;
+  }
+  gguf_decoder* dec = new gguf_decoder();
+  dec->d = D;
+  dec->L.assign(layers, layers + D.n_layers);
+  dec->c = c;
+  dec->max_chunk = (D.max_ctx + kAttnChunk - 1) / kAttnChunk;
+  dec->layer_kv = (size_t)D.n_kv_heads * D.max_ctx * D.head_size;
+  const size_t kvb = dec->layer_kv * D.n_layers * (D.kv_f16 ? 2 : 4);
+  if ((st = cuda_status(cudaMalloc(&dec->x, (size_t)D.dim * 4))) ||
+      (st = cuda_status(cudaMalloc(&dec->xb, (size_t)D.dim * 4))) ||
+      (st = cuda_status(cudaMalloc(&dec->y, (size_t)D.dim * 4))) ||
+      (st = cuda_status(cudaMalloc(&dec->q, (size_t)nq * 4))) ||
+      (st = cuda_status(cudaMalloc(&dec->k, (size_t)nk * 4))) ||
+      (st = cuda_status(cudaMalloc(&dec->v, (size_t)nk * 4))) ||
+      (st = cuda_status(cudaMalloc(&dec->att, (size_t)nq * 4))) ||
+      (st = cuda_status(cudaMalloc(&dec->part, (size_t)D.n_heads * dec->max_chunk * (D.head_size + 2) * 4))) ||
+      (st = cuda_status(cudaMalloc(&dec->logits, (size_t)D.vocab * 4))) ||
+      (st = cuda_status(cudaMalloc(&dec->kc, kvb))) || (st = cuda_status(cudaMalloc(&dec->vc, kvb))) ||
+      (st = cuda_status(cudaMemset(dec->x, 0, (size_t)D.dim * 4)))) {
+    gguf_decoder_destroy(dec);
+    return st;
+  }
+  *out = dec;
+  return VIREO_OK;
+}
+
+// one step; the token is a host value (token_dev NULL) or read on the device
+static int decoder_step(gguf_decoder* dec, int token, const int32_t* token_dev, int pos, float* logits, int32_t* next,
+                        void* stream) {
+  if (!dec) return VIREO_ERR_ARG;
+  const gguf_decoder_desc& D = dec->d;
+  if ((!token_dev && (token < 0 || token >= D.vocab)) || pos < 0 || pos >= D.max_ctx) return VIREO_ERR_ARG;
+  cudaStream_t s = stream ? (cudaStream_t)stream : dec->c->stream;
+  Ctx* c = dec->c;
+  const int d = D.dim, hs = D.head_size, nq = D.n_heads * hs, nk = D.n_kv_heads * hs;
+  int st;
+  // embedding row (gguf_run.c:218)
+  if (token_dev)
+    st = launch_embed(D.tok_embd_type, D.tok_embd, token_dev, D.vocab, dec->x, d, c->d_err, s);
+  else
+    st = launch_dequant(D.tok_embd_type, (const uint8_t*)D.tok_embd + (size_t)token * row_bytes(D.tok_embd_type, d),
+                        dec->x, d, s);
+  if (st) return st;
+  const int npos = pos + 1, nchunk = (npos + kAttnChunk - 1) / kAttnChunk;
+  const size_t kv_el = D.kv_f16 ? 2 : 4;
+  for (int l = 0; l < D.n_layers; l++) {
+    const gguf_decoder_layer& y = dec->L[l];
+    dec_rmsnorm<<<1, kDecThreads, 0, s>>>(dec->x, nullptr, y.attn_norm, dec->xb, d, D.eps);
+    if ((st = gemv_dev(c, y.wq_type, y.wq, dec->xb, dec->q, d, nq, s)) ||
+        (st = gemv_dev(c, y.wk_type, y.wk, dec->xb, dec->k, d, nk, s)) ||
+        (st = gemv_dev(c, y.wv_type, y.wv, dec->xb, dec->v, d, nk, s)))
+      return st;
+    AttnPrepParams ap;
+    ap.q = dec->q;
+    ap.k = dec->k;
+    ap.v = dec->v;
+    ap.bq = y.bq;
+    ap.bk = y.bk;
+    ap.bv = y.bv;
+    ap.qn = y.q_norm;
+    ap.kn = y.k_norm;
+    ap.qn_len = y.q_norm_len;
+    ap.kn_len = y.k_norm_len;
+    ap.nh = D.n_heads;
+    ap.nkv = D.n_kv_heads;
+    ap.hs = hs;
+    ap.pos = pos;
+    ap.max_ctx = D.max_ctx;
+    ap.f16 = D.kv_f16;
+    ap.eps = D.eps;
+    ap.base = D.rope_base;
+    ap.kc = (uint8_t*)dec->kc + (size_t)l * dec->layer_kv * kv_el;
+    ap.vc = (uint8_t*)dec->vc + (size_t)l * dec->layer_kv * kv_el;
+    dec_attn_prep<<<1, kDecThreads, 0, s>>>(ap);
+    AttnParams at;
+    at.q = dec->q;
+    at.kc = ap.kc;
+    at.vc = ap.vc;
+    at.nh = D.n_heads;
+    at.nkv = D.n_kv_heads;
+    at.hs = hs;
+    at.npos = npos;
+    at.max_ctx = D.max_ctx;
+    at.nchunk = nchunk;
+    at.scale = 1.0f / sqrtf((float)hs);
+    at.part = dec->part;
+    if (D.kv_f16)
+      dec_attn_partial<__half><<<dim3(nchunk, D.n_heads), 32 * kAttnWarps, 0, s>>>(at);
+    else
+      dec_attn_partial<float><<<dim3(nchunk, D.n_heads), 32 * kAttnWarps, 0, s>>>(at);
+    dec_attn_combine<<<D.n_heads, hs, 0, s>>>(at, dec->att);
+    if ((st = gemv_dev(c, y.wo_type, y.wo, dec->att, dec->y, nq, d, s))) return st;
+    // x += attention output; xb = ffn_norm(x)   (gguf_run.c:237-238)
+    dec_rmsnorm<<<1, kDecThreads, 0, s>>>(dec->x, dec->y, y.ffn_norm, dec->xb, d, D.eps);
+    // x += MoE(xb)   (gguf_run.c:239)
+    if ((st = gguf_moe_ffn(y.moe, dec->xb, dec->x, 1, nullptr, nullptr, s))) return st;
+  }
+  if (logits || next) {
+    float* lg = logits ? logits : dec->logits;
+    dec_rmsnorm<<<1, kDecThreads, 0, s>>>(dec->x, nullptr, D.out_norm, dec->xb, d, D.eps);
+    if ((st = gemv_dev(c, D.lm_head_type, D.lm_head, dec->xb, lg, d, D.vocab, s))) return st;
+    if (next) dec_argmax<<<1, kDecThreads, 0, s>>>(lg, D.vocab, next);
+  }
+  return cuda_status(cudaGetLastError());
+}
+
+int gguf_decoder_step(gguf_decoder* dec, int token, int pos, float* logits, int32_t* next, void* stream) {
+  return decoder_step(dec, token, nullptr, pos, logits, next, stream);
+}
+
+int gguf_decoder_step_dev(gguf_decoder* dec, const int32_t* token, int pos, float* logits, int32_t* next,
+                          void* stream) {
+  if (!token) return VIREO_ERR_ARG;
+  return decoder_step(dec, 0, token, pos, logits, next, stream);
+}
+
+const float* gguf_decoder_hidden(const gguf_decoder* dec) { return dec ? dec->x : nullptr; }
+
+int gguf_decoder_sync(gguf_decoder* dec, void* stream) {
+  if (!dec) return VIREO_ERR_ARG;
+  cudaStream_t s = stream ? (cudaStream_t)stream : dec->c->stream;
+  int st = cuda_status(cudaStreamSynchronize(s));
+  if (st) return st;
+  int herr = 0;
+  if ((st = cuda_status(cudaMemcpy(&herr, dec->c->d_err, sizeof(int), cudaMemcpyDeviceToHost)))) return st;
+  if (herr) {
+    cudaMemset(dec->c->d_err, 0, sizeof(int));
+    return herr;
+  }
+  for (const auto& y : dec->L)
+    if ((st = gguf_moe_sync(y.moe, stream))) return st;
+  return VIREO_OK;
+}
+
+}  // extern "C"

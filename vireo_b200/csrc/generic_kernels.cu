@@ -81,6 +81,19 @@ __global__ void dequant_kernel(uint32_t type, const uint8_t* src, float* dst, in
     dst[i] = deq_elem(type, src, i);
 }
 
+// one row of an embedding table, the row index read from device memory
+// (a token id another kernel wrote, e.g. the previous step's argmax); an id
+// outside [0, vocab) gives zeros and records VIREO_ERR_ARG
+__global__ void embed_kernel(uint32_t type, const uint8_t* table, uint64_t rb, const int32_t* token, int vocab,
+                             float* dst, int n, int* err) {
+  const int t = *token;
+  const bool ok = t >= 0 && t < vocab;
+  if (!ok && blockIdx.x == 0 && threadIdx.x == 0) atomicCAS(err, 0, VIREO_ERR_ARG);
+  const uint8_t* row = table + (ok ? (uint64_t)t * rb : 0);
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    dst[i] = ok ? deq_elem(type, row, i) : 0.f;
+}
+
 // one warp per row; lanes stride over K, then a fixed xor-tree reduction
 __global__ void gemv_generic_kernel(uint32_t type, const uint8_t* w, const float* x, float* y, int n, int d,
                                     uint64_t rb) {
@@ -102,6 +115,15 @@ int launch_dequant(uint32_t type, const void* src, float* dst, int n, cudaStream
   int blocks = (n + 255) / 256;
   if (blocks > 4096) blocks = 4096;
   dequant_kernel<<<blocks, 256, 0, s>>>(type, (const uint8_t*)src, dst, n);
+  return cuda_status(cudaGetLastError());
+}
+
+int launch_embed(uint32_t type, const void* table, const int32_t* token, int vocab, float* dst, int n, int* err,
+                 cudaStream_t s) {
+  int be, bb;
+  if (type_block(type, &be, &bb) || n <= 0 || n % be) return VIREO_ERR_UNSUPPORTED;
+  embed_kernel<<<(n + 255) / 256, 256, 0, s>>>(type, (const uint8_t*)table, row_bytes(type, n), token, vocab, dst, n,
+                                               err);
   return cuda_status(cudaGetLastError());
 }
 

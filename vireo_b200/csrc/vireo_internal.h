@@ -92,6 +92,8 @@ int prefill_tile_rows();  // rows per activation tile (row ranges per expert are
 // generic kernels (any supported type/shape), generic_kernels.cu
 int launch_dequant(uint32_t type, const void* src, float* dst, int n, cudaStream_t s);
 int launch_gemv_generic(uint32_t type, const void* w, const float* x, float* y, int n, int d, cudaStream_t s);
+int launch_embed(uint32_t type, const void* table, const int32_t* token, int vocab, float* dst, int n, int* err,
+                 cudaStream_t s);
 
 // process-wide device context
 struct HostRange {

@@ -275,3 +275,118 @@ def olmoe_q4km_layer() -> MoeLayerSpec:
 def qwen3_layer() -> MoeLayerSpec:
     """Configs 3-5: Qwen3-30B-A3B-shaped layer, 128 experts top-8 renorm."""
     return MoeLayerSpec(2048, 768, 128, 8, 1, GGML_Q4_K, GGML_Q4_K, GGML_Q6_K)
+
+
+# ---------------------------------------------------------------------------
+# whole decoders (configs 2 and 3): attention + MoE layers
+# ---------------------------------------------------------------------------
+
+class DecoderSpec:
+    """Shapes and formats of a MoE decoder (the Model fields of the reference
+    runner, gguf_run.c:146-155).  qk_norm: "full" (one RMSNorm over all heads,
+    OLMoE), "head" (per-head, Qwen3) or None."""
+
+    def __init__(self, n_layers, dim, n_heads, n_kv_heads, head_size, vocab, moe: MoeLayerSpec,
+                 qk_norm="full", attn_type=GGML_Q4_K, embd_type=GGML_Q4_K, lm_type=GGML_Q6_K,
+                 eps=1e-5, rope_base=10000.0):
+        self.n_layers, self.dim, self.n_heads, self.n_kv_heads = n_layers, dim, n_heads, n_kv_heads
+        self.head_size, self.vocab, self.moe, self.qk_norm = head_size, vocab, moe, qk_norm
+        self.attn_type, self.embd_type, self.lm_type = attn_type, embd_type, lm_type
+        self.eps, self.rope_base = float(eps), float(rope_base)
+        assert moe.dim == dim
+
+    @property
+    def q_dim(self):
+        return self.n_heads * self.head_size
+
+    @property
+    def kv_dim(self):
+        return self.n_kv_heads * self.head_size
+
+    def attn_bytes(self):
+        """Weight bytes of one layer's attention block (q, k, v, o matrices
+        and the F32 norm vectors)."""
+        rb = row_bytes
+        b = self.q_dim * rb(self.attn_type, self.dim) + 2 * self.kv_dim * rb(self.attn_type, self.dim)
+        b += self.dim * rb(self.attn_type, self.q_dim) + 2 * 4 * self.dim
+        if self.qk_norm == "full":
+            b += 4 * (self.q_dim + self.kv_dim)
+        elif self.qk_norm == "head":
+            b += 8 * self.head_size
+        return b
+
+    def weight_bytes_per_token(self):
+        """Algorithmic weight bytes of one decode step with logits: every
+        layer's attention and router rows and its n_used experts, the final
+        norm, the LM head, and one embedding row."""
+        m = self.moe
+        per_layer = self.attn_bytes() + m.router_bytes + m.n_used * m.expert_bytes
+        return self.n_layers * per_layer + self.vocab * row_bytes(self.lm_type, self.dim) + 4 * self.dim \
+            + row_bytes(self.embd_type, self.dim)
+
+    def kv_bytes_per_position(self, elem_bytes=2):
+        """KV cache bytes read per cached position per decode step."""
+        return self.n_layers * 2 * self.kv_dim * elem_bytes
+
+
+class DecoderLayer:
+    def __init__(self, spec: DecoderSpec, seed: int, layer: int):
+        s = spec
+        base = 100000 + 100 * layer
+        self.attn_norm = (1.0 + 0.1 * normal(seed, base + 1, s.dim)).astype(np.float32)
+        self.ffn_norm = (1.0 + 0.1 * normal(seed, base + 2, s.dim)).astype(np.float32)
+        self.wq = tensor(s.attn_type, seed, base + 3, s.q_dim, s.dim)
+        self.wk = tensor(s.attn_type, seed, base + 4, s.kv_dim, s.dim)
+        self.wv = tensor(s.attn_type, seed, base + 5, s.kv_dim, s.dim)
+        self.wo = tensor(s.attn_type, seed, base + 6, s.dim, s.q_dim)
+        if s.qk_norm == "full":
+            self.q_norm = (1.0 + 0.1 * normal(seed, base + 7, s.q_dim)).astype(np.float32)
+            self.k_norm = (1.0 + 0.1 * normal(seed, base + 8, s.kv_dim)).astype(np.float32)
+        elif s.qk_norm == "head":
+            self.q_norm = (1.0 + 0.1 * normal(seed, base + 7, s.head_size)).astype(np.float32)
+            self.k_norm = (1.0 + 0.1 * normal(seed, base + 8, s.head_size)).astype(np.float32)
+        else:
+            self.q_norm = self.k_norm = None
+        self.moe = MoeLayer(s.moe, seed, layer=layer)
+
+
+class Decoder:
+    """A generated decoder: embedding, layers, final norm, LM head."""
+
+    def __init__(self, spec: DecoderSpec, seed: int, n_distinct_layers: int | None = None):
+        """n_distinct_layers: generate only that many layers and repeat them
+        (large configurations, where the device copies still get distinct
+        addresses per layer)."""
+        s = spec
+        self.spec, self.seed = s, seed
+        self.tok_embd = tensor(s.embd_type, seed, 90001, s.vocab, s.dim)
+        self.out_norm = (1.0 + 0.1 * normal(seed, 90002, s.dim)).astype(np.float32)
+        self.lm_head = tensor(s.lm_type, seed, 90003, s.vocab, s.dim)
+        nd = s.n_layers if n_distinct_layers is None else max(1, min(n_distinct_layers, s.n_layers))
+        made = [DecoderLayer(s, seed, l) for l in range(nd)]
+        self.layers = [made[l % nd] for l in range(s.n_layers)]
+
+
+def tiny_olmoe_decoder(n_layers=2) -> DecoderSpec:
+    return DecoderSpec(n_layers, 512, 4, 4, 128, 512,
+                       MoeLayerSpec(512, 256, 16, 4, 0, GGML_Q4_K, GGML_Q4_K, GGML_Q6_K), qk_norm="full")
+
+
+def tiny_qwen3_decoder(n_layers=2) -> DecoderSpec:
+    return DecoderSpec(n_layers, 512, 8, 2, 128, 768,
+                       MoeLayerSpec(512, 256, 32, 8, 1, GGML_Q4_K, GGML_Q4_K, GGML_Q6_K), qk_norm="head",
+                       eps=1e-6, rope_base=1000000.0)
+
+
+def olmoe_decoder() -> DecoderSpec:
+    """Config 2: OLMoE-1B-7B-shaped, 16 layers, 16 heads x 128, full-width QK
+    norm, vocab 50304, 64 experts top-8 (no renorm), Q4_K attention and
+    gate/up, Q6_K down and LM head."""
+    return DecoderSpec(16, 2048, 16, 16, 128, 50304, olmoe_q4km_layer(), qk_norm="full")
+
+
+def qwen3_decoder() -> DecoderSpec:
+    """Config 3: Qwen3-30B-A3B-shaped, 48 layers, 32 q / 4 kv heads x 128,
+    per-head QK norm, vocab 151936, 128 experts top-8 renormalised."""
+    return DecoderSpec(48, 2048, 32, 4, 128, 151936, qwen3_layer(), qk_norm="head", eps=1e-6,
+                       rope_base=1000000.0)
