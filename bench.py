@@ -653,7 +653,7 @@ def run_decoder(args, wl):
                 "cpu_baseline": cpu,
                 "e2e": {"value": e2e_tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4,
                         "note": "gguf_decoder_step with a host token id per step, next token read back"},
-                "gpu_launches": gen * (1 + 10 * spec.n_layers + 3), "clocks": clk.summary()}
+                "gpu_launches": gen * (8 * spec.n_layers + 4), "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
     G.close()
     if world > 1:

@@ -54,7 +54,9 @@ typedef struct {
 
 typedef struct gguf_decoder gguf_decoder;
 
-/* Validates the shapes and allocates the KV cache and the activations. */
+/* Validates the shapes and allocates the KV cache and the activations.
+ * Supported: head_size 64 or 128, n_heads / n_kv_heads in
+ * {1, 2, 4, 8}, dim <= 16384. */
 int gguf_decoder_create(const gguf_decoder_desc *desc, const gguf_decoder_layer *layers, gguf_decoder **out);
 
 /* One decode step (forward(m, token, pos, want_logits), gguf_run.c:216):

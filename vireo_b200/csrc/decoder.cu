@@ -21,9 +21,7 @@
 namespace vireo {
 
 constexpr int kDecThreads = 1024;
-constexpr int kAttnChunk = 256;  // cached positions per attention CTA
-constexpr int kAttnWarps = 4;
-constexpr int kMaxHeadSize = 256;
+constexpr int kAttnChunk = 128;  // cached positions per attention CTA (one per thread)
 
 VDEV float warp_sum(float v) {
 #pragma unroll
@@ -63,6 +61,7 @@ __global__ void __launch_bounds__(kDecThreads) dec_rmsnorm(float* x, const float
 }
 
 struct AttnPrepParams {
+  const float* freq;  // [hs / 2] RoPE frequencies, base^(-2j/hs)
   float *q, *k, *v;
   const float *bq, *bk, *bv;
   const float *qn, *kn;
@@ -96,42 +95,47 @@ VDEV void qk_norm(float* v, int nv, int hs, const float* w, int len, float eps, 
 }
 
 // bias (gguf_run.c:223-225), QK norm (:226-229), NEOX RoPE (:230-231,
-// rope_neox :168-173) and the KV append (:232-233), one CTA
+// rope_neox :168-173) and the KV append (:232-233), one CTA; q, k and v are
+// staged in shared memory (dynamic, (nq + 2 nk) floats) so that the steps
+// between the one read and the one write are on-chip
 __global__ void __launch_bounds__(kDecThreads) dec_attn_prep(const __grid_constant__ AttnPrepParams p) {
+  extern __shared__ float prep_sh[];
   __shared__ float red[32];
   const int nq = p.nh * p.hs, nk = p.nkv * p.hs;
-  for (int i = threadIdx.x; i < nq; i += blockDim.x)
-    if (p.bq) p.q[i] = p.q[i] + p.bq[i];
+  float* q = prep_sh;
+  float* k = q + nq;
+  float* v = k + nk;
+  for (int i = threadIdx.x; i < nq; i += blockDim.x) q[i] = p.bq ? p.q[i] + p.bq[i] : p.q[i];
   for (int i = threadIdx.x; i < nk; i += blockDim.x) {
-    if (p.bk) p.k[i] = p.k[i] + p.bk[i];
-    if (p.bv) p.v[i] = p.v[i] + p.bv[i];
+    k[i] = p.bk ? p.k[i] + p.bk[i] : p.k[i];
+    v[i] = p.bv ? p.v[i] + p.bv[i] : p.v[i];
   }
   __syncthreads();
-  if (p.qn) qk_norm(p.q, p.nh, p.hs, p.qn, p.qn_len, p.eps, red);
+  if (p.qn) qk_norm(q, p.nh, p.hs, p.qn, p.qn_len, p.eps, red);
   __syncthreads();
-  if (p.kn) qk_norm(p.k, p.nkv, p.hs, p.kn, p.kn_len, p.eps, red);
+  if (p.kn) qk_norm(k, p.nkv, p.hs, p.kn, p.kn_len, p.eps, red);
   __syncthreads();
   const int half = p.hs / 2, pairs = (p.nh + p.nkv) * half;
   for (int idx = threadIdx.x; idx < pairs; idx += blockDim.x) {
     const int h = idx / half, j = idx - h * half;
-    float* v = h < p.nh ? p.q + (size_t)h * p.hs : p.k + (size_t)(h - p.nh) * p.hs;
-    const float freq = powf(p.base, -2.0f * j / p.hs);
-    const float a = (float)p.pos * freq;
+    float* w = h < p.nh ? q + (size_t)h * p.hs : k + (size_t)(h - p.nh) * p.hs;
+    const float a = (float)p.pos * p.freq[j];
     const float c = cosf(a), s = sinf(a);
-    const float x0 = v[j], x1 = v[j + half];
-    v[j] = x0 * c - x1 * s;
-    v[j + half] = x0 * s + x1 * c;
+    const float x0 = w[j], x1 = w[j + half];
+    w[j] = x0 * c - x1 * s;
+    w[j + half] = x0 * s + x1 * c;
   }
   __syncthreads();
+  for (int i = threadIdx.x; i < nq; i += blockDim.x) p.q[i] = q[i];
   for (int i = threadIdx.x; i < nk; i += blockDim.x) {
     const int kh = i / p.hs, e = i - kh * p.hs;
     const size_t at = ((size_t)kh * p.max_ctx + p.pos) * p.hs + e;
     if (p.f16) {
-      reinterpret_cast<__half*>(p.kc)[at] = __float2half_rn(p.k[i]);
-      reinterpret_cast<__half*>(p.vc)[at] = __float2half_rn(p.v[i]);
+      reinterpret_cast<__half*>(p.kc)[at] = __float2half_rn(k[i]);
+      reinterpret_cast<__half*>(p.vc)[at] = __float2half_rn(v[i]);
     } else {
-      reinterpret_cast<float*>(p.kc)[at] = p.k[i];
-      reinterpret_cast<float*>(p.vc)[at] = p.v[i];
+      reinterpret_cast<float*>(p.kc)[at] = k[i];
+      reinterpret_cast<float*>(p.vc)[at] = v[i];
     }
   }
 }
@@ -147,64 +151,146 @@ struct AttnParams {
 VDEV float kv_load(const float* p, size_t i) { return p[i]; }
 VDEV float kv_load(const __half* p, size_t i) { return __half2float(p[i]); }
 
-// One (position chunk, q head): the reference's online softmax step
-// (kvstore.h:90-98) over the chunk's positions, split over 4 warps, then the
-// warps' states merged; the chunk's state goes to part.
-template <class KT>
-__global__ void __launch_bounds__(32 * kAttnWarps) dec_attn_partial(const __grid_constant__ AttnParams p) {
-  __shared__ float sm_m[kAttnWarps], sm_l[kAttnWarps];
-  __shared__ float sm_acc[kAttnWarps][kMaxHeadSize];
-  const int c = blockIdx.x, h = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kh = h / (p.nh / p.nkv), nr = p.hs / 32;
-  const KT* kb = reinterpret_cast<const KT*>(p.kc) + (size_t)kh * p.max_ctx * p.hs;
-  const KT* vb = reinterpret_cast<const KT*>(p.vc) + (size_t)kh * p.max_ctx * p.hs;
-  float q[kMaxHeadSize / 32], acc[kMaxHeadSize / 32];
+// 8 consecutive cache values starting at element i (i a multiple of 8)
+VDEV void kv_load8(const float* p, size_t i, float (&o)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p + i), b = *reinterpret_cast<const float4*>(p + i + 4);
+  o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+}
+VDEV void kv_load8(const __half* p, size_t i, float (&o)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p + i);
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
-  for (int r = 0; r < kMaxHeadSize / 32; r++) {
-    q[r] = r < nr ? p.q[(size_t)h * p.hs + lane + 32 * r] : 0.f;
-    acc[r] = 0.f;
+  for (int j = 0; j < 4; j++) {
+    const float2 f = __half22float2(h[j]);
+    o[2 * j] = f.x;
+    o[2 * j + 1] = f.y;
   }
-  float m = -INFINITY, l = 0.f;
-  const int t0 = c * kAttnChunk, t1 = min(t0 + kAttnChunk, p.npos);
-  for (int t = t0 + warp; t < t1; t += kAttnWarps) {
-    const size_t row = (size_t)t * p.hs;
-    float s = 0.f;
-#pragma unroll
-    for (int r = 0; r < kMaxHeadSize / 32; r++)
-      if (r < nr) s += q[r] * kv_load(kb, row + lane + 32 * r);
-    s = warp_sum(s) * p.scale;
-    const float nm = s > m ? s : m;
-    const float cf = expf(m - nm), pe = expf(s - nm);
-    l = l * cf + pe;
-#pragma unroll
-    for (int r = 0; r < kMaxHeadSize / 32; r++)
-      if (r < nr) acc[r] = acc[r] * cf + pe * kv_load(vb, row + lane + 32 * r);
-    m = nm;
-  }
-  if (lane == 0) {
-    sm_m[warp] = m;
-    sm_l[warp] = l;
-  }
-#pragma unroll
-  for (int r = 0; r < kMaxHeadSize / 32; r++)
-    if (r < nr) sm_acc[warp][lane + 32 * r] = acc[r];
+}
+
+// One (chunk of kAttnChunk positions, kv head) with all QG q heads that
+// share the kv head (GQA).  Scores: thread t takes position t, reads its key
+// row once (HS/8 16-byte loads in flight) and scores it against every q head.
+// The chunk's softmax state per q head is formed (max, exp, sum).  Values:
+// thread (dg, pg) accumulates dimensions 8 dg .. 8 dg + 7 over positions
+// pg, pg + PG, ... with 16-byte loads, and the position groups are summed.
+// The state (acc, m, l) of each (q head, chunk) goes to part and
+// dec_attn_combine merges the chunks: the reference's softmax attention
+// (kvstore.h:77-101) evaluated chunk-parallel instead of one position at a time.
+template <class KT, int QG, int HS>
+__global__ void __launch_bounds__(kAttnChunk) dec_attn_partial(const __grid_constant__ AttnParams p) {
+  constexpr int DG = HS / 8, PG = kAttnChunk / DG, NW = kAttnChunk / 32;
+  __shared__ __align__(16) float sq[QG][HS];
+  __shared__ float sp[QG][kAttnChunk];
+  __shared__ float red[QG][NW];
+  __shared__ float racc[NW][QG * HS];
+  const int c = blockIdx.x, kh = blockIdx.y, t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int h0 = kh * QG;
+  const KT* kb = reinterpret_cast<const KT*>(p.kc) + (size_t)kh * p.max_ctx * HS;
+  const KT* vb = reinterpret_cast<const KT*>(p.vc) + (size_t)kh * p.max_ctx * HS;
+  for (int i = t; i < QG * HS; i += kAttnChunk) sq[i / HS][i % HS] = p.q[(size_t)h0 * HS + i];
   __syncthreads();
-  float M = -INFINITY;
-  for (int w = 0; w < kAttnWarps; w++) M = fmaxf(M, sm_m[w]);
-  float* out = p.part + ((size_t)h * p.nchunk + c) * (p.hs + 2);
-  for (int i = threadIdx.x; i < p.hs; i += blockDim.x) {
+  const int n = min(kAttnChunk, p.npos - c * kAttnChunk);
+  const bool live = t < n;
+  float s[QG];
+#pragma unroll
+  for (int g = 0; g < QG; g++) s[g] = 0.f;
+  if (live) {
+    const size_t row = ((size_t)c * kAttnChunk + t) * HS;
+#pragma unroll
+    for (int i = 0; i < HS; i += 8) {
+      float e[8];
+      kv_load8(kb, row + i, e);
+#pragma unroll
+      for (int g = 0; g < QG; g++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) s[g] += sq[g][i + j] * e[j];
+    }
+  }
+  // chunk max and sum per q head
+#pragma unroll
+  for (int g = 0; g < QG; g++) {
+    float v = live ? s[g] * p.scale : -INFINITY;
+    s[g] = v;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) red[g][warp] = v;
+  }
+  __syncthreads();
+  float M[QG];
+#pragma unroll
+  for (int g = 0; g < QG; g++) {
+    float m = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; w++) m = fmaxf(m, red[g][w]);
+    M[g] = m;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < QG; g++) {
+    const float e = live ? expf(s[g] - M[g]) : 0.f;
+    sp[g][t] = e;
+    float v = e;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[g][warp] = v;
+  }
+  __syncthreads();
+  // values: thread (dg, pg), 8 dimensions x the chunk's positions pg + PG u
+  const int dg = t % DG, pg = t / DG;
+  float acc[QG][8];
+#pragma unroll
+  for (int g = 0; g < QG; g++)
+#pragma unroll
+    for (int j = 0; j < 8; j++) acc[g][j] = 0.f;
+  const size_t vbase = (size_t)c * kAttnChunk * HS + 8 * dg;
+#pragma unroll 4
+  for (int u = pg; u < n; u += PG) {
+    float v[8];
+    kv_load8(vb, vbase + (size_t)u * HS, v);
+#pragma unroll
+    for (int g = 0; g < QG; g++) {
+      const float w = sp[g][u];
+#pragma unroll
+      for (int j = 0; j < 8; j++) acc[g][j] += w * v[j];
+    }
+  }
+  // sum the position groups: lanes with the same dg within a warp, then warps
+#pragma unroll
+  for (int o = DG; o < 32; o <<= 1)
+#pragma unroll
+    for (int g = 0; g < QG; g++)
+#pragma unroll
+      for (int j = 0; j < 8; j++) acc[g][j] += __shfl_xor_sync(0xffffffffu, acc[g][j], o);
+  if (lane < DG)
+#pragma unroll
+    for (int g = 0; g < QG; g++)
+#pragma unroll
+      for (int j = 0; j < 8; j++) racc[warp][g * HS + 8 * dg + j] = acc[g][j];
+  __syncthreads();
+  for (int i = t; i < QG * HS; i += kAttnChunk) {
     float a = 0.f;
-    for (int w = 0; w < kAttnWarps; w++)
-      if (sm_m[w] > -INFINITY) a += sm_acc[w][i] * expf(sm_m[w] - M);
-    out[i] = a;
+#pragma unroll
+    for (int w = 0; w < NW; w++) a += racc[w][i];
+    const int g = i / HS, e = i - g * HS;
+    p.part[((size_t)(h0 + g) * p.nchunk + c) * (HS + 2) + e] = a;
   }
-  if (threadIdx.x == 0) {
-    float L = 0.f;
-    for (int w = 0; w < kAttnWarps; w++)
-      if (sm_m[w] > -INFINITY) L += sm_l[w] * expf(sm_m[w] - M);
-    out[p.hs] = M;
-    out[p.hs + 1] = L;
+  if (t == 0) {
+#pragma unroll
+    for (int g = 0; g < QG; g++) {
+      float L = 0.f;
+#pragma unroll
+      for (int w = 0; w < NW; w++) L += red[g][w];
+      float* out = p.part + ((size_t)(h0 + g) * p.nchunk + c) * (HS + 2);
+      out[HS] = M[g];
+      out[HS + 1] = L;
+    }
   }
+}
+
+// RoPE frequencies (rope_neox, gguf_run.c:171): freq[j] = powf(base, -2j/hs)
+__global__ void dec_rope_freq(float* freq, int hs, float base) {
+  const int j = threadIdx.x;
+  if (j < hs / 2) freq[j] = powf(base, -2.0f * j / hs);
 }
 
 // the chunks' states merged; out = acc / l (kv_softmax_finish, kvstore.h:99-101)
@@ -268,6 +354,32 @@ __global__ void __launch_bounds__(kDecThreads) dec_argmax(const float* v, int n,
   }
 }
 
+template <class KT, int HS>
+static int launch_attn_h(const AttnParams& at, int qg, int nchunk, int nkv, cudaStream_t s) {
+  const dim3 grid(nchunk, nkv);
+  switch (qg) {
+    case 1: dec_attn_partial<KT, 1, HS><<<grid, kAttnChunk, 0, s>>>(at); break;
+    case 2: dec_attn_partial<KT, 2, HS><<<grid, kAttnChunk, 0, s>>>(at); break;
+    case 4: dec_attn_partial<KT, 4, HS><<<grid, kAttnChunk, 0, s>>>(at); break;
+    case 8: dec_attn_partial<KT, 8, HS><<<grid, kAttnChunk, 0, s>>>(at); break;
+    default: return VIREO_ERR_UNSUPPORTED;
+  }
+  return VIREO_OK;
+}
+
+template <class KT>
+static int launch_attn_t(const AttnParams& at, int qg, int nchunk, int nkv, cudaStream_t s) {
+  switch (at.hs) {
+    case 64: return launch_attn_h<KT, 64>(at, qg, nchunk, nkv, s);
+    case 128: return launch_attn_h<KT, 128>(at, qg, nchunk, nkv, s);
+    default: return VIREO_ERR_UNSUPPORTED;
+  }
+}
+
+static int launch_attn(const AttnParams& at, int qg, int f16, int nchunk, int nkv, cudaStream_t s) {
+  return f16 ? launch_attn_t<__half>(at, qg, nchunk, nkv, s) : launch_attn_t<float>(at, qg, nchunk, nkv, s);
+}
+
 }  // namespace vireo
 
 using namespace vireo;
@@ -275,6 +387,8 @@ using namespace vireo;
 struct gguf_decoder {
   gguf_decoder_desc d;
   std::vector<gguf_decoder_layer> L;
+  std::vector<void*> wqkv;  // per layer: wq | wk | wv rows in one buffer (one mat-vec), or null
+  float* freq = nullptr;
   Ctx* c = nullptr;
   float *x = nullptr, *xb = nullptr, *y = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr,
         *part = nullptr, *logits = nullptr;
@@ -287,8 +401,10 @@ extern "C" {
 
 void gguf_decoder_destroy(gguf_decoder* dec) {
   if (!dec) return;
-  for (void* p : {(void*)dec->x, (void*)dec->xb, (void*)dec->y, (void*)dec->q, (void*)dec->k, (void*)dec->v,
-                  (void*)dec->att, (void*)dec->part, (void*)dec->logits, dec->kc, dec->vc})
+  for (void* p : {(void*)dec->x, (void*)dec->xb, (void*)dec->y, (void*)dec->q, (void*)dec->att, (void*)dec->part,
+                  (void*)dec->logits, dec->kc, dec->vc, (void*)dec->freq})
+    if (p) cudaFree(p);
+  for (void* p : dec->wqkv)
     if (p) cudaFree(p);
   delete dec;
 }
@@ -301,7 +417,10 @@ int gguf_decoder_create(const gguf_decoder_desc* desc, const gguf_decoder_layer*
   if (!c) return st;
   const gguf_decoder_desc& D = *desc;
   if (D.n_layers < 1 || D.dim < 1 || D.dim > 16384 || D.n_heads < 1 || D.n_kv_heads < 1 ||
-      D.n_heads % D.n_kv_heads || D.head_size < 32 || D.head_size % 32 || D.head_size > kMaxHeadSize ||
+      D.n_heads % D.n_kv_heads || (D.head_size != 64 && D.head_size != 128) ||
+      (D.n_heads / D.n_kv_heads != 1 && D.n_heads / D.n_kv_heads != 2 && D.n_heads / D.n_kv_heads != 4 &&
+       D.n_heads / D.n_kv_heads != 8) ||
+      (size_t)(D.n_heads + 2 * D.n_kv_heads) * D.head_size * 4 > 48 * 1024 ||
       D.vocab < 1 || D.max_ctx < 1 || !D.tok_embd || !D.out_norm || !D.lm_head)
     return VIREO_ERR_ARG;
   int be, bb;
@@ -328,14 +447,38 @@ int gguf_decoder_create(const gguf_decoder_desc* desc, const gguf_decoder_layer*
   if ((st = cuda_status(cudaMalloc(&dec->x, (size_t)D.dim * 4))) ||
       (st = cuda_status(cudaMalloc(&dec->xb, (size_t)D.dim * 4))) ||
       (st = cuda_status(cudaMalloc(&dec->y, (size_t)D.dim * 4))) ||
-      (st = cuda_status(cudaMalloc(&dec->q, (size_t)nq * 4))) ||
-      (st = cuda_status(cudaMalloc(&dec->k, (size_t)nk * 4))) ||
-      (st = cuda_status(cudaMalloc(&dec->v, (size_t)nk * 4))) ||
+      (st = cuda_status(cudaMalloc(&dec->q, (size_t)(nq + 2 * nk) * 4))) ||
+      (st = cuda_status(cudaMalloc(&dec->freq, (size_t)D.head_size / 2 * 4))) ||
       (st = cuda_status(cudaMalloc(&dec->att, (size_t)nq * 4))) ||
       (st = cuda_status(cudaMalloc(&dec->part, (size_t)D.n_heads * dec->max_chunk * (D.head_size + 2) * 4))) ||
       (st = cuda_status(cudaMalloc(&dec->logits, (size_t)D.vocab * 4))) ||
       (st = cuda_status(cudaMalloc(&dec->kc, kvb))) || (st = cuda_status(cudaMalloc(&dec->vc, kvb))) ||
       (st = cuda_status(cudaMemset(dec->x, 0, (size_t)D.dim * 4)))) {
+    gguf_decoder_destroy(dec);
+    return st;
+  }
+  // q, k and v are one vector: one mat-vec over wq | wk | wv writes all three
+  dec->k = dec->q + nq;
+  dec->v = dec->k + nk;
+  dec_rope_freq<<<1, 128, 0, c->stream>>>(dec->freq, D.head_size, D.rope_base);
+  dec->wqkv.assign(D.n_layers, nullptr);
+  for (int l = 0; l < D.n_layers; l++) {
+    const gguf_decoder_layer& y = layers[l];
+    if (y.wq_type != y.wk_type || y.wq_type != y.wv_type) continue;
+    const size_t rb = row_bytes(y.wq_type, D.dim);
+    void* w = nullptr;
+    if ((st = cuda_status(cudaMalloc(&w, rb * (nq + 2 * nk)))) ||
+        (st = cuda_status(cudaMemcpyAsync(w, y.wq, rb * nq, cudaMemcpyDeviceToDevice, c->stream))) ||
+        (st = cuda_status(cudaMemcpyAsync((uint8_t*)w + rb * nq, y.wk, rb * nk, cudaMemcpyDeviceToDevice, c->stream))) ||
+        (st = cuda_status(
+             cudaMemcpyAsync((uint8_t*)w + rb * (nq + nk), y.wv, rb * nk, cudaMemcpyDeviceToDevice, c->stream)))) {
+      if (w) cudaFree(w);
+      gguf_decoder_destroy(dec);
+      return st;
+    }
+    dec->wqkv[l] = w;
+  }
+  if ((st = cuda_status(cudaStreamSynchronize(c->stream)))) {
     gguf_decoder_destroy(dec);
     return st;
   }
@@ -365,11 +508,15 @@ static int decoder_step(gguf_decoder* dec, int token, const int32_t* token_dev, 
   for (int l = 0; l < D.n_layers; l++) {
     const gguf_decoder_layer& y = dec->L[l];
     dec_rmsnorm<<<1, kDecThreads, 0, s>>>(dec->x, nullptr, y.attn_norm, dec->xb, d, D.eps);
-    if ((st = gemv_dev(c, y.wq_type, y.wq, dec->xb, dec->q, d, nq, s)) ||
-        (st = gemv_dev(c, y.wk_type, y.wk, dec->xb, dec->k, d, nk, s)) ||
-        (st = gemv_dev(c, y.wv_type, y.wv, dec->xb, dec->v, d, nk, s)))
+    if (dec->wqkv[l]) {
+      if ((st = gemv_dev(c, y.wq_type, dec->wqkv[l], dec->xb, dec->q, d, nq + 2 * nk, s))) return st;
+    } else if ((st = gemv_dev(c, y.wq_type, y.wq, dec->xb, dec->q, d, nq, s)) ||
+               (st = gemv_dev(c, y.wk_type, y.wk, dec->xb, dec->k, d, nk, s)) ||
+               (st = gemv_dev(c, y.wv_type, y.wv, dec->xb, dec->v, d, nk, s))) {
       return st;
+    }
     AttnPrepParams ap;
+    ap.freq = dec->freq;
     ap.q = dec->q;
     ap.k = dec->k;
     ap.v = dec->v;
@@ -390,7 +537,7 @@ static int decoder_step(gguf_decoder* dec, int token, const int32_t* token_dev, 
     ap.base = D.rope_base;
     ap.kc = (uint8_t*)dec->kc + (size_t)l * dec->layer_kv * kv_el;
     ap.vc = (uint8_t*)dec->vc + (size_t)l * dec->layer_kv * kv_el;
-    dec_attn_prep<<<1, kDecThreads, 0, s>>>(ap);
+    dec_attn_prep<<<1, kDecThreads, (size_t)(nq + 2 * nk) * 4, s>>>(ap);
     AttnParams at;
     at.q = dec->q;
     at.kc = ap.kc;
@@ -403,10 +550,7 @@ static int decoder_step(gguf_decoder* dec, int token, const int32_t* token_dev, 
     at.nchunk = nchunk;
     at.scale = 1.0f / sqrtf((float)hs);
     at.part = dec->part;
-    if (D.kv_f16)
-      dec_attn_partial<__half><<<dim3(nchunk, D.n_heads), 32 * kAttnWarps, 0, s>>>(at);
-    else
-      dec_attn_partial<float><<<dim3(nchunk, D.n_heads), 32 * kAttnWarps, 0, s>>>(at);
+    if ((st = launch_attn(at, D.n_heads / D.n_kv_heads, D.kv_f16, nchunk, D.n_kv_heads, s))) return st;
     dec_attn_combine<<<D.n_heads, hs, 0, s>>>(at, dec->att);
     if ((st = gemv_dev(c, y.wo_type, y.wo, dec->att, dec->y, nq, d, s))) return st;
     // x += attention output; xb = ffn_norm(x)   (gguf_run.c:237-238)
