@@ -12,6 +12,7 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <utility>
 #include <vector>
 
 #include "gguf_decoder.h"
@@ -45,6 +46,8 @@ VDEV float block_sum(float v, float* red) {
 // gguf_run.c:161-165; with y the residual add of gguf_run.c:237 first)
 __global__ void __launch_bounds__(kDecThreads) dec_rmsnorm(float* x, const float* y, const float* w, float* out, int n,
                                                            float eps) {
+  pdl_launch_dependents();  // the next kernel may take SMs now; it waits in its own prologue
+  pdl_wait();  // inputs written by the previous kernel on the stream
   __shared__ float red[32];
   float ss = 0.f;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -99,6 +102,8 @@ VDEV void qk_norm(float* v, int nv, int hs, const float* w, int len, float eps, 
 // staged in shared memory (dynamic, (nq + 2 nk) floats) so that the steps
 // between the one read and the one write are on-chip
 __global__ void __launch_bounds__(kDecThreads) dec_attn_prep(const __grid_constant__ AttnPrepParams p) {
+  pdl_launch_dependents();  // the next kernel may take SMs now; it waits in its own prologue
+  pdl_wait();  // inputs written by the previous kernel on the stream
   extern __shared__ float prep_sh[];
   __shared__ float red[32];
   const int nq = p.nh * p.hs, nk = p.nkv * p.hs;
@@ -178,6 +183,8 @@ VDEV void kv_load8(const __half* p, size_t i, float (&o)[8]) {
 // (kvstore.h:77-101) evaluated chunk-parallel instead of one position at a time.
 template <class KT, int QG, int HS>
 __global__ void __launch_bounds__(kAttnChunk) dec_attn_partial(const __grid_constant__ AttnParams p) {
+  pdl_launch_dependents();  // the next kernel may take SMs now; it waits in its own prologue
+  pdl_wait();  // inputs written by the previous kernel on the stream
   constexpr int DG = HS / 8, PG = kAttnChunk / DG, NW = kAttnChunk / 32;
   __shared__ __align__(16) float sq[QG][HS];
   __shared__ float sp[QG][kAttnChunk];
@@ -295,6 +302,8 @@ __global__ void dec_rope_freq(float* freq, int hs, float base) {
 
 // the chunks' states merged; out = acc / l (kv_softmax_finish, kvstore.h:99-101)
 __global__ void dec_attn_combine(const __grid_constant__ AttnParams p, float* out) {
+  pdl_launch_dependents();  // the next kernel may take SMs now; it waits in its own prologue
+  pdl_wait();  // inputs written by the previous kernel on the stream
   const int h = blockIdx.x;
   const float* base = p.part + (size_t)h * p.nchunk * (p.hs + 2);
   float M = -INFINITY;
@@ -316,6 +325,8 @@ __global__ void dec_attn_combine(const __grid_constant__ AttnParams p, float* ou
 // greedy argmax (gguf_run.c:253): strict '>' from index 0, so the lowest id
 // wins ties and a NaN never wins
 __global__ void __launch_bounds__(kDecThreads) dec_argmax(const float* v, int n, int32_t* out) {
+  pdl_launch_dependents();  // the next kernel may take SMs now; it waits in its own prologue
+  pdl_wait();  // inputs written by the previous kernel on the stream
   __shared__ float bv_s[32];
   __shared__ int bi_s[32];
   float bv = -INFINITY;
@@ -354,17 +365,35 @@ __global__ void __launch_bounds__(kDecThreads) dec_argmax(const float* v, int n,
   }
 }
 
+// Launch with programmatic stream serialization: the kernel may be scheduled
+// while the previous kernel on the stream runs and waits for it in its
+// prologue (griddepcontrol.wait), so the launch latency overlaps work.
+template <typename... KArgs, typename... Args>
+static int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                      Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
+
 template <class KT, int HS>
 static int launch_attn_h(const AttnParams& at, int qg, int nchunk, int nkv, cudaStream_t s) {
   const dim3 grid(nchunk, nkv);
   switch (qg) {
-    case 1: dec_attn_partial<KT, 1, HS><<<grid, kAttnChunk, 0, s>>>(at); break;
-    case 2: dec_attn_partial<KT, 2, HS><<<grid, kAttnChunk, 0, s>>>(at); break;
-    case 4: dec_attn_partial<KT, 4, HS><<<grid, kAttnChunk, 0, s>>>(at); break;
-    case 8: dec_attn_partial<KT, 8, HS><<<grid, kAttnChunk, 0, s>>>(at); break;
+    case 1: return launch_pdl(dec_attn_partial<KT, 1, HS>, grid, dim3(kAttnChunk), 0, s, at);
+    case 2: return launch_pdl(dec_attn_partial<KT, 2, HS>, grid, dim3(kAttnChunk), 0, s, at);
+    case 4: return launch_pdl(dec_attn_partial<KT, 4, HS>, grid, dim3(kAttnChunk), 0, s, at);
+    case 8: return launch_pdl(dec_attn_partial<KT, 8, HS>, grid, dim3(kAttnChunk), 0, s, at);
     default: return VIREO_ERR_UNSUPPORTED;
   }
-  return VIREO_OK;
 }
 
 template <class KT>
@@ -507,7 +536,9 @@ static int decoder_step(gguf_decoder* dec, int token, const int32_t* token_dev, 
   const size_t kv_el = D.kv_f16 ? 2 : 4;
   for (int l = 0; l < D.n_layers; l++) {
     const gguf_decoder_layer& y = dec->L[l];
-    dec_rmsnorm<<<1, kDecThreads, 0, s>>>(dec->x, nullptr, y.attn_norm, dec->xb, d, D.eps);
+    if ((st = launch_pdl(dec_rmsnorm, dim3(1), dim3(kDecThreads), 0, s, dec->x, (const float*)nullptr, y.attn_norm,
+                         dec->xb, d, D.eps)))
+      return st;
     if (dec->wqkv[l]) {
       if ((st = gemv_dev(c, y.wq_type, dec->wqkv[l], dec->xb, dec->q, d, nq + 2 * nk, s))) return st;
     } else if ((st = gemv_dev(c, y.wq_type, y.wq, dec->xb, dec->q, d, nq, s)) ||
@@ -537,7 +568,7 @@ static int decoder_step(gguf_decoder* dec, int token, const int32_t* token_dev, 
     ap.base = D.rope_base;
     ap.kc = (uint8_t*)dec->kc + (size_t)l * dec->layer_kv * kv_el;
     ap.vc = (uint8_t*)dec->vc + (size_t)l * dec->layer_kv * kv_el;
-    dec_attn_prep<<<1, kDecThreads, (size_t)(nq + 2 * nk) * 4, s>>>(ap);
+    if ((st = launch_pdl(dec_attn_prep, dim3(1), dim3(kDecThreads), (size_t)(nq + 2 * nk) * 4, s, ap))) return st;
     AttnParams at;
     at.q = dec->q;
     at.kc = ap.kc;
@@ -551,18 +582,23 @@ static int decoder_step(gguf_decoder* dec, int token, const int32_t* token_dev, 
     at.scale = 1.0f / sqrtf((float)hs);
     at.part = dec->part;
     if ((st = launch_attn(at, D.n_heads / D.n_kv_heads, D.kv_f16, nchunk, D.n_kv_heads, s))) return st;
-    dec_attn_combine<<<D.n_heads, hs, 0, s>>>(at, dec->att);
+    if ((st = launch_pdl(dec_attn_combine, dim3(D.n_heads), dim3(hs), 0, s, at, dec->att))) return st;
     if ((st = gemv_dev(c, y.wo_type, y.wo, dec->att, dec->y, nq, d, s))) return st;
     // x += attention output; xb = ffn_norm(x)   (gguf_run.c:237-238)
-    dec_rmsnorm<<<1, kDecThreads, 0, s>>>(dec->x, dec->y, y.ffn_norm, dec->xb, d, D.eps);
+    if ((st = launch_pdl(dec_rmsnorm, dim3(1), dim3(kDecThreads), 0, s, dec->x, (const float*)dec->y, y.ffn_norm,
+                         dec->xb, d, D.eps)))
+      return st;
     // x += MoE(xb)   (gguf_run.c:239)
     if ((st = gguf_moe_ffn(y.moe, dec->xb, dec->x, 1, nullptr, nullptr, s))) return st;
   }
   if (logits || next) {
     float* lg = logits ? logits : dec->logits;
-    dec_rmsnorm<<<1, kDecThreads, 0, s>>>(dec->x, nullptr, D.out_norm, dec->xb, d, D.eps);
+    if ((st = launch_pdl(dec_rmsnorm, dim3(1), dim3(kDecThreads), 0, s, dec->x, (const float*)nullptr, D.out_norm,
+                         dec->xb, d, D.eps)))
+      return st;
     if ((st = gemv_dev(c, D.lm_head_type, D.lm_head, dec->xb, lg, d, D.vocab, s))) return st;
-    if (next) dec_argmax<<<1, kDecThreads, 0, s>>>(lg, D.vocab, next);
+    if (next && (st = launch_pdl(dec_argmax, dim3(1), dim3(kDecThreads), 0, s, (const float*)lg, D.vocab, next)))
+      return st;
   }
   return cuda_status(cudaGetLastError());
 }
