@@ -71,6 +71,15 @@ def test_decoder_f16_kv_and_long_context():
     assert worst < 1e-2, worst
 
 
+def test_decoder_gqa8_head64_no_qk_norm_across_chunks():
+    # 8 q heads per kv head (config 3's grouping), 64-wide heads, no QK norm;
+    # 140 positions cross the 128-position attention chunk boundary
+    spec = S.DecoderSpec(2, 512, 8, 1, 64, 640, S.MoeLayerSpec(512, 256, 16, 4, 1, S.GGML_Q4_K, S.GGML_Q4_K,
+                                                               S.GGML_Q6_K), qk_norm=None)
+    worst = run_case(spec, 35, kv_f16=False, steps=140, check_from=120)
+    assert worst < 2e-3, worst
+
+
 def test_decoder_device_token_chain_matches_host_tokens():
     """gguf_decoder_step_dev fed by the previous step's argmax gives the same
     tokens and logits as gguf_decoder_step fed the same ids from the host."""

@@ -94,39 +94,50 @@ static int ensure_smem_attr(const Ctx* c, const void* fn) {
   return VIREO_OK;
 }
 
+int gemv_dev_fast(Ctx* c, uint32_t type, const void* w, const float* x, float* y, int n, int d, cudaStream_t s,
+                  const float* norm_w, float eps, uint32_t prefetch_bytes) {
+  if (n <= 0 || d <= 0) return VIREO_ERR_ARG;
+  if (!fast_format(type) || n % kSegElems || d % 16 || ((uintptr_t)w % 16)) return VIREO_ERR_UNSUPPORTED;
+  GemvParams p;
+  memset(&p, 0, sizeof(p));
+  if (stage_geom(type, n, &p.sg) != VIREO_OK) return VIREO_ERR_UNSUPPORTED;
+  p.W = (const uint8_t*)w;
+  p.x = x;
+  p.y = y;
+  p.n = n;
+  p.d = d;
+  p.err = c->d_err;
+  p.norm_w = norm_w;
+  p.eps = eps;
+  p.prefetch_bytes = prefetch_bytes & ~15u;
+  const int grid = std::min(c->num_sms, d / 16);
+  // a ring deeper than the CTA's units only holds shared memory that the
+  // next kernel's CTAs could use
+  const int units_per_cta = (d / 16 + grid - 1) / grid;
+  const uint32_t smem = gemv_layout(&p, dyn_smem_limit(c), units_per_cta);
+  if (!smem) return VIREO_ERR_UNSUPPORTED;
+  const void* fn = gemv_kernel_for(type);
+  int st = ensure_smem_attr(c, fn);
+  if (st) return st;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kDecodeThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* args[] = {&p};
+  return cuda_status(cudaLaunchKernelExC(&cfg, fn, args));
+}
+
 int gemv_dev(Ctx* c, uint32_t type, const void* w, const float* x, float* y, int n, int d, cudaStream_t s) {
   if (n <= 0 || d < 0) return VIREO_ERR_ARG;
   if (d == 0) return VIREO_OK;
-  if (fast_format(type) && n % kSegElems == 0 && d % 16 == 0 && ((uintptr_t)w % 16) == 0) {
-    GemvParams p;
-    memset(&p, 0, sizeof(p));
-    if (stage_geom(type, n, &p.sg) == VIREO_OK) {
-      p.W = (const uint8_t*)w;
-      p.x = x;
-      p.y = y;
-      p.n = n;
-      p.d = d;
-      p.err = c->d_err;
-      const uint32_t smem = gemv_layout(&p, dyn_smem_limit(c));
-      if (smem) {
-        const void* fn = gemv_kernel_for(type);
-        int st = ensure_smem_attr(c, fn);
-        if (st) return st;
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(std::min(c->num_sms, d / 16));
-        cfg.blockDim = dim3(kDecodeThreads);
-        cfg.dynamicSmemBytes = smem;
-        cfg.stream = s;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        void* args[] = {&p};
-        return cuda_status(cudaLaunchKernelExC(&cfg, fn, args));
-      }
-    }
-  }
+  const int st = gemv_dev_fast(c, type, w, x, y, n, d, s, nullptr, 0.f, 0u);
+  if (st != VIREO_ERR_UNSUPPORTED) return st;
   return launch_gemv_generic(type, w, x, y, n, d, s);
 }
 

@@ -16,6 +16,7 @@ struct Ctl {
   int ids[kMaxTopK];
   float wts[kMaxTopK];
   int tile_cnt[2];  // down units finished per tile buffer
+  float nred[kConsumerWarps];  // gemv_kernel: per-warp sums of squares for the fused norm
 };
 
 VDEV void trace(const MoeDecodeParams& p, int slot) {
@@ -514,6 +515,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) gemv_kernel(const __grid_co
   const int U = p.d / 16;
   const int u0 = (int)((long long)blockIdx.x * U / gridDim.x), u1 = (int)((long long)(blockIdx.x + 1) * U / gridDim.x);
   const int nU = u1 - u0, nseg = p.n / kSegElems;
+  // the weight rows do not depend on the previous kernel: start them toward
+  // L2 while it finishes
+  if (p.prefetch_bytes && threadIdx.x == 0 && nU > 0)
+    prefetch_l2(p.W + (size_t)(16 * u0) * p.sg.rb,
+                (uint32_t)min((uint64_t)(16 * nU) * p.sg.rb, (uint64_t)p.prefetch_bytes));
   pdl_launch_dependents();
   pdl_wait();
   __syncthreads();
@@ -539,6 +545,20 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) gemv_kernel(const __grid_co
       for (int i = threadIdx.x; i < p.n; i += NC) xs[i] = __ldg(p.x + i);
     }
     named_bar(1, NC);
+    if (p.norm_w) {
+      // x * (1 / sqrt(mean(x^2) + eps)) * w, every CTA on its own copy
+      float ss = 0.f;
+      for (int i = threadIdx.x; i < p.n; i += NC) ss += xs[i] * xs[i];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0) ctl->nred[warp] = ss;
+      named_bar(1, NC);
+      float tot = 0.f;
+      for (int w = 0; w < W; w++) tot += ctl->nred[w];
+      const float r = 1.0f / sqrtf(tot / (float)p.n + p.eps);
+      for (int i = threadIdx.x; i < p.n; i += NC) xs[i] = xs[i] * r * __ldg(p.norm_w + i);
+      named_bar(1, NC);
+    }
     build_tables<SF>(xs, xtab, xsx, p.n / kSegElems, warp, W, lane);
     named_bar(1, NC);
   }
@@ -671,12 +691,14 @@ const void* gemv_kernel_for(uint32_t type) {
   return nullptr;
 }
 
-uint32_t gemv_layout(GemvParams* p, uint32_t smem_limit) {
+// Shared-memory layout for gemv_kernel: the deepest ring that fits, and no
+// deeper than the max_units units a CTA streams (at least 2 stages).
+uint32_t gemv_layout(GemvParams* p, uint32_t smem_limit, int max_units) {
   const int W = kConsumerWarps;
   const uint32_t stage = up_to(2u * p->sg.hstride, 128u);
   p->stage_bytes = stage;
   p->part_stride = (uint32_t)std::max(W, p->n / kSegElems) * 16u;
-  for (int S = kMaxStages; S >= 2; S--) {
+  for (int S = std::max(2, std::min(kMaxStages, max_units)); S >= 2; S--) {
     uint32_t off = 2u * kMaxStages * 8u;
     p->off_ctl = off;
     off = up_to(off + (uint32_t)sizeof(Ctl), 16);

@@ -23,6 +23,9 @@ namespace vireo {
 
 constexpr int kDecThreads = 1024;
 constexpr int kAttnChunk = 128;  // cached positions per attention CTA (one per thread)
+// weight bytes per mat-vec CTA sent toward L2 before the CTA waits on the
+// previous kernel
+constexpr uint32_t kDecPrefetch = 128u << 10;
 
 VDEV float warp_sum(float v) {
 #pragma unroll
@@ -63,98 +66,42 @@ __global__ void __launch_bounds__(kDecThreads) dec_rmsnorm(float* x, const float
   for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = x[i] * r * w[i];
 }
 
-struct AttnPrepParams {
-  const float* freq;  // [hs / 2] RoPE frequencies, base^(-2j/hs)
-  float *q, *k, *v;
-  const float *bq, *bk, *bv;
-  const float *qn, *kn;
-  int qn_len, kn_len;
-  int nh, nkv, hs, pos, max_ctx, f16;
-  float eps, base;
-  void *kc, *vc;  // this layer's caches, [nkv][max_ctx][hs]
-};
-
-// RMSNorm of `nv` heads of hs values in place, per head (len == hs) or over
-// the whole vector (len == nv hs); the caller syncs before and after
-VDEV void qk_norm(float* v, int nv, int hs, const float* w, int len, float eps, float* red) {
-  if (len == hs) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    for (int h = warp; h < nv; h += nw) {
-      float* p = v + (size_t)h * hs;
-      float ss = 0.f;
-      for (int i = lane; i < hs; i += 32) ss += p[i] * p[i];
-      ss = warp_sum(ss);
-      const float r = 1.0f / sqrtf(ss / (float)hs + eps);
-      for (int i = lane; i < hs; i += 32) p[i] = p[i] * r * w[i];
-    }
-  } else {
-    const int n = nv * hs;
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) ss += v[i] * v[i];
-    ss = block_sum(ss, red);
-    const float r = 1.0f / sqrtf(ss / (float)n + eps);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) v[i] = v[i] * r * w[i];
-  }
+// RMSNorm of one head (hs values in shared memory) by one warp:
+// v * (1 / sqrt(ss / len + eps)) * w, with ss given (the head's own sum of
+// squares for a per-head norm, the whole vector's for a full-width one)
+VDEV void norm_head(float* v, int hs, const float* w, float ss, int len, float eps, int lane) {
+  const float r = 1.0f / sqrtf(ss / (float)len + eps);
+  for (int i = lane; i < hs; i += 32) v[i] = v[i] * r * w[i];
 }
 
-// bias (gguf_run.c:223-225), QK norm (:226-229), NEOX RoPE (:230-231,
-// rope_neox :168-173) and the KV append (:232-233), one CTA; q, k and v are
-// staged in shared memory (dynamic, (nq + 2 nk) floats) so that the steps
-// between the one read and the one write are on-chip
-__global__ void __launch_bounds__(kDecThreads) dec_attn_prep(const __grid_constant__ AttnPrepParams p) {
-  pdl_launch_dependents();  // the next kernel may take SMs now; it waits in its own prologue
-  pdl_wait();  // inputs written by the previous kernel on the stream
-  extern __shared__ float prep_sh[];
-  __shared__ float red[32];
-  const int nq = p.nh * p.hs, nk = p.nkv * p.hs;
-  float* q = prep_sh;
-  float* k = q + nq;
-  float* v = k + nk;
-  for (int i = threadIdx.x; i < nq; i += blockDim.x) q[i] = p.bq ? p.q[i] + p.bq[i] : p.q[i];
-  for (int i = threadIdx.x; i < nk; i += blockDim.x) {
-    k[i] = p.bk ? p.k[i] + p.bk[i] : p.k[i];
-    v[i] = p.bv ? p.v[i] + p.bv[i] : p.v[i];
+// sum of squares of (a[i] + b[i]) over n values (b may be null), block-wide
+VDEV float block_sumsq(const float* a, const float* b, int n, float* red) {
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = b ? a[i] + b[i] : a[i];
+    ss += v * v;
   }
-  __syncthreads();
-  if (p.qn) qk_norm(q, p.nh, p.hs, p.qn, p.qn_len, p.eps, red);
-  __syncthreads();
-  if (p.kn) qk_norm(k, p.nkv, p.hs, p.kn, p.kn_len, p.eps, red);
-  __syncthreads();
-  const int half = p.hs / 2, pairs = (p.nh + p.nkv) * half;
-  for (int idx = threadIdx.x; idx < pairs; idx += blockDim.x) {
-    const int h = idx / half, j = idx - h * half;
-    float* w = h < p.nh ? q + (size_t)h * p.hs : k + (size_t)(h - p.nh) * p.hs;
-    const float a = (float)p.pos * p.freq[j];
-    const float c = cosf(a), s = sinf(a);
-    const float x0 = w[j], x1 = w[j + half];
-    w[j] = x0 * c - x1 * s;
-    w[j + half] = x0 * s + x1 * c;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < nq; i += blockDim.x) p.q[i] = q[i];
-  for (int i = threadIdx.x; i < nk; i += blockDim.x) {
-    const int kh = i / p.hs, e = i - kh * p.hs;
-    const size_t at = ((size_t)kh * p.max_ctx + p.pos) * p.hs + e;
-    if (p.f16) {
-      reinterpret_cast<__half*>(p.kc)[at] = __float2half_rn(k[i]);
-      reinterpret_cast<__half*>(p.vc)[at] = __float2half_rn(v[i]);
-    } else {
-      reinterpret_cast<float*>(p.kc)[at] = k[i];
-      reinterpret_cast<float*>(p.vc)[at] = v[i];
-    }
-  }
+  return block_sum(ss, red);
 }
 
 struct AttnParams {
-  const float* q;
-  const void *kc, *vc;
-  int nh, nkv, hs, npos, max_ctx, nchunk;
-  float scale;
+  const float *q, *k, *v;     // this position's projections [nh hs], [nkv hs], [nkv hs]
+  const float *bq, *bk, *bv;  // biases or null
+  const float *qn, *kn;       // QK-norm weights or null
+  int qn_len, kn_len;         // hs (per head) or the full width
+  const float* freq;          // [hs / 2] RoPE frequencies, base^(-2j/hs)
+  void *kc, *vc;              // this layer's caches, [nkv][max_ctx][hs]
+  int nh, nkv, hs, pos, npos, max_ctx, nchunk;
+  float scale, eps;
   float* part;  // [nh][nchunk][hs + 2]: acc, m, l
 };
 
 VDEV float kv_load(const float* p, size_t i) { return p[i]; }
 VDEV float kv_load(const __half* p, size_t i) { return __half2float(p[i]); }
+VDEV float kv_round(float v, const float*) { return v; }
+VDEV float kv_round(float v, const __half*) { return __half2float(__float2half_rn(v)); }
+VDEV void kv_store(float* p, size_t i, float v) { p[i] = v; }
+VDEV void kv_store(__half* p, size_t i, float v) { p[i] = __float2half_rn(v); }
 
 // 8 consecutive cache values starting at element i (i a multiple of 8)
 VDEV void kv_load8(const float* p, size_t i, float (&o)[8]) {
@@ -172,36 +119,136 @@ VDEV void kv_load8(const __half* p, size_t i, float (&o)[8]) {
   }
 }
 
-// One (chunk of kAttnChunk positions, kv head) with all QG q heads that
-// share the kv head (GQA).  Scores: thread t takes position t, reads its key
-// row once (HS/8 16-byte loads in flight) and scores it against every q head.
-// The chunk's softmax state per q head is formed (max, exp, sum).  Values:
-// thread (dg, pg) accumulates dimensions 8 dg .. 8 dg + 7 over positions
-// pg, pg + PG, ... with 16-byte loads, and the position groups are summed.
-// The state (acc, m, l) of each (q head, chunk) goes to part and
-// dec_attn_combine merges the chunks: the reference's softmax attention
-// (kvstore.h:77-101) evaluated chunk-parallel instead of one position at a time.
+// NEOX rotation of `nv` heads of HS values in place (rope_neox,
+// gguf_run.c:168-173): pairs (j, j + HS/2) turned by pos * freq[j]
+template <int HS>
+VDEV void rope_heads(float* v, int nv, int pos, const float* freq) {
+  constexpr int half = HS / 2;
+  for (int idx = threadIdx.x; idx < nv * half; idx += blockDim.x) {
+    const int h = idx / half, j = idx - h * half;
+    float* w = v + h * HS;
+    const float a = (float)pos * freq[j];
+    const float c = cosf(a), s = sinf(a);
+    const float x0 = w[j], x1 = w[j + half];
+    w[j] = x0 * c - x1 * s;
+    w[j + half] = x0 * s + x1 * c;
+  }
+}
+
+// Attention of one token, one (chunk of kAttnChunk positions, kv head) per
+// CTA, with all QG q heads that share the kv head (GQA).
+//
+// Prologue (the token's q/k post-processing, done by each CTA for its own
+// heads): bias (gguf_run.c:223-225), QK RMSNorm per head or over the full
+// width (:226-229, :177-179), NEOX RoPE (:230-231); the CTA whose chunk
+// holds position pos also appends this position's k and v to the cache
+// (:232-233) and scores that position from shared memory.  The cached rows of
+// earlier positions were written by earlier steps, so they are prefetched to
+// L2 before the kernel waits on the projection kernel.
+//
+// Scores: thread t takes position t, reads its key row once (HS/8 16-byte
+// loads in flight) and scores it against every q head.  The chunk's softmax
+// state per q head is formed (max, exp, sum).  Values: thread (dg, pg)
+// accumulates dimensions 8 dg .. 8 dg + 7 over positions pg, pg + PG, ...
+// with 16-byte loads, and the position groups are summed.  The state
+// (acc, m, l) of each (q head, chunk) goes to part and dec_attn_combine
+// merges the chunks: the reference's softmax attention (kvstore.h:77-101)
+// evaluated chunk-parallel instead of one position at a time.
 template <class KT, int QG, int HS>
 __global__ void __launch_bounds__(kAttnChunk) dec_attn_partial(const __grid_constant__ AttnParams p) {
-  pdl_launch_dependents();  // the next kernel may take SMs now; it waits in its own prologue
-  pdl_wait();  // inputs written by the previous kernel on the stream
   constexpr int DG = HS / 8, PG = kAttnChunk / DG, NW = kAttnChunk / 32;
   __shared__ __align__(16) float sq[QG][HS];
+  __shared__ __align__(16) float skv[2][HS];  // this position's k and v, as cached
   __shared__ float sp[QG][kAttnChunk];
   __shared__ float red[QG][NW];
+  __shared__ float bred[32];
   __shared__ float racc[NW][QG * HS];
   const int c = blockIdx.x, kh = blockIdx.y, t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int h0 = kh * QG;
-  const KT* kb = reinterpret_cast<const KT*>(p.kc) + (size_t)kh * p.max_ctx * HS;
-  const KT* vb = reinterpret_cast<const KT*>(p.vc) + (size_t)kh * p.max_ctx * HS;
-  for (int i = t; i < QG * HS; i += kAttnChunk) sq[i / HS][i % HS] = p.q[(size_t)h0 * HS + i];
-  __syncthreads();
+  KT* kb = reinterpret_cast<KT*>(p.kc) + (size_t)kh * p.max_ctx * HS;
+  KT* vb = reinterpret_cast<KT*>(p.vc) + (size_t)kh * p.max_ctx * HS;
   const int n = min(kAttnChunk, p.npos - c * kAttnChunk);
+  const int cur = p.pos - c * kAttnChunk;  // this position's row in the chunk
+  const bool has_cur = cur >= 0 && cur < n;
+  if (t == 0) {
+    const int nold = has_cur ? cur : n;
+    if (nold > 0) {
+      const size_t at = (size_t)c * kAttnChunk * HS;
+      prefetch_l2(kb + at, (uint32_t)(nold * HS * sizeof(KT)));
+      prefetch_l2(vb + at, (uint32_t)(nold * HS * sizeof(KT)));
+    }
+  }
+  pdl_launch_dependents();  // the next kernel may take SMs now; it waits in its own prologue
+  pdl_wait();               // q, k, v written by the projection kernel
+
+  // ---- q heads h0 .. h0 + QG - 1 (and this position's k, v): bias, norm, rotation
+  for (int i = t; i < QG * HS; i += kAttnChunk) {
+    const size_t gi = (size_t)h0 * HS + i;
+    sq[i / HS][i % HS] = p.bq ? p.q[gi] + p.bq[gi] : p.q[gi];
+  }
+  if (has_cur)
+    for (int i = t; i < HS; i += kAttnChunk) {
+      const size_t gi = (size_t)kh * HS + i;
+      skv[0][i] = p.bk ? p.k[gi] + p.bk[gi] : p.k[gi];
+      skv[1][i] = p.bv ? p.v[gi] + p.bv[gi] : p.v[gi];
+    }
+  // full-width norms need the whole vector's sum of squares
+  float qss = 0.f, kss = 0.f;
+  if (p.qn && p.qn_len != HS) qss = block_sumsq(p.q, p.bq, p.qn_len, bred);
+  if (has_cur && p.kn && p.kn_len != HS) {
+    __syncthreads();
+    kss = block_sumsq(p.k, p.bk, p.kn_len, bred);
+  }
+  __syncthreads();
+  if (p.qn) {
+    for (int g = warp; g < QG; g += NW) {
+      float ss = qss;
+      if (p.qn_len == HS) {
+        ss = 0.f;
+        for (int i = lane; i < HS; i += 32) ss += sq[g][i] * sq[g][i];
+        ss = warp_sum(ss);
+      }
+      norm_head(sq[g], HS, p.qn_len == HS ? p.qn : p.qn + (size_t)(h0 + g) * HS, ss, p.qn_len, p.eps, lane);
+    }
+  }
+  if (has_cur && p.kn && warp == NW - 1) {
+    float ss = kss;
+    if (p.kn_len == HS) {
+      ss = 0.f;
+      for (int i = lane; i < HS; i += 32) ss += skv[0][i] * skv[0][i];
+      ss = warp_sum(ss);
+    }
+    norm_head(skv[0], HS, p.kn_len == HS ? p.kn : p.kn + (size_t)kh * HS, ss, p.kn_len, p.eps, lane);
+  }
+  __syncthreads();
+  rope_heads<HS>(&sq[0][0], QG, p.pos, p.freq);
+  if (has_cur) rope_heads<HS>(skv[0], 1, p.pos, p.freq);
+  __syncthreads();
+  if (has_cur) {
+    // append to the cache; the chunk uses the values as cached (rounded to KT)
+    for (int i = t; i < HS; i += kAttnChunk) {
+      const size_t at = (size_t)p.pos * HS + i;
+      kv_store(kb, at, skv[0][i]);
+      kv_store(vb, at, skv[1][i]);
+      skv[0][i] = kv_round(skv[0][i], kb);
+      skv[1][i] = kv_round(skv[1][i], vb);
+    }
+    __syncthreads();
+  }
+
+  // ---- scores
   const bool live = t < n;
   float s[QG];
 #pragma unroll
   for (int g = 0; g < QG; g++) s[g] = 0.f;
-  if (live) {
+  if (t == cur) {
+#pragma unroll
+    for (int i = 0; i < HS; i += 8)
+#pragma unroll
+      for (int g = 0; g < QG; g++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) s[g] += sq[g][i + j] * skv[0][i + j];
+  } else if (live) {
     const size_t row = ((size_t)c * kAttnChunk + t) * HS;
 #pragma unroll
     for (int i = 0; i < HS; i += 8) {
@@ -253,7 +300,12 @@ __global__ void __launch_bounds__(kAttnChunk) dec_attn_partial(const __grid_cons
 #pragma unroll 4
   for (int u = pg; u < n; u += PG) {
     float v[8];
-    kv_load8(vb, vbase + (size_t)u * HS, v);
+    if (u == cur) {
+#pragma unroll
+      for (int j = 0; j < 8; j++) v[j] = skv[1][8 * dg + j];
+    } else {
+      kv_load8(vb, vbase + (size_t)u * HS, v);
+    }
 #pragma unroll
     for (int g = 0; g < QG; g++) {
       const float w = sp[g][u];
@@ -536,54 +588,55 @@ static int decoder_step(gguf_decoder* dec, int token, const int32_t* token_dev, 
   const size_t kv_el = D.kv_f16 ? 2 : 4;
   for (int l = 0; l < D.n_layers; l++) {
     const gguf_decoder_layer& y = dec->L[l];
-    if ((st = launch_pdl(dec_rmsnorm, dim3(1), dim3(kDecThreads), 0, s, dec->x, (const float*)nullptr, y.attn_norm,
-                         dec->xb, d, D.eps)))
-      return st;
-    if (dec->wqkv[l]) {
-      if ((st = gemv_dev(c, y.wq_type, dec->wqkv[l], dec->xb, dec->q, d, nq + 2 * nk, s))) return st;
-    } else if ((st = gemv_dev(c, y.wq_type, y.wq, dec->xb, dec->q, d, nq, s)) ||
-               (st = gemv_dev(c, y.wk_type, y.wk, dec->xb, dec->k, d, nk, s)) ||
-               (st = gemv_dev(c, y.wv_type, y.wv, dec->xb, dec->v, d, nk, s))) {
+    // xb = attn_norm(x); q | k | v = W . xb   (gguf_run.c:222-225): one
+    // mat-vec whose CTAs normalise x themselves when wq, wk, wv share a type
+    st = dec->wqkv[l] ? gemv_dev_fast(c, y.wq_type, dec->wqkv[l], dec->x, dec->q, d, nq + 2 * nk, s, y.attn_norm,
+                                      D.eps, kDecPrefetch)
+                      : VIREO_ERR_UNSUPPORTED;
+    if (st == VIREO_ERR_UNSUPPORTED) {
+      if ((st = launch_pdl(dec_rmsnorm, dim3(1), dim3(kDecThreads), 0, s, dec->x, (const float*)nullptr,
+                           y.attn_norm, dec->xb, d, D.eps)))
+        return st;
+      if (dec->wqkv[l]) {
+        if ((st = gemv_dev(c, y.wq_type, dec->wqkv[l], dec->xb, dec->q, d, nq + 2 * nk, s))) return st;
+      } else if ((st = gemv_dev(c, y.wq_type, y.wq, dec->xb, dec->q, d, nq, s)) ||
+                 (st = gemv_dev(c, y.wk_type, y.wk, dec->xb, dec->k, d, nk, s)) ||
+                 (st = gemv_dev(c, y.wv_type, y.wv, dec->xb, dec->v, d, nk, s))) {
+        return st;
+      }
+    } else if (st) {
       return st;
     }
-    AttnPrepParams ap;
-    ap.freq = dec->freq;
-    ap.q = dec->q;
-    ap.k = dec->k;
-    ap.v = dec->v;
-    ap.bq = y.bq;
-    ap.bk = y.bk;
-    ap.bv = y.bv;
-    ap.qn = y.q_norm;
-    ap.kn = y.k_norm;
-    ap.qn_len = y.q_norm_len;
-    ap.kn_len = y.k_norm_len;
-    ap.nh = D.n_heads;
-    ap.nkv = D.n_kv_heads;
-    ap.hs = hs;
-    ap.pos = pos;
-    ap.max_ctx = D.max_ctx;
-    ap.f16 = D.kv_f16;
-    ap.eps = D.eps;
-    ap.base = D.rope_base;
-    ap.kc = (uint8_t*)dec->kc + (size_t)l * dec->layer_kv * kv_el;
-    ap.vc = (uint8_t*)dec->vc + (size_t)l * dec->layer_kv * kv_el;
-    if ((st = launch_pdl(dec_attn_prep, dim3(1), dim3(kDecThreads), (size_t)(nq + 2 * nk) * 4, s, ap))) return st;
+    // q/k post-processing, KV append and attention over every cached position
     AttnParams at;
     at.q = dec->q;
-    at.kc = ap.kc;
-    at.vc = ap.vc;
+    at.k = dec->k;
+    at.v = dec->v;
+    at.bq = y.bq;
+    at.bk = y.bk;
+    at.bv = y.bv;
+    at.qn = y.q_norm;
+    at.kn = y.k_norm;
+    at.qn_len = y.q_norm_len;
+    at.kn_len = y.k_norm_len;
+    at.freq = dec->freq;
+    at.kc = (uint8_t*)dec->kc + (size_t)l * dec->layer_kv * kv_el;
+    at.vc = (uint8_t*)dec->vc + (size_t)l * dec->layer_kv * kv_el;
     at.nh = D.n_heads;
     at.nkv = D.n_kv_heads;
     at.hs = hs;
+    at.pos = pos;
     at.npos = npos;
     at.max_ctx = D.max_ctx;
     at.nchunk = nchunk;
     at.scale = 1.0f / sqrtf((float)hs);
+    at.eps = D.eps;
     at.part = dec->part;
     if ((st = launch_attn(at, D.n_heads / D.n_kv_heads, D.kv_f16, nchunk, D.n_kv_heads, s))) return st;
     if ((st = launch_pdl(dec_attn_combine, dim3(D.n_heads), dim3(hs), 0, s, at, dec->att))) return st;
-    if ((st = gemv_dev(c, y.wo_type, y.wo, dec->att, dec->y, nq, d, s))) return st;
+    st = gemv_dev_fast(c, y.wo_type, y.wo, dec->att, dec->y, nq, d, s, nullptr, 0.f, kDecPrefetch);
+    if (st == VIREO_ERR_UNSUPPORTED) st = gemv_dev(c, y.wo_type, y.wo, dec->att, dec->y, nq, d, s);
+    if (st) return st;
     // x += attention output; xb = ffn_norm(x)   (gguf_run.c:237-238)
     if ((st = launch_pdl(dec_rmsnorm, dim3(1), dim3(kDecThreads), 0, s, dec->x, (const float*)dec->y, y.ffn_norm,
                          dec->xb, d, D.eps)))
@@ -593,10 +646,15 @@ static int decoder_step(gguf_decoder* dec, int token, const int32_t* token_dev, 
   }
   if (logits || next) {
     float* lg = logits ? logits : dec->logits;
-    if ((st = launch_pdl(dec_rmsnorm, dim3(1), dim3(kDecThreads), 0, s, dec->x, (const float*)nullptr, D.out_norm,
-                         dec->xb, d, D.eps)))
-      return st;
-    if ((st = gemv_dev(c, D.lm_head_type, D.lm_head, dec->xb, lg, d, D.vocab, s))) return st;
+    // logits = lm_head . out_norm(x)   (gguf_run.c:249-251), the norm inside the mat-vec where it can be
+    st = gemv_dev_fast(c, D.lm_head_type, D.lm_head, dec->x, lg, d, D.vocab, s, D.out_norm, D.eps, kDecPrefetch);
+    if (st == VIREO_ERR_UNSUPPORTED) {
+      if ((st = launch_pdl(dec_rmsnorm, dim3(1), dim3(kDecThreads), 0, s, dec->x, (const float*)nullptr,
+                           D.out_norm, dec->xb, d, D.eps)))
+        return st;
+      st = gemv_dev(c, D.lm_head_type, D.lm_head, dec->xb, lg, d, D.vocab, s);
+    }
+    if (st) return st;
     if (next && (st = launch_pdl(dec_argmax, dim3(1), dim3(kDecThreads), 0, s, (const float*)lg, D.vocab, next)))
       return st;
   }

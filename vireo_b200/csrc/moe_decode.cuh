@@ -108,6 +108,13 @@ struct GemvParams {
   uint32_t off_part, off_ucnt, off_ctl, off_xtab, off_xsx, off_stg, off_stage;
   uint32_t part_stride;
   int* err;
+  // optional, zero by default: y = W . rmsnorm(x, norm_w, eps) (the norm
+  // computed by every CTA from x), and an L2 prefetch of up to
+  // prefetch_bytes of the CTA's weight rows issued before the kernel waits
+  // on its predecessor (weights are not written by the kernels of a step)
+  const float* norm_w;
+  float eps;
+  uint32_t prefetch_bytes;
 };
 
 }  // namespace vireo

@@ -41,7 +41,7 @@ int stage_geom(uint32_t type, int K, StageGeom* sg);
 const void* moe_decode_kernel_for(uint32_t gtype, uint32_t dtype, bool routed = false);
 uint32_t moe_decode_layout(MoeDecodeParams* p, uint32_t smem_limit, int grid);
 const void* gemv_kernel_for(uint32_t type);
-uint32_t gemv_layout(GemvParams* p, uint32_t smem_limit);
+uint32_t gemv_layout(GemvParams* p, uint32_t smem_limit, int max_units);
 
 // batched (prefill) MoE FFN, prefill.cu
 struct PrefillLayer {
@@ -121,5 +121,12 @@ void* ctx_scratch(Ctx* c, size_t bytes);  // grows, caller holds c->mu
 
 // device-pointer GEMV with the fast path when possible
 int gemv_dev(Ctx* c, uint32_t type, const void* w, const float* x, float* y, int n, int d, cudaStream_t s);
+// The fast path only (VIREO_ERR_UNSUPPORTED when the type, shape or
+// alignment rules it out): y = W . rmsnorm(x, norm_w, eps) when norm_w is
+// set (x * (1 / sqrt(mean(x^2) + eps)) * norm_w), and an L2 prefetch of up
+// to prefetch_bytes of each CTA's weight rows before the kernel waits on its
+// predecessor on the stream.
+int gemv_dev_fast(Ctx* c, uint32_t type, const void* w, const float* x, float* y, int n, int d, cudaStream_t s,
+                  const float* norm_w, float eps, uint32_t prefetch_bytes);
 
 }  // namespace vireo
