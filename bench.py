@@ -617,6 +617,19 @@ def run_decoder(args, wl):
         host_tok = int(nxt.item())
     e2e_tps = n_e2e * world / (time.perf_counter() - t0)
     G.sync(sp)
+    if args.timeline:
+        # two more greedy steps at the full context under the CUDA activity
+        # profiler (untimed)
+        tl_pos = [pos]
+
+        def tl_step():
+            with torch.cuda.stream(stream):
+                G.step_dev(tok, tl_pos[0], next=tok, stream=sp)
+            tl_pos[0] += 1
+
+        write_timeline(args.timeline, rank, tl_step, 2)
+        pos = tl_pos[0]
+        G.sync(sp)
 
     avg_ctx = ctx0 + gen / 2
     wbytes = spec.weight_bytes_per_token()
