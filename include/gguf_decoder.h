@@ -29,7 +29,7 @@ extern "C" {
 typedef struct {
     int n_layers, dim, n_heads, n_kv_heads, head_size, vocab;
     float eps, rope_base;
-    int max_ctx;              /* KV cache positions to hold */
+    int max_ctx;              /* KV cache positions to hold (at most 1,441,792) */
     int kv_f16;               /* 1: keys and values cached as f16; 0: f32 (the reference's) */
     uint32_t tok_embd_type;   /* any type gguf_dequant_row reads */
     const void *tok_embd;     /* [vocab] rows of dim */

@@ -114,6 +114,8 @@ def ref():
         lib.ref_decoder_forward.restype = C.c_int
         lib.ref_decoder_destroy.argtypes = [C.c_void_p]
         lib.ref_decoder_destroy.restype = None
+        lib.ref_decoder_last_gap.argtypes = []
+        lib.ref_decoder_last_gap.restype = C.c_double
         _ref = lib
     return _ref
 
@@ -243,6 +245,11 @@ class RefDecoder:
         a = ref().ref_decoder_forward(self.h, int(token), int(pos), int(want_logits), lg.ctypes.data,
                                       x.ctypes.data)
         return (lg if want_logits else None), x, a
+
+    def last_gap(self) -> float:
+        """Smallest log-probability gap among the top n_used + 1 router
+        choices over every layer of the last step (a near-tie when ~0)."""
+        return float(ref().ref_decoder_last_gap())
 
     def close(self):
         if getattr(self, "h", None):

@@ -30,9 +30,42 @@ int expert_store_lookup(ExpertStore *s, int layer, int expert, ExpertView *view)
 static int g_rec_ids[64];
 static int g_rec_n;
 
+/* Routing margin of the decoder forward() in progress: at the first lookup
+ * of each layer, m->rlog holds that layer's router softmax (gguf_run.c:
+ * 187-188, the top-k scan :191 has just run); the smallest log-probability
+ * gap among its n_used + 1 largest values is recorded.  A gap near zero is
+ * a near-tie, where any other summation order may pick another expert. */
+static Model *g_gap_model;
+static int g_gap_layer;
+static double g_gap_min;
+
+static double topk_log_gap(const float *p, int ne, int k) {
+    float top[65];
+    int n = k + 1 < ne ? k + 1 : ne;
+    if (n > 65) n = 65;
+    for (int i = 0; i < n; i++) top[i] = -1.0f;
+    for (int e = 0; e < ne; e++) {
+        float v = p[e];
+        for (int i = 0; i < n; i++)
+            if (v > top[i]) { float t = top[i]; top[i] = v; v = t; }
+    }
+    double g = INFINITY;
+    for (int i = 0; i + 1 < n; i++) {
+        if (top[i + 1] <= 0.0f) break;
+        double d = log((double)top[i]) - log((double)top[i + 1]);
+        if (d < g) g = d;
+    }
+    return g;
+}
+
 int ref_hook_lookup(ExpertStore *s, int layer, int expert, ExpertView *view) {
     if (g_rec_n < 64) g_rec_ids[g_rec_n] = expert;
     g_rec_n++;
+    if (g_gap_model && layer != g_gap_layer) {
+        g_gap_layer = layer;
+        double g = topk_log_gap(g_gap_model->rlog, g_gap_model->n_experts, g_gap_model->n_used);
+        if (g < g_gap_min) g_gap_min = g;
+    }
     return expert_store_lookup(s, layer, expert, view);
 }
 
@@ -278,11 +311,19 @@ RefDec *ref_decoder_create(int n_layers, int dim, int n_heads, int n_kv_heads, i
  * and x_out [dim] (the residual stream) may be NULL. */
 int ref_decoder_forward(RefDec *r, int token, int pos, int want_logits, float *logits_out, float *x_out) {
     Model *m = &r->m;
+    g_gap_model = m;
+    g_gap_layer = -1;
+    g_gap_min = INFINITY;
     float *lg = forward(m, token, pos, want_logits);
+    g_gap_model = NULL;
     if (lg && logits_out) memcpy(logits_out, lg, sizeof(float) * (size_t)m->vocab);
     if (x_out) memcpy(x_out, m->x, sizeof(float) * (size_t)m->dim);
     return lg ? argmax(lg, m->vocab) : -1;
 }
+
+/* The smallest router log-probability gap among the top n_used + 1 experts
+ * over every layer of the last ref_decoder_forward call. */
+double ref_decoder_last_gap(void) { return g_gap_min; }
 
 void ref_decoder_destroy(RefDec *r) {
     if (!r) return;

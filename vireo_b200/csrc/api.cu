@@ -90,6 +90,11 @@ static int ensure_smem_attr(const Ctx* c, const void* fn) {
   if (g_attr_done.count(fn)) return VIREO_OK;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn_smem_limit(c));
   if (e != cudaSuccess) return cuda_status(e);
+  // one shared-memory configuration for every kernel of a decode chain: an
+  // SM can only hold CTAs of kernels that agree on it, and the programmatic
+  // launches overlap only CTAs that can be co-resident
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return cuda_status(e);
   g_attr_done.insert(fn);
   return VIREO_OK;
 }

@@ -23,9 +23,19 @@ namespace vireo {
 
 constexpr int kDecThreads = 1024;
 constexpr int kAttnChunk = 128;  // cached positions per attention CTA (one per thread)
+constexpr int kCombThreads = 1024;  // threads of the chunk-merging kernel
+// positions a cache may hold: the merging kernel keeps a weight per chunk in
+// (at most 48 KB of) shared memory
+constexpr int kMaxCtx = (48 * 1024 / 4 - kCombThreads) * kAttnChunk;
 // weight bytes per mat-vec CTA sent toward L2 before the CTA waits on the
 // previous kernel
 constexpr uint32_t kDecPrefetch = 128u << 10;
+
+VDEV float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
 
 VDEV float warp_sum(float v) {
 #pragma unroll
@@ -98,8 +108,6 @@ struct AttnParams {
 
 VDEV float kv_load(const float* p, size_t i) { return p[i]; }
 VDEV float kv_load(const __half* p, size_t i) { return __half2float(p[i]); }
-VDEV float kv_round(float v, const float*) { return v; }
-VDEV float kv_round(float v, const __half*) { return __half2float(__float2half_rn(v)); }
 VDEV void kv_store(float* p, size_t i, float v) { p[i] = v; }
 VDEV void kv_store(__half* p, size_t i, float v) { p[i] = __float2half_rn(v); }
 
@@ -142,25 +150,31 @@ VDEV void rope_heads(float* v, int nv, int pos, const float* freq) {
 // heads): bias (gguf_run.c:223-225), QK RMSNorm per head or over the full
 // width (:226-229, :177-179), NEOX RoPE (:230-231); the CTA whose chunk
 // holds position pos also appends this position's k and v to the cache
-// (:232-233) and scores that position from shared memory.  The cached rows of
+// (:232-233) and reads it back with the rest of its chunk.  The cached rows of
 // earlier positions were written by earlier steps, so they are prefetched to
 // L2 before the kernel waits on the projection kernel.
 //
-// Scores: thread t takes position t, reads its key row once (HS/8 16-byte
-// loads in flight) and scores it against every q head.  The chunk's softmax
+// Scores: thread (position t, head group) reads the position's key row once
+// (HS/8 16-byte loads in flight) and scores it against the group's q heads
+// (two groups of 128 threads when QG >= 2, so that each thread's chain of
+// FMAs is half as long and an SM holds twice the warps).  The chunk's softmax
 // state per q head is formed (max, exp, sum).  Values: thread (dg, pg)
 // accumulates dimensions 8 dg .. 8 dg + 7 over positions pg, pg + PG, ...
 // with 16-byte loads, and the position groups are summed.  The state
 // (acc, m, l) of each (q head, chunk) goes to part and dec_attn_combine
 // merges the chunks: the reference's softmax attention (kvstore.h:77-101)
 // evaluated chunk-parallel instead of one position at a time.
-template <class KT, int QG, int HS>
-__global__ void __launch_bounds__(kAttnChunk) dec_attn_partial(const __grid_constant__ AttnParams p) {
-  constexpr int DG = HS / 8, PG = kAttnChunk / DG, NW = kAttnChunk / 32;
+template <class KT, int QG, int HS, int SPLIT>
+__global__ void __launch_bounds__(kAttnChunk* SPLIT) dec_attn_partial(const __grid_constant__ AttnParams p) {
+  // SPLIT groups of kAttnChunk threads; in the score phase group hg scores
+  // every position of the chunk against q heads hg QH .. hg QH + QH - 1
+  constexpr int NT = kAttnChunk * SPLIT, QH = QG / SPLIT, NWG = kAttnChunk / 32, NW = NT / 32;
+  constexpr int DG = HS / 8, PG = NT / DG;
+  static_assert(QG % SPLIT == 0, "heads split evenly over the groups");
   __shared__ __align__(16) float sq[QG][HS];
-  __shared__ __align__(16) float skv[2][HS];  // this position's k and v, as cached
+  __shared__ __align__(16) float skv[2][HS];  // this position's k and v
   __shared__ float sp[QG][kAttnChunk];
-  __shared__ float red[QG][NW];
+  __shared__ float redm[QG][NWG], reds[QG][NWG];
   __shared__ float bred[32];
   __shared__ float racc[NW][QG * HS];
   const int c = blockIdx.x, kh = blockIdx.y, t = threadIdx.x, warp = t >> 5, lane = t & 31;
@@ -182,12 +196,12 @@ __global__ void __launch_bounds__(kAttnChunk) dec_attn_partial(const __grid_cons
   pdl_wait();               // q, k, v written by the projection kernel
 
   // ---- q heads h0 .. h0 + QG - 1 (and this position's k, v): bias, norm, rotation
-  for (int i = t; i < QG * HS; i += kAttnChunk) {
+  for (int i = t; i < QG * HS; i += NT) {
     const size_t gi = (size_t)h0 * HS + i;
     sq[i / HS][i % HS] = p.bq ? p.q[gi] + p.bq[gi] : p.q[gi];
   }
   if (has_cur)
-    for (int i = t; i < HS; i += kAttnChunk) {
+    for (int i = t; i < HS; i += NT) {
       const size_t gi = (size_t)kh * HS + i;
       skv[0][i] = p.bk ? p.k[gi] + p.bk[gi] : p.k[gi];
       skv[1][i] = p.bv ? p.v[gi] + p.bv[gi] : p.v[gi];
@@ -225,71 +239,56 @@ __global__ void __launch_bounds__(kAttnChunk) dec_attn_partial(const __grid_cons
   if (has_cur) rope_heads<HS>(skv[0], 1, p.pos, p.freq);
   __syncthreads();
   if (has_cur) {
-    // append to the cache; the chunk uses the values as cached (rounded to KT)
-    for (int i = t; i < HS; i += kAttnChunk) {
+    // append to the cache; after the barrier the chunk reads the row back
+    // like every other (coherent loads: the same pointers are stored to)
+    for (int i = t; i < HS; i += NT) {
       const size_t at = (size_t)p.pos * HS + i;
       kv_store(kb, at, skv[0][i]);
       kv_store(vb, at, skv[1][i]);
-      skv[0][i] = kv_round(skv[0][i], kb);
-      skv[1][i] = kv_round(skv[1][i], vb);
     }
     __syncthreads();
   }
 
-  // ---- scores
-  const bool live = t < n;
-  float s[QG];
+  // ---- scores: thread (position pp, head group hg)
+  const int pp = t % kAttnChunk, hg = t / kAttnChunk, wg = pp >> 5;
+  const bool live = pp < n;
+  float s[QH];
 #pragma unroll
-  for (int g = 0; g < QG; g++) s[g] = 0.f;
-  if (t == cur) {
-#pragma unroll
-    for (int i = 0; i < HS; i += 8)
-#pragma unroll
-      for (int g = 0; g < QG; g++)
-#pragma unroll
-        for (int j = 0; j < 8; j++) s[g] += sq[g][i + j] * skv[0][i + j];
-  } else if (live) {
-    const size_t row = ((size_t)c * kAttnChunk + t) * HS;
+  for (int g = 0; g < QH; g++) s[g] = 0.f;
+  if (live) {
+    const size_t row = ((size_t)c * kAttnChunk + pp) * HS;
 #pragma unroll
     for (int i = 0; i < HS; i += 8) {
       float e[8];
       kv_load8(kb, row + i, e);
 #pragma unroll
-      for (int g = 0; g < QG; g++)
+      for (int g = 0; g < QH; g++)
 #pragma unroll
-        for (int j = 0; j < 8; j++) s[g] += sq[g][i + j] * e[j];
+        for (int j = 0; j < 8; j++) s[g] += sq[hg * QH + g][i + j] * e[j];
     }
   }
-  // chunk max and sum per q head
+  // chunk max and sum per q head (over the NWG warps of the head's group)
 #pragma unroll
-  for (int g = 0; g < QG; g++) {
-    float v = live ? s[g] * p.scale : -INFINITY;
+  for (int g = 0; g < QH; g++) {
+    const float v = live ? s[g] * p.scale : -INFINITY;
     s[g] = v;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    if (lane == 0) red[g][warp] = v;
+    const float m = warp_max(v);
+    if (lane == 0) redm[hg * QH + g][wg] = m;
   }
   __syncthreads();
-  float M[QG];
 #pragma unroll
-  for (int g = 0; g < QG; g++) {
+  for (int g = 0; g < QH; g++) {
     float m = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < NW; w++) m = fmaxf(m, red[g][w]);
-    M[g] = m;
+    for (int w = 0; w < NWG; w++) m = fmaxf(m, redm[hg * QH + g][w]);
+    const float e = live ? expf(s[g] - m) : 0.f;
+    sp[hg * QH + g][pp] = e;
+    const float v = warp_sum(e);
+    if (lane == 0) reds[hg * QH + g][wg] = v;
   }
   __syncthreads();
-#pragma unroll
-  for (int g = 0; g < QG; g++) {
-    const float e = live ? expf(s[g] - M[g]) : 0.f;
-    sp[g][t] = e;
-    float v = e;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0) red[g][warp] = v;
-  }
-  __syncthreads();
-  // values: thread (dg, pg), 8 dimensions x the chunk's positions pg + PG u
+  // values: thread (dg, pg), 8 dimensions x the chunk's positions pg + PG u,
+  // every q head
   const int dg = t % DG, pg = t / DG;
   float acc[QG][8];
 #pragma unroll
@@ -300,12 +299,7 @@ __global__ void __launch_bounds__(kAttnChunk) dec_attn_partial(const __grid_cons
 #pragma unroll 4
   for (int u = pg; u < n; u += PG) {
     float v[8];
-    if (u == cur) {
-#pragma unroll
-      for (int j = 0; j < 8; j++) v[j] = skv[1][8 * dg + j];
-    } else {
-      kv_load8(vb, vbase + (size_t)u * HS, v);
-    }
+    kv_load8(vb, vbase + (size_t)u * HS, v);
 #pragma unroll
     for (int g = 0; g < QG; g++) {
       const float w = sp[g][u];
@@ -326,23 +320,23 @@ __global__ void __launch_bounds__(kAttnChunk) dec_attn_partial(const __grid_cons
 #pragma unroll
       for (int j = 0; j < 8; j++) racc[warp][g * HS + 8 * dg + j] = acc[g][j];
   __syncthreads();
-  for (int i = t; i < QG * HS; i += kAttnChunk) {
+  for (int i = t; i < QG * HS; i += NT) {
     float a = 0.f;
 #pragma unroll
     for (int w = 0; w < NW; w++) a += racc[w][i];
     const int g = i / HS, e = i - g * HS;
     p.part[((size_t)(h0 + g) * p.nchunk + c) * (HS + 2) + e] = a;
   }
-  if (t == 0) {
+  if (t < QG) {
+    float M = -INFINITY, L = 0.f;
 #pragma unroll
-    for (int g = 0; g < QG; g++) {
-      float L = 0.f;
-#pragma unroll
-      for (int w = 0; w < NW; w++) L += red[g][w];
-      float* out = p.part + ((size_t)(h0 + g) * p.nchunk + c) * (HS + 2);
-      out[HS] = M[g];
-      out[HS + 1] = L;
+    for (int w = 0; w < NWG; w++) {
+      M = fmaxf(M, redm[t][w]);
+      L += reds[t][w];
     }
+    float* out = p.part + ((size_t)(h0 + t) * p.nchunk + c) * (HS + 2);
+    out[HS] = M;
+    out[HS + 1] = L;
   }
 }
 
@@ -352,25 +346,50 @@ __global__ void dec_rope_freq(float* freq, int hs, float base) {
   if (j < hs / 2) freq[j] = powf(base, -2.0f * j / hs);
 }
 
-// the chunks' states merged; out = acc / l (kv_softmax_finish, kvstore.h:99-101)
-__global__ void dec_attn_combine(const __grid_constant__ AttnParams p, float* out) {
+// the chunks' states merged; out = acc / l (kv_softmax_finish, kvstore.h:99-101).
+// One CTA per q head: the chunk maxima and weighted sums are reduced by the
+// whole block first, then kCombThreads / hs groups of hs threads each sum a
+// share of the chunks' accumulators (independent loads in flight) and the
+// groups' sums are added.  Dynamic shared memory: (nchunk + kCombThreads)
+// floats.
+__global__ void __launch_bounds__(kCombThreads) dec_attn_combine(const __grid_constant__ AttnParams p, float* out) {
   pdl_launch_dependents();  // the next kernel may take SMs now; it waits in its own prologue
   pdl_wait();  // inputs written by the previous kernel on the stream
-  const int h = blockIdx.x;
-  const float* base = p.part + (size_t)h * p.nchunk * (p.hs + 2);
+  extern __shared__ float comb_sh[];
+  __shared__ float red[32];
+  const int h = blockIdx.x, t = threadIdx.x, hs = p.hs, nc = p.nchunk;
+  const size_t st = (size_t)hs + 2;
+  const float* base = p.part + (size_t)h * nc * st;
+  float* cf = comb_sh;       // [nc] chunk weights exp(m_c - M)
+  float* gs = comb_sh + nc;  // [groups][hs] group sums
+  float m = -INFINITY;
+  for (int c = t; c < nc; c += blockDim.x) m = fmaxf(m, base[c * st + hs]);
+  m = warp_max(m);
+  __syncthreads();
+  if ((t & 31) == 0) red[t >> 5] = m;
+  __syncthreads();
   float M = -INFINITY;
-  for (int c = 0; c < p.nchunk; c++) M = fmaxf(M, base[(size_t)c * (p.hs + 2) + p.hs]);
-  for (int i = threadIdx.x; i < p.hs; i += blockDim.x) {
-    float a = 0.f, L = 0.f;
-    for (int c = 0; c < p.nchunk; c++) {
-      const float* pc = base + (size_t)c * (p.hs + 2);
-      if (pc[p.hs] > -INFINITY) {
-        const float f = expf(pc[p.hs] - M);
-        a += pc[i] * f;
-        L += pc[p.hs + 1] * f;
-      }
-    }
-    out[(size_t)h * p.hs + i] = L > 0.f ? a * (1.0f / L) : 0.f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); w++) M = fmaxf(M, red[w]);
+  float L = 0.f;
+  for (int c = t; c < nc; c += blockDim.x) {
+    const float mc = base[c * st + hs];
+    const float f = mc > -INFINITY ? expf(mc - M) : 0.f;
+    cf[c] = f;
+    L += base[c * st + hs + 1] * f;
+  }
+  L = block_sum(L, red);  // its barriers also publish cf
+  const int ng = blockDim.x / hs, g = t / hs, i = t - g * hs;
+  if (g < ng) {
+    float a = 0.f;
+#pragma unroll 4
+    for (int c = g; c < nc; c += ng) a += base[c * st + i] * cf[c];
+    gs[g * hs + i] = a;
+  }
+  __syncthreads();
+  if (t < hs) {
+    float a = 0.f;
+    for (int q = 0; q < ng; q++) a += gs[q * hs + t];
+    out[(size_t)h * hs + t] = L > 0.f ? a * (1.0f / L) : 0.f;
   }
 }
 
@@ -440,10 +459,10 @@ template <class KT, int HS>
 static int launch_attn_h(const AttnParams& at, int qg, int nchunk, int nkv, cudaStream_t s) {
   const dim3 grid(nchunk, nkv);
   switch (qg) {
-    case 1: return launch_pdl(dec_attn_partial<KT, 1, HS>, grid, dim3(kAttnChunk), 0, s, at);
-    case 2: return launch_pdl(dec_attn_partial<KT, 2, HS>, grid, dim3(kAttnChunk), 0, s, at);
-    case 4: return launch_pdl(dec_attn_partial<KT, 4, HS>, grid, dim3(kAttnChunk), 0, s, at);
-    case 8: return launch_pdl(dec_attn_partial<KT, 8, HS>, grid, dim3(kAttnChunk), 0, s, at);
+    case 1: return launch_pdl(dec_attn_partial<KT, 1, HS, 1>, grid, dim3(kAttnChunk), 0, s, at);
+    case 2: return launch_pdl(dec_attn_partial<KT, 2, HS, 2>, grid, dim3(2 * kAttnChunk), 0, s, at);
+    case 4: return launch_pdl(dec_attn_partial<KT, 4, HS, 2>, grid, dim3(2 * kAttnChunk), 0, s, at);
+    case 8: return launch_pdl(dec_attn_partial<KT, 8, HS, 2>, grid, dim3(2 * kAttnChunk), 0, s, at);
     default: return VIREO_ERR_UNSUPPORTED;
   }
 }
@@ -459,6 +478,40 @@ static int launch_attn_t(const AttnParams& at, int qg, int nchunk, int nkv, cuda
 
 static int launch_attn(const AttnParams& at, int qg, int f16, int nchunk, int nkv, cudaStream_t s) {
   return f16 ? launch_attn_t<__half>(at, qg, nchunk, nkv, s) : launch_attn_t<float>(at, qg, nchunk, nkv, s);
+}
+
+template <class KT, int HS>
+static const void* attn_kernel_h(int qg) {
+  switch (qg) {
+    case 1: return reinterpret_cast<const void*>(&dec_attn_partial<KT, 1, HS, 1>);
+    case 2: return reinterpret_cast<const void*>(&dec_attn_partial<KT, 2, HS, 2>);
+    case 4: return reinterpret_cast<const void*>(&dec_attn_partial<KT, 4, HS, 2>);
+    case 8: return reinterpret_cast<const void*>(&dec_attn_partial<KT, 8, HS, 2>);
+    default: return nullptr;
+  }
+}
+
+// the attention kernel a decoder of this shape launches
+static const void* attn_kernel(int qg, int f16, int hs) {
+  if (hs == 64) return f16 ? attn_kernel_h<__half, 64>(qg) : attn_kernel_h<float, 64>(qg);
+  if (hs == 128) return f16 ? attn_kernel_h<__half, 128>(qg) : attn_kernel_h<float, 128>(qg);
+  return nullptr;
+}
+
+// Every kernel of the decode chain asks for the largest shared-memory
+// configuration, the one the mat-vec and MoE kernels need: an SM only holds
+// CTAs of kernels that agree on it, and a programmatic launch overlaps its
+// predecessor only where their CTAs can share SMs.
+static int set_chain_carveout(int qg, int f16, int hs) {
+  const void* fns[] = {reinterpret_cast<const void*>(&dec_rmsnorm), reinterpret_cast<const void*>(&dec_attn_combine),
+                       reinterpret_cast<const void*>(&dec_argmax), attn_kernel(qg, f16, hs)};
+  for (const void* fn : fns) {
+    if (!fn) return VIREO_ERR_UNSUPPORTED;
+    const int st = cuda_status(
+        cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared));
+    if (st) return st;
+  }
+  return VIREO_OK;
 }
 
 }  // namespace vireo
@@ -502,7 +555,7 @@ int gguf_decoder_create(const gguf_decoder_desc* desc, const gguf_decoder_layer*
       (D.n_heads / D.n_kv_heads != 1 && D.n_heads / D.n_kv_heads != 2 && D.n_heads / D.n_kv_heads != 4 &&
        D.n_heads / D.n_kv_heads != 8) ||
       (size_t)(D.n_heads + 2 * D.n_kv_heads) * D.head_size * 4 > 48 * 1024 ||
-      D.vocab < 1 || D.max_ctx < 1 || !D.tok_embd || !D.out_norm || !D.lm_head)
+      D.vocab < 1 || D.max_ctx < 1 || D.max_ctx > kMaxCtx || !D.tok_embd || !D.out_norm || !D.lm_head)
     return VIREO_ERR_ARG;
   int be, bb;
   if (type_block(D.tok_embd_type, &be, &bb) || D.dim % be || type_block(D.lm_head_type, &be, &bb) || D.dim % be)
@@ -518,6 +571,7 @@ int gguf_decoder_create(const gguf_decoder_desc* desc, const gguf_decoder_layer*
       if (type_block(t, &be, &bb) || D.dim % be) return VIREO_ERR_UNSUPPORTED;
     if (type_block(y.wo_type, &be, &bb) || nq % be) return VIREO_ERR_UNSUPPORTED;
   }
+  if ((st = set_chain_carveout(D.n_heads / D.n_kv_heads, D.kv_f16, D.head_size))) return st;
   gguf_decoder* dec = new gguf_decoder();
   dec->d = D;
   dec->L.assign(layers, layers + D.n_layers);
@@ -633,7 +687,9 @@ static int decoder_step(gguf_decoder* dec, int token, const int32_t* token_dev, 
     at.eps = D.eps;
     at.part = dec->part;
     if ((st = launch_attn(at, D.n_heads / D.n_kv_heads, D.kv_f16, nchunk, D.n_kv_heads, s))) return st;
-    if ((st = launch_pdl(dec_attn_combine, dim3(D.n_heads), dim3(hs), 0, s, at, dec->att))) return st;
+    if ((st = launch_pdl(dec_attn_combine, dim3(D.n_heads), dim3(kCombThreads),
+                         (size_t)(nchunk + kCombThreads) * sizeof(float), s, at, dec->att)))
+      return st;
     st = gemv_dev_fast(c, y.wo_type, y.wo, dec->att, dec->y, nq, d, s, nullptr, 0.f, kDecPrefetch);
     if (st == VIREO_ERR_UNSUPPORTED) st = gemv_dev(c, y.wo_type, y.wo, dec->att, dec->y, nq, d, s);
     if (st) return st;
