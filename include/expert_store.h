@@ -21,8 +21,10 @@
  *    (offsets relative to base; pinned by the store while it lives) and the
  *    cache is plain device memory; views are device pointers only.
  *  - expert_store_lookup_async: a miss is copied host -> device on the
- *    store's copy stream; `stream` is made to wait for that copy; returns at
- *    once.
+ *    store's copy stream and the call returns at once; `stream` (NULL = the
+ *    legacy default stream) is made to wait for the expert's copy on a miss,
+ *    and also on a hit while an earlier lookup's copy of that expert may
+ *    still be running.
  *  - expert_store_release_after: the lease ends when the work queued on
  *    `stream` so far has completed (the expert may not be evicted or
  *    overwritten before).
@@ -83,7 +85,7 @@ typedef struct {
     uint64_t h2d_bytes;  /* bytes copied host -> device (misses) */
     uint64_t copies;     /* miss copies issued */
     uint64_t evictions;
-    uint64_t over_budget_loads; /* loads placed outside the budget (all leased) */
+    uint64_t over_budget_loads; /* loads that left resident bytes over the budget (all leased) */
 } ExpertStatsExt;
 void expert_store_stats_ext(const ExpertStore *s, ExpertStatsExt *out);
 

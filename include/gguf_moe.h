@@ -7,10 +7,11 @@
  * SwiGLU and down matvec with a rank-ordered weighted combine (:198-213),
  * adding the result into the residual x.  This header exports that block
  * as a C-ABI call so a host model loop can replace the body of moe_ffn with
- * one gguf_moe_ffn call per layer (see INTEGRATION.md).
+ * one gguf_moe_ffn call per layer.
  *
- * One decode token runs as one persistent cooperative kernel: router,
- * top-k, gate/up + SwiGLU and down + combine, with the expert weights
+ * One decode token runs as one kernel launch with one CTA per SM: router,
+ * top-k, then each selected expert's gate/up + SwiGLU and down on its own
+ * group of CTAs, and the rank-ordered combine, with the expert weights
  * streamed raw (GGUF blocks, no repacking) from HBM. */
 #ifndef VIREO_GGUF_MOE_H
 #define VIREO_GGUF_MOE_H
@@ -43,7 +44,8 @@ typedef struct gguf_moe gguf_moe;
 
 /* Validates the layer, picks the kernel and allocates its device scratch.
  * Fast path: router F32; gate/up (same type) and down in Q8_0/Q4_K/Q6_K;
- * dim % 512 == 0; ffn_exp % 256 == 0; n_experts <= 256; n_used <= 64. */
+ * dim % 512 == 0; ffn_exp % 256 == 0; n_experts <= 256; n_used <= 64 and
+ * at most the GPU's SM count. */
 int gguf_moe_create(const gguf_moe_desc *desc, gguf_moe **out);
 
 /* n_tok independent tokens through the layer, one after another (decode).
@@ -178,13 +180,14 @@ void gguf_moe_ep_destroy(gguf_moe_ep *ep);
  * allocate device memory.  Same computation and arguments as gguf_moe_ffn,
  * with the layer given by its descriptor (device pointers, the rules of
  * gguf_moe_create) instead of a handle.  Allocates nothing: the kernel's
- * scratch is a fixed 64 KiB device array in the library, enough for every
- * shape gguf_moe_create accepts; a shape needing more returns
- * VIREO_ERR_NOMEM.  The first call on a device sets that device up (takes
+ * scratch is a fixed 256 KiB device array in the library (a layer needs
+ * about 17 KiB plus 4 B per value of n_used * (dim + ffn_exp), 128 B per 16
+ * rows of dim and 24 B per expert: 131 KiB for dim 2048, 64 experts top-8,
+ * ffn_exp 1024); a layer needing more returns VIREO_ERR_NOMEM.  The first call on a device sets that device up (takes
  * the array's address, zeroes it) and must come before any stream capture.
- * Every call zeroes the launch's sync and status words first.  The call
- * synchronises stream (NULL = the legacy default stream) and returns the
- * kernel's status.  All calls on one device share the array: calls that
+ * Every call zeroes the launch's sync, status and counter words first.
+ * Every call synchronises stream (NULL = the legacy default stream) before
+ * it returns, also when a launch fails, and returns the kernel's status.  All calls on one device share the array: calls that
  * overlap on the GPU race. */
 int gguf_moe_ffn_noalloc(const gguf_moe_desc *desc, const float *hb, float *x, int n_tok, int32_t *ids,
                          float *wts, void *stream);

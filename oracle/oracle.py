@@ -116,6 +116,19 @@ def ref():
         lib.ref_decoder_destroy.restype = None
         lib.ref_decoder_last_gap.argtypes = []
         lib.ref_decoder_last_gap.restype = C.c_double
+        # the reference's own ExpertStore (src/expert_store.c, compiled into the same library)
+        lib.expert_store_create.argtypes = [C.c_int, C.c_uint64, C.c_int, C.c_int]
+        lib.expert_store_create.restype = C.c_void_p
+        lib.expert_store_register.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+        lib.expert_store_register.restype = None
+        lib.expert_store_lookup.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+        lib.expert_store_lookup.restype = C.c_int
+        lib.expert_store_release.argtypes = [C.c_void_p, C.c_void_p]
+        lib.expert_store_release.restype = None
+        lib.expert_store_stats.argtypes = [C.c_void_p, C.POINTER(ExpertStats)]
+        lib.expert_store_stats.restype = None
+        lib.expert_store_destroy.argtypes = [C.c_void_p]
+        lib.expert_store_destroy.restype = None
         _ref = lib
     return _ref
 

@@ -211,3 +211,149 @@ def test_host_image_store_async_and_deferred_release(V):
         assert ext.over_budget_loads == 0
     finally:
         L.expert_store_destroy(s)
+
+
+STATS_FIELDS = ("requests", "hits", "misses", "bytes_read", "resident_bytes", "capacity_bytes", "experts_resident")
+
+
+def stats_tuple(st):
+    return tuple(int(getattr(st, f)) for f in STATS_FIELDS)
+
+
+def test_store_stats_match_reference_golden(V, golden):
+    """The reference's capped pager on the tiny Q8_0 layer (cap = 3 experts,
+    6 tokens of 2 experts, tests/golden/gen_golden.py): the same lookups and
+    releases, in moe_ffn's order (lookup, compute, release per selected expert,
+    gguf_run.c:199-210), give the reference's counters exactly."""
+    from vireo_b200 import synth as S
+    sp = golden["moe_tiny_q8_spec"]
+    spec = S.MoeLayerSpec(int(sp[0]), int(sp[1]), int(sp[2]), int(sp[3]), int(sp[4]), int(sp[6]), int(sp[7]),
+                          int(sp[8]), router_type=int(sp[5]))
+    ids = golden["moe_tiny_q8_ids"]
+    L = V.lib()
+    gs, us, ds = spec.gate_slice, spec.up_slice, spec.down_slice
+    G, U = gs * spec.n_experts, us * spec.n_experts
+    with tempfile.TemporaryFile() as f:
+        f.write(b"\0" * (G + U + ds * spec.n_experts))
+        f.flush()
+        s = L.expert_store_create(f.fileno(), 3 * spec.expert_bytes, 1, spec.n_experts)
+        try:
+            for e in range(spec.n_experts):
+                L.expert_store_register(s, 0, e, C.byref(V.ExpertSlices(e * gs, G + e * us, G + U + e * ds,
+                                                                         gs, us, ds)))
+            v = V.ExpertView()
+            for row in ids:
+                for e in row:
+                    assert L.expert_store_lookup(s, 0, int(e), C.byref(v)) == 0
+                    L.expert_store_release(s, C.byref(v))
+            got = stats_tuple(stats(V, s))
+        finally:
+            L.expert_store_destroy(s)
+    assert got == tuple(int(v) for v in golden["es_tiny_q8_stats"]), got
+
+
+@pytest.mark.parametrize("uniform", [True, False])
+def test_store_policy_matches_reference_step_by_step(V, uniform):
+    """The device store and the reference's own store (src/expert_store.c,
+    compiled into oracle/_ref) driven by the same seeded sequence of lookups,
+    held leases and releases over slices whose sizes are not multiples of 256
+    bytes (equal for every expert, or different per expert): identical
+    counters after every step, and the bytes behind every view intact."""
+    from oracle import oracle as O
+    if not O.ref_available():
+        pytest.skip("reference library not built")
+    R = O.ref()
+    L = V.lib()
+    nl, ne = 2, 8
+    sizes = {}
+    blobs, off = [], 0
+    for l in range(nl):
+        for e in range(ne):
+            sz = (1000, 1000, 700) if uniform else (1000 + 40 * e, 1000 + 24 * l, 700 + 56 * e)
+            offs = []
+            for k, n in enumerate(sz):
+                blobs.append(pattern(l, e, k, n))
+                offs.append(off)
+                off += n
+            sizes[(l, e)] = (offs, sz)
+    data = np.concatenate(blobs)
+    cap = int(3.5 * data.nbytes / (nl * ne))
+    rng = np.random.default_rng(31 if uniform else 32)
+    with tempfile.TemporaryFile() as f:
+        f.write(data.tobytes())
+        f.flush()
+        ours = L.expert_store_create(f.fileno(), cap, nl, ne)
+        ref = R.expert_store_create(f.fileno(), cap, nl, ne)
+        assert ours and ref
+        held = []
+        try:
+            for (l, e), (offs, sz) in sizes.items():
+                loc = V.ExpertSlices(offs[0], offs[1], offs[2], *sz)
+                L.expert_store_register(ours, l, e, C.byref(loc))
+                R.expert_store_register(ref, l, e, C.byref(loc))
+            for step in range(300):
+                op = rng.random()
+                if op < 0.25 and held:
+                    vo, vr = held.pop(int(rng.integers(len(held))))
+                    L.expert_store_release(ours, C.byref(vo))
+                    R.expert_store_release(ref, C.byref(vr))
+                else:
+                    l, e = int(rng.integers(nl)), int(rng.integers(ne))
+                    vo, vr = V.ExpertView(), V.ExpertView()
+                    assert L.expert_store_lookup(ours, l, e, C.byref(vo)) == 0
+                    assert R.expert_store_lookup(ref, l, e, C.byref(vr)) == 0
+                    offs, sz = sizes[(l, e)]
+                    for ptr, k in ((vo.gate, 0), (vo.up, 1), (vo.down, 2)):
+                        got = np.frombuffer(C.string_at(ptr, sz[k]), dtype=np.uint8)
+                        assert np.array_equal(got, pattern(l, e, k, sz[k])), (step, l, e, k)
+                    if op < 0.45 and len(held) < 3:
+                        held.append((vo, vr))
+                    else:
+                        L.expert_store_release(ours, C.byref(vo))
+                        R.expert_store_release(ref, C.byref(vr))
+                so, sr = V.ExpertStats(), O.ExpertStats()
+                L.expert_store_stats(ours, C.byref(so))
+                R.expert_store_stats(ref, C.byref(sr))
+                assert stats_tuple(so) == stats_tuple(sr), (step, stats_tuple(so), stats_tuple(sr))
+        finally:
+            for vo, vr in held:
+                L.expert_store_release(ours, C.byref(vo))
+                R.expert_store_release(ref, C.byref(vr))
+            L.expert_store_destroy(ours)
+            R.expert_store_destroy(ref)
+
+
+def test_async_hit_waits_for_a_copy_started_by_another_stream(V):
+    """A miss looked up for stream A and then a hit on the same expert for
+    stream B (before A's copy is known complete): B's kernel sees the
+    expert's bytes, because every async lookup orders its stream after the
+    expert's copy.  The NULL stream stands for the legacy default stream."""
+    import torch
+    L = V.lib()
+    rt = cudart()
+    rt.cudaMemcpy.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int]
+    data, locs = expert_file()
+    s = L.expert_store_create_host(data.ctypes.data, data.nbytes, 0, NL, NE)
+    assert s
+    a, b = torch.cuda.Stream(), torch.cuda.Stream()
+    try:
+        register_all(V, s, locs)
+        for e in range(NE):
+            va, vb = V.ExpertView(), V.ExpertView()
+            assert L.expert_store_lookup_async(s, 2, e, C.byref(va), C.c_void_p(a.cuda_stream)) == 0
+            assert L.expert_store_lookup_async(s, 2, e, C.byref(vb), C.c_void_p(b.cuda_stream)) == 0
+            assert vb.down == va.down
+            out = torch.empty(SIZES[2], dtype=torch.uint8, device="cuda")
+            # a device -> device copy on stream b reads the view in b's stream order
+            rt.cudaMemcpyAsync.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int, C.c_void_p]
+            assert rt.cudaMemcpyAsync(out.data_ptr(), vb.down, SIZES[2], 3, C.c_void_p(b.cuda_stream)) == 0
+            b.synchronize()
+            assert np.array_equal(out.cpu().numpy(), pattern(2, e, 2, SIZES[2])), e
+            vn = V.ExpertView()
+            assert L.expert_store_lookup_async(s, 2, e, C.byref(vn), None) == 0  # legacy stream: a hit
+            for v, st in ((va, a), (vb, b)):
+                assert L.expert_store_release_after(s, C.byref(v), C.c_void_p(st.cuda_stream)) == 0
+            L.expert_store_release(s, C.byref(vn))
+        torch.cuda.synchronize()
+    finally:
+        L.expert_store_destroy(s)

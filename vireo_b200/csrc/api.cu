@@ -389,9 +389,10 @@ struct gguf_moe {
   std::vector<const uint8_t*> h_exp_tab;
   void* scratch = nullptr;
   size_t scratch_bytes = 0;
-  float* d_io = nullptr;  // host-API staging: hb, x
-  int32_t* d_ids = nullptr;
-  float* d_wts = nullptr;
+  // host-API staging, the same layout on the device and in pinned host
+  // memory: hb [n][d] | x [n][d] | status (16 B) | ids [n][k] | wts [n][k]
+  uint8_t* d_io = nullptr;
+  uint8_t* h_io = nullptr;
   int io_cap = 0;
   bool pdl = true;
   cudaStream_t stream = nullptr;
@@ -472,33 +473,23 @@ int gguf_moe_create(const gguf_moe_desc* desc, gguf_moe** out) {
     delete m;
     return e != cudaSuccess ? cuda_status(e) : VIREO_ERR_UNSUPPORTED;
   }
+  // one CTA per SM; the k expert groups need at least one CTA each
+  if (c->num_sms < D.n_used) {
+    delete m;
+    return VIREO_ERR_UNSUPPORTED;
+  }
   m->grid = c->num_sms;
   m->num_sms = c->num_sms;
 
-  // scratch: logit partials, h, per-launch sync words, status
-  p.hsx_count = (uint32_t)(D.ffn_exp / kSegElems * kMeta);
-  const size_t n_lp = (size_t)(D.dim / kRouterChunk) * D.n_experts, n_h = (size_t)D.n_used * D.ffn_exp;
-  size_t off = 0;
-  const size_t o_lp = off;
-  off = up256(off + n_lp * 4);
-  const size_t o_h = off;
-  off = up256(off + n_h * 4);
-  const size_t o_sy = off;
-  off = up256(off + sizeof(MoeSync));
-  const size_t o_err = off;
-  off = up256(off + sizeof(int));
-  m->scratch_bytes = off;
+  // scratch: sync words, status, tile counters, router partials, h, down outputs
+  m->scratch_bytes = moe_scratch_bytes(D.dim, D.ffn_exp, D.n_experts, D.n_used);
   if ((st = cuda_status(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking))) ||
-      (st = cuda_status(cudaMalloc(&m->scratch, off))) ||
-      (st = cuda_status(cudaMemset(m->scratch, 0, off)))) {
+      (st = cuda_status(cudaMalloc(&m->scratch, m->scratch_bytes))) ||
+      (st = cuda_status(cudaMemset(m->scratch, 0, m->scratch_bytes)))) {
     gguf_moe_destroy(m);
     return st;
   }
-  uint8_t* sb = (uint8_t*)m->scratch;
-  p.s.logit_part = (float*)(sb + o_lp);
-  p.s.hbuf = (float*)(sb + o_h);
-  p.s.sync = (MoeSync*)(sb + o_sy);
-  p.s.err = (int*)(sb + o_err);
+  moe_scratch_carve((uint8_t*)m->scratch, D.dim, D.ffn_exp, D.n_experts, D.n_used, nullptr, &p.s);
 
   m->h_exp_tab.resize((size_t)3 * D.n_experts);
   for (int ex = 0; ex < D.n_experts; ex++) {
@@ -549,11 +540,11 @@ static int moe_launch(gguf_moe* m, const void* kernel, void** args, cudaStream_t
   return cuda_status(e);
 }
 
-int gguf_moe_ffn(gguf_moe* m, const float* hb, float* x, int n_tok, int32_t* ids, float* wts, void* stream) {
-  if (!m || !hb || !x || n_tok < 0) return VIREO_ERR_ARG;
-  if (((uintptr_t)hb % 16) || ((size_t)m->prm.d * 4) % 16) return VIREO_ERR_ARG;
-  cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
+// n_tok decode launches; the kernels record failures in *err
+static int moe_ffn_launches(gguf_moe* m, const float* hb, float* x, int n_tok, int32_t* ids, float* wts,
+                            cudaStream_t s, int* err) {
   MoeDecodeParams p = m->prm;
+  p.s.err = err;
   for (int i = 0; i < n_tok; i++) {
     p.hb = hb + (size_t)i * p.d;
     p.x = x + (size_t)i * p.d;
@@ -564,6 +555,13 @@ int gguf_moe_ffn(gguf_moe* m, const float* hb, float* x, int n_tok, int32_t* ids
     if (st) return st;
   }
   return VIREO_OK;
+}
+
+int gguf_moe_ffn(gguf_moe* m, const float* hb, float* x, int n_tok, int32_t* ids, float* wts, void* stream) {
+  if (!m || !hb || !x || n_tok < 0) return VIREO_ERR_ARG;
+  if (((uintptr_t)hb % 16) || ((size_t)m->prm.d * 4) % 16) return VIREO_ERR_ARG;
+  cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
+  return moe_ffn_launches(m, hb, x, n_tok, ids, wts, s, m->prm.s.err);
 }
 
 int gguf_moe_ffn_routed(gguf_moe* m, const float* hb, float* x, int n_tok, const int32_t* ids, const float* wts,
@@ -660,36 +658,53 @@ int gguf_moe_sync(gguf_moe* m, void* stream) {
   return VIREO_OK;
 }
 
+// One round trip for n_tok tokens: the inputs and a zeroed status word go
+// to the device in one copy, the launches record failures in that word, and
+// the outputs, the status and the selection come back in one copy.
 int gguf_moe_ffn_host(gguf_moe* m, const float* hb, float* x, int n_tok, int32_t* ids, float* wts) {
   if (!m || !hb || !x || n_tok < 0) return VIREO_ERR_ARG;
   if (n_tok == 0) return VIREO_OK;
-  const size_t d = (size_t)m->prm.d, k = (size_t)m->prm.k;
+  const size_t d = (size_t)m->prm.d, k = (size_t)m->prm.k, n = (size_t)n_tok;
+  const size_t o_x = n * d * 4, o_st = 2 * n * d * 4, o_ids = o_st + 16, o_wts = o_ids + n * k * 4,
+               total = o_wts + n * k * 4;
   int st;
   if (n_tok > m->io_cap) {
     cudaFree(m->d_io);
-    cudaFree(m->d_ids);
-    cudaFree(m->d_wts);
+    cudaFreeHost(m->h_io);
     m->d_io = nullptr;
-    m->d_ids = nullptr;
-    m->d_wts = nullptr;
+    m->h_io = nullptr;
     m->io_cap = 0;
-    if ((st = cuda_status(cudaMalloc(&m->d_io, 2 * d * n_tok * 4))) ||
-        (st = cuda_status(cudaMalloc(&m->d_ids, k * n_tok * 4))) ||
-        (st = cuda_status(cudaMalloc(&m->d_wts, k * n_tok * 4))))
+    if ((st = cuda_status(cudaMalloc(&m->d_io, total))) ||
+        (st = cuda_status(cudaMallocHost(&m->h_io, total))))
       return st;
     m->io_cap = n_tok;
   }
-  float* dh = m->d_io;
-  float* dx = m->d_io + d * n_tok;
   cudaStream_t s = m->stream;
-  if ((st = cuda_status(cudaMemcpyAsync(dh, hb, d * n_tok * 4, cudaMemcpyHostToDevice, s))) ||
-      (st = cuda_status(cudaMemcpyAsync(dx, x, d * n_tok * 4, cudaMemcpyHostToDevice, s))))
-    return st;
-  if ((st = gguf_moe_ffn(m, dh, dx, n_tok, m->d_ids, m->d_wts, s))) return st;
-  if ((st = cuda_status(cudaMemcpyAsync(x, dx, d * n_tok * 4, cudaMemcpyDeviceToHost, s)))) return st;
-  if (ids && (st = cuda_status(cudaMemcpyAsync(ids, m->d_ids, k * n_tok * 4, cudaMemcpyDeviceToHost, s)))) return st;
-  if (wts && (st = cuda_status(cudaMemcpyAsync(wts, m->d_wts, k * n_tok * 4, cudaMemcpyDeviceToHost, s)))) return st;
-  return gguf_moe_sync(m, s);
+  // the previous call's device-to-host copy has completed (that call synchronised)
+  memcpy(m->h_io, hb, n * d * 4);
+  memcpy(m->h_io + o_x, x, n * d * 4);
+  memset(m->h_io + o_st, 0, 16);
+  if ((st = cuda_status(cudaMemcpyAsync(m->d_io, m->h_io, o_st + 16, cudaMemcpyHostToDevice, s)))) return st;
+  int* d_status = (int*)(m->d_io + o_st);
+  st = moe_ffn_launches(m, (const float*)m->d_io, (float*)(m->d_io + o_x), n_tok, (int32_t*)(m->d_io + o_ids),
+                        (float*)(m->d_io + o_wts), s, d_status);
+  if (!st)
+    st = cuda_status(cudaMemcpyAsync(m->h_io + o_x, m->d_io + o_x, total - o_x, cudaMemcpyDeviceToHost, s));
+  const int sync = cuda_status(cudaStreamSynchronize(s));
+  if (st) return st;
+  if (sync) return sync;
+  int herr = 0;
+  memcpy(&herr, m->h_io + o_st, sizeof(int));
+  if (herr) {
+    // a launch gave up: its sync words may be left mid-protocol
+    moe_reset_scratch(m, s);
+    cudaStreamSynchronize(s);
+    return herr;
+  }
+  memcpy(x, m->h_io + o_x, n * d * 4);
+  if (ids) memcpy(ids, m->h_io + o_ids, n * k * 4);
+  if (wts) memcpy(wts, m->h_io + o_wts, n * k * 4);
+  return VIREO_OK;
 }
 
 int gguf_moe_set_expert_ptrs(gguf_moe* m, const void* const* gate, const void* const* up, const void* const* down) {
@@ -721,8 +736,7 @@ void gguf_moe_destroy(gguf_moe* m) {
   cudaFree(m->scratch);
   cudaFree(m->d_exp_tab);
   cudaFree(m->d_io);
-  cudaFree(m->d_ids);
-  cudaFree(m->d_wts);
+  cudaFreeHost(m->h_io);
   if (m->stream) cudaStreamDestroy(m->stream);
   delete m;
 }

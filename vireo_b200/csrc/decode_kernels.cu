@@ -1,6 +1,6 @@
-// Decode kernels: the MoE FFN block (one token, all phases in one
-// cooperative launch) and the stand-alone quantised GEMV behind
-// gguf_matmul.  See moe_decode.cuh and engine.cuh for the design.
+// Decode kernels: the MoE FFN block (one token per launch, all phases in
+// one kernel) and the stand-alone quantised GEMV behind gguf_matmul.  See
+// moe_decode.cuh and engine.cuh for the design.
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -15,7 +15,6 @@ struct Ctl {
   float wsum;  // renorm denominator
   int ids[kMaxTopK];
   float wts[kMaxTopK];
-  int tile_cnt[2];  // down units finished per tile buffer
   float nred[kConsumerWarps];  // gemv_kernel: per-warp sums of squares for the fused norm
 };
 
@@ -82,23 +81,155 @@ VDEV void stage_vec_cg8(const float* g, float* s, int n, int tid, int nthr) {
   }
 }
 
+// Softmax and top-k of the router logits by warps 0 .. R - 1 (R = ne / 32
+// rounded up).  Warp w sums the chunk partials of experts 32 w .. 32 w + 31
+// in chunk order (logit e) into lg; then every one of the R warps takes the
+// softmax of all the logits with expf into its own copy of p (pw + w ne) and
+// ranks its 32 experts against it: expert e takes rank r = #{j : p_j > p_e,
+// or p_j == p_e and j < e}, the position the reference's greedy strict-'>'
+// selection gives it (gguf_run.c:190-191).  Ranks < k are the selection, in
+// rank order (NaN never selected; unused slots hold id -1 and weight -1, as
+// the reference's scan leaves them).  The weights are the probabilities;
+// renormalisation comes later (route_finish).  lg: 32 R floats; pw: R ne
+// floats (shared memory).
+VDEV void route_warps(const MoeDecodeParams& p, Ctl* ctl, float* lg, float* pw, int warp, int lane) {
+  constexpr int kPer = kMaxExperts / 32;
+  const int ne = p.ne, k = p.k, nchunk = p.d / kRouterChunk, R = (ne + 31) / 32;
+  {
+    // every load issued at once (clamped addresses), then the chunk-order sum
+    const int e = 32 * warp + lane, ec = min(e, ne - 1);
+    float pc[8];
+#pragma unroll
+    for (int c = 0; c < 8; c++) pc[c] = __ldcg(p.s.logit_part + (size_t)min(c, nchunk - 1) * ne + ec);
+    float v = 0.f;
+#pragma unroll
+    for (int c = 0; c < 8; c++)
+      if (c < nchunk) v += pc[c];
+    lg[e] = e < ne ? v : -INFINITY;
+  }
+  named_bar(2, 32 * R);
+  float lv[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; i++) lv[i] = i < R ? lg[lane + 32 * i] : -INFINITY;
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < kPer; i++) m = fmaxf(m, lv[i]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float ex[kPer], sm = 0.f;
+#pragma unroll
+  for (int i = 0; i < kPer; i++) {
+    ex[i] = (i < R && lane + 32 * i < ne) ? expf(lv[i] - m) : 0.f;
+    sm += ex[i];
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+  float* pr = pw + (size_t)warp * ne;
+  int nvalid = 0;
+#pragma unroll
+  for (int i = 0; i < kPer; i++) {
+    const int e = lane + 32 * i;
+    if (i < R && e < ne) {
+      const float pe = ex[i] / sm;
+      pr[e] = pe;
+      nvalid += !isnan(pe);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) nvalid += __shfl_xor_sync(0xffffffffu, nvalid, o);
+  __syncwarp();
+  const int e = 32 * warp + lane;
+  if (e < ne) {
+    const float pe = pr[e];
+    int rank = 0;
+    const float4* pr4 = reinterpret_cast<const float4*>(pr);
+#pragma unroll 4
+    for (int j4 = 0; j4 < ne / 4; j4++) {
+      const float4 q = pr4[j4];
+      const int j = 4 * j4;
+      rank += (q.x > pe) || (q.x == pe && j < e);
+      rank += (q.y > pe) || (q.y == pe && j + 1 < e);
+      rank += (q.z > pe) || (q.z == pe && j + 2 < e);
+      rank += (q.w > pe) || (q.w == pe && j + 3 < e);
+    }
+    for (int j = ne & ~3; j < ne; j++) rank += (pr[j] > pe) || (pr[j] == pe && j < e);
+    if (!isnan(pe) && rank < k) {
+      ctl->ids[rank] = e;
+      ctl->wts[rank] = pe;
+    }
+  }
+  if (warp == 0)
+    for (int t = lane; t < k; t += 32)
+      if (t >= nvalid) {
+        ctl->ids[t] = -1;
+        ctl->wts[t] = -1.f;
+      }
+}
+
+// One thread, after the selection is published: the optional
+// renormalisation by the sequential rank-order sum of the weights
+// (gguf_run.c:192), and the selection out.
+VDEV void route_finish(const MoeDecodeParams& p, Ctl* ctl, bool write_out) {
+  const int k = p.k;
+  float ws = 0.f;
+#pragma unroll 1
+  for (int j = 0; j < k; j++) ws = ws + ctl->wts[j];
+#pragma unroll 1
+  for (int t = 0; t < k; t++) {
+    float w = ctl->wts[t];
+    if (p.renorm && ws > 0.f) w = w / ws;
+    ctl->wts[t] = w;
+    if (write_out) {
+      if (p.ids_out) p.ids_out[t] = ctl->ids[t];
+      if (p.wts_out) p.wts_out[t] = w;
+    }
+  }
+}
+
+// Segments [s0, s1) of one 16-row weight tile (rows g and g + 8 of lane
+// (g, t)) against the activation tables, summed in segment order: every
+// lane of a quad ends holding its two rows' sums.
+template <class SF>
+VDEV void tile_dot(const uint8_t* stage, const StageGeom& sg, int s0, int s1, const uint8_t* btab, const float* meta,
+                   const LaneCtx& L, BFrag& bf, float& a0, float& a1) {
+  const uint8_t* r0 = stage_row(stage, sg, L.g);
+  const uint8_t* r1 = stage_row(stage, sg, L.g + 8);
+  a0 = 0.f;
+  a1 = 0.f;
+#pragma unroll 1
+  for (int seg = s0; seg < s1; seg++) {
+    float tot0 = 0.f, tot1 = 0.f;
+    bf.get(btab + seg * kSegTabBytes, L);
+    SF::run(r0 + seg * SF::kSegBytes, r1 + seg * SF::kSegBytes, bf, meta + seg * kMeta, L, tot0, tot1);
+    tot0 += __shfl_xor_sync(0xffffffffu, tot0, 1);
+    tot1 += __shfl_xor_sync(0xffffffffu, tot1, 1);
+    tot0 += __shfl_xor_sync(0xffffffffu, tot0, 2);
+    tot1 += __shfl_xor_sync(0xffffffffu, tot1, 2);
+    a0 += tot0;
+    a1 += tot1;
+  }
+}
+
+// The consumer warps work in kUnitGroups groups of kUnitWarps warps; the
+// warps of a group share each unit or tile, warp r taking a contiguous run
+// of its segments, and the group's first warp adds the warps' sums in warp
+// order (named barrier 2 + group between them).
+constexpr int kUnitWarps = 4;
+constexpr int kUnitGroups = kConsumerWarps / kUnitWarps;
+
 // The decode kernel body.  ROUTED: the route comes from the caller (rt) and
 // the router phase is skipped; otherwise every CTA computes it.
 template <class SG, class SD, bool ROUTED>
 __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const MoeRoute* rt) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ float red[kDecodeThreads / 32 + 1];
-  // gate/up ring (S stages) and down ring (SD slots over the same memory)
+  // gate/up ring (S stages) and down ring (slots over the same memory)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kMaxStages;
   uint64_t* full_d = empty + kMaxStages;
   uint64_t* empty_d = full_d + kMaxStages;
   Ctl* ctl = reinterpret_cast<Ctl*>(smem + p.off_ctl);
-  float* part = reinterpret_cast<float*>(smem + p.off_part);
-  float* part_d = reinterpret_cast<float*>(smem + p.off_part_d);
-  int* ucnt = reinterpret_cast<int*>(smem + p.off_ucnt);
-  int* ucnt_d = ucnt + kMaxStages;
-  float* ytile = reinterpret_cast<float*>(smem + p.off_ytile); // [2][k][16] expert rows of a tile
+  const uint8_t** etab = reinterpret_cast<const uint8_t**>(smem + p.off_etab);  // [ne][3] expert slices
+  float* part = reinterpret_cast<float*>(smem + p.off_part);  // [groups][2][kUnitWarps][16] warp sums
   uint8_t* xtab = smem + p.off_xtab;
   float* xsx = reinterpret_cast<float*>(smem + p.off_xsx);
   uint8_t* htab = smem + p.off_htab;
@@ -110,24 +241,25 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
   constexpr int W = kConsumerWarps;
   constexpr int NC = W * 32;  // consumer threads
   const int G = gridDim.x, cta = blockIdx.x;
-  const int d = p.d, fe = p.fe, ne = p.ne, k = p.k, S = p.nstages, SD_ = p.nstages_d;
+  const int d = p.d, fe = p.fe, ne = p.ne, k = p.k, S = p.nstages;
   MoeSync* sy = p.s.sync;
 
   if (threadIdx.x == 0) {
     trace(p, kTrStart);
     for (int s = 0; s < S; s++) {
       mbar_init(&full[s], kProducerThreads);  // every producer's copies
-      mbar_init(&empty[s], W);
+      mbar_init(&empty[s], 1);                // the unit's first warp
     }
-    for (int s = 0; s < SD_; s++) {
+    for (int s = 0; s < kMaxStages; s++) {
       mbar_init(&full_d[s], kProducerThreads);
-      mbar_init(&empty_d[s], W);
+      mbar_init(&empty_d[s], 1);
     }
     ctl->abort = 0;
-    ctl->tile_cnt[0] = ctl->tile_cnt[1] = 0;
     mbar_fence_init();
   }
-  for (int i = threadIdx.x; i < 2 * kMaxStages; i += blockDim.x) ucnt[i] = 0;
+  // expert slice table (weights metadata: not written by the previous kernel)
+  if constexpr (!ROUTED)
+    for (int i = threadIdx.x; i < 3 * ne; i += blockDim.x) etab[i] = p.exp_tab[i];
   // the next token's kernel may start its own prologue as SMs free up
   pdl_launch_dependents();
 
@@ -148,10 +280,9 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
     __syncthreads();
     if (threadIdx.x == 0) trace(p, kTrRouted);
   } else {
-  // ---- phase R: router partial dot products --------------------------------
-  // Router rows are weights (independent of the previous kernel): their loads
-  // are issued before waiting on the previous kernel in the stream.
-  {
+    // ---- phase R: router partial dot products --------------------------------
+    // Router rows are weights (independent of the previous kernel): their loads
+    // are issued before waiting on the previous kernel in the stream.
     const int nchunk = d / kRouterChunk;
     const int ntask = ne * nchunk, nw = G * (int)(blockDim.x / 32);
     const int gw = warp * G + cta;  // spread tasks over all CTAs first
@@ -186,18 +317,18 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
         for (int i = 0; i < 4; i++) r[i] = __ldg(row + lane + 32 * i);
       }
       const float4* xv = reinterpret_cast<const float4*>(p.hb + (size_t)c * kRouterChunk);
-      float s = 0.f;
+      float sdot = 0.f;
 #pragma unroll
       for (int i = 0; i < 4; i++) {
         const float4 xx = __ldg(xv + lane + 32 * i);
-        s = fmaf(r[i].x, xx.x, s);
-        s = fmaf(r[i].y, xx.y, s);
-        s = fmaf(r[i].z, xx.z, s);
-        s = fmaf(r[i].w, xx.w, s);
+        sdot = fmaf(r[i].x, xx.x, sdot);
+        sdot = fmaf(r[i].y, xx.y, sdot);
+        sdot = fmaf(r[i].z, xx.z, sdot);
+        sdot = fmaf(r[i].w, xx.w, sdot);
       }
 #pragma unroll
-      for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane == 0) p.s.logit_part[(size_t)c * ne + e] = s;
+      for (int o = 16; o; o >>= 1) sdot += __shfl_xor_sync(0xffffffffu, sdot, o);
+      if (lane == 0) p.s.logit_part[(size_t)c * ne + e] = sdot;
     }
     __syncthreads();
     // every CTA has written its router partials once router_arrive == G
@@ -212,148 +343,81 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
       trace(p, kTrPartials);
     }
     __syncthreads();
-    // ---- softmax + top-k in every CTA (no second hop) ----------------------
-    // logits l[e] = sum of the chunk partials in chunk order; p = softmax(l);
-    // expert e takes rank r = #{j : p_j > p_e, or p_j == p_e and j < e}, the
-    // position the reference's greedy strict-'>' selection gives it
-    // (gguf_run.c:190-191); ranks < k are the selection.  NaN never ranks.
-    float* pr = reinterpret_cast<float*>(htab);  // probabilities (htab idle until the down phase)
-    if (!aborted(ctl)) {
-      float lv = -INFINITY;
-      const int e = threadIdx.x;
-      if (e < ne) {
-        float part_c[8];
-#pragma unroll
-        for (int c = 0; c < 8; c++) part_c[c] = (c < nchunk) ? __ldcg(p.s.logit_part + (size_t)c * ne + e) : 0.f;
-        lv = 0.f;
-#pragma unroll
-        for (int c = 0; c < 8; c++)
-          if (c < nchunk) lv += part_c[c];
-      }
-      float m = lv;
-#pragma unroll
-      for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      if (lane == 0) red[warp] = m;
-      __syncthreads();
-      float mx = -INFINITY;
-      for (int i = 0; i < (int)(blockDim.x / 32); i++) mx = fmaxf(mx, red[i]);
-      const float ex = (e < ne) ? expf(lv - mx) : 0.f;
-      float sm = ex;
-#pragma unroll
-      for (int o = 16; o; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
-      __syncthreads();
-      if (lane == 0) red[warp] = sm;
-      __syncthreads();
-      float sum = 0.f;
-      for (int i = 0; i < (int)(blockDim.x / 32); i++) sum += red[i];
-      const float pe = ex / sum;
-      if (e < ne) pr[e] = pe;
-      __syncthreads();
-      if (e < ne && !isnan(pe)) {
-        int rank = 0;
-        const float4* pr4 = reinterpret_cast<const float4*>(pr);
-#pragma unroll 4
-        for (int j4 = 0; j4 < ne / 4; j4++) {
-          const float4 q = pr4[j4];
-          const int j = 4 * j4;
-          rank += (q.x > pe) || (q.x == pe && j < e);
-          rank += (q.y > pe) || (q.y == pe && j + 1 < e);
-          rank += (q.z > pe) || (q.z == pe && j + 2 < e);
-          rank += (q.w > pe) || (q.w == pe && j + 3 < e);
-        }
-        for (int j = ne & ~3; j < ne; j++) {
-          const float pj = pr[j];
-          rank += (pj > pe) || (pj == pe && j < e);
-        }
-        if (rank < k) {
-          ctl->ids[rank] = e;
-          ctl->wts[rank] = pe;
-        }
-      }
-      // fewer than k selectable experts (NaN probabilities): unused slots
-      // hold id -1, weight -1 as in the reference's scan
-      const int nsel = __syncthreads_count(e < ne && !isnan(pe));
-      const int t = threadIdx.x;
-      if (t < k && t >= nsel) {
-        ctl->ids[t] = -1;
-        ctl->wts[t] = -1.f;
-      }
-      __syncthreads();
-      if (t == 0) {
-        // renorm denominator: the sequential rank-order sum (gguf_run.c:192)
-        float ws = 0.f;
-#pragma unroll 1
-        for (int j = 0; j < k; j++) ws = ws + ctl->wts[j];
-        ctl->wsum = ws;
-      }
-      __syncthreads();
-      if (t < k) {
-        const float ws = ctl->wsum;
-        float w = ctl->wts[t];
-        if (p.renorm && ws > 0.f) w = w / ws;
-        ctl->wts[t] = w;
-        if (cta == 0) {
-          if (p.ids_out) p.ids_out[t] = ctl->ids[t];
-          if (p.wts_out) p.wts_out[t] = w;
-        }
-      }
-      if (t == 0) trace(p, kTrRouted);
-    }
+    // logits in stg (the x table is built), probabilities in htab (idle
+    // until the down phase)
+    if (warp < (ne + 31) / 32 && !aborted(ctl))
+      route_warps(p, ctl, stg, reinterpret_cast<float*>(htab), warp, lane);
     __syncthreads();
-  }
+    if (threadIdx.x == 0) trace(p, kTrRouted);
   }
 
-  // device address of slice `which` (0 gate, 1 up, 2 down) of expert slot t
-  auto expert_ptr = [&](int t, int which) -> const uint8_t* {
+  // ---- this CTA's share of one selected expert ---------------------------------
+  // group t (the expert of rank t) = CTAs [t G / k, (t + 1) G / k), i.e.
+  // t = ((cta + 1) k - 1) / G; CTA j of the m in the group takes an even
+  // share of the expert's fe / 8 gate/up units and of its d / 16 down tiles
+  const int t = ((cta + 1) * k - 1) / G;
+  const int c0 = t * G / k, c1 = (t + 1) * G / k;
+  const int m = c1 - c0, j = cta - c0;
+  const int U = fe / 8, NT = d / 16;
+  const int u0 = j * U / m, u1 = (j + 1) * U / m;
+  const int i0 = j * NT / m, i1 = (j + 1) * NT / m;
+  const bool active = !aborted(ctl) && ctl->ids[t] >= 0;
+  const int nG = active ? u1 - u0 : 0, nD = i1 - i0;  // an unused slot still counts its tiles
+  // Down slots: after the gate/up stages this CTA uses when all of its tiles
+  // fit there (no wait on gate/up), else over the whole ring, each slot's
+  // first use waiting for the gate/up stages under it.
+  const int nGs = min(nG, S);
+  const int sd_after = min((int)((uint32_t)(S - nGs) * p.stage_bytes / p.dslot_bytes), kMaxStages);
+  const bool dsep = nD > 0 && sd_after >= nD;
+  const int SDn = dsep ? sd_after : p.nstages_d;
+  uint8_t* dring = stages + (dsep ? (size_t)nGs * p.stage_bytes : 0);
+  float* xs = reinterpret_cast<float*>(smem + p.off_xs);  // residual rows of this CTA's tiles
+  for (int i = threadIdx.x; i < 16 * nD; i += blockDim.x) xs[i] = p.x[16 * i0 + i];
+  const uint8_t* gsl = nullptr;
+  const uint8_t* usl = nullptr;
+  const uint8_t* dsl = nullptr;
+  if (active) {
     if constexpr (ROUTED) {
-      return ctl->ids[t] < 0 ? nullptr : rt->ptr[t][which];
+      gsl = rt->ptr[t][0];
+      usl = rt->ptr[t][1];
+      dsl = rt->ptr[t][2];
     } else {
       const int e = ctl->ids[t];
-      return e < 0 ? nullptr : p.exp_tab[3 * e + which];
+      gsl = etab[3 * e + 0];
+      usl = etab[3 * e + 1];
+      dsl = etab[3 * e + 2];
     }
-  };
+  }
 
-  const int rgG = fe / 8, UG = k * rgG, ntile = d / 16;
-  const int g0 = (int)((long long)cta * UG / G), g1 = (int)((long long)(cta + 1) * UG / G);
-  const int my_tiles = (cta < ntile) ? (ntile - 1 - cta) / G + 1 : 0;
-
-  const int nG = g1 - g0, nD = my_tiles * k;
   if (warp >= W) {
     // ---- producers: 16-byte cp.async copies ---------------------------------
     const int ptid = threadIdx.x - NC;
-    // gate/up units: a contiguous range per CTA
     if (ptid == 0) trace(p, kTrProdFirst);
-    for (int v = 0; v < nG; v++) {
-      const int slot = v % S;
-      if (!warp_wait(&empty[slot], ((uint32_t)(v / S) & 1u) ^ 1u, ctl, p.s.err)) break;
-      const int u = g0 + v, t = u / rgG, rg = u - t * rgG;
-      const uint8_t* gb = expert_ptr(t, 0);
-      const uint8_t* ub = expert_ptr(t, 1);
-      const uint8_t* gsrc = gb ? gb + (size_t)(8 * rg) * p.sg_gu.rb : nullptr;
-      const uint8_t* usrc = ub ? ub + (size_t)(8 * rg) * p.sg_gu.rb : nullptr;
-      issue_unit(stages + (size_t)slot * p.stage_bytes, &full[slot], gsrc, usrc, p.sg_gu, ptid, kProducerThreads);
-    }
-    // down units: every expert slot of each of this CTA's 16-row tiles, in
-    // the down ring.  A slot's first use waits for the last release of every
-    // gate/up stage it overlaps (the down weights do not depend on h, so
-    // they stream in while gate/up is still being consumed).
-    if (ptid == 0) trace(p, kTrProdFirstD);
-    for (int j = 0; j < nD && !aborted(ctl); j++) {
-      const int slot = j % SD_;
-      bool ok = true;
-      if (j < SD_) {
-        const uint32_t lo = (uint32_t)slot * p.dslot_bytes, hi = lo + p.dslot_bytes - 1u;
-        for (int st = (int)(lo / p.stage_bytes); ok && st <= (int)(hi / p.stage_bytes) && st < nG; st++)
-          ok = warp_wait(&empty[st], (uint32_t)((nG - 1 - st) / S) & 1u, ctl, p.s.err);
-      } else {
-        ok = warp_wait(&empty_d[slot], ((uint32_t)(j / SD_) & 1u) ^ 1u, ctl, p.s.err);
+    if (active) {
+      for (int v = 0; v < nG; v++) {
+        const int slot = v % S;
+        if (!warp_wait(&empty[slot], ((uint32_t)(v / S) & 1u) ^ 1u, ctl, p.s.err)) break;
+        const size_t row = (size_t)(8 * (u0 + v)) * p.sg_gu.rb;
+        issue_unit(stages + (size_t)slot * p.stage_bytes, &full[slot], gsl + row, usl + row, p.sg_gu, ptid,
+                   kProducerThreads);
       }
-      if (!ok) break;
-      const int i = j / k, t = j - i * k, tile = cta + i * G;
-      const uint8_t* db = expert_ptr(t, 2);
-      const uint8_t* src = db ? db + (size_t)(16 * tile) * p.sg_d.rb : nullptr;
-      issue_unit(stages + (size_t)slot * p.dslot_bytes, &full_d[slot], src, src ? src + 8 * (size_t)p.sg_d.rb : nullptr,
-                 p.sg_d, ptid, kProducerThreads);
+      if (ptid == 0) trace(p, kTrProdFirstD);
+      for (int jj = 0; jj < nD && !aborted(ctl); jj++) {
+        const int slot = jj % SDn;
+        bool ok = true;
+        if (jj >= SDn) {
+          ok = warp_wait(&empty_d[slot], ((uint32_t)(jj / SDn) & 1u) ^ 1u, ctl, p.s.err);
+        } else if (!dsep) {
+          // first use of a slot over the gate/up stages: their last release
+          const uint32_t lo = (uint32_t)slot * p.dslot_bytes, hi = lo + p.dslot_bytes - 1u;
+          for (int st = (int)(lo / p.stage_bytes); ok && st <= (int)(hi / p.stage_bytes) && st < nG; st++)
+            ok = warp_wait(&empty[st], (uint32_t)((nG - 1 - st) / S) & 1u, ctl, p.s.err);
+        }
+        if (!ok) break;
+        const uint8_t* src = dsl + (size_t)(16 * (i0 + jj)) * p.sg_d.rb;
+        issue_unit(dring + (size_t)slot * p.dslot_bytes, &full_d[slot], src, src + 8 * (size_t)p.sg_d.rb, p.sg_d,
+                   ptid, kProducerThreads);
+      }
     }
     if (ptid == 0) trace(p, kTrProdLast);
     cp_async_wait_all();  // no copy may still target this CTA's shared memory at exit
@@ -361,101 +425,135 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
     return;
   }
 
-  // ---- consumers -------------------------------------------------------------
+  // ---- consumers ----------------------------------------------------------------
   const LaneCtx L = lane_ctx();
+  const int q = warp / kUnitWarps, r = warp - q * kUnitWarps;  // unit group, warp in it
+  const int nsg = d / kSegElems, nsd = fe / kSegElems;
   BFrag bf;
   bf.reset();
-  for (int v = 0; v < nG; v++) {
+  if (threadIdx.x == 0 && !ROUTED && !aborted(ctl)) route_finish(p, ctl, cta == 0);  // read after the G phase
+  // gate/up units: unit v to group v mod kUnitGroups
+  int nst = 0;  // warp 0's unit stamps
+#pragma unroll 1
+  for (int v = q, it = 0; v < nG; v += kUnitGroups, it++) {
     const int slot = v % S;
-    if (!warp_wait(&full[slot], (uint32_t)(v / S) & 1u, ctl, p.s.err)) break;
-    const int u = g0 + v;
-    if (threadIdx.x == 0 && v < kTrUnits) trace(p, kTrUnitBase + 2 * v);
-    const int t = u / rgG, rg = u - t * rgG;
-    const bool active = ctl->ids[t] >= 0;
-    float val = 0.f;
-    const bool last = consume<SG>(stages + (size_t)slot * p.stage_bytes, p.sg_gu, v, p.d / kSegElems, warp, xtab,
-                                  xsx, part + slot * p.part_stride, &ucnt[slot], L, &val, active, bf);
-    if (last) {
-      const float up = __shfl_sync(0xffffffffu, val, (lane + 8) & 31);
-      float hv = 0.f;
-      if (active && lane < 8) {
-        // the reference's SwiGLU, gguf_run.c:206
-        hv = (val / (1.0f + expf(-val))) * up;
-        p.s.hbuf[(size_t)t * fe + 8 * rg + lane] = hv;
+    const bool ok = warp_wait(&full[slot], (uint32_t)(v / S) & 1u, ctl, p.s.err);
+    if (warp == 0 && lane == 0 && nst < kTrUnits) trace(p, kTrUnitBase + 2 * nst);
+    float g = 0.f, u = 0.f;
+    if (warp == 1 && lane == 0 && it == 0) trace(p, kTrDbg + 6);
+    if (ok)
+      tile_dot<SG>(stages + (size_t)slot * p.stage_bytes, p.sg_gu, r * nsg / kUnitWarps, (r + 1) * nsg / kUnitWarps,
+                   xtab, xsx, L, bf, g, u);
+    if (warp == 1 && lane == 0 && it == 0) trace(p, kTrDbg + 7);
+    float* pb = part + (size_t)((q * 2 + (it & 1)) * kUnitWarps) * 16;
+    if (L.t == 0) {
+      pb[r * 16 + L.g] = g;
+      pb[r * 16 + L.g + 8] = u;
+    }
+    named_bar(2 + q, kUnitWarps * 32);
+    if (r == 0) {
+      if (lane == 0) mbar_arrive(&empty[slot]);  // every warp of the group is done with the stage
+      if (lane < 8 && ok) {
+        float gs = 0.f, us = 0.f;
+#pragma unroll
+        for (int rr = 0; rr < kUnitWarps; rr++) {
+          gs += pb[rr * 16 + lane];
+          us += pb[rr * 16 + 8 + lane];
+        }
+        // rows 0..7 of a unit are gate rows, 8..15 the matching up rows: the
+        // reference's SwiGLU, gguf_run.c:206
+        p.s.hbuf[(size_t)t * fe + 8 * (u0 + v) + lane] = (gs / (1.0f + expf(-gs))) * us;
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);
-    if (threadIdx.x == 0 && v < kTrUnits) trace(p, kTrUnitBase + 2 * v + 1);
+    if (warp == 0 && lane == 0 && nst < kTrUnits) trace(p, kTrUnitBase + 2 * nst + 1);
+    nst++;
   }
-  // publish this CTA's gate/up results (h rows in scratch): one count
+  __threadfence();  // this warp's h values before the group's count
   named_bar(1, NC);
   if (threadIdx.x == 0) {
     trace(p, kTrGDone);
-    __threadfence();
-    red_add_release_gpu(&sy->g_done.v, (unsigned)(g1 - g0));
+    if (nG > 0) red_add_release_gpu(&sy->group[t].v, (unsigned)nG);
   }
 
-  if (my_tiles > 0) {
-    // ---- every h row written: build the k down-projection B tables ----------
-    if (threadIdx.x == 0) {
-      if (!aborted(ctl) && !wait_geq(&sy->g_done.v, (unsigned)UG, p.s.err)) ctl->abort = 1;
-      trace(p, kTrGAll);
-    }
-    named_bar(1, NC);
-    if (!aborted(ctl)) {
-      if (threadIdx.x == 0) trace(p, kTrDbg + 0);
-      // h rows (written by other CTAs) into the table area with coalesced
-      // 16-byte loads, then the tables built in place
-      stage_vec_cg8(p.s.hbuf, reinterpret_cast<float*>(htab), k * fe, threadIdx.x, NC);
+  if (nD > 0) {
+    if (active) {
+      // ---- the group's h row complete: stage it, build its tables ------------
+      if (threadIdx.x == 0) {
+        if (!aborted(ctl) && !wait_geq(&sy->group[t].v, (unsigned)U, p.s.err)) ctl->abort = 1;
+        trace(p, kTrGAll);
+      }
       named_bar(1, NC);
-      if (threadIdx.x == 0) trace(p, kTrDbg + 2);
-      build_tables<SD>(reinterpret_cast<const float*>(htab), htab, hsx, k * fe / kSegElems, warp, W, lane);
-      if (threadIdx.x == 0) trace(p, kTrDbg + 1);
+      if (!aborted(ctl)) {
+        stage_vec_cg8(p.s.hbuf + (size_t)t * fe, reinterpret_cast<float*>(htab), fe, threadIdx.x, NC);
+        named_bar(1, NC);
+        build_tables<SD>(reinterpret_cast<const float*>(htab), htab, hsx, nsd, warp, W, lane);
+      }
+      named_bar(1, NC);
+      if (threadIdx.x == 0) trace(p, kTrHtab);
     }
-    named_bar(1, NC);
-    if (threadIdx.x == 0) trace(p, kTrHtab);
-
-    // ---- down units: tile-major, combined in this CTA ------------------------
-    for (int i = 0, j = 0; i < my_tiles; i++) {
-      const int tb = i & 1;
-      for (int t = 0; t < k; t++, j++) {
-        const int slot = j % SD_;
-        const bool ok = warp_wait(&full_d[slot], (uint32_t)(j / SD_) & 1u, ctl, p.s.err);
-        if (threadIdx.x == 0 && nG + j < kTrUnits) trace(p, kTrUnitBase + 2 * (nG + j));
-        const int tile = cta + i * G;
-        const bool active = ok && ctl->ids[t] >= 0;
-        float val = 0.f;
-        const bool last = consume<SD>(stages + (size_t)slot * p.dslot_bytes, p.sg_d, j, fe / kSegElems, warp,
-                                      htab + (size_t)t * p.htab_bytes, hsx + (size_t)t * p.hsx_count,
-                                      part_d + slot * p.part_stride, &ucnt_d[slot], L, &val, active, bf);
-        if (last) {
-          if (lane < 16) ytile[(tb * k + t) * 16 + lane] = active ? val : 0.f;
-          __syncwarp();
-          int done = 0;
-          if (lane == 0) {
-            __threadfence_block();
-            done = (atomicAdd(&ctl->tile_cnt[tb], 1) == k - 1);
-          }
-          done = __shfl_sync(0xffffffffu, done, 0);
-          if (done) {
-            __threadfence_block();
-            if (lane < 16 && ok) {
-              // the reference's combine order: acc = sum over rank t of w_t * y_t, then x += acc
-              const int r = 16 * tile + lane;
-              float acc = 0.f;
-              for (int tt = 0; tt < k; tt++)
-                if (ctl->ids[tt] >= 0)
-                  acc = __fadd_rn(acc, __fmul_rn(ctl->wts[tt], ((volatile float*)ytile)[(tb * k + tt) * 16 + lane]));
-              p.x[r] = __fadd_rn(p.x[r], acc);
-            }
-            __syncwarp();
-            if (lane == 0) ctl->tile_cnt[tb] = 0;
+    // ---- down tiles: tile jj to group jj mod kUnitGroups ------------------
+    float* yb = p.s.ybuf + (size_t)t * d;
+    if (active) {
+#pragma unroll 1
+      for (int jj = q, it = 0; jj < nD; jj += kUnitGroups, it++) {
+        const int slot = jj % SDn;
+        const bool ok = warp_wait(&full_d[slot], (uint32_t)(jj / SDn) & 1u, ctl, p.s.err);
+        if (warp == 0 && lane == 0 && nst < kTrUnits) trace(p, kTrUnitBase + 2 * nst);
+        if (warp == 1 && lane == 0 && it < 3) trace(p, kTrDbg + 2 * it);
+        float y0 = 0.f, y1 = 0.f;
+        if (ok)
+          tile_dot<SD>(dring + (size_t)slot * p.dslot_bytes, p.sg_d, r * nsd / kUnitWarps, (r + 1) * nsd / kUnitWarps,
+                       htab, hsx, L, bf, y0, y1);
+        if (warp == 1 && lane == 0 && it < 3) trace(p, kTrDbg + 2 * it + 1);
+        float* pb = part + (size_t)((q * 2 + (it & 1)) * kUnitWarps) * 16;
+        if (L.t == 0) {
+          pb[r * 16 + L.g] = y0;
+          pb[r * 16 + L.g + 8] = y1;
+        }
+        named_bar(2 + q, kUnitWarps * 32);
+        if (r == 0) {
+          if (lane == 0) mbar_arrive(&empty_d[slot]);
+          if (lane < 16 && ok) {
+            float y = 0.f;
+#pragma unroll
+            for (int rr = 0; rr < kUnitWarps; rr++) y += pb[rr * 16 + lane];
+            yb[16 * (i0 + jj) + lane] = y;
           }
         }
+        if (warp == 0 && lane == 0 && nst < kTrUnits) trace(p, kTrUnitBase + 2 * nst + 1);
+        nst++;
+      }
+    }
+    // ---- count this CTA's tiles, all at once; the last of the k experts to
+    // finish a tile combines them --------------------------------------------
+    __threadfence();  // the tiles' rows before their counts
+    named_bar(1, NC);
+#pragma unroll 1
+    for (int jj = warp; jj < nD; jj += W) {
+      const int tile = i0 + jj;
+      int last = 0;
+      if (lane == 0) last = atomicAdd(&p.s.tile_cnt[(size_t)tile * kTileCntStride], 1u) == (unsigned)(k - 1);
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {
+        __threadfence();
+        if (lane < 16 && !aborted(ctl)) {
+          // the reference's combine order: acc = sum over rank tt of w_tt * y_tt, then x += acc
+          const int row = 16 * tile + lane;
+          float acc = 0.f;
+#pragma unroll 1
+          for (int t0 = 0; t0 < k; t0 += 8) {
+            float yv[8];  // eight experts' rows in flight at once
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+              yv[u] = (t0 + u < k && ctl->ids[t0 + u] >= 0) ? __ldcg(p.s.ybuf + (size_t)(t0 + u) * d + row) : 0.f;
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+              if (t0 + u < k && ctl->ids[t0 + u] >= 0) acc = __fadd_rn(acc, __fmul_rn(ctl->wts[t0 + u], yv[u]));
+          }
+          p.x[row] = __fadd_rn(xs[16 * jj + lane], acc);
+        }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty_d[slot]);
-        if (threadIdx.x == 0 && nG + j < kTrUnits) trace(p, kTrUnitBase + 2 * (nG + j) + 1);
+        if (lane == 0) p.s.tile_cnt[(size_t)tile * kTileCntStride] = 0u;
       }
     }
   }
@@ -466,7 +564,7 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
   if (threadIdx.x == 0) {
     if (atom_add_acq_rel_gpu(&sy->exit_cnt.v, 1u) == (unsigned)G - 1u) {
       sy->router_arrive.v = 0u;
-      sy->g_done.v = 0u;
+      for (int tt = 0; tt < k; tt++) sy->group[tt].v = 0u;
       __threadfence();
       sy->exit_cnt.v = 0u;
     }
@@ -640,48 +738,68 @@ const void* moe_decode_kernel_for(uint32_t gtype, uint32_t dtype, bool routed) {
 // Shared-memory layout for the MoE kernel; picks the deepest stage ring that
 // fits.  Returns the dynamic shared-memory bytes (0 if nothing fits).
 uint32_t moe_decode_layout(MoeDecodeParams* p, uint32_t smem_limit, int grid) {
-  (void)grid;
-  const int W = kConsumerWarps;
   const uint32_t stage = up_to(std::max(2u * p->sg_gu.hstride, 2u * p->sg_d.hstride), 128u);
   const uint32_t dslot = up_to(2u * p->sg_d.hstride, 128u);
   p->stage_bytes = stage;
   p->dslot_bytes = dslot;
-  p->htab_bytes = (uint32_t)(4 * p->fe);
-  const uint32_t htab_region = std::max((uint32_t)p->k * p->htab_bytes, (uint32_t)(4 * p->ne));
-  const uint32_t stg_bytes = (uint32_t)std::max(4 * p->d, 4 * p->k);
-  p->part_stride = (uint32_t)std::max(W, std::max(p->d, p->fe) / kSegElems) * 16u;
+  uint32_t off = 4u * kMaxStages * 8u;  // full/empty barriers of both rings
+  p->off_ctl = off;
+  off = up_to(off + (uint32_t)sizeof(Ctl), 16);
+  p->off_etab = off;
+  off = up_to(off + (uint32_t)(3 * p->ne * sizeof(void*)), 16);
+  p->off_part = off;
+  off = up_to(off + (uint32_t)(kUnitGroups * 2 * kUnitWarps * 16 * 4), 16);
+  p->off_xtab = off;
+  off = up_to(off + (uint32_t)(4 * p->d), 16);
+  p->off_xsx = off;
+  off = up_to(off + (uint32_t)(p->d / kSegElems * kMeta * 4), 16);
+  p->off_htab = off;  // one expert's h tables; the routing warps' probabilities before that
+  off = up_to(off + (uint32_t)std::max(4 * p->fe, 4 * p->ne * ((p->ne + 31) / 32)), 16);
+  p->off_hsx = off;
+  off = up_to(off + (uint32_t)((p->fe / kSegElems) * kMeta * 4), 16);
+  p->off_xs = off;  // residual rows of a CTA's tiles: at most d / 16 / floor(grid / k) + 1 tiles
+  off = up_to(off + (uint32_t)(64 * (p->d / 16 / std::max(1, grid / std::max(1, p->k)) + 1)), 16);
+  p->off_stg = off;
+  off = up_to(off + (uint32_t)std::max(4 * p->d, 4 * p->k), 128);
+  p->off_stage = off;
   for (int S = kMaxStages; S >= 2; S--) {
     const int SD = (int)std::min<uint32_t>((uint32_t)kMaxStages, (uint32_t)S * stage / dslot);
-    uint32_t off = 4u * kMaxStages * 8u;  // full/empty barriers of both rings
-    p->off_ctl = off;
-    off = up_to(off + (uint32_t)sizeof(Ctl), 16);
-    p->off_part = off;
-    off = up_to(off + (uint32_t)S * p->part_stride * 4u, 16);
-    p->off_part_d = off;
-    off = up_to(off + (uint32_t)SD * p->part_stride * 4u, 16);
-    p->off_ucnt = off;
-    off = up_to(off + (uint32_t)(2 * kMaxStages * 4), 16);
-    p->off_ytile = off;
-    off = up_to(off + (uint32_t)(2 * p->k * 16 * 4), 16);
-    p->off_xtab = off;
-    off = up_to(off + (uint32_t)(4 * p->d), 16);
-    p->off_xsx = off;
-    off = up_to(off + (uint32_t)(p->d / kSegElems * kMeta * 4), 16);
-    p->off_htab = off;
-    off = up_to(off + htab_region, 16);
-    p->off_hsx = off;
-    off = up_to(off + (uint32_t)(p->k * (p->fe / kSegElems) * kMeta * 4), 16);
-    p->off_stg = off;
-    off = up_to(off + stg_bytes, 128);
-    p->off_stage = off;
-    off += (uint32_t)S * stage + 16;
-    if (off <= smem_limit && SD >= 1) {
+    const uint32_t total = off + (uint32_t)S * stage + 16;
+    if (total <= smem_limit && SD >= 1) {
       p->nstages = S;
       p->nstages_d = SD;
-      return off;
+      return total;
     }
   }
   return 0;
+}
+
+static size_t up256s(size_t v) { return (v + 255) & ~(size_t)255; }
+
+size_t moe_scratch_bytes(int d, int fe, int ne, int k) {
+  size_t off = 0;
+  off = up256s(off + sizeof(MoeSync));
+  off = up256s(off + sizeof(int));                                       // status
+  off = up256s(off + (size_t)(d / 16) * kTileCntStride * 4);              // tile counters
+  off = up256s(off + 4 * (size_t)(d / kRouterChunk) * ne);                // router partials
+  off = up256s(off + 4 * (size_t)k * fe);                                 // h
+  off = up256s(off + 4 * (size_t)k * d);                                  // down outputs
+  return off;
+}
+
+void moe_scratch_carve(uint8_t* base, int d, int fe, int ne, int k, int* err, MoeScratch* s) {
+  size_t off = 0;
+  s->sync = (MoeSync*)(base + off);
+  off = up256s(off + sizeof(MoeSync));
+  s->err = err ? err : (int*)(base + off);
+  off = up256s(off + sizeof(int));
+  s->tile_cnt = (unsigned int*)(base + off);
+  off = up256s(off + (size_t)(d / 16) * kTileCntStride * 4);
+  s->logit_part = (float*)(base + off);
+  off = up256s(off + 4 * (size_t)(d / kRouterChunk) * ne);
+  s->hbuf = (float*)(base + off);
+  off = up256s(off + 4 * (size_t)k * fe);
+  s->ybuf = (float*)(base + off);
 }
 
 const void* gemv_kernel_for(uint32_t type) {

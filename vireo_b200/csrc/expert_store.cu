@@ -12,12 +12,17 @@
 // lease and zeroes the view (:91-95); stats copy the counters (:97-102).
 //
 // Device side: a resident expert is one frame [gate | up | down] (each slice
-// 256-byte aligned) in a chunk of device memory sized to the budget,
-// allocated first-fit from a coalescing free list; a frame that does not fit
-// even after every evictable expert is gone goes to a separate allocation
-// (counted as an over-budget load).  Misses are copied host -> device on the
-// store's copy stream, from the host image (create_host), from the fd's
-// pages mapped and pinned, or through a pinned staging buffer after pread.
+// 256-byte aligned) in a chunk of device memory, allocated first-fit from a
+// coalescing free list.  With a budget the chunk holds budget / (first
+// expert's bytes) + 1 frames of the first expert's size, so when every
+// expert has that size a frame fits whenever the byte count does; eviction
+// follows the byte count alone, exactly as the reference, and a frame that
+// finds no hole (slices of other sizes fragmented the chunk) gets a separate
+// allocation.  Misses are copied host -> device on the store's copy stream,
+// from the host image (create_host), from the fd's pages mapped and pinned,
+// or through a pinned staging buffer after pread; each load records an
+// event on the copy stream, and every later lookup of the expert orders the
+// caller's work after it until the copy is seen complete.
 #include <cuda_runtime.h>
 #include <fcntl.h>
 #include <stdint.h>
@@ -79,6 +84,8 @@ struct Slot {
   uint64_t last_used = 0;
   uint8_t* dev = nullptr;
   int chunk = -1;  // index into chunks, or -1 for a separate allocation
+  cudaEvent_t ready = nullptr;  // recorded on the copy stream after the last load
+  bool loaded = false;          // that load is known to have completed
 };
 
 }  // namespace
@@ -175,14 +182,16 @@ cudaError_t device_alloc(ExpertStore* s, uint8_t** p, uint64_t bytes) {
   return cudaMalloc((void**)p, bytes);
 }
 
-// a frame for slot i: from a chunk (evicting the coldest unleased experts
-// until one fits), else a separate allocation
+// a frame for slot i: from a chunk, else a separate allocation.  No expert
+// is evicted here: eviction is the byte-count rule of lookup_impl alone.
 bool place(ExpertStore* s, int i) {
   Slot& sl = s->slots[i];
   if (s->chunks.empty()) {
-    // first use (budgeted: one chunk of the budget; unbounded: grow by >= 256 MiB)
+    // first use.  Budgeted: room for budget / bytes + 1 frames of this
+    // expert's size.  Unbounded: grow by >= 256 MiB.
     Chunk c;
-    c.size = s->capacity_bytes ? up256(s->capacity_bytes) : std::max<uint64_t>(256ull << 20, sl.frame);
+    c.size = s->capacity_bytes ? up256((s->capacity_bytes / std::max<uint64_t>(sl.bytes, 1) + 1) * sl.frame)
+                               : std::max<uint64_t>(256ull << 20, sl.frame);
     if (device_alloc(s, &c.base, c.size) != cudaSuccess) return false;
     c.free_[0] = c.size;
     s->chunks.push_back(c);
@@ -196,22 +205,16 @@ bool place(ExpertStore* s, int i) {
         return true;
       }
     }
-    if (s->capacity_bytes == 0) {  // unbounded: add a chunk
-      Chunk c;
-      c.size = std::max<uint64_t>(256ull << 20, sl.frame);
-      if (device_alloc(s, &c.base, c.size) != cudaSuccess) return false;
-      c.free_[0] = c.size;
-      s->chunks.push_back(c);
-      continue;
-    }
-    const int v = lru_victim(s);
-    if (v < 0) break;
-    evict(s, v);
+    if (s->capacity_bytes) break;
+    Chunk c;  // unbounded: add a chunk
+    c.size = std::max<uint64_t>(256ull << 20, sl.frame);
+    if (device_alloc(s, &c.base, c.size) != cudaSuccess) return false;
+    c.free_[0] = c.size;
+    s->chunks.push_back(c);
   }
-  // every evictable expert is gone and no hole fits: over budget
+  // no hole of this size in the budgeted chunk
   if (device_alloc(s, &sl.dev, sl.frame) != cudaSuccess) return false;
   sl.chunk = -1;
-  s->ext.over_budget_loads++;
   return true;
 }
 
@@ -240,7 +243,30 @@ bool load(ExpertStore* s, int i) {
     dst += up256(lens[k]);
   }
   s->ext.copies++;
+  if (ok && !sl.ready) ok = cudaEventCreateWithFlags(&sl.ready, cudaEventDisableTiming) == cudaSuccess;
+  if (ok) ok = cudaEventRecord(sl.ready, s->copy) == cudaSuccess;
+  sl.loaded = false;
   return ok;
+}
+
+// Orders work after slot i's last load: the host (sync) or `stream` (NULL =
+// the legacy default stream) waits for the load's event unless the load is
+// already known complete.  False if a CUDA call fails.
+bool order_after_load(Slot& sl, bool sync, cudaStream_t stream) {
+  if (sl.loaded || !sl.ready) return true;
+  const cudaError_t q = cudaEventQuery(sl.ready);
+  if (q == cudaSuccess) {
+    sl.loaded = true;
+    return true;
+  }
+  if (q != cudaErrorNotReady) return false;
+  cudaGetLastError();  // cudaErrorNotReady is not an error here
+  if (sync) {
+    if (cudaEventSynchronize(sl.ready) != cudaSuccess) return false;
+    sl.loaded = true;
+    return true;
+  }
+  return cudaStreamWaitEvent(stream, sl.ready, 0) == cudaSuccess;
 }
 
 void fill_view(const Slot& sl, int i, ExpertView* v, ExpertStore* s) {
@@ -250,8 +276,10 @@ void fill_view(const Slot& sl, int i, ExpertView* v, ExpertStore* s) {
   v->slot = &s->slots[i];
 }
 
-// lookup body; `wait_on` (may be null) is made to wait for a miss's copy
-int lookup_impl(ExpertStore* s, int layer, int expert, ExpertView* view, cudaStream_t wait_on, bool sync) {
+// lookup body.  sync: the view is usable by the host and by any stream on
+// return; otherwise `stream` (NULL = the legacy default stream) is ordered
+// after the expert's copy, on a hit as well as on a miss.
+int lookup_impl(ExpertStore* s, int layer, int expert, ExpertView* view, cudaStream_t stream, bool sync) {
   if (!s || !view) return -1;
   if (layer < 0 || layer >= s->n_layers || expert < 0 || expert >= s->n_experts) {
     memset(view, 0, sizeof(*view));
@@ -275,6 +303,7 @@ int lookup_impl(ExpertStore* s, int layer, int expert, ExpertView* view, cudaStr
         if (v < 0) break;  // all resident experts are leased: stay over budget
         evict(s, v);
       }
+      if (s->resident_bytes + sl.bytes > s->capacity_bytes) s->ext.over_budget_loads++;
     }
     if (!place(s, i) || !load(s, i)) {
       if (sl.dev) {
@@ -289,17 +318,10 @@ int lookup_impl(ExpertStore* s, int layer, int expert, ExpertView* view, cudaStr
     sl.resident = true;
     s->resident_bytes += sl.bytes;
     s->st.experts_resident++;
-    if (sync) {
-      if (cudaStreamSynchronize(s->copy) != cudaSuccess) {
-        memset(view, 0, sizeof(*view));
-        return -1;
-      }
-    } else if (wait_on) {
-      cudaEvent_t e = get_event(s);
-      if (!e || cudaEventRecord(e, s->copy) != cudaSuccess || cudaStreamWaitEvent(wait_on, e, 0) != cudaSuccess)
-        cudaStreamSynchronize(s->copy);
-      if (e) s->event_pool.push_back(e);  // recorded work keeps the wait valid after reuse
-    }
+  }
+  if (!order_after_load(sl, sync, stream)) {
+    cudaStreamSynchronize(s->copy);  // last resort: the copy is done when this returns
+    sl.loaded = true;
   }
   sl.last_used = ++s->tick;
   sl.lease++;
@@ -446,8 +468,10 @@ void expert_store_destroy(ExpertStore* s) {
     cudaEventDestroy(pr.second);
   }
   for (cudaEvent_t e : s->event_pool) cudaEventDestroy(e);
-  for (auto& sl : s->slots)
+  for (auto& sl : s->slots) {
     if (sl.resident && sl.chunk < 0 && sl.dev) cudaFree(sl.dev);
+    if (sl.ready) cudaEventDestroy(sl.ready);
+  }
   for (auto& c : s->chunks) cudaFree(c.base);
   if (s->staging) cudaFreeHost(s->staging);
   if (s->image_registered) cudaHostUnregister((void*)s->image);

@@ -1,4 +1,4 @@
-// Batch-1 MoE FFN decode: one persistent cooperative kernel per token.
+// Batch-1 MoE FFN decode: one kernel launch per token.
 //
 // Replaces, for one token, the reference's moe_ffn (vireo src/gguf_run.c:
 // 185-214): router matvec (:187), softmax (:181-182, :188), greedy top-k
@@ -6,20 +6,25 @@
 // (:192), per expert gate/up matvec + SwiGLU + down matvec (:198-208), the
 // weighted combine in rank order (:209) and the residual add (:213).
 //
-// Phases (one CTA per SM, all co-resident):
+// One CTA per SM, every CTA resident (each cross-CTA wait is bounded).
 //   R  router partial dot products, 512-value K chunks, one warp per task
-//      -> grid barrier ->
-//      every CTA sums the partials in chunk order, softmax, top-k, renorm
-//   G  units (expert slot t, 8 rows): 8 gate rows + 8 up rows per MMA tile,
-//      epilogue h = silu(g) * u into scratch
-//      -> grid barrier (consumers only; the producer keeps streaming the
-//         down rows, which do not depend on h) ->
-//   D  units (expert slot t, 16 rows of the down matrix); epilogue writes the
-//      expert's rows and the last of the k experts to finish a 16-row tile
-//      combines them in rank order into the residual.
+//      -> grid arrival counter -> every CTA: one warp sums the partials in
+//      chunk order, takes the softmax and ranks the top-k.
+//   The CTAs are then split into k groups, group t serving the expert of
+//   rank t; a CTA of group t streams its share of that expert's gate/up
+//   rows and then its share of the expert's down rows (16-row tiles), all
+//   into one shared-memory ring, so the down rows arrive while gate/up is
+//   still computed.
+//   G  units of 8 gate + 8 up rows, one warp per unit: h = silu(g) * u into
+//      the expert's h row in scratch; the group counts finished units.
+//   D  once the group's units are all counted, the CTA stages the expert's h,
+//      builds its activation tables and runs its down tiles, one warp per
+//      tile; each tile's 16 outputs go to scratch, and the last of the k
+//      groups to finish a tile combines the k experts' rows in rank order
+//      and adds them into the residual.
 // The weight stages form two rings over one shared-memory area: gate/up
-// units in stages sized for them, down units in (usually smaller) slots of
-// their own, so that more down units are in flight during gate/up.
+// units in stages sized for them, down tiles in (usually smaller) slots of
+// their own.
 #pragma once
 #include <stdint.h>
 
@@ -33,7 +38,9 @@ constexpr int kProducerThreads = 32 * kProducerWarps;
 constexpr int kDecodeThreads = 32 * (kConsumerWarps + kProducerWarps);
 constexpr int kRouterChunk = 512;
 constexpr int kMaxTopK = 64;
-constexpr int kMaxHValues = 8192;  // n_used * ffn_exp: h scratch and the down tables in shared memory
+constexpr int kMaxExperts = 256;
+constexpr int kMaxHValues = 8192;  // n_used * ffn_exp
+constexpr int kTileCntStride = 32;  // words between two tiles' counters (one 128-byte line each)
 
 // Per-launch synchronisation words in device scratch.  All start at zero;
 // the last CTA to leave a launch puts them back to zero.
@@ -44,14 +51,17 @@ struct alignas(256) SyncWord {
   unsigned int pad[63];
 };
 struct MoeSync {
-  SyncWord router_arrive;  // CTAs done with their router partials
-  SyncWord g_done;         // gate/up units finished (added once per CTA)
-  SyncWord exit_cnt;       // CTAs done with the launch
+  SyncWord router_arrive;    // CTAs done with their router partials
+  SyncWord exit_cnt;         // CTAs done with the launch
+  SyncWord group[kMaxTopK];  // gate/up units finished per expert slot
 };
 
+// Device scratch of one layer handle (or of the fixed no-allocation array).
 struct MoeScratch {
-  float* logit_part;  // [d/512][ne]
-  float* hbuf;        // [k][fe]
+  float* logit_part;        // [d/512][ne] router partials
+  float* hbuf;              // [k][fe] h rows of the selected experts
+  float* ybuf;              // [k][d] down outputs of the selected experts
+  unsigned int* tile_cnt;   // [d/16][kTileCntStride]: expert rows finished per 16-row tile; back to 0 by the combiner
   MoeSync* sync;
   int* err;
 };
@@ -71,13 +81,14 @@ struct MoeDecodeParams {
   uint32_t dslot_bytes;  // down ring: nstages_d slots of dslot_bytes over the same memory
   int nstages_d;
   // shared-memory offsets (bytes)
-  uint32_t off_part, off_part_d, off_ucnt, off_ytile, off_ctl, off_xtab, off_xsx, off_htab, off_hsx, off_stg,
-      off_stage;
-  uint32_t htab_bytes;  // per expert table bytes
-  uint32_t hsx_count;   // activation metadata floats per expert table
-  uint32_t part_stride; // floats of segment partials per stage
+  uint32_t off_ctl, off_etab, off_part, off_xtab, off_xsx, off_htab, off_hsx, off_xs, off_stg, off_stage;
   unsigned long long* trace;  // optional: kTraceSlots %globaltimer stamps per CTA
 };
+
+// Scratch bytes of a layer and the pointers into a block of that size (256-
+// byte aligned); the sync words and the tile counters must start at zero.
+size_t moe_scratch_bytes(int d, int fe, int ne, int k);
+void moe_scratch_carve(uint8_t* base, int d, int fe, int ne, int k, int* err, MoeScratch* s);
 
 // A route given by the caller (routed launches, no router phase): rank-order
 // expert ids (-1 = unused slot), gate weights as used in the combine, and the
@@ -93,7 +104,7 @@ struct MoeRoute {
 enum TraceSlot {
   kTrStart = 0, kTrRouterDone, kTrPartials, kTrRouted, kTrGDone, kTrGAll, kTrHtab, kTrDDone,
   kTrProdFirst, kTrProdFirstD, kTrProdLast, kTrProdDrained,
-  kTrUnitBase = 16,  // per-unit stamps for the first kTrUnits units: ready, done
+  kTrUnitBase = 16,  // warp 0's first kTrUnits units: (ready, done)
   kTrUnits = 24, kTrDbg = 64, kTraceSlots = 72
 };
 

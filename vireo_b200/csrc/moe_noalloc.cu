@@ -2,20 +2,22 @@
 // not allocate device memory.
 //
 // The launch is the one gguf_moe_ffn makes (same kernel, same parameters),
-// except that the kernel's scratch (per-launch sync words, status word,
-// expert pointer table, router partials, h) lives in the file-scope array
-// below instead of a cudaMalloc'd block, and the descriptor is taken per
-// call instead of through a gguf_moe handle.  Nothing here calls cudaMalloc,
-// cudaFree, stream creation or any allocating library routine.
+// except that the kernel's scratch (per-launch sync words, status word, tile
+// counters, router partials, h, the experts' down outputs, the expert
+// pointer table) lives in the file-scope array below instead of a
+// cudaMalloc'd block, and the descriptor is taken per call instead of
+// through a gguf_moe handle.  Nothing here calls cudaMalloc, cudaFree,
+// stream creation or any allocating library routine.
 //
 // Set-up: the first call on a device (with that device current) takes the
 // array's address with cudaGetSymbolAddress, reads the SM count and the
 // shared-memory limit, and zeroes the array.  That first call must come
 // before any stream capture.
 //
-// Every call first zeroes the words that must start at zero (the sync words
-// and the status word; the kernel's last CTA also puts the sync words back),
-// and uploads the expert pointer table.  All calls on one device share the
+// Every call first zeroes the words that must start at zero (the sync words,
+// the status word and the tile counters; the kernel also puts the sync words
+// and counters back), and uploads the expert pointer table.  Every call
+// synchronises its stream before returning, also when a launch fails.  All calls on one device share the
 // one array: calls whose work overlaps on the GPU (other streams, other host
 // threads) race on it.
 #include <cuda_runtime.h>
@@ -31,10 +33,13 @@
 namespace vireo {
 namespace {
 
-// sync words (768 B) + status (256 B) + expert table (<= 6 KiB for 256
-// experts) + router partials (<= 8 KiB) + h (<= 32 KiB): 64 KiB covers every
-// shape gguf_moe_create accepts
-constexpr size_t kNoAllocScratchBytes = 64 * 1024;
+// 256 KiB.  A layer needs the sync words (16.9 KiB), the status word, 128 B
+// per 16 output rows of tile counters, 4 B per (512-value chunk, expert) of
+// router partials, 4 B per value of the k selected experts' h rows and of
+// their d outputs, and 24 B per expert of pointers: 131 KiB for the
+// OLMoE-shaped layer (d 2048, 64 experts top-8, fe 1024), 128 KiB for the
+// Qwen3-shaped one.  A layer needing more is refused with VIREO_ERR_NOMEM.
+constexpr size_t kNoAllocScratchBytes = 256 * 1024;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 constexpr int kMaxDevices = 64;
@@ -108,20 +113,11 @@ extern "C" int gguf_moe_ffn_noalloc(const gguf_moe_desc* desc, const float* hb, 
     return fail(VIREO_ERR_UNSUPPORTED);
   if (((uintptr_t)hb % 16) || ((size_t)D.dim * 4) % 16) return fail(VIREO_ERR_ARG);
 
-  // scratch layout inside the fixed array
-  size_t off = 0;
-  const size_t o_sy = off;
-  off = up256(off + sizeof(MoeSync));
-  const size_t o_err = off;
-  off = up256(off + sizeof(int));
-  const size_t zero_bytes = off;  // everything before here must start at zero
-  const size_t o_tab = off;
-  off = up256(off + sizeof(void*) * 3 * (size_t)D.n_experts);
-  const size_t o_lp = off;
-  off = up256(off + 4 * (size_t)(D.dim / kRouterChunk) * D.n_experts);
-  const size_t o_h = off;
-  off = up256(off + 4 * (size_t)D.n_used * D.ffn_exp);
-  if (off > kNoAllocScratchBytes) return fail(VIREO_ERR_NOMEM);  // beyond the fixed scratch array
+  // scratch layout inside the fixed array: the layer's scratch, then the
+  // expert pointer table
+  const size_t o_tab = moe_scratch_bytes(D.dim, D.ffn_exp, D.n_experts, D.n_used);
+  const size_t need = o_tab + up256(sizeof(void*) * 3 * (size_t)D.n_experts);
+  if (need > kNoAllocScratchBytes) return fail(VIREO_ERR_NOMEM);  // beyond the fixed scratch array
   if (n_tok == 0) return VIREO_OK;
 
   DevSetup* S = nullptr;
@@ -143,13 +139,12 @@ extern "C" int gguf_moe_ffn_noalloc(const gguf_moe_desc* desc, const float* hb, 
   if ((st = cuda_status(
            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S->smem_limit))))
     return fail(st);
-  p.hsx_count = (uint32_t)(D.ffn_exp / kSegElems * kMeta);
+  if (S->num_sms < D.n_used) return fail(VIREO_ERR_UNSUPPORTED);  // one CTA per expert group at least
   uint8_t* sb = S->scratch;
-  p.s.sync = (MoeSync*)(sb + o_sy);
-  p.s.err = (int*)(sb + o_err);
+  moe_scratch_carve(sb, D.dim, D.ffn_exp, D.n_experts, D.n_used, nullptr, &p.s);
   p.exp_tab = (const uint8_t* const*)(sb + o_tab);
-  p.s.logit_part = (float*)(sb + o_lp);
-  p.s.hbuf = (float*)(sb + o_h);
+  // the words that must start at zero: sync words, status, tile counters
+  const size_t zero_bytes = (size_t)((uint8_t*)p.s.logit_part - sb);
 
   // expert pointer table, staged on the stack (pageable: the copy has
   // consumed it when cudaMemcpyAsync returns)
@@ -181,12 +176,17 @@ extern "C" int gguf_moe_ffn_noalloc(const gguf_moe_desc* desc, const float* hb, 
     p.ids_out = ids ? ids + (size_t)i * p.k : nullptr;
     p.wts_out = wts ? wts + (size_t)i * p.k : nullptr;
     void* args[] = {&p};
-    if ((st = cuda_status(cudaLaunchKernelExC(&cfg, kernel, args)))) return fail(st);
+    if ((st = cuda_status(cudaLaunchKernelExC(&cfg, kernel, args)))) {
+      // earlier launches of this call may still be using the shared array:
+      // wait for them before reporting, so that the next call starts clean
+      cudaStreamSynchronize(s);
+      return fail(st);
+    }
   }
   // the kernel's status word: wait for the launches, read it back
   if ((st = cuda_status(cudaStreamSynchronize(s)))) return fail(st);
   int herr = 0;
-  if ((st = cuda_status(cudaMemcpy(&herr, sb + o_err, sizeof(int), cudaMemcpyDeviceToHost)))) return fail(st);
+  if ((st = cuda_status(cudaMemcpy(&herr, p.s.err, sizeof(int), cudaMemcpyDeviceToHost)))) return fail(st);
   if (herr) {
     // a launch gave up (timeout/abort): leave zeroed words for the next call
     cudaMemset(sb, 0, zero_bytes);
