@@ -157,6 +157,14 @@ def cpu_reference_rate(layer, toks, seconds, threads, warm=4):
     return n / el, n, el, kind
 
 
+def ref_build_name(kind):
+    """Compiler target of the reference library that produced a CPU rate."""
+    if kind != "reference":
+        return "port"
+    from oracle import oracle as O
+    return O.ref_build()
+
+
 def host_threads():
     try:
         return len(os.sched_getaffinity(0))
@@ -165,38 +173,62 @@ def host_threads():
 
 
 def run_reference(args, spec_w):
-    """--impl reference: the reference CPU path on the host cores."""
+    """--impl reference: the reference's own moe_ffn (compiled from its
+    sources, oracle/_ref) on the host cores, over the same layer and the same
+    tokens as our arm, T tokens per step.  Under torchrun only rank 0 runs."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     spec = spec_w["spec"]()
     layer = S.MoeLayer(spec, spec_w["seed"])
-    toks, _ = S.routed_tokens(layer, 256, spec_w["seed"])
+    T = args.tokens
+    toks, _ = S.routed_tokens(layer, min(T, 1000), spec_w["seed"])
+    nt = toks.shape[0]
     th = host_threads()
     from oracle import oracle as O
     O.build(ref=False)
     kind = "reference" if O.ref_available() else "port"
     impl = O.RefMoe(layer) if kind == "reference" else O.PortMoe(layer)
     (O.ref().ref_set_threads if kind == "reference" else O.port().orc_set_threads)(th)
-    per_step = 16
+
+    def step():
+        done = 0
+        while done < T:
+            n = min(nt, T - done)
+            impl(toks[:n])
+            done += n
+
     impl(toks[:8])
-    for i in range(args.warmup):
-        impl(toks[(i * per_step) % 240:(i * per_step) % 240 + per_step])
+    for _ in range(args.warmup):
+        step()
     t0 = time.perf_counter()
-    for i in range(args.steps):
-        j = (i * per_step) % 240
-        impl(toks[j:j + per_step])
+    for _ in range(args.steps):
+        step()
     el = time.perf_counter() - t0
-    tps = args.steps * per_step / el
+    tps = args.steps * T / el
+    per_tok = spec.bytes_per_token()
     line = {"metric": "moe_decode_tok_per_s", "value": tps, "unit": "tok/s", "impl": "reference",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded GGUF blocks, random-init)",
-            "config": {"workload": args.workload, "desc": spec_w["desc"], "tokens_per_step": per_step},
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded GGUF blocks, random-init weights)",
+            "config": {"workload": args.workload, "desc": spec_w["desc"], "baseline_config": spec_w["config"],
+                       "tokens_per_step": T, "batch": 1, "parallelism": "host cores",
+                       "l2": "host caches (the reference's CPU path)", "bytes_per_token": per_tok},
             "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": th, "kind": kind,
-                             "sample": f"{args.steps} steps x {per_step} tokens, OMP threads={th}"},
+                             "build": O.ref_build() if kind == "reference" else "port",
+                             "sample": f"{args.steps} steps x {T} tokens, OMP threads={th}"},
             "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if kind == "reference":
+        impl.close()
     print(json.dumps(line), flush=True)
+
+
+SUB_RECORDS = {
+    # name: (workload, steps, warmup, CPU-baseline seconds)
+    "cfg4_prefill": ("qwen3_prefill", 10, 3, 8.0),
+    "cfg3_decoder": ("qwen3_decoder", 64, 3, 8.0),
+    "cfg5_cached": ("qwen3_cached_decode", 3, 2, 6.0),
+}
 
 
 def main():
@@ -210,6 +242,11 @@ def main():
     ap.add_argument("--copies", type=int, default=8, help="layer copies rotated per token")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sub", action="store_true",
+                    help="cfg1_moe_decode: skip the config 3/4/5 sub-records")
+    ap.add_argument("--sub", default=None,
+                    help="cfg1_moe_decode: comma-separated sub-records to run (default: all of "
+                         + ", ".join(SUB_RECORDS) + ")")
     ap.add_argument("--prompt", type=int, default=None, help="decoder workloads: prompt tokens (default: the config's)")
     ap.add_argument("--timeline", default=None,
                     help="prefill only: after the timed steps, record 3 more steps under the CUDA activity "
@@ -219,25 +256,72 @@ def main():
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
         return run_reference(args, wl)
-    if args.workload == "qwen3_cached_decode":
-        return run_cached(args, wl)
-    if args.workload == "qwen3_prefill":
-        return run_prefill(args, wl)
-    if args.workload in ("olmoe_decoder", "qwen3_decoder"):
-        return run_decoder(args, wl)
+    runner = {"qwen3_cached_decode": run_cached, "qwen3_prefill": run_prefill, "olmoe_decoder": run_decoder,
+              "qwen3_decoder": run_decoder}.get(args.workload, run_cfg1)
+    try:
+        line = runner(args, wl)
+        if runner is run_cfg1 and not args.no_sub:
+            want = list(SUB_RECORDS) if args.sub is None else [x for x in args.sub.split(",") if x]
+            world = int(os.environ.get("WORLD_SIZE", "1"))
+            for name in want:
+                wname, steps, warm, cpu_s = SUB_RECORDS[name]
+                if name == "cfg5_cached" and world > 1:
+                    # every rank would pin its own 18.8 GB host image; decode
+                    # runs replicas only, so the 1-GPU record stands for it
+                    if line is not None:
+                        line[name] = {"skipped": "one GPU only (replicas; the N=1 record stands)"}
+                    continue
+                sub = argparse.Namespace(**vars(args))
+                sub.workload, sub.steps, sub.warmup, sub.cpu_seconds = wname, steps, warm, cpu_s
+                sub.prompt, sub.timeline = None, None
+                sub.no_cpu_baseline = args.no_cpu_baseline or cpu_s <= 0
+                rec = SUB_RUNNERS[wname](sub, WORKLOADS[wname])
+                if line is not None:
+                    line[name] = rec
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        dist_stop()
 
+
+_DIST = {"started": False}
+
+
+def dist_start():
+    """(world, rank, local rank) of this process; the first call sets the
+    CUDA device and, under torchrun, starts the NCCL process group (short
+    timeout: ranks that wait for one another end with an error)."""
     import torch
-    import vireo_b200 as V
-
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        import datetime
+    if not _DIST["started"]:
+        torch.cuda.set_device(local)
+        if world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                    device_id=torch.device("cuda", local))
+        _DIST["started"] = True
+    return world, rank, local
+
+
+def dist_stop():
+    if _DIST["started"] and int(os.environ.get("WORLD_SIZE", "1")) > 1:
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        if dist.is_initialized():
+            dist.destroy_process_group()
+    _DIST["started"] = False
+
+
+def run_cfg1(args, wl):
+    """Config 1 (and the Qwen3 layer in decode): T batch-1 decode tokens per
+    step through gguf_moe_ffn, one launch per token, rotating over layer
+    copies."""
+    import torch
+    import vireo_b200 as V
+
+    world, rank, local = dist_start()
     V.check(V.lib().vireo_device_init(local), "vireo_device_init")
 
     spec = wl["spec"]()
@@ -343,7 +427,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         th = host_threads()
         rate, n, el, kind = cpu_reference_rate(layer, toks, args.cpu_seconds, th)
-        cpu = {"value": rate, "unit": "tok/s", "cores": th, "kind": kind,
+        cpu = {"value": rate, "unit": "tok/s", "cores": th, "kind": kind, "build": ref_build_name(kind),
                "sample": f"{n} tokens of the same workload in {el:.1f} s, OMP threads={th}"}
 
     if rank == 0:
@@ -358,11 +442,9 @@ def main():
                            "bytes_per_token": per_tok},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
                 "clocks": clk.summary(), "hbm_gbs": achieved}
-        print(json.dumps(line), flush=True)
     for m in layers:
         m.close()
-    if world > 1:
-        torch.distributed.destroy_process_group()
+    return line if rank == 0 else None
 
 
 def run_prefill(args, wl):
@@ -378,15 +460,7 @@ def run_prefill(args, wl):
     import torch
     import vireo_b200 as V
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+    world, rank, local = dist_start()
     L = V.lib()
     V.check(L.vireo_device_init(local), "vireo_device_init")
     spec = wl["spec"]()
@@ -444,6 +518,11 @@ def run_prefill(args, wl):
 
     if args.timeline:
         write_timeline(args.timeline, rank, lambda: step(hb.data_ptr(), x.data_ptr()), 3)
+    shares = None
+    try:
+        shares = kernel_shares(lambda: step(hb.data_ptr(), x.data_ptr()), 2)
+    except Exception as ex:  # the profiler is a diagnostic; the timed numbers stand without it
+        shares = [{"error": str(ex)[:120]}]
 
     # end to end: hidden states and residual from pinned host memory, residual back
     hb_h = x_bf.pin_memory()
@@ -480,7 +559,7 @@ def run_prefill(args, wl):
         th = host_threads()
         toks, _ = S.routed_tokens(layer, 64, wl["seed"])
         rate, n, el, kind = cpu_reference_rate(layer, toks, args.cpu_seconds, th)
-        cpu = {"value": rate, "unit": "tok/s", "cores": th, "kind": kind,
+        cpu = {"value": rate, "unit": "tok/s", "cores": th, "kind": kind, "build": ref_build_name(kind),
                "sample": f"{n} tokens through the reference's moe_ffn (one token at a time, its only "
                          f"path) in {el:.1f} s, OMP threads={th}, no router bias"}
     if rank == 0:
@@ -501,20 +580,22 @@ def run_prefill(args, wl):
                 "e2e": {"value": e2e_tps, "unit": "tok/s", "h2d_bytes_per_step": T * d * (2 + 4),
                         "d2h_bytes_per_step": T * d * 4,
                         "note": "bf16 tokens + fp32 residual in from pinned host, residual out (all ranks)"},
-                "gpu_launches": launches * args.steps, "clocks": clk.summary()}
-        print(json.dumps(line), flush=True)
+                "gpu_launches": launches * args.steps, "clocks": clk.summary(),
+                "kernel_shares": shares}
     if world > 1:
         ep.close()
-        torch.distributed.destroy_process_group()
     else:
         m.close()
+    return line if rank == 0 else None
 
 
-def cpu_decoder_rate(dec, seconds, threads):
+def cpu_decoder_rate(dec, seconds, threads, ctx=0):
     """The reference's own forward() (oracle/_ref, its dense KV store and
-    ExpertStore) over 1- and 2-layer slices of the same decoder at short
-    context; seconds per token for the full layer count by a linear fit
-    (a + b L: the LM head and embedding plus L layers)."""
+    ExpertStore) over 1- and 2-layer slices of the same decoder, with every
+    layer's KV store holding ctx positions (seeded through the reference's
+    kv_append) so that each timed step attends over ctx + 1 positions;
+    seconds per token for the full layer count by a linear fit (a + b L: the
+    LM head and embedding plus L layers)."""
     from oracle import oracle as O
     if not O.ref_available():
         return None
@@ -529,10 +610,12 @@ def cpu_decoder_rate(dec, seconds, threads):
         sub.layers = dec.layers[:nl]
         R = O.RefDecoder(sub)
         try:
-            R.step(1, 0, True)
+            if ctx:
+                R.fill_kv(ctx, 5)
+            R.step(1, ctx, True)
             n, t0 = 0, time.perf_counter()
             while time.perf_counter() - t0 < seconds / 2 and n < 64:
-                R.step((7 * n + 3) % dec.spec.vocab, n + 1, True)
+                R.step((7 * n + 3) % dec.spec.vocab, ctx + n + 1, True)
                 n += 1
             per[nl] = (time.perf_counter() - t0) / n
         finally:
@@ -553,15 +636,7 @@ def run_decoder(args, wl):
     import torch
     import vireo_b200 as V
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                device_id=torch.device("cuda", local))
+    world, rank, local = dist_start()
     L = V.lib()
     V.check(L.vireo_device_init(local), "vireo_device_init")
     spec = wl["spec"]()
@@ -640,14 +715,16 @@ def run_decoder(args, wl):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         th = host_threads()
-        r = cpu_decoder_rate(dec, args.cpu_seconds, th)
+        r = cpu_decoder_rate(dec, args.cpu_seconds, th, ctx=ctx0)
         if r:
+            from oracle import oracle as O
             full, per = r
             cpu = {"value": 1.0 / full, "unit": "tok/s", "cores": th, "kind": "reference",
-                   "sample": f"the reference's forward() on 1- and 2-layer slices of this decoder at context "
-                             f"<= 64 ({per[1] * 1e3:.1f} / {per[2] * 1e3:.1f} ms per token), linear in the layer "
-                             f"count to {spec.n_layers} layers; long-context attention not included; "
-                             f"OMP threads={th}"}
+                   "build": O.ref_build(),
+                   "sample": f"the reference's forward() on 1- and 2-layer slices of this decoder, each step "
+                             f"attending over {ctx0}+ cached positions (its dense KV store filled through "
+                             f"kv_append) ({per[1] * 1e3:.1f} / {per[2] * 1e3:.1f} ms per token), linear in the "
+                             f"layer count to {spec.n_layers} layers; OMP threads={th}"}
     if rank == 0:
         line = {"metric": "decoder_decode_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": world,
                 "steps": gen, "warmup": args.warmup, "ms_per_step": t_sec / gen * 1e3,
@@ -667,10 +744,34 @@ def run_decoder(args, wl):
                 "e2e": {"value": e2e_tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4,
                         "note": "gguf_decoder_step with a host token id per step, next token read back"},
                 "gpu_launches": gen * (8 * spec.n_layers + 4), "clocks": clk.summary()}
-        print(json.dumps(line), flush=True)
     G.close()
-    if world > 1:
-        torch.distributed.destroy_process_group()
+    return line if rank == 0 else None
+
+
+def kernel_shares(step, n, top=5):
+    """Per-kernel share of GPU time over n untimed steps, from the CUDA
+    activity profiler (CUPTI via torch.profiler): [{name, us_per_step,
+    share}] of the top kernels by total duration, for naming the limiter.
+    Under torchrun the ranks meet at a barrier once every profiler is up, so
+    that no rank's kernels wait on a peer still starting its profiler."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+            torch.distributed.barrier()
+            torch.cuda.synchronize()
+        for _ in range(n):
+            step()
+        torch.cuda.synchronize()
+    tot = {}
+    for e in prof.events():
+        if e.device_type == torch.autograd.DeviceType.CUDA:
+            nm = e.name.split("(")[0][:80]
+            tot[nm] = tot.get(nm, 0.0) + e.device_time_total
+    allt = sum(tot.values()) or 1.0
+    rows = sorted(tot.items(), key=lambda kv: -kv[1])[:top]
+    return [{"name": k, "us_per_step": v / n, "share": v / allt} for k, v in rows]
 
 
 def write_timeline(path, rank, step, n):
@@ -716,6 +817,39 @@ def zipf_routes(n_tok, n_layers, ne, k, seed):
     return ids, wts
 
 
+def cpu_cached_rate(layer, seconds, threads):
+    """The reference's moe_ffn with its own ExpertStore capped at the same
+    share of the budget per layer (4 GiB / 48 layers), on tokens routed by
+    its own router (it has no routing override): layer-tokens per second,
+    divided by 48 for tokens through the whole stack."""
+    from oracle import oracle as O
+    if not O.ref_available():
+        return None
+    O.ref().ref_set_threads(threads)
+    cap = CACHE_BYTES // CACHED_LAYERS
+    toks, _ = S.routed_tokens(layer, 256, 99)
+    R = O.RefMoe(layer, cap)
+    try:
+        R(toks[:8])
+        n, t0 = 0, time.perf_counter()
+        while True:
+            R(toks[n % 256:n % 256 + 1])
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= seconds and n >= 8:
+                break
+        st = R.stats()
+    finally:
+        R.close()
+    rate = n / el
+    return {"value": rate / CACHED_LAYERS, "unit": "tok/s", "cores": threads, "kind": "reference",
+            "build": O.ref_build(),
+            "sample": f"{n} tokens through one Qwen3-shaped layer's moe_ffn with the reference ExpertStore "
+                      f"capped at {cap >> 20} MiB (4 GiB / {CACHED_LAYERS} layers; misses pread from its "
+                      f"backing file) in {el:.1f} s = {rate:.1f} layer-tokens/s, / {CACHED_LAYERS} layers; "
+                      f"its own routing (hit rate {st.hits / max(st.requests, 1):.2f}); OMP threads={threads}"}
+
+
 def run_cached(args, wl):
     """Config 5: the 48-layer MoE stack with every expert in pinned host
     memory and a 4 GiB device ExpertStore; each layer is one
@@ -725,15 +859,7 @@ def run_cached(args, wl):
     import torch
     import vireo_b200 as V
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+    world, rank, local = dist_start()
     L = V.lib()
     V.check(L.vireo_device_init(local), "vireo_device_init")
     spec = wl["spec"]()
@@ -844,6 +970,9 @@ def run_cached(args, wl):
     L.expert_store_destroy(cached)
 
     layer_bytes = k * (gs + us + ds) + 2 * 4 * d  # routed launch: no router rows
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_cached_rate(layer, args.cpu_seconds, host_threads())
     peak, peak_kind = peaks()
     achieved = layer_bytes * NLY * ntimed / t_hit / 1e9
     if rank == 0:
@@ -864,16 +993,17 @@ def run_cached(args, wl):
                              "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
                              "algorithmic_bytes_per_launch": layer_bytes,
                              "kernel": "moe_routed_kernel (one launch per layer), all-hit run"},
-                "cpu_baseline": None,
+                "cpu_baseline": cpu,
                 "e2e": {"value": e2e_tps * world, "unit": "tok/s", "h2d_bytes_per_step": T * (hbs.nbytes + 4 * d),
                         "d2h_bytes_per_step": T * 4 * d,
                         "note": "per token: hidden vectors + residual in from pinned host, residual out"},
                 "gpu_launches": ntimed * NLY, "clocks": clk.summary()}
-        print(json.dumps(line), flush=True)
     m.close()
-    if world > 1:
-        torch.distributed.destroy_process_group()
+    return line if rank == 0 else None
 
+
+SUB_RUNNERS = {"qwen3_prefill": run_prefill, "qwen3_decoder": run_decoder, "olmoe_decoder": run_decoder,
+               "qwen3_cached_decode": run_cached}
 
 if __name__ == "__main__":
     main()

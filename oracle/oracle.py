@@ -20,6 +20,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 PORT_SO = os.path.join(HERE, "_build", "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libvireo_ref.so")
+REF_SO_V4 = os.path.join(HERE, "_ref", "libvireo_ref_v4.so")
 
 _f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 _i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
@@ -27,10 +28,28 @@ _u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
 
 
 def build(ref: bool = True) -> None:
-    """Compile the checkers (the reference library only when its sources exist)."""
+    """Compile the checkers; the reference libraries too when ref is set and
+    the environment variable VIREO_REF_SRC names the reference source tree
+    (otherwise the prebuilt ones are kept)."""
     targets = ["port"] + (["ref", "ref_store_test"] if ref else [])
-    subprocess.run(["make", "-s", "-C", HERE] + targets, check=True,
+    extra = [f"REF={os.environ['VIREO_REF_SRC']}"] if ref and os.environ.get("VIREO_REF_SRC") else []
+    subprocess.run(["make", "-s", "-C", HERE] + extra + targets, check=True,
                    env={**os.environ, "OCC": os.environ.get("ORACLE_CC", "gcc")})
+
+
+def host_has_avx512() -> bool:
+    """The x86-64-v4 feature set (AVX-512 F, BW, CD, DQ, VL) on this host."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            flags = next((l.split(":", 1)[1].split() for l in f if l.startswith("flags")), [])
+    except OSError:
+        return False
+    return all(x in flags for x in ("avx512f", "avx512bw", "avx512cd", "avx512dq", "avx512vl"))
+
+
+def ref_build() -> str:
+    """Which reference library ref() loads on this host: "x86-64-v4" or "x86-64-v3"."""
+    return "x86-64-v4" if host_has_avx512() and os.path.exists(REF_SO_V4) else "x86-64-v3"
 
 
 class OrcMoeLayer(C.Structure):
@@ -74,6 +93,8 @@ def port():
         lib.orc_moe_ffn_batch_bias.argtypes = [C.POINTER(OrcMoeLayer), C.c_int, _f32p, _f32p, _i32p, _f32p,
                                                C.c_void_p]
         lib.orc_moe_ffn_batch_bias.restype = C.c_int
+        lib.orc_route_batch_bias.argtypes = [C.POINTER(OrcMoeLayer), C.c_int, _f32p, _i32p, _f32p, C.c_void_p]
+        lib.orc_route_batch_bias.restype = C.c_int
         lib.orc_expert_ffn.argtypes = [C.POINTER(OrcMoeLayer), C.c_int, _f32p, _f32p]
         lib.orc_expert_ffn.restype = C.c_int
         lib.orc_set_threads.argtypes = [C.c_int]
@@ -91,7 +112,7 @@ def ref():
     if _ref is None:
         if not os.path.exists(REF_SO):
             raise FileNotFoundError(REF_SO + " (reference library not built)")
-        lib = C.CDLL(REF_SO)
+        lib = C.CDLL(REF_SO_V4 if ref_build() == "x86-64-v4" else REF_SO)
         lib.gguf_f16_to_f32.argtypes = [C.c_uint16]
         lib.gguf_f16_to_f32.restype = C.c_float
         lib.gguf_dequant_row.argtypes = [C.c_uint32, _u8p, _f32p, C.c_int]
@@ -114,6 +135,8 @@ def ref():
         lib.ref_decoder_forward.restype = C.c_int
         lib.ref_decoder_destroy.argtypes = [C.c_void_p]
         lib.ref_decoder_destroy.restype = None
+        lib.ref_decoder_fill_kv.argtypes = [C.c_void_p, C.c_int, C.c_uint64]
+        lib.ref_decoder_fill_kv.restype = None
         lib.ref_decoder_last_gap.argtypes = []
         lib.ref_decoder_last_gap.restype = C.c_double
         # the reference's own ExpertStore (src/expert_store.c, compiled into the same library)
@@ -196,6 +219,20 @@ class PortMoe:
         return x, ids, wts
 
 
+    def route(self, hb, bias=None):
+        """The routing alone (router, optional bias, softmax, top-k, renorm):
+        (ids, wts) for a batch of tokens, as __call__ returns them."""
+        s = self.layer.spec
+        hb = np.ascontiguousarray(hb, dtype=np.float32).reshape(-1, s.dim)
+        n = hb.shape[0]
+        k = min(s.n_used, 64)
+        ids = np.zeros((n, k), dtype=np.int32)
+        wts = np.zeros((n, k), dtype=np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        port().orc_route_batch_bias(C.byref(self.desc), n, hb.reshape(-1), ids.reshape(-1), wts.reshape(-1),
+                                    None if b is None else b.ctypes.data)
+        return ids, wts
+
     def expert(self, e: int, hb) -> np.ndarray:
         """One expert's FFN output (before the gate weight) for one token:
         the body of the reference's per-expert loop, gguf_run.c:202-208."""
@@ -258,6 +295,11 @@ class RefDecoder:
         a = ref().ref_decoder_forward(self.h, int(token), int(pos), int(want_logits), lg.ctypes.data,
                                       x.ctypes.data)
         return (lg if want_logits else None), x, a
+
+    def fill_kv(self, n_pos: int, seed: int = 1) -> None:
+        """Seeded K/V for positions [0, n_pos) of every layer and kv head,
+        through the reference's own kv_append (timing at long context)."""
+        ref().ref_decoder_fill_kv(self.h, int(n_pos), int(seed))
 
     def last_gap(self) -> float:
         """Smallest log-probability gap among the top n_used + 1 router

@@ -321,6 +321,34 @@ int ref_decoder_forward(RefDec *r, int token, int pos, int want_logits, float *l
     return lg ? argmax(lg, m->vocab) : -1;
 }
 
+/* Positions [0, n_pos) of every (layer, kv head) of the reference's dense KV
+ * store filled through its own kv_append (src/kvstore.h:60-63) with seeded
+ * vectors (each value the sum of four uniforms on [-0.5, 0.5), so about
+ * N(0, 1/3)): the state a prompt of n_pos tokens leaves, for timing decode
+ * steps at that context without running the prompt (CPU baseline only; the
+ * values steer nothing but the softmax weights). */
+void ref_decoder_fill_kv(RefDec *r, int n_pos, uint64_t seed) {
+    Model *m = &r->m;
+    int hs = m->head_size;
+    float *k = (float *)malloc(sizeof(float) * (size_t)hs);
+    float *v = (float *)malloc(sizeof(float) * (size_t)hs);
+    uint64_t z = seed * 0x9E3779B97F4A7C15ull + 1;
+    for (int l = 0; l < m->n_layers; l++)
+        for (int kh = 0; kh < m->n_kv_heads; kh++)
+            for (int pos = 0; pos < n_pos; pos++) {
+                for (int i = 0; i < 2 * hs; i++) {
+                    float a = 0.0f;
+                    for (int j = 0; j < 4; j++) {
+                        z = z * 6364136223846793005ull + 1442695040888963407ull;
+                        a += (float)(z >> 40) * (1.0f / 16777216.0f) - 0.5f;
+                    }
+                    if (i < hs) k[i] = a; else v[i - hs] = a;
+                }
+                kv_append(m->kv, l * m->n_kv_heads + kh, pos, k, v);
+            }
+    free(k); free(v);
+}
+
 /* The smallest router log-probability gap among the top n_used + 1 experts
  * over every layer of the last ref_decoder_forward call. */
 double ref_decoder_last_gap(void) { return g_gap_min; }

@@ -324,23 +324,20 @@ int orc_moe_ffn(const orc_moe_layer *L, const float *hb, float *x, int32_t *ids,
 /* The same with a per-expert bias added to the router logits before the
  * softmax (the imbalanced-routing configuration adds it in its harness; the
  * reference has no bias, and bias == NULL is exactly orc_moe_ffn). */
-int orc_moe_ffn_bias(const orc_moe_layer *L, const float *hb, float *x, int32_t *ids, float *wts,
-                     float *probs, const float *bias) {
-    int d = L->dim, fe = L->ffn_exp, ne = L->n_experts, k = L->n_used;
+/* Routing of one token (gguf_run.c:187-192): router mat-vec, optional
+ * per-expert bias, softmax, greedy top-k (k passes of a strict '>' argmax
+ * over the unused experts, starting from -1, so ties go to the lowest id),
+ * optional renormalisation by the sequential sum of the selected weights.
+ * idx/w receive min(n_used, 64) entries; probs (optional) the softmax. */
+static int route_token(const orc_moe_layer *L, const float *hb, const float *bias, int *idx, float *w,
+                       float *probs) {
+    int d = L->dim, ne = L->n_experts, k = L->n_used;
     int kk = k < 64 ? k : 64;
     float *rl = (float *)malloc(sizeof(float) * (size_t)ne);
-    float *g = (float *)malloc(sizeof(float) * (size_t)fe);
-    float *u = (float *)malloc(sizeof(float) * (size_t)fe);
-    float *dn = (float *)malloc(sizeof(float) * (size_t)d);
-    float *acc = (float *)calloc((size_t)d, sizeof(float));
-    int idx[64];
-    float w[64];
     orc_matmul(rl, hb, L->router_type, L->router, d, ne);
     if (bias) for (int e = 0; e < ne; e++) rl[e] = rl[e] + bias[e];
     softmax_inplace(rl, ne);
     if (probs) memcpy(probs, rl, sizeof(float) * (size_t)ne);
-    /* greedy top-k: k passes of a strict '>' argmax over the unused experts,
-     * starting from -1, so ties go to the lowest expert id */
     for (int t = 0; t < kk; t++) {
         int best = -1;
         float bv = -1.0f;
@@ -357,6 +354,20 @@ int orc_moe_ffn_bias(const orc_moe_layer *L, const float *hb, float *x, int32_t 
         for (int t = 0; t < kk; t++) ws = ws + w[t];
         if (ws > 0) for (int t = 0; t < kk; t++) w[t] = w[t] / ws;
     }
+    free(rl);
+    return kk;
+}
+
+int orc_moe_ffn_bias(const orc_moe_layer *L, const float *hb, float *x, int32_t *ids, float *wts,
+                     float *probs, const float *bias) {
+    int d = L->dim, fe = L->ffn_exp;
+    float *g = (float *)malloc(sizeof(float) * (size_t)fe);
+    float *u = (float *)malloc(sizeof(float) * (size_t)fe);
+    float *dn = (float *)malloc(sizeof(float) * (size_t)d);
+    float *acc = (float *)calloc((size_t)d, sizeof(float));
+    int idx[64];
+    float w[64];
+    int kk = route_token(L, hb, bias, idx, w, probs);
     for (int t = 0; t < kk; t++) {
         int e = idx[t];
         if (e < 0) continue;
@@ -366,7 +377,7 @@ int orc_moe_ffn_bias(const orc_moe_layer *L, const float *hb, float *x, int32_t 
     for (int i = 0; i < d; i++) x[i] = x[i] + acc[i];
     if (ids) for (int t = 0; t < kk; t++) ids[t] = idx[t];
     if (wts) for (int t = 0; t < kk; t++) wts[t] = w[t];
-    free(rl); free(g); free(u); free(dn); free(acc);
+    free(g); free(u); free(dn); free(acc);
     return kk;
 }
 
@@ -394,6 +405,27 @@ int orc_moe_ffn_batch_bias(const orc_moe_layer *L, int n_tok, const float *hb, f
     for (int t = 0; t < n_tok; t++)
         orc_moe_ffn_bias(L, hb + (size_t)t * L->dim, x + (size_t)t * L->dim,
                          ids ? ids + (size_t)t * kk : NULL, wts ? wts + (size_t)t * kk : NULL, NULL, bias);
+    orc_set_threads(saved);
+    return kk;
+}
+
+/* Routing alone for n_tok tokens (route_token per token, tokens in
+ * parallel; bias may be NULL): ids/wts [n_tok][min(n_used, 64)]. */
+int orc_route_batch_bias(const orc_moe_layer *L, int n_tok, const float *hb, int32_t *ids, float *wts,
+                         const float *bias) {
+    int kk = L->n_used < 64 ? L->n_used : 64;
+    int saved = orc_max_threads();
+    orc_set_threads(1);
+    #pragma omp parallel for schedule(dynamic, 16) num_threads(saved)
+    for (int t = 0; t < n_tok; t++) {
+        int idx[64];
+        float w[64];
+        route_token(L, hb + (size_t)t * L->dim, bias, idx, w, NULL);
+        for (int j = 0; j < kk; j++) {
+            ids[(size_t)t * kk + j] = idx[j];
+            wts[(size_t)t * kk + j] = w[j];
+        }
+    }
     orc_set_threads(saved);
     return kk;
 }

@@ -47,8 +47,17 @@ def long_f16_spec():
                          rope_base=1000000.0)
 
 
+def qwen3_geometry_spec():
+    """Config 3's geometry in one layer: dim 2048, 32 q / 4 kv heads x 128,
+    per-head QK norm, 128 experts top-8 renormalised (ffn 768), and the
+    151,936-row Q6_K LM head."""
+    return S.DecoderSpec(1, 2048, 32, 4, 128, 151936, S.qwen3_layer(), qk_norm="head", eps=1e-6,
+                         rope_base=1000000.0)
+
+
 # (spec, seed, steps, min_gap) of every reference comparison below
 MARGIN_CASES = [
+    (qwen3_geometry_spec, 101, 320, 1e-4),
     (S.tiny_olmoe_decoder, 31, 12, 1e-4),
     (S.tiny_qwen3_decoder, 32, 12, 1e-4),
     (long_f16_spec, 41, 260, 5e-4),
@@ -148,6 +157,17 @@ def test_decoder_gqa8_across_chunks(head_size, qk_norm):
 
 
 @gpu
+def test_decoder_qwen3_geometry_long_lm_head():
+    """Config 3's attention geometry and LM head: 320 positions (three
+    128-position attention chunks) teacher-forced through one layer of the
+    Qwen3-shaped decoder with the f32 KV cache; logits of the last 8
+    positions (the 151,936-row Q6_K LM head through gemv_kernel) against the
+    reference's forward()."""
+    worst = run_case(qwen3_geometry_spec(), 101, kv_f16=False, steps=320, check_from=312)
+    assert worst < 2e-3, worst
+
+
+@gpu
 def test_decoder_device_token_chain_matches_host_tokens():
     """gguf_decoder_step_dev fed by the previous step's argmax gives the same
     tokens and logits as gguf_decoder_step fed the same ids from the host."""
@@ -179,6 +199,21 @@ def test_decoder_device_token_chain_matches_host_tokens():
             G.close()
     assert runs[0][0] == runs[1][0]
     assert np.array_equal(runs[0][1], runs[1][1])
+
+
+@gpu
+def test_decoder_rejects_moe_of_another_dim():
+    """A layer whose MoE handle was made for another hidden size is refused
+    at create (the MoE block reads hb and writes x over its own dim)."""
+    import vireo_b200 as V
+    spec = S.tiny_olmoe_decoder(n_layers=1)
+    D = S.Decoder(spec, 35)
+    other = S.MoeLayer(S.MoeLayerSpec(1024, 256, 16, 4, 0, S.GGML_Q4_K, S.GGML_Q4_K, S.GGML_Q6_K), 35)
+    D.layers = [D.layers[0]]
+    D.layers[0].moe = other
+    with pytest.raises(V.VireoError) as ei:
+        V.Decoder(D, max_ctx=4)
+    assert ei.value.status == -1
 
 
 @gpu

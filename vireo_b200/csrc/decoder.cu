@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "gguf_decoder.h"
+#include "moe_view.h"
 #include "vireo_internal.h"
 #include "vireo_ptx.cuh"
 
@@ -570,6 +571,9 @@ int gguf_decoder_create(const gguf_decoder_desc* desc, const gguf_decoder_layer*
     for (uint32_t t : {y.wq_type, y.wk_type, y.wv_type})
       if (type_block(t, &be, &bb) || D.dim % be) return VIREO_ERR_UNSUPPORTED;
     if (type_block(y.wo_type, &be, &bb) || nq % be) return VIREO_ERR_UNSUPPORTED;
+    // the MoE block reads hb and writes x over its own dim: it must be D.dim
+    MoeView mv;
+    if (moe_view(y.moe, &mv) || !mv.desc || mv.desc->dim != D.dim) return VIREO_ERR_ARG;
   }
   if ((st = set_chain_carveout(D.n_heads / D.n_kv_heads, D.kv_f16, D.head_size))) return st;
   gguf_decoder* dec = new gguf_decoder();
