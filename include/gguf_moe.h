@@ -48,6 +48,13 @@ typedef struct gguf_moe gguf_moe;
  * at most the GPU's SM count. */
 int gguf_moe_create(const gguf_moe_desc *desc, gguf_moe **out);
 
+/* The same layer with HOST pointers in desc (e.g. the tensors of an mmap'd
+ * GGUF file, as the reference's loader finds them, src/gguf_run.c:312-315):
+ * the layer is checked as gguf_moe_create checks it, then its router and
+ * expert tensors are copied to device memory owned by the handle (freed by
+ * gguf_moe_destroy).  Host memory is not needed after the call. */
+int gguf_moe_create_host(const gguf_moe_desc *desc, gguf_moe **out);
+
 /* n_tok independent tokens through the layer, one after another (decode).
  * hb: [n_tok][dim] normalised hidden; x: [n_tok][dim] residual, updated in
  * place (x += MoE(hb)); ids / wts: [n_tok][n_used] selected experts in rank

@@ -37,6 +37,17 @@ def build(ref: bool = True) -> None:
                    env={**os.environ, "OCC": os.environ.get("ORACLE_CC", "gcc")})
 
 
+def build_dropin() -> bool:
+    """The drop-in checkers (oracle/dropin.py) when VIREO_REF_SRC names the
+    reference source tree; False when it does not (prebuilt ones are kept)."""
+    src = os.environ.get("VIREO_REF_SRC")
+    if not src or not os.path.isdir(os.path.join(src, "src")):
+        return False
+    from oracle import dropin
+    dropin.build(src, os.environ.get("ORACLE_CC", "gcc"))
+    return True
+
+
 def host_has_avx512() -> bool:
     """The x86-64-v4 feature set (AVX-512 F, BW, CD, DQ, VL) on this host."""
     try:
@@ -353,6 +364,60 @@ class RefMoe:
     def close(self):
         if self.h:
             ref().ref_moe_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class DropInDecoder:
+    """The reference's decoder opened from a GGUF file by its own loader
+    (oracle/dropin_harness.c): b200=False is the reference as it ships;
+    b200=True is the same runner with gguf_compute.c and expert_store.c
+    replaced by libvireo_b200.so and every MoE block run by gguf_moe_ffn_host
+    from the hook at the top of moe_ffn."""
+
+    def __init__(self, path: str, b200: bool):
+        from oracle import dropin
+        so = dropin.B200_SO if b200 else dropin.REF_SO
+        if not os.path.exists(so):
+            raise FileNotFoundError(so + " (drop-in checker not built)")
+        lib = C.CDLL(so)
+        lib.dropin_open.argtypes = [C.c_char_p]
+        lib.dropin_open.restype = C.c_void_p
+        lib.dropin_forward.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+        lib.dropin_forward.restype = C.c_int
+        lib.dropin_close.argtypes = [C.c_void_p]
+        lib.dropin_close.restype = None
+        lib.dropin_vocab.argtypes = [C.c_void_p]
+        lib.dropin_vocab.restype = C.c_int
+        lib.dropin_dim.argtypes = [C.c_void_p]
+        lib.dropin_dim.restype = C.c_int
+        lib.dropin_hook_calls.argtypes = []
+        lib.dropin_hook_calls.restype = C.c_long
+        self.lib = lib
+        self.h = lib.dropin_open(path.encode())
+        if not self.h:
+            raise RuntimeError(f"dropin_open failed on {path}")
+        self.vocab = lib.dropin_vocab(self.h)
+        self.dim = lib.dropin_dim(self.h)
+
+    def step(self, token: int, pos: int, want_logits: bool = True):
+        """(logits or None, residual x after the step, argmax or -1)."""
+        lg = np.zeros(self.vocab, dtype=np.float32)
+        x = np.zeros(self.dim, dtype=np.float32)
+        a = self.lib.dropin_forward(self.h, int(token), int(pos), int(want_logits), lg.ctypes.data, x.ctypes.data)
+        return (lg if want_logits else None), x, a
+
+    def hook_calls(self) -> int:
+        return int(self.lib.dropin_hook_calls())
+
+    def close(self):
+        if self.h:
+            self.lib.dropin_close(self.h)
             self.h = None
 
     def __del__(self):

@@ -74,7 +74,8 @@ def test_matmul_golden(V, golden, t):
 SHAPES = [(S.GGML_Q8_0, 2048, 1024), (S.GGML_Q8_0, 1024, 2048), (S.GGML_Q4_K, 2048, 768),
           (S.GGML_Q4_K, 2048, 1024), (S.GGML_Q6_K, 768, 2048), (S.GGML_Q6_K, 1024, 2048),
           (S.GGML_Q6_K, 2048, 4096), (S.GGML_Q4_K, 4096, 256), (S.GGML_Q8_0, 256, 16),
-          (S.GGML_Q8_0, 96, 40), (S.GGML_Q4_K, 512, 24), (S.GGML_F32, 2048, 128)]
+          (S.GGML_Q8_0, 96, 40), (S.GGML_Q4_K, 512, 24), (S.GGML_F32, 2048, 128),
+          (S.GGML_Q5_0, 2048, 1024), (S.GGML_Q5_0, 768, 2048), (S.GGML_Q5_0, 256, 16), (S.GGML_Q5_0, 96, 40)]
 
 
 @pytest.mark.parametrize("t,n,d", SHAPES)
@@ -155,6 +156,31 @@ def test_moe_many_tokens_device_api(V, golden, name):
     m.sync()
     assert torch.equal(x, x2)
     m.close()
+
+
+@pytest.mark.parametrize("gt,dt,dim,fe,ne,k", [(S.GGML_Q5_0, S.GGML_Q6_K, 512, 256, 16, 4),
+                                               (S.GGML_Q4_K, S.GGML_Q5_0, 2048, 768, 32, 8),
+                                               (S.GGML_Q5_0, S.GGML_Q5_0, 1024, 512, 16, 4)])
+def test_moe_q5_0_experts(V, gt, dt, dim, fe, ne, k):
+    """Q5_0 expert matrices (gguf_compute.c:68-82) on the decode path: a
+    layer with Q5_0 gate/up, one with Q5_0 down, one with both, against the
+    CPU oracle."""
+    import torch
+    spec = S.MoeLayerSpec(dim, fe, ne, k, 1, gt, gt, dt)
+    L = S.MoeLayer(spec, 71)
+    toks, _ = S.routed_tokens(L, 24, 71)
+    x0 = (S.normal(71, 9, toks.size) * 0.3).astype(np.float32).reshape(toks.shape)
+    rx, rids, rwts = O.PortMoe(L)(toks, x0)
+    m = V.MoeLayer(L)
+    try:
+        hb, x = torch.from_numpy(toks).cuda(), torch.from_numpy(x0.copy()).cuda()
+        ids = torch.zeros((toks.shape[0], k), dtype=torch.int32, device="cuda")
+        wts = torch.zeros((toks.shape[0], k), dtype=torch.float32, device="cuda")
+        m.ffn(hb, x, ids, wts)
+        m.sync()
+        check_moe(x0, x.cpu().numpy(), ids.cpu().numpy(), wts.cpu().numpy(), rx, rids, rwts)
+    finally:
+        m.close()
 
 
 def test_moe_unsupported_layer_is_rejected(V):

@@ -393,6 +393,7 @@ struct gguf_moe {
   // memory: hb [n][d] | x [n][d] | status (16 B) | ids [n][k] | wts [n][k]
   uint8_t* d_io = nullptr;
   uint8_t* h_io = nullptr;
+  void* owned[4] = {};  // device copies of the layer's tensors (gguf_moe_create_host)
   int io_cap = 0;
   bool pdl = true;
   cudaStream_t stream = nullptr;
@@ -417,13 +418,9 @@ static int moe_reset_scratch(gguf_moe* m, cudaStream_t s) {
 
 extern "C" {
 
-int gguf_moe_create(const gguf_moe_desc* desc, gguf_moe** out) {
-  int st;
-  Ctx* c = ctx_get(&st);
-  if (!c) return st;
-  if (!desc || !out) return VIREO_ERR_ARG;
-  *out = nullptr;
-  const gguf_moe_desc& D = *desc;
+// The layer rules gguf_moe_create applies to a descriptor, apart from where
+// its tensors live and their alignment.
+static int moe_check_shape(const gguf_moe_desc& D) {
   if (D.dim <= 0 || D.ffn_exp <= 0 || D.n_experts <= 0 || D.n_used <= 0 || D.n_used > D.n_experts ||
       !D.router || !D.gate_exps || !D.up_exps || !D.down_exps)
     return VIREO_ERR_ARG;
@@ -436,10 +433,22 @@ int gguf_moe_create(const gguf_moe_desc* desc, gguf_moe** out) {
   const uint64_t dsl = (uint64_t)D.dim * row_bytes(D.down_type, D.ffn_exp);
   if (D.gate_nbytes < gsl * D.n_experts || D.up_nbytes < gsl * D.n_experts || D.down_nbytes < dsl * D.n_experts)
     return VIREO_ERR_ARG;
+  if ((D.gate_nbytes / D.n_experts) % 16 || (D.up_nbytes / D.n_experts) % 16 || (D.down_nbytes / D.n_experts) % 16)
+    return VIREO_ERR_UNSUPPORTED;
+  return VIREO_OK;
+}
+
+int gguf_moe_create(const gguf_moe_desc* desc, gguf_moe** out) {
+  int st;
+  Ctx* c = ctx_get(&st);
+  if (!c) return st;
+  if (!desc || !out) return VIREO_ERR_ARG;
+  *out = nullptr;
+  const gguf_moe_desc& D = *desc;
+  if ((st = moe_check_shape(D))) return st;
   const uint64_t gstep = D.gate_nbytes / D.n_experts, ustep = D.up_nbytes / D.n_experts,
                  dstep = D.down_nbytes / D.n_experts;
-  if (((uintptr_t)D.router | (uintptr_t)D.gate_exps | (uintptr_t)D.up_exps | (uintptr_t)D.down_exps) % 16 ||
-      gstep % 16 || ustep % 16 || dstep % 16)
+  if (((uintptr_t)D.router | (uintptr_t)D.gate_exps | (uintptr_t)D.up_exps | (uintptr_t)D.down_exps) % 16)
     return VIREO_ERR_UNSUPPORTED;
 
   gguf_moe* m = new gguf_moe();
@@ -505,6 +514,39 @@ int gguf_moe_create(const gguf_moe_desc* desc, gguf_moe** out) {
   }
   p.exp_tab = m->d_exp_tab;
   *out = m;
+  return VIREO_OK;
+}
+
+// A layer whose tensors are in host memory (the mmap of a GGUF file):
+// checked first, then the router and the three expert tensors are copied
+// into device memory that the handle owns and frees on destroy.
+int gguf_moe_create_host(const gguf_moe_desc* desc, gguf_moe** out) {
+  int st;
+  Ctx* c = ctx_get(&st);
+  if (!c) return st;
+  if (!desc || !out) return VIREO_ERR_ARG;
+  *out = nullptr;
+  const gguf_moe_desc& H = *desc;
+  if ((st = moe_check_shape(H))) return st;
+  const void* src[4] = {H.router, H.gate_exps, H.up_exps, H.down_exps};
+  const uint64_t nb[4] = {(uint64_t)H.n_experts * row_bytes(H.router_type, H.dim), H.gate_nbytes, H.up_nbytes,
+                          H.down_nbytes};
+  void* dev[4] = {};
+  for (int i = 0; i < 4 && !st; i++) {
+    if ((st = cuda_status(cudaMalloc(&dev[i], nb[i])))) break;
+    st = cuda_status(cudaMemcpy(dev[i], src[i], nb[i], cudaMemcpyHostToDevice));
+  }
+  gguf_moe_desc D = H;
+  D.router = dev[0];
+  D.gate_exps = dev[1];
+  D.up_exps = dev[2];
+  D.down_exps = dev[3];
+  if (!st) st = gguf_moe_create(&D, out);
+  if (st) {
+    for (void* p : dev) cudaFree(p);
+    return st;
+  }
+  for (int i = 0; i < 4; i++) (*out)->owned[i] = dev[i];
   return VIREO_OK;
 }
 
@@ -737,6 +779,7 @@ void gguf_moe_destroy(gguf_moe* m) {
   cudaFree(m->d_exp_tab);
   cudaFree(m->d_io);
   cudaFreeHost(m->h_io);
+  for (void* p : m->owned) cudaFree(p);
   if (m->stream) cudaStreamDestroy(m->stream);
   delete m;
 }

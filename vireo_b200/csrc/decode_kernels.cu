@@ -30,14 +30,6 @@ VDEV void do_abort(Ctl* c, int* err, int code) {
   *reinterpret_cast<volatile int*>(&c->abort) = 1;
 }
 
-// consume_unit variant that can skip the math (inactive unit) while keeping
-// the partial/counter protocol intact
-template <class S>
-VDEV bool consume(const uint8_t* stage, const StageGeom& sg, int v, int nseg, int w, const uint8_t* btab,
-                  const float* sx, float* part, int* ucnt, const LaneCtx& L, float* val, bool active, BFrag& bf) {
-  return consume_unit<S>(stage, sg, v, active ? nseg : 0, kConsumerWarps, w, btab, sx, part, ucnt, L, val, bf);
-}
-
 // Warp-collective stage wait: lane 0 waits (bounded), the result and the
 // completed phase are shared with the warp.  False when aborted or timed out
 // (the timeout is recorded).
@@ -90,8 +82,9 @@ VDEV void stage_vec_cg8(const float* g, float* s, int n, int tid, int nthr) {
 // selection gives it (gguf_run.c:190-191).  Ranks < k are the selection, in
 // rank order (NaN never selected; unused slots hold id -1 and weight -1, as
 // the reference's scan leaves them).  The weights are the probabilities;
-// renormalisation comes later (route_finish).  lg: 32 R floats; pw: R ne
-// floats (shared memory).
+// renormalisation comes later (route_finish).  lg: 32 R floats; pw: R rows
+// of ne rounded up to a multiple of 4 floats (shared memory, 16-byte
+// aligned).
 VDEV void route_warps(const MoeDecodeParams& p, Ctl* ctl, float* lg, float* pw, int warp, int lane) {
   constexpr int kPer = kMaxExperts / 32;
   const int ne = p.ne, k = p.k, nchunk = p.d / kRouterChunk, R = (ne + 31) / 32;
@@ -124,7 +117,7 @@ VDEV void route_warps(const MoeDecodeParams& p, Ctl* ctl, float* lg, float* pw, 
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
-  float* pr = pw + (size_t)warp * ne;
+  float* pr = pw + (size_t)warp * ((ne + 3) & ~3);  // rows 16-byte aligned for the float4 scan
   int nvalid = 0;
 #pragma unroll
   for (int i = 0; i < kPer; i++) {
@@ -186,55 +179,88 @@ VDEV void route_finish(const MoeDecodeParams& p, Ctl* ctl, bool write_out) {
   }
 }
 
-// Segments [s0, s1) of one 16-row weight tile (rows g and g + 8 of lane
-// (g, t)) against the activation tables, summed in segment order: every
-// lane of a quad ends holding its two rows' sums.
-template <class SF>
-VDEV void tile_dot(const uint8_t* stage, const StageGeom& sg, int s0, int s1, const uint8_t* btab, const float* meta,
-                   const LaneCtx& L, BFrag& bf, float& a0, float& a1) {
-  const uint8_t* r0 = stage_row(stage, sg, L.g);
-  const uint8_t* r1 = stage_row(stage, sg, L.g + 8);
-  a0 = 0.f;
-  a1 = 0.f;
-#pragma unroll 1
-  for (int seg = s0; seg < s1; seg++) {
-    float tot0 = 0.f, tot1 = 0.f;
-    bf.get(btab + seg * kSegTabBytes, L);
-    SF::run(r0 + seg * SF::kSegBytes, r1 + seg * SF::kSegBytes, bf, meta + seg * kMeta, L, tot0, tot1);
-    tot0 += __shfl_xor_sync(0xffffffffu, tot0, 1);
-    tot1 += __shfl_xor_sync(0xffffffffu, tot1, 1);
-    tot0 += __shfl_xor_sync(0xffffffffu, tot0, 2);
-    tot1 += __shfl_xor_sync(0xffffffffu, tot1, 2);
-    a0 += tot0;
-    a1 += tot1;
-  }
+// Bounded wait on a phase with no early exit on abort: used where bulk
+// copies may still be writing this CTA's shared memory (they complete
+// whatever the kernel's state), so that the CTA never exits before them.
+VDEV bool wait_copies(uint64_t* bar, uint32_t par) {
+  const int never = 0;
+  return mbar_wait(bar, par, &never);
 }
 
-// The consumer warps work in kUnitGroups groups of kUnitWarps warps; the
-// warps of a group share each unit or tile, warp r taking a contiguous run
-// of its segments, and the group's first warp adds the warps' sums in warp
-// order (named barrier 2 + group between them).
-constexpr int kUnitWarps = 4;
-constexpr int kUnitGroups = kConsumerWarps / kUnitWarps;
+// The producer warp's item loop over one ring: item i goes to slot i % S
+// once its previous occupant (item i - S) has been released by every
+// consumer warp (empty) and its copies have landed (full), so no two copies
+// ever target one slot at once; at the end it waits for the copies of the
+// last S items.  issue(i, slot_base) announces the item's bytes on full[slot]
+// and issues its copies (warp-collective).  Returns the items issued.
+template <class Issue>
+VDEV int produce_ring(uint64_t* full, uint64_t* empty, uint8_t* stages, uint32_t stage_bytes, int S, int n,
+                      Ctl* ctl, int* err, Issue&& issue) {
+  int i = 0;
+  for (; i < n; i++) {
+    const int slot = i % S;
+    if (i >= S) {
+      if (!warp_wait(&empty[slot], ((uint32_t)(i / S) & 1u) ^ 1u, ctl, err)) break;
+      if ((threadIdx.x & 31) == 0) wait_copies(&full[slot], (uint32_t)((i - S) / S) & 1u);
+      __syncwarp();
+    }
+    if (aborted(ctl)) break;
+    issue(i, slot, stages + (size_t)slot * stage_bytes);
+  }
+  if ((threadIdx.x & 31) == 0)
+    for (int j = i > S ? i - S : 0; j < i; j++) wait_copies(&full[j % S], (uint32_t)(j / S) & 1u);
+  __syncwarp();
+  return i;
+}
+
+// Partial of one (tile, segment) pair into part (16 floats), then the tile's
+// shared-memory counter; true in the warp that completed the tile, whose
+// lanes 0..15 then hold the tile's row sums in segment order (the counter is
+// put back to zero).
+VDEV bool pair_done(float t0, float t1, float* pt, const float* tile_part, int* cnt, int nseg, const LaneCtx& L,
+                    float& row) {
+  t0 += __shfl_xor_sync(0xffffffffu, t0, 1);
+  t1 += __shfl_xor_sync(0xffffffffu, t1, 1);
+  t0 += __shfl_xor_sync(0xffffffffu, t0, 2);
+  t1 += __shfl_xor_sync(0xffffffffu, t1, 2);
+  if (L.t == 0) {
+    pt[L.g] = t0;
+    pt[L.g + 8] = t1;
+  }
+  __syncwarp();
+  int last = 0;
+  if (L.lane == 0) {
+    __threadfence_block();
+    last = atomicAdd(cnt, 1) == nseg - 1;
+  }
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return false;
+  __threadfence_block();
+  float acc = 0.f;
+  if (L.lane < 16)
+    for (int s = 0; s < nseg; s++) acc += ((const volatile float*)tile_part)[s * 16 + L.lane];
+  row = acc;
+  __syncwarp();
+  if (L.lane == 0) *cnt = 0;
+  return true;
+}
 
 // The decode kernel body.  ROUTED: the route comes from the caller (rt) and
 // the router phase is skipped; otherwise every CTA computes it.
 template <class SG, class SD, bool ROUTED>
 __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const MoeRoute* rt) {
   extern __shared__ __align__(128) uint8_t smem[];
-  // gate/up ring (S stages) and down ring (slots over the same memory)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kMaxStages;
-  uint64_t* full_d = empty + kMaxStages;
-  uint64_t* empty_d = full_d + kMaxStages;
   Ctl* ctl = reinterpret_cast<Ctl*>(smem + p.off_ctl);
   const uint8_t** etab = reinterpret_cast<const uint8_t**>(smem + p.off_etab);  // [ne][3] expert slices
-  float* part = reinterpret_cast<float*>(smem + p.off_part);  // [groups][2][kUnitWarps][16] warp sums
-  uint8_t* xtab = smem + p.off_xtab;
-  float* xsx = reinterpret_cast<float*>(smem + p.off_xsx);
-  uint8_t* htab = smem + p.off_htab;
-  float* hsx = reinterpret_cast<float*>(smem + p.off_hsx);
-  float* stg = reinterpret_cast<float*>(smem + p.off_stg);  // x staging
+  int* ucnt = reinterpret_cast<int*>(smem + p.off_ucnt);        // [S][kMaxDTiles] pairs done per tile
+  float* part = reinterpret_cast<float*>(smem + p.off_part);    // [S][maxp][16] pair partials
+  const VecTab xt = {smem + p.off_xtab, reinterpret_cast<float*>(smem + p.off_xmeta), smem + p.off_xrtab,
+                     reinterpret_cast<float*>(smem + p.off_xrmeta)};
+  const VecTab ht = {smem + p.off_htab, reinterpret_cast<float*>(smem + p.off_hmeta), smem + p.off_hrtab,
+                     reinterpret_cast<float*>(smem + p.off_hrmeta)};
+  float* xs = reinterpret_cast<float*>(smem + p.off_xs);  // residual rows of this CTA's down tiles
   uint8_t* stages = smem + p.off_stage;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -247,16 +273,13 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
   if (threadIdx.x == 0) {
     trace(p, kTrStart);
     for (int s = 0; s < S; s++) {
-      mbar_init(&full[s], kProducerThreads);  // every producer's copies
-      mbar_init(&empty[s], 1);                // the unit's first warp
-    }
-    for (int s = 0; s < kMaxStages; s++) {
-      mbar_init(&full_d[s], kProducerThreads);
-      mbar_init(&empty_d[s], 1);
+      mbar_init(&full[s], 1);  // the producer's arrive.expect_tx; the copies complete the bytes
+      mbar_init(&empty[s], W);  // every consumer warp, once per item
     }
     ctl->abort = 0;
     mbar_fence_init();
   }
+  for (int i = threadIdx.x; i < S * kMaxDTiles; i += blockDim.x) ucnt[i] = 0;
   // expert slice table (weights metadata: not written by the previous kernel)
   if constexpr (!ROUTED)
     for (int i = threadIdx.x; i < 3 * ne; i += blockDim.x) etab[i] = p.exp_tab[i];
@@ -266,7 +289,7 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
   if constexpr (ROUTED) {
     // ---- caller's route: x tables and the selection, no router phase --------
     pdl_wait();
-    stage_vec(p.hb, stg, d, threadIdx.x, blockDim.x, false);
+    stage_vec(p.hb, reinterpret_cast<float*>(xt.tab), d, threadIdx.x, blockDim.x, false);
     if (threadIdx.x < k) {
       ctl->ids[threadIdx.x] = rt->ids[threadIdx.x];
       ctl->wts[threadIdx.x] = rt->wts[threadIdx.x];
@@ -276,7 +299,7 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
       }
     }
     __syncthreads();
-    build_tables<SG>(stg, xtab, xsx, d / kSegElems, warp, (int)(blockDim.x / 32), lane);
+    build_tables<SG>(reinterpret_cast<const float*>(xt.tab), xt, d / kSegElems, warp, (int)(blockDim.x / 32), lane);
     __syncthreads();
     if (threadIdx.x == 0) trace(p, kTrRouted);
   } else {
@@ -301,7 +324,8 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
       for (int i = 0; i < 4; i++) r1[i] = __ldg(row + lane + 32 * i);
     }
     pdl_wait();
-    stage_vec(p.hb, stg, d, threadIdx.x, blockDim.x, false);
+    if (threadIdx.x == 0) trace(p, kTrPdl);
+    stage_vec(p.hb, reinterpret_cast<float*>(xt.tab), d, threadIdx.x, blockDim.x, false);
     for (int task = gw, it = 0; task < ntask; task += nw, it++) {
       const int e = task / nchunk, c = task - e * nchunk;
       float4 r[4];
@@ -336,17 +360,19 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
       trace(p, kTrRouterDone);
       red_add_release_gpu(&sy->router_arrive.v, 1u);
     }
-    // x table while the other CTAs finish their router partials
-    build_tables<SG>(stg, xtab, xsx, d / kSegElems, warp, (int)(blockDim.x / 32), lane);
+    // x table (in place over the staged x) while the other CTAs finish
+    build_tables<SG>(reinterpret_cast<const float*>(xt.tab), xt, d / kSegElems, warp, (int)(blockDim.x / 32), lane);
     if (threadIdx.x == 0) {
       if (!wait_geq(&sy->router_arrive.v, (unsigned)G, p.s.err)) ctl->abort = 1;
       trace(p, kTrPartials);
     }
     __syncthreads();
-    // logits in stg (the x table is built), probabilities in htab (idle
-    // until the down phase)
-    if (warp < (ne + 31) / 32 && !aborted(ctl))
-      route_warps(p, ctl, stg, reinterpret_cast<float*>(htab), warp, lane);
+    // logits and probabilities in the h table area (idle until the down phase)
+    const int R = (ne + 31) / 32;
+    if (warp < R && !aborted(ctl)) {
+      float* lg = reinterpret_cast<float*>(ht.tab);
+      route_warps(p, ctl, lg, lg + 32 * R, warp, lane);
+    }
     __syncthreads();
     if (threadIdx.x == 0) trace(p, kTrRouted);
   }
@@ -358,20 +384,13 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
   const int t = ((cta + 1) * k - 1) / G;
   const int c0 = t * G / k, c1 = (t + 1) * G / k;
   const int m = c1 - c0, j = cta - c0;
-  const int U = fe / 8, NT = d / 16;
+  const int U = fe / 8, NT = d / 16, P = p.dtiles;
   const int u0 = j * U / m, u1 = (j + 1) * U / m;
   const int i0 = j * NT / m, i1 = (j + 1) * NT / m;
   const bool active = !aborted(ctl) && ctl->ids[t] >= 0;
   const int nG = active ? u1 - u0 : 0, nD = i1 - i0;  // an unused slot still counts its tiles
-  // Down slots: after the gate/up stages this CTA uses when all of its tiles
-  // fit there (no wait on gate/up), else over the whole ring, each slot's
-  // first use waiting for the gate/up stages under it.
-  const int nGs = min(nG, S);
-  const int sd_after = min((int)((uint32_t)(S - nGs) * p.stage_bytes / p.dslot_bytes), kMaxStages);
-  const bool dsep = nD > 0 && sd_after >= nD;
-  const int SDn = dsep ? sd_after : p.nstages_d;
-  uint8_t* dring = stages + (dsep ? (size_t)nGs * p.stage_bytes : 0);
-  float* xs = reinterpret_cast<float*>(smem + p.off_xs);  // residual rows of this CTA's tiles
+  const int nDI = active ? (nD + P - 1) / P : 0;    // down items (up to P tiles per stage)
+  const int nItems = nG + nDI;
   for (int i = threadIdx.x; i < 16 * nD; i += blockDim.x) xs[i] = p.x[16 * i0 + i];
   const uint8_t* gsl = nullptr;
   const uint8_t* usl = nullptr;
@@ -390,173 +409,146 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
   }
 
   if (warp >= W) {
-    // ---- producers: 16-byte cp.async copies ---------------------------------
-    const int ptid = threadIdx.x - NC;
-    if (ptid == 0) trace(p, kTrProdFirst);
+    // ---- producer warp: bulk copies of the items, in ring order ---------------
+    if (lane == 0) trace(p, kTrProdFirst);
     if (active) {
-      for (int v = 0; v < nG; v++) {
-        const int slot = v % S;
-        if (!warp_wait(&empty[slot], ((uint32_t)(v / S) & 1u) ^ 1u, ctl, p.s.err)) break;
-        const size_t row = (size_t)(8 * (u0 + v)) * p.sg_gu.rb;
-        issue_unit(stages + (size_t)slot * p.stage_bytes, &full[slot], gsl + row, usl + row, p.sg_gu, ptid,
-                   kProducerThreads);
-      }
-      if (ptid == 0) trace(p, kTrProdFirstD);
-      for (int jj = 0; jj < nD && !aborted(ctl); jj++) {
-        const int slot = jj % SDn;
-        bool ok = true;
-        if (jj >= SDn) {
-          ok = warp_wait(&empty_d[slot], ((uint32_t)(jj / SDn) & 1u) ^ 1u, ctl, p.s.err);
-        } else if (!dsep) {
-          // first use of a slot over the gate/up stages: their last release
-          const uint32_t lo = (uint32_t)slot * p.dslot_bytes, hi = lo + p.dslot_bytes - 1u;
-          for (int st = (int)(lo / p.stage_bytes); ok && st <= (int)(hi / p.stage_bytes) && st < nG; st++)
-            ok = warp_wait(&empty[st], (uint32_t)((nG - 1 - st) / S) & 1u, ctl, p.s.err);
+      produce_ring(full, empty, stages, p.stage_bytes, S, nItems, ctl, p.s.err, [&](int i, int slot, uint8_t* st) {
+        if (i < nG) {
+          if (lane == 0) mbar_arrive_expect_tx(&full[slot], 16u * p.sg_gu.rb);
+          __syncwarp();
+          const size_t row = (size_t)(8 * (u0 + i)) * p.sg_gu.rb;
+          issue_tile_bulk(st, &full[slot], gsl + row, usl + row, p.sg_gu, lane);
+        } else {
+          if (i == nG && lane == 0) trace(p, kTrProdFirstD);
+          const int tt0 = (i - nG) * P, nt = min(P, nD - tt0);
+          if (lane == 0) mbar_arrive_expect_tx(&full[slot], (uint32_t)nt * 16u * p.sg_d.rb);
+          __syncwarp();
+          for (int tt = 0; tt < nt; tt++) {
+            const uint8_t* src = dsl + (size_t)(16 * (i0 + tt0 + tt)) * p.sg_d.rb;
+            issue_tile_bulk(st + (size_t)tt * p.dslot_bytes, &full[slot], src, src + 8 * (size_t)p.sg_d.rb, p.sg_d,
+                            lane);
+          }
         }
-        if (!ok) break;
-        const uint8_t* src = dsl + (size_t)(16 * (i0 + jj)) * p.sg_d.rb;
-        issue_unit(dring + (size_t)slot * p.dslot_bytes, &full_d[slot], src, src + 8 * (size_t)p.sg_d.rb, p.sg_d,
-                   ptid, kProducerThreads);
-      }
+      });
     }
-    if (ptid == 0) trace(p, kTrProdLast);
-    cp_async_wait_all();  // no copy may still target this CTA's shared memory at exit
-    if (ptid == 0) trace(p, kTrProdDrained);
+    if (lane == 0) trace(p, kTrProdDrained);
     return;
   }
 
   // ---- consumers ----------------------------------------------------------------
   const LaneCtx L = lane_ctx();
-  const int q = warp / kUnitWarps, r = warp - q * kUnitWarps;  // unit group, warp in it
   const int nsg = d / kSegElems, nsd = fe / kSegElems;
   BFrag bf;
   bf.reset();
-  if (threadIdx.x == 0 && !ROUTED && !aborted(ctl)) route_finish(p, ctl, cta == 0);  // read after the G phase
-  // gate/up units: unit v to group v mod kUnitGroups
-  int nst = 0;  // warp 0's unit stamps
-#pragma unroll 1
-  for (int v = q, it = 0; v < nG; v += kUnitGroups, it++) {
-    const int slot = v % S;
-    const bool ok = warp_wait(&full[slot], (uint32_t)(v / S) & 1u, ctl, p.s.err);
-    if (warp == 0 && lane == 0 && nst < kTrUnits) trace(p, kTrUnitBase + 2 * nst);
-    float g = 0.f, u = 0.f;
-    if (warp == 1 && lane == 0 && it == 0) trace(p, kTrDbg + 6);
-    if (ok)
-      tile_dot<SG>(stages + (size_t)slot * p.stage_bytes, p.sg_gu, r * nsg / kUnitWarps, (r + 1) * nsg / kUnitWarps,
-                   xtab, xsx, L, bf, g, u);
-    if (warp == 1 && lane == 0 && it == 0) trace(p, kTrDbg + 7);
-    float* pb = part + (size_t)((q * 2 + (it & 1)) * kUnitWarps) * 16;
-    if (L.t == 0) {
-      pb[r * 16 + L.g] = g;
-      pb[r * 16 + L.g + 8] = u;
-    }
-    named_bar(2 + q, kUnitWarps * 32);
-    if (r == 0) {
-      if (lane == 0) mbar_arrive(&empty[slot]);  // every warp of the group is done with the stage
-      if (lane < 8 && ok) {
-        float gs = 0.f, us = 0.f;
-#pragma unroll
-        for (int rr = 0; rr < kUnitWarps; rr++) {
-          gs += pb[rr * 16 + lane];
-          us += pb[rr * 16 + 8 + lane];
-        }
-        // rows 0..7 of a unit are gate rows, 8..15 the matching up rows: the
-        // reference's SwiGLU, gguf_run.c:206
-        p.s.hbuf[(size_t)t * fe + 8 * (u0 + v) + lane] = (gs / (1.0f + expf(-gs))) * us;
-      }
-    }
-    if (warp == 0 && lane == 0 && nst < kTrUnits) trace(p, kTrUnitBase + 2 * nst + 1);
-    nst++;
-  }
-  __threadfence();  // this warp's h values before the group's count
-  named_bar(1, NC);
-  if (threadIdx.x == 0) {
-    trace(p, kTrGDone);
-    if (nG > 0) red_add_release_gpu(&sy->group[t].v, (unsigned)nG);
-  }
+  if (threadIdx.x == 0 && !ROUTED && !aborted(ctl)) route_finish(p, ctl, cta == 0);
+  named_bar(1, NC);  // the renormalised weights before any combine reads them
 
-  if (nD > 0) {
-    if (active) {
-      // ---- the group's h row complete: stage it, build its tables ------------
-      if (threadIdx.x == 0) {
-        if (!aborted(ctl) && !wait_geq(&sy->group[t].v, (unsigned)U, p.s.err)) ctl->abort = 1;
-        trace(p, kTrGAll);
-      }
-      named_bar(1, NC);
-      if (!aborted(ctl)) {
-        stage_vec_cg8(p.s.hbuf + (size_t)t * fe, reinterpret_cast<float*>(htab), fe, threadIdx.x, NC);
-        named_bar(1, NC);
-        build_tables<SD>(reinterpret_cast<const float*>(htab), htab, hsx, nsd, warp, W, lane);
-      }
-      named_bar(1, NC);
-      if (threadIdx.x == 0) trace(p, kTrHtab);
-    }
-    // ---- down tiles: tile jj to group jj mod kUnitGroups ------------------
-    float* yb = p.s.ybuf + (size_t)t * d;
-    if (active) {
+  // count one finished down tile; the last of the k experts to finish it
+  // combines them in the reference's order (acc = sum over rank tt of
+  // w_tt * y_tt, then x += acc) into the residual
+  auto count_tile = [&](int tile) {
+    __threadfence();  // this warp's rows of the tile before its count
+    int last = 0;
+    if (lane == 0) last = atomicAdd(&p.s.tile_cnt[(size_t)tile * kTileCntStride], 1u) == (unsigned)(k - 1);
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last) {
+      __threadfence();
+      if (lane < 16 && !aborted(ctl)) {
+        const int row = 16 * tile + lane;
+        float acc = 0.f;
 #pragma unroll 1
-      for (int jj = q, it = 0; jj < nD; jj += kUnitGroups, it++) {
-        const int slot = jj % SDn;
-        const bool ok = warp_wait(&full_d[slot], (uint32_t)(jj / SDn) & 1u, ctl, p.s.err);
-        if (warp == 0 && lane == 0 && nst < kTrUnits) trace(p, kTrUnitBase + 2 * nst);
-        if (warp == 1 && lane == 0 && it < 3) trace(p, kTrDbg + 2 * it);
-        float y0 = 0.f, y1 = 0.f;
-        if (ok)
-          tile_dot<SD>(dring + (size_t)slot * p.dslot_bytes, p.sg_d, r * nsd / kUnitWarps, (r + 1) * nsd / kUnitWarps,
-                       htab, hsx, L, bf, y0, y1);
-        if (warp == 1 && lane == 0 && it < 3) trace(p, kTrDbg + 2 * it + 1);
-        float* pb = part + (size_t)((q * 2 + (it & 1)) * kUnitWarps) * 16;
-        if (L.t == 0) {
-          pb[r * 16 + L.g] = y0;
-          pb[r * 16 + L.g + 8] = y1;
-        }
-        named_bar(2 + q, kUnitWarps * 32);
-        if (r == 0) {
-          if (lane == 0) mbar_arrive(&empty_d[slot]);
-          if (lane < 16 && ok) {
-            float y = 0.f;
+        for (int t0 = 0; t0 < k; t0 += 8) {
+          float yv[8];  // eight experts' rows in flight at once
 #pragma unroll
-            for (int rr = 0; rr < kUnitWarps; rr++) y += pb[rr * 16 + lane];
-            yb[16 * (i0 + jj) + lane] = y;
-          }
+          for (int u = 0; u < 8; u++)
+            yv[u] = (t0 + u < k && ctl->ids[t0 + u] >= 0) ? __ldcg(p.s.ybuf + (size_t)(t0 + u) * d + row) : 0.f;
+#pragma unroll
+          for (int u = 0; u < 8; u++)
+            if (t0 + u < k && ctl->ids[t0 + u] >= 0) acc = __fadd_rn(acc, __fmul_rn(ctl->wts[t0 + u], yv[u]));
         }
-        if (warp == 0 && lane == 0 && nst < kTrUnits) trace(p, kTrUnitBase + 2 * nst + 1);
-        nst++;
+        p.x[row] = __fadd_rn(xs[16 * (tile - i0) + lane], acc);
       }
+      __syncwarp();
+      if (lane == 0) p.s.tile_cnt[(size_t)tile * kTileCntStride] = 0u;
     }
-    // ---- count this CTA's tiles, all at once; the last of the k experts to
-    // finish a tile combines them --------------------------------------------
-    __threadfence();  // the tiles' rows before their counts
+  };
+
+  // the G -> D boundary: publish this CTA's units, wait for the group's, then
+  // stage the expert's h and build its tables
+  auto g_to_d = [&](bool need_h) {
+    __threadfence();  // this warp's h values before the group's count
     named_bar(1, NC);
-#pragma unroll 1
-    for (int jj = warp; jj < nD; jj += W) {
-      const int tile = i0 + jj;
-      int last = 0;
-      if (lane == 0) last = atomicAdd(&p.s.tile_cnt[(size_t)tile * kTileCntStride], 1u) == (unsigned)(k - 1);
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (last) {
-        __threadfence();
-        if (lane < 16 && !aborted(ctl)) {
-          // the reference's combine order: acc = sum over rank tt of w_tt * y_tt, then x += acc
-          const int row = 16 * tile + lane;
-          float acc = 0.f;
-#pragma unroll 1
-          for (int t0 = 0; t0 < k; t0 += 8) {
-            float yv[8];  // eight experts' rows in flight at once
-#pragma unroll
-            for (int u = 0; u < 8; u++)
-              yv[u] = (t0 + u < k && ctl->ids[t0 + u] >= 0) ? __ldcg(p.s.ybuf + (size_t)(t0 + u) * d + row) : 0.f;
-#pragma unroll
-            for (int u = 0; u < 8; u++)
-              if (t0 + u < k && ctl->ids[t0 + u] >= 0) acc = __fadd_rn(acc, __fmul_rn(ctl->wts[t0 + u], yv[u]));
-          }
-          p.x[row] = __fadd_rn(xs[16 * jj + lane], acc);
-        }
-        __syncwarp();
-        if (lane == 0) p.s.tile_cnt[(size_t)tile * kTileCntStride] = 0u;
-      }
+    if (threadIdx.x == 0) {
+      trace(p, kTrGDone);
+      if (nG > 0) red_add_release_gpu(&sy->group[t].v, (unsigned)nG);
+      if (need_h && !aborted(ctl) && !wait_geq(&sy->group[t].v, (unsigned)U, p.s.err)) ctl->abort = 1;
+      trace(p, kTrGAll);
     }
+    if (!need_h) return;
+    // every warp meets the same barriers whatever the abort flag says (the
+    // producer may set it at any time): it only decides whether work is done
+    named_bar(1, NC);
+    if (!aborted(ctl))
+      stage_vec_cg8(p.s.hbuf + (size_t)t * fe, reinterpret_cast<float*>(ht.tab), fe, threadIdx.x, NC);
+    named_bar(1, NC);
+    if (!aborted(ctl)) build_tables<SD>(reinterpret_cast<const float*>(ht.tab), ht, nsd, warp, W, lane);
+    named_bar(1, NC);
+    if (threadIdx.x == 0) trace(p, kTrHtab);
+  };
+
+#pragma unroll 1
+  for (int i = 0; i < nItems; i++) {
+    const int slot = i % S;
+    const uint32_t par = (uint32_t)(i / S) & 1u;
+    const bool isd = i >= nG;
+    if (i == nG) g_to_d(true);
+    const int nt = isd ? min(P, nD - (i - nG) * P) : 1;
+    const int nseg = isd ? nsd : nsg;
+    const int np = nt * nseg;
+    const int q0 = isd ? nG * nsg + (i - nG) * P * nsd : i * nsg;  // pairs dealt before this item
+    int first = (warp - q0 % W) % W;
+    if (first < 0) first += W;
+    if (first < np) {
+      const bool ok = warp_wait(&full[slot], par, ctl, p.s.err);
+      uint8_t* st = stages + (size_t)slot * p.stage_bytes;
+      float* sp = part + (size_t)slot * p.maxp * 16;
+#pragma unroll 1
+      for (int pp = first; pp < np; pp += W) {
+        const int tt = pp / nseg, seg = pp - tt * nseg;
+        float t0 = 0.f, t1 = 0.f;
+        if (ok) {
+          if (isd) {
+            const uint8_t* base = st + (size_t)tt * p.dslot_bytes;
+            seg_dot<SD>(stage_row(base, p.sg_d, L.g), stage_row(base, p.sg_d, L.g + 8), seg, ht, L, bf, t0, t1);
+          } else {
+            seg_dot<SG>(stage_row(st, p.sg_gu, L.g), stage_row(st, p.sg_gu, L.g + 8), seg, xt, L, bf, t0, t1);
+          }
+        }
+        float row;
+        if (!pair_done(t0, t1, sp + pp * 16, sp + tt * nseg * 16, &ucnt[slot * kMaxDTiles + tt], nseg, L, row))
+          continue;
+        if (!isd) {
+          // rows 0..7 of a unit are gate rows, 8..15 the matching up rows: the
+          // reference's SwiGLU, gguf_run.c:206
+          const float up = __shfl_down_sync(0xffffffffu, row, 8);
+          if (lane < 8 && ok) p.s.hbuf[(size_t)t * fe + 8 * (u0 + i) + lane] = (row / (1.0f + expf(-row))) * up;
+        } else {
+          const int tile = i0 + (i - nG) * P + tt;
+          if (lane < 16 && ok) p.s.ybuf[(size_t)t * d + 16 * tile + lane] = row;
+          count_tile(tile);
+        }
+      }
+    } else if (i >= S) {
+      // nothing of this item here: wait until the slot's previous item is
+      // released, so that this arrival counts for this item's phase
+      warp_wait(&empty[slot], par ^ 1u, ctl, p.s.err);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
   }
+  if (active && nDI == 0) g_to_d(false);  // no down tiles here: publish the units only
+  if (!active)
+    for (int jj = warp; jj < nD; jj += W) count_tile(i0 + jj);
   if (threadIdx.x == 0) trace(p, kTrDDone);
 
   // ---- launch exit: the last CTA out resets the per-launch words -------------
@@ -593,8 +585,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) gemv_kernel(const __grid_co
   Ctl* ctl = reinterpret_cast<Ctl*>(smem + p.off_ctl);
   float* part = reinterpret_cast<float*>(smem + p.off_part);
   int* ucnt = reinterpret_cast<int*>(smem + p.off_ucnt);
-  uint8_t* xtab = smem + p.off_xtab;
-  float* xsx = reinterpret_cast<float*>(smem + p.off_xsx);
+  const VecTab xt = {smem + p.off_xtab, reinterpret_cast<float*>(smem + p.off_xmeta), smem + p.off_xrtab,
+                     reinterpret_cast<float*>(smem + p.off_xrmeta)};
   uint8_t* stages = smem + p.off_stage;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int W = kConsumerWarps;
@@ -603,7 +595,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) gemv_kernel(const __grid_co
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; s++) {
-      mbar_init(&full[s], kProducerThreads);
+      mbar_init(&full[s], 1);
       mbar_init(&empty[s], W);
     }
     ctl->abort = 0;
@@ -623,20 +615,18 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) gemv_kernel(const __grid_co
   __syncthreads();
 
   if (warp >= W) {
-    const int ptid = threadIdx.x - NC;
-    for (int v = 0; v < nU; v++) {
-      const int slot = v % S;
-      if (!warp_wait(&empty[slot], (((uint32_t)(v / S)) & 1u) ^ 1u, ctl, p.err)) break;
+    produce_ring(full, empty, stages, p.stage_bytes, S, nU, ctl, p.err, [&](int v, int slot, uint8_t* st) {
+      if (lane == 0) mbar_arrive_expect_tx(&full[slot], 16u * p.sg.rb);
+      __syncwarp();
       const uint8_t* src = p.W + (size_t)(16 * (u0 + v)) * p.sg.rb;
-      issue_unit(stages + (size_t)slot * p.stage_bytes, &full[slot], src, src + 8 * (size_t)p.sg.rb, p.sg, ptid,
-                 kProducerThreads);
-    }
-    cp_async_wait_all();
+      issue_tile_bulk(st, &full[slot], src, src + 8 * (size_t)p.sg.rb, p.sg, lane);
+    });
     return;
   }
-  // x table (consumers only; the producers already stream weights)
+  // x table (consumers only; the producer already streams weights), built
+  // in place over the staged x
   {
-    float* xs = reinterpret_cast<float*>(smem + p.off_stg);
+    float* xs = reinterpret_cast<float*>(xt.tab);
     if (((uintptr_t)p.x & 15) == 0 && (p.n & 3) == 0) {
       stage_vec(p.x, xs, p.n, threadIdx.x, NC, false);
     } else {
@@ -657,7 +647,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) gemv_kernel(const __grid_co
       for (int i = threadIdx.x; i < p.n; i += NC) xs[i] = xs[i] * r * __ldg(p.norm_w + i);
       named_bar(1, NC);
     }
-    build_tables<SF>(xs, xtab, xsx, p.n / kSegElems, warp, W, lane);
+    build_tables<SF>(xs, xt, nseg, warp, W, lane);
     named_bar(1, NC);
   }
   const LaneCtx L = lane_ctx();
@@ -667,8 +657,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) gemv_kernel(const __grid_co
     const int slot = v % S;
     const bool ok = warp_wait(&full[slot], (uint32_t)(v / S) & 1u, ctl, p.err);
     float val = 0.f;
-    const bool last = consume<SF>(stages + (size_t)slot * p.stage_bytes, p.sg, v, nseg, warp, xtab, xsx,
-                                  part + slot * p.part_stride, &ucnt[slot], L, &val, ok, bf);
+    const bool last = consume_unit<SF>(stages + (size_t)slot * p.stage_bytes, p.sg, v, ok ? nseg : 0, W, warp, xt,
+                                       part + slot * p.part_stride, &ucnt[slot], L, &val, bf);
     if (last && ok && lane < 16) p.y[16 * (u0 + v) + lane] = val;
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
@@ -687,7 +677,7 @@ static uint32_t gcd_u(uint32_t a, uint32_t b) {
   return a;
 }
 
-bool fast_format(uint32_t type) { return type == T_Q8_0 || type == T_Q4_K || type == T_Q6_K; }
+bool fast_format(uint32_t type) { return type == T_Q8_0 || type == T_Q4_K || type == T_Q6_K || type == T_Q5_0; }
 
 int stage_geom(uint32_t type, int K, StageGeom* sg) {
   if (!fast_format(type) || K <= 0 || K % kSegElems) return VIREO_ERR_UNSUPPORTED;
@@ -696,7 +686,7 @@ int stage_geom(uint32_t type, int K, StageGeom* sg) {
   const uint32_t rb = (uint32_t)(K / be) * (uint32_t)bb;
   uint32_t G = 16u / gcd_u(rb, 16u);
   if (G > 8) return VIREO_ERR_UNSUPPORTED;
-  if ((type == T_Q8_0 || type == T_Q4_K) && G != 1) return VIREO_ERR_UNSUPPORTED;
+  if ((type == T_Q8_0 || type == T_Q4_K || type == T_Q5_0) && G != 1) return VIREO_ERR_UNSUPPORTED;
   const uint32_t gbytes = G * rb;
   const uint32_t pad = (16u - gbytes % 128u + 128u) % 128u;
   sg->rb = rb;
@@ -725,6 +715,7 @@ static const void* moe_kernel_for(uint32_t dtype, bool routed) {
   if (dtype == T_Q8_0) return moe_kernel_ptr<SG, SegQ8>(routed);
   if (dtype == T_Q4_K) return moe_kernel_ptr<SG, SegQ4K>(routed);
   if (dtype == T_Q6_K) return moe_kernel_ptr<SG, SegQ6K>(routed);
+  if (dtype == T_Q5_0) return moe_kernel_ptr<SG, SegQ5>(routed);
   return nullptr;
 }
 
@@ -732,42 +723,56 @@ const void* moe_decode_kernel_for(uint32_t gtype, uint32_t dtype, bool routed) {
   if (gtype == T_Q8_0) return moe_kernel_for<SegQ8>(dtype, routed);
   if (gtype == T_Q4_K) return moe_kernel_for<SegQ4K>(dtype, routed);
   if (gtype == T_Q6_K) return moe_kernel_for<SegQ6K>(dtype, routed);
+  if (gtype == T_Q5_0) return moe_kernel_for<SegQ5>(dtype, routed);
   return nullptr;
 }
 
 // Shared-memory layout for the MoE kernel; picks the deepest stage ring that
 // fits.  Returns the dynamic shared-memory bytes (0 if nothing fits).
 uint32_t moe_decode_layout(MoeDecodeParams* p, uint32_t smem_limit, int grid) {
-  const uint32_t stage = up_to(std::max(2u * p->sg_gu.hstride, 2u * p->sg_d.hstride), 128u);
-  const uint32_t dslot = up_to(2u * p->sg_d.hstride, 128u);
+  // a stage holds one gate/up unit or the whole number of down tiles nearest
+  // to the same bytes (the stage grows to fit them)
+  const uint32_t gstage = up_to(2u * p->sg_gu.hstride, 128u);  // one gate/up unit
+  const uint32_t dslot = up_to(2u * p->sg_d.hstride, 16u);     // one down tile
+  const uint32_t dt = std::min<uint32_t>(std::max<uint32_t>((gstage + dslot / 2) / dslot, 1u), (uint32_t)kMaxDTiles);
+  const uint32_t stage = up_to(std::max(gstage, dt * dslot), 128u);
   p->stage_bytes = stage;
   p->dslot_bytes = dslot;
-  uint32_t off = 4u * kMaxStages * 8u;  // full/empty barriers of both rings
+  p->dtiles = (int)dt;
+  const int nsg = p->d / kSegElems, nsd = p->fe / kSegElems, R = (p->ne + 31) / 32;
+  p->maxp = std::max(nsg, p->dtiles * nsd);
+  uint32_t off = 2u * kMaxStages * 8u;  // full/empty barriers
   p->off_ctl = off;
   off = up_to(off + (uint32_t)sizeof(Ctl), 16);
   p->off_etab = off;
   off = up_to(off + (uint32_t)(3 * p->ne * sizeof(void*)), 16);
-  p->off_part = off;
-  off = up_to(off + (uint32_t)(kUnitGroups * 2 * kUnitWarps * 16 * 4), 16);
-  p->off_xtab = off;
-  off = up_to(off + (uint32_t)(4 * p->d), 16);
-  p->off_xsx = off;
-  off = up_to(off + (uint32_t)(p->d / kSegElems * kMeta * 4), 16);
-  p->off_htab = off;  // one expert's h tables; the routing warps' probabilities before that
-  off = up_to(off + (uint32_t)std::max(4 * p->fe, 4 * p->ne * ((p->ne + 31) / 32)), 16);
-  p->off_hsx = off;
-  off = up_to(off + (uint32_t)((p->fe / kSegElems) * kMeta * 4), 16);
+  p->off_ucnt = off;
+  off = up_to(off + (uint32_t)(kMaxStages * kMaxDTiles * 4), 16);
+  p->off_xtab = off;  // x tables (the staged x before that)
+  off = up_to(off + (uint32_t)(nsg * kSegTabBytes), 16);
+  p->off_xmeta = off;
+  off = up_to(off + (uint32_t)(nsg * kMeta * 4), 16);
+  p->off_xrtab = off;
+  off = up_to(off + (uint32_t)(nsg * kResTabBytes), 16);
+  p->off_xrmeta = off;
+  off = up_to(off + (uint32_t)(nsg * kMeta * 4), 16);
+  p->off_htab = off;  // one expert's h tables; the routing warps' logits and probabilities before that
+  off = up_to(off + (uint32_t)std::max(nsd * kSegTabBytes, 4 * (32 * R + R * ((p->ne + 3) & ~3))), 16);
+  p->off_hmeta = off;
+  off = up_to(off + (uint32_t)(nsd * kMeta * 4), 16);
+  p->off_hrtab = off;
+  off = up_to(off + (uint32_t)(nsd * kResTabBytes), 16);
+  p->off_hrmeta = off;
+  off = up_to(off + (uint32_t)(nsd * kMeta * 4), 16);
   p->off_xs = off;  // residual rows of a CTA's tiles: at most d / 16 / floor(grid / k) + 1 tiles
   off = up_to(off + (uint32_t)(64 * (p->d / 16 / std::max(1, grid / std::max(1, p->k)) + 1)), 16);
-  p->off_stg = off;
-  off = up_to(off + (uint32_t)std::max(4 * p->d, 4 * p->k), 128);
-  p->off_stage = off;
+  p->off_part = off;
   for (int S = kMaxStages; S >= 2; S--) {
-    const int SD = (int)std::min<uint32_t>((uint32_t)kMaxStages, (uint32_t)S * stage / dslot);
-    const uint32_t total = off + (uint32_t)S * stage + 16;
-    if (total <= smem_limit && SD >= 1) {
+    const uint32_t st = up_to(off + (uint32_t)(S * p->maxp * 64), 128);
+    const uint32_t total = st + (uint32_t)S * stage;
+    if (total <= smem_limit) {
       p->nstages = S;
-      p->nstages_d = SD;
+      p->off_stage = st;
       return total;
     }
   }
@@ -806,16 +811,17 @@ const void* gemv_kernel_for(uint32_t type) {
   if (type == T_Q8_0) return reinterpret_cast<const void*>(&gemv_kernel<SegQ8>);
   if (type == T_Q4_K) return reinterpret_cast<const void*>(&gemv_kernel<SegQ4K>);
   if (type == T_Q6_K) return reinterpret_cast<const void*>(&gemv_kernel<SegQ6K>);
+  if (type == T_Q5_0) return reinterpret_cast<const void*>(&gemv_kernel<SegQ5>);
   return nullptr;
 }
 
 // Shared-memory layout for gemv_kernel: the deepest ring that fits, and no
 // deeper than the max_units units a CTA streams (at least 2 stages).
 uint32_t gemv_layout(GemvParams* p, uint32_t smem_limit, int max_units) {
-  const int W = kConsumerWarps;
+  const int W = kConsumerWarps, nseg = p->n / kSegElems;
   const uint32_t stage = up_to(2u * p->sg.hstride, 128u);
   p->stage_bytes = stage;
-  p->part_stride = (uint32_t)std::max(W, p->n / kSegElems) * 16u;
+  p->part_stride = (uint32_t)std::max(W, nseg) * 16u;
   for (int S = std::max(2, std::min(kMaxStages, max_units)); S >= 2; S--) {
     uint32_t off = 2u * kMaxStages * 8u;
     p->off_ctl = off;
@@ -824,14 +830,16 @@ uint32_t gemv_layout(GemvParams* p, uint32_t smem_limit, int max_units) {
     off = up_to(off + (uint32_t)S * p->part_stride * 4u, 16);
     p->off_ucnt = off;
     off = up_to(off + (uint32_t)(S * 4), 16);
-    p->off_xtab = off;
-    off = up_to(off + (uint32_t)(4 * p->n), 16);
-    p->off_xsx = off;
-    off = up_to(off + (uint32_t)(p->n / kSegElems * kMeta * 4), 16);
-    p->off_stg = off;
-    off = up_to(off + (uint32_t)(4 * p->n), 128);
+    p->off_xtab = off;  // x tables (the staged x before that)
+    off = up_to(off + (uint32_t)(nseg * kSegTabBytes), 16);
+    p->off_xmeta = off;
+    off = up_to(off + (uint32_t)(nseg * kMeta * 4), 16);
+    p->off_xrtab = off;
+    off = up_to(off + (uint32_t)(nseg * kResTabBytes), 16);
+    p->off_xrmeta = off;
+    off = up_to(off + (uint32_t)(nseg * kMeta * 4), 128);
     p->off_stage = off;
-    off += (uint32_t)S * stage + 16;
+    off += (uint32_t)S * stage;
     if (off <= smem_limit) {
       p->nstages = S;
       return off;

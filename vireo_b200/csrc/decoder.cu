@@ -105,6 +105,7 @@ struct AttnParams {
   int nh, nkv, hs, pos, npos, max_ctx, nchunk;
   float scale, eps;
   float* part;  // [nh][nchunk][hs + 2]: acc, m, l
+  int* err;     // status word (tensor-core path: a copy that never landed)
 };
 
 VDEV float kv_load(const float* p, size_t i) { return p[i]; }
@@ -131,9 +132,13 @@ VDEV void kv_load8(const __half* p, size_t i, float (&o)[8]) {
 // NEOX rotation of `nv` heads of HS values in place (rope_neox,
 // gguf_run.c:168-173): pairs (j, j + HS/2) turned by pos * freq[j]
 template <int HS>
-VDEV void rope_heads(float* v, int nv, int pos, const float* freq) {
+VDEV void rope_heads(float* v, int nv, int pos, const float* freq, int tid = -1, int nthr = 0) {
   constexpr int half = HS / 2;
-  for (int idx = threadIdx.x; idx < nv * half; idx += blockDim.x) {
+  if (tid < 0) {
+    tid = threadIdx.x;
+    nthr = blockDim.x;
+  }
+  for (int idx = tid; idx < nv * half; idx += nthr) {
     const int h = idx / half, j = idx - h * half;
     float* w = v + h * HS;
     const float a = (float)pos * freq[j];
@@ -341,6 +346,347 @@ __global__ void __launch_bounds__(kAttnChunk* SPLIT) dec_attn_partial(const __gr
   }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core attention over the f16 KV cache: one CTA per (chunk of
+// positions, kv head), four consumer warps and one producer warp.
+//
+// The producer streams the chunk's cached K and V rows in tiles of
+// kAttnTile positions into a ring of shared-memory stages (one 1-D bulk copy
+// per row, rows padded to HS * 2 + 16 bytes so that the 8 rows an ldmatrix
+// reads fall on distinct banks).  Consumer warp w takes rows 16 w .. 16 w + 15
+// of every tile:
+//   scores  S = Q K^T with mma.m16n8k16 (f16 in, fp32 accumulate): the QG q
+//           heads of the kv group are the M rows (rows QG..15 zero), 8
+//           positions are the N columns, K is the head dimension; the K rows
+//           load as B fragments with ldmatrix.  Q carries the 1/sqrt(HS)
+//           scale.
+//   softmax per head over the warp's positions, online across tiles (the
+//           reference's running max / sum rule, kvstore.h:77-101), in fp32;
+//   values  O += P V with the score accumulators of two position tiles
+//           reused as the A fragment (P rounded to f16) and the V rows loaded
+//           transposed (ldmatrix.trans) as B fragments.
+// The four warps' states are merged in shared memory; the CTA's state per q
+// head (acc, m, l) goes to part, and the last CTA of the kv head to finish
+// merges the chunks in chunk order and writes the attention output.
+// The q/k post-processing and the KV append are those of dec_attn_partial.
+// ---------------------------------------------------------------------------
+constexpr int kAttnTile = 64;   // positions per stage
+constexpr int kAttnWarps = 4;   // consumer warps, 16 positions of a tile each
+constexpr int kAttnStages = 3;
+constexpr int kAttnMmaThreads = 32 * (kAttnWarps + 1);
+
+template <int HS>
+struct AttnMmaLayout {
+  static constexpr int kRow = HS * 2 + 16;          // padded f16 row bytes
+  static constexpr int kStage = 2 * kAttnTile * kRow;  // K rows then V rows
+  static constexpr int kOffQ = 64;                  // after the barriers
+};
+
+template <int QG, int HS>
+constexpr size_t attn_mma_smem() {
+  using Ly = AttnMmaLayout<HS>;
+  size_t off = Ly::kOffQ + sizeof(float) * (QG * HS + 2 * HS + 32 + 8);
+  off += sizeof(float) * kAttnWarps * QG * (HS + 2);  // warp states for the merge
+  off = (off + 127) / 128 * 128;
+  return off + (size_t)kAttnStages * Ly::kStage;
+}
+
+template <int QG, int HS>
+__global__ void __launch_bounds__(kAttnMmaThreads) dec_attn_mma(const __grid_constant__ AttnParams p, int C,
+                                                                 float* out, unsigned int* cnt) {
+  using Ly = AttnMmaLayout<HS>;
+  constexpr int NC = 32 * kAttnWarps;  // consumer threads
+  constexpr int KS = HS / 16;          // k16 steps of the scores
+  constexpr int NT = HS / 8;           // n8 tiles of the values
+  extern __shared__ __align__(128) uint8_t sm[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm);
+  uint64_t* empty = full + kAttnStages;
+  float* sq = reinterpret_cast<float*>(sm + Ly::kOffQ);  // [QG][HS] q heads
+  float* skv = sq + QG * HS;                             // [2][HS] this position's k, v
+  float* bred = skv + 2 * HS;                            // [32]
+  int* flags = reinterpret_cast<int*>(bred + 32);        // [8]: abort, last
+  float* wst = bred + 40;                                // [warps][QG][HS + 2] warp states
+  uint8_t* ring = sm + ((Ly::kOffQ + sizeof(float) * (QG * HS + 2 * HS + 40 + kAttnWarps * QG * (HS + 2)) + 127) /
+                        128 * 128);
+  const int c = blockIdx.x, kh = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int h0 = kh * QG;
+  __half* kb = reinterpret_cast<__half*>(p.kc) + (size_t)kh * p.max_ctx * HS;
+  __half* vb = reinterpret_cast<__half*>(p.vc) + (size_t)kh * p.max_ctx * HS;
+  const int p0 = c * C, n = min(C, p.npos - p0);
+  const int cur = p.pos - p0;  // this position's row in the chunk (the chunk's last, if it holds it)
+  const bool has_cur = cur >= 0 && cur < n;
+  const int nold = has_cur ? cur : n;  // cached rows to stream
+  const int ntile = (n + kAttnTile - 1) / kAttnTile;
+  if (tid == 0) {
+    for (int s = 0; s < kAttnStages; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kAttnWarps);
+    }
+    flags[0] = 0;
+    mbar_fence_init();
+    if (nold > 0) {
+      prefetch_l2(kb + (size_t)p0 * HS, (uint32_t)(nold * HS * 2));
+      prefetch_l2(vb + (size_t)p0 * HS, (uint32_t)(nold * HS * 2));
+    }
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+  pdl_wait();  // q, k, v written by the projection kernel; earlier rows by earlier steps
+
+  if (warp == kAttnWarps) {
+    // ---- producer: the chunk's cached rows, tile by tile ----------------------
+    int i = 0;
+    for (; i < ntile; i++) {
+      const int slot = i % kAttnStages;
+      if (i >= kAttnStages) {
+        int ok = 1;
+        if (lane == 0) ok = mbar_wait(&empty[slot], ((uint32_t)(i / kAttnStages) & 1u) ^ 1u, flags) ? 1 : 0;
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      }
+      const int r0 = i * kAttnTile, rows = max(0, min(kAttnTile, nold - r0));
+      uint8_t* st = ring + (size_t)slot * Ly::kStage;
+      if (lane == 0) mbar_arrive_expect_tx(&full[slot], (uint32_t)(2 * rows * HS * 2));
+      __syncwarp();
+      for (int r = lane; r < rows; r += 32) {
+        const size_t g = (size_t)(p0 + r0 + r) * HS;
+        bulk_g2s(st + (size_t)r * Ly::kRow, kb + g, HS * 2, &full[slot]);
+        bulk_g2s(st + (size_t)(kAttnTile + r) * Ly::kRow, vb + g, HS * 2, &full[slot]);
+      }
+    }
+    // no copy may still be landing when the CTA exits
+    if (lane == 0) {
+      const int never = 0;
+      for (int j = i > kAttnStages ? i - kAttnStages : 0; j < i; j++)
+        mbar_wait(&full[j % kAttnStages], (uint32_t)(j / kAttnStages) & 1u, &never);
+    }
+    __syncwarp();
+    return;
+  }
+
+  // ---- consumers: q heads h0 .. h0 + QG - 1 (and this position's k, v) -------
+  for (int i = tid; i < QG * HS; i += NC) {
+    const size_t gi = (size_t)h0 * HS + i;
+    sq[i] = p.bq ? p.q[gi] + p.bq[gi] : p.q[gi];
+  }
+  if (has_cur)
+    for (int i = tid; i < HS; i += NC) {
+      const size_t gi = (size_t)kh * HS + i;
+      skv[i] = p.bk ? p.k[gi] + p.bk[gi] : p.k[gi];
+      skv[HS + i] = p.bv ? p.v[gi] + p.bv[gi] : p.v[gi];
+    }
+  // full-width norms need the whole vector's sum of squares
+  float qss = 0.f, kss = 0.f;
+  if (p.qn && p.qn_len != HS) {
+    float v = 0.f;
+    for (int i = tid; i < p.qn_len; i += NC) {
+      const float a = p.bq ? p.q[i] + p.bq[i] : p.q[i];
+      v += a * a;
+    }
+    v = warp_sum(v);
+    if (lane == 0) bred[warp] = v;
+    asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
+    for (int w = 0; w < kAttnWarps; w++) qss += bred[w];
+    asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
+  }
+  if (has_cur && p.kn && p.kn_len != HS) {
+    float v = 0.f;
+    for (int i = tid; i < p.kn_len; i += NC) {
+      const float a = p.bk ? p.k[i] + p.bk[i] : p.k[i];
+      v += a * a;
+    }
+    v = warp_sum(v);
+    if (lane == 0) bred[warp] = v;
+    asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
+    for (int w = 0; w < kAttnWarps; w++) kss += bred[w];
+    asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
+  if (p.qn)
+    for (int g = warp; g < QG; g += kAttnWarps) {
+      float ss = qss;
+      if (p.qn_len == HS) {
+        ss = 0.f;
+        for (int i = lane; i < HS; i += 32) ss += sq[g * HS + i] * sq[g * HS + i];
+        ss = warp_sum(ss);
+      }
+      norm_head(sq + g * HS, HS, p.qn_len == HS ? p.qn : p.qn + (size_t)(h0 + g) * HS, ss, p.qn_len, p.eps, lane);
+    }
+  if (has_cur && p.kn && warp == kAttnWarps - 1) {
+    float ss = kss;
+    if (p.kn_len == HS) {
+      ss = 0.f;
+      for (int i = lane; i < HS; i += 32) ss += skv[i] * skv[i];
+      ss = warp_sum(ss);
+    }
+    norm_head(skv, HS, p.kn_len == HS ? p.kn : p.kn + (size_t)kh * HS, ss, p.kn_len, p.eps, lane);
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
+  rope_heads<HS>(sq, QG, p.pos, p.freq, tid, NC);
+  if (has_cur) rope_heads<HS>(skv, 1, p.pos, p.freq, tid, NC);
+  asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
+  if (has_cur)  // the cache row later steps read
+    for (int i = tid; i < HS; i += NC) {
+      kb[(size_t)p.pos * HS + i] = __float2half_rn(skv[i]);
+      vb[(size_t)p.pos * HS + i] = __float2half_rn(skv[HS + i]);
+    }
+
+  // Q as A fragments, scaled: row g (a q head when g < QG), rows g + 8 zero
+  const int g = lane >> 2, t4 = lane & 3;
+  uint32_t qa[KS][2];
+#pragma unroll
+  for (int s = 0; s < KS; s++) {
+    if (g < QG) {
+      const float* q = sq + g * HS + 16 * s + 2 * t4;
+      qa[s][0] = pack_h2(q[0] * p.scale, q[1] * p.scale);
+      qa[s][1] = pack_h2(q[8] * p.scale, q[9] * p.scale);
+    } else {
+      qa[s][0] = qa[s][1] = 0u;
+    }
+  }
+  float o[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;
+
+#pragma unroll 1
+  for (int i = 0; i < ntile; i++) {
+    const int slot = i % kAttnStages;
+    int ok = 1;
+    if (lane == 0) ok = mbar_wait(&full[slot], (uint32_t)(i / kAttnStages) & 1u, flags) ? 1 : 0;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    __syncwarp();
+    if (!ok && lane == 0 && !flags[0]) {
+      flags[0] = 1;
+      set_error(p.err, VIREO_ERR_TIMEOUT);
+    }
+    uint8_t* st = ring + (size_t)slot * Ly::kStage;
+    const int rows = min(kAttnTile, n - i * kAttnTile);  // positions of this tile
+    const int wr = 16 * warp;                             // this warp's first row
+    if (ok && wr < rows) {
+      // rows the copies did not fill: this position's k, v (from the q/k
+      // step, f16) and, past the chunk's end, zeros (P = 0 cannot cancel a
+      // NaN left in shared memory)
+      const int last = (n - 1) - i * kAttnTile;  // the chunk's last row in this tile, if it is here
+      for (int r = wr; r < wr + 16; r++) {
+        const bool is_cur = has_cur && r == cur - i * kAttnTile;
+        if (r < rows && !is_cur) continue;
+        __half* kr = reinterpret_cast<__half*>(st + (size_t)r * Ly::kRow);
+        __half* vr = reinterpret_cast<__half*>(st + (size_t)(kAttnTile + r) * Ly::kRow);
+        for (int e = lane; e < HS; e += 32) {
+          kr[e] = is_cur ? __float2half_rn(skv[e]) : __float2half_rn(0.f);
+          vr[e] = is_cur ? __float2half_rn(skv[HS + e]) : __float2half_rn(0.f);
+        }
+      }
+      (void)last;
+      // generic writes into a stage that bulk copies also write
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      // scores of positions wr .. wr + 15: two n8 tiles
+      float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int s = 0; s < KS; s += 2) {
+        uint32_t b[2][4];
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+          const uint8_t* row = st + (size_t)(wr + 8 * j + (lane & 7)) * Ly::kRow + 2 * (16 * s + 8 * (lane >> 3));
+          ldsm_x4(row, b[j][0], b[j][1], b[j][2], b[j][3]);
+        }
+        uint32_t a0[4] = {qa[s][0], 0u, qa[s][1], 0u}, a1[4] = {qa[s + 1][0], 0u, qa[s + 1][1], 0u};
+        mma_16816(s0, a0, b[0][0], b[0][1]);
+        mma_16816(s0, a1, b[0][2], b[0][3]);
+        mma_16816(s1, a0, b[1][0], b[1][1]);
+        mma_16816(s1, a1, b[1][2], b[1][3]);
+      }
+      // positions of this lane's scores: wr + 2 t4 (+1) and wr + 8 + 2 t4 (+1)
+      const int q0 = wr + 2 * t4;
+      float v0 = q0 < rows ? s0[0] : -INFINITY, v1 = q0 + 1 < rows ? s0[1] : -INFINITY;
+      float v2 = q0 + 8 < rows ? s1[0] : -INFINITY, v3 = q0 + 9 < rows ? s1[1] : -INFINITY;
+      float mt = fmaxf(fmaxf(v0, v1), fmaxf(v2, v3));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+      const float m_new = fmaxf(m_run, mt);  // finite: the warp's first row is a position
+      const float alpha = expf(m_run - m_new);
+      const float e0 = expf(v0 - m_new), e1 = expf(v1 - m_new), e2 = expf(v2 - m_new), e3 = expf(v3 - m_new);
+      l_run = l_run * alpha + ((e0 + e1) + (e2 + e3));
+      m_run = m_new;
+#pragma unroll
+      for (int j = 0; j < NT; j++) {
+        o[j][0] *= alpha;
+        o[j][1] *= alpha;
+      }
+      const uint32_t pa[4] = {pack_h2(e0, e1), 0u, pack_h2(e2, e3), 0u};
+      // values: O[g][8 j + 2 t4 ..] += P V
+#pragma unroll
+      for (int j = 0; j < NT; j += 2) {
+        uint32_t b0, b1, b2, b3;
+        const uint8_t* row = st + (size_t)(kAttnTile + wr + (lane & 7) + 8 * ((lane >> 3) & 1)) * Ly::kRow +
+                             2 * (8 * (j + (lane >> 4)));
+        ldsm_x4_trans(row, b0, b1, b2, b3);
+        mma_16816(o[j], pa, b0, b1);
+        mma_16816(o[j + 1], pa, b2, b3);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+  }
+  // ---- the four warps' states (row g = q head g) merged in shared memory ------
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+  float* ws = wst + (size_t)warp * QG * (HS + 2);
+  if (g < QG) {
+#pragma unroll
+    for (int j = 0; j < NT; j++) {
+      ws[g * (HS + 2) + 8 * j + 2 * t4] = o[j][0];
+      ws[g * (HS + 2) + 8 * j + 2 * t4 + 1] = o[j][1];
+    }
+    if (t4 == 0) {
+      ws[g * (HS + 2) + HS] = m_run;
+      ws[g * (HS + 2) + HS + 1] = l_run;
+    }
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
+  float* cp = p.part + (size_t)h0 * p.nchunk * (HS + 2);
+  for (int idx = tid; idx < QG * (HS + 2); idx += NC) {
+    const int h = idx / (HS + 2), e = idx - h * (HS + 2);
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; w++) M = fmaxf(M, wst[(w * QG + h) * (HS + 2) + HS]);
+    float a = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; w++) {
+      const float mw = wst[(w * QG + h) * (HS + 2) + HS];
+      const float f = mw > -INFINITY ? expf(mw - M) : 0.f;
+      if (e < HS) a += wst[(w * QG + h) * (HS + 2) + e] * f;
+      else if (e == HS + 1) a += wst[(w * QG + h) * (HS + 2) + HS + 1] * f;
+    }
+    cp[((size_t)h * p.nchunk + c) * (HS + 2) + e] = e == HS ? M : a;
+  }
+  // ---- the last CTA of this kv head merges the chunks in chunk order ---------
+  __threadfence();
+  asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
+  if (tid == 0) flags[1] = atomicAdd(&cnt[kh], 1u) == (unsigned)(p.nchunk - 1);
+  asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
+  if (!flags[1]) return;
+  __threadfence();
+  const int nc = p.nchunk;
+  for (int idx = tid; idx < QG * HS; idx += NC) {
+    const int h = idx / HS, e = idx - h * HS;
+    const float* base = p.part + (size_t)(h0 + h) * nc * (HS + 2);
+    float M = -INFINITY;
+    for (int cc = 0; cc < nc; cc++) M = fmaxf(M, __ldcg(base + (size_t)cc * (HS + 2) + HS));
+    float a = 0.f, L = 0.f;
+#pragma unroll 4
+    for (int cc = 0; cc < nc; cc++) {
+      const float mc = __ldcg(base + (size_t)cc * (HS + 2) + HS);
+      const float f = mc > -INFINITY ? expf(mc - M) : 0.f;
+      a += __ldcg(base + (size_t)cc * (HS + 2) + e) * f;
+      L += __ldcg(base + (size_t)cc * (HS + 2) + HS + 1) * f;
+    }
+    out[(size_t)(h0 + h) * HS + e] = L > 0.f ? a * (1.0f / L) : 0.f;
+  }
+  if (tid == 0) cnt[kh] = 0u;
+}
+
 // RoPE frequencies (rope_neox, gguf_run.c:171): freq[j] = powf(base, -2j/hs)
 __global__ void dec_rope_freq(float* freq, int hs, float base) {
   const int j = threadIdx.x;
@@ -499,6 +845,31 @@ static const void* attn_kernel(int qg, int f16, int hs) {
   return nullptr;
 }
 
+// the tensor-core attention kernel (f16 cache) and its shared memory
+template <int HS>
+static const void* attn_mma_kernel_h(int qg, size_t* smem) {
+  switch (qg) {
+    case 1: *smem = attn_mma_smem<1, HS>(); return reinterpret_cast<const void*>(&dec_attn_mma<1, HS>);
+    case 2: *smem = attn_mma_smem<2, HS>(); return reinterpret_cast<const void*>(&dec_attn_mma<2, HS>);
+    case 4: *smem = attn_mma_smem<4, HS>(); return reinterpret_cast<const void*>(&dec_attn_mma<4, HS>);
+    case 8: *smem = attn_mma_smem<8, HS>(); return reinterpret_cast<const void*>(&dec_attn_mma<8, HS>);
+    default: return nullptr;
+  }
+}
+static const void* attn_mma_kernel(int qg, int hs, size_t* smem) {
+  if (hs == 64) return attn_mma_kernel_h<64>(qg, smem);
+  if (hs == 128) return attn_mma_kernel_h<128>(qg, smem);
+  return nullptr;
+}
+
+// positions per attention CTA: whole tiles, as few as keep about one CTA per
+// SM busy over the kv heads
+static int attn_mma_chunk(int npos, int nkv, int num_sms) {
+  const int tiles = (npos + kAttnTile - 1) / kAttnTile;
+  const int target = std::max(1, (num_sms + nkv - 1) / nkv);
+  return kAttnTile * ((tiles + target - 1) / target);
+}
+
 // Every kernel of the decode chain asks for the largest shared-memory
 // configuration, the one the mat-vec and MoE kernels need: an SM only holds
 // CTAs of kernels that agree on it, and a programmatic launch overlaps its
@@ -510,6 +881,15 @@ static int set_chain_carveout(int qg, int f16, int hs) {
     if (!fn) return VIREO_ERR_UNSUPPORTED;
     const int st = cuda_status(
         cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared));
+    if (st) return st;
+  }
+  if (f16) {
+    size_t smem = 0;
+    const void* fn = attn_mma_kernel(qg, hs, &smem);
+    if (!fn) return VIREO_ERR_UNSUPPORTED;
+    int st = cuda_status(
+        cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared));
+    if (!st) st = cuda_status(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     if (st) return st;
   }
   return VIREO_OK;
@@ -530,6 +910,7 @@ struct gguf_decoder {
   void *kc = nullptr, *vc = nullptr;
   size_t layer_kv = 0;  // elements of one layer's K (or V) cache
   int max_chunk = 0;
+  unsigned int* attn_cnt = nullptr;  // per kv head: attention CTAs finished (tensor-core path)
 };
 
 extern "C" {
@@ -537,7 +918,7 @@ extern "C" {
 void gguf_decoder_destroy(gguf_decoder* dec) {
   if (!dec) return;
   for (void* p : {(void*)dec->x, (void*)dec->xb, (void*)dec->y, (void*)dec->q, (void*)dec->att, (void*)dec->part,
-                  (void*)dec->logits, dec->kc, dec->vc, (void*)dec->freq})
+                  (void*)dec->logits, dec->kc, dec->vc, (void*)dec->freq, (void*)dec->attn_cnt})
     if (p) cudaFree(p);
   for (void* p : dec->wqkv)
     if (p) cudaFree(p);
@@ -580,7 +961,12 @@ int gguf_decoder_create(const gguf_decoder_desc* desc, const gguf_decoder_layer*
   dec->d = D;
   dec->L.assign(layers, layers + D.n_layers);
   dec->c = c;
-  dec->max_chunk = (D.max_ctx + kAttnChunk - 1) / kAttnChunk;
+  // chunks per head: the chunk-parallel kernel's, or the tensor-core one's,
+  // which is at most the tiles of the longest context and at most its CTA
+  // target per kv head (not monotone in the context length, so bounded by both)
+  dec->max_chunk = std::max((D.max_ctx + kAttnChunk - 1) / kAttnChunk,
+                            std::min((D.max_ctx + kAttnTile - 1) / kAttnTile,
+                                     std::max(1, (c->num_sms + D.n_kv_heads - 1) / D.n_kv_heads)));
   dec->layer_kv = (size_t)D.n_kv_heads * D.max_ctx * D.head_size;
   const size_t kvb = dec->layer_kv * D.n_layers * (D.kv_f16 ? 2 : 4);
   if ((st = cuda_status(cudaMalloc(&dec->x, (size_t)D.dim * 4))) ||
@@ -592,6 +978,8 @@ int gguf_decoder_create(const gguf_decoder_desc* desc, const gguf_decoder_layer*
       (st = cuda_status(cudaMalloc(&dec->part, (size_t)D.n_heads * dec->max_chunk * (D.head_size + 2) * 4))) ||
       (st = cuda_status(cudaMalloc(&dec->logits, (size_t)D.vocab * 4))) ||
       (st = cuda_status(cudaMalloc(&dec->kc, kvb))) || (st = cuda_status(cudaMalloc(&dec->vc, kvb))) ||
+      (st = cuda_status(cudaMalloc(&dec->attn_cnt, sizeof(unsigned int) * (size_t)D.n_kv_heads))) ||
+      (st = cuda_status(cudaMemset(dec->attn_cnt, 0, sizeof(unsigned int) * (size_t)D.n_kv_heads))) ||
       (st = cuda_status(cudaMemset(dec->x, 0, (size_t)D.dim * 4)))) {
     gguf_decoder_destroy(dec);
     return st;
@@ -690,10 +1078,34 @@ static int decoder_step(gguf_decoder* dec, int token, const int32_t* token_dev, 
     at.scale = 1.0f / sqrtf((float)hs);
     at.eps = D.eps;
     at.part = dec->part;
-    if ((st = launch_attn(at, D.n_heads / D.n_kv_heads, D.kv_f16, nchunk, D.n_kv_heads, s))) return st;
-    if ((st = launch_pdl(dec_attn_combine, dim3(D.n_heads), dim3(kCombThreads),
-                         (size_t)(nchunk + kCombThreads) * sizeof(float), s, at, dec->att)))
-      return st;
+    at.err = c->d_err;
+    if (D.kv_f16) {
+      // tensor-core attention; its last CTA per kv head merges the chunks
+      size_t smem = 0;
+      const void* fn = attn_mma_kernel(D.n_heads / D.n_kv_heads, hs, &smem);
+      const int C = attn_mma_chunk(npos, D.n_kv_heads, c->num_sms);
+      at.nchunk = (npos + C - 1) / C;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(at.nchunk, D.n_kv_heads);
+      cfg.blockDim = dim3(kAttnMmaThreads);
+      cfg.dynamicSmemBytes = smem;
+      cfg.stream = s;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int Cv = C;
+      float* outp = dec->att;
+      unsigned int* cntp = dec->attn_cnt;
+      void* args[] = {&at, &Cv, &outp, &cntp};
+      if ((st = cuda_status(cudaLaunchKernelExC(&cfg, fn, args)))) return st;
+    } else {
+      if ((st = launch_attn(at, D.n_heads / D.n_kv_heads, D.kv_f16, nchunk, D.n_kv_heads, s))) return st;
+      if ((st = launch_pdl(dec_attn_combine, dim3(D.n_heads), dim3(kCombThreads),
+                           (size_t)(nchunk + kCombThreads) * sizeof(float), s, at, dec->att)))
+        return st;
+    }
     st = gemv_dev_fast(c, y.wo_type, y.wo, dec->att, dec->y, nq, d, s, nullptr, 0.f, kDecPrefetch);
     if (st == VIREO_ERR_UNSUPPORTED) st = gemv_dev(c, y.wo_type, y.wo, dec->att, dec->y, nq, d, s);
     if (st) return st;

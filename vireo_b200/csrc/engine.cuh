@@ -1,13 +1,15 @@
 // Streaming dequant-GEMV engine shared by the decode kernels.
 //
-// Work is cut into units of 16 weight rows x full K.  A producer warp moves
-// each unit's raw GGUF rows from HBM into a ring of shared-memory stages
-// with 1-D bulk copies (TMA engine, mbarrier completion); W consumer warps
-// split each unit's K into 256-value segments, round-robin over the whole
-// (unit, segment) sequence, and run the tensor-core segment kernels below.
-// Each warp leaves one 16-row partial per unit in shared memory; the last
-// warp to finish a unit sums the W partials in warp order (deterministic)
-// and runs the caller's epilogue.
+// Work is cut into tiles of 16 weight rows x full K.  One producer warp moves
+// the raw GGUF rows of each item (one or more tiles) from HBM into a ring of
+// shared-memory stages with 1-D bulk copies (cp.async.bulk: one instruction
+// per row or per group of rows, executed by the TMA engine, completing on the
+// stage's mbarrier; never multicast).  The consumer warps split each tile's K
+// into 256-value segments and run the tensor-core segment kernels below on
+// (tile, segment) pairs dealt round-robin over the warps; each pair leaves a
+// 16-row partial in shared memory and the warp that completes a tile's last
+// segment sums the partials in segment order (so the result does not depend
+// on which warp computed what) and runs the caller's epilogue.
 //
 // Stage layout: rows 0..7 ("half 0") and 8..15 ("half 1") may come from
 // different matrices (gate and up rows of one expert).  Rows are copied
@@ -39,30 +41,19 @@ VDEV const uint8_t* stage_row(const uint8_t* stage, const StageGeom& sg, int r) 
   return stage + h * sg.hstride + (r8 / (int)sg.G) * sg.gstride + (r8 % (int)sg.G) * sg.rb;
 }
 
-// Producer side: nprod threads (ptid = 0..nprod-1) copy a unit into a stage
-// in 16-byte pieces and each arrives on the stage's full barrier (expected
-// count nprod) once its pieces have landed.  A null src0 issues nothing
-// (the unit is skipped) but still arrives.
-// Each half (8 rows, contiguous in global memory) is walked as one flat
-// byte range so that consecutive lanes copy consecutive 16-byte pieces; the
-// destination of a piece is its copy group's padded slot, found with a
-// multiply-shift division.
-VDEV void issue_unit(uint8_t* stage, uint64_t* full, const uint8_t* src0, const uint8_t* src1,
-                     const StageGeom& sg, int ptid, int nprod) {
-  if (src0) {
-    const uint32_t gbytes = sg.G * sg.rb;  // bytes per copy group (multiple of 16)
-    const uint32_t hbytes = 8u * sg.rb;
-#pragma unroll 1
-    for (uint32_t h = 0; h < 2; h++) {
-      const uint8_t* hs = h ? src1 : src0;
-      uint8_t* hd = stage + h * sg.hstride;
-      for (uint32_t b = 16u * (uint32_t)ptid; b < hbytes; b += 16u * (uint32_t)nprod) {
-        const uint32_t j = __umulhi(b, sg.gmagic);
-        cp_async16(hd + j * sg.gstride + (b - j * gbytes), hs + b);
-      }
-    }
+// Producer side: one tile (16 rows) of bulk copies, issued by lanes
+// 0 .. 2 (8 / G) - 1 of the calling warp (one copy per row or row group).
+// The caller has already announced the item's bytes on `full` with
+// mbar_arrive_expect_tx (16 rb per tile); each copy completes its bytes on
+// it.  Source and destination addresses and sizes are multiples of 16.
+VDEV void issue_tile_bulk(uint8_t* stage, uint64_t* full, const uint8_t* src0, const uint8_t* src1,
+                          const StageGeom& sg, int lane) {
+  const int groups = 8 / (int)sg.G;
+  if (lane < 2 * groups) {
+    const int h = lane >= groups ? 1 : 0, j = lane - h * groups;
+    const uint32_t gbytes = sg.G * sg.rb;
+    bulk_g2s(stage + h * sg.hstride + j * sg.gstride, (h ? src1 : src0) + (size_t)j * gbytes, gbytes, full);
   }
-  cp_async_arrive(full);
 }
 
 struct LaneCtx {
@@ -176,6 +167,59 @@ struct SegQ8 : Q8 {
   }
 };
 
+// The u8 values v .. v+3 (v a multiple of 4) of a Q5_0 block from its qs
+// words and qh: low or high nibbles, bit v + i of qh as bit 4 of byte i (the
+// multiply spreads four bits to bytes 0..3 without carries).
+VDEV uint32_t q5_four(const uint32_t (&qs)[4], uint32_t qh, int v) {
+  const uint32_t nib = (qs[(v & 15) >> 2] >> (v >= 16 ? 4 : 0)) & 0x0F0F0F0Fu;
+  const uint32_t hb = ((((qh >> v) & 0xFu) * 0x00204081u) & 0x01010101u) << 4;
+  return nib | hb;
+}
+
+struct SegQ5 : Q5 {
+  VDEV static void run(const uint8_t* r0, const uint8_t* r1, const BFrag& B, const float* meta, const LaneCtx& L,
+                       float& tot0, float& tot1) {
+    const uint8_t* p0 = r0 + 44 * L.t;
+    const uint8_t* p1 = r1 + 44 * L.t;
+    uint32_t wa[11], wb[11];
+#pragma unroll
+    for (int i = 0; i < 11; i++) {
+      wa[i] = lds32(p0 + 4 * i);
+      wb[i] = lds32(p1 + 4 * i);
+    }
+    const uint32_t qha = __funnelshift_r(wa[0], wa[1], 16), qhb = __funnelshift_r(wb[0], wb[1], 16);
+    const uint32_t sa[4] = {__funnelshift_r(wa[1], wa[2], 16), __funnelshift_r(wa[2], wa[3], 16),
+                            __funnelshift_r(wa[3], wa[4], 16), __funnelshift_r(wa[4], wa[5], 16)};
+    const uint32_t sb[4] = {__funnelshift_r(wb[1], wb[2], 16), __funnelshift_r(wb[2], wb[3], 16),
+                            __funnelshift_r(wb[3], wb[4], 16), __funnelshift_r(wb[4], wb[5], 16)};
+    const uint32_t ta[4] = {wa[7], wa[8], wa[9], wa[10]}, tb[4] = {wb[7], wb[8], wb[9], wb[10]};
+    int ca[4], cb[4];
+#pragma unroll
+    for (int m = 0; m < 4; m++) {
+      uint32_t a[4], e[4];
+      a[0] = q5_four(sa, qha, 8 * m);
+      a[1] = q5_four(sb, qhb, 8 * m);
+      a[2] = q5_four(sa, qha, 8 * m + 4);
+      a[3] = q5_four(sb, qhb, 8 * m + 4);
+      e[0] = q5_four(ta, wa[6], 8 * m);
+      e[1] = q5_four(tb, wb[6], 8 * m);
+      e[2] = q5_four(ta, wa[6], 8 * m + 4);
+      e[3] = q5_four(tb, wb[6], 8 * m + 4);
+      if (m == 0) {
+        imma_u8_z(ca, a, B.b[0][0], B.b[0][1]);
+        imma_u8_z(cb, e, B.b[4][0], B.b[4][1]);
+      } else {
+        imma_u8(ca, a, B.b[m][0], B.b[m][1]);
+        imma_u8(cb, e, B.b[4 + m][0], B.b[4 + m][1]);
+      }
+    }
+    const int ga = 2 * L.t, gb = 2 * L.t + 1;
+    const float sA = meta[ga], sB = meta[gb], SA = 16.f * meta[8 + ga], SB = 16.f * meta[8 + gb];
+    tot0 += h_lo(wa[0]) * (sA * dig(ca[0], ca[1]) - SA) + h_hi(wa[5]) * (sB * dig(cb[0], cb[1]) - SB);
+    tot1 += h_lo(wb[0]) * (sA * dig(ca[2], ca[3]) - SA) + h_hi(wb[5]) * (sB * dig(cb[2], cb[3]) - SB);
+  }
+};
+
 struct SegQ4K : Q4K {
   VDEV static void run(const uint8_t* r0, const uint8_t* r1, const BFrag& B, const float* meta, const LaneCtx& L,
                        float& tot0, float& tot1) {
@@ -255,23 +299,124 @@ struct SegQ6K : Q6K {
 };
 
 // ---------------------------------------------------------------------------
-// B tables of 256-value segments, one warp per segment.  Segment i of the
-// source is the fp32 values src[256 i, 256 i + 256).  Its table is the first
-// 512 bytes of dst + kSegTabBytes i: step m, thread t, digit c at byte
-// 64 m + 16 t + 8 c: the digits of elements F::elem(m, t, r, j) for r = 0, 1
-// and j = 0..3.  Its metadata meta[kMeta i ..] holds, per natural 32-value
-// group q, the scale s_q = max|x| / 127 and the sum of x~ = s (d1 + d2/254),
-// and the same sums per 16-value group.  A group holding inf or NaN gets a
-// NaN scale, so that its dot products come out NaN as the reference's do.
-// Every read of a segment precedes every write to it (warp-synchronous), so
-// dst may alias src (the same 1 KB footprint per segment).
+// Activation tables.  Segment i of a vector is its values [256 i, 256 i +
+// 256).  Its B table is the first 512 bytes of tab + kSegTabBytes i: step m,
+// thread t, digit c at byte 64 m + 16 t + 8 c: the digits of elements
+// F::elem(m, t, r, j) for r = 0, 1 and j = 0..3.  Its metadata meta[kMeta i
+// ..] holds, per natural 32-value group q, the scale s_q = max|x| / 127 and
+// the sum of x~ = s (d1 + d2/254), the same sums per 16-value group, and at
+// kMetaFlag whether the segment has a residual table.
+//
+// Residual tables: the two digits leave an error of up to max|x| / 64516 on
+// every value of a group, which is small against the group's own values
+// unless one value dwarfs the others (an outlier channel).  A segment in
+// which some group's largest magnitude exceeds kResRatio times the group's
+// root mean square gets a second table of the same form for the remainder
+// r = x - x~ (rtab + kResTabBytes i, rmeta + kMeta i); the consumers add the
+// products with it, so every value of such a segment is carried to about
+// max|x| / 64516^2.  The dot products are linear in the activations, so the
+// segment kernels run unchanged on the second table.
+//
+// A group holding inf or NaN gets a NaN scale (and no residual table), so
+// that its dot products come out NaN as the reference's do.  Every read of a
+// segment's source precedes every write to its table (warp-synchronous), so
+// the source may alias tab (the same 1 KB footprint per segment).
 // ---------------------------------------------------------------------------
+constexpr int kResTabBytes = 512;
+constexpr float kResRatio = 8.0f;
+
+struct VecTab {
+  uint8_t* tab;   // [nseg][kSegTabBytes]
+  float* meta;    // [nseg][kMeta]
+  uint8_t* rtab;  // [nseg][kResTabBytes]
+  float* rmeta;   // [nseg][kMeta]
+};
+
+// Two int8 digits of 8 values under scale 1 / inv (inv = 0: all zero):
+// packed natural-order bytes of digit 1 (lo1 | hi1) and digit 2, and their
+// sums over the 8 values.
+VDEV void digits8(const float (&x)[8], float inv, uint32_t& lo1, uint32_t& hi1, uint32_t& lo2, uint32_t& hi2,
+                  int& s1, int& s2, float (&used)[8]) {
+  lo1 = hi1 = lo2 = hi2 = 0;
+  s1 = s2 = 0;
+#pragma unroll
+  for (int q = 0; q < 8; q++) {
+    const float y = x[q] * inv;
+    const float r1 = fminf(fmaxf(rintf(y), -127.f), 127.f);
+    const float r2 = fminf(fmaxf(rintf((y - r1) * 254.f), -127.f), 127.f);
+    const int i1 = (int)r1, i2 = (int)r2;
+    used[q] = r1 + r2 * kInv254;
+    s1 += i1;
+    s2 += i2;
+    const uint32_t b1 = (uint32_t)(i1 & 0xFF), b2 = (uint32_t)(i2 & 0xFF);
+    if (q < 4) {
+      lo1 |= b1 << (8 * q);
+      lo2 |= b2 << (8 * q);
+    } else {
+      hi1 |= b1 << (8 * (q - 4));
+      hi2 |= b2 << (8 * (q - 4));
+    }
+  }
+}
+
+// Natural-order digits (8 bytes per lane per digit) through the scratch half
+// of tab into the step layout, written to out (512 bytes).  Warp-collective.
 template <class F>
-VDEV void build_tables(const float* src, uint8_t* dst, float* meta, int nseg, int warp, int nwarps, int lane) {
+VDEV void digits_to_table(uint8_t* tab, uint8_t* out, int lane, uint32_t lo1, uint32_t hi1, uint32_t lo2,
+                          uint32_t hi2) {
+  __syncwarp();
+  *reinterpret_cast<uint2*>(tab + 512 + 8 * lane) = make_uint2(lo1, hi1);
+  *reinterpret_cast<uint2*>(tab + 768 + 8 * lane) = make_uint2(lo2, hi2);
+  __syncwarp();
+  // table chunks ch = lane, lane + 32: step m = ch >> 3, thread t = (ch >> 1) & 3, digit c = ch & 1
+  uint2 o[2];
+#pragma unroll
+  for (int hh = 0; hh < 2; hh++) {
+    const int ch = lane + 32 * hh, m = ch >> 3, t = (ch >> 1) & 3, c = ch & 1;
+    const uint8_t* nat = tab + 512 + 256 * c;
+    uint32_t w[2];
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+      uint32_t acc = 0;
+#pragma unroll
+      for (int j = 0; j < 4; j++) acc |= (uint32_t)nat[F::elem(m, t, r, j)] << (8 * j);
+      w[r] = acc;
+    }
+    o[hh] = make_uint2(w[0], w[1]);
+  }
+  __syncwarp();
+  reinterpret_cast<uint2*>(out)[lane] = o[0];
+  reinterpret_cast<uint2*>(out)[lane + 32] = o[1];
+  __syncwarp();
+}
+
+// Per-group scale and metadata sums of one digit pair: lane l holds 8 values
+// of 32-group l / 4; meta gets s, the 32-group sum and the 16-group sum.
+VDEV void group_meta(float* meta, int lane, float sc, int s1, int s2) {
+  s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+  s2 += __shfl_xor_sync(0xffffffffu, s2, 1);
+  const float sum16 = sc * ((float)s1 + (float)s2 * kInv254);
+  const int t1 = s1 + __shfl_xor_sync(0xffffffffu, s1, 2), t2 = s2 + __shfl_xor_sync(0xffffffffu, s2, 2);
+  const float sum32 = sc * ((float)t1 + (float)t2 * kInv254);
+  if ((lane & 3) == 0) {
+    meta[lane / 4] = sc;
+    meta[8 + lane / 4] = sum32;
+  }
+  if ((lane & 1) == 0) meta[16 + lane / 2] = sum16;
+}
+
+VDEV float quad_max(float v) {
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+  return fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+}
+
+template <class F>
+VDEV void build_tables(const float* src, const VecTab& T, int nseg, int warp, int nwarps, int lane) {
 #pragma unroll 1
   for (int i = warp; i < nseg; i += nwarps) {
     const float* v = src + (size_t)i * kSegElems;
-    uint8_t* tab = dst + (size_t)i * kSegTabBytes;
+    uint8_t* tab = T.tab + (size_t)i * kSegTabBytes;
+    float* meta = T.meta + (size_t)i * kMeta;
     // lane l holds the natural values [8 l, 8 l + 8): 32-group l / 4
     const float4 a4 = *reinterpret_cast<const float4*>(v + 8 * lane);
     const float4 b4 = *reinterpret_cast<const float4*>(v + 8 * lane + 4);
@@ -283,81 +428,69 @@ VDEV void build_tables(const float* src, uint8_t* dst, float* meta, int nseg, in
       mx = fmaxf(mx, fabsf(x[q]));
       bad |= !(fabsf(x[q]) <= 3.402823466e38f);
     }
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    mx = quad_max(mx);
     bad = __shfl_xor_sync(0xffffffffu, (int)bad, 1) | __shfl_xor_sync(0xffffffffu, (int)bad, 2) | bad;
     const float sc = bad ? __int_as_float(0x7fc00000) : mx * (1.0f / 127.0f);
     const float inv = (mx > 0.f && !bad) ? 127.0f / mx : 0.f;
-    uint32_t lo1 = 0, hi1 = 0, lo2 = 0, hi2 = 0;
-    int s1 = 0, s2 = 0;
+    // sum of squares of the scaled values (|x inv| <= 127, no overflow)
+    float ss = 0.f;
 #pragma unroll
-    for (int q = 0; q < 8; q++) {
-      const float y = x[q] * inv;
-      const float r1 = fminf(fmaxf(rintf(y), -127.f), 127.f);
-      const float r2 = fminf(fmaxf(rintf((y - r1) * 254.f), -127.f), 127.f);
-      const int i1 = (int)r1, i2 = (int)r2;
-      s1 += i1;
-      s2 += i2;
-      const uint32_t b1 = (uint32_t)(i1 & 0xFF), b2 = (uint32_t)(i2 & 0xFF);
-      if (q < 4) {
-        lo1 |= b1 << (8 * q);
-        lo2 |= b2 << (8 * q);
-      } else {
-        hi1 |= b1 << (8 * (q - 4));
-        hi2 |= b2 << (8 * (q - 4));
-      }
+    for (int q = 0; q < 8; q++) ss = fmaf(x[q] * inv, x[q] * inv, ss);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+    uint32_t lo1, hi1, lo2, hi2;
+    int s1, s2;
+    float used[8];
+    digits8(x, inv, lo1, hi1, lo2, hi2, s1, s2, used);
+    // an outlier group: max^2 > ratio^2 * mean square (finite groups only);
+    // in scaled units the max is 127
+    const bool want = !bad && mx > 0.f && 127.f * 127.f > kResRatio * kResRatio * (ss * (1.0f / 32.0f));
+    const bool flagged = __any_sync(0xffffffffu, want);
+    group_meta(meta, lane, sc, s1, s2);
+    digits_to_table<F>(tab, tab, lane, lo1, hi1, lo2, hi2);
+    if (flagged) {
+      float r[8];
+#pragma unroll
+      for (int q = 0; q < 8; q++) r[q] = bad ? 0.f : x[q] - sc * used[q];
+      float mr = 0.f;
+#pragma unroll
+      for (int q = 0; q < 8; q++) mr = fmaxf(mr, fabsf(r[q]));
+      mr = quad_max(mr);
+      const float scr = mr * (1.0f / 127.0f), invr = mr > 0.f ? 127.0f / mr : 0.f;
+      digits8(r, invr, lo1, hi1, lo2, hi2, s1, s2, used);
+      group_meta(T.rmeta + (size_t)i * kMeta, lane, scr, s1, s2);
+      digits_to_table<F>(tab, T.rtab + (size_t)i * kResTabBytes, lane, lo1, hi1, lo2, hi2);
     }
-    // sums of x~ per 16-group (lane pairs) and per 32-group (lane quads)
-    s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
-    s2 += __shfl_xor_sync(0xffffffffu, s2, 1);
-    const float sum16 = sc * ((float)s1 + (float)s2 * kInv254);
-    const int t1 = s1 + __shfl_xor_sync(0xffffffffu, s1, 2), t2 = s2 + __shfl_xor_sync(0xffffffffu, s2, 2);
-    const float sum32 = sc * ((float)t1 + (float)t2 * kInv254);
-    __syncwarp();  // every lane holds its values: the segment may be overwritten
-    // natural-order digits in the scratch half: d1 at +512, d2 at +768
-    *reinterpret_cast<uint2*>(tab + 512 + 8 * lane) = make_uint2(lo1, hi1);
-    *reinterpret_cast<uint2*>(tab + 768 + 8 * lane) = make_uint2(lo2, hi2);
-    if ((lane & 3) == 0) {
-      meta[(size_t)i * kMeta + lane / 4] = sc;
-      meta[(size_t)i * kMeta + 8 + lane / 4] = sum32;
-    }
-    if ((lane & 1) == 0) meta[(size_t)i * kMeta + 16 + lane / 2] = sum16;
-    __syncwarp();
-    // table chunks ch = lane, lane + 32: step m = ch >> 3, thread t = (ch >> 1) & 3, digit c = ch & 1
-    uint2 out[2];
-#pragma unroll
-    for (int hh = 0; hh < 2; hh++) {
-      const int ch = lane + 32 * hh, m = ch >> 3, t = (ch >> 1) & 3, c = ch & 1;
-      const uint8_t* nat = tab + 512 + 256 * c;
-      uint32_t w[2];
-#pragma unroll
-      for (int r = 0; r < 2; r++) {
-        uint32_t acc = 0;
-#pragma unroll
-        for (int j = 0; j < 4; j++) acc |= (uint32_t)nat[F::elem(m, t, r, j)] << (8 * j);
-        w[r] = acc;
-      }
-      out[hh] = make_uint2(w[0], w[1]);
-    }
-    __syncwarp();
-    reinterpret_cast<uint2*>(tab)[lane] = out[0];
-    reinterpret_cast<uint2*>(tab)[lane + 32] = out[1];
-    __syncwarp();
+    if (lane == 0) meta[kMetaFlag] = flagged ? 1.f : 0.f;
+  }
+}
+
+// One segment of rows g (r0) and g + 8 (r1) of a tile against a vector's
+// tables, both passes (main table, and the residual table when the segment
+// has one), accumulated into this lane's totals.
+template <class SF>
+VDEV void seg_dot(const uint8_t* r0, const uint8_t* r1, int seg, const VecTab& T, const LaneCtx& L, BFrag& bf,
+                  float& tot0, float& tot1) {
+  const int passes = T.meta[(size_t)seg * kMeta + kMetaFlag] != 0.f ? 2 : 1;
+#pragma unroll 1
+  for (int ps = 0; ps < passes; ps++) {
+    bf.get(ps ? T.rtab + (size_t)seg * kResTabBytes : T.tab + (size_t)seg * kSegTabBytes, L);
+    SF::run(r0 + seg * SF::kSegBytes, r1 + seg * SF::kSegBytes, bf, (ps ? T.rmeta : T.meta) + (size_t)seg * kMeta,
+            L, tot0, tot1);
   }
 }
 
 // ---------------------------------------------------------------------------
-// Consumer side of one unit for warp w: run this warp's segments, reduce each
+// Consumer side of one tile for warp w: run this warp's segments, reduce each
 // over the 4 lanes of a row, publish one 16-row partial per segment, and
-// return true in the warp that completes the unit, which sums the segment
+// return true in the warp that completes the tile, which sums the segment
 // partials in segment order (so the result does not depend on which warp
 // computed which segment) into *row_val (lanes 0..15).
 // part: [max(nseg, W)][16] floats for this stage.
 // ---------------------------------------------------------------------------
 template <class S>
-VDEV bool consume_unit(const uint8_t* stage, const StageGeom& sg, int v, int nseg, int W, int w,
-                       const uint8_t* btab, const float* meta, float* part, int* ucnt, const LaneCtx& L,
-                       float* row_val, BFrag& bf) {
+VDEV bool consume_unit(const uint8_t* stage, const StageGeom& sg, int v, int nseg, int W, int w, const VecTab& T,
+                       float* part, int* ucnt, const LaneCtx& L, float* row_val, BFrag& bf) {
   const uint8_t* r0 = stage_row(stage, sg, L.g);
   const uint8_t* r1 = stage_row(stage, sg, L.g + 8);
   int first = (w - (v * nseg) % W) % W;
@@ -365,8 +498,7 @@ VDEV bool consume_unit(const uint8_t* stage, const StageGeom& sg, int v, int nse
 #pragma unroll 1
   for (int seg = first; seg < nseg; seg += W) {
     float tot0 = 0.f, tot1 = 0.f;
-    bf.get(btab + seg * kSegTabBytes, L);
-    S::run(r0 + seg * S::kSegBytes, r1 + seg * S::kSegBytes, bf, meta + seg * kMeta, L, tot0, tot1);
+    seg_dot<S>(r0, r1, seg, T, L, bf, tot0, tot1);
     tot0 += __shfl_xor_sync(0xffffffffu, tot0, 1);
     tot1 += __shfl_xor_sync(0xffffffffu, tot1, 1);
     tot0 += __shfl_xor_sync(0xffffffffu, tot0, 2);

@@ -8,23 +8,21 @@
 //
 // One CTA per SM, every CTA resident (each cross-CTA wait is bounded).
 //   R  router partial dot products, 512-value K chunks, one warp per task
-//      -> grid arrival counter -> every CTA: one warp sums the partials in
-//      chunk order, takes the softmax and ranks the top-k.
+//      -> grid arrival counter -> every CTA: one warp per 32 experts sums the
+//      partials in chunk order, takes the softmax and ranks the top-k.
 //   The CTAs are then split into k groups, group t serving the expert of
-//   rank t; a CTA of group t streams its share of that expert's gate/up
-//   rows and then its share of the expert's down rows (16-row tiles), all
-//   into one shared-memory ring, so the down rows arrive while gate/up is
-//   still computed.
-//   G  units of 8 gate + 8 up rows, one warp per unit: h = silu(g) * u into
-//      the expert's h row in scratch; the group counts finished units.
-//   D  once the group's units are all counted, the CTA stages the expert's h,
-//      builds its activation tables and runs its down tiles, one warp per
-//      tile; each tile's 16 outputs go to scratch, and the last of the k
-//      groups to finish a tile combines the k experts' rows in rank order
-//      and adds them into the residual.
-// The weight stages form two rings over one shared-memory area: gate/up
-// units in stages sized for them, down tiles in (usually smaller) slots of
-// their own.
+//   rank t.  A CTA of group t streams, through one ring of shared-memory
+//   stages, its share of that expert's gate/up units (8 gate + 8 up rows)
+//   and then its share of the expert's down tiles (16 rows; several per
+//   stage), so the down rows arrive while gate/up is still computed.
+//   G  (unit, segment) pairs dealt over the consumer warps; the warp that
+//      completes a unit writes h = silu(g) * u for its 8 rows to scratch;
+//      the group counts finished units.
+//   D  once the group's units are all counted, the CTA stages the expert's h
+//      and builds its activation tables; (tile, segment) pairs are dealt
+//      likewise, the warp completing a tile writes its 16 outputs to scratch,
+//      and the last of the k groups to finish a tile combines the k experts'
+//      rows in rank order and adds them into the residual.
 #pragma once
 #include <stdint.h>
 
@@ -32,10 +30,10 @@
 
 namespace vireo {
 
-constexpr int kConsumerWarps = 12;
-constexpr int kProducerWarps = 4;  // issue the 16-byte cp.async weight copies
-constexpr int kProducerThreads = 32 * kProducerWarps;
+constexpr int kConsumerWarps = 15;
+constexpr int kProducerWarps = 1;  // issues the bulk weight copies
 constexpr int kDecodeThreads = 32 * (kConsumerWarps + kProducerWarps);
+constexpr int kMaxDTiles = 4;      // down tiles per ring stage
 constexpr int kRouterChunk = 512;
 constexpr int kMaxTopK = 64;
 constexpr int kMaxExperts = 256;
@@ -76,12 +74,14 @@ struct MoeDecodeParams {
   float* wts_out;                    // [k] or null
   MoeScratch s;
   StageGeom sg_gu, sg_d;
-  uint32_t stage_bytes;  // gate/up ring: nstages stages of stage_bytes
+  uint32_t stage_bytes;  // ring stage: one gate/up unit or dtiles down tiles
   int nstages;
-  uint32_t dslot_bytes;  // down ring: nstages_d slots of dslot_bytes over the same memory
-  int nstages_d;
+  uint32_t dslot_bytes;  // one down tile inside a stage
+  int dtiles;            // down tiles per stage
+  int maxp;              // (tile, segment) pairs of one stage at most
   // shared-memory offsets (bytes)
-  uint32_t off_ctl, off_etab, off_part, off_xtab, off_xsx, off_htab, off_hsx, off_xs, off_stg, off_stage;
+  uint32_t off_ctl, off_etab, off_ucnt, off_part, off_xtab, off_xmeta, off_xrtab, off_xrmeta, off_htab, off_hmeta,
+      off_hrtab, off_hrmeta, off_xs, off_stage;
   unsigned long long* trace;  // optional: kTraceSlots %globaltimer stamps per CTA
 };
 
@@ -103,9 +103,8 @@ struct MoeRoute {
 // phase trace slots (per CTA): consumer thread 0 and producer thread 0
 enum TraceSlot {
   kTrStart = 0, kTrRouterDone, kTrPartials, kTrRouted, kTrGDone, kTrGAll, kTrHtab, kTrDDone,
-  kTrProdFirst, kTrProdFirstD, kTrProdLast, kTrProdDrained,
-  kTrUnitBase = 16,  // warp 0's first kTrUnits units: (ready, done)
-  kTrUnits = 24, kTrDbg = 64, kTraceSlots = 72
+  kTrProdFirst, kTrProdFirstD, kTrProdLast, kTrProdDrained, kTrPdl,
+  kTrDbg = 64, kTraceSlots = 72
 };
 
 struct GemvParams {
@@ -116,7 +115,7 @@ struct GemvParams {
   StageGeom sg;
   uint32_t stage_bytes;
   int nstages;
-  uint32_t off_part, off_ucnt, off_ctl, off_xtab, off_xsx, off_stg, off_stage;
+  uint32_t off_part, off_ucnt, off_ctl, off_xtab, off_xmeta, off_xrtab, off_xrmeta, off_stage;
   uint32_t part_stride;
   int* err;
   // optional, zero by default: y = W . rmsnorm(x, norm_w, eps) (the norm

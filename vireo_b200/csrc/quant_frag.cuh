@@ -42,9 +42,11 @@ constexpr int kSegElems = 256;   // every fast-path format works in 256-value se
 constexpr int kSegSteps = 8;     // k32 tensor-core steps per segment
 constexpr int kStepBytesB = 64;  // B table bytes per step: [t][digit][2 regs x 4 x int8]
 constexpr int kSegTabBytes = 1024;  // B table stride per segment (512 used, 512 build scratch)
-constexpr int kMeta = 32;        // floats of per-segment activation metadata:
+constexpr int kMeta = 36;        // floats of per-segment activation metadata:
                                  // [0,8) scale of each 32-group, [8,16) sum of x~ per
-                                 // 32-group, [16,32) sum of x~ per 16-group
+                                 // 32-group, [16,32) sum of x~ per 16-group, [32] residual
+                                 // table flag, [33,36) padding
+constexpr int kMetaFlag = 32;
 
 // ---- portable bit helpers (host versions for the self-test) --------------
 // 3-input bitwise function with lookup table lut (a, b, c <-> 0xF0, 0xCC, 0xAA)
@@ -96,6 +98,21 @@ struct Q8 {
     if (m < 3 || r == 0) return base + 4 * (1 + 2 * m + r) - 2 + j;
     return base + (j < 2 ? j : 28 + j);
   }
+};
+
+// ---- Q5_0: 22-byte blocks (f16 d, 4 bytes qh, 16 bytes qs), segment = 8
+// blocks.  Value j of a block (reference dequant_row_q5_0, gguf_compute.c:
+// 68-82): q = (j < 16 ? qs[j] & 15 : qs[j - 16] >> 4) | (bit j of qh) << 4,
+// value = d (q - 16).  Thread t owns the block pair (2t, 2t+1) = bytes [44t,
+// 44t + 44) of the segment, 11 aligned words: W0 = [dA dA qhA qhA], W1 =
+// [qhA qhA qs0 qs1], .., W5 = [qs14 qs15 dB dB], W6 = qhB, W7..W10 = block
+// B's qs.  Steps 0..3 cover block 2t (values 8 m + 4 r + j), steps 4..7
+// block 2t+1.  The u8 q values are the A operand; the 16 is removed with the
+// 32-group sum of x.
+struct Q5 {
+  static constexpr uint32_t kType = T_Q5_0;
+  static constexpr int kSegBytes = 176;
+  VHD static int elem(int m, int t, int r, int j) { return 64 * t + 8 * m + 4 * r + j; }
 };
 
 // ---- Q4_K: 144-byte super-blocks, segment = 1 super-block ---------------

@@ -5,6 +5,7 @@
 // records VIREO_ERR_TIMEOUT in a device status word and returns false so
 // the kernel can drain its copies and exit instead of hanging the GPU.
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -114,6 +115,29 @@ VDEV void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t
       "{%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// ---- shared-memory matrix loads for the f16 MMA operands -----------------
+// Four 8x8 b16 matrices: lane l supplies the address of row l % 8 of matrix
+// l / 8 (16 bytes, 16-byte aligned); register i receives matrix i in the MMA
+// fragment layout (lane 4 g + t: row g, columns 2t, 2t + 1), or, with
+// .trans, the transposed matrix.
+VDEV void ldsm_x4(const void* row, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_addr(row))
+               : "memory");
+}
+VDEV void ldsm_x4_trans(const void* row, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_addr(row))
+               : "memory");
+}
+// two floats as one f16x2 register (lo = a), round to nearest
+VDEV uint32_t pack_h2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
 }
 
 // ---- integer tensor core: D = A(16x32 int8) * B(32x8 s8) (+ C), s32 ------
