@@ -58,6 +58,7 @@ def qwen3_geometry_spec():
 # (spec, seed, steps, min_gap) of every reference comparison below
 MARGIN_CASES = [
     (qwen3_geometry_spec, 101, 320, 1e-4),
+    (qwen3_geometry_spec, 171, 136, 5e-4),
     (S.tiny_olmoe_decoder, 31, 12, 1e-4),
     (S.tiny_qwen3_decoder, 32, 12, 1e-4),
     (long_f16_spec, 41, 260, 5e-4),
@@ -165,6 +166,16 @@ def test_decoder_qwen3_geometry_long_lm_head():
     reference's forward()."""
     worst = run_case(qwen3_geometry_spec(), 101, kv_f16=False, steps=320, check_from=312)
     assert worst < 2e-3, worst
+
+
+@gpu
+def test_decoder_qwen3_geometry_f16_cache():
+    """The same geometry on the f16 KV cache (the tensor-core attention
+    kernel: 8 q heads per kv head as the MMA rows, 136 positions over three
+    tiles of 64): logits of the last 8 positions against the reference's
+    forward() at the f16 cache's tolerance."""
+    worst = run_case(qwen3_geometry_spec(), 171, kv_f16=True, steps=136, check_from=128, min_gap=5e-4)
+    assert worst < 1e-2, worst
 
 
 @gpu

@@ -10,12 +10,16 @@
 
 namespace vireo {
 
+constexpr int kTrItems = 16;  // items with per-item trace stamps
+
 struct Ctl {
   int abort;
   float wsum;  // renorm denominator
   int ids[kMaxTopK];
   float wts[kMaxTopK];
   float nred[kConsumerWarps];  // gemv_kernel: per-warp sums of squares for the fused norm
+  // trace only: first full-wait return and last empty arrival of the first items
+  unsigned long long it_land[kTrItems], it_done[kTrItems];
 };
 
 VDEV void trace(const MoeDecodeParams& p, int slot) {
@@ -280,6 +284,11 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
     mbar_fence_init();
   }
   for (int i = threadIdx.x; i < S * kMaxDTiles; i += blockDim.x) ucnt[i] = 0;
+  if (p.trace)
+    for (int i = threadIdx.x; i < kTrItems; i += blockDim.x) {
+      ctl->it_land[i] = ~0ull;
+      ctl->it_done[i] = 0ull;
+    }
   // expert slice table (weights metadata: not written by the previous kernel)
   if constexpr (!ROUTED)
     for (int i = threadIdx.x; i < 3 * ne; i += blockDim.x) etab[i] = p.exp_tab[i];
@@ -391,7 +400,6 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
   const int nG = active ? u1 - u0 : 0, nD = i1 - i0;  // an unused slot still counts its tiles
   const int nDI = active ? (nD + P - 1) / P : 0;    // down items (up to P tiles per stage)
   const int nItems = nG + nDI;
-  for (int i = threadIdx.x; i < 16 * nD; i += blockDim.x) xs[i] = p.x[16 * i0 + i];
   const uint8_t* gsl = nullptr;
   const uint8_t* usl = nullptr;
   const uint8_t* dsl = nullptr;
@@ -413,6 +421,7 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
     if (lane == 0) trace(p, kTrProdFirst);
     if (active) {
       produce_ring(full, empty, stages, p.stage_bytes, S, nItems, ctl, p.s.err, [&](int i, int slot, uint8_t* st) {
+        if (p.trace && lane == 0 && i < kTrItems) p.trace[blockIdx.x * kTraceSlots + 16 + i] = now_ns();
         if (i < nG) {
           if (lane == 0) mbar_arrive_expect_tx(&full[slot], 16u * p.sg_gu.rb);
           __syncwarp();
@@ -436,6 +445,7 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
   }
 
   // ---- consumers ----------------------------------------------------------------
+  for (int i = threadIdx.x; i < 16 * nD; i += NC) xs[i] = p.x[16 * i0 + i];
   const LaneCtx L = lane_ctx();
   const int nsg = d / kSegElems, nsd = fe / kSegElems;
   BFrag bf;
@@ -446,8 +456,7 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
   // count one finished down tile; the last of the k experts to finish it
   // combines them in the reference's order (acc = sum over rank tt of
   // w_tt * y_tt, then x += acc) into the residual
-  auto count_tile = [&](int tile) {
-    __threadfence();  // this warp's rows of the tile before its count
+  auto count_tile = [&](int tile) {  // after the down rows were fenced (below)
     int last = 0;
     if (lane == 0) last = atomicAdd(&p.s.tile_cnt[(size_t)tile * kTileCntStride], 1u) == (unsigned)(k - 1);
     last = __shfl_sync(0xffffffffu, last, 0);
@@ -510,6 +519,7 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
     if (first < 0) first += W;
     if (first < np) {
       const bool ok = warp_wait(&full[slot], par, ctl, p.s.err);
+      if (p.trace && lane == 0 && i < kTrItems) atomicMin(&ctl->it_land[i], now_ns());
       uint8_t* st = stages + (size_t)slot * p.stage_bytes;
       float* sp = part + (size_t)slot * p.maxp * 16;
 #pragma unroll 1
@@ -535,7 +545,6 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
         } else {
           const int tile = i0 + (i - nG) * P + tt;
           if (lane < 16 && ok) p.s.ybuf[(size_t)t * d + 16 * tile + lane] = row;
-          count_tile(tile);
         }
       }
     } else if (i >= S) {
@@ -544,12 +553,22 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
       warp_wait(&empty[slot], par ^ 1u, ctl, p.s.err);
     }
     __syncwarp();
+    if (p.trace && lane == 0 && i < kTrItems) atomicMax(&ctl->it_done[i], now_ns());
     if (lane == 0) mbar_arrive(&empty[slot]);
   }
   if (active && nDI == 0) g_to_d(false);  // no down tiles here: publish the units only
-  if (!active)
-    for (int jj = warp; jj < nD; jj += W) count_tile(i0 + jj);
+  // count this CTA's tiles, one warp per tile, all at once (the down rows
+  // stored above are made visible first); the last of the k experts to
+  // finish a tile combines it
+  __threadfence();
+  named_bar(1, NC);
+  for (int jj = warp; jj < nD; jj += W) count_tile(i0 + jj);
   if (threadIdx.x == 0) trace(p, kTrDDone);
+  if (p.trace && threadIdx.x < kTrItems) {
+    const unsigned long long ld = ctl->it_land[threadIdx.x];
+    p.trace[blockIdx.x * kTraceSlots + 32 + threadIdx.x] = ld == ~0ull ? 0ull : ld;
+    p.trace[blockIdx.x * kTraceSlots + 48 + threadIdx.x] = ctl->it_done[threadIdx.x];
+  }
 
   // ---- launch exit: the last CTA out resets the per-launch words -------------
   named_bar(1, NC);
@@ -679,26 +698,37 @@ static uint32_t gcd_u(uint32_t a, uint32_t b) {
 
 bool fast_format(uint32_t type) { return type == T_Q8_0 || type == T_Q4_K || type == T_Q6_K || type == T_Q5_0; }
 
+// Rows per copy group.  A group is G consecutive rows copied densely by one
+// bulk copy (the copy engine spends about the same time on a copy of 1 KB as
+// of 8 KB, so groups keep the copies few and large); groups are padded to
+// start 16 B apart modulo 128 B.  G is at most 8 and at least the rows that
+// make a multiple of 16 bytes; within that, the rows a warp reads together
+// lie rb apart inside a group, and a bank model of each segment kernel's
+// shared loads gives: Q6_K conflict-free for G <= 128 / gcd(rb, 128); Q8_0
+// and Q5_0 (17 and 11 4-byte loads per segment, cheap next to a copy) at
+// most two-way for twice that; Q4_K's 16-byte loads two wavefronts per
+// quarter warp instead of one at G = 8.
+static uint32_t copy_group_rows(uint32_t type, uint32_t rb) {
+  const uint32_t gmin = 16u / gcd_u(rb, 16u);
+  const uint32_t spread = 128u / gcd_u(rb, 128u);
+  uint32_t g = type == T_Q4_K ? 8u : type == T_Q6_K ? spread : 2u * spread;
+  if (g > 8u) g = 8u;
+  return g < gmin ? gmin : g;
+}
+
 int stage_geom(uint32_t type, int K, StageGeom* sg) {
   if (!fast_format(type) || K <= 0 || K % kSegElems) return VIREO_ERR_UNSUPPORTED;
   int be, bb;
   if (type_block(type, &be, &bb)) return VIREO_ERR_UNSUPPORTED;
   const uint32_t rb = (uint32_t)(K / be) * (uint32_t)bb;
-  uint32_t G = 16u / gcd_u(rb, 16u);
+  const uint32_t G = copy_group_rows(type, rb);
   if (G > 8) return VIREO_ERR_UNSUPPORTED;
-  if ((type == T_Q8_0 || type == T_Q4_K || type == T_Q5_0) && G != 1) return VIREO_ERR_UNSUPPORTED;
   const uint32_t gbytes = G * rb;
   const uint32_t pad = (16u - gbytes % 128u + 128u) % 128u;
   sg->rb = rb;
   sg->G = G;
   sg->gstride = gbytes + pad;
   sg->hstride = (8u / G) * sg->gstride;
-  // multiply-shift division by gbytes, verified exact over the half's range
-  const uint64_t magic = ((1ull << 32) + gbytes - 1) / gbytes;
-  if (magic > 0xFFFFFFFFull) return VIREO_ERR_UNSUPPORTED;
-  sg->gmagic = (uint32_t)magic;
-  for (uint32_t b = 0; b < 8u * rb; b += 16u)
-    if ((uint32_t)(((uint64_t)b * sg->gmagic) >> 32) != b / gbytes) return VIREO_ERR_UNSUPPORTED;
   return VIREO_OK;
 }
 

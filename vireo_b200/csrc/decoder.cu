@@ -350,11 +350,13 @@ __global__ void __launch_bounds__(kAttnChunk* SPLIT) dec_attn_partial(const __gr
 // Tensor-core attention over the f16 KV cache: one CTA per (chunk of
 // positions, kv head), four consumer warps and one producer warp.
 //
-// The producer streams the chunk's cached K and V rows in tiles of
-// kAttnTile positions into a ring of shared-memory stages (one 1-D bulk copy
-// per row, rows padded to HS * 2 + 16 bytes so that the 8 rows an ldmatrix
-// reads fall on distinct banks).  Consumer warp w takes rows 16 w .. 16 w + 15
-// of every tile:
+// The f16 cache rows are stored swizzled: the 16-byte chunk c of position
+// p's row sits at chunk c ^ (p & 7) (kv_swz), so that 8 consecutive
+// positions read at the same logical chunk fall on 8 distinct bank groups.
+// The producer streams the chunk's cached K and V rows in tiles of kAttnTile
+// positions into a ring of shared-memory stages, one 1-D bulk copy for a
+// tile's K rows and one for its V rows (the rows are contiguous in the
+// cache).  Consumer warp w takes rows 16 w .. 16 w + 15 of every tile:
 //   scores  S = Q K^T with mma.m16n8k16 (f16 in, fp32 accumulate): the QG q
 //           heads of the kv group are the M rows (rows QG..15 zero), 8
 //           positions are the N columns, K is the head dimension; the K rows
@@ -377,10 +379,14 @@ constexpr int kAttnMmaThreads = 32 * (kAttnWarps + 1);
 
 template <int HS>
 struct AttnMmaLayout {
-  static constexpr int kRow = HS * 2 + 16;          // padded f16 row bytes
+  static constexpr int kRow = HS * 2;               // f16 row bytes
   static constexpr int kStage = 2 * kAttnTile * kRow;  // K rows then V rows
   static constexpr int kOffQ = 64;                  // after the barriers
 };
+
+// element index inside a swizzled f16 cache row of position pos: dimension
+// e's 16-byte chunk is stored at chunk (e / 8) ^ (pos & 7)
+VDEV int kv_swz(int e, int pos) { return ((((e >> 3) ^ (pos & 7))) << 3) | (e & 7); }
 
 template <int QG, int HS>
 constexpr size_t attn_mma_smem() {
@@ -445,12 +451,13 @@ __global__ void __launch_bounds__(kAttnMmaThreads) dec_attn_mma(const __grid_con
       }
       const int r0 = i * kAttnTile, rows = max(0, min(kAttnTile, nold - r0));
       uint8_t* st = ring + (size_t)slot * Ly::kStage;
-      if (lane == 0) mbar_arrive_expect_tx(&full[slot], (uint32_t)(2 * rows * HS * 2));
-      __syncwarp();
-      for (int r = lane; r < rows; r += 32) {
-        const size_t g = (size_t)(p0 + r0 + r) * HS;
-        bulk_g2s(st + (size_t)r * Ly::kRow, kb + g, HS * 2, &full[slot]);
-        bulk_g2s(st + (size_t)(kAttnTile + r) * Ly::kRow, vb + g, HS * 2, &full[slot]);
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&full[slot], (uint32_t)(2 * rows * HS * 2));
+        if (rows > 0) {
+          const size_t g = (size_t)(p0 + r0) * HS;
+          bulk_g2s(st, kb + g, (uint32_t)(rows * HS * 2), &full[slot]);
+          bulk_g2s(st + (size_t)kAttnTile * Ly::kRow, vb + g, (uint32_t)(rows * HS * 2), &full[slot]);
+        }
       }
     }
     // no copy may still be landing when the CTA exits
@@ -524,10 +531,10 @@ __global__ void __launch_bounds__(kAttnMmaThreads) dec_attn_mma(const __grid_con
   rope_heads<HS>(sq, QG, p.pos, p.freq, tid, NC);
   if (has_cur) rope_heads<HS>(skv, 1, p.pos, p.freq, tid, NC);
   asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
-  if (has_cur)  // the cache row later steps read
+  if (has_cur)  // the cache row later steps read (swizzled)
     for (int i = tid; i < HS; i += NC) {
-      kb[(size_t)p.pos * HS + i] = __float2half_rn(skv[i]);
-      vb[(size_t)p.pos * HS + i] = __float2half_rn(skv[HS + i]);
+      kb[(size_t)p.pos * HS + kv_swz(i, p.pos)] = __float2half_rn(skv[i]);
+      vb[(size_t)p.pos * HS + kv_swz(i, p.pos)] = __float2half_rn(skv[HS + i]);
     }
 
   // Q as A fragments, scaled: row g (a q head when g < QG), rows g + 8 zero
@@ -573,8 +580,9 @@ __global__ void __launch_bounds__(kAttnMmaThreads) dec_attn_mma(const __grid_con
         __half* kr = reinterpret_cast<__half*>(st + (size_t)r * Ly::kRow);
         __half* vr = reinterpret_cast<__half*>(st + (size_t)(kAttnTile + r) * Ly::kRow);
         for (int e = lane; e < HS; e += 32) {
-          kr[e] = is_cur ? __float2half_rn(skv[e]) : __float2half_rn(0.f);
-          vr[e] = is_cur ? __float2half_rn(skv[HS + e]) : __float2half_rn(0.f);
+          const int se = kv_swz(e, r);  // the tile's rows start at a multiple of 8 positions
+          kr[se] = is_cur ? __float2half_rn(skv[e]) : __float2half_rn(0.f);
+          vr[se] = is_cur ? __float2half_rn(skv[HS + e]) : __float2half_rn(0.f);
         }
       }
       (void)last;
@@ -588,7 +596,8 @@ __global__ void __launch_bounds__(kAttnMmaThreads) dec_attn_mma(const __grid_con
         uint32_t b[2][4];
 #pragma unroll
         for (int j = 0; j < 2; j++) {
-          const uint8_t* row = st + (size_t)(wr + 8 * j + (lane & 7)) * Ly::kRow + 2 * (16 * s + 8 * (lane >> 3));
+          const int r = wr + 8 * j + (lane & 7), ch = 2 * s + (lane >> 3);
+          const uint8_t* row = st + (size_t)r * Ly::kRow + 16 * (ch ^ (r & 7));
           ldsm_x4(row, b[j][0], b[j][1], b[j][2], b[j][3]);
         }
         uint32_t a0[4] = {qa[s][0], 0u, qa[s][1], 0u}, a1[4] = {qa[s + 1][0], 0u, qa[s + 1][1], 0u};
@@ -619,8 +628,8 @@ __global__ void __launch_bounds__(kAttnMmaThreads) dec_attn_mma(const __grid_con
 #pragma unroll
       for (int j = 0; j < NT; j += 2) {
         uint32_t b0, b1, b2, b3;
-        const uint8_t* row = st + (size_t)(kAttnTile + wr + (lane & 7) + 8 * ((lane >> 3) & 1)) * Ly::kRow +
-                             2 * (8 * (j + (lane >> 4)));
+        const int r = wr + (lane & 7) + 8 * ((lane >> 3) & 1), ch = j + (lane >> 4);
+        const uint8_t* row = st + (size_t)(kAttnTile + r) * Ly::kRow + 16 * (ch ^ (r & 7));
         ldsm_x4_trans(row, b0, b1, b2, b3);
         mma_16816(o[j], pa, b0, b1);
         mma_16816(o[j + 1], pa, b2, b3);
@@ -876,7 +885,7 @@ static int attn_mma_chunk(int npos, int nkv, int num_sms) {
 // predecessor only where their CTAs can share SMs.
 static int set_chain_carveout(int qg, int f16, int hs) {
   const void* fns[] = {reinterpret_cast<const void*>(&dec_rmsnorm), reinterpret_cast<const void*>(&dec_attn_combine),
-                       reinterpret_cast<const void*>(&dec_argmax), attn_kernel(qg, f16, hs)};
+                       reinterpret_cast<const void*>(&dec_argmax), attn_kernel(qg, 0, hs)};
   for (const void* fn : fns) {
     if (!fn) return VIREO_ERR_UNSUPPORTED;
     const int st = cuda_status(

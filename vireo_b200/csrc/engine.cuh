@@ -12,11 +12,10 @@
 // on which warp computed what) and runs the caller's epilogue.
 //
 // Stage layout: rows 0..7 ("half 0") and 8..15 ("half 1") may come from
-// different matrices (gate and up rows of one expert).  Rows are copied
-// one by one when a row is a multiple of 16 bytes (padded so consecutive
-// rows start 16 B apart modulo 128 B, which spreads the lanes of a warp over
-// all 32 banks), or in dense groups of G rows when only G rows together
-// form a multiple of 16 bytes.
+// different matrices (gate and up rows of one expert).  Rows are copied in
+// dense groups of G rows, one bulk copy per group, the groups padded to
+// start 16 B apart modulo 128 B (stage_geom picks G per format and row
+// size so that the lanes of a warp spread over the banks).
 #pragma once
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -33,7 +32,6 @@ struct StageGeom {
   uint32_t G;        // rows per copy group (1, 2, 4 or 8)
   uint32_t gstride;  // smem bytes between copy groups inside a half
   uint32_t hstride;  // smem bytes from half 0 to half 1
-  uint32_t gmagic;   // floor(b / (G * rb)) == (b * gmagic) >> 32 for b < 8 * rb
 };
 
 VDEV const uint8_t* stage_row(const uint8_t* stage, const StageGeom& sg, int r) {
@@ -310,8 +308,9 @@ struct SegQ6K : Q6K {
 // Residual tables: the two digits leave an error of up to max|x| / 64516 on
 // every value of a group, which is small against the group's own values
 // unless one value dwarfs the others (an outlier channel).  A segment in
-// which some group's largest magnitude exceeds kResRatio times the group's
-// root mean square gets a second table of the same form for the remainder
+// which some group's largest magnitude exceeds kResRatio times the median of
+// the segment's eight group maxima gets a second table of the same form for
+// the remainder
 // r = x - x~ (rtab + kResTabBytes i, rmeta + kMeta i); the consumers add the
 // products with it, so every value of such a segment is carried to about
 // max|x| / 64516^2.  The dot products are linear in the activations, so the
@@ -323,7 +322,7 @@ struct SegQ6K : Q6K {
 // the source may alias tab (the same 1 KB footprint per segment).
 // ---------------------------------------------------------------------------
 constexpr int kResTabBytes = 512;
-constexpr float kResRatio = 8.0f;
+constexpr float kResRatio = 4.0f;
 
 struct VecTab {
   uint8_t* tab;   // [nseg][kSegTabBytes]
@@ -432,20 +431,26 @@ VDEV void build_tables(const float* src, const VecTab& T, int nseg, int warp, in
     bad = __shfl_xor_sync(0xffffffffu, (int)bad, 1) | __shfl_xor_sync(0xffffffffu, (int)bad, 2) | bad;
     const float sc = bad ? __int_as_float(0x7fc00000) : mx * (1.0f / 127.0f);
     const float inv = (mx > 0.f && !bad) ? 127.0f / mx : 0.f;
-    // sum of squares of the scaled values (|x inv| <= 127, no overflow)
-    float ss = 0.f;
-#pragma unroll
-    for (int q = 0; q < 8; q++) ss = fmaf(x[q] * inv, x[q] * inv, ss);
-    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
     uint32_t lo1, hi1, lo2, hi2;
     int s1, s2;
     float used[8];
     digits8(x, inv, lo1, hi1, lo2, hi2, s1, s2, used);
-    // an outlier group: max^2 > ratio^2 * mean square (finite groups only);
-    // in scaled units the max is 127
-    const bool want = !bad && mx > 0.f && 127.f * 127.f > kResRatio * kResRatio * (ss * (1.0f / 32.0f));
-    const bool flagged = __any_sync(0xffffffffu, want);
+    // an outlier group: its max above kResRatio x the median (the mean of
+    // the 4th and 5th smallest) of the segment's 8 group maxima; finite
+    // segments only
+    float gm[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) gm[k] = __shfl_sync(0xffffffffu, mx, 4 * k);
+#pragma unroll
+    for (int a = 1; a < 8; a++)
+#pragma unroll
+      for (int b = a; b > 0; b--) {
+        const float lo = fminf(gm[b - 1], gm[b]), hi = fmaxf(gm[b - 1], gm[b]);
+        gm[b - 1] = lo;
+        gm[b] = hi;
+      }
+    const bool seg_bad = __any_sync(0xffffffffu, bad);
+    const bool flagged = !seg_bad && gm[7] > kResRatio * 0.5f * (gm[3] + gm[4]);
     group_meta(meta, lane, sc, s1, s2);
     digits_to_table<F>(tab, tab, lane, lo1, hi1, lo2, hi2);
     if (flagged) {
