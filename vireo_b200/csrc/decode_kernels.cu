@@ -18,6 +18,9 @@ struct Ctl {
   int ids[kMaxTopK];
   float wts[kMaxTopK];
   float nred[kConsumerWarps];  // gemv_kernel: per-warp sums of squares for the fused norm
+  // the item each ring slot holds now (-1: none yet), written by the producer
+  // before it issues the item's copies
+  int slot_item[kMaxStages];
   // trace only: first full-wait return and last empty arrival of the first items
   unsigned long long it_land[kTrItems], it_done[kTrItems];
 };
@@ -41,6 +44,39 @@ VDEV bool warp_wait(uint64_t* bar, uint32_t par, Ctl* ctl, int* err) {
   int ok = 1;
   if ((threadIdx.x & 31) == 0) {
     ok = (!aborted(ctl) && mbar_wait(bar, par, &ctl->abort)) ? 1 : 0;
+    if (!ok && !aborted(ctl)) do_abort(ctl, err, VIREO_ERR_TIMEOUT);
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
+}
+
+// Warp-collective wait for item i's data in its ring slot.  A warp that owns
+// only some items may reach item i while the slot still holds item i - S, in
+// which case a parity wait alone would see the earlier phase and return at
+// once; so the warp first waits (bounded) until the producer has recorded
+// item i in the slot, and only then waits on the full barrier's parity.
+VDEV bool item_wait(uint64_t* full, Ctl* ctl, int* err, int i, int S) {
+  const int slot = i % S;
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) {
+    const volatile int* rec = &ctl->slot_item[slot];
+    if (*rec != i) {
+      const uint64_t t0 = now_ns();
+      while (*rec != i) {
+        if (aborted(ctl)) {
+          ok = 0;
+          break;
+        }
+        if (now_ns() - t0 > kWaitLimitNs) {
+          do_abort(ctl, err, VIREO_ERR_TIMEOUT);
+          ok = 0;
+          break;
+        }
+        __nanosleep(32);
+      }
+    }
+    if (ok) ok = (!aborted(ctl) && mbar_wait(&full[slot], (uint32_t)(i / S) & 1u, &ctl->abort)) ? 1 : 0;
     if (!ok && !aborted(ctl)) do_abort(ctl, err, VIREO_ERR_TIMEOUT);
   }
   ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -209,44 +245,15 @@ VDEV int produce_ring(uint64_t* full, uint64_t* empty, uint8_t* stages, uint32_t
       __syncwarp();
     }
     if (aborted(ctl)) break;
+    // the slot's previous item is released and its copies landed: the full
+    // barrier's open phase is item i's from here on
+    if ((threadIdx.x & 31) == 0) *reinterpret_cast<volatile int*>(&ctl->slot_item[slot]) = i;
     issue(i, slot, stages + (size_t)slot * stage_bytes);
   }
   if ((threadIdx.x & 31) == 0)
     for (int j = i > S ? i - S : 0; j < i; j++) wait_copies(&full[j % S], (uint32_t)(j / S) & 1u);
   __syncwarp();
   return i;
-}
-
-// Partial of one (tile, segment) pair into part (16 floats), then the tile's
-// shared-memory counter; true in the warp that completed the tile, whose
-// lanes 0..15 then hold the tile's row sums in segment order (the counter is
-// put back to zero).
-VDEV bool pair_done(float t0, float t1, float* pt, const float* tile_part, int* cnt, int nseg, const LaneCtx& L,
-                    float& row) {
-  t0 += __shfl_xor_sync(0xffffffffu, t0, 1);
-  t1 += __shfl_xor_sync(0xffffffffu, t1, 1);
-  t0 += __shfl_xor_sync(0xffffffffu, t0, 2);
-  t1 += __shfl_xor_sync(0xffffffffu, t1, 2);
-  if (L.t == 0) {
-    pt[L.g] = t0;
-    pt[L.g + 8] = t1;
-  }
-  __syncwarp();
-  int last = 0;
-  if (L.lane == 0) {
-    __threadfence_block();
-    last = atomicAdd(cnt, 1) == nseg - 1;
-  }
-  last = __shfl_sync(0xffffffffu, last, 0);
-  if (!last) return false;
-  __threadfence_block();
-  float acc = 0.f;
-  if (L.lane < 16)
-    for (int s = 0; s < nseg; s++) acc += ((const volatile float*)tile_part)[s * 16 + L.lane];
-  row = acc;
-  __syncwarp();
-  if (L.lane == 0) *cnt = 0;
-  return true;
 }
 
 // The decode kernel body.  ROUTED: the route comes from the caller (rt) and
@@ -258,8 +265,7 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
   uint64_t* empty = full + kMaxStages;
   Ctl* ctl = reinterpret_cast<Ctl*>(smem + p.off_ctl);
   const uint8_t** etab = reinterpret_cast<const uint8_t**>(smem + p.off_etab);  // [ne][3] expert slices
-  int* ucnt = reinterpret_cast<int*>(smem + p.off_ucnt);        // [S][kMaxDTiles] pairs done per tile
-  float* part = reinterpret_cast<float*>(smem + p.off_part);    // [S][maxp][16] pair partials
+  int* ucnt = reinterpret_cast<int*>(smem + p.off_ucnt);  // [S][kMaxDTiles]: [0] = tiles of the item done
   const VecTab xt = {smem + p.off_xtab, reinterpret_cast<float*>(smem + p.off_xmeta), smem + p.off_xrtab,
                      reinterpret_cast<float*>(smem + p.off_xrmeta)};
   const VecTab ht = {smem + p.off_htab, reinterpret_cast<float*>(smem + p.off_hmeta), smem + p.off_hrtab,
@@ -277,8 +283,9 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
   if (threadIdx.x == 0) {
     trace(p, kTrStart);
     for (int s = 0; s < S; s++) {
-      mbar_init(&full[s], 1);  // the producer's arrive.expect_tx; the copies complete the bytes
-      mbar_init(&empty[s], W);  // every consumer warp, once per item
+      mbar_init(&full[s], 1);   // the producer's arrive.expect_tx; the copies complete the bytes
+      mbar_init(&empty[s], 1);  // the warp that finishes the item's last unit or tile
+      ctl->slot_item[s] = -1;
     }
     ctl->abort = 0;
     mbar_fence_init();
@@ -505,58 +512,68 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
     if (threadIdx.x == 0) trace(p, kTrHtab);
   };
 
+  // ---- gate/up units: unit i to warp i mod W, its segments in order ----------
 #pragma unroll 1
-  for (int i = 0; i < nItems; i++) {
+  for (int i = warp; i < nG; i += W) {
     const int slot = i % S;
-    const uint32_t par = (uint32_t)(i / S) & 1u;
-    const bool isd = i >= nG;
-    if (i == nG) g_to_d(true);
-    const int nt = isd ? min(P, nD - (i - nG) * P) : 1;
-    const int nseg = isd ? nsd : nsg;
-    const int np = nt * nseg;
-    const int q0 = isd ? nG * nsg + (i - nG) * P * nsd : i * nsg;  // pairs dealt before this item
-    int first = (warp - q0 % W) % W;
-    if (first < 0) first += W;
-    if (first < np) {
-      const bool ok = warp_wait(&full[slot], par, ctl, p.s.err);
-      if (p.trace && lane == 0 && i < kTrItems) atomicMin(&ctl->it_land[i], now_ns());
-      uint8_t* st = stages + (size_t)slot * p.stage_bytes;
-      float* sp = part + (size_t)slot * p.maxp * 16;
+    const bool ok = item_wait(full, ctl, p.s.err, i, S);
+    if (p.trace && lane == 0 && i < kTrItems) atomicMin(&ctl->it_land[i], now_ns());
+    const uint8_t* st = stages + (size_t)slot * p.stage_bytes;
+    const uint8_t* r0 = stage_row(st, p.sg_gu, L.g);
+    const uint8_t* r1 = stage_row(st, p.sg_gu, L.g + 8);
+    float gs = 0.f, us = 0.f;
+    if (ok)
 #pragma unroll 1
-      for (int pp = first; pp < np; pp += W) {
-        const int tt = pp / nseg, seg = pp - tt * nseg;
-        float t0 = 0.f, t1 = 0.f;
-        if (ok) {
-          if (isd) {
-            const uint8_t* base = st + (size_t)tt * p.dslot_bytes;
-            seg_dot<SD>(stage_row(base, p.sg_d, L.g), stage_row(base, p.sg_d, L.g + 8), seg, ht, L, bf, t0, t1);
-          } else {
-            seg_dot<SG>(stage_row(st, p.sg_gu, L.g), stage_row(st, p.sg_gu, L.g + 8), seg, xt, L, bf, t0, t1);
-          }
-        }
-        float row;
-        if (!pair_done(t0, t1, sp + pp * 16, sp + tt * nseg * 16, &ucnt[slot * kMaxDTiles + tt], nseg, L, row))
-          continue;
-        if (!isd) {
-          // rows 0..7 of a unit are gate rows, 8..15 the matching up rows: the
-          // reference's SwiGLU, gguf_run.c:206
-          const float up = __shfl_down_sync(0xffffffffu, row, 8);
-          if (lane < 8 && ok) p.s.hbuf[(size_t)t * fe + 8 * (u0 + i) + lane] = (row / (1.0f + expf(-row))) * up;
-        } else {
-          const int tile = i0 + (i - nG) * P + tt;
-          if (lane < 16 && ok) p.s.ybuf[(size_t)t * d + 16 * tile + lane] = row;
-        }
-      }
-    } else if (i >= S) {
-      // nothing of this item here: wait until the slot's previous item is
-      // released, so that this arrival counts for this item's phase
-      warp_wait(&empty[slot], par ^ 1u, ctl, p.s.err);
-    }
+      for (int seg = 0; seg < nsg; seg++) seg_dot<SG>(r0, r1, seg, xt, L, bf, gs, us);
+    gs += __shfl_xor_sync(0xffffffffu, gs, 1);
+    us += __shfl_xor_sync(0xffffffffu, us, 1);
+    gs += __shfl_xor_sync(0xffffffffu, gs, 2);
+    us += __shfl_xor_sync(0xffffffffu, us, 2);
+    // lane (g, 0) holds gate row g and its up row (rows g and g + 8 of the
+    // unit): the reference's SwiGLU, gguf_run.c:206
+    if (L.t == 0 && ok) p.s.hbuf[(size_t)t * fe + 8 * (u0 + i) + L.g] = (gs / (1.0f + expf(-gs))) * us;
     __syncwarp();
     if (p.trace && lane == 0 && i < kTrItems) atomicMax(&ctl->it_done[i], now_ns());
     if (lane == 0) mbar_arrive(&empty[slot]);
   }
-  if (active && nDI == 0) g_to_d(false);  // no down tiles here: publish the units only
+  if (nDI > 0)
+    g_to_d(true);
+  else if (active)
+    g_to_d(false);  // no down tiles here: publish the units only
+
+  // ---- down tiles: the CTA's tile u to warp u mod W; the last tile of an
+  // item to finish releases its stage ------------------------------------------
+  const int nDT = nDI > 0 ? nD : 0;
+#pragma unroll 1
+  for (int u = warp; u < nDT; u += W) {
+    const int i = nG + u / P, tt = u - (u / P) * P;
+    const int slot = i % S;
+    const int nt = min(P, nD - (i - nG) * P);
+    const bool ok = item_wait(full, ctl, p.s.err, i, S);
+    if (p.trace && lane == 0 && i < kTrItems) atomicMin(&ctl->it_land[i], now_ns());
+    const uint8_t* base = stages + (size_t)slot * p.stage_bytes + (size_t)tt * p.dslot_bytes;
+    const uint8_t* r0 = stage_row(base, p.sg_d, L.g);
+    const uint8_t* r1 = stage_row(base, p.sg_d, L.g + 8);
+    float y0 = 0.f, y1 = 0.f;
+    if (ok)
+#pragma unroll 1
+      for (int seg = 0; seg < nsd; seg++) seg_dot<SD>(r0, r1, seg, ht, L, bf, y0, y1);
+    y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
+    y1 += __shfl_xor_sync(0xffffffffu, y1, 1);
+    y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
+    y1 += __shfl_xor_sync(0xffffffffu, y1, 2);
+    const int tile = i0 + u;
+    if (L.t == 0 && ok) {
+      p.s.ybuf[(size_t)t * d + 16 * tile + L.g] = y0;
+      p.s.ybuf[(size_t)t * d + 16 * tile + L.g + 8] = y1;
+    }
+    __syncwarp();
+    if (p.trace && lane == 0 && i < kTrItems) atomicMax(&ctl->it_done[i], now_ns());
+    if (lane == 0 && atomicAdd(&ucnt[slot * kMaxDTiles], 1) == nt - 1) {
+      ucnt[slot * kMaxDTiles] = 0;
+      mbar_arrive(&empty[slot]);
+    }
+  }
   // count this CTA's tiles, one warp per tile, all at once (the down rows
   // stored above are made visible first); the last of the k experts to
   // finish a tile combines it
@@ -770,7 +787,9 @@ uint32_t moe_decode_layout(MoeDecodeParams* p, uint32_t smem_limit, int grid) {
   p->dslot_bytes = dslot;
   p->dtiles = (int)dt;
   const int nsg = p->d / kSegElems, nsd = p->fe / kSegElems, R = (p->ne + 31) / 32;
-  p->maxp = std::max(nsg, p->dtiles * nsd);
+  p->maxp = 0;  // (tile, segment) partials: none (a warp takes a whole unit or tile)
+  (void)nsg;
+  (void)nsd;
   uint32_t off = 2u * kMaxStages * 8u;  // full/empty barriers
   p->off_ctl = off;
   off = up_to(off + (uint32_t)sizeof(Ctl), 16);

@@ -4,12 +4,13 @@
 // the raw GGUF rows of each item (one or more tiles) from HBM into a ring of
 // shared-memory stages with 1-D bulk copies (cp.async.bulk: one instruction
 // per row or per group of rows, executed by the TMA engine, completing on the
-// stage's mbarrier; never multicast).  The consumer warps split each tile's K
-// into 256-value segments and run the tensor-core segment kernels below on
-// (tile, segment) pairs dealt round-robin over the warps; each pair leaves a
-// 16-row partial in shared memory and the warp that completes a tile's last
-// segment sums the partials in segment order (so the result does not depend
-// on which warp computed what) and runs the caller's epilogue.
+// stage's mbarrier; never multicast).  The consumer warps run the
+// tensor-core segment kernels below over each tile's 256-value segments:
+// the MoE kernel gives a whole tile to one warp (segments in order, in
+// registers); the stand-alone GEMV deals a tile's segments over the warps
+// (consume_unit) and the warp that completes the tile sums the segment
+// partials in segment order.  Either way the result does not depend on
+// which warp computed what.
 //
 // Stage layout: rows 0..7 ("half 0") and 8..15 ("half 1") may come from
 // different matrices (gate and up rows of one expert).  Rows are copied in

@@ -15,14 +15,14 @@
 //   stages, its share of that expert's gate/up units (8 gate + 8 up rows)
 //   and then its share of the expert's down tiles (16 rows; several per
 //   stage), so the down rows arrive while gate/up is still computed.
-//   G  (unit, segment) pairs dealt over the consumer warps; the warp that
-//      completes a unit writes h = silu(g) * u for its 8 rows to scratch;
-//      the group counts finished units.
+//   G  unit i to consumer warp i mod W, which runs all of its segments and
+//      writes h = silu(g) * u for its 8 rows to scratch; the group counts
+//      finished units.
 //   D  once the group's units are all counted, the CTA stages the expert's h
-//      and builds its activation tables; (tile, segment) pairs are dealt
-//      likewise, the warp completing a tile writes its 16 outputs to scratch,
-//      and the last of the k groups to finish a tile combines the k experts'
-//      rows in rank order and adds them into the residual.
+//      and builds its activation tables; down tile u to warp u mod W, which
+//      writes its 16 outputs to scratch; then every tile is counted and the
+//      last of the k groups to finish a tile combines the k experts' rows in
+//      rank order and adds them into the residual.
 #pragma once
 #include <stdint.h>
 
@@ -78,7 +78,7 @@ struct MoeDecodeParams {
   int nstages;
   uint32_t dslot_bytes;  // one down tile inside a stage
   int dtiles;            // down tiles per stage
-  int maxp;              // (tile, segment) pairs of one stage at most
+  int maxp;              // shared partials per stage (0: a warp takes a whole unit or tile)
   // shared-memory offsets (bytes)
   uint32_t off_ctl, off_etab, off_ucnt, off_part, off_xtab, off_xmeta, off_xrtab, off_xrmeta, off_htab, off_hmeta,
       off_hrtab, off_hrmeta, off_xs, off_stage;

@@ -58,15 +58,20 @@ VDEV bool mbar_test_suspend(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
       : "memory");
   return ok != 0;
 }
+// Suspend-time hint of the barrier waits, in ns (0: the hardware's default).
+#ifndef VIREO_MBAR_HINT_NS
+#define VIREO_MBAR_HINT_NS 0
+#endif
+
 // Waits for the phase with the given parity to complete: try_wait in a loop
-// (each try may suspend the thread for the hardware's own short limit and
-// resumes it when the phase completes).  Gives up (false) when the time limit
-// passes or *abort becomes non-zero.
+// (each try may suspend the thread, for at most the hint, and resumes it when
+// the phase completes).  Gives up (false) when the time limit passes or
+// *abort becomes non-zero.
 VDEV bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort) {
   if (mbar_test(bar, parity)) return true;
   uint64_t t0 = now_ns();
   for (;;) {
-    if (mbar_test(bar, parity)) return true;
+    if (VIREO_MBAR_HINT_NS ? mbar_test_suspend(bar, parity, VIREO_MBAR_HINT_NS) : mbar_test(bar, parity)) return true;
     if (*abort) return false;
     if (now_ns() - t0 > kWaitLimitNs) return false;
   }
