@@ -367,9 +367,8 @@ __global__ void __launch_bounds__(kAttnChunk* SPLIT) dec_attn_partial(const __gr
 //   values  O += P V with the score accumulators of two position tiles
 //           reused as the A fragment (P rounded to f16) and the V rows loaded
 //           transposed (ldmatrix.trans) as B fragments.
-// The four warps' states are merged in shared memory; the CTA's state per q
-// head (acc, m, l) goes to part, and the last CTA of the kv head to finish
-// merges the chunks in chunk order and writes the attention output.
+// The four warps' states are merged in shared memory and the CTA's state per
+// q head (acc, m, l) goes to part; dec_attn_combine merges the chunks.
 // The q/k post-processing and the KV append are those of dec_attn_partial.
 // ---------------------------------------------------------------------------
 constexpr int kAttnTile = 64;   // positions per stage
@@ -398,8 +397,7 @@ constexpr size_t attn_mma_smem() {
 }
 
 template <int QG, int HS>
-__global__ void __launch_bounds__(kAttnMmaThreads) dec_attn_mma(const __grid_constant__ AttnParams p, int C,
-                                                                 float* out, unsigned int* cnt) {
+__global__ void __launch_bounds__(kAttnMmaThreads) dec_attn_mma(const __grid_constant__ AttnParams p, int C) {
   using Ly = AttnMmaLayout<HS>;
   constexpr int NC = 32 * kAttnWarps;  // consumer threads
   constexpr int KS = HS / 16;          // k16 steps of the scores
@@ -670,30 +668,6 @@ __global__ void __launch_bounds__(kAttnMmaThreads) dec_attn_mma(const __grid_con
     }
     cp[((size_t)h * p.nchunk + c) * (HS + 2) + e] = e == HS ? M : a;
   }
-  // ---- the last CTA of this kv head merges the chunks in chunk order ---------
-  __threadfence();
-  asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
-  if (tid == 0) flags[1] = atomicAdd(&cnt[kh], 1u) == (unsigned)(p.nchunk - 1);
-  asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
-  if (!flags[1]) return;
-  __threadfence();
-  const int nc = p.nchunk;
-  for (int idx = tid; idx < QG * HS; idx += NC) {
-    const int h = idx / HS, e = idx - h * HS;
-    const float* base = p.part + (size_t)(h0 + h) * nc * (HS + 2);
-    float M = -INFINITY;
-    for (int cc = 0; cc < nc; cc++) M = fmaxf(M, __ldcg(base + (size_t)cc * (HS + 2) + HS));
-    float a = 0.f, L = 0.f;
-#pragma unroll 4
-    for (int cc = 0; cc < nc; cc++) {
-      const float mc = __ldcg(base + (size_t)cc * (HS + 2) + HS);
-      const float f = mc > -INFINITY ? expf(mc - M) : 0.f;
-      a += __ldcg(base + (size_t)cc * (HS + 2) + e) * f;
-      L += __ldcg(base + (size_t)cc * (HS + 2) + HS + 1) * f;
-    }
-    out[(size_t)(h0 + h) * HS + e] = L > 0.f ? a * (1.0f / L) : 0.f;
-  }
-  if (tid == 0) cnt[kh] = 0u;
 }
 
 // RoPE frequencies (rope_neox, gguf_run.c:171): freq[j] = powf(base, -2j/hs)
@@ -919,7 +893,6 @@ struct gguf_decoder {
   void *kc = nullptr, *vc = nullptr;
   size_t layer_kv = 0;  // elements of one layer's K (or V) cache
   int max_chunk = 0;
-  unsigned int* attn_cnt = nullptr;  // per kv head: attention CTAs finished (tensor-core path)
 };
 
 extern "C" {
@@ -927,7 +900,7 @@ extern "C" {
 void gguf_decoder_destroy(gguf_decoder* dec) {
   if (!dec) return;
   for (void* p : {(void*)dec->x, (void*)dec->xb, (void*)dec->y, (void*)dec->q, (void*)dec->att, (void*)dec->part,
-                  (void*)dec->logits, dec->kc, dec->vc, (void*)dec->freq, (void*)dec->attn_cnt})
+                  (void*)dec->logits, dec->kc, dec->vc, (void*)dec->freq})
     if (p) cudaFree(p);
   for (void* p : dec->wqkv)
     if (p) cudaFree(p);
@@ -987,8 +960,6 @@ int gguf_decoder_create(const gguf_decoder_desc* desc, const gguf_decoder_layer*
       (st = cuda_status(cudaMalloc(&dec->part, (size_t)D.n_heads * dec->max_chunk * (D.head_size + 2) * 4))) ||
       (st = cuda_status(cudaMalloc(&dec->logits, (size_t)D.vocab * 4))) ||
       (st = cuda_status(cudaMalloc(&dec->kc, kvb))) || (st = cuda_status(cudaMalloc(&dec->vc, kvb))) ||
-      (st = cuda_status(cudaMalloc(&dec->attn_cnt, sizeof(unsigned int) * (size_t)D.n_kv_heads))) ||
-      (st = cuda_status(cudaMemset(dec->attn_cnt, 0, sizeof(unsigned int) * (size_t)D.n_kv_heads))) ||
       (st = cuda_status(cudaMemset(dec->x, 0, (size_t)D.dim * 4)))) {
     gguf_decoder_destroy(dec);
     return st;
@@ -1089,7 +1060,7 @@ static int decoder_step(gguf_decoder* dec, int token, const int32_t* token_dev, 
     at.part = dec->part;
     at.err = c->d_err;
     if (D.kv_f16) {
-      // tensor-core attention; its last CTA per kv head merges the chunks
+      // tensor-core attention per (chunk, kv head), then the chunk merge
       size_t smem = 0;
       const void* fn = attn_mma_kernel(D.n_heads / D.n_kv_heads, hs, &smem);
       const int C = attn_mma_chunk(npos, D.n_kv_heads, c->num_sms);
@@ -1105,10 +1076,11 @@ static int decoder_step(gguf_decoder* dec, int token, const int32_t* token_dev, 
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int Cv = C;
-      float* outp = dec->att;
-      unsigned int* cntp = dec->attn_cnt;
-      void* args[] = {&at, &Cv, &outp, &cntp};
+      void* args[] = {&at, &Cv};
       if ((st = cuda_status(cudaLaunchKernelExC(&cfg, fn, args)))) return st;
+      if ((st = launch_pdl(dec_attn_combine, dim3(D.n_heads), dim3(kCombThreads),
+                           (size_t)(at.nchunk + kCombThreads) * sizeof(float), s, at, dec->att)))
+        return st;
     } else {
       if ((st = launch_attn(at, D.n_heads / D.n_kv_heads, D.kv_f16, nchunk, D.n_kv_heads, s))) return st;
       if ((st = launch_pdl(dec_attn_combine, dim3(D.n_heads), dim3(kCombThreads),
