@@ -183,6 +183,38 @@ def test_moe_q5_0_experts(V, gt, dt, dim, fe, ne, k):
         m.close()
 
 
+@pytest.mark.parametrize("name", ["cfg1_olmoe_q8", "qwen3"])
+def test_moe_router_exact_ties(V, golden, name):
+    """Experts 2j and 2j + 1 share one router row, so every probability is
+    tied with its partner's bit for bit, and the selection must take the
+    lower id first (the reference's strict '>' scan from id 0,
+    gguf_run.c:190-191).  Router entries are multiples of 1/64 and the
+    hidden values small integers, so every logit is exact in any summation
+    order and distinct logits differ by at least 1/64: ids bit-exact against
+    the oracle on every token."""
+    import torch
+    L = golden_layer(golden, name)
+    s = L.spec
+    R = L.router.view(np.float32).reshape(s.n_experts, s.dim)
+    R[:] = ((S.u64(91, 1, s.n_experts * s.dim) % np.uint64(17)).astype(np.float32) - 8.0).reshape(R.shape) / 64.0
+    R[1::2] = R[0::2]
+    n = 12
+    toks = ((S.u64(91, 2, n * s.dim) % np.uint64(5)).astype(np.float32) - 2.0).reshape(n, s.dim)
+    x0 = (S.normal(91, 3, toks.size) * 0.3).astype(np.float32).reshape(toks.shape)
+    rx, rids, rwts = O.PortMoe(L)(toks, x0)
+    assert (rids[:, 0] % 2 == 0).all()  # the lower id of the top pair first
+    m = V.MoeLayer(L)
+    try:
+        hb, x = torch.from_numpy(toks).cuda(), torch.from_numpy(x0.copy()).cuda()
+        ids = torch.zeros((n, s.n_used), dtype=torch.int32, device="cuda")
+        wts = torch.zeros((n, s.n_used), dtype=torch.float32, device="cuda")
+        m.ffn(hb, x, ids, wts)
+        m.sync()
+        check_moe(x0, x.cpu().numpy(), ids.cpu().numpy(), wts.cpu().numpy(), rx, rids, rwts)
+    finally:
+        m.close()
+
+
 def test_moe_unsupported_layer_is_rejected(V):
     spec = S.MoeLayerSpec(512, 256, 8, 2, 0, S.GGML_F16, S.GGML_F16, S.GGML_Q8_0)
     L = S.MoeLayer(spec, 1)

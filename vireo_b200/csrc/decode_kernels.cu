@@ -5,6 +5,8 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "moe_decode.cuh"
 #include "vireo_internal.h"
 
@@ -113,37 +115,28 @@ VDEV void stage_vec_cg8(const float* g, float* s, int n, int tid, int nthr) {
   }
 }
 
-// Softmax and top-k of the router logits by warps 0 .. R - 1 (R = ne / 32
-// rounded up).  Warp w sums the chunk partials of experts 32 w .. 32 w + 31
-// in chunk order (logit e) into lg; then every one of the R warps takes the
-// softmax of all the logits with expf into its own copy of p (pw + w ne) and
-// ranks its 32 experts against it: expert e takes rank r = #{j : p_j > p_e,
-// or p_j == p_e and j < e}, the position the reference's greedy strict-'>'
-// selection gives it (gguf_run.c:190-191).  Ranks < k are the selection, in
-// rank order (NaN never selected; unused slots hold id -1 and weight -1, as
-// the reference's scan leaves them).  The weights are the probabilities;
-// renormalisation comes later (route_finish).  lg: 32 R floats; pw: R rows
-// of ne rounded up to a multiple of 4 floats (shared memory, 16-byte
-// aligned).
-VDEV void route_warps(const MoeDecodeParams& p, Ctl* ctl, float* lg, float* pw, int warp, int lane) {
+// Routing after every CTA's logits are in, in two steps.
+//
+// route_keys (one warp): the softmax of the ne logits with expf (max
+// subtracted; the sum over a lane's experts l, l + 32, ... in order, then
+// across lanes by an xor tree) and, per expert, a 64-bit selection key:
+// the probability's bits above (p >= 0, so bit order is value order) and
+// 0xffffffff - e below, or 0 for NaN.  Key order is the order (p desc, id
+// asc) in which the reference's greedy strict-'>' scan from id 0 takes the
+// experts (gguf_run.c:190-191), and a NaN key never outranks a valid one.
+// Keys past ne up to np (a power of two) are 0.  Slots from the number of
+// valid experts to k get id -1 and weight -1, as the reference's scan
+// leaves them.
+VDEV void route_keys(const MoeDecodeParams& p, Ctl* ctl, unsigned long long* key, int np, int lane) {
   constexpr int kPer = kMaxExperts / 32;
-  const int ne = p.ne, k = p.k, nchunk = p.d / kRouterChunk, R = (ne + 31) / 32;
-  {
-    // every load issued at once (clamped addresses), then the chunk-order sum
-    const int e = 32 * warp + lane, ec = min(e, ne - 1);
-    float pc[8];
-#pragma unroll
-    for (int c = 0; c < 8; c++) pc[c] = __ldcg(p.s.logit_part + (size_t)min(c, nchunk - 1) * ne + ec);
-    float v = 0.f;
-#pragma unroll
-    for (int c = 0; c < 8; c++)
-      if (c < nchunk) v += pc[c];
-    lg[e] = e < ne ? v : -INFINITY;
-  }
-  named_bar(2, 32 * R);
+  const int ne = p.ne, k = p.k, R = (ne + 31) / 32;
   float lv[kPer];
 #pragma unroll
-  for (int i = 0; i < kPer; i++) lv[i] = i < R ? lg[lane + 32 * i] : -INFINITY;
+  for (int i = 0; i < kPer; i++) {
+    const int e = lane + 32 * i;
+    lv[i] = -INFINITY;
+    if (i < R && e < ne) lv[i] = __ldcg(p.s.logit_part + e);
+  }
   float m = -INFINITY;
 #pragma unroll
   for (int i = 0; i < kPer; i++) m = fmaxf(m, lv[i]);
@@ -157,58 +150,69 @@ VDEV void route_warps(const MoeDecodeParams& p, Ctl* ctl, float* lg, float* pw, 
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
-  float* pr = pw + (size_t)warp * ((ne + 3) & ~3);  // rows 16-byte aligned for the float4 scan
   int nvalid = 0;
 #pragma unroll
   for (int i = 0; i < kPer; i++) {
     const int e = lane + 32 * i;
+    unsigned long long kv = 0ull;
     if (i < R && e < ne) {
       const float pe = ex[i] / sm;
-      pr[e] = pe;
-      nvalid += !isnan(pe);
+      if (!isnan(pe)) kv = ((unsigned long long)__float_as_uint(pe) << 32) | (0xffffffffu - (unsigned)e);
     }
+    nvalid += __popc(__ballot_sync(0xffffffffu, kv != 0ull));
+    if (e < np) key[e] = kv;
   }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) nvalid += __shfl_xor_sync(0xffffffffu, nvalid, o);
-  __syncwarp();
-  const int e = 32 * warp + lane;
-  if (e < ne) {
-    const float pe = pr[e];
-    int rank = 0;
-    const float4* pr4 = reinterpret_cast<const float4*>(pr);
-#pragma unroll 4
-    for (int j4 = 0; j4 < ne / 4; j4++) {
-      const float4 q = pr4[j4];
-      const int j = 4 * j4;
-      rank += (q.x > pe) || (q.x == pe && j < e);
-      rank += (q.y > pe) || (q.y == pe && j + 1 < e);
-      rank += (q.z > pe) || (q.z == pe && j + 2 < e);
-      rank += (q.w > pe) || (q.w == pe && j + 3 < e);
-    }
-    for (int j = ne & ~3; j < ne; j++) rank += (pr[j] > pe) || (pr[j] == pe && j < e);
-    if (!isnan(pe) && rank < k) {
-      ctl->ids[rank] = e;
-      ctl->wts[rank] = pe;
-    }
+  for (int t = nvalid + lane; t < k; t += 32) {
+    ctl->ids[t] = -1;
+    ctl->wts[t] = -1.f;
   }
-  if (warp == 0)
-    for (int t = lane; t < k; t += 32)
-      if (t >= nvalid) {
-        ctl->ids[t] = -1;
-        ctl->wts[t] = -1.f;
-      }
 }
 
-// One thread, after the selection is published: the optional
-// renormalisation by the sequential rank-order sum of the weights
-// (gguf_run.c:192), and the selection out.
-VDEV void route_finish(const MoeDecodeParams& p, Ctl* ctl, bool write_out) {
+// route_select (every thread of the CTA): expert e's rank is the number of
+// keys above its own; Q = threads / np threads share an expert, thread q
+// counting the 16-byte key pairs q, q + Q, q + 2Q, ... (the Q threads of an
+// expert read Q adjacent pairs: no bank conflicts), summed across the Q
+// lanes.  Ranks below k are the selection, in rank order, with the
+// probabilities as the weights (renormalisation comes after: route_finish).
+VDEV void route_select(Ctl* ctl, const unsigned long long* key, int np, int k) {
+  const int nthr = blockDim.x, Q = nthr / np;  // np <= 256 <= nthr / 2: Q >= 2, a power of two
+  const int e = threadIdx.x / Q, q = threadIdx.x - e * Q, npair = np / 2 / Q;
+  const unsigned long long ke = key[e];
+  const ulonglong2* k2 = reinterpret_cast<const ulonglong2*>(key) + q;
+  int r0 = 0, r1 = 0, r2 = 0, r3 = 0;
+#pragma unroll 4
+  for (int j = 0; j < npair; j += 2) {  // npair is even (np >= 64)
+    const ulonglong2 v = k2[j * Q], w = k2[(j + 1) * Q];
+    r0 += v.x > ke;
+    r1 += v.y > ke;
+    r2 += w.x > ke;
+    r3 += w.y > ke;
+  }
+  int rank = (r0 + r1) + (r2 + r3);
+  for (int o = Q >> 1; o; o >>= 1) rank += __shfl_xor_sync(0xffffffffu, rank, o);
+  if (q == 0 && ke != 0ull && rank < k) {
+    ctl->ids[rank] = e;
+    ctl->wts[rank] = __uint_as_float((unsigned)(ke >> 32));
+  }
+}
+
+// One warp, after the selection is published: the optional renormalisation
+// by the sequential rank-order sum of the weights (gguf_run.c:192), -1 slots
+// included as the reference adds them, and the selection out.
+VDEV void route_finish(const MoeDecodeParams& p, Ctl* ctl, int lane, bool write_out) {
   const int k = p.k;
   float ws = 0.f;
 #pragma unroll 1
-  for (int j = 0; j < k; j++) ws = ws + ctl->wts[j];
-#pragma unroll 1
-  for (int t = 0; t < k; t++) {
+  for (int j0 = 0; j0 < k; j0 += 8) {
+    float w8[8];  // eight loads in flight, then the adds in order
+#pragma unroll
+    for (int u = 0; u < 8; u++) w8[u] = j0 + u < k ? ctl->wts[j0 + u] : 0.f;
+#pragma unroll
+    for (int u = 0; u < 8; u++)
+      if (j0 + u < k) ws = ws + w8[u];
+  }
+  __syncwarp();
+  for (int t = lane; t < k; t += 32) {
     float w = ctl->wts[t];
     if (p.renorm && ws > 0.f) w = w / ws;
     ctl->wts[t] = w;
@@ -217,6 +221,7 @@ VDEV void route_finish(const MoeDecodeParams& p, Ctl* ctl, bool write_out) {
       if (p.wts_out) p.wts_out[t] = w;
     }
   }
+  __syncwarp();
 }
 
 // Bounded wait on a phase with no early exit on abort: used where bulk
@@ -279,6 +284,17 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
   const int G = gridDim.x, cta = blockIdx.x;
   const int d = p.d, fe = p.fe, ne = p.ne, k = p.k, S = p.nstages;
   MoeSync* sy = p.s.sync;
+  // This CTA's share of the work (known before the route, and worked out
+  // here, off the serial path): group t (the expert of rank t) = CTAs
+  // [t G / k, (t + 1) G / k), i.e. t = ((cta + 1) k - 1) / G; CTA j of the m
+  // in the group takes an even share of the expert's fe / 8 gate/up units
+  // and of its d / 16 down tiles.
+  const int t = ((cta + 1) * k - 1) / G;
+  const int c0 = t * G / k, c1 = (t + 1) * G / k;
+  const int m = c1 - c0, j = cta - c0;
+  const int U = fe / 8, NT = d / 16, P = p.dtiles;
+  const int u0 = j * U / m, u1 = (j + 1) * U / m;
+  const int i0 = j * NT / m, i1 = (j + 1) * NT / m;
 
   if (threadIdx.x == 0) {
     trace(p, kTrStart);
@@ -319,90 +335,92 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
     __syncthreads();
     if (threadIdx.x == 0) trace(p, kTrRouted);
   } else {
-    // ---- phase R: router partial dot products --------------------------------
-    // Router rows are weights (independent of the previous kernel): their loads
-    // are issued before waiting on the previous kernel in the stream.
+    // ---- phase R: router logits, one warp per expert ----------------------------
+    // A warp takes expert e's whole row against x (staged once in shared
+    // memory): each lane's products over the row in order, then an xor tree
+    // across the warp; the logit goes to scratch.  The row's first four
+    // 512-value chunks are weights (independent of the previous kernel):
+    // their loads are issued before waiting on the previous kernel.
     const int nchunk = d / kRouterChunk;
-    const int ntask = ne * nchunk, nw = G * (int)(blockDim.x / 32);
-    const int gw = warp * G + cta;  // spread tasks over all CTAs first
-    float4 r0[4], r1[4];
-    const bool has0 = gw < ntask, has1 = gw + nw < ntask;
-    if (has0) {
-      const int e = gw / nchunk, c = gw - e * nchunk;
-      const float4* row = reinterpret_cast<const float4*>(p.router + (size_t)e * d + (size_t)c * kRouterChunk);
+    const int nw = G * (int)(blockDim.x / 32);
+    const int gw = warp * G + cta;  // spread experts over all CTAs first
+    constexpr int kPre = 4;         // chunks held in registers across the wait
+    float4 rp[kPre][4];
+    if (gw < ne) {
 #pragma unroll
-      for (int i = 0; i < 4; i++) r0[i] = __ldg(row + lane + 32 * i);
-    }
-    if (has1) {
-      const int t1 = gw + nw, e = t1 / nchunk, c = t1 - e * nchunk;
-      const float4* row = reinterpret_cast<const float4*>(p.router + (size_t)e * d + (size_t)c * kRouterChunk);
+      for (int c = 0; c < kPre; c++)
+        if (c < nchunk) {
+          const float4* row = reinterpret_cast<const float4*>(p.router + (size_t)gw * d + (size_t)c * kRouterChunk);
 #pragma unroll
-      for (int i = 0; i < 4; i++) r1[i] = __ldg(row + lane + 32 * i);
+          for (int i = 0; i < 4; i++) rp[c][i] = __ldg(row + lane + 32 * i);
+        }
     }
     pdl_wait();
     if (threadIdx.x == 0) trace(p, kTrPdl);
+    const float* xsm = reinterpret_cast<const float*>(xt.tab);
     stage_vec(p.hb, reinterpret_cast<float*>(xt.tab), d, threadIdx.x, blockDim.x, false);
-    for (int task = gw, it = 0; task < ntask; task += nw, it++) {
-      const int e = task / nchunk, c = task - e * nchunk;
-      float4 r[4];
-      if (it == 0) {
-#pragma unroll
-        for (int i = 0; i < 4; i++) r[i] = r0[i];
-      } else if (it == 1) {
-#pragma unroll
-        for (int i = 0; i < 4; i++) r[i] = r1[i];
-      } else {
-        const float4* row = reinterpret_cast<const float4*>(p.router + (size_t)e * d + (size_t)c * kRouterChunk);
-#pragma unroll
-        for (int i = 0; i < 4; i++) r[i] = __ldg(row + lane + 32 * i);
-      }
-      const float4* xv = reinterpret_cast<const float4*>(p.hb + (size_t)c * kRouterChunk);
-      float sdot = 0.f;
-#pragma unroll
-      for (int i = 0; i < 4; i++) {
-        const float4 xx = __ldg(xv + lane + 32 * i);
-        sdot = fmaf(r[i].x, xx.x, sdot);
-        sdot = fmaf(r[i].y, xx.y, sdot);
-        sdot = fmaf(r[i].z, xx.z, sdot);
-        sdot = fmaf(r[i].w, xx.w, sdot);
-      }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) sdot += __shfl_xor_sync(0xffffffffu, sdot, o);
-      if (lane == 0) p.s.logit_part[(size_t)c * ne + e] = sdot;
-    }
     __syncthreads();
-    // every CTA has written its router partials once router_arrive == G
-    if (threadIdx.x == 0) {
+    for (int e = gw; e < ne; e += nw) {
+      float v = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < nchunk; c++) {
+        float4 r[4];
+        if (e == gw && c < kPre) {
+#pragma unroll
+          for (int cc = 0; cc < kPre; cc++)
+            if (cc == c) {
+#pragma unroll
+              for (int i = 0; i < 4; i++) r[i] = rp[cc][i];
+            }
+        } else {
+          const float4* row = reinterpret_cast<const float4*>(p.router + (size_t)e * d + (size_t)c * kRouterChunk);
+#pragma unroll
+          for (int i = 0; i < 4; i++) r[i] = __ldg(row + lane + 32 * i);
+        }
+        const float4* xv = reinterpret_cast<const float4*>(xsm + (size_t)c * kRouterChunk);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const float4 xx = xv[lane + 32 * i];
+          v = fmaf(r[i].x, xx.x, v);
+          v = fmaf(r[i].y, xx.y, v);
+          v = fmaf(r[i].z, xx.z, v);
+          v = fmaf(r[i].w, xx.w, v);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) p.s.logit_part[e] = v;
+    }
+    __syncthreads();  // this CTA's logits are written
+    if (warp == W && lane == 0) {
       trace(p, kTrRouterDone);
       red_add_release_gpu(&sy->router_arrive.v, 1u);
-    }
-    // x table (in place over the staged x) while the other CTAs finish
-    build_tables<SG>(reinterpret_cast<const float*>(xt.tab), xt, d / kSegElems, warp, (int)(blockDim.x / 32), lane);
-    if (threadIdx.x == 0) {
       if (!wait_geq(&sy->router_arrive.v, (unsigned)G, p.s.err)) ctl->abort = 1;
       trace(p, kTrPartials);
     }
+    __syncthreads();  // every CTA's logits are in (or the wait gave up)
+    // selection keys in the h table area (idle until the down phase)
+    int np = 64;
+    while (np < ne) np <<= 1;
+    unsigned long long* key = reinterpret_cast<unsigned long long*>(ht.tab);
+    const bool go = !aborted(ctl);
+    if (go && warp == 0) route_keys(p, ctl, key, np, lane);
     __syncthreads();
-    // logits and probabilities in the h table area (idle until the down phase)
-    const int R = (ne + 31) / 32;
-    if (warp < R && !aborted(ctl)) {
-      float* lg = reinterpret_cast<float*>(ht.tab);
-      route_warps(p, ctl, lg, lg + 32 * R, warp, lane);
+    if (go) route_select(ctl, key, np, k);
+    __syncthreads();  // the selection (weights not yet renormalised)
+    if (warp == W) {
+      if (lane == 0) trace(p, kTrRouted);
+    } else {
+      // consumer warp 0 renormalises the weights and writes the selection
+      // out while the others build the x tables (in place over the staged
+      // x); the producer starts on the copies at once
+      if (warp == 0 && go) route_finish(p, ctl, lane, cta == 0);
+      build_tables<SG>(xsm, xt, d / kSegElems, warp, W, lane);
+      named_bar(1, NC);
     }
-    __syncthreads();
-    if (threadIdx.x == 0) trace(p, kTrRouted);
   }
 
-  // ---- this CTA's share of one selected expert ---------------------------------
-  // group t (the expert of rank t) = CTAs [t G / k, (t + 1) G / k), i.e.
-  // t = ((cta + 1) k - 1) / G; CTA j of the m in the group takes an even
-  // share of the expert's fe / 8 gate/up units and of its d / 16 down tiles
-  const int t = ((cta + 1) * k - 1) / G;
-  const int c0 = t * G / k, c1 = (t + 1) * G / k;
-  const int m = c1 - c0, j = cta - c0;
-  const int U = fe / 8, NT = d / 16, P = p.dtiles;
-  const int u0 = j * U / m, u1 = (j + 1) * U / m;
-  const int i0 = j * NT / m, i1 = (j + 1) * NT / m;
+  // ---- this CTA's share of the selected expert of rank t ----------------------
   const bool active = !aborted(ctl) && ctl->ids[t] >= 0;
   const int nG = active ? u1 - u0 : 0, nD = i1 - i0;  // an unused slot still counts its tiles
   const int nDI = active ? (nD + P - 1) / P : 0;    // down items (up to P tiles per stage)
@@ -457,8 +475,6 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
   const int nsg = d / kSegElems, nsd = fe / kSegElems;
   BFrag bf;
   bf.reset();
-  if (threadIdx.x == 0 && !ROUTED && !aborted(ctl)) route_finish(p, ctl, cta == 0);
-  named_bar(1, NC);  // the renormalised weights before any combine reads them
 
   // count one finished down tile; the last of the k experts to finish it
   // combines them in the reference's order (acc = sum over rank tt of
@@ -512,66 +528,104 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
     if (threadIdx.x == 0) trace(p, kTrHtab);
   };
 
-  // ---- gate/up units: unit i to warp i mod W, its segments in order ----------
+  // Units and tiles go to warp groups; with pairs, warp 2q + hf of pair q
+  // runs half hf of the segments (the first half the lower ones), the pair adds the two
+  // halves' row sums in that order through shared memory (a double buffer
+  // by iteration parity, so a warp one iteration ahead never overwrites
+  // sums its partner has not read), and warp 2q finishes the row values.
+  // Warps per unit or tile: two for Q8_0 gate/up rows (the heaviest
+  // segment kernel: a pair halves the per-unit latency that bounds the ring's
+  // turnover), one for the lighter formats, where the pair's exchange cost
+  // more than it saved (measured on the OLMoE- and Qwen3-shaped layers).
+  constexpr int WPU = std::is_same<SG, SegQ8>::value ? 2 : 1;
+  constexpr int NP = W / WPU;  // warp groups; with pairs, a last odd warp idles in these phases
+  const int q = warp / WPU, hf = warp % WPU;
+  float* pbuf = reinterpret_cast<float*>(smem + p.off_part) + (WPU == 2 ? q * 32 : 0);  // [2 parities][16]
+  auto pair_sum = [&](float& v0, float& v1, int iter) {
+    if constexpr (WPU == 1) return;
+    float* pb = pbuf + 16 * (iter & 1);
+    if (hf && L.t == 0) {
+      pb[L.g] = v0;
+      pb[8 + L.g] = v1;
+    }
+    named_bar(4 + q, 64);
+    if (!hf && L.t == 0) {
+      v0 += pb[L.g];
+      v1 += pb[8 + L.g];
+    }
+  };
+
+  // ---- gate/up units: unit i to pair i mod NP ----------------------------------
+  const int nsg_lo = WPU == 2 ? nsg / 2 : nsg, nsd_lo = WPU == 2 ? nsd / 2 : nsd;
+  if (q < NP) {
 #pragma unroll 1
-  for (int i = warp; i < nG; i += W) {
-    const int slot = i % S;
-    const bool ok = item_wait(full, ctl, p.s.err, i, S);
-    if (p.trace && lane == 0 && i < kTrItems) atomicMin(&ctl->it_land[i], now_ns());
-    const uint8_t* st = stages + (size_t)slot * p.stage_bytes;
-    const uint8_t* r0 = stage_row(st, p.sg_gu, L.g);
-    const uint8_t* r1 = stage_row(st, p.sg_gu, L.g + 8);
-    float gs = 0.f, us = 0.f;
-    if (ok)
+    for (int i = q, it = 0; i < nG; i += NP, it++) {
+      const int slot = i % S;
+      const bool ok = item_wait(full, ctl, p.s.err, i, S);
+      if (p.trace && lane == 0 && !hf && i < kTrItems) atomicMin(&ctl->it_land[i], now_ns());
+      const uint8_t* st = stages + (size_t)slot * p.stage_bytes;
+      const uint8_t* r0 = stage_row(st, p.sg_gu, L.g);
+      const uint8_t* r1 = stage_row(st, p.sg_gu, L.g + 8);
+      float gs = 0.f, us = 0.f;
+      if (ok)
 #pragma unroll 1
-      for (int seg = 0; seg < nsg; seg++) seg_dot<SG>(r0, r1, seg, xt, L, bf, gs, us);
-    gs += __shfl_xor_sync(0xffffffffu, gs, 1);
-    us += __shfl_xor_sync(0xffffffffu, us, 1);
-    gs += __shfl_xor_sync(0xffffffffu, gs, 2);
-    us += __shfl_xor_sync(0xffffffffu, us, 2);
-    // lane (g, 0) holds gate row g and its up row (rows g and g + 8 of the
-    // unit): the reference's SwiGLU, gguf_run.c:206
-    if (L.t == 0 && ok) p.s.hbuf[(size_t)t * fe + 8 * (u0 + i) + L.g] = (gs / (1.0f + expf(-gs))) * us;
-    __syncwarp();
-    if (p.trace && lane == 0 && i < kTrItems) atomicMax(&ctl->it_done[i], now_ns());
-    if (lane == 0) mbar_arrive(&empty[slot]);
+        for (int seg = hf ? nsg_lo : 0; seg < (hf ? nsg : nsg_lo); seg++) seg_dot<SG>(r0, r1, seg, xt, L, bf, gs, us);
+      gs += __shfl_xor_sync(0xffffffffu, gs, 1);
+      us += __shfl_xor_sync(0xffffffffu, us, 1);
+      gs += __shfl_xor_sync(0xffffffffu, gs, 2);
+      us += __shfl_xor_sync(0xffffffffu, us, 2);
+      pair_sum(gs, us, it);  // both warps are done with the stage past this point
+      if (!hf) {
+        // lane (g, 0) holds gate row g and its up row (rows g and g + 8 of
+        // the unit): the reference's SwiGLU, gguf_run.c:206
+        if (L.t == 0 && ok) p.s.hbuf[(size_t)t * fe + 8 * (u0 + i) + L.g] = (gs / (1.0f + expf(-gs))) * us;
+        __syncwarp();
+        if (p.trace && lane == 0 && i < kTrItems) atomicMax(&ctl->it_done[i], now_ns());
+        if (lane == 0) mbar_arrive(&empty[slot]);
+      }
+    }
   }
   if (nDI > 0)
     g_to_d(true);
   else if (active)
     g_to_d(false);  // no down tiles here: publish the units only
 
-  // ---- down tiles: the CTA's tile u to warp u mod W; the last tile of an
+  // ---- down tiles: the CTA's tile u to pair u mod NP; the last tile of an
   // item to finish releases its stage ------------------------------------------
   const int nDT = nDI > 0 ? nD : 0;
+  if (q < NP) {
 #pragma unroll 1
-  for (int u = warp; u < nDT; u += W) {
-    const int i = nG + u / P, tt = u - (u / P) * P;
-    const int slot = i % S;
-    const int nt = min(P, nD - (i - nG) * P);
-    const bool ok = item_wait(full, ctl, p.s.err, i, S);
-    if (p.trace && lane == 0 && i < kTrItems) atomicMin(&ctl->it_land[i], now_ns());
-    const uint8_t* base = stages + (size_t)slot * p.stage_bytes + (size_t)tt * p.dslot_bytes;
-    const uint8_t* r0 = stage_row(base, p.sg_d, L.g);
-    const uint8_t* r1 = stage_row(base, p.sg_d, L.g + 8);
-    float y0 = 0.f, y1 = 0.f;
-    if (ok)
+    for (int u = q, it = 0; u < nDT; u += NP, it++) {
+      const int i = nG + u / P, tt = u - (u / P) * P;
+      const int slot = i % S;
+      const int nt = min(P, nD - (i - nG) * P);
+      const bool ok = item_wait(full, ctl, p.s.err, i, S);
+      if (p.trace && lane == 0 && !hf && i < kTrItems) atomicMin(&ctl->it_land[i], now_ns());
+      const uint8_t* base = stages + (size_t)slot * p.stage_bytes + (size_t)tt * p.dslot_bytes;
+      const uint8_t* r0 = stage_row(base, p.sg_d, L.g);
+      const uint8_t* r1 = stage_row(base, p.sg_d, L.g + 8);
+      float y0 = 0.f, y1 = 0.f;
+      if (ok)
 #pragma unroll 1
-      for (int seg = 0; seg < nsd; seg++) seg_dot<SD>(r0, r1, seg, ht, L, bf, y0, y1);
-    y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
-    y1 += __shfl_xor_sync(0xffffffffu, y1, 1);
-    y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
-    y1 += __shfl_xor_sync(0xffffffffu, y1, 2);
-    const int tile = i0 + u;
-    if (L.t == 0 && ok) {
-      p.s.ybuf[(size_t)t * d + 16 * tile + L.g] = y0;
-      p.s.ybuf[(size_t)t * d + 16 * tile + L.g + 8] = y1;
-    }
-    __syncwarp();
-    if (p.trace && lane == 0 && i < kTrItems) atomicMax(&ctl->it_done[i], now_ns());
-    if (lane == 0 && atomicAdd(&ucnt[slot * kMaxDTiles], 1) == nt - 1) {
-      ucnt[slot * kMaxDTiles] = 0;
-      mbar_arrive(&empty[slot]);
+        for (int seg = hf ? nsd_lo : 0; seg < (hf ? nsd : nsd_lo); seg++) seg_dot<SD>(r0, r1, seg, ht, L, bf, y0, y1);
+      y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
+      y1 += __shfl_xor_sync(0xffffffffu, y1, 1);
+      y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
+      y1 += __shfl_xor_sync(0xffffffffu, y1, 2);
+      pair_sum(y0, y1, it);
+      if (!hf) {
+        const int tile = i0 + u;
+        if (L.t == 0 && ok) {
+          p.s.ybuf[(size_t)t * d + 16 * tile + L.g] = y0;
+          p.s.ybuf[(size_t)t * d + 16 * tile + L.g + 8] = y1;
+        }
+        __syncwarp();
+        if (p.trace && lane == 0 && i < kTrItems) atomicMax(&ctl->it_done[i], now_ns());
+        if (lane == 0 && atomicAdd(&ucnt[slot * kMaxDTiles], 1) == nt - 1) {
+          ucnt[slot * kMaxDTiles] = 0;
+          mbar_arrive(&empty[slot]);
+        }
+      }
     }
   }
   // count this CTA's tiles, one warp per tile, all at once (the down rows
@@ -786,8 +840,9 @@ uint32_t moe_decode_layout(MoeDecodeParams* p, uint32_t smem_limit, int grid) {
   p->stage_bytes = stage;
   p->dslot_bytes = dslot;
   p->dtiles = (int)dt;
-  const int nsg = p->d / kSegElems, nsd = p->fe / kSegElems, R = (p->ne + 31) / 32;
-  p->maxp = 0;  // (tile, segment) partials: none (a warp takes a whole unit or tile)
+  const int nsg = p->d / kSegElems, nsd = p->fe / kSegElems;
+  int np = 64;  // the routing keys: ne rounded up to a power of two
+  while (np < p->ne) np <<= 1;
   (void)nsg;
   (void)nsd;
   uint32_t off = 2u * kMaxStages * 8u;  // full/empty barriers
@@ -805,8 +860,8 @@ uint32_t moe_decode_layout(MoeDecodeParams* p, uint32_t smem_limit, int grid) {
   off = up_to(off + (uint32_t)(nsg * kResTabBytes), 16);
   p->off_xrmeta = off;
   off = up_to(off + (uint32_t)(nsg * kMeta * 4), 16);
-  p->off_htab = off;  // one expert's h tables; the routing warps' logits and probabilities before that
-  off = up_to(off + (uint32_t)std::max(nsd * kSegTabBytes, 4 * (32 * R + R * ((p->ne + 3) & ~3))), 16);
+  p->off_htab = off;  // one expert's h tables; the routing keys before that
+  off = up_to(off + (uint32_t)std::max(nsd * kSegTabBytes, 8 * std::max(64, np)), 16);
   p->off_hmeta = off;
   off = up_to(off + (uint32_t)(nsd * kMeta * 4), 16);
   p->off_hrtab = off;
@@ -815,9 +870,10 @@ uint32_t moe_decode_layout(MoeDecodeParams* p, uint32_t smem_limit, int grid) {
   off = up_to(off + (uint32_t)(nsd * kMeta * 4), 16);
   p->off_xs = off;  // residual rows of a CTA's tiles: at most d / 16 / floor(grid / k) + 1 tiles
   off = up_to(off + (uint32_t)(64 * (p->d / 16 / std::max(1, grid / std::max(1, p->k)) + 1)), 16);
-  p->off_part = off;
+  p->off_part = off;  // warp pairs' row-sum exchange: [pairs][2 parities][16] floats
+  off = up_to(off + (uint32_t)(kConsumerWarps / 2 * 32 * 4), 16);
   for (int S = kMaxStages; S >= 2; S--) {
-    const uint32_t st = up_to(off + (uint32_t)(S * p->maxp * 64), 128);
+    const uint32_t st = up_to(off, 128);
     const uint32_t total = st + (uint32_t)S * stage;
     if (total <= smem_limit) {
       p->nstages = S;
@@ -835,7 +891,7 @@ size_t moe_scratch_bytes(int d, int fe, int ne, int k) {
   off = up256s(off + sizeof(MoeSync));
   off = up256s(off + sizeof(int));                                       // status
   off = up256s(off + (size_t)(d / 16) * kTileCntStride * 4);              // tile counters
-  off = up256s(off + 4 * (size_t)(d / kRouterChunk) * ne);                // router partials
+  off = up256s(off + 4 * (size_t)ne);                                     // router logits
   off = up256s(off + 4 * (size_t)k * fe);                                 // h
   off = up256s(off + 4 * (size_t)k * d);                                  // down outputs
   return off;
@@ -850,7 +906,7 @@ void moe_scratch_carve(uint8_t* base, int d, int fe, int ne, int k, int* err, Mo
   s->tile_cnt = (unsigned int*)(base + off);
   off = up256s(off + (size_t)(d / 16) * kTileCntStride * 4);
   s->logit_part = (float*)(base + off);
-  off = up256s(off + 4 * (size_t)(d / kRouterChunk) * ne);
+  off = up256s(off + 4 * (size_t)ne);
   s->hbuf = (float*)(base + off);
   off = up256s(off + 4 * (size_t)k * fe);
   s->ybuf = (float*)(base + off);

@@ -7,22 +7,26 @@
 // weighted combine in rank order (:209) and the residual add (:213).
 //
 // One CTA per SM, every CTA resident (each cross-CTA wait is bounded).
-//   R  router partial dot products, 512-value K chunks, one warp per task
-//      -> grid arrival counter -> every CTA: one warp per 32 experts sums the
-//      partials in chunk order, takes the softmax and ranks the top-k.
+//   R  router logits, one warp per expert row (512-value chunks summed in
+//      order) -> grid arrival counter -> in every CTA the producer warp
+//      reads the ne logits, takes the softmax and selects the top-k
+//      (k rounds of a warp arg-max) while the consumer warps build the
+//      activation tables of x.
 //   The CTAs are then split into k groups, group t serving the expert of
 //   rank t.  A CTA of group t streams, through one ring of shared-memory
 //   stages, its share of that expert's gate/up units (8 gate + 8 up rows)
 //   and then its share of the expert's down tiles (16 rows; several per
 //   stage), so the down rows arrive while gate/up is still computed.
-//   G  unit i to consumer warp i mod W, which runs all of its segments and
-//      writes h = silu(g) * u for its 8 rows to scratch; the group counts
-//      finished units.
+//   G  unit i to consumer warp group i mod (W / g) (g = 2 warps for Q8_0
+//      gate/up rows, each running half of the segments and adding the
+//      halves; g = 1 otherwise), which writes h = silu(g) * u for its 8 rows
+//      to scratch; the group counts finished units.
 //   D  once the group's units are all counted, the CTA stages the expert's h
-//      and builds its activation tables; down tile u to warp u mod W, which
-//      writes its 16 outputs to scratch; then every tile is counted and the
-//      last of the k groups to finish a tile combines the k experts' rows in
-//      rank order and adds them into the residual.
+//      and builds its activation tables; down tile u to warp group
+//      u mod (W / g), which writes its 16 outputs to scratch; then every
+//      tile is counted and the last of the k groups to finish a tile
+//      combines the k experts' rows in rank order and adds them into the
+//      residual.
 #pragma once
 #include <stdint.h>
 
@@ -56,7 +60,7 @@ struct MoeSync {
 
 // Device scratch of one layer handle (or of the fixed no-allocation array).
 struct MoeScratch {
-  float* logit_part;        // [d/512][ne] router partials
+  float* logit_part;        // [ne] router logits
   float* hbuf;              // [k][fe] h rows of the selected experts
   float* ybuf;              // [k][d] down outputs of the selected experts
   unsigned int* tile_cnt;   // [d/16][kTileCntStride]: expert rows finished per 16-row tile; back to 0 by the combiner
@@ -78,7 +82,6 @@ struct MoeDecodeParams {
   int nstages;
   uint32_t dslot_bytes;  // one down tile inside a stage
   int dtiles;            // down tiles per stage
-  int maxp;              // shared partials per stage (0: a warp takes a whole unit or tile)
   // shared-memory offsets (bytes)
   uint32_t off_ctl, off_etab, off_ucnt, off_part, off_xtab, off_xmeta, off_xrtab, off_xrmeta, off_htab, off_hmeta,
       off_hrtab, off_hrmeta, off_xs, off_stage;

@@ -34,11 +34,11 @@ namespace vireo {
 namespace {
 
 // 256 KiB.  A layer needs the sync words (16.9 KiB), the status word, 128 B
-// per 16 output rows of tile counters, 4 B per (512-value chunk, expert) of
-// router partials, 4 B per value of the k selected experts' h rows and of
-// their d outputs, and 24 B per expert of pointers: 131 KiB for the
-// OLMoE-shaped layer (d 2048, 64 experts top-8, fe 1024), 128 KiB for the
-// Qwen3-shaped one.  A layer needing more is refused with VIREO_ERR_NOMEM.
+// per 16 output rows of tile counters, 4 B per expert of router logits, 4 B
+// per value of the k selected experts' h rows and of their d outputs, and
+// 24 B per expert of pointers: 130.5 KiB for the OLMoE-shaped layer (d 2048,
+// 64 experts top-8, fe 1024), 124.3 KiB for the Qwen3-shaped one.  A layer
+// needing more is refused with VIREO_ERR_NOMEM.
 constexpr size_t kNoAllocScratchBytes = 256 * 1024;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
