@@ -5,6 +5,7 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <algorithm>
 #include <mutex>
 #include <unordered_set>
 #include <vector>
@@ -393,6 +394,7 @@ struct gguf_moe {
   // memory: hb [n][d] | x [n][d] | status (16 B) | ids [n][k] | wts [n][k]
   uint8_t* d_io = nullptr;
   uint8_t* h_io = nullptr;
+  uint8_t* h_io_dev = nullptr;  // h_io as the device addresses it (mapped pinned memory)
   void* owned[4] = {};  // device copies of the layer's tensors (gguf_moe_create_host)
   int io_cap = 0;
   bool pdl = true;
@@ -561,6 +563,17 @@ int gguf_moe_create_host(const gguf_moe_desc* desc, gguf_moe** out) {
 // holding the SMs; every such wait is bounded, so a launch that shares the
 // GPU with another kernel that holds SMs ends with VIREO_ERR_TIMEOUT instead
 // of hanging.
+// The host call's input copy: the hidden rows from mapped pinned memory into
+// device memory (the decode kernel's CTAs all read them), and the status
+// word zeroed.  It lets the next kernel launch at once; that kernel's
+// griddepcontrol.wait orders its reads after this copy.
+__global__ void host_stage_kernel(const float4* src, float4* dst, size_t n4, int* status) {
+  pdl_launch_dependents();
+  if (blockIdx.x == 0 && threadIdx.x == 0) *status = 0;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = src[i];
+}
+
 static int moe_launch(gguf_moe* m, const void* kernel, void** args, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(m->grid);
@@ -582,12 +595,14 @@ static int moe_launch(gguf_moe* m, const void* kernel, void** args, cudaStream_t
   return cuda_status(e);
 }
 
-// n_tok decode launches; the kernels record failures in *err
+// n_tok decode launches; the kernels record failures in *err (and, when
+// err_out is given, the last launch's last CTA reports there: status, done)
 static int moe_ffn_launches(gguf_moe* m, const float* hb, float* x, int n_tok, int32_t* ids, float* wts,
-                            cudaStream_t s, int* err) {
+                            cudaStream_t s, int* err, int* err_out = nullptr) {
   MoeDecodeParams p = m->prm;
   p.s.err = err;
   for (int i = 0; i < n_tok; i++) {
+    p.err_out = i == n_tok - 1 ? err_out : nullptr;
     p.hb = hb + (size_t)i * p.d;
     p.x = x + (size_t)i * p.d;
     p.ids_out = ids ? ids + (size_t)i * p.k : nullptr;
@@ -715,26 +730,54 @@ int gguf_moe_ffn_host(gguf_moe* m, const float* hb, float* x, int n_tok, int32_t
     cudaFreeHost(m->h_io);
     m->d_io = nullptr;
     m->h_io = nullptr;
+    m->h_io_dev = nullptr;
     m->io_cap = 0;
+    void* hd = nullptr;
     if ((st = cuda_status(cudaMalloc(&m->d_io, total))) ||
-        (st = cuda_status(cudaMallocHost(&m->h_io, total))))
+        (st = cuda_status(cudaHostAlloc(&m->h_io, total, cudaHostAllocMapped))) ||
+        (st = cuda_status(cudaHostGetDevicePointer(&hd, m->h_io, 0))))
       return st;
+    m->h_io_dev = (uint8_t*)hd;
     m->io_cap = n_tok;
   }
   cudaStream_t s = m->stream;
-  // the previous call's device-to-host copy has completed (that call synchronised)
+  // One round trip through mapped pinned memory, no copy-engine transfers:
+  // the previous call synchronised, so the buffer is free.  The hidden rows
+  // go to device memory by a staging kernel; the residual rows are read and
+  // written, and the selection written, by the decode kernels in host
+  // memory directly (each CTA touches only its own rows); the status word
+  // comes back through the last CTA of each launch.
   memcpy(m->h_io, hb, n * d * 4);
   memcpy(m->h_io + o_x, x, n * d * 4);
   memset(m->h_io + o_st, 0, 16);
-  if ((st = cuda_status(cudaMemcpyAsync(m->d_io, m->h_io, o_st + 16, cudaMemcpyHostToDevice, s)))) return st;
   int* d_status = (int*)(m->d_io + o_st);
-  st = moe_ffn_launches(m, (const float*)m->d_io, (float*)(m->d_io + o_x), n_tok, (int32_t*)(m->d_io + o_ids),
-                        (float*)(m->d_io + o_wts), s, d_status);
+  const size_t n4 = n * d / 4;
+  const int sg = (int)std::min<size_t>((n4 + 511) / 512, (size_t)m->num_sms);
+  host_stage_kernel<<<sg, 512, 0, s>>>((const float4*)m->h_io_dev, (float4*)m->d_io, n4, d_status);
+  st = cuda_status(cudaGetLastError());
   if (!st)
-    st = cuda_status(cudaMemcpyAsync(m->h_io + o_x, m->d_io + o_x, total - o_x, cudaMemcpyDeviceToHost, s));
-  const int sync = cuda_status(cudaStreamSynchronize(s));
-  if (st) return st;
-  if (sync) return sync;
+    st = moe_ffn_launches(m, (const float*)m->d_io, (float*)(m->h_io_dev + o_x), n_tok,
+                          (int32_t*)(m->h_io_dev + o_ids), (float*)(m->h_io_dev + o_wts), s, d_status,
+                          (int*)(m->h_io_dev + o_st));
+  if (st) {
+    cudaStreamSynchronize(s);
+    return st;
+  }
+  // the last CTA's done word: it follows every output (the kernel fences its
+  // host writes system-wide first), so the call returns without waiting for
+  // the launch to be retired; the stream is still polled now and then, so a
+  // launch that failed outright is reported instead of awaited
+  volatile int* done = (volatile int*)(m->h_io + o_st + 4);
+  for (long it = 0; !*done; it++) {
+    if ((it & 4095) == 4095) {
+      const cudaError_t q = cudaStreamQuery(s);
+      if (q == cudaSuccess) {
+        if (!*done) return VIREO_ERR_CUDA;  // retired without reporting
+        break;
+      }
+      if (q != cudaErrorNotReady) return cuda_status(q);
+    }
+  }
   int herr = 0;
   memcpy(&herr, m->h_io + o_st, sizeof(int));
   if (herr) {

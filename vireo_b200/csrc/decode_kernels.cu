@@ -644,7 +644,16 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
   // ---- launch exit: the last CTA out resets the per-launch words -------------
   named_bar(1, NC);
   if (threadIdx.x == 0) {
+    // host-memory outputs (the host entry's residual rows and selection) are
+    // visible system-wide before this CTA counts out, so the word the last
+    // CTA writes tells the host that every output is in place
+    if (p.err_out) __threadfence_system();
     if (atom_add_acq_rel_gpu(&sy->exit_cnt.v, 1u) == (unsigned)G - 1u) {
+      if (p.err_out) {
+        reinterpret_cast<volatile int*>(p.err_out)[0] = *reinterpret_cast<volatile int*>(p.s.err);
+        __threadfence_system();
+        reinterpret_cast<volatile int*>(p.err_out)[1] = 1;  // done
+      }
       sy->router_arrive.v = 0u;
       for (int tt = 0; tt < k; tt++) sy->group[tt].v = 0u;
       __threadfence();

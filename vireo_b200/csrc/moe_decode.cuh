@@ -86,6 +86,8 @@ struct MoeDecodeParams {
   uint32_t off_ctl, off_etab, off_ucnt, off_part, off_xtab, off_xmeta, off_xrtab, off_xrmeta, off_htab, off_hmeta,
       off_hrtab, off_hrmeta, off_xs, off_stage;
   unsigned long long* trace;  // optional: kTraceSlots %globaltimer stamps per CTA
+  int* err_out;               // optional, mapped host memory: the last CTA out writes the status word to
+                              // [0], then 1 to [1]
 };
 
 // Scratch bytes of a layer and the pointers into a block of that size (256-
