@@ -24,7 +24,7 @@ namespace vireo {
 
 constexpr int kDecThreads = 1024;
 constexpr int kAttnChunk = 128;  // cached positions per attention CTA (one per thread)
-constexpr int kCombThreads = 1024;  // threads of the chunk-merging kernel
+constexpr int kCombThreads = 128;  // threads of the chunk-merging kernel
 // positions a cache may hold: the merging kernel keeps a weight per chunk in
 // (at most 48 KB of) shared memory
 constexpr int kMaxCtx = (48 * 1024 / 4 - kCombThreads) * kAttnChunk;
@@ -105,7 +105,9 @@ struct AttnParams {
   int nh, nkv, hs, pos, npos, max_ctx, nchunk;
   float scale, eps;
   float* part;  // [nh][nchunk][hs + 2]: acc, m, l
-  int* err;     // status word (tensor-core path: a copy that never landed)
+  int* err;     // status word (tensor-core path: a copy or a merge that timed out)
+  unsigned int* cnt;  // tensor-core path: per kv head, [0] chunks written, [1] merges done (zero between launches)
+  float* out;         // tensor-core path: the merged attention output [nh][hs]
 };
 
 VDEV float kv_load(const float* p, size_t i) { return p[i]; }
@@ -392,6 +394,7 @@ constexpr size_t attn_mma_smem() {
   using Ly = AttnMmaLayout<HS>;
   size_t off = Ly::kOffQ + sizeof(float) * (QG * HS + 2 * HS + 32 + 8);
   off += sizeof(float) * kAttnWarps * QG * (HS + 2);  // warp states for the merge
+  off += sizeof(float) * (2 * QG * HS + 4 * HS + 4 * QG);  // RoPE table, norm weights, biases, merge weights
   off = (off + 127) / 128 * 128;
   return off + (size_t)kAttnStages * Ly::kStage;
 }
@@ -410,7 +413,15 @@ __global__ void __launch_bounds__(kAttnMmaThreads) dec_attn_mma(const __grid_con
   float* bred = skv + 2 * HS;                            // [32]
   int* flags = reinterpret_cast<int*>(bred + 32);        // [8]: abort, last
   float* wst = bred + 40;                                // [warps][QG][HS + 2] warp states
-  uint8_t* ring = sm + ((Ly::kOffQ + sizeof(float) * (QG * HS + 2 * HS + 40 + kAttnWarps * QG * (HS + 2)) + 127) /
+  float* rcs = wst + kAttnWarps * QG * (HS + 2);         // [HS]: cos, then sin, of pos * freq[j]
+  float* wqs = rcs + HS;                                 // [QG][HS] q norm weights (per head: [HS])
+  float* wks = wqs + QG * HS;                            // [HS] k norm weights
+  float* bqs = wks + HS;                                 // [QG][HS] q bias (0 without one)
+  float* bks = bqs + QG * HS;                            // [HS] k bias
+  float* bvs = bks + HS;                                 // [HS] v bias
+  float* mw = bvs + HS;                                  // [kAttnWarps][QG] merge weights
+  uint8_t* ring = sm + ((Ly::kOffQ + sizeof(float) * (QG * HS + 2 * HS + 40 + kAttnWarps * QG * (HS + 2) +
+                                                      2 * QG * HS + 4 * HS + 4 * QG) + 127) /
                         128 * 128);
   const int c = blockIdx.x, kh = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int h0 = kh * QG;
@@ -431,6 +442,27 @@ __global__ void __launch_bounds__(kAttnMmaThreads) dec_attn_mma(const __grid_con
     if (nold > 0) {
       prefetch_l2(kb + (size_t)p0 * HS, (uint32_t)(nold * HS * 2));
       prefetch_l2(vb + (size_t)p0 * HS, (uint32_t)(nold * HS * 2));
+    }
+  }
+  // weights and this position's RoPE table (independent of the previous
+  // kernel), staged while the projection kernel finishes
+  if (tid < NC) {
+    for (int j = tid; j < HS / 2; j += NC) {
+      const float a = (float)p.pos * p.freq[j];
+      rcs[j] = cosf(a);
+      rcs[HS / 2 + j] = sinf(a);
+    }
+    const bool qfull = p.qn && p.qn_len != HS, kfull = p.kn && p.kn_len != HS;
+    for (int i = tid; i < QG * HS; i += NC) {
+      const size_t gi = (size_t)h0 * HS + i;
+      bqs[i] = p.bq ? p.bq[gi] : 0.f;
+      if (p.qn) wqs[i] = qfull ? p.qn[gi] : p.qn[i % HS];
+    }
+    for (int i = tid; i < HS; i += NC) {
+      const size_t gi = (size_t)kh * HS + i;
+      bks[i] = p.bk ? p.bk[gi] : 0.f;
+      bvs[i] = p.bv ? p.bv[gi] : 0.f;
+      if (p.kn) wks[i] = kfull ? p.kn[gi] : p.kn[i];
     }
   }
   __syncthreads();
@@ -469,15 +501,12 @@ __global__ void __launch_bounds__(kAttnMmaThreads) dec_attn_mma(const __grid_con
   }
 
   // ---- consumers: q heads h0 .. h0 + QG - 1 (and this position's k, v) -------
-  for (int i = tid; i < QG * HS; i += NC) {
-    const size_t gi = (size_t)h0 * HS + i;
-    sq[i] = p.bq ? p.q[gi] + p.bq[gi] : p.q[gi];
-  }
+  for (int i = tid; i < QG * HS; i += NC) sq[i] = p.q[(size_t)h0 * HS + i] + bqs[i];
   if (has_cur)
     for (int i = tid; i < HS; i += NC) {
       const size_t gi = (size_t)kh * HS + i;
-      skv[i] = p.bk ? p.k[gi] + p.bk[gi] : p.k[gi];
-      skv[HS + i] = p.bv ? p.v[gi] + p.bv[gi] : p.v[gi];
+      skv[i] = p.k[gi] + bks[i];
+      skv[HS + i] = p.v[gi] + bvs[i];
     }
   // full-width norms need the whole vector's sum of squares
   float qss = 0.f, kss = 0.f;
@@ -514,7 +543,7 @@ __global__ void __launch_bounds__(kAttnMmaThreads) dec_attn_mma(const __grid_con
         for (int i = lane; i < HS; i += 32) ss += sq[g * HS + i] * sq[g * HS + i];
         ss = warp_sum(ss);
       }
-      norm_head(sq + g * HS, HS, p.qn_len == HS ? p.qn : p.qn + (size_t)(h0 + g) * HS, ss, p.qn_len, p.eps, lane);
+      norm_head(sq + g * HS, HS, wqs + g * HS, ss, p.qn_len, p.eps, lane);
     }
   if (has_cur && p.kn && warp == kAttnWarps - 1) {
     float ss = kss;
@@ -523,11 +552,18 @@ __global__ void __launch_bounds__(kAttnMmaThreads) dec_attn_mma(const __grid_con
       for (int i = lane; i < HS; i += 32) ss += skv[i] * skv[i];
       ss = warp_sum(ss);
     }
-    norm_head(skv, HS, p.kn_len == HS ? p.kn : p.kn + (size_t)kh * HS, ss, p.kn_len, p.eps, lane);
+    norm_head(skv, HS, wks, ss, p.kn_len, p.eps, lane);
   }
   asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
-  rope_heads<HS>(sq, QG, p.pos, p.freq, tid, NC);
-  if (has_cur) rope_heads<HS>(skv, 1, p.pos, p.freq, tid, NC);
+  // NEOX RoPE from the staged table
+  for (int idx = tid; idx < (QG + (has_cur ? 1 : 0)) * (HS / 2); idx += NC) {
+    const int hh = idx / (HS / 2), j = idx - hh * (HS / 2);
+    float* w = hh < QG ? sq + hh * HS : skv;
+    const float c = rcs[j], sn = rcs[HS / 2 + j];
+    const float x0 = w[j], x1 = w[j + HS / 2];
+    w[j] = x0 * c - x1 * sn;
+    w[j + HS / 2] = x0 * sn + x1 * c;
+  }
   asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
   if (has_cur)  // the cache row later steps read (swizzled)
     for (int i = tid; i < HS; i += NC) {
@@ -652,21 +688,98 @@ __global__ void __launch_bounds__(kAttnMmaThreads) dec_attn_mma(const __grid_con
     }
   }
   asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
+  // per (warp, head) weights exp(m_w - M) once, then the weighted sums
+  if (tid < kAttnWarps * QG) {
+    const int w = tid / QG, h = tid - w * QG;
+    float M = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < kAttnWarps; u++) M = fmaxf(M, wst[(u * QG + h) * (HS + 2) + HS]);
+    const float m1 = wst[(w * QG + h) * (HS + 2) + HS];
+    mw[tid] = m1 > -INFINITY ? expf(m1 - M) : 0.f;
+    if (w == 0) bred[h] = M;
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
   float* cp = p.part + (size_t)h0 * p.nchunk * (HS + 2);
   for (int idx = tid; idx < QG * (HS + 2); idx += NC) {
     const int h = idx / (HS + 2), e = idx - h * (HS + 2);
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kAttnWarps; w++) M = fmaxf(M, wst[(w * QG + h) * (HS + 2) + HS]);
     float a = 0.f;
+    if (e == HS) {
+      a = bred[h];
+    } else {
 #pragma unroll
-    for (int w = 0; w < kAttnWarps; w++) {
-      const float mw = wst[(w * QG + h) * (HS + 2) + HS];
-      const float f = mw > -INFINITY ? expf(mw - M) : 0.f;
-      if (e < HS) a += wst[(w * QG + h) * (HS + 2) + e] * f;
-      else if (e == HS + 1) a += wst[(w * QG + h) * (HS + 2) + HS + 1] * f;
+      for (int w = 0; w < kAttnWarps; w++) a += wst[(w * QG + h) * (HS + 2) + e] * mw[w * QG + h];
     }
-    cp[((size_t)h * p.nchunk + c) * (HS + 2) + e] = e == HS ? M : a;
+    cp[((size_t)h * p.nchunk + c) * (HS + 2) + e] = a;
+  }
+
+  // ---- the chunk merge (kv_softmax_finish, kvstore.h:99-101) -----------------
+  // Once every chunk of this kv head has written its state, CTAs c <
+  // min(QG, nchunk) of the kv head merge its q heads h0 + c, h0 + c + nchunk,
+  // ...: thread e on dimension e, every chunk's value in flight at once, the
+  // weights exp(m_c - M) and L = sum l_c exp(m_c - M) in chunk order.  The
+  // last merging CTA puts the two counters back to zero.
+  const int nc = p.nchunk, nmerge = min(QG, nc);
+  __threadfence();
+  asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
+  if (tid == 0) red_add_release_gpu(&p.cnt[2 * kh], 1u);
+  if (c >= nmerge) return;
+  if (tid == 0) flags[1] = wait_geq(&p.cnt[2 * kh], (unsigned)nc, p.err) ? 1 : 0;
+  asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
+  if (flags[1]) {
+    // the ring is idle now (every copy landed and was consumed): chunk
+    // weights f_c and l_c f_c there
+    float* cf = reinterpret_cast<float*>(ring);
+    float* cl = cf + nc;
+    for (int hh = c; hh < QG; hh += nc) {
+      const float* base = p.part + (size_t)(h0 + hh) * nc * (HS + 2);
+      constexpr int kPre = 40;
+      float pre[kPre];
+      if (tid < HS) {
+#pragma unroll
+        for (int u = 0; u < kPre; u++) pre[u] = u < nc ? __ldcg(base + (size_t)u * (HS + 2) + tid) : 0.f;
+      }
+      float mloc = -INFINITY;
+      for (int u = tid; u < nc; u += NC) {
+        const float mc = __ldcg(base + (size_t)u * (HS + 2) + HS);
+        cf[u] = mc;
+        cl[u] = __ldcg(base + (size_t)u * (HS + 2) + HS + 1);
+        mloc = fmaxf(mloc, mc);
+      }
+      mloc = warp_max(mloc);
+      if (lane == 0) bred[warp] = mloc;
+      asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
+      float M = bred[0];
+#pragma unroll
+      for (int w = 1; w < kAttnWarps; w++) M = fmaxf(M, bred[w]);
+      for (int u = tid; u < nc; u += NC) {
+        const float mc = cf[u];
+        const float f = mc > -INFINITY ? expf(mc - M) : 0.f;
+        cf[u] = f;
+        cl[u] *= f;
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
+      if (tid < HS) {
+        float L = 0.f, acc = 0.f;
+        for (int u = 0; u < nc; u++) L += cl[u];
+#pragma unroll
+        for (int u = 0; u < kPre; u++)
+          if (u < nc) acc += pre[u] * cf[u];
+        for (int u0 = kPre; u0 < nc; u0 += 8) {
+          float v8[8];  // eight chunks in flight
+#pragma unroll
+          for (int j = 0; j < 8; j++) v8[j] = u0 + j < nc ? __ldcg(base + (size_t)(u0 + j) * (HS + 2) + tid) : 0.f;
+#pragma unroll
+          for (int j = 0; j < 8; j++)
+            if (u0 + j < nc) acc += v8[j] * cf[u0 + j];
+        }
+        p.out[(size_t)(h0 + hh) * HS + tid] = L > 0.f ? acc * (1.0f / L) : 0.f;
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
+    }
+  }
+  if (tid == 0 && atomicAdd(&p.cnt[2 * kh + 1], 1u) == (unsigned)(nmerge - 1)) {
+    p.cnt[2 * kh] = 0u;
+    p.cnt[2 * kh + 1] = 0u;
   }
 }
 
@@ -677,11 +790,15 @@ __global__ void dec_rope_freq(float* freq, int hs, float base) {
 }
 
 // the chunks' states merged; out = acc / l (kv_softmax_finish, kvstore.h:99-101).
-// One CTA per q head: the chunk maxima and weighted sums are reduced by the
-// whole block first, then kCombThreads / hs groups of hs threads each sum a
-// share of the chunks' accumulators (independent loads in flight) and the
-// groups' sums are added.  Dynamic shared memory: (nchunk + kCombThreads)
-// floats.
+// One CTA of kCombThreads per q head, thread t on dimension t mod hs of
+// chunk group t / hs (kCombThreads / hs groups, group q taking chunks q,
+// q + groups, ...).  Every load that does not depend on the maximum (the
+// chunk maxima and sums, and the first kCombPre accumulator values of the
+// thread's chunks) is issued at once; then M = max m_c, the chunk weights
+// f_c = exp(m_c - M) into shared memory, L = sum l_c f_c (a fixed-order
+// block reduction) and the weighted accumulator sums, the groups added in
+// group order.  Dynamic shared memory: nchunk + kCombThreads floats.
+constexpr int kCombPre = 40;
 __global__ void __launch_bounds__(kCombThreads) dec_attn_combine(const __grid_constant__ AttnParams p, float* out) {
   pdl_launch_dependents();  // the next kernel may take SMs now; it waits in its own prologue
   pdl_wait();  // inputs written by the previous kernel on the stream
@@ -692,34 +809,42 @@ __global__ void __launch_bounds__(kCombThreads) dec_attn_combine(const __grid_co
   const float* base = p.part + (size_t)h * nc * st;
   float* cf = comb_sh;       // [nc] chunk weights exp(m_c - M)
   float* gs = comb_sh + nc;  // [groups][hs] group sums
+  const int ng = kCombThreads / hs, g = t / hs, e = t - g * hs;
+  float pre[kCombPre];
+#pragma unroll
+  for (int u = 0; u < kCombPre; u++) {
+    const int c = g + u * ng;
+    pre[u] = c < nc ? __ldcg(base + (size_t)c * st + e) : 0.f;
+  }
   float m = -INFINITY;
-  for (int c = t; c < nc; c += blockDim.x) m = fmaxf(m, base[c * st + hs]);
+  for (int c = t; c < nc; c += kCombThreads) m = fmaxf(m, __ldcg(base + (size_t)c * st + hs));
   m = warp_max(m);
-  __syncthreads();
   if ((t & 31) == 0) red[t >> 5] = m;
   __syncthreads();
   float M = -INFINITY;
-  for (int w = 0; w < (int)(blockDim.x >> 5); w++) M = fmaxf(M, red[w]);
+#pragma unroll
+  for (int w = 0; w < kCombThreads / 32; w++) M = fmaxf(M, red[w]);
   float L = 0.f;
-  for (int c = t; c < nc; c += blockDim.x) {
-    const float mc = base[c * st + hs];
+  for (int c = t; c < nc; c += kCombThreads) {
+    const float mc = __ldcg(base + (size_t)c * st + hs);
     const float f = mc > -INFINITY ? expf(mc - M) : 0.f;
     cf[c] = f;
-    L += base[c * st + hs + 1] * f;
+    L += __ldcg(base + (size_t)c * st + hs + 1) * f;
   }
   L = block_sum(L, red);  // its barriers also publish cf
-  const int ng = blockDim.x / hs, g = t / hs, i = t - g * hs;
-  if (g < ng) {
-    float a = 0.f;
-#pragma unroll 4
-    for (int c = g; c < nc; c += ng) a += base[c * st + i] * cf[c];
-    gs[g * hs + i] = a;
+  float a = 0.f;
+#pragma unroll
+  for (int u = 0; u < kCombPre; u++) {
+    const int c = g + u * ng;
+    if (c < nc) a += pre[u] * cf[c];
   }
+  for (int c = g + kCombPre * ng; c < nc; c += ng) a += __ldcg(base + (size_t)c * st + e) * cf[c];
+  gs[g * hs + e] = a;
   __syncthreads();
   if (t < hs) {
-    float a = 0.f;
-    for (int q = 0; q < ng; q++) a += gs[q * hs + t];
-    out[(size_t)h * hs + t] = L > 0.f ? a * (1.0f / L) : 0.f;
+    float acc = 0.f;
+    for (int q = 0; q < ng; q++) acc += gs[q * hs + t];
+    out[(size_t)h * hs + t] = L > 0.f ? acc * (1.0f / L) : 0.f;
   }
 }
 
@@ -893,6 +1018,7 @@ struct gguf_decoder {
   void *kc = nullptr, *vc = nullptr;
   size_t layer_kv = 0;  // elements of one layer's K (or V) cache
   int max_chunk = 0;
+  unsigned int* attn_cnt = nullptr;  // [n_kv_heads][2] merge counters of the tensor-core attention
 };
 
 extern "C" {
@@ -900,7 +1026,7 @@ extern "C" {
 void gguf_decoder_destroy(gguf_decoder* dec) {
   if (!dec) return;
   for (void* p : {(void*)dec->x, (void*)dec->xb, (void*)dec->y, (void*)dec->q, (void*)dec->att, (void*)dec->part,
-                  (void*)dec->logits, dec->kc, dec->vc, (void*)dec->freq})
+                  (void*)dec->logits, dec->kc, dec->vc, (void*)dec->freq, (void*)dec->attn_cnt})
     if (p) cudaFree(p);
   for (void* p : dec->wqkv)
     if (p) cudaFree(p);
@@ -959,6 +1085,8 @@ int gguf_decoder_create(const gguf_decoder_desc* desc, const gguf_decoder_layer*
       (st = cuda_status(cudaMalloc(&dec->att, (size_t)nq * 4))) ||
       (st = cuda_status(cudaMalloc(&dec->part, (size_t)D.n_heads * dec->max_chunk * (D.head_size + 2) * 4))) ||
       (st = cuda_status(cudaMalloc(&dec->logits, (size_t)D.vocab * 4))) ||
+      (st = cuda_status(cudaMalloc(&dec->attn_cnt, (size_t)D.n_kv_heads * 2 * 4))) ||
+      (st = cuda_status(cudaMemset(dec->attn_cnt, 0, (size_t)D.n_kv_heads * 2 * 4))) ||
       (st = cuda_status(cudaMalloc(&dec->kc, kvb))) || (st = cuda_status(cudaMalloc(&dec->vc, kvb))) ||
       (st = cuda_status(cudaMemset(dec->x, 0, (size_t)D.dim * 4)))) {
     gguf_decoder_destroy(dec);
@@ -1058,9 +1186,11 @@ static int decoder_step(gguf_decoder* dec, int token, const int32_t* token_dev, 
     at.scale = 1.0f / sqrtf((float)hs);
     at.eps = D.eps;
     at.part = dec->part;
+    at.cnt = dec->attn_cnt;
+    at.out = dec->att;
     at.err = c->d_err;
     if (D.kv_f16) {
-      // tensor-core attention per (chunk, kv head), then the chunk merge
+      // tensor-core attention per (chunk, kv head), the chunk merge in the same kernel
       size_t smem = 0;
       const void* fn = attn_mma_kernel(D.n_heads / D.n_kv_heads, hs, &smem);
       const int C = attn_mma_chunk(npos, D.n_kv_heads, c->num_sms);
@@ -1078,9 +1208,6 @@ static int decoder_step(gguf_decoder* dec, int token, const int32_t* token_dev, 
       int Cv = C;
       void* args[] = {&at, &Cv};
       if ((st = cuda_status(cudaLaunchKernelExC(&cfg, fn, args)))) return st;
-      if ((st = launch_pdl(dec_attn_combine, dim3(D.n_heads), dim3(kCombThreads),
-                           (size_t)(at.nchunk + kCombThreads) * sizeof(float), s, at, dec->att)))
-        return st;
     } else {
       if ((st = launch_attn(at, D.n_heads / D.n_kv_heads, D.kv_f16, nchunk, D.n_kv_heads, s))) return st;
       if ((st = launch_pdl(dec_attn_combine, dim3(D.n_heads), dim3(kCombThreads),
@@ -1135,6 +1262,7 @@ int gguf_decoder_sync(gguf_decoder* dec, void* stream) {
   if ((st = cuda_status(cudaMemcpy(&herr, dec->c->d_err, sizeof(int), cudaMemcpyDeviceToHost)))) return st;
   if (herr) {
     cudaMemset(dec->c->d_err, 0, sizeof(int));
+    cudaMemset(dec->attn_cnt, 0, (size_t)dec->d.n_kv_heads * 2 * 4);  // a merge may have given up mid-count
     return herr;
   }
   for (const auto& y : dec->L)
