@@ -743,7 +743,7 @@ def run_decoder(args, wl):
                 "cpu_baseline": cpu,
                 "e2e": {"value": e2e_tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4,
                         "note": "gguf_decoder_step with a host token id per step, next token read back"},
-                "gpu_launches": gen * (5 * spec.n_layers + 3), "clocks": clk.summary()}
+                "gpu_launches": gen * (4 * spec.n_layers + 3), "clocks": clk.summary()}
     G.close()
     return line if rank == 0 else None
 

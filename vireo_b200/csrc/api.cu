@@ -621,6 +621,24 @@ int gguf_moe_ffn(gguf_moe* m, const float* hb, float* x, int n_tok, int32_t* ids
   return moe_ffn_launches(m, hb, x, n_tok, ids, wts, s, m->prm.s.err);
 }
 
+}  // extern "C"
+
+int vireo::moe_ffn_norm(gguf_moe* m, float* x, const float* y, const float* w, float eps, cudaStream_t s) {
+  if (!m || !x || !y || !w) return VIREO_ERR_ARG;
+  MoeDecodeParams p = m->prm;
+  p.hb = nullptr;
+  p.x = x;
+  p.res_y = y;
+  p.norm_w = w;
+  p.norm_eps = eps;
+  p.ids_out = nullptr;
+  p.wts_out = nullptr;
+  void* args[] = {&p};
+  return moe_launch(m, m->kernel, args, s ? s : m->stream);
+}
+
+extern "C" {
+
 int gguf_moe_ffn_routed(gguf_moe* m, const float* hb, float* x, int n_tok, const int32_t* ids, const float* wts,
                         const void* const* expert_ptrs, void* stream) {
   if (!m || !hb || !x || n_tok < 0 || (n_tok && (!ids || !wts || !expert_ptrs))) return VIREO_ERR_ARG;

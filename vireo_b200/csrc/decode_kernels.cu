@@ -20,6 +20,7 @@ struct Ctl {
   int ids[kMaxTopK];
   float wts[kMaxTopK];
   float nred[kConsumerWarps];  // gemv_kernel: per-warp sums of squares for the fused norm
+  float sred[kConsumerWarps + kProducerWarps];  // moe_decode: per-warp sums of squares for the fused norm
   // the item each ring slot holds now (-1: none yet), written by the producer
   // before it issues the item's copies
   int slot_item[kMaxStages];
@@ -358,7 +359,28 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
     pdl_wait();
     if (threadIdx.x == 0) trace(p, kTrPdl);
     const float* xsm = reinterpret_cast<const float*>(xt.tab);
-    stage_vec(p.hb, reinterpret_cast<float*>(xt.tab), d, threadIdx.x, blockDim.x, false);
+    if (p.norm_w) {
+      // the decoder's x += attention output, xb = ffn_norm(x) (gguf_run.c:
+      // 237-238, rmsnorm :161-165), formed by every CTA into the staged vector
+      float* xv = reinterpret_cast<float*>(xt.tab);
+      float ss = 0.f;
+      for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        const float v = p.x[i] + p.res_y[i];
+        xv[i] = v;
+        ss += v * v;
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0) ctl->sred[warp] = ss;
+      __syncthreads();
+      ss = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps + kProducerWarps; w++) ss += ctl->sred[w];
+      const float r = 1.0f / sqrtf(ss / (float)d + p.norm_eps);
+      for (int i = threadIdx.x; i < d; i += blockDim.x) xv[i] = xv[i] * r * p.norm_w[i];
+    } else {
+      stage_vec(p.hb, reinterpret_cast<float*>(xt.tab), d, threadIdx.x, blockDim.x, false);
+    }
     __syncthreads();
     for (int e = gw; e < ne; e += nw) {
       float v = 0.f;
@@ -470,7 +492,8 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
   }
 
   // ---- consumers ----------------------------------------------------------------
-  for (int i = threadIdx.x; i < 16 * nD; i += NC) xs[i] = p.x[16 * i0 + i];
+  for (int i = threadIdx.x; i < 16 * nD; i += NC)
+    xs[i] = p.norm_w ? p.x[16 * i0 + i] + p.res_y[16 * i0 + i] : p.x[16 * i0 + i];
   const LaneCtx L = lane_ctx();
   const int nsg = d / kSegElems, nsd = fe / kSegElems;
   BFrag bf;

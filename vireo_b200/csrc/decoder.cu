@@ -1217,12 +1217,9 @@ static int decoder_step(gguf_decoder* dec, int token, const int32_t* token_dev, 
     st = gemv_dev_fast(c, y.wo_type, y.wo, dec->att, dec->y, nq, d, s, nullptr, 0.f, kDecPrefetch);
     if (st == VIREO_ERR_UNSUPPORTED) st = gemv_dev(c, y.wo_type, y.wo, dec->att, dec->y, nq, d, s);
     if (st) return st;
-    // x += attention output; xb = ffn_norm(x)   (gguf_run.c:237-238)
-    if ((st = launch_pdl(dec_rmsnorm, dim3(1), dim3(kDecThreads), 0, s, dec->x, (const float*)dec->y, y.ffn_norm,
-                         dec->xb, d, D.eps)))
-      return st;
-    // x += MoE(xb)   (gguf_run.c:239)
-    if ((st = gguf_moe_ffn(y.moe, dec->xb, dec->x, 1, nullptr, nullptr, s))) return st;
+    // x += attention output; x += MoE(ffn_norm(x))   (gguf_run.c:237-239): the
+    // residual add and the norm inside the MoE kernel
+    if ((st = moe_ffn_norm(y.moe, dec->x, dec->y, y.ffn_norm, D.eps, s))) return st;
   }
   if (logits || next) {
     float* lg = logits ? logits : dec->logits;

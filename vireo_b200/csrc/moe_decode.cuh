@@ -86,6 +86,12 @@ struct MoeDecodeParams {
   uint32_t off_ctl, off_etab, off_ucnt, off_part, off_xtab, off_xmeta, off_xrtab, off_xrmeta, off_htab, off_hmeta,
       off_hrtab, off_hrmeta, off_xs, off_stage;
   unsigned long long* trace;  // optional: kTraceSlots %globaltimer stamps per CTA
+  // optional (decoder): hb is not given; every CTA forms x + res_y (the
+  // residual add before the FFN) and its RMSNorm with norm_w as the hidden
+  // vector, and x + res_y is the residual the output is added to
+  const float* res_y;
+  const float* norm_w;
+  float norm_eps;
   int* err_out;               // optional, mapped host memory: the last CTA out writes the status word to
                               // [0], then 1 to [1]
 };

@@ -18,4 +18,8 @@ struct MoeView {
 };
 int moe_view(gguf_moe* m, MoeView* v);
 
+// One decode launch with the residual add and the FFN norm folded in: x +=
+// y, then x += MoE(rmsnorm(x) * w) (the decoder's gguf_run.c:237-239).
+int moe_ffn_norm(gguf_moe* m, float* x, const float* y, const float* w, float eps, cudaStream_t s);
+
 }  // namespace vireo
