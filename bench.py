@@ -248,6 +248,9 @@ def main():
                     help="cfg1_moe_decode: comma-separated sub-records to run (default: all of "
                          + ", ".join(SUB_RECORDS) + ")")
     ap.add_argument("--prompt", type=int, default=None, help="decoder workloads: prompt tokens (default: the config's)")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="decoder workloads: layer count (default: the config's; fewer layers only for profiling "
+                         "runs, the line then names the count)")
     ap.add_argument("--timeline", default=None,
                     help="prefill only: after the timed steps, record 3 more steps under the CUDA activity "
                          "profiler and write each rank's kernel timeline to TIMELINE.rank<r>.txt (not timed)")
@@ -640,6 +643,9 @@ def run_decoder(args, wl):
     L = V.lib()
     V.check(L.vireo_device_init(local), "vireo_device_init")
     spec = wl["spec"]()
+    if args.layers:
+        spec = S.DecoderSpec(args.layers, spec.dim, spec.n_heads, spec.n_kv_heads, spec.head_size, spec.vocab, spec.moe,
+                             spec.qk_norm, spec.attn_type, spec.embd_type, spec.lm_type, spec.eps, spec.rope_base)
     P, gen = (wl["prompt"] if args.prompt is None else args.prompt), max(args.steps, 1)
     dec = S.Decoder(spec, wl["seed"], n_distinct_layers=1)
     dev = torch.device("cuda", local)

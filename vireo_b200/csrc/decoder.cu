@@ -850,28 +850,38 @@ __global__ void __launch_bounds__(kCombThreads) dec_attn_combine(const __grid_co
 
 // greedy argmax (gguf_run.c:253): strict '>' from index 0, so the lowest id
 // wins ties and a NaN never wins
-__global__ void __launch_bounds__(kDecThreads) dec_argmax(const float* v, int n, int32_t* out) {
+// Spread over the SMs: CTA b reduces a contiguous slice to its (value,
+// index) under (value desc, index asc), NaN never winning; the last CTA to
+// finish (an arrival count, put back to zero) reduces the slices' winners
+// in slice order.  scratch: [kArgmaxMaxCtas] values, [kArgmaxMaxCtas]
+// indices, one counter.
+constexpr int kArgmaxThreads = 256, kArgmaxMaxCtas = 256;
+VDEV void amax_take(float& bv, int& bi, float ov, int oi) {
+  if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) {
+    bv = ov;
+    bi = oi;
+  }
+}
+__global__ void __launch_bounds__(kArgmaxThreads) dec_argmax(const float* v, int n, int32_t* out, float* sv) {
   pdl_launch_dependents();  // the next kernel may take SMs now; it waits in its own prologue
   pdl_wait();  // inputs written by the previous kernel on the stream
   __shared__ float bv_s[32];
   __shared__ int bi_s[32];
+  __shared__ int last;
+  int* si = reinterpret_cast<int*>(sv + kArgmaxMaxCtas);
+  unsigned int* cnt = reinterpret_cast<unsigned int*>(si + kArgmaxMaxCtas);
+  const int span = (n + gridDim.x - 1) / gridDim.x, lo = blockIdx.x * span, hi = min(n, lo + span);
   float bv = -INFINITY;
   int bi = -1;
-  for (int i = threadIdx.x; i < n; i += blockDim.x)
-    if (v[i] > bv || (bi < 0 && v[i] == bv)) {
-      bv = v[i];
+  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+    const float x = __ldcg(v + i);
+    if (x > bv || (bi < 0 && x == bv)) {
+      bv = x;
       bi = i;
     }
-  // (value desc, index asc), empty (bi < 0) last
-#pragma unroll
-  for (int o = 16; o; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) {
-      bv = ov;
-      bi = oi;
-    }
   }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) amax_take(bv, bi, __shfl_xor_sync(0xffffffffu, bv, o), __shfl_xor_sync(0xffffffffu, bi, o));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) {
     bv_s[warp] = bv;
@@ -881,13 +891,33 @@ __global__ void __launch_bounds__(kDecThreads) dec_argmax(const float* v, int n,
   if (threadIdx.x == 0) {
     float b = -INFINITY;
     int ix = -1;
-    for (int w = 0; w < (int)(blockDim.x >> 5); w++)
-      if (bi_s[w] >= 0 && (ix < 0 || bv_s[w] > b || (bv_s[w] == b && bi_s[w] < ix))) {
-        b = bv_s[w];
-        ix = bi_s[w];
-      }
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) amax_take(b, ix, bv_s[w], bi_s[w]);
+    sv[blockIdx.x] = b;
+    si[blockIdx.x] = ix;
+    __threadfence();
+    last = atomicAdd(cnt, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  bv = -INFINITY;
+  bi = -1;
+  for (int j = threadIdx.x; j < (int)gridDim.x; j += blockDim.x) amax_take(bv, bi, __ldcg(sv + j), __ldcg(si + j));
+#pragma unroll
+  for (int o = 16; o; o >>= 1) amax_take(bv, bi, __shfl_xor_sync(0xffffffffu, bv, o), __shfl_xor_sync(0xffffffffu, bi, o));
+  __syncthreads();
+  if (lane == 0) {
+    bv_s[warp] = bv;
+    bi_s[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = -INFINITY;
+    int ix = -1;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) amax_take(b, ix, bv_s[w], bi_s[w]);
     // the reference starts from v[0]: when v[0] is NaN nothing beats it
-    *out = (ix < 0 || isnan(v[0])) ? 0 : ix;
+    *out = (ix < 0 || isnan(__ldcg(v))) ? 0 : ix;
+    *cnt = 0u;
   }
 }
 
@@ -1019,6 +1049,7 @@ struct gguf_decoder {
   size_t layer_kv = 0;  // elements of one layer's K (or V) cache
   int max_chunk = 0;
   unsigned int* attn_cnt = nullptr;  // [n_kv_heads][2] merge counters of the tensor-core attention
+  float* amax = nullptr;             // argmax scratch: per-CTA winners and the arrival count
 };
 
 extern "C" {
@@ -1026,7 +1057,7 @@ extern "C" {
 void gguf_decoder_destroy(gguf_decoder* dec) {
   if (!dec) return;
   for (void* p : {(void*)dec->x, (void*)dec->xb, (void*)dec->y, (void*)dec->q, (void*)dec->att, (void*)dec->part,
-                  (void*)dec->logits, dec->kc, dec->vc, (void*)dec->freq, (void*)dec->attn_cnt})
+                  (void*)dec->logits, dec->kc, dec->vc, (void*)dec->freq, (void*)dec->attn_cnt, (void*)dec->amax})
     if (p) cudaFree(p);
   for (void* p : dec->wqkv)
     if (p) cudaFree(p);
@@ -1087,6 +1118,8 @@ int gguf_decoder_create(const gguf_decoder_desc* desc, const gguf_decoder_layer*
       (st = cuda_status(cudaMalloc(&dec->logits, (size_t)D.vocab * 4))) ||
       (st = cuda_status(cudaMalloc(&dec->attn_cnt, (size_t)D.n_kv_heads * 2 * 4))) ||
       (st = cuda_status(cudaMemset(dec->attn_cnt, 0, (size_t)D.n_kv_heads * 2 * 4))) ||
+      (st = cuda_status(cudaMalloc(&dec->amax, (size_t)(2 * kArgmaxMaxCtas + 1) * 4))) ||
+      (st = cuda_status(cudaMemset(dec->amax, 0, (size_t)(2 * kArgmaxMaxCtas + 1) * 4))) ||
       (st = cuda_status(cudaMalloc(&dec->kc, kvb))) || (st = cuda_status(cudaMalloc(&dec->vc, kvb))) ||
       (st = cuda_status(cudaMemset(dec->x, 0, (size_t)D.dim * 4)))) {
     gguf_decoder_destroy(dec);
@@ -1232,7 +1265,8 @@ static int decoder_step(gguf_decoder* dec, int token, const int32_t* token_dev, 
       st = gemv_dev(c, D.lm_head_type, D.lm_head, dec->xb, lg, d, D.vocab, s);
     }
     if (st) return st;
-    if (next && (st = launch_pdl(dec_argmax, dim3(1), dim3(kDecThreads), 0, s, (const float*)lg, D.vocab, next)))
+    if (next && (st = launch_pdl(dec_argmax, dim3(std::min(std::min(c->num_sms, kArgmaxMaxCtas), (D.vocab + 1023) / 1024)),
+                                 dim3(kArgmaxThreads), 0, s, (const float*)lg, D.vocab, next, dec->amax)))
       return st;
   }
   return cuda_status(cudaGetLastError());
