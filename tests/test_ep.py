@@ -1,8 +1,10 @@
 """Expert-parallel batched MoE FFN (gguf_moe_prefill_ep) on the GPU, through
-the C-ABI.  The expert-parallel result must be bit-identical to
-gguf_moe_prefill on one GPU over the same tokens (same GEMM arithmetic per
-row, same combine order), and within the oracle tolerance of the CPU
-restatement of the reference's moe_ffn.
+the C-ABI.  The expert-parallel result uses the same GEMM arithmetic per row
+and the same combine order as gguf_moe_prefill on one GPU, with each
+expert's weighted output row rounded to f16 for the return over NVLink: ids
+and gate weights bit-identical to one GPU, each token's FFN output within
+the 2e-3 bar of it and of the CPU restatement of the reference's moe_ffn,
+and repeated calls bit-identical to each other.
 
 world 1 runs in this process (the whole dispatch / return path over an NCCL
 communicator of one rank); world 2 runs as two spawned processes and is
@@ -19,6 +21,13 @@ from vireo_b200 import synth as S
 pytestmark = pytest.mark.gpu
 
 TOL = 2e-3
+
+
+def _close(x, ref, x0):
+    """Per token: the FFN output x - x0 against ref - x0, max|diff| / max|ref|."""
+    d, r = (x - x0).astype(np.float64), (ref - x0).astype(np.float64)
+    err = np.abs(d - r).max(axis=1) / np.maximum(np.abs(r).max(axis=1), 1e-30)
+    return float(err.max()) if err.size else 0.0
 
 
 def _case(seed):
@@ -73,7 +82,7 @@ def _ep_run(L, toks, x0, bias, owner, rank, world, uid, device, max_tokens):
         ep.close()
 
 
-def test_ep_world1_matches_single_gpu_bits():
+def test_ep_world1_matches_single_gpu():
     import torch
     import vireo_b200 as V
     assert torch.cuda.is_available()
@@ -85,7 +94,8 @@ def test_ep_world1_matches_single_gpu_bits():
     for x, ids, wts in outs:
         assert np.array_equal(ids, ref[1])
         assert np.array_equal(wts.view(np.uint32), ref[2].view(np.uint32))
-        assert np.array_equal(x.view(np.uint32), ref[0].view(np.uint32)), np.abs(x - ref[0]).max()
+        assert _close(x, ref[0], x0) < TOL
+    assert np.array_equal(outs[0][0].view(np.uint32), outs[1][0].view(np.uint32))
     # and the CPU restatement of the reference, within tolerance (bf16-rounded inputs)
     hb = torch.from_numpy(toks).to(torch.bfloat16).float().numpy()
     rx, rids, _ = O.PortMoe(L)(hb[:40], x0[:40], bias)
@@ -122,7 +132,7 @@ def _rank_main(rank, world, tmp, split):
 
 
 @pytest.mark.parametrize("split", [(0, 150, 300), (0, 300, 300)])
-def test_ep_world2_matches_single_gpu_bits(tmp_path, split):
+def test_ep_world2_matches_single_gpu(tmp_path, split):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
@@ -141,5 +151,6 @@ def test_ep_world2_matches_single_gpu_bits(tmp_path, split):
         lo, hi = split[r], split[r + 1]
         xs = np.load(tmp_path / f"x{r}.npy")
         for x in xs:
-            assert np.array_equal(x.view(np.uint32), ref[0][lo:hi].view(np.uint32)), (r, np.abs(x - ref[0][lo:hi]).max())
+            assert _close(x, ref[0][lo:hi], x0[lo:hi]) < TOL, r
+        assert np.array_equal(xs[0].view(np.uint32), xs[-1].view(np.uint32))
         assert np.array_equal(np.load(tmp_path / f"ids{r}.npy"), ref[1][lo:hi])

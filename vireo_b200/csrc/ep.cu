@@ -10,32 +10,39 @@
 //
 //   route     prep + router GEMM + top-k on the local tokens (prefill.cu);
 //             per expert, the local pair count and each pair's index in it
-//   count     all-gather of the [ne] counts (NCCL, 512 bytes per rank): every
-//             rank knows the [G][ne] matrix and computes from it, on the
-//             device, where each of its pairs lands in its expert's row range
-//             on the owning rank (the ranges are laid out as prefill_scan lays
-//             them out); no host synchronisation anywhere in a call
+//   count     every rank stores its [ne] counts into every rank's signal
+//             buffer (peer memory) and raises its flag there; once all flags
+//             are up, every rank knows the [G][ne] matrix and computes from
+//             it, on the device, where each of its pairs lands in its
+//             expert's row range on the owning rank (the ranges are laid out
+//             as prefill_scan lays them out); no host synchronisation anywhere
+//             in a call
 //   dispatch  one warp per (token, slot) pair writes the token's activation
 //             row, the gate weight and the pair's origin straight into the
 //             owning rank's GEMM operand (peer stores), then a barrier
 //   experts   the owner runs the tcgen05 gate/up and down GEMMs of prefill.cu
-//             over its rows; the down GEMM's epilogue stores each output row
-//             into the SOURCE rank's return buffer over NVLink, tile by tile
-//             while the next tiles' MMAs run (one kernel: GEMM + return)
+//             over its rows; the down GEMM's epilogue stores each output row,
+//             rounded to f16, into the SOURCE rank's return buffer over
+//             NVLink, tile by tile while the next tiles' MMAs run (one
+//             kernel: GEMM + return)
 //   combine   after a barrier, x[t] += sum over rank order of the returned
-//             rows (the reference's combine order, gguf_run.c:209, 213)
+//             rows in fp32 (the reference's combine order, gguf_run.c:209, 213)
 // Every output row comes from the same GEMM arithmetic as on one GPU and the
-// combine order is the same, so the result is bit-identical to
-// gguf_moe_prefill on one GPU over the same tokens.
+// combine order is the same; the f16 rounding of the returned rows (half
+// the NVLink bytes of fp32 rows) is the only difference from
+// gguf_moe_prefill on one GPU, so results agree to the f16 rounding of each
+// expert's weighted output (tested at the 2e-3 bar of the decode path).
 //
 // Ordering across ranks: every rank's writes into a peer's buffers are
-// followed by a system-scope fence and the end of the kernel, then an NCCL
-// all-reduce of one word on the stream (the barrier); the peer reads only
-// after its own copy of that barrier.  A buffer a peer writes in call n + 1
-// was last read in call n before this rank's count all-gather of call n + 1,
-// which the writer waits for.
+// followed by a system-scope fence and the end of the kernel; then a barrier
+// over peer memory (ep_signal: each rank raises its flag of the phase, the
+// number of the call, on every rank and waits, bounded, for every rank's
+// flag in its own buffer); a rank reads the data only after its own copy of
+// that barrier.  A buffer a peer writes in call n + 1 was last read in call
+// n before this rank raised a flag of call n that the writer waited for.
 //
-// NCCL (counts, barriers, IPC handle exchange) is loaded at run time (dlopen
+// NCCL (communicator set-up, the IPC handle exchange, the last barrier at
+// destroy) is loaded at run time (dlopen
 // of libnccl.so.2; in a process that already loaded it, e.g. through PyTorch,
 // that copy is used).  Host-side waits on the stream (gguf_moe_ep_sync, set-up)
 // are bounded: a peer that stops answering ends them with VIREO_ERR_TIMEOUT and aborts the
@@ -57,6 +64,7 @@
 #include "gguf_moe.h"
 #include "moe_view.h"
 #include "vireo_internal.h"
+#include "vireo_ptx.cuh"
 
 namespace vireo {
 
@@ -123,14 +131,15 @@ __global__ void ep_count(const int32_t* ids, int pairs, int* cnt, int* pos) {
 // inside a range.  dst_off[e]: the first row of this rank's pairs in expert
 // e's range on owner[e]; totals[e]: rows expert e receives if held here, else
 // 0 (the counts prefill_scan lays out).  One block, thread e per expert.
-__global__ void ep_layout(const int* cntall, const int32_t* owner, int G, int ne, int rank, int tile, int* dst_off,
-                          int* totals) {
+// cstride: ints between two ranks' count rows in cntall.
+__device__ void ep_layout_body(const int* cntall, int cstride, const int32_t* owner, int G, int ne, int rank,
+                               int tile, int* dst_off, int* totals) {
   __shared__ int pad[kEpMaxExperts], own_s[kEpMaxExperts];
   const int e = threadIdx.x;
   int n = 0, b = 0, q = 0;
   if (e < ne) {
     for (int s = 0; s < G; s++) {
-      const int c = cntall[s * ne + e];
+      const int c = cntall[s * cstride + e];
       if (s < rank) b += c;
       n += c;
     }
@@ -146,6 +155,73 @@ __global__ void ep_layout(const int* cntall, const int32_t* owner, int G, int ne
     dst_off[e] = base + b;
     totals[e] = q == rank ? n : 0;
   }
+}
+
+// The signal buffer every rank exports (CUDA IPC): each rank's per-expert
+// counts, written by that rank into every peer's copy, and one flag per
+// (phase, rank) on its own 128-byte line; a flag holds the number of the
+// call whose phase the rank has reached (calls are numbered alike on every
+// rank: all ranks make the same calls in the same order).
+struct EpSig {
+  int cnt[kEpMaxWorld][kEpMaxExperts];
+  unsigned int flag[3][kEpMaxWorld][32];
+};
+constexpr int kSigCounts = 0, kSigDispatched = 1, kSigReturned = 2;
+struct EpPeers {
+  EpSig* sig[kEpMaxWorld];
+};
+
+// Bounded wait until *f >= v (a peer's flag in this rank's memory).
+__device__ bool ep_wait_flag(const volatile unsigned int* f, unsigned int v, int* err) {
+  const unsigned long long t0 = now_ns();
+  while (*f < v) {
+    if (now_ns() - t0 > kWaitLimitNs) {
+      atomicCAS(err, 0, VIREO_ERR_TIMEOUT);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
+
+// The count exchange over peer memory (in place of a count all-gather) and
+// the layout: thread e stores this rank's count of expert e into every
+// rank's signal buffer, the counts are made visible system-wide, thread 0
+// raises this rank's counts flag on every rank, threads q < G wait for rank
+// q's flag here, then the layout of ep_layout_body from the gathered counts.
+__global__ void ep_exchange(const int* cnt, EpSig* mine, const __grid_constant__ EpPeers P, unsigned int call,
+                            const int32_t* owner, int G, int ne, int rank, int tile, int* dst_off, int* totals,
+                            int* err) {
+  const int e = threadIdx.x;
+  if (e < ne) {
+    const int c = cnt[e];
+    for (int q = 0; q < G; q++) P.sig[q]->cnt[rank][e] = c;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (e < G) *reinterpret_cast<volatile unsigned int*>(&P.sig[e]->flag[kSigCounts][rank][0]) = call;
+  __shared__ int ok;
+  if (e == 0) ok = 1;
+  __syncthreads();
+  if (e < G && !ep_wait_flag(&mine->flag[kSigCounts][e][0], call, err)) ok = 0;
+  __syncthreads();
+  __threadfence_system();
+  if (!ok) return;
+  ep_layout_body(&mine->cnt[0][0], kEpMaxExperts, owner, G, ne, rank, tile, dst_off, totals);
+}
+
+// A barrier over peer memory: every kernel before this one on the stream has
+// completed (its peer stores fenced system-wide), lane q raises this rank's
+// flag of the phase on rank q and waits for rank q's flag here.
+__global__ void ep_signal(EpSig* mine, const __grid_constant__ EpPeers P, int phase, unsigned int call, int G,
+                          int rank, int* err) {
+  const int q = threadIdx.x;
+  __threadfence_system();
+  if (q < G) {
+    *reinterpret_cast<volatile unsigned int*>(&P.sig[q]->flag[phase][rank][0]) = call;
+    ep_wait_flag(&mine->flag[phase][q][0], call, err);
+  }
+  __threadfence_system();
 }
 
 // one warp per (token, slot) pair: the token's activation row, the gate
@@ -172,19 +248,20 @@ __global__ void ep_dispatch(const __half* xa, const int32_t* ids, const float* w
   __threadfence_system();
 }
 
-// x[t] += sum over rank order of the returned rows (prefill_combine's order),
-// four columns per thread; the slots' loads are issued together
-__global__ void ep_combine(const int32_t* ids, const float* yret, float* x, int T, int k, int d) {
+// x[t] += sum over rank order of the returned f16 rows, in fp32
+// (prefill_combine's order), four columns per thread; the slots' loads are
+// issued together
+__global__ void ep_combine(const int32_t* ids, const __half* yret, float* x, int T, int k, int d) {
   const int t = blockIdx.x;
   if (t >= T) return;
   bool on[kEpMaxTopK];
 #pragma unroll
   for (int i = 0; i < kEpMaxTopK; i++) on[i] = i < k && ids[(size_t)t * k + i] >= 0;
   const int d4 = d / 4;
-  const float4* y4 = reinterpret_cast<const float4*>(yret) + (size_t)t * k * d4;
+  const uint2* y4 = reinterpret_cast<const uint2*>(yret) + (size_t)t * k * d4;
   float4* x4 = reinterpret_cast<float4*>(x) + (size_t)t * d4;
   for (int c = threadIdx.x; c < d4; c += blockDim.x) {
-    float4 v[kEpMaxTopK];
+    uint2 v[kEpMaxTopK];
 #pragma unroll
     for (int i = 0; i < kEpMaxTopK; i++)
       if (on[i]) v[i] = __ldcs(y4 + (size_t)i * d4 + c);
@@ -192,10 +269,12 @@ __global__ void ep_combine(const int32_t* ids, const float* yret, float* x, int 
 #pragma unroll
     for (int i = 0; i < kEpMaxTopK; i++)
       if (on[i]) {
-        acc.x = __fadd_rn(acc.x, v[i].x);
-        acc.y = __fadd_rn(acc.y, v[i].y);
-        acc.z = __fadd_rn(acc.z, v[i].z);
-        acc.w = __fadd_rn(acc.w, v[i].w);
+        const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&v[i].x));
+        const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&v[i].y));
+        acc.x = __fadd_rn(acc.x, lo.x);
+        acc.y = __fadd_rn(acc.y, lo.y);
+        acc.z = __fadd_rn(acc.z, hi.x);
+        acc.w = __fadd_rn(acc.w, hi.y);
       }
     float4 xv = x4[c];
     xv.x = __fadd_rn(xv.x, acc.x);
@@ -229,12 +308,15 @@ struct gguf_moe_ep {
   __half* xg = nullptr;     // [rows_cap][Kx]
   float* wrow = nullptr;    // [rows_cap]
   int* ysrc = nullptr;      // [rows_cap]
-  float* yret = nullptr;    // [max_tok * k][d]
+  __half* yret = nullptr;   // [max_tok * k][d] f16 returned rows
   // every rank's buffers as mapped here (own entry = the local pointer)
   __half* p_xg[kEpMaxWorld] = {};
   float* p_wrow[kEpMaxWorld] = {};
   int* p_ysrc[kEpMaxWorld] = {};
-  float* p_yret[kEpMaxWorld] = {};
+  __half* p_yret[kEpMaxWorld] = {};
+  EpSig* sig = nullptr;                 // this rank's signal buffer (peers write it)
+  EpSig* p_sig[kEpMaxWorld] = {};
+  unsigned int call = 0;                // calls made so far (the same on every rank)
   bool mapped[kEpMaxWorld] = {};
 };
 
@@ -389,7 +471,9 @@ int gguf_moe_ep_create(const gguf_moe_desc* desc, const int32_t* owner, int rank
       (st = cuda_status(cudaMalloc(&ep->xg, ep->rows_cap * Kx * 2))) ||
       (st = cuda_status(cudaMalloc(&ep->wrow, ep->rows_cap * 4))) ||
       (st = cuda_status(cudaMalloc(&ep->ysrc, ep->rows_cap * 4))) ||
-      (st = cuda_status(cudaMalloc(&ep->yret, pairs_cap * d * 4))) ||
+      (st = cuda_status(cudaMalloc(&ep->yret, pairs_cap * d * 2))) ||
+      (st = cuda_status(cudaMalloc(&ep->sig, sizeof(EpSig)))) ||
+      (st = cuda_status(cudaMemset(ep->sig, 0, sizeof(EpSig)))) ||
       (st = cuda_status(cudaMemset(ep->d_bar, 0, 16))) ||
       (st = cuda_status(cudaMemcpy(ep->d_owner, owner, ne * 4, cudaMemcpyHostToDevice))) ||
       (st = cuda_status(cudaMemcpy(ep->d_own, own.data(), ne * 4, cudaMemcpyHostToDevice)))) {
@@ -407,14 +491,14 @@ int gguf_moe_ep_create(const gguf_moe_desc* desc, const int32_t* owner, int rank
   // every rank must size its buffers alike (a peer writes up to its own
   // max_tokens * n_used rows into them)
   struct {
-    cudaIpcMemHandle_t h[4];
+    cudaIpcMemHandle_t h[5];
     int64_t max_tok, pad;
   } mine;
   static_assert(sizeof(mine) % 16 == 0, "exchange record");
   mine.max_tok = max_tokens;
   mine.pad = 0;
-  void* bufs[4] = {ep->xg, ep->wrow, ep->ysrc, ep->yret};
-  for (int i = 0; i < 4; i++)
+  void* bufs[5] = {ep->xg, ep->wrow, ep->ysrc, ep->yret, ep->sig};
+  for (int i = 0; i < 5; i++)
     if ((st = cuda_status(cudaIpcGetMemHandle(&mine.h[i], bufs[i])))) {
       gguf_moe_ep_destroy(ep);
       return st;
@@ -440,15 +524,17 @@ int gguf_moe_ep_create(const gguf_moe_desc* desc, const int32_t* owner, int rank
       ep->p_wrow[q] = ep->wrow;
       ep->p_ysrc[q] = ep->ysrc;
       ep->p_yret[q] = ep->yret;
+      ep->p_sig[q] = ep->sig;
       continue;
     }
-    void* ptr[4] = {};
-    for (int i = 0; i < 4 && !st; i++)
+    void* ptr[5] = {};
+    for (int i = 0; i < 5 && !st; i++)
       st = cuda_status(cudaIpcOpenMemHandle(&ptr[i], all[q].h[i], cudaIpcMemLazyEnablePeerAccess));
     ep->p_xg[q] = (__half*)ptr[0];
     ep->p_wrow[q] = (float*)ptr[1];
     ep->p_ysrc[q] = (int*)ptr[2];
-    ep->p_yret[q] = (float*)ptr[3];
+    ep->p_yret[q] = (__half*)ptr[3];
+    ep->p_sig[q] = (EpSig*)ptr[4];
     ep->mapped[q] = true;
   }
   if (st) {
@@ -490,10 +576,14 @@ int gguf_moe_prefill_ep(gguf_moe_ep* ep, const void* hb_bf16, float* x, int n_to
   if (n_tok == 0 && (rc = prefill_prepare(L, S, s))) return rc;
   if ((rc = cuda_status(cudaMemsetAsync(ep->d_cnt, 0, ne * 4, s)))) return rc;
   if (pairs) ep_count<<<(unsigned)((pairs + 255) / 256), 256, 0, s>>>(S->ids, (int)pairs, ep->d_cnt, ep->d_pos);
-  // the [G][ne] count matrix on every rank; the row layout from it, on the device
-  if (N.allGather(ep->d_cnt, ep->d_cntall, (size_t)ne, ncclInt32, ep->comm, s) != ncclSuccess) return VIREO_ERR_CUDA;
-  ep_layout<<<1, kEpMaxExperts, 0, s>>>(ep->d_cntall, ep->d_owner, G, ne, r, prefill_tile_rows(), ep->d_dstoff,
-                                        ep->d_totals);
+  // the [G][ne] count matrix on every rank, exchanged over peer memory, and
+  // the row layout from it, on the device
+  const unsigned int call = ++ep->call;
+  EpPeers P;
+  memset(&P, 0, sizeof(P));
+  for (int q = 0; q < G; q++) P.sig[q] = ep->p_sig[q];
+  ep_exchange<<<1, kEpMaxExperts, 0, s>>>(ep->d_cnt, ep->sig, P, call, ep->d_owner, G, ne, r, prefill_tile_rows(),
+                                          ep->d_dstoff, ep->d_totals, v.err);
   EpDispatch Dp;
   memset(&Dp, 0, sizeof(Dp));
   for (int q = 0; q < G; q++) {
@@ -515,11 +605,11 @@ int gguf_moe_prefill_ep(gguf_moe_ep* ep, const void* hb_bf16, float* x, int n_to
   if (pairs)
     ep_dispatch<<<(unsigned)((pairs + 7) / 8), 256, 0, s>>>(S->xa, S->ids, S->wts, ep->d_owner, ep->d_pos,
                                                              (int)pairs, k, Kx, r, Dp, v.err);
-  if ((rc = ep_barrier(ep, s))) return rc;
+  ep_signal<<<1, 32, 0, s>>>(ep->sig, P, kSigDispatched, call, G, r, v.err);
   // the experts held here; the down GEMM returns each row to its source rank
   prefill_scan_launch(ep->d_totals, ne, S, s);
   if ((rc = prefill_experts(L, S, rows, v.err, v.num_sms, s, ep->ysrc, ep->p_yret, G))) return rc;
-  if ((rc = ep_barrier(ep, s))) return rc;
+  ep_signal<<<1, 32, 0, s>>>(ep->sig, P, kSigReturned, call, G, r, v.err);
   if (n_tok > 0) ep_combine<<<n_tok, 256, 0, s>>>(S->ids, ep->yret, x, n_tok, k, d);
   if (ids_out && pairs && cudaMemcpyAsync(ids_out, S->ids, pairs * 4, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
     return cuda_status(cudaGetLastError());
@@ -546,7 +636,8 @@ void gguf_moe_ep_destroy(gguf_moe_ep* ep) {
   const bool clean = cudaDeviceSynchronize() == cudaSuccess;
   for (int q = 0; q < kEpMaxWorld; q++)
     if (ep->mapped[q])
-      for (void* p : {(void*)ep->p_xg[q], (void*)ep->p_wrow[q], (void*)ep->p_ysrc[q], (void*)ep->p_yret[q]})
+      for (void* p : {(void*)ep->p_xg[q], (void*)ep->p_wrow[q], (void*)ep->p_ysrc[q], (void*)ep->p_yret[q],
+                      (void*)ep->p_sig[q]})
         if (p) cudaIpcCloseMemHandle(p);
   if (ep->comm) {
     // the peers unmap this rank's buffers before any of them is freed: one
@@ -569,7 +660,7 @@ void gguf_moe_ep_destroy(gguf_moe_ep* ep) {
   }
   for (void* p : {(void*)ep->d_owner, (void*)ep->d_own, (void*)ep->d_cnt, (void*)ep->d_cntall, (void*)ep->d_totals, (void*)ep->d_dstoff,
                   (void*)ep->d_pos, (void*)ep->d_bar, (void*)ep->xg, (void*)ep->wrow, (void*)ep->ysrc,
-                  (void*)ep->yret})
+                  (void*)ep->yret, (void*)ep->sig})
     if (p) cudaFree(p);
   delete ep;
 }

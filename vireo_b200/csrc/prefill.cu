@@ -100,8 +100,8 @@ struct PRing {
   static constexpr uint32_t BYTES = OFF_R + (MODE == 0 ? 0u : NR * RB);
 };
 constexpr uint32_t cmax(uint32_t a, uint32_t b) { return a > b ? a : b; }
-// the down GEMM's epilogue stages each warp's 32 x 32 output block here
-// (row stride 33 floats) when its rows return to other ranks
+// the down GEMM's epilogue stages each warp's 32-row x 64-column f16 output
+// block here (row stride 33 words) when its rows return to other ranks
 constexpr uint32_t kPEpiStage = 4 * 32 * 33 * 4;
 template <int MODE>
 constexpr uint32_t psmem() {
@@ -140,7 +140,7 @@ struct PrefillParams {
   // rank ysrc[r] >> 24's buffer ypeer[rank], row ysrc[r] & 0xFFFFFF, instead
   // of y (peer memory: the NVLink write overlaps the next tile's MMAs)
   const int* ysrc;
-  float* ypeer[kPMaxPeers];
+  __half* ypeer[kPMaxPeers];  // f16 rows (half the NVLink bytes of fp32)
   int* err;
 };
 
@@ -578,29 +578,36 @@ __global__ void __launch_bounds__(kPThreads, 1)
         const float w = valid ? p.wrow[row] : 0.f;
         if (p.ysrc) {
           // expert-parallel return: each row goes to its source rank's buffer
-          // (peer memory over NVLink).  A thread holds one row, so the warp's
-          // 32 rows are staged per 32-column chunk in shared memory and stored
-          // row by row, 8 lanes per row: every store is a whole 128-byte line.
-          float* stg = reinterpret_cast<float*>(sm + RG::BYTES) + q * (32 * 33);
+          // (peer memory over NVLink) as f16.  A thread holds one row, so the
+          // warp's 32 rows are staged per 64-column chunk in shared memory and
+          // stored row by row, 8 lanes per row: every store is a whole
+          // 128-byte line.
+          uint32_t* stg = reinterpret_cast<uint32_t*>(sm + RG::BYTES) + q * (32 * 33);
           unsigned long long dst = 0;
           if (valid) {
             const int src = p.ysrc[row];
             dst = reinterpret_cast<unsigned long long>(p.ypeer[src >> 24] + (size_t)(src & 0xFFFFFF) * p.d + n0);
           }
 #pragma unroll 1
-          for (int c = 0; c < kPN; c += 32) {
-            uint32_t v[32];
-            tmem_ld32(ta + c, v);
+          for (int c = 0; c < kPN; c += 64) {
+            uint32_t v0[32], v1[32];
+            tmem_ld32(ta + c, v0);
+            tmem_ld32(ta + c + 32, v1);
 #pragma unroll
-            for (int j = 0; j < 32; j++) stg[lane * 33 + j] = __uint_as_float(v[j]) * w;
+            for (int j = 0; j < 16; j++) {
+              stg[lane * 33 + j] =
+                  h2u(__floats2half2_rn(__uint_as_float(v0[2 * j]) * w, __uint_as_float(v0[2 * j + 1]) * w));
+              stg[lane * 33 + 16 + j] =
+                  h2u(__floats2half2_rn(__uint_as_float(v1[2 * j]) * w, __uint_as_float(v1[2 * j + 1]) * w));
+            }
             __syncwarp();
 #pragma unroll
             for (int pass = 0; pass < 8; pass++) {
-              const int rr = 4 * pass + (lane >> 3), c4 = lane & 7;
+              const int rr = 4 * pass + (lane >> 3), c8 = lane & 7;
               const unsigned long long drow = __shfl_sync(0xffffffffu, dst, rr);
               if (drow) {
-                const float* sr = stg + rr * 33 + 4 * c4;
-                reinterpret_cast<float4*>(drow)[(c >> 2) + c4] = make_float4(sr[0], sr[1], sr[2], sr[3]);
+                const uint32_t* sr = stg + rr * 33 + 4 * c8;
+                reinterpret_cast<uint4*>(drow)[(c >> 3) + c8] = make_uint4(sr[0], sr[1], sr[2], sr[3]);
               }
             }
             __syncwarp();
@@ -1013,7 +1020,7 @@ void prefill_scan_launch(const int* counts, int ne, PrefillScratch* S, cudaStrea
 }
 
 int prefill_experts(const PrefillLayer& L, PrefillScratch* S, size_t rows, int* d_err, int num_sms, cudaStream_t st,
-                    const int* ysrc, float* const* ypeer, int npeers) {
+                    const int* ysrc, __half* const* ypeer, int npeers) {
   if (npeers > kPMaxPeers) return VIREO_ERR_ARG;
   const int d = L.d, fe = L.fe, ne = L.ne, Kx = prefill_kx(d), Km = Kx - d;
   rows = std::max<size_t>(rows, kPM);

@@ -83,10 +83,11 @@ int prefill_route(const PrefillLayer& L, PrefillScratch* S, const void* hb, int 
 size_t prefill_row_capacity(size_t pairs, int ne);
 int prefill_grow_rows(const PrefillLayer& L, PrefillScratch* S, size_t rows, bool need_y);
 void prefill_scan_launch(const int* counts, int ne, PrefillScratch* S, cudaStream_t st);
-// ysrc / ypeer: the expert-parallel return (row r's output to rank ysrc[r] >> 24's
-// ypeer buffer, row ysrc[r] & 0xFFFFFF); null = outputs into S->y
+// ysrc / ypeer: the expert-parallel return (row r's output, as f16, to rank
+// ysrc[r] >> 24's ypeer buffer, row ysrc[r] & 0xFFFFFF); null = fp32 outputs
+// into S->y
 int prefill_experts(const PrefillLayer& L, PrefillScratch* S, size_t rows, int* d_err, int num_sms, cudaStream_t st,
-                    const int* ysrc, float* const* ypeer, int npeers);
+                    const int* ysrc, __half* const* ypeer, int npeers);
 int prefill_tile_rows();  // rows per activation tile (row ranges per expert are padded to it)
 
 // generic kernels (any supported type/shape), generic_kernels.cu
