@@ -199,6 +199,34 @@ void gguf_moe_ep_destroy(gguf_moe_ep *ep);
 int gguf_moe_ffn_noalloc(const gguf_moe_desc *desc, const float *hb, float *x, int n_tok, int32_t *ids,
                          float *wts, void *stream);
 
+/* Shared expert.  No counterpart in the reference's code (its roadmap names
+ * shared-expert models, Qwen2-MoE and DeepSeek, as the next step): one
+ * expert FFN that every token takes beside the routed ones.  Per token
+ * x += s * down(silu(gate . hb) * (up . hb)), the reference's expert
+ * arithmetic (gguf_run.c:202-208) on the shared tensors, with
+ * s = sigmoid(gate_inp . hb) when gate_inp is given (Qwen2-MoE's
+ * ffn_gate_inp_shexp) and s = 1 otherwise (DeepSeek).  Called after
+ * gguf_moe_ffn with the same hb and x it completes such a layer:
+ * x += MoE(hb), then x += s * E(hb).  Tensors as for gguf_moe_create
+ * (DEVICE pointers, GGUF rows: gate and up [ffn][dim], down [dim][ffn];
+ * Q8_0 / Q4_K / Q6_K / Q5_0; dim % 512 == 0, ffn % 256 == 0); gate_inp:
+ * DEVICE [dim] fp32 or NULL. */
+typedef struct {
+    int dim, ffn;
+    uint32_t gate_type, up_type, down_type;
+    const void *gate, *up, *down;
+    const float *gate_inp;
+} gguf_moe_shexp_desc;
+
+typedef struct gguf_moe_shexp gguf_moe_shexp;
+
+int gguf_moe_shexp_create(const gguf_moe_shexp_desc *desc, gguf_moe_shexp **out);
+/* n_tok tokens (hb, x: DEVICE [n_tok][dim]), one launch each, stream-ordered;
+ * failures surface in gguf_moe_shexp_sync. */
+int gguf_moe_shexp_ffn(gguf_moe_shexp *sh, const float *hb, float *x, int n_tok, void *stream);
+int gguf_moe_shexp_sync(gguf_moe_shexp *sh, void *stream);
+void gguf_moe_shexp_destroy(gguf_moe_shexp *sh);
+
 #ifdef __cplusplus
 }
 #endif

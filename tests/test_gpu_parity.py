@@ -215,6 +215,55 @@ def test_moe_router_exact_ties(V, golden, name):
         m.close()
 
 
+@pytest.mark.parametrize("gated", [True, False])
+@pytest.mark.parametrize("gt,dt,ffn", [(S.GGML_Q4_K, S.GGML_Q6_K, 2048), (S.GGML_Q8_0, S.GGML_Q8_0, 768)])
+def test_shared_expert_after_routed_block(V, gated, gt, dt, ffn):
+    """A shared-expert layer (Qwen2-MoE with the sigmoid gate, DeepSeek
+    without): gguf_moe_ffn then gguf_moe_shexp_ffn on one stream give
+    x += MoE(hb), then x += s * down(silu(gate hb) * (up hb)), s =
+    sigmoid(gate_inp . hb) or 1; against the CPU restatement of the
+    reference's moe_ffn followed by the same expert arithmetic
+    (gguf_run.c:202-208) on the shared tensors, each mat-vec by the restated
+    gguf_matmul.  The shared expert's width differs from the routed
+    experts'."""
+    import ctypes as C
+    import torch
+    spec = S.MoeLayerSpec(1024, 512, 16, 4, 1, S.GGML_Q4_K, S.GGML_Q4_K, S.GGML_Q6_K)
+    L = S.MoeLayer(spec, 81)
+    sh = S.SharedExpert(spec.dim, ffn, gt, gt, dt, 81, gated=gated)
+    toks, _ = S.routed_tokens(L, 12, 81)
+    n = toks.shape[0]
+    x0 = (S.normal(81, 9, toks.size) * 0.3).astype(np.float32).reshape(toks.shape)
+    rx, rids, _ = O.PortMoe(L)(toks, x0)
+    ref = rx.astype(np.float64).copy()
+    for i in range(n):
+        g = O.matmul(gt, sh.gate, toks[i], spec.dim, ffn)
+        u = O.matmul(gt, sh.up, toks[i], spec.dim, ffn)
+        h = (g / (np.float32(1) + np.exp(-g)) * u).astype(np.float32)
+        y = O.matmul(dt, sh.down, h, ffn, spec.dim).astype(np.float64)
+        sc = 1.0 / (1.0 + np.exp(-float(np.dot(sh.gate_inp.astype(np.float64), toks[i])))) if gated else 1.0
+        ref[i] += sc * y
+    m = V.MoeLayer(L)
+    e = V.SharedExpert(sh)
+    try:
+        st = torch.cuda.Stream()
+        sp = C.c_void_p(st.cuda_stream)
+        hb, x = torch.from_numpy(toks).cuda(), torch.from_numpy(x0.copy()).cuda()
+        ids = torch.zeros((n, spec.n_used), dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+        m.ffn(hb, x, ids, stream=sp)
+        e.ffn(hb, x, stream=sp)
+        m.sync(sp)
+        e.sync(sp)
+        got, gi = x.cpu().numpy(), ids.cpu().numpy()
+    finally:
+        e.close()
+        m.close()
+    assert np.array_equal(gi, rids)
+    errs = [rel_err(got[i] - x0[i], ref[i] - x0[i]) for i in range(n)]
+    assert max(errs) < TOL, errs
+
+
 def test_moe_unsupported_layer_is_rejected(V):
     spec = S.MoeLayerSpec(512, 256, 8, 2, 0, S.GGML_F16, S.GGML_F16, S.GGML_Q8_0)
     L = S.MoeLayer(spec, 1)

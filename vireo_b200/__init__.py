@@ -55,6 +55,12 @@ class GgufMoeDesc(C.Structure):
                 ("gate_nbytes", C.c_uint64), ("up_nbytes", C.c_uint64), ("down_nbytes", C.c_uint64)]
 
 
+class GgufMoeShexpDesc(C.Structure):
+    _fields_ = [("dim", C.c_int), ("ffn", C.c_int), ("gate_type", C.c_uint32), ("up_type", C.c_uint32),
+                ("down_type", C.c_uint32), ("gate", C.c_void_p), ("up", C.c_void_p), ("down", C.c_void_p),
+                ("gate_inp", C.c_void_p)]
+
+
 class ExpertStats(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in ("requests", "hits", "misses", "bytes_read", "resident_bytes",
                                           "capacity_bytes", "experts_resident")]
@@ -104,6 +110,10 @@ def lib():
         L.gguf_moe_sync.argtypes = [C.c_void_p, C.c_void_p]
         L.gguf_moe_set_expert_ptrs.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
         L.gguf_moe_destroy.argtypes = [C.c_void_p]
+        L.gguf_moe_shexp_create.argtypes = [C.POINTER(GgufMoeShexpDesc), C.POINTER(C.c_void_p)]
+        L.gguf_moe_shexp_ffn.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]
+        L.gguf_moe_shexp_sync.argtypes = [C.c_void_p, C.c_void_p]
+        L.gguf_moe_shexp_destroy.argtypes = [C.c_void_p]
         L.gguf_moe_ffn_noalloc.argtypes = [C.POINTER(GgufMoeDesc), C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
                                            C.c_void_p, C.c_void_p]
         L.gguf_moe_destroy.restype = None
@@ -289,6 +299,40 @@ def ep_unique_id() -> bytes:
     buf = C.create_string_buffer(128)
     check(lib().gguf_moe_ep_unique_id(buf), "gguf_moe_ep_unique_id")
     return buf.raw
+
+
+class SharedExpert:
+    """A shared expert (gguf_moe_shexp_*): ``sh`` is a
+    ``vireo_b200.synth.SharedExpert`` (dim, ffn, *_type, raw GGUF ``gate``,
+    ``up``, ``down`` and an optional fp32 ``gate_inp``)."""
+
+    def __init__(self, sh, device: int = 0):
+        import torch
+        dev = torch.device("cuda", device)
+        up = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.uint8).reshape(-1)).to(dev)
+        self._keep = [up(sh.gate), up(sh.up), up(sh.down)]
+        gi = None
+        if sh.gate_inp is not None:
+            gi = torch.from_numpy(np.ascontiguousarray(sh.gate_inp, dtype=np.float32)).to(dev)
+            self._keep.append(gi)
+        g, u, dn = self._keep[:3]
+        self.desc = GgufMoeShexpDesc(sh.dim, sh.ffn, sh.gate_type, sh.up_type, sh.down_type, g.data_ptr(),
+                                     u.data_ptr(), dn.data_ptr(), gi.data_ptr() if gi is not None else None)
+        h = C.c_void_p()
+        check(lib().gguf_moe_shexp_create(C.byref(self.desc), C.byref(h)), "gguf_moe_shexp_create")
+        self.h = h
+
+    def ffn(self, hb, x, stream=None) -> None:
+        n = hb.shape[0] if hb.dim() > 1 else 1
+        check(lib().gguf_moe_shexp_ffn(self.h, hb.data_ptr(), x.data_ptr(), n, stream), "gguf_moe_shexp_ffn")
+
+    def sync(self, stream=None) -> None:
+        check(lib().gguf_moe_shexp_sync(self.h, stream), "gguf_moe_shexp_sync")
+
+    def close(self) -> None:
+        if self.h:
+            lib().gguf_moe_shexp_destroy(self.h)
+            self.h = None
 
 
 class MoeLayerEP:

@@ -832,6 +832,88 @@ int gguf_moe_set_trace(gguf_moe* m, unsigned long long* dev_buf) {
 
 int gguf_moe_grid(const gguf_moe* m) { return m ? m->grid : 0; }
 
+// ---- shared expert: a one-expert layer over the shared tensors, run by the
+// routed kernel with the gate weight formed on the device -------------------
+struct gguf_moe_shexp {
+  gguf_moe* m = nullptr;
+  float* zero_router = nullptr;  // the one-expert layer's router (never read: routed launches)
+  const float* gate_inp = nullptr;
+  const uint8_t* ptr[3] = {};
+};
+
+int gguf_moe_shexp_create(const gguf_moe_shexp_desc* desc, gguf_moe_shexp** out) {
+  if (!desc || !out || !desc->gate || !desc->up || !desc->down || desc->dim <= 0 || desc->ffn <= 0)
+    return VIREO_ERR_ARG;
+  *out = nullptr;
+  gguf_moe_shexp* sh = new gguf_moe_shexp();
+  int st = cuda_status(cudaMalloc(&sh->zero_router, (size_t)desc->dim * 4));
+  if (!st) st = cuda_status(cudaMemset(sh->zero_router, 0, (size_t)desc->dim * 4));
+  if (st) {
+    gguf_moe_shexp_destroy(sh);
+    return st;
+  }
+  gguf_moe_desc d;
+  memset(&d, 0, sizeof(d));
+  d.dim = desc->dim;
+  d.ffn_exp = desc->ffn;
+  d.n_experts = 1;
+  d.n_used = 1;
+  d.router_type = T_F32;
+  d.gate_type = desc->gate_type;
+  d.up_type = desc->up_type;
+  d.down_type = desc->down_type;
+  d.router = sh->zero_router;
+  d.gate_exps = desc->gate;
+  d.up_exps = desc->up;
+  d.down_exps = desc->down;
+  d.gate_nbytes = (uint64_t)desc->ffn * row_bytes(desc->gate_type, desc->dim);
+  d.up_nbytes = (uint64_t)desc->ffn * row_bytes(desc->up_type, desc->dim);
+  d.down_nbytes = (uint64_t)desc->dim * row_bytes(desc->down_type, desc->ffn);
+  if ((st = gguf_moe_create(&d, &sh->m))) {
+    gguf_moe_shexp_destroy(sh);
+    return st;
+  }
+  sh->gate_inp = desc->gate_inp;
+  sh->ptr[0] = (const uint8_t*)desc->gate;
+  sh->ptr[1] = (const uint8_t*)desc->up;
+  sh->ptr[2] = (const uint8_t*)desc->down;
+  *out = sh;
+  return VIREO_OK;
+}
+
+int gguf_moe_shexp_ffn(gguf_moe_shexp* sh, const float* hb, float* x, int n_tok, void* stream) {
+  if (!sh || !hb || !x || n_tok < 0) return VIREO_ERR_ARG;
+  gguf_moe* m = sh->m;
+  if (((uintptr_t)hb % 16) || ((uintptr_t)sh->gate_inp % 16)) return VIREO_ERR_ARG;
+  cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
+  MoeDecodeParams p = m->prm;
+  MoeRoute r;
+  memset(&r, 0, sizeof(r));
+  r.ids[0] = 0;
+  r.wts[0] = 1.0f;  // replaced on the device by sigmoid(gate_inp . hb) when there is a gate
+  for (int j = 0; j < 3; j++) r.ptr[0][j] = sh->ptr[j];
+  p.sh_gate = sh->gate_inp;
+  p.ids_out = nullptr;
+  p.wts_out = nullptr;
+  for (int i = 0; i < n_tok; i++) {
+    p.hb = hb + (size_t)i * p.d;
+    p.x = x + (size_t)i * p.d;
+    void* args[] = {&p, &r};
+    int st = moe_launch(m, m->rkernel, args, s);
+    if (st) return st;
+  }
+  return VIREO_OK;
+}
+
+int gguf_moe_shexp_sync(gguf_moe_shexp* sh, void* stream) { return sh ? gguf_moe_sync(sh->m, stream) : VIREO_ERR_ARG; }
+
+void gguf_moe_shexp_destroy(gguf_moe_shexp* sh) {
+  if (!sh) return;
+  if (sh->m) gguf_moe_destroy(sh->m);
+  if (sh->zero_router) cudaFree(sh->zero_router);
+  delete sh;
+}
+
 void gguf_moe_destroy(gguf_moe* m) {
   if (!m) return;
   if (m->stream) cudaStreamSynchronize(m->stream);

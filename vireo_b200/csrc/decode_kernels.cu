@@ -332,6 +332,22 @@ __device__ __forceinline__ void moe_decode_body(const MoeDecodeParams& p, const 
       }
     }
     __syncthreads();
+    if (p.sh_gate) {
+      // a shared expert's gate: sigmoid(g . hb), the dot in every CTA
+      const float* xv = reinterpret_cast<const float*>(xt.tab);
+      float z = 0.f;
+      for (int i = threadIdx.x; i < d; i += blockDim.x) z = fmaf(__ldg(p.sh_gate + i), xv[i], z);
+#pragma unroll
+      for (int o = 16; o; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+      if (lane == 0) ctl->sred[warp] = z;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        float tot = 0.f;
+        for (int w = 0; w < kConsumerWarps + kProducerWarps; w++) tot += ctl->sred[w];
+        ctl->wts[0] = 1.0f / (1.0f + expf(-tot));
+      }
+      __syncthreads();
+    }
     build_tables<SG>(reinterpret_cast<const float*>(xt.tab), xt, d / kSegElems, warp, (int)(blockDim.x / 32), lane);
     __syncthreads();
     if (threadIdx.x == 0) trace(p, kTrRouted);

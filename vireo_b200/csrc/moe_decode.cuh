@@ -92,6 +92,9 @@ struct MoeDecodeParams {
   const float* res_y;
   const float* norm_w;
   float norm_eps;
+  // optional (shared expert, routed launches): the weight of slot 0 is
+  // sigmoid(sh_gate . hb), formed by every CTA, instead of the route's
+  const float* sh_gate;
   int* err_out;               // optional, mapped host memory: the last CTA out writes the status word to
                               // [0], then 1 to [1]
 };

@@ -230,6 +230,22 @@ class MoeLayer:
         raise ValueError("router type must be F32 or F16 for margin filtering")
 
 
+class SharedExpert:
+    """A generated shared expert (the Qwen2-MoE / DeepSeek always-on expert
+    FFN): gate and up [ffn][dim], down [dim][ffn] as raw GGUF bytes, and,
+    with ``gated``, an fp32 gate vector [dim] (Qwen2-MoE's
+    ffn_gate_inp_shexp)."""
+
+    def __init__(self, dim, ffn, gate_type, up_type, down_type, seed, gated=True, layer: int = 0):
+        self.dim, self.ffn = dim, ffn
+        self.gate_type, self.up_type, self.down_type = gate_type, up_type, down_type
+        base = 1000 * (layer + 1) + 500
+        self.gate = tensor(gate_type, seed, base + 2, ffn, dim)
+        self.up = tensor(up_type, seed, base + 3, ffn, dim)
+        self.down = tensor(down_type, seed, base + 4, dim, ffn)
+        self.gate_inp = (normal(seed, base + 5, dim) * 0.05).astype(np.float32) if gated else None
+
+
 def routed_tokens(layer: MoeLayer, n_tok: int, seed: int, stream: int = 7,
                   margin: float = 1e-4, bias=None, dtype=np.float32):
     """n_tok token vectors x ~ N(0,1) whose fp64 router logits (plus an
