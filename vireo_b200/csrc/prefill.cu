@@ -12,7 +12,8 @@
 //                      accumulate; epilogue = softmax, top-k (the reference's
 //                      strict-'>' scan, ties to the lower id), renorm, and a
 //                      count per expert
-//   scan     per-expert row ranges padded to 128, the table of 128-row tiles
+//   scan     per-expert row ranges padded to 128, the table of 256-row tiles
+//            (a range's last tile may hold one 128-row sub-tile)
 //   place    every (token, slot) pair gets a row of its expert's range; the
 //            token's xa row is copied there
 //   gate/up  h = silu(X_e W_gate,e^T) * (X_e W_up,e^T) for every expert's rows
@@ -22,15 +23,20 @@
 //
 // GEMM kernel (prefill_gemm<MODE>): persistent, one CTA per SM, 16 warps:
 // warp 0 allocates TMEM (512 columns: two 128 x 256 fp32 accumulators) and
-// issues the TMA loads of the activation tiles (128 rows x 64 K, 128-byte
-// swizzle); warp 1 issues the tcgen05.mma (M 128, N 256, K 16) from one
-// thread; warps 4-11 write the weight tiles (256 rows x 64 K) into shared
-// memory, dequantising GGUF blocks straight into the swizzled f16 layout (the
-// router's weight tile comes by TMA instead); warps 12-15 are the epilogue,
-// reading their 32 TMEM lanes with tcgen05.ld.  A 4-stage ring of 48 KB
-// stages (full / empty mbarriers) connects loads to MMAs; the two
-// accumulators let the epilogue of one tile overlap the main loop of the
-// next.  Every wait is bounded (kWaitLimitNs) and sets the status word.
+// issues the TMA loads of the activation tiles (128-byte swizzle; 256 rows x
+// 64 K for the expert GEMMs, 128 rows for the router); warp 1 issues the
+// tcgen05.mma (M 128, N 256, K 16) from one thread; warps 4-11 write the
+// weight tiles (256 rows x 64 K) into shared memory, dequantising GGUF
+// blocks straight into the swizzled f16 layout (the router's weight tile
+// comes by TMA instead); warps 12-15 are the epilogue, reading their 32 TMEM
+// lanes with tcgen05.ld.  Rings of stages (full / empty mbarriers) connect
+// loads, dequantisation and MMAs.  In the expert GEMMs a tile's two 128-row
+// sub-tiles go to the two accumulators and share every converted weight
+// stage: the dequantisation, which bounded these GEMMs when each converted
+// tile fed one sub-tile, is spread over twice the MMAs (the tile's epilogue
+// no longer overlaps the next tile's MMAs).  The router GEMM alternates the
+// two accumulators between tiles so its epilogue overlaps the next tile.
+// Every wait is bounded (kWaitLimitNs) and sets the status word.
 //
 // Precision: activations and dequantised weights are f16 (the bf16 input is
 // exact in f16 for |x| in [2^-14, 65504]); a weight is round(scale * q) with
@@ -71,7 +77,7 @@ constexpr uint32_t kPRawGU = kPN * 48, kPRawDN = kPN * 80;
 // several stages ahead of the MMA so their latency is hidden; only a few
 // 32 KB converted tiles need to be resident.
 #ifndef VIREO_P_NA_GU
-#define VIREO_P_NA_GU 4
+#define VIREO_P_NA_GU 2
 #endif
 #ifndef VIREO_P_NB_GU
 #define VIREO_P_NB_GU 3
@@ -80,14 +86,22 @@ constexpr uint32_t kPRawGU = kPN * 48, kPRawDN = kPN * 80;
 #define VIREO_P_NR_GU 4
 #endif
 #ifndef VIREO_P_NA_DN
-#define VIREO_P_NA_DN 3
+#define VIREO_P_NA_DN 2
 #endif
 #ifndef VIREO_P_NB_DN
-#define VIREO_P_NB_DN 3
+#define VIREO_P_NB_DN 2
 #endif
 #ifndef VIREO_P_NR_DN
 #define VIREO_P_NR_DN 3
 #endif
+// The expert GEMMs (gate/up, down) take 256-row tiles: two 128-row
+// sub-tiles in two TMEM accumulators share every converted weight stage, so
+// each dequantised tile feeds twice the MMAs.  The router GEMM keeps 128-row
+// tiles and double-buffered accumulators.
+template <int MODE>
+__host__ __device__ constexpr int psub() {
+  return MODE == 0 ? 1 : 2;
+}
 template <int MODE>
 struct PRing {
   // activation stages, converted weight stages, raw chunk stages
@@ -95,7 +109,8 @@ struct PRing {
   static constexpr int NB = MODE == 2 ? VIREO_P_NB_DN : (MODE == 1 ? VIREO_P_NB_GU : 3);
   static constexpr int NR = MODE == 1 ? VIREO_P_NR_GU : (MODE == 2 ? VIREO_P_NR_DN : 1);
   static constexpr uint32_t RB = MODE == 2 ? kPRawDN : kPRawGU;   // raw chunk bytes
-  static constexpr uint32_t OFF_B = NA * kPStageA;
+  static constexpr uint32_t SA = psub<MODE>() * kPStageA;          // activation stage bytes
+  static constexpr uint32_t OFF_B = NA * SA;
   static constexpr uint32_t OFF_R = OFF_B + NB * kPStageB;
   static constexpr uint32_t BYTES = OFF_R + (MODE == 0 ? 0u : NR * RB);
 };
@@ -311,8 +326,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&fullA[a], kPStageA);
-          tma_load_2d(sA + a * kPStageA, &tmA, kt * kPK, t.row0, &fullA[a]);
+          mbar_arrive_expect_tx(&fullA[a], RG::SA);
+          tma_load_2d(sA + a * RG::SA, &tmA, kt * kPK, t.row0, &fullA[a]);
           if constexpr (MODE == P_ROUTER) {
             mbar_arrive_expect_tx(&fullB[b], kPStageB);
             tma_load_2d(sB + b * kPStageB, &tmB, kt * kPK, 0, &fullB[b]);
@@ -358,10 +373,19 @@ __global__ void __launch_bounds__(kPThreads, 1)
       uint32_t g = 0;
       int it = 0;
       for (int item = blockIdx.x; item < n_items && !abort_s; item += gridDim.x, it++) {
-        const int b2 = it & 1;
-        if (it >= 2 && !pwait(&tempty[b2], ((it >> 1) - 1) & 1, &abort_s, p.err)) break;
+        // router: two 256-column accumulators, alternating (the epilogue of
+        // one tile overlaps the next tile's MMAs); expert GEMMs: one pair of
+        // accumulators, sub-tile s in columns 256 s .. 256 s + 255
+        const int b2 = MODE == P_ROUTER ? (it & 1) : 0;
+        if constexpr (MODE == P_ROUTER) {
+          if (it >= 2 && !pwait(&tempty[b2], ((it >> 1) - 1) & 1, &abort_s, p.err)) break;
+        } else {
+          if (it >= 1 && !pwait(&tempty[0], (it - 1) & 1, &abort_s, p.err)) break;
+        }
         tc_fence_after();
         const uint32_t dt = tmem + (uint32_t)(b2 * kPN);
+        // the second sub-tile only when the tile has rows there
+        const bool two = MODE != P_ROUTER && tile_of(item / p.n_ntiles).nrows > kPM;
         bool ok = true;
         for (int kt = 0; kt < p.nk; kt++, g++) {
           const int a = (int)(g % NA), b = (int)(g % NB);
@@ -370,10 +394,16 @@ __global__ void __launch_bounds__(kPThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint64_t da = umma_desc_sw128(sA + a * kPStageA), db = umma_desc_sw128(sB + b * kPStageB);
+          const uint64_t da = umma_desc_sw128(sA + a * RG::SA), db = umma_desc_sw128(sB + b * kPStageB);
 #pragma unroll
           for (int kk = 0; kk < kPK / 16; kk++)
             umma_f16_ss(dt, da + 2 * kk, db + 2 * kk, idesc, (kt | kk) != 0 ? 1u : 0u);
+          if (two) {
+            const uint64_t da1 = umma_desc_sw128(sA + a * RG::SA + kPStageA);
+#pragma unroll
+            for (int kk = 0; kk < kPK / 16; kk++)
+              umma_f16_ss(dt + (uint32_t)kPN, da1 + 2 * kk, db + 2 * kk, idesc, (kt | kk) != 0 ? 1u : 0u);
+          }
           umma_commit(&emptyA[a]);
           umma_commit(&emptyB[b]);
         }
@@ -458,18 +488,20 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const int q = warp & 3;
     int it = 0;
     for (int item = blockIdx.x; item < n_items && !abort_s; item += gridDim.x, it++) {
-      const int b = it & 1;
+      const int b = MODE == P_ROUTER ? (it & 1) : 0;
       int w_ok = 1;
-      if (lane == 0) w_ok = pwait(&tfull[b], (it >> 1) & 1, &abort_s, p.err);
+      if (lane == 0) w_ok = pwait(&tfull[b], MODE == P_ROUTER ? (it >> 1) & 1 : it & 1, &abort_s, p.err);
       w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
       if (!w_ok) break;
       tc_fence_after();
       const int mt = item / p.n_ntiles, nt = item - mt * p.n_ntiles;
       const PTile t = tile_of(mt);
-      const int rt = 32 * q + lane;  // row within the tile
+      for (int sub = 0; sub < psub<MODE>(); sub++) {
+      if (sub > 0 && t.nrows <= kPM) break;  // no rows in the second sub-tile
+      const int rt = kPM * sub + 32 * q + lane;  // row within the tile
       const bool valid = rt < t.nrows;
       const int row = t.row0 + rt;
-      const uint32_t ta = tmem + (uint32_t)(b * kPN) + ((uint32_t)(32 * q) << 16);
+      const uint32_t ta = tmem + (uint32_t)((b + sub) * kPN) + ((uint32_t)(32 * q) << 16);
       if constexpr (MODE == P_ROUTER) {
         // logits = hi + lo (+ bias); softmax; top-k; renorm  (gguf_run.c:187-192)
         const int ne = p.ne;
@@ -627,6 +659,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         }
         }
       }
+      }  // sub-tiles
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
@@ -766,30 +799,34 @@ __global__ void prefill_pack_dn(const uint8_t* const* exp_tab, const int* own, i
 
 // ---- scan: padded row ranges, the tile table, placement cursors ------------
 __global__ void prefill_scan(const int* counts, int ne, int* cursor, PTile* tiles, int* n_mtiles) {
+  // ranges padded to kPM rows; tiles of up to 2 kPM rows (the expert GEMMs'
+  // two sub-tiles), a range's last tile possibly one sub-tile
+  constexpr int kT = 2 * kPM;
   __shared__ int mts[256], offs[256];
   const int e = threadIdx.x;
   const int n = e < ne ? counts[e] : 0;
-  mts[e] = (n + kPM - 1) / kPM;
+  mts[e] = (n + kT - 1) / kT;
+  offs[e] = (n + kPM - 1) / kPM * kPM;
   __syncthreads();
   if (e == 0) {
     int mt = 0, off = 0;
     for (int i = 0; i < ne; i++) {
-      const int m = mts[i];
+      const int m = mts[i], pad = offs[i];
       mts[i] = mt;
       offs[i] = off;
       mt += m;
-      off += m * kPM;
+      off += pad;
     }
     *n_mtiles = mt;
   }
   __syncthreads();
   if (e < ne) {
     cursor[e] = offs[e];
-    for (int i = 0; i * kPM < n; i++) {
+    for (int i = 0; i * kT < n; i++) {
       PTile t;
       t.e = e;
-      t.row0 = offs[e] + i * kPM;
-      t.nrows = min(kPM, n - i * kPM);
+      t.row0 = offs[e] + i * kT;
+      t.nrows = min(kT, n - i * kT);
       tiles[mts[e] + i] = t;
     }
   }
@@ -1026,7 +1063,7 @@ int prefill_experts(const PrefillLayer& L, PrefillScratch* S, size_t rows, int* 
   rows = std::max<size_t>(rows, kPM);
   CUtensorMap mA_gu, mA_d, mM;
   int rc;
-  if ((rc = make_map(&mA_gu, S->xg, rows, Kx, kPM)) || (rc = make_map(&mA_d, S->hg, rows, fe, kPM)) ||
+  if ((rc = make_map(&mA_gu, S->xg, rows, Kx, 2 * kPM)) || (rc = make_map(&mA_d, S->hg, rows, fe, 2 * kPM)) ||
       (rc = make_map(&mM, S->minmat, (uint64_t)ne * 2 * fe, Km, 128)))
     return rc;
   set_attrs_once();
