@@ -6,8 +6,9 @@
 // per row or per group of rows, executed by the TMA engine, completing on the
 // stage's mbarrier; never multicast).  The consumer warps run the
 // tensor-core segment kernels below over each tile's 256-value segments:
-// the MoE kernel gives a whole tile to one warp (segments in order, in
-// registers); the stand-alone GEMV deals a tile's segments over the warps
+// the MoE kernel gives a whole tile to one warp, or to a warp pair that
+// splits its segments (segments in order, in registers); the stand-alone
+// GEMV deals a tile's segments over the warps
 // (consume_unit) and the warp that completes the tile sums the segment
 // partials in segment order.  Either way the result does not depend on
 // which warp computed what.
