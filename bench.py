@@ -413,10 +413,57 @@ def run_cfg1(args, wl):
         tt = torch.tensor([el], device=dev)
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
         e2e_tps = e2e_iters * n_e2e * world / float(tt.item())
+    # the step's tokens through the host API in one call per layer copy (the
+    # step's T tokens split over the NL copies, tokens of a call one after
+    # another on the device): one round trip per call instead of per token
+    per_call = max(1, T // NL)
+    hb_s = torch.from_numpy(np.ascontiguousarray(np.resize(toks, (NL * per_call, spec.dim)))).pin_memory()
+    x_s = torch.zeros_like(hb_s).pin_memory()
+    ids_s = torch.zeros((NL * per_call, spec.n_used), dtype=torch.int32).pin_memory()
+    w_s = torch.zeros((NL * per_call, spec.n_used), dtype=torch.float32).pin_memory()
     d = spec.dim
-    e2e = {"value": e2e_tps, "unit": "tok/s", "h2d_bytes_per_step": T * 2 * 4 * d,
+    bcalls = [(layers[j].h, hb_s.data_ptr() + j * per_call * 4 * d, x_s.data_ptr() + j * per_call * 4 * d, per_call,
+               ids_s.data_ptr() + j * per_call * 4 * spec.n_used, w_s.data_ptr() + j * per_call * 4 * spec.n_used)
+              for j in range(NL)]
+
+    def e2e_batched_step():
+        for a in bcalls:
+            if fh(*a):
+                raise RuntimeError("gguf_moe_ffn_host failed")
+
+    e2e_batched_step()
+    t0 = time.perf_counter()
+    for _ in range(e2e_iters):
+        e2e_batched_step()
+    elb = time.perf_counter() - t0
+    if world > 1:
+        tt = torch.tensor([elb], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        elb = float(tt.item())
+    e2e_b = e2e_iters * NL * per_call * world / elb
+    # the same grouping on device pointers (tokens of one copy back to back):
+    # shows whether consecutive tokens on one copy gain from L2
+    gcalls = [(layers[(i // per_call) % NL].h, hb.data_ptr() + (i % nt) * d * 4, x.data_ptr() + (i % nt) * d * 4, 1,
+               None, None, sp) for i in range(NL * per_call)]
+    torch.cuda.synchronize(dev)
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record(stream)
+    for _ in range(max(1, args.steps // 4)):
+        for a in gcalls:
+            if ffn(*a):
+                raise RuntimeError("gguf_moe_ffn failed")
+    g1.record(stream)
+    torch.cuda.synchronize(dev)
+    grouped_tps = max(1, args.steps // 4) * NL * per_call / (g0.elapsed_time(g1) / 1e3)
+    e2e = {"value": e2e_b, "unit": "tok/s", "h2d_bytes_per_step": T * 2 * 4 * d,
            "d2h_bytes_per_step": T * (4 * d + 8 * spec.n_used),
-           "note": "gguf_moe_ffn_host per token, pinned host buffers"}
+           "note": f"gguf_moe_ffn_host, pinned host buffers: the step's {T} tokens in {NL} calls of {per_call} "
+                   f"tokens (one per layer copy), x / ids / wts returned and the status checked per call",
+           "per_token_calls": {"value": e2e_tps, "unit": "tok/s",
+                               "note": "one gguf_moe_ffn_host call per token (a synchronous decode hook)"},
+           "device_rate_same_grouping": {"value": grouped_tps, "unit": "tok/s",
+                                         "note": "gguf_moe_ffn on device pointers with the tokens grouped by layer "
+                                                 "copy as in the host calls (L2 reuse check against value)"}}
 
     peak, peak_kind = peaks()
     per_launch_s = t_sec / launches if world == 1 else ms / 1e3 / launches
