@@ -115,3 +115,33 @@ def test_prefill_deterministic_and_unsupported():
         assert V.lib().gguf_moe_prefill(m.h, hb.data_ptr(), xd.data_ptr(), 4, None, None, None, None) == -3
     finally:
         m.close()
+
+
+@pytest.mark.parametrize("ne,k", [(16, 4), (64, 8), (128, 8)])
+def test_prefill_router_exact_ties(ne, k):
+    """Experts 2j and 2j + 1 share one router row, so every routing
+    probability is tied with its partner's bit for bit, and the selection
+    must take the lower id first and keep it when a larger probability is
+    inserted ahead of the pair (the reference's strict '>' scan from id 0,
+    gguf_run.c:190-191).  Router entries are multiples of 1/64 and the hidden
+    values small integers, so every logit is exact in bf16 operands with any
+    summation order and distinct logits differ by at least 1/64: ids
+    bit-exact against the oracle on every token, over several row tiles."""
+    import torch
+    assert torch.cuda.is_available()
+    import vireo_b200 as V
+    spec = S.MoeLayerSpec(512, 256, ne, k, 1, S.GGML_Q4_K, S.GGML_Q4_K, S.GGML_Q6_K)
+    L = S.MoeLayer(spec, 93)
+    R = L.router.view(np.float32).reshape(ne, spec.dim)
+    R[:] = ((S.u64(93, 1, ne * spec.dim) % np.uint64(17)).astype(np.float32) - 8.0).reshape(R.shape) / 64.0
+    R[1::2] = R[0::2]
+    T = 300
+    toks = ((S.u64(93, 2, T * spec.dim) % np.uint64(5)).astype(np.float32) - 2.0).reshape(T, spec.dim)
+    x0 = (S.normal(93, 3, toks.size) * 0.3).astype(np.float32).reshape(toks.shape)
+    x, ids, wts = run_prefill(V, L, toks, x0, None)
+    rx, rids, rwts = O.PortMoe(L)(toks, x0, None)
+    assert (rids[:, 0] % 2 == 0).all()
+    assert np.array_equal(ids, rids), np.argwhere(ids != rids)[:5]
+    assert rel_err(wts, rwts) < 1e-5, rel_err(wts, rwts)
+    worst = max(rel_err(x[i] - x0[i], rx[i] - x0[i]) for i in range(T))
+    assert worst < TOL, worst

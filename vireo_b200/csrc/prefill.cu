@@ -63,6 +63,7 @@ constexpr int kPN = 256;   // weight rows per tile
 constexpr int kPK = 64;    // K per stage
 constexpr int kPThreads = 512;
 constexpr int kDqWarp0 = 4, kDqWarps = 8, kEpiWarp0 = 12;
+constexpr int kPWarps = kPThreads / 32;
 constexpr int kPTopK = 8;  // prefill top-k limit (held in registers)
 constexpr int kPMaxPeers = 8;  // expert-parallel ranks (one node)
 constexpr uint32_t kPStageA = kPM * kPK * 2, kPStageB = kPN * kPK * 2;
@@ -118,9 +119,12 @@ constexpr uint32_t cmax(uint32_t a, uint32_t b) { return a > b ? a : b; }
 // the down GEMM's epilogue stages each warp's 32-row x 64-column f16 output
 // block here (row stride 33 words) when its rows return to other ranks
 constexpr uint32_t kPEpiStage = 4 * 32 * 33 * 4;
+// the router's epilogue spills each tile's logits here ([128][129] floats)
+// so that twelve warps share the softmax and top-k
+constexpr uint32_t kPLogits = kPM * (128 + 1) * 4;
 template <int MODE>
 constexpr uint32_t psmem() {
-  return 1024 + PRing<MODE>::BYTES + (MODE == 2 ? kPEpiStage : 0u);
+  return 1024 + PRing<MODE>::BYTES + (MODE == 2 ? kPEpiStage : 0u) + (MODE == 0 ? kPLogits : 0u);
 }
 static_assert(psmem<0>() <= 227 * 1024 && psmem<1>() <= 227 * 1024 && psmem<2>() <= 227 * 1024,
               "prefill rings exceed the shared memory of one CTA");
@@ -415,6 +419,160 @@ __global__ void __launch_bounds__(kPThreads, 1)
       volatile int never = 0;
       mbar_wait(&drain, 0, &never);
     }
+  } else if (MODE == P_ROUTER && warp >= kDqWarp0) {
+    if constexpr (MODE == P_ROUTER) {
+      // ---- router epilogue: logits = hi + lo (+ bias); softmax; top-k; renorm
+      // (gguf_run.c:187-192).  The four epilogue warps move each row's logits
+      // from TMEM to shared memory and free the accumulator; then the twelve
+      // warps 4-15 (the dequantisation warps have no weights to convert here)
+      // take the rows, eight lanes per row, sixteen experts per lane: the
+      // max and the sum by a 3-step xor tree, each lane's top k of its
+      // experts by the reference's rule (strict '>' in increasing id, so the
+      // lower id stays ahead of an equal one; NaN never enters), then k
+      // rounds that take the best head among the eight lanes under (value
+      // desc, id asc).  Slots beyond the valid experts hold id -1, weight -1.
+      float* lgs = reinterpret_cast<float*>(sm + RG::BYTES);
+      constexpr int kSelThreads = 32 * (kPWarps - kDqWarp0), kGroups = kSelThreads / 8;
+      static_assert(kGroups % 4 == 0, "a warp's four row groups stay together across iterations");
+      const int st = threadIdx.x - 32 * kDqWarp0, grp = st >> 3, j = st & 7;
+      const int ne = p.ne, k = p.k;
+      int it = 0;
+      for (int item = blockIdx.x; item < n_items; item += gridDim.x, it++) {
+        const PTile t = tile_of(item);
+        if (warp >= kEpiWarp0) {
+          const int q = warp & 3, b = it & 1;
+          int w_ok = 0;
+          if (!__any_sync(0xffffffffu, abort_s != 0)) {
+            if (lane == 0) w_ok = pwait(&tfull[b], (it >> 1) & 1, &abort_s, p.err);
+            w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
+          }
+          if (w_ok) {
+            tc_fence_after();
+            const int rt = 32 * q + lane;
+            const uint32_t ta = tmem + (uint32_t)(b * kPN) + ((uint32_t)(32 * q) << 16);
+            for (int c = 0; c < 128; c += 32) {
+              uint32_t vh[32], vl[32];
+              tmem_ld32(ta + c, vh);
+              tmem_ld32(ta + 128 + c, vl);
+#pragma unroll
+              for (int jj = 0; jj < 32; jj++) {
+                const int e = c + jj;
+                lgs[rt * 129 + e] = e < ne ? __uint_as_float(vh[jj]) + __uint_as_float(vl[jj]) + (p.bias ? p.bias[e] : 0.f)
+                                           : -INFINITY;
+              }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[b]);
+          }
+        }
+        asm volatile("bar.sync 5, %0;" ::"r"(kSelThreads) : "memory");  // the tile's logits are in shared memory
+        if (!__any_sync(0xffffffffu, abort_s != 0)) {
+          // a warp takes four rows at a time, so all its lanes run the same
+          // iterations (the shuffles name the whole warp); lanes past the
+          // tile's last row compute on rows the logit buffer holds and write
+          // nothing
+          for (int r = grp; (r & ~3) < t.nrows; r += kGroups) {
+            const float* L = lgs + r * 129 + 16 * j;
+            float ex[16];
+            float mx = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+              ex[i] = L[i];
+              mx = fmaxf(mx, ex[i]);
+            }
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            float sum = 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+              ex[i] = 16 * j + i < ne ? expf(ex[i] - mx) : 0.f;
+              sum += ex[i];
+            }
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+            float tv[kPTopK];
+            int ti[kPTopK];
+#pragma unroll
+            for (int i = 0; i < kPTopK; i++) {
+              tv[i] = -1.f;
+              ti[i] = -1;
+            }
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+              const int e = 16 * j + i;
+              if (e >= ne) continue;
+              float pe = ex[i] / sum;  // NaN never enters (strict '>')
+              int pe_i = e;
+              // insert before the first strictly smaller entry; everything
+              // after it shifts down one slot (an entry equal to its new
+              // neighbour keeps its place ahead of it: it has the lower id)
+              bool moved = false;
+#pragma unroll
+              for (int u = 0; u < kPTopK; u++) {
+                if (u < k && (moved || pe > tv[u])) {
+                  moved = true;
+                  const float fv = tv[u];
+                  const int fi = ti[u];
+                  tv[u] = pe;
+                  ti[u] = pe_i;
+                  pe = fv;
+                  pe_i = fi;
+                }
+              }
+            }
+            float ov[kPTopK];
+            int oi[kPTopK];
+#pragma unroll
+            for (int u = 0; u < kPTopK; u++) {
+              float bv = tv[0];
+              int bi = ti[0];
+#pragma unroll
+              for (int o = 1; o < 8; o <<= 1) {
+                const float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+                // (value desc, id asc); an empty head (-1) loses to any expert
+                if (i2 >= 0 && (bi < 0 || v2 > bv || (v2 == bv && i2 < bi))) {
+                  bv = v2;
+                  bi = i2;
+                }
+              }
+              ov[u] = bv;
+              oi[u] = bi;
+              if (bi >= 0 && ti[0] == bi) {  // the lane that held it moves to its next
+#pragma unroll
+                for (int w2 = 0; w2 < kPTopK - 1; w2++) {
+                  tv[w2] = tv[w2 + 1];
+                  ti[w2] = ti[w2 + 1];
+                }
+                tv[kPTopK - 1] = -1.f;
+                ti[kPTopK - 1] = -1;
+              }
+            }
+            if (j == 0 && r < t.nrows) {
+              float ws = 0.f;
+#pragma unroll
+              for (int u = 0; u < kPTopK; u++)
+                if (u < k) ws = ws + (oi[u] >= 0 ? ov[u] : -1.f);
+              const int row = t.row0 + r;
+#pragma unroll
+              for (int u = 0; u < kPTopK; u++) {
+                if (u < k) {
+                  const float v = oi[u] >= 0 ? ov[u] : -1.f;
+                  const float w = (p.renorm && ws > 0.f) ? v / ws : v;
+                  p.ids[(size_t)row * k + u] = oi[u];
+                  p.wts[(size_t)row * k + u] = w;
+                  if (oi[u] >= 0) atomicAdd(&p.counts[oi[u]], 1);
+                }
+              }
+            }
+          }
+        }
+        asm volatile("bar.sync 5, %0;" ::"r"(kSelThreads) : "memory");  // the logit buffer is free for the next tile
+      }
+    }
   } else if (warp >= kDqWarp0 && warp < kDqWarp0 + kDqWarps) {
     if constexpr (MODE != P_ROUTER) {
       // ---- weight tiles: raw chunks -> swizzled f16 in shared memory ----------
@@ -502,81 +660,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
       const bool valid = rt < t.nrows;
       const int row = t.row0 + rt;
       const uint32_t ta = tmem + (uint32_t)((b + sub) * kPN) + ((uint32_t)(32 * q) << 16);
-      if constexpr (MODE == P_ROUTER) {
-        // logits = hi + lo (+ bias); softmax; top-k; renorm  (gguf_run.c:187-192)
-        const int ne = p.ne;
-        float mx = -INFINITY;
-        for (int c = 0; c < 128; c += 32) {
-          uint32_t vh[32], vl[32];
-          tmem_ld32(ta + c, vh);
-          tmem_ld32(ta + 128 + c, vl);
-#pragma unroll
-          for (int j = 0; j < 32; j++)
-            if (c + j < ne) {
-              const float l = __uint_as_float(vh[j]) + __uint_as_float(vl[j]) + (p.bias ? p.bias[c + j] : 0.f);
-              mx = (j == 0 && c == 0) ? l : (l > mx ? l : mx);
-            }
-        }
-        float sum = 0.f;
-        for (int c = 0; c < 128; c += 32) {
-          uint32_t vh[32], vl[32];
-          tmem_ld32(ta + c, vh);
-          tmem_ld32(ta + 128 + c, vl);
-#pragma unroll
-          for (int j = 0; j < 32; j++)
-            if (c + j < ne) {
-              const float l = __uint_as_float(vh[j]) + __uint_as_float(vl[j]) + (p.bias ? p.bias[c + j] : 0.f);
-              sum += expf(l - mx);
-            }
-        }
-        float tv[kPTopK];
-        int ti[kPTopK];
-#pragma unroll
-        for (int i = 0; i < kPTopK; i++) {
-          tv[i] = -1.f;
-          ti[i] = -1;
-        }
-        const int k = p.k;
-        for (int c = 0; c < 128; c += 32) {
-          uint32_t vh[32], vl[32];
-          tmem_ld32(ta + c, vh);
-          tmem_ld32(ta + 128 + c, vl);
-#pragma unroll
-          for (int j = 0; j < 32; j++) {
-            const int e = c + j;
-            if (e >= ne) continue;
-            const float l = __uint_as_float(vh[j]) + __uint_as_float(vl[j]) + (p.bias ? p.bias[e] : 0.f);
-            float pe = expf(l - mx) / sum;  // NaN never enters (strict '>')
-            int pe_i = e;
-#pragma unroll
-            for (int i = 0; i < kPTopK; i++) {
-              if (i < k && pe > tv[i]) {
-                const float fv = tv[i];
-                const int fi = ti[i];
-                tv[i] = pe;
-                ti[i] = pe_i;
-                pe = fv;
-                pe_i = fi;
-              }
-            }
-          }
-        }
-        float ws = 0.f;
-#pragma unroll
-        for (int i = 0; i < kPTopK; i++)
-          if (i < k) ws = ws + tv[i];
-        if (valid) {
-#pragma unroll
-          for (int i = 0; i < kPTopK; i++) {
-            if (i < k) {
-              const float w = (p.renorm && ws > 0.f) ? tv[i] / ws : tv[i];
-              p.ids[(size_t)row * k + i] = ti[i];
-              p.wts[(size_t)row * k + i] = w;
-              if (ti[i] >= 0) atomicAdd(&p.counts[ti[i]], 1);
-            }
-          }
-        }
-      } else if constexpr (MODE == P_GATEUP) {
+      if constexpr (MODE == P_GATEUP) {
         // h = silu(g) * u (gguf_run.c:206), f16, columns permuted as xa's
         const int f0 = nt * 128;
 #pragma unroll 1
