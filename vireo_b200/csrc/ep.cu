@@ -27,11 +27,10 @@
 //             kernel: GEMM + return)
 //   combine   after a barrier, x[t] += sum over rank order of the returned
 //             rows in fp32 (the reference's combine order, gguf_run.c:209, 213)
-// Every output row comes from the same GEMM arithmetic as on one GPU and the
-// combine order is the same; the f16 rounding of the returned rows (half
-// the NVLink bytes of fp32 rows) is the only difference from
-// gguf_moe_prefill on one GPU, so results agree to the f16 rounding of each
-// expert's weighted output (tested at the 2e-3 bar of the decode path).
+// Every output row comes from the same GEMM arithmetic as on one GPU, is
+// rounded to f16 as on one GPU, and the combine (prefill_combine) is the
+// same kernel in the same order, so the results equal gguf_moe_prefill's on
+// one GPU for the same routing.
 //
 // Ordering across ranks: every rank's writes into a peer's buffers are
 // followed by a system-scope fence and the end of the kernel; then a barrier
@@ -70,7 +69,6 @@ namespace vireo {
 
 constexpr int kEpMaxWorld = 8;    // one node
 constexpr int kEpMaxExperts = 128;
-constexpr int kEpMaxTopK = 8;    // the batched path's top-k limit
 constexpr double kEpWaitSeconds = 60.0;
 
 // ---- NCCL entry points, resolved once ---------------------------------------
@@ -248,42 +246,6 @@ __global__ void ep_dispatch(const __half* xa, const int32_t* ids, const float* w
   __threadfence_system();
 }
 
-// x[t] += sum over rank order of the returned f16 rows, in fp32
-// (prefill_combine's order), four columns per thread; the slots' loads are
-// issued together
-__global__ void ep_combine(const int32_t* ids, const __half* yret, float* x, int T, int k, int d) {
-  const int t = blockIdx.x;
-  if (t >= T) return;
-  bool on[kEpMaxTopK];
-#pragma unroll
-  for (int i = 0; i < kEpMaxTopK; i++) on[i] = i < k && ids[(size_t)t * k + i] >= 0;
-  const int d4 = d / 4;
-  const uint2* y4 = reinterpret_cast<const uint2*>(yret) + (size_t)t * k * d4;
-  float4* x4 = reinterpret_cast<float4*>(x) + (size_t)t * d4;
-  for (int c = threadIdx.x; c < d4; c += blockDim.x) {
-    uint2 v[kEpMaxTopK];
-#pragma unroll
-    for (int i = 0; i < kEpMaxTopK; i++)
-      if (on[i]) v[i] = __ldcs(y4 + (size_t)i * d4 + c);
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int i = 0; i < kEpMaxTopK; i++)
-      if (on[i]) {
-        const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&v[i].x));
-        const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&v[i].y));
-        acc.x = __fadd_rn(acc.x, lo.x);
-        acc.y = __fadd_rn(acc.y, lo.y);
-        acc.z = __fadd_rn(acc.z, hi.x);
-        acc.w = __fadd_rn(acc.w, hi.y);
-      }
-    float4 xv = x4[c];
-    xv.x = __fadd_rn(xv.x, acc.x);
-    xv.y = __fadd_rn(xv.y, acc.y);
-    xv.z = __fadd_rn(xv.z, acc.z);
-    xv.w = __fadd_rn(xv.w, acc.w);
-    x4[c] = xv;
-  }
-}
 
 }  // namespace vireo
 
@@ -600,7 +562,7 @@ int gguf_moe_prefill_ep(gguf_moe_ep* ep, const void* hb_bf16, float* x, int n_to
   S->c_xg = ep->rows_cap * Kx * 2;
   S->c_wrow = ep->rows_cap * 4;
   const size_t rows = ep->rows_cap;
-  if ((rc = prefill_grow_rows(L, S, rows, false))) return rc;  // outputs go to the sources, not S->y
+  if ((rc = prefill_grow_rows(L, S, rows))) return rc;
   // dispatch straight into the owners' operands, then every rank's rows are in place
   if (pairs)
     ep_dispatch<<<(unsigned)((pairs + 7) / 8), 256, 0, s>>>(S->xa, S->ids, S->wts, ep->d_owner, ep->d_pos,
@@ -610,7 +572,7 @@ int gguf_moe_prefill_ep(gguf_moe_ep* ep, const void* hb_bf16, float* x, int n_to
   prefill_scan_launch(ep->d_totals, ne, S, s);
   if ((rc = prefill_experts(L, S, rows, v.err, v.num_sms, s, ep->ysrc, ep->p_yret, G))) return rc;
   ep_signal<<<1, 32, 0, s>>>(ep->sig, P, kSigReturned, call, G, r, v.err);
-  if (n_tok > 0) ep_combine<<<n_tok, 256, 0, s>>>(S->ids, ep->yret, x, n_tok, k, d);
+  prefill_combine_launch(S->ids, ep->yret, x, n_tok, k, d, s);
   if (ids_out && pairs && cudaMemcpyAsync(ids_out, S->ids, pairs * 4, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
     return cuda_status(cudaGetLastError());
   if (wts_out && pairs && cudaMemcpyAsync(wts_out, S->wts, pairs * 4, cudaMemcpyDeviceToDevice, s) != cudaSuccess)

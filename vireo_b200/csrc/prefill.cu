@@ -18,8 +18,9 @@
 //            token's xa row is copied there
 //   gate/up  h = silu(X_e W_gate,e^T) * (X_e W_up,e^T) for every expert's rows
 //            (tcgen05 GEMM, Q4_K weights dequantised to f16 in shared memory)
-//   down     y = w_pair * (H_e W_down,e^T) (Q6_K weights, f16)
-//   combine  x[t] += sum over rank t of y(t, slot), in rank order
+//   down     y = w_pair * (H_e W_down,e^T) (Q6_K weights, f16), rounded to
+//            f16 into the pair's token-slot row of the return buffer
+//   combine  x[t] += sum over slots of y(t, slot), in slot order, fp32
 //
 // GEMM kernel (prefill_gemm<MODE>): persistent, one CTA per SM, 16 warps:
 // warp 0 allocates TMEM (512 columns: two 128 x 256 fp32 accumulators) and
@@ -29,7 +30,7 @@
 // weight tiles (256 rows x 64 K) into shared memory, dequantising GGUF
 // blocks straight into the swizzled f16 layout (the router's weight tile
 // comes by TMA instead); warps 12-15 are the epilogue, reading their 32 TMEM
-// lanes with tcgen05.ld.  Rings of stages (full / empty mbarriers) connect
+// lanes with tcgen05.ld (the router's top-k runs on warps 4-15).  Rings of stages (full / empty mbarriers) connect
 // loads, dequantisation and MMAs.  In the expert GEMMs a tile's two 128-row
 // sub-tiles go to the two accumulators and share every converted weight
 // stage: the dequantisation, which bounded these GEMMs when each converted
@@ -154,12 +155,13 @@ struct PrefillParams {
   __half* hg;  // [rows][fe], columns permuted as xa's
   // down
   const float* wrow;
-  float* y;  // [rows][d]
-  // expert-parallel return (ep.cu): when ysrc is set, row r's output goes to
-  // rank ysrc[r] >> 24's buffer ypeer[rank], row ysrc[r] & 0xFFFFFF, instead
-  // of y (peer memory: the NVLink write overlaps the next tile's MMAs)
+  // row r's output, as f16, goes to rank ysrc[r] >> 24's buffer
+  // ypeer[rank], row ysrc[r] & 0xFFFFFF: the token slot's row of the
+  // caller's return buffer (its own on one GPU; on several, peer memory
+  // written over NVLink while the next tile's MMAs run)
   const int* ysrc;
-  __half* ypeer[kPMaxPeers];  // f16 rows (half the NVLink bytes of fp32)
+  __half* ypeer[kPMaxPeers];
+  int remote;  // some ypeer is another GPU's memory
   int* err;
 };
 
@@ -689,15 +691,15 @@ __global__ void __launch_bounds__(kPThreads, 1)
           }
         }
       } else {
-        // y = w * (H W_down^T), fp32
+        // y = w * (H W_down^T), rounded to f16 into its token slot's row of
+        // the return buffer (on several GPUs, the source rank's; half the
+        // bytes of fp32, on NVLink and in the combine).  A thread holds one
+        // row, so the warp's 32 rows are staged per 64-column chunk in shared
+        // memory and stored row by row, 8 lanes per row: every store is a
+        // whole 128-byte line.
         const int n0 = nt * kPN;
         const float w = valid ? p.wrow[row] : 0.f;
-        if (p.ysrc) {
-          // expert-parallel return: each row goes to its source rank's buffer
-          // (peer memory over NVLink) as f16.  A thread holds one row, so the
-          // warp's 32 rows are staged per 64-column chunk in shared memory and
-          // stored row by row, 8 lanes per row: every store is a whole
-          // 128-byte line.
+        {
           uint32_t* stg = reinterpret_cast<uint32_t*>(sm + RG::BYTES) + q * (32 * 33);
           unsigned long long dst = 0;
           if (valid) {
@@ -728,19 +730,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
             }
             __syncwarp();
           }
-        } else {
-#pragma unroll 1
-        for (int c = 0; c < kPN; c += 32) {
-          uint32_t v[32];
-          tmem_ld32(ta + c, v);
-          if (valid) {
-            float4* dst = reinterpret_cast<float4*>(p.y + (size_t)row * p.d + n0 + c);
-#pragma unroll
-            for (int i = 0; i < 8; i++)
-              dst[i] = make_float4(__uint_as_float(v[4 * i]) * w, __uint_as_float(v[4 * i + 1]) * w,
-                                   __uint_as_float(v[4 * i + 2]) * w, __uint_as_float(v[4 * i + 3]) * w);
-          }
-        }
         }
       }
       }  // sub-tiles
@@ -749,7 +738,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
       if (lane == 0) mbar_arrive(&tempty[b]);
     }
   }
-  if (MODE == P_DOWN && p.ysrc) __threadfence_system();  // peer rows written before the kernel ends
+  if (MODE == P_DOWN && p.remote) __threadfence_system();  // peer rows written before the kernel ends
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, 512);
@@ -916,9 +905,10 @@ __global__ void prefill_scan(const int* counts, int ne, int* cursor, PTile* tile
   }
 }
 
-// ---- place: a row per (token, slot), the token's xa row copied there ------
+// ---- place: a row per (token, slot), the token's xa row copied there; the
+// row's return slot is the pair itself (rank 0) ---------------------------
 __global__ void prefill_place(const int32_t* ids, const float* wts, const __half* xa, int T, int k, int Kx,
-                              int* cursor, int* rowpos, float* wrow, __half* xg) {
+                              int* cursor, int* ysrc, float* wrow, __half* xg) {
   const int pair = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (pair >= T * k) return;
   int pos = -1;
@@ -927,8 +917,8 @@ __global__ void prefill_place(const int32_t* ids, const float* wts, const __half
     if (e >= 0) {
       pos = atomicAdd(&cursor[e], 1);
       wrow[pos] = wts[pair];
+      ysrc[pos] = pair;
     }
-    rowpos[pair] = pos;
   }
   pos = __shfl_sync(0xffffffffu, pos, 0);
   if (pos < 0) return;
@@ -937,39 +927,50 @@ __global__ void prefill_place(const int32_t* ids, const float* wts, const __half
   for (int i = lane; i < Kx / 8; i += 32) dst[i] = s[i];
 }
 
-// ---- combine: x[t] += sum over rank of y(t, slot) (gguf_run.c:209, 213) ----
-// four columns per thread; the slots' rows are loaded together, then summed
-// in rank order
-__global__ void prefill_combine(const int* rowpos, const float* y, float* x, int T, int k, int d) {
+// ---- combine: x[t] += sum in slot order of the f16 rows yret[t * k + i]
+// (gguf_run.c:209, 213: moe_acc summed over the selected experts in order,
+// then added to x), in fp32; eight columns per thread, the slots' loads
+// issued together.  A slot whose id is -1 has no row.
+__global__ void prefill_combine(const int32_t* ids, const __half* yret, float* x, int T, int k, int d) {
   const int t = blockIdx.x;
   if (t >= T) return;
-  int rp[kPTopK];
+  bool on[kPTopK];
 #pragma unroll
-  for (int i = 0; i < kPTopK; i++) rp[i] = i < k ? rowpos[(size_t)t * k + i] : -1;
-  const int d4 = d / 4;
-  const float4* y4 = reinterpret_cast<const float4*>(y);
-  float4* x4 = reinterpret_cast<float4*>(x) + (size_t)t * d4;
-  for (int c = threadIdx.x; c < d4; c += blockDim.x) {
-    float4 v[kPTopK];
-#pragma unroll
-    for (int i = 0; i < kPTopK; i++)
-      if (rp[i] >= 0) v[i] = __ldcs(y4 + (size_t)rp[i] * d4 + c);
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int i = 0; i < kPTopK; i++) on[i] = i < k && ids[(size_t)t * k + i] >= 0;
+  const int d8 = d / 8;
+  const uint4* y8 = reinterpret_cast<const uint4*>(yret) + (size_t)t * k * d8;
+  float4* x4 = reinterpret_cast<float4*>(x) + (size_t)t * (d / 4);
+  for (int c = threadIdx.x; c < d8; c += blockDim.x) {
+    uint4 v[kPTopK];
 #pragma unroll
     for (int i = 0; i < kPTopK; i++)
-      if (rp[i] >= 0) {
-        acc.x = __fadd_rn(acc.x, v[i].x);
-        acc.y = __fadd_rn(acc.y, v[i].y);
-        acc.z = __fadd_rn(acc.z, v[i].z);
-        acc.w = __fadd_rn(acc.w, v[i].w);
+      if (on[i]) v[i] = __ldcs(y8 + (size_t)i * d8 + c);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < kPTopK; i++)
+      if (on[i]) {
+        const uint32_t w4[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+        for (int h = 0; h < 4; h++) {
+          const float2 f = __half22float2(u2h(w4[h]));
+          acc[2 * h] = __fadd_rn(acc[2 * h], f.x);
+          acc[2 * h + 1] = __fadd_rn(acc[2 * h + 1], f.y);
+        }
       }
-    float4 xv = x4[c];
-    xv.x = __fadd_rn(xv.x, acc.x);
-    xv.y = __fadd_rn(xv.y, acc.y);
-    xv.z = __fadd_rn(xv.z, acc.z);
-    xv.w = __fadd_rn(xv.w, acc.w);
-    x4[c] = xv;
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      float4 xv = x4[2 * c + h];
+      xv.x = __fadd_rn(xv.x, acc[4 * h]);
+      xv.y = __fadd_rn(xv.y, acc[4 * h + 1]);
+      xv.z = __fadd_rn(xv.z, acc[4 * h + 2]);
+      xv.w = __fadd_rn(xv.w, acc[4 * h + 3]);
+      x4[2 * c + h] = xv;
+    }
   }
+}
+
+void prefill_combine_launch(const int32_t* ids, const __half* yret, float* x, int T, int k, int d, cudaStream_t st) {
+  if (T > 0) prefill_combine<<<T, 256, 0, st>>>(ids, yret, x, T, k, d);
 }
 
 // ---------------------------------------------------------------------------
@@ -1014,7 +1015,7 @@ int prefill_supported(int d, int fe, int ne, int k, uint32_t rt, uint32_t gt, ui
 
 void prefill_scratch_free(PrefillScratch* s) {
   for (void* p : {(void*)s->xa, (void*)s->ids, (void*)s->wts, (void*)s->counts, (void*)s->cursor, (void*)s->tiles,
-                  (void*)s->n_mtiles, (void*)s->rowpos, (void*)s->wrow, (void*)s->xg, (void*)s->hg, (void*)s->y,
+                  (void*)s->n_mtiles, (void*)s->ysrc, (void*)s->wrow, (void*)s->xg, (void*)s->hg, (void*)s->yret,
                   (void*)s->r2, (void*)s->minmat, (void*)s->gu_pack, (void*)s->dn_pack})
     if (p) cudaFree(p);
   *s = PrefillScratch();
@@ -1066,7 +1067,6 @@ static PrefillParams base_params(const PrefillLayer& L, PrefillScratch* S, int T
   p.tiles = S->tiles;
   p.hg = (__half*)S->hg;
   p.wrow = S->wrow;
-  p.y = S->y;
   p.err = d_err;
   return p;
 }
@@ -1121,7 +1121,7 @@ int prefill_route(const PrefillLayer& L, PrefillScratch* S, const void* hb, int 
 
 size_t prefill_row_capacity(size_t pairs, int ne) { return ((pairs + (size_t)ne * (kPM - 1)) + kPM - 1) / kPM * kPM; }
 
-int prefill_grow_rows(const PrefillLayer& L, PrefillScratch* S, size_t rows, bool need_y) {
+int prefill_grow_rows(const PrefillLayer& L, PrefillScratch* S, size_t rows) {
   const int Kx = prefill_kx(L.d);
   rows = std::max<size_t>(rows, kPM);
   const size_t max_mtiles = rows / kPM + 1;
@@ -1130,8 +1130,7 @@ int prefill_grow_rows(const PrefillLayer& L, PrefillScratch* S, size_t rows, boo
       (rc = grow((void**)&S->n_mtiles, &S->c_n_mtiles, 16)) ||
       (rc = grow((void**)&S->tiles, &S->c_tiles, max_mtiles * sizeof(PTile))) ||
       (rc = grow((void**)&S->wrow, &S->c_wrow, rows * 4)) || (rc = grow((void**)&S->xg, &S->c_xg, rows * Kx * 2)) ||
-      (rc = grow((void**)&S->hg, &S->c_hg, rows * L.fe * 2)) ||
-      (need_y && (rc = grow((void**)&S->y, &S->c_y, rows * L.d * 4))))
+      (rc = grow((void**)&S->hg, &S->c_hg, rows * L.fe * 2)))
     return rc;
   return VIREO_OK;
 }
@@ -1163,6 +1162,7 @@ int prefill_experts(const PrefillLayer& L, PrefillScratch* S, size_t rows, int* 
   p.pack = S->dn_pack;
   p.ysrc = ysrc;
   for (int i = 0; i < npeers; i++) p.ypeer[i] = ypeer[i];
+  p.remote = npeers > 1;
   prefill_gemm<P_DOWN><<<num_sms, kPThreads, psmem<P_DOWN>(), st>>>(mA_d, mA_d, p);
   return cuda_status(cudaGetLastError());
 }
@@ -1173,12 +1173,16 @@ int prefill_run(const PrefillLayer& L, PrefillScratch* S, const void* hb, float*
   const size_t pairs = (size_t)T * k, rows = prefill_row_capacity(pairs, ne);
   int rc;
   if ((rc = prefill_route(L, S, hb, T, bias, d_err, num_sms, st))) return rc;
-  if ((rc = grow((void**)&S->rowpos, &S->c_rowpos, pairs * 4)) || (rc = prefill_grow_rows(L, S, rows, true))) return rc;
+  if (pairs >= (1u << 24)) return VIREO_ERR_ARG;  // a return slot is 24 bits
+  if ((rc = grow((void**)&S->ysrc, &S->c_ysrc, rows * 4)) || (rc = grow((void**)&S->yret, &S->c_yret, pairs * d * 2)) ||
+      (rc = prefill_grow_rows(L, S, rows)))
+    return rc;
   prefill_scan_launch(S->counts, ne, S, st);
   prefill_place<<<(unsigned)((pairs + 7) / 8), 256, 0, st>>>(S->ids, S->wts, (const __half*)S->xa, T, k, Kx,
-                                                              S->cursor, S->rowpos, S->wrow, (__half*)S->xg);
-  if ((rc = prefill_experts(L, S, rows, d_err, num_sms, st, nullptr, nullptr, 0))) return rc;
-  prefill_combine<<<T, 256, 0, st>>>(S->rowpos, S->y, x, T, k, d);
+                                                              S->cursor, S->ysrc, S->wrow, (__half*)S->xg);
+  __half* const self[1] = {S->yret};
+  if ((rc = prefill_experts(L, S, rows, d_err, num_sms, st, S->ysrc, self, 1))) return rc;
+  prefill_combine_launch(S->ids, S->yret, x, T, k, d, st);
   if (ids_out && cudaMemcpyAsync(ids_out, S->ids, pairs * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
     return cuda_status(cudaGetLastError());
   if (wts_out && cudaMemcpyAsync(wts_out, S->wts, pairs * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)

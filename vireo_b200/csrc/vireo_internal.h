@@ -58,18 +58,18 @@ struct PrefillScratch {
   int* cursor = nullptr;
   struct PTile* tiles = nullptr;
   int* n_mtiles = nullptr;
-  int* rowpos = nullptr;
+  int* ysrc = nullptr;     // [rows]: token slot (t * k + i) of each placed row
   float* wrow = nullptr;
   __half* xg = nullptr;
   __half* hg = nullptr;
-  float* y = nullptr;
+  __half* yret = nullptr;  // [T * k][d]: each token slot's weighted expert output, f16
   __half* r2 = nullptr;
   __half* minmat = nullptr;  // Q4_K min block of every gate/up row (depends on the expert pointers)
   uint8_t* gu_pack = nullptr;  // repacked gate/up and down weight chunks (likewise)
   uint8_t* dn_pack = nullptr;
   bool minmat_ok = false;
-  size_t c_xa = 0, c_ids = 0, c_wts = 0, c_counts = 0, c_cursor = 0, c_tiles = 0, c_n_mtiles = 0, c_rowpos = 0,
-         c_wrow = 0, c_xg = 0, c_hg = 0, c_y = 0, c_r2 = 0, c_minmat = 0, c_gu_pack = 0, c_dn_pack = 0;
+  size_t c_xa = 0, c_ids = 0, c_wts = 0, c_counts = 0, c_cursor = 0, c_tiles = 0, c_n_mtiles = 0, c_ysrc = 0,
+         c_wrow = 0, c_xg = 0, c_hg = 0, c_yret = 0, c_r2 = 0, c_minmat = 0, c_gu_pack = 0, c_dn_pack = 0;
 };
 int prefill_supported(int d, int fe, int ne, int k, uint32_t rt, uint32_t gt, uint32_t ut, uint32_t dt);
 int prefill_run(const PrefillLayer& L, PrefillScratch* S, const void* hb_bf16, float* x, int T, const float* bias,
@@ -81,13 +81,15 @@ int prefill_prepare(const PrefillLayer& L, PrefillScratch* S, cudaStream_t st);
 int prefill_route(const PrefillLayer& L, PrefillScratch* S, const void* hb, int T, const float* bias, int* d_err,
                   int num_sms, cudaStream_t st);
 size_t prefill_row_capacity(size_t pairs, int ne);
-int prefill_grow_rows(const PrefillLayer& L, PrefillScratch* S, size_t rows, bool need_y);
+int prefill_grow_rows(const PrefillLayer& L, PrefillScratch* S, size_t rows);
 void prefill_scan_launch(const int* counts, int ne, PrefillScratch* S, cudaStream_t st);
-// ysrc / ypeer: the expert-parallel return (row r's output, as f16, to rank
-// ysrc[r] >> 24's ypeer buffer, row ysrc[r] & 0xFFFFFF); null = fp32 outputs
-// into S->y
+// ysrc / ypeer: where row r's output goes, as f16: rank ysrc[r] >> 24's
+// ypeer buffer, row ysrc[r] & 0xFFFFFF (a single-GPU call passes its own
+// map and S->yret as the only peer; npeers > 1 means peer memory)
 int prefill_experts(const PrefillLayer& L, PrefillScratch* S, size_t rows, int* d_err, int num_sms, cudaStream_t st,
                     const int* ysrc, __half* const* ypeer, int npeers);
+// x[t] += sum in slot order of yret[t * k + i] (slots whose id is -1 skipped)
+void prefill_combine_launch(const int32_t* ids, const __half* yret, float* x, int T, int k, int d, cudaStream_t st);
 int prefill_tile_rows();  // rows per activation tile (row ranges per expert are padded to it)
 
 // generic kernels (any supported type/shape), generic_kernels.cu
