@@ -295,7 +295,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
     mbar_init(&drain, 1);
     mbar_fence_init();
     abort_s = 0;
-    n_items_s = MODE == P_ROUTER ? (p.T + kPM - 1) / kPM : (*p.n_mtiles) * p.n_ntiles;
+    // router: n_ntiles CTAs per row tile, each selecting for its share of the rows
+    n_items_s = MODE == P_ROUTER ? (p.T + kPM - 1) / kPM * p.n_ntiles : (*p.n_mtiles) * p.n_ntiles;
   }
   if (warp == 0) tmem_alloc(&tbase, 512);
   tc_fence_before();
@@ -439,8 +440,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
       const int st = threadIdx.x - 32 * kDqWarp0, grp = st >> 3, j = st & 7;
       const int ne = p.ne, k = p.k;
       int it = 0;
+      const int rpp = kPM / p.n_ntiles;  // rows per part (a multiple of 4)
       for (int item = blockIdx.x; item < n_items; item += gridDim.x, it++) {
-        const PTile t = tile_of(item);
+        const PTile t = tile_of(item / p.n_ntiles);
+        const int rb = (item % p.n_ntiles) * rpp, nsel = min(t.nrows, rb + rpp) - rb;
         if (warp >= kEpiWarp0) {
           const int q = warp & 3, b = it & 1;
           int w_ok = 0;
@@ -449,18 +452,20 @@ __global__ void __launch_bounds__(kPThreads, 1)
             w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
           }
           if (w_ok) {
-            tc_fence_after();
-            const int rt = 32 * q + lane;
-            const uint32_t ta = tmem + (uint32_t)(b * kPN) + ((uint32_t)(32 * q) << 16);
-            for (int c = 0; c < 128; c += 32) {
-              uint32_t vh[32], vl[32];
-              tmem_ld32(ta + c, vh);
-              tmem_ld32(ta + 128 + c, vl);
+            if (32 * q < rb + rpp && 32 * q + 32 > rb) {  // this warp's 32 rows meet the part's
+              tc_fence_after();
+              const int rt = 32 * q + lane;
+              const uint32_t ta = tmem + (uint32_t)(b * kPN) + ((uint32_t)(32 * q) << 16);
+              for (int c = 0; c < 128; c += 32) {
+                uint32_t vh[32], vl[32];
+                tmem_ld32(ta + c, vh);
+                tmem_ld32(ta + 128 + c, vl);
 #pragma unroll
-              for (int jj = 0; jj < 32; jj++) {
-                const int e = c + jj;
-                lgs[rt * 129 + e] = e < ne ? __uint_as_float(vh[jj]) + __uint_as_float(vl[jj]) + (p.bias ? p.bias[e] : 0.f)
-                                           : -INFINITY;
+                for (int jj = 0; jj < 32; jj++) {
+                  const int e = c + jj;
+                  lgs[rt * 129 + e] = e < ne ? __uint_as_float(vh[jj]) + __uint_as_float(vl[jj]) + (p.bias ? p.bias[e] : 0.f)
+                                             : -INFINITY;
+                }
               }
             }
             tc_fence_before();
@@ -474,7 +479,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
           // iterations (the shuffles name the whole warp); lanes past the
           // tile's last row compute on rows the logit buffer holds and write
           // nothing
-          for (int r = grp; (r & ~3) < t.nrows; r += kGroups) {
+          for (int rr = grp; (rr & ~3) < nsel; rr += kGroups) {
+            const int r = rb + rr;
             const float* L = lgs + r * 129 + 16 * j;
             float ex[16];
             float mx = -INFINITY;
@@ -553,7 +559,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 ti[kPTopK - 1] = -1;
               }
             }
-            if (j == 0 && r < t.nrows) {
+            if (j == 0 && rr < nsel) {
               float ws = 0.f;
 #pragma unroll
               for (int u = 0; u < kPTopK; u++)
@@ -1114,8 +1120,10 @@ int prefill_route(const PrefillLayer& L, PrefillScratch* S, const void* hb, int 
   if (cudaMemsetAsync(S->counts, 0, 256 * 4, st) != cudaSuccess) return cuda_status(cudaGetLastError());
   prefill_prep<<<T, 256, 0, st>>>((const __nv_bfloat16*)hb, (__half*)S->xa, T, d, Kx);
   p.nk = d / kPK;
-  p.n_ntiles = 1;
-  prefill_gemm<P_ROUTER><<<std::min(num_sms, (T + kPM - 1) / kPM), kPThreads, psmem<P_ROUTER>(), st>>>(mA_r, mB_r, p);
+  // idle SMs repeat a row tile's GEMM so that its top-k is split 2 or 4 ways
+  const int tiles = (T + kPM - 1) / kPM;
+  p.n_ntiles = tiles * 4 <= num_sms ? 4 : tiles * 2 <= num_sms ? 2 : 1;
+  prefill_gemm<P_ROUTER><<<std::min(num_sms, tiles * p.n_ntiles), kPThreads, psmem<P_ROUTER>(), st>>>(mA_r, mB_r, p);
   return cuda_status(cudaGetLastError());
 }
 
