@@ -913,8 +913,8 @@ __global__ void prefill_scan(const int* counts, int ne, int* cursor, PTile* tile
 
 // ---- place: a row per (token, slot), the token's xa row copied there; the
 // row's return slot is the pair itself (rank 0) ---------------------------
-__global__ void prefill_place(const int32_t* ids, const float* wts, const __half* xa, int T, int k, int Kx,
-                              int* cursor, int* ysrc, float* wrow, __half* xg) {
+__global__ void prefill_place(const int32_t* ids, const float* wts, const __half* __restrict__ xa, int T, int k,
+                              int Kx, int* cursor, int* ysrc, float* wrow, __half* __restrict__ xg) {
   const int pair = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (pair >= T * k) return;
   int pos = -1;
@@ -930,7 +930,19 @@ __global__ void prefill_place(const int32_t* ids, const float* wts, const __half
   if (pos < 0) return;
   const uint4* s = reinterpret_cast<const uint4*>(xa + (size_t)(pair / k) * Kx);
   uint4* dst = reinterpret_cast<uint4*>(xg + (size_t)pos * Kx);
-  for (int i = lane; i < Kx / 8; i += 32) dst[i] = s[i];
+  // a lane's loads of a chunk are all issued before its stores (one chunk
+  // is a whole row up to d = 2240)
+  constexpr int kPlaceVec = 9;
+  const int n16 = Kx / 8;
+  for (int c0 = lane; c0 < n16; c0 += 32 * kPlaceVec) {
+    uint4 v[kPlaceVec];
+#pragma unroll
+    for (int j = 0; j < kPlaceVec; j++)
+      if (c0 + 32 * j < n16) v[j] = __ldg(s + c0 + 32 * j);
+#pragma unroll
+    for (int j = 0; j < kPlaceVec; j++)
+      if (c0 + 32 * j < n16) dst[c0 + 32 * j] = v[j];
+  }
 }
 
 // ---- combine: x[t] += sum in slot order of the f16 rows yret[t * k + i]
