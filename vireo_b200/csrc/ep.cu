@@ -17,12 +17,17 @@
 //             expert's row range on the owning rank (the ranges are laid out
 //             as prefill_scan lays them out); no host synchronisation anywhere
 //             in a call
-//   dispatch  one warp per (token, slot) pair writes the token's activation
-//             row, the gate weight and the pair's origin straight into the
-//             owning rank's GEMM operand (peer stores), then a barrier
-//   experts   the owner runs the tcgen05 gate/up and down GEMMs of prefill.cu
-//             over its rows; the down GEMM's epilogue stores each output row,
-//             rounded to f16, into the SOURCE rank's return buffer over
+//   dispatch  one warp per token writes each pair's gate weight and origin
+//             at its row on the owning rank, the token's activation row into
+//             its rows on this rank, and the row ONCE into the receive buffer
+//             of every other rank holding one of its experts (peer stores;
+//             a token with several experts on one peer crosses NVLink once),
+//             then a barrier
+//   experts   the owner copies each received row into its expert rows
+//             (prefill_expand), then runs the tcgen05 gate/up and down
+//             GEMMs of prefill.cu over its rows; the down GEMM's epilogue
+//             stores each output row, rounded to f16, into the SOURCE rank's
+//             return buffer over
 //             NVLink, tile by tile while the next tiles' MMAs run (one
 //             kernel: GEMM + return)
 //   combine   after a barrier, x[t] += sum over rank order of the returned
@@ -111,8 +116,11 @@ struct EpDispatch {
   __half* xg[kEpMaxWorld];
   float* wrow[kEpMaxWorld];
   int* ysrc[kEpMaxWorld];
-  const int* dst_off;  // [ne], device (ep_layout)
-  int rows_cap;        // rows of every rank's operand buffers
+  __half* xr[kEpMaxWorld];  // receive buffers: [world * max_tok][Kx], slot = source rank * max_tok + token
+  int* xsrc[kEpMaxWorld];   // [rows_cap]: a row's receive slot, or -1 when placed directly
+  const int* dst_off;       // [ne], device (ep_layout)
+  int rows_cap;             // rows of every rank's operand buffers
+  int max_tok;
 };
 
 // ---- kernels ------------------------------------------------------------------
@@ -222,24 +230,58 @@ __global__ void ep_signal(EpSig* mine, const __grid_constant__ EpPeers P, int ph
   __threadfence_system();
 }
 
-// one warp per (token, slot) pair: the token's activation row, the gate
-// weight and the pair's origin, stored into the owner's operand buffers
-__global__ void ep_dispatch(const __half* xa, const int32_t* ids, const float* wts, const int32_t* owner,
-                            const int* pos, int pairs, int k, int Kx, int rank, const __grid_constant__ EpDispatch D,
-                            int* err) {
-  const int p = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (p < pairs) {
-    const int e = ids[p];
-    const int q = e >= 0 ? owner[e] : 0, row = e >= 0 ? D.dst_off[e] + pos[p] : -1;
-    if (e >= 0 && row >= D.rows_cap) {
-      if (lane == 0) atomicCAS(err, 0, VIREO_ERR_ARG);  // inconsistent counts: never write past a buffer
-    } else if (e >= 0) {
-      const uint4* s4 = reinterpret_cast<const uint4*>(xa + (size_t)(p / k) * Kx);
-      uint4* d4 = reinterpret_cast<uint4*>(D.xg[q] + (size_t)row * Kx);
-      for (int i = lane; i < Kx / 8; i += 32) d4[i] = s4[i];
-      if (lane == 0) {
-        D.wrow[q][row] = wts[p];
-        D.ysrc[q][row] = (rank << 24) | p;
+// One warp per token.  Lane j < k takes slot j: the gate weight, the
+// return slot and the row's source (its receive slot, or -1) go to the
+// slot's row on its owner.  The token's activation row is read once and
+// stored into each of its rows held on this rank, and ONCE into the receive
+// buffer of every other rank that holds one of its experts (that owner
+// copies it into its rows: prefill_expand), so a token with several experts
+// on one peer crosses NVLink once.
+__global__ void ep_dispatch(const __half* __restrict__ xa, const int32_t* ids, const float* wts,
+                            const int32_t* owner, const int* pos, int n_tok, int k, int Kx, int rank,
+                            const __grid_constant__ EpDispatch D, int* err) {
+  const int t = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (t < n_tok) {
+    const int p = t * k + lane;
+    int q = -1, row = -1;
+    if (lane < k) {
+      const int e = ids[p];
+      if (e >= 0) {
+        q = owner[e];
+        row = D.dst_off[e] + pos[p];
+        if (row >= D.rows_cap) {  // inconsistent counts: never write past a buffer
+          atomicCAS(err, 0, VIREO_ERR_ARG);
+          q = row = -1;
+        } else {
+          D.wrow[q][row] = wts[p];
+          D.ysrc[q][row] = (rank << 24) | p;
+          D.xsrc[q][row] = q == rank ? -1 : rank * D.max_tok + t;
+        }
+      }
+    }
+    const unsigned remote = __reduce_or_sync(0xffffffffu, q >= 0 && q != rank ? 1u << q : 0u);
+    const unsigned local = __ballot_sync(0xffffffffu, q == rank);
+    const uint4* s4 = reinterpret_cast<const uint4*>(xa + (size_t)t * Kx);
+    const int n16 = Kx / 8;
+    constexpr int kVec = 9;
+    for (int c0 = lane; c0 < n16; c0 += 32 * kVec) {
+      uint4 v[kVec];
+#pragma unroll
+      for (int j = 0; j < kVec; j++)
+        if (c0 + 32 * j < n16) v[j] = __ldg(s4 + c0 + 32 * j);
+      for (unsigned m = local; m; m &= m - 1) {
+        const int r2 = __shfl_sync(0xffffffffu, row, __ffs(m) - 1);
+        uint4* d4 = reinterpret_cast<uint4*>(D.xg[rank] + (size_t)r2 * Kx);
+#pragma unroll
+        for (int j = 0; j < kVec; j++)
+          if (c0 + 32 * j < n16) d4[c0 + 32 * j] = v[j];
+      }
+      for (unsigned m = remote; m; m &= m - 1) {
+        const int q2 = __ffs(m) - 1;
+        uint4* d4 = reinterpret_cast<uint4*>(D.xr[q2] + ((size_t)rank * D.max_tok + t) * Kx);
+#pragma unroll
+        for (int j = 0; j < kVec; j++)
+          if (c0 + 32 * j < n16) d4[c0 + 32 * j] = v[j];
       }
     }
   }
@@ -271,11 +313,15 @@ struct gguf_moe_ep {
   float* wrow = nullptr;    // [rows_cap]
   int* ysrc = nullptr;      // [rows_cap]
   __half* yret = nullptr;   // [max_tok * k][d] f16 returned rows
+  __half* xr = nullptr;     // [world * max_tok][Kx] rows received from the sources
+  int* xsrc = nullptr;      // [rows_cap] receive slot of each row (-1: placed by its source)
   // every rank's buffers as mapped here (own entry = the local pointer)
   __half* p_xg[kEpMaxWorld] = {};
   float* p_wrow[kEpMaxWorld] = {};
   int* p_ysrc[kEpMaxWorld] = {};
   __half* p_yret[kEpMaxWorld] = {};
+  __half* p_xr[kEpMaxWorld] = {};
+  int* p_xsrc[kEpMaxWorld] = {};
   EpSig* sig = nullptr;                 // this rank's signal buffer (peers write it)
   EpSig* p_sig[kEpMaxWorld] = {};
   unsigned int call = 0;                // calls made so far (the same on every rank)
@@ -434,6 +480,8 @@ int gguf_moe_ep_create(const gguf_moe_desc* desc, const int32_t* owner, int rank
       (st = cuda_status(cudaMalloc(&ep->wrow, ep->rows_cap * 4))) ||
       (st = cuda_status(cudaMalloc(&ep->ysrc, ep->rows_cap * 4))) ||
       (st = cuda_status(cudaMalloc(&ep->yret, pairs_cap * d * 2))) ||
+      (st = cuda_status(cudaMalloc(&ep->xr, (size_t)world * max_tokens * Kx * 2))) ||
+      (st = cuda_status(cudaMalloc(&ep->xsrc, ep->rows_cap * 4))) ||
       (st = cuda_status(cudaMalloc(&ep->sig, sizeof(EpSig)))) ||
       (st = cuda_status(cudaMemset(ep->sig, 0, sizeof(EpSig)))) ||
       (st = cuda_status(cudaMemset(ep->d_bar, 0, 16))) ||
@@ -449,18 +497,18 @@ int gguf_moe_ep_create(const gguf_moe_desc* desc, const int32_t* owner, int rank
     gguf_moe_ep_destroy(ep);
     return VIREO_ERR_CUDA;
   }
-  // exchange the IPC handles of the four exported buffers, with max_tokens:
+  // exchange the IPC handles of the exported buffers, with max_tokens:
   // every rank must size its buffers alike (a peer writes up to its own
   // max_tokens * n_used rows into them)
   struct {
-    cudaIpcMemHandle_t h[5];
+    cudaIpcMemHandle_t h[7];
     int64_t max_tok, pad;
   } mine;
   static_assert(sizeof(mine) % 16 == 0, "exchange record");
   mine.max_tok = max_tokens;
   mine.pad = 0;
-  void* bufs[5] = {ep->xg, ep->wrow, ep->ysrc, ep->yret, ep->sig};
-  for (int i = 0; i < 5; i++)
+  void* bufs[7] = {ep->xg, ep->wrow, ep->ysrc, ep->yret, ep->sig, ep->xr, ep->xsrc};
+  for (int i = 0; i < 7; i++)
     if ((st = cuda_status(cudaIpcGetMemHandle(&mine.h[i], bufs[i])))) {
       gguf_moe_ep_destroy(ep);
       return st;
@@ -487,16 +535,20 @@ int gguf_moe_ep_create(const gguf_moe_desc* desc, const int32_t* owner, int rank
       ep->p_ysrc[q] = ep->ysrc;
       ep->p_yret[q] = ep->yret;
       ep->p_sig[q] = ep->sig;
+      ep->p_xr[q] = ep->xr;
+      ep->p_xsrc[q] = ep->xsrc;
       continue;
     }
-    void* ptr[5] = {};
-    for (int i = 0; i < 5 && !st; i++)
+    void* ptr[7] = {};
+    for (int i = 0; i < 7 && !st; i++)
       st = cuda_status(cudaIpcOpenMemHandle(&ptr[i], all[q].h[i], cudaIpcMemLazyEnablePeerAccess));
     ep->p_xg[q] = (__half*)ptr[0];
     ep->p_wrow[q] = (float*)ptr[1];
     ep->p_ysrc[q] = (int*)ptr[2];
     ep->p_yret[q] = (__half*)ptr[3];
     ep->p_sig[q] = (EpSig*)ptr[4];
+    ep->p_xr[q] = (__half*)ptr[5];
+    ep->p_xsrc[q] = (int*)ptr[6];
     ep->mapped[q] = true;
   }
   if (st) {
@@ -552,9 +604,12 @@ int gguf_moe_prefill_ep(gguf_moe_ep* ep, const void* hb_bf16, float* x, int n_to
     Dp.xg[q] = ep->p_xg[q];
     Dp.wrow[q] = ep->p_wrow[q];
     Dp.ysrc[q] = ep->p_ysrc[q];
+    Dp.xr[q] = ep->p_xr[q];
+    Dp.xsrc[q] = ep->p_xsrc[q];
   }
   Dp.dst_off = ep->d_dstoff;
   Dp.rows_cap = (int)ep->rows_cap;
+  Dp.max_tok = ep->max_tok;
   // the GEMMs of this rank run on the exported operand buffers, sized for the
   // most rows any call can bring (no host read of the counts)
   S->xg = ep->xg;
@@ -563,13 +618,16 @@ int gguf_moe_prefill_ep(gguf_moe_ep* ep, const void* hb_bf16, float* x, int n_to
   S->c_wrow = ep->rows_cap * 4;
   const size_t rows = ep->rows_cap;
   if ((rc = prefill_grow_rows(L, S, rows))) return rc;
-  // dispatch straight into the owners' operands, then every rank's rows are in place
-  if (pairs)
-    ep_dispatch<<<(unsigned)((pairs + 7) / 8), 256, 0, s>>>(S->xa, S->ids, S->wts, ep->d_owner, ep->d_pos,
-                                                             (int)pairs, k, Kx, r, Dp, v.err);
+  // dispatch into the owners' operands (a token's row once per other owner),
+  // then every rank's rows and receive buffer are in place
+  if (n_tok)
+    ep_dispatch<<<(unsigned)((n_tok + 7) / 8), 256, 0, s>>>(S->xa, S->ids, S->wts, ep->d_owner, ep->d_pos, n_tok,
+                                                             k, Kx, r, Dp, v.err);
   ep_signal<<<1, 32, 0, s>>>(ep->sig, P, kSigDispatched, call, G, r, v.err);
-  // the experts held here; the down GEMM returns each row to its source rank
+  // the experts held here (rows received once per token copied into each of
+  // its rows); the down GEMM returns each row to its source rank
   prefill_scan_launch(ep->d_totals, ne, S, s);
+  if (G > 1) prefill_expand_launch(S, rows, ep->xsrc, ep->xr, Kx, G * ep->max_tok, s);
   if ((rc = prefill_experts(L, S, rows, v.err, v.num_sms, s, ep->ysrc, ep->p_yret, G))) return rc;
   ep_signal<<<1, 32, 0, s>>>(ep->sig, P, kSigReturned, call, G, r, v.err);
   prefill_combine_launch(S->ids, ep->yret, x, n_tok, k, d, s);
@@ -599,7 +657,7 @@ void gguf_moe_ep_destroy(gguf_moe_ep* ep) {
   for (int q = 0; q < kEpMaxWorld; q++)
     if (ep->mapped[q])
       for (void* p : {(void*)ep->p_xg[q], (void*)ep->p_wrow[q], (void*)ep->p_ysrc[q], (void*)ep->p_yret[q],
-                      (void*)ep->p_sig[q]})
+                      (void*)ep->p_sig[q], (void*)ep->p_xr[q], (void*)ep->p_xsrc[q]})
         if (p) cudaIpcCloseMemHandle(p);
   if (ep->comm) {
     // the peers unmap this rank's buffers before any of them is freed: one
@@ -622,7 +680,7 @@ void gguf_moe_ep_destroy(gguf_moe_ep* ep) {
   }
   for (void* p : {(void*)ep->d_owner, (void*)ep->d_own, (void*)ep->d_cnt, (void*)ep->d_cntall, (void*)ep->d_totals, (void*)ep->d_dstoff,
                   (void*)ep->d_pos, (void*)ep->d_bar, (void*)ep->xg, (void*)ep->wrow, (void*)ep->ysrc,
-                  (void*)ep->yret, (void*)ep->sig})
+                  (void*)ep->yret, (void*)ep->sig, (void*)ep->xr, (void*)ep->xsrc})
     if (p) cudaFree(p);
   delete ep;
 }

@@ -945,6 +945,39 @@ __global__ void prefill_place(const int32_t* ids, const float* wts, const __half
   }
 }
 
+// ---- expand (expert-parallel owner): a token's row crosses NVLink once per
+// owner, into the receive buffer; each of the owner's rows whose source slot
+// xsrc[row] is set copies it from there (rows placed directly hold -1).  One
+// block per M tile, a warp per row.
+__global__ void prefill_expand(const PTile* tiles, const int* n_mtiles, const int* xsrc, const __half* __restrict__ xr,
+                               __half* __restrict__ xg, int Kx, int n_slots) {
+  if ((int)blockIdx.x >= *n_mtiles) return;
+  const PTile t = tiles[blockIdx.x];
+  const int lane = threadIdx.x & 31, n16 = Kx / 8;
+  constexpr int kVec = 9;
+  for (int i = threadIdx.x >> 5; i < t.nrows; i += blockDim.x / 32) {
+    const int row = t.row0 + i, src = xsrc[row];
+    if (src < 0 || src >= n_slots) continue;
+    const uint4* s4 = reinterpret_cast<const uint4*>(xr + (size_t)src * Kx);
+    uint4* d4 = reinterpret_cast<uint4*>(xg + (size_t)row * Kx);
+    for (int c0 = lane; c0 < n16; c0 += 32 * kVec) {
+      uint4 v[kVec];
+#pragma unroll
+      for (int j = 0; j < kVec; j++)
+        if (c0 + 32 * j < n16) v[j] = __ldcs(s4 + c0 + 32 * j);
+#pragma unroll
+      for (int j = 0; j < kVec; j++)
+        if (c0 + 32 * j < n16) d4[c0 + 32 * j] = v[j];
+    }
+  }
+}
+
+void prefill_expand_launch(const PrefillScratch* S, size_t rows, const int* xsrc, const __half* xr, int Kx,
+                           int n_slots, cudaStream_t st) {
+  rows = std::max<size_t>(rows, kPM);
+  prefill_expand<<<(unsigned)(rows / kPM + 1), 256, 0, st>>>(S->tiles, S->n_mtiles, xsrc, xr, S->xg, Kx, n_slots);
+}
+
 // ---- combine: x[t] += sum in slot order of the f16 rows yret[t * k + i]
 // (gguf_run.c:209, 213: moe_acc summed over the selected experts in order,
 // then added to x), in fp32; eight columns per thread, the slots' loads

@@ -88,6 +88,10 @@ void prefill_scan_launch(const int* counts, int ne, PrefillScratch* S, cudaStrea
 // map and S->yret as the only peer; npeers > 1 means peer memory)
 int prefill_experts(const PrefillLayer& L, PrefillScratch* S, size_t rows, int* d_err, int num_sms, cudaStream_t st,
                     const int* ysrc, __half* const* ypeer, int npeers);
+// expert-parallel owner: row r of S->xg (over the M tiles prefill_scan laid
+// out for `rows` rows) <- xr row xsrc[r] where xsrc[r] is in [0, n_slots)
+void prefill_expand_launch(const PrefillScratch* S, size_t rows, const int* xsrc, const __half* xr, int Kx,
+                           int n_slots, cudaStream_t st);
 // x[t] += sum in slot order of yret[t * k + i] (slots whose id is -1 skipped)
 void prefill_combine_launch(const int32_t* ids, const __half* yret, float* x, int T, int k, int d, cudaStream_t st);
 int prefill_tile_rows();  // rows per activation tile (row ranges per expert are padded to it)
