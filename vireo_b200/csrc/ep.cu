@@ -75,6 +75,7 @@ namespace vireo {
 constexpr int kEpMaxWorld = 8;    // one node
 constexpr int kEpMaxExperts = 128;
 constexpr double kEpWaitSeconds = 60.0;
+constexpr int kEpSplit = 4;  // warps sharing one token's row in the dispatch
 
 // ---- NCCL entry points, resolved once ---------------------------------------
 struct NcclApi {
@@ -230,9 +231,10 @@ __global__ void ep_signal(EpSig* mine, const __grid_constant__ EpPeers P, int ph
   __threadfence_system();
 }
 
-// One warp per token.  Lane j < k takes slot j: the gate weight, the
-// return slot and the row's source (its receive slot, or -1) go to the
-// slot's row on its owner.  The token's activation row is read once and
+// kEpSplit warps per token, each copying one part of the row.  Lane j < k
+// of the first takes slot j: the gate weight, the return slot and the row's
+// source (its receive slot, or -1) go to the slot's row on its owner.  The
+// token's activation row is read once and
 // stored into each of its rows held on this rank, and ONCE into the receive
 // buffer of every other rank that holds one of its experts (that owner
 // copies it into its rows: prefill_expand), so a token with several experts
@@ -240,7 +242,8 @@ __global__ void ep_signal(EpSig* mine, const __grid_constant__ EpPeers P, int ph
 __global__ void ep_dispatch(const __half* __restrict__ xa, const int32_t* ids, const float* wts,
                             const int32_t* owner, const int* pos, int n_tok, int k, int Kx, int rank,
                             const __grid_constant__ EpDispatch D, int* err) {
-  const int t = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int w = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int t = w / kEpSplit, part = w % kEpSplit;
   if (t < n_tok) {
     const int p = t * k + lane;
     int q = -1, row = -1;
@@ -250,9 +253,9 @@ __global__ void ep_dispatch(const __half* __restrict__ xa, const int32_t* ids, c
         q = owner[e];
         row = D.dst_off[e] + pos[p];
         if (row >= D.rows_cap) {  // inconsistent counts: never write past a buffer
-          atomicCAS(err, 0, VIREO_ERR_ARG);
+          if (part == 0) atomicCAS(err, 0, VIREO_ERR_ARG);
           q = row = -1;
-        } else {
+        } else if (part == 0) {
           D.wrow[q][row] = wts[p];
           D.ysrc[q][row] = (rank << 24) | p;
           D.xsrc[q][row] = q == rank ? -1 : rank * D.max_tok + t;
@@ -262,9 +265,9 @@ __global__ void ep_dispatch(const __half* __restrict__ xa, const int32_t* ids, c
     const unsigned remote = __reduce_or_sync(0xffffffffu, q >= 0 && q != rank ? 1u << q : 0u);
     const unsigned local = __ballot_sync(0xffffffffu, q == rank);
     const uint4* s4 = reinterpret_cast<const uint4*>(xa + (size_t)t * Kx);
-    const int n16 = Kx / 8;
-    constexpr int kVec = 9;
-    for (int c0 = lane; c0 < n16; c0 += 32 * kVec) {
+    const int per = (Kx / 8 + kEpSplit - 1) / kEpSplit, c_beg = part * per, n16 = min(Kx / 8, c_beg + per);
+    constexpr int kVec = 3;
+    for (int c0 = c_beg + lane; c0 < n16; c0 += 32 * kVec) {
       uint4 v[kVec];
 #pragma unroll
       for (int j = 0; j < kVec; j++)
@@ -621,7 +624,7 @@ int gguf_moe_prefill_ep(gguf_moe_ep* ep, const void* hb_bf16, float* x, int n_to
   // dispatch into the owners' operands (a token's row once per other owner),
   // then every rank's rows and receive buffer are in place
   if (n_tok)
-    ep_dispatch<<<(unsigned)((n_tok + 7) / 8), 256, 0, s>>>(S->xa, S->ids, S->wts, ep->d_owner, ep->d_pos, n_tok,
+    ep_dispatch<<<(unsigned)(((size_t)n_tok * kEpSplit + 7) / 8), 256, 0, s>>>(S->xa, S->ids, S->wts, ep->d_owner, ep->d_pos, n_tok,
                                                              k, Kx, r, Dp, v.err);
   ep_signal<<<1, 32, 0, s>>>(ep->sig, P, kSigDispatched, call, G, r, v.err);
   // the experts held here (rows received once per token copied into each of

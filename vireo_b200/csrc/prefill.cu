@@ -947,15 +947,15 @@ __global__ void prefill_place(const int32_t* ids, const float* wts, const __half
 
 // ---- expand (expert-parallel owner): a token's row crosses NVLink once per
 // owner, into the receive buffer; each of the owner's rows whose source slot
-// xsrc[row] is set copies it from there (rows placed directly hold -1).  One
-// block per M tile, a warp per row.
+// xsrc[row] is set copies it from there (rows placed directly hold -1).
+// gridDim.y blocks per M tile, a warp per row.
 __global__ void prefill_expand(const PTile* tiles, const int* n_mtiles, const int* xsrc, const __half* __restrict__ xr,
                                __half* __restrict__ xg, int Kx, int n_slots) {
   if ((int)blockIdx.x >= *n_mtiles) return;
   const PTile t = tiles[blockIdx.x];
   const int lane = threadIdx.x & 31, n16 = Kx / 8;
   constexpr int kVec = 9;
-  for (int i = threadIdx.x >> 5; i < t.nrows; i += blockDim.x / 32) {
+  for (int i = (threadIdx.x >> 5) + blockIdx.y * (blockDim.x / 32); i < t.nrows; i += gridDim.y * (blockDim.x / 32)) {
     const int row = t.row0 + i, src = xsrc[row];
     if (src < 0 || src >= n_slots) continue;
     const uint4* s4 = reinterpret_cast<const uint4*>(xr + (size_t)src * Kx);
@@ -975,7 +975,7 @@ __global__ void prefill_expand(const PTile* tiles, const int* n_mtiles, const in
 void prefill_expand_launch(const PrefillScratch* S, size_t rows, const int* xsrc, const __half* xr, int Kx,
                            int n_slots, cudaStream_t st) {
   rows = std::max<size_t>(rows, kPM);
-  prefill_expand<<<(unsigned)(rows / kPM + 1), 256, 0, st>>>(S->tiles, S->n_mtiles, xsrc, xr, S->xg, Kx, n_slots);
+  prefill_expand<<<dim3((unsigned)(rows / kPM + 1), 8), 256, 0, st>>>(S->tiles, S->n_mtiles, xsrc, xr, S->xg, Kx, n_slots);
 }
 
 // ---- combine: x[t] += sum in slot order of the f16 rows yret[t * k + i]
