@@ -68,6 +68,7 @@
 #include "gguf_moe.h"
 #include "moe_view.h"
 #include "vireo_internal.h"
+#include "pdl_launch.cuh"
 #include "vireo_ptx.cuh"
 
 namespace vireo {
@@ -127,6 +128,7 @@ struct EpDispatch {
 // ---- kernels ------------------------------------------------------------------
 // per expert: the local pair count and each pair's index among them
 __global__ void ep_count(const int32_t* ids, int pairs, int* cnt, int* pos) {
+  pdl_wait();
   const int p = blockIdx.x * blockDim.x + threadIdx.x;
   if (p >= pairs) return;
   const int e = ids[p];
@@ -196,12 +198,14 @@ __device__ bool ep_wait_flag(const volatile unsigned int* f, unsigned int v, int
 // rank's signal buffer, the counts are made visible system-wide, thread 0
 // raises this rank's counts flag on every rank, threads q < G wait for rank
 // q's flag here, then the layout of ep_layout_body from the gathered counts.
-__global__ void ep_exchange(const int* cnt, EpSig* mine, const __grid_constant__ EpPeers P, unsigned int call,
+__global__ void ep_exchange(int* cnt, EpSig* mine, const __grid_constant__ EpPeers P, unsigned int call,
                             const int32_t* owner, int G, int ne, int rank, int tile, int* dst_off, int* totals,
                             int* err) {
+  pdl_wait();
   const int e = threadIdx.x;
   if (e < ne) {
     const int c = cnt[e];
+    cnt[e] = 0;  // zero for the next call's ep_count (the buffer starts zeroed)
     for (int q = 0; q < G; q++) P.sig[q]->cnt[rank][e] = c;
   }
   __threadfence_system();
@@ -222,6 +226,7 @@ __global__ void ep_exchange(const int* cnt, EpSig* mine, const __grid_constant__
 // flag of the phase on rank q and waits for rank q's flag here.
 __global__ void ep_signal(EpSig* mine, const __grid_constant__ EpPeers P, int phase, unsigned int call, int G,
                           int rank, int* err) {
+  pdl_wait();
   const int q = threadIdx.x;
   __threadfence_system();
   if (q < G) {
@@ -242,6 +247,7 @@ __global__ void ep_signal(EpSig* mine, const __grid_constant__ EpPeers P, int ph
 __global__ void ep_dispatch(const __half* __restrict__ xa, const int32_t* ids, const float* wts,
                             const int32_t* owner, const int* pos, int n_tok, int k, int Kx, int rank,
                             const __grid_constant__ EpDispatch D, int* err) {
+  pdl_wait();
   const int w = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   const int t = w / kEpSplit, part = w % kEpSplit;
   if (t < n_tok) {
@@ -487,7 +493,7 @@ int gguf_moe_ep_create(const gguf_moe_desc* desc, const int32_t* owner, int rank
       (st = cuda_status(cudaMalloc(&ep->xsrc, ep->rows_cap * 4))) ||
       (st = cuda_status(cudaMalloc(&ep->sig, sizeof(EpSig)))) ||
       (st = cuda_status(cudaMemset(ep->sig, 0, sizeof(EpSig)))) ||
-      (st = cuda_status(cudaMemset(ep->d_bar, 0, 16))) ||
+      (st = cuda_status(cudaMemset(ep->d_bar, 0, 16))) || (st = cuda_status(cudaMemset(ep->d_cnt, 0, ne * 4))) ||
       (st = cuda_status(cudaMemcpy(ep->d_owner, owner, ne * 4, cudaMemcpyHostToDevice))) ||
       (st = cuda_status(cudaMemcpy(ep->d_own, own.data(), ne * 4, cudaMemcpyHostToDevice)))) {
     gguf_moe_ep_destroy(ep);
@@ -591,16 +597,18 @@ int gguf_moe_prefill_ep(gguf_moe_ep* ep, const void* hb_bf16, float* x, int n_to
   // route the local tokens (only this rank's experts are packed)
   if (n_tok > 0 && (rc = prefill_route(L, S, hb_bf16, n_tok, router_bias, v.err, v.num_sms, s))) return rc;
   if (n_tok == 0 && (rc = prefill_prepare(L, S, s))) return rc;
-  if ((rc = cuda_status(cudaMemsetAsync(ep->d_cnt, 0, ne * 4, s)))) return rc;
-  if (pairs) ep_count<<<(unsigned)((pairs + 255) / 256), 256, 0, s>>>(S->ids, (int)pairs, ep->d_cnt, ep->d_pos);
+  if (pairs && (rc = pdl_launch(ep_count, dim3((unsigned)((pairs + 255) / 256)), dim3(256), 0, s, (const int32_t*)S->ids,
+                                (int)pairs, ep->d_cnt, ep->d_pos)))
+    return rc;
   // the [G][ne] count matrix on every rank, exchanged over peer memory, and
   // the row layout from it, on the device
   const unsigned int call = ++ep->call;
   EpPeers P;
   memset(&P, 0, sizeof(P));
   for (int q = 0; q < G; q++) P.sig[q] = ep->p_sig[q];
-  ep_exchange<<<1, kEpMaxExperts, 0, s>>>(ep->d_cnt, ep->sig, P, call, ep->d_owner, G, ne, r, prefill_tile_rows(),
-                                          ep->d_dstoff, ep->d_totals, v.err);
+  if ((rc = pdl_launch(ep_exchange, dim3(1), dim3(kEpMaxExperts), 0, s, ep->d_cnt, ep->sig, P, call,
+                       (const int32_t*)ep->d_owner, G, ne, r, prefill_tile_rows(), ep->d_dstoff, ep->d_totals, v.err)))
+    return rc;
   EpDispatch Dp;
   memset(&Dp, 0, sizeof(Dp));
   for (int q = 0; q < G; q++) {
@@ -623,16 +631,19 @@ int gguf_moe_prefill_ep(gguf_moe_ep* ep, const void* hb_bf16, float* x, int n_to
   if ((rc = prefill_grow_rows(L, S, rows))) return rc;
   // dispatch into the owners' operands (a token's row once per other owner),
   // then every rank's rows and receive buffer are in place
-  if (n_tok)
-    ep_dispatch<<<(unsigned)(((size_t)n_tok * kEpSplit + 7) / 8), 256, 0, s>>>(S->xa, S->ids, S->wts, ep->d_owner, ep->d_pos, n_tok,
-                                                             k, Kx, r, Dp, v.err);
-  ep_signal<<<1, 32, 0, s>>>(ep->sig, P, kSigDispatched, call, G, r, v.err);
+  if (n_tok && (rc = pdl_launch(ep_dispatch, dim3((unsigned)(((size_t)n_tok * kEpSplit + 7) / 8)), dim3(256), 0, s,
+                                (const __half*)S->xa, (const int32_t*)S->ids, (const float*)S->wts,
+                                (const int32_t*)ep->d_owner, (const int*)ep->d_pos, n_tok, k, Kx, r, Dp, v.err)))
+    return rc;
+  if ((rc = pdl_launch(ep_signal, dim3(1), dim3(32), 0, s, ep->sig, P, (int)kSigDispatched, call, G, r, v.err)))
+    return rc;
   // the experts held here (rows received once per token copied into each of
   // its rows); the down GEMM returns each row to its source rank
   prefill_scan_launch(ep->d_totals, ne, S, s);
   if (G > 1) prefill_expand_launch(S, rows, ep->xsrc, ep->xr, Kx, G * ep->max_tok, s);
   if ((rc = prefill_experts(L, S, rows, v.err, v.num_sms, s, ep->ysrc, ep->p_yret, G))) return rc;
-  ep_signal<<<1, 32, 0, s>>>(ep->sig, P, kSigReturned, call, G, r, v.err);
+  if ((rc = pdl_launch(ep_signal, dim3(1), dim3(32), 0, s, ep->sig, P, (int)kSigReturned, call, G, r, v.err)))
+    return rc;
   prefill_combine_launch(S->ids, ep->yret, x, n_tok, k, d, s);
   if (ids_out && pairs && cudaMemcpyAsync(ids_out, S->ids, pairs * 4, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
     return cuda_status(cudaGetLastError());

@@ -54,6 +54,7 @@
 
 #include "engine.cuh"
 #include "moe_decode.cuh"
+#include "pdl_launch.cuh"
 #include "umma.cuh"
 #include "vireo_internal.h"
 
@@ -261,6 +262,7 @@ template <int MODE>
 __global__ void __launch_bounds__(kPThreads, 1)
     prefill_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ PrefillParams p) {
+  pdl_wait();  // launched with programmatic serialization: the previous kernel is complete
   extern __shared__ __align__(1024) uint8_t praw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>(((uintptr_t)praw + 1023) & ~(uintptr_t)1023);
   using RG = PRing<MODE>;
@@ -752,8 +754,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
 
 // ---- prep: xa[t] = [f16 of the token's values, columns (0 2 1 3) per group
 // of 4 | f16 of the 32-value group sums | zero padding], Kx columns --------
-__global__ void prefill_prep(const __nv_bfloat16* hb, __half* xa, int T, int d, int Kx) {
+__global__ void prefill_prep(const __nv_bfloat16* hb, __half* xa, int T, int d, int Kx, int* counts) {
+  pdl_wait();
   const int t = blockIdx.x;
+  // the router's per-expert counts start at zero (in place of a memset, which
+  // would break the chain of dependent launches)
+  if (t == 0 && threadIdx.x < 256) counts[threadIdx.x] = 0;
   if (t >= T) return;
   const __nv_bfloat16* src = hb + (size_t)t * d;
   __half* dst = xa + (size_t)t * Kx;
@@ -878,6 +884,7 @@ __global__ void prefill_pack_dn(const uint8_t* const* exp_tab, const int* own, i
 
 // ---- scan: padded row ranges, the tile table, placement cursors ------------
 __global__ void prefill_scan(const int* counts, int ne, int* cursor, PTile* tiles, int* n_mtiles) {
+  pdl_wait();
   // ranges padded to kPM rows; tiles of up to 2 kPM rows (the expert GEMMs'
   // two sub-tiles), a range's last tile possibly one sub-tile
   constexpr int kT = 2 * kPM;
@@ -915,6 +922,7 @@ __global__ void prefill_scan(const int* counts, int ne, int* cursor, PTile* tile
 // row's return slot is the pair itself (rank 0) ---------------------------
 __global__ void prefill_place(const int32_t* ids, const float* wts, const __half* __restrict__ xa, int T, int k,
                               int Kx, int* cursor, int* ysrc, float* wrow, __half* __restrict__ xg) {
+  pdl_wait();
   const int pair = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (pair >= T * k) return;
   int pos = -1;
@@ -951,6 +959,7 @@ __global__ void prefill_place(const int32_t* ids, const float* wts, const __half
 // gridDim.y blocks per M tile, a warp per row.
 __global__ void prefill_expand(const PTile* tiles, const int* n_mtiles, const int* xsrc, const __half* __restrict__ xr,
                                __half* __restrict__ xg, int Kx, int n_slots) {
+  pdl_wait();
   if ((int)blockIdx.x >= *n_mtiles) return;
   const PTile t = tiles[blockIdx.x];
   const int lane = threadIdx.x & 31, n16 = Kx / 8;
@@ -975,7 +984,8 @@ __global__ void prefill_expand(const PTile* tiles, const int* n_mtiles, const in
 void prefill_expand_launch(const PrefillScratch* S, size_t rows, const int* xsrc, const __half* xr, int Kx,
                            int n_slots, cudaStream_t st) {
   rows = std::max<size_t>(rows, kPM);
-  prefill_expand<<<dim3((unsigned)(rows / kPM + 1), 8), 256, 0, st>>>(S->tiles, S->n_mtiles, xsrc, xr, S->xg, Kx, n_slots);
+  pdl_launch(prefill_expand, dim3((unsigned)(rows / kPM + 1), 8), dim3(256), 0, st, (const PTile*)S->tiles,
+             (const int*)S->n_mtiles, xsrc, xr, (__half*)S->xg, Kx, n_slots);
 }
 
 // ---- combine: x[t] += sum in slot order of the f16 rows yret[t * k + i]
@@ -983,6 +993,7 @@ void prefill_expand_launch(const PrefillScratch* S, size_t rows, const int* xsrc
 // then added to x), in fp32; eight columns per thread, the slots' loads
 // issued together.  A slot whose id is -1 has no row.
 __global__ void prefill_combine(const int32_t* ids, const __half* yret, float* x, int T, int k, int d) {
+  pdl_wait();
   const int t = blockIdx.x;
   if (t >= T) return;
   bool on[kPTopK];
@@ -1021,7 +1032,7 @@ __global__ void prefill_combine(const int32_t* ids, const __half* yret, float* x
 }
 
 void prefill_combine_launch(const int32_t* ids, const __half* yret, float* x, int T, int k, int d, cudaStream_t st) {
-  if (T > 0) prefill_combine<<<T, 256, 0, st>>>(ids, yret, x, T, k, d);
+  if (T > 0) pdl_launch(prefill_combine, dim3(T), dim3(256), 0, st, ids, yret, x, T, k, d);
 }
 
 // ---------------------------------------------------------------------------
@@ -1162,13 +1173,15 @@ int prefill_route(const PrefillLayer& L, PrefillScratch* S, const void* hb, int 
   set_attrs_once();
   PrefillParams p = base_params(L, S, T, d_err);
   p.bias = bias;
-  if (cudaMemsetAsync(S->counts, 0, 256 * 4, st) != cudaSuccess) return cuda_status(cudaGetLastError());
-  prefill_prep<<<T, 256, 0, st>>>((const __nv_bfloat16*)hb, (__half*)S->xa, T, d, Kx);
+  if ((rc = pdl_launch(prefill_prep, dim3(T), dim3(256), 0, st, (const __nv_bfloat16*)hb, (__half*)S->xa, T, d, Kx,
+                       (int*)S->counts)))
+    return rc;
   p.nk = d / kPK;
   // idle SMs repeat a row tile's GEMM so that its top-k is split 2 or 4 ways
   const int tiles = (T + kPM - 1) / kPM;
   p.n_ntiles = tiles * 4 <= num_sms ? 4 : tiles * 2 <= num_sms ? 2 : 1;
-  prefill_gemm<P_ROUTER><<<std::min(num_sms, tiles * p.n_ntiles), kPThreads, psmem<P_ROUTER>(), st>>>(mA_r, mB_r, p);
+  return pdl_launch(prefill_gemm<P_ROUTER>, dim3(std::min(num_sms, tiles * p.n_ntiles)), dim3(kPThreads),
+                    psmem<P_ROUTER>(), st, mA_r, mB_r, p);
   return cuda_status(cudaGetLastError());
 }
 
@@ -1189,7 +1202,7 @@ int prefill_grow_rows(const PrefillLayer& L, PrefillScratch* S, size_t rows) {
 }
 
 void prefill_scan_launch(const int* counts, int ne, PrefillScratch* S, cudaStream_t st) {
-  prefill_scan<<<1, 256, 0, st>>>(counts, ne, S->cursor, S->tiles, S->n_mtiles);
+  pdl_launch(prefill_scan, dim3(1), dim3(256), 0, st, counts, ne, (int*)S->cursor, (PTile*)S->tiles, (int*)S->n_mtiles);
 }
 
 int prefill_experts(const PrefillLayer& L, PrefillScratch* S, size_t rows, int* d_err, int num_sms, cudaStream_t st,
@@ -1208,7 +1221,8 @@ int prefill_experts(const PrefillLayer& L, PrefillScratch* S, size_t rows, int* 
   p.nk = Kx / kPK;
   p.n_ntiles = fe / 128;
   p.pack = S->gu_pack;
-  prefill_gemm<P_GATEUP><<<num_sms, kPThreads, psmem<P_GATEUP>(), st>>>(mA_gu, mM, p);
+  if ((rc = pdl_launch(prefill_gemm<P_GATEUP>, dim3(num_sms), dim3(kPThreads), psmem<P_GATEUP>(), st, mA_gu, mM, p)))
+    return rc;
   // down, scaled by the routing weight
   p.nk = fe / kPK;
   p.n_ntiles = d / kPN;
@@ -1216,7 +1230,8 @@ int prefill_experts(const PrefillLayer& L, PrefillScratch* S, size_t rows, int* 
   p.ysrc = ysrc;
   for (int i = 0; i < npeers; i++) p.ypeer[i] = ypeer[i];
   p.remote = npeers > 1;
-  prefill_gemm<P_DOWN><<<num_sms, kPThreads, psmem<P_DOWN>(), st>>>(mA_d, mA_d, p);
+  if ((rc = pdl_launch(prefill_gemm<P_DOWN>, dim3(num_sms), dim3(kPThreads), psmem<P_DOWN>(), st, mA_d, mA_d, p)))
+    return rc;
   return cuda_status(cudaGetLastError());
 }
 
@@ -1231,8 +1246,10 @@ int prefill_run(const PrefillLayer& L, PrefillScratch* S, const void* hb, float*
       (rc = prefill_grow_rows(L, S, rows)))
     return rc;
   prefill_scan_launch(S->counts, ne, S, st);
-  prefill_place<<<(unsigned)((pairs + 7) / 8), 256, 0, st>>>(S->ids, S->wts, (const __half*)S->xa, T, k, Kx,
-                                                              S->cursor, S->ysrc, S->wrow, (__half*)S->xg);
+  if ((rc = pdl_launch(prefill_place, dim3((unsigned)((pairs + 7) / 8)), dim3(256), 0, st, (const int32_t*)S->ids,
+                       (const float*)S->wts, (const __half*)S->xa, T, k, Kx, (int*)S->cursor, (int*)S->ysrc,
+                       (float*)S->wrow, (__half*)S->xg)))
+    return rc;
   __half* const self[1] = {S->yret};
   if ((rc = prefill_experts(L, S, rows, d_err, num_sms, st, S->ysrc, self, 1))) return rc;
   prefill_combine_launch(S->ids, S->yret, x, T, k, d, st);
