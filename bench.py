@@ -535,10 +535,13 @@ def run_prefill(args, wl):
         uid = [V.ep_unique_id() if rank == 0 else None]
         torch.distributed.broadcast_object_list(uid, src=0)
         ep = V.MoeLayerEP(layer, owner, rank, world, uid[0], Tl, local)
-        fn, handle, sync, launches = L.gguf_moe_prefill_ep, ep.h, L.gguf_moe_ep_sync, 9
+        # prep, router, count, exchange, dispatch, barrier, scan, expand,
+        # gate/up, down, barrier, combine
+        fn, handle, sync, launches = L.gguf_moe_prefill_ep, ep.h, L.gguf_moe_ep_sync, 12
         what = "gguf_moe_prefill_ep"
     else:
         m = V.MoeLayer(layer, local)
+        # prep, router, scan, place, gate/up, down, combine
         fn, handle, sync, launches = L.gguf_moe_prefill, m.h, L.gguf_moe_sync, 7
         what = "gguf_moe_prefill"
 
