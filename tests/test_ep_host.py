@@ -4,10 +4,13 @@ expert-parallel dataflow of gguf_moe_prefill_ep run end to end as two gloo
 ranks on CPU with the CPU oracle as the expert math.
 
 The dataflow test follows the device path step by step: each rank routes its
-own tokens and counts pairs per expert, the counts are all-gathered, every
-(token, slot) row goes to the row gguf_moe_ep_rows assigns it in its expert's
-range on the owning rank (gloo stands in for the peer stores), the owner
-finds each row's expert from that layout alone and computes w * expert(x),
+own tokens and counts pairs per expert, the counts are all-gathered, a
+token's hidden row goes once to each other rank holding one of its experts
+(its receive buffer) and each (token, slot) pair's metadata to the row
+gguf_moe_ep_rows assigns it in its expert's range on the owning rank (gloo
+stands in for the peer stores), the owner fills each row from its own tokens
+or its receive buffer, finds each row's expert from the layout alone and
+computes w * expert(x),
 the rows return to (source rank, pair), and each token is combined in rank
 order.  The result must equal the single-process restatement of the
 reference's moe_ffn bit for bit (same float32 operations in the same order).
@@ -122,23 +125,55 @@ def _ep_rank(rank, world, port, seed, n_tok, out_dir):
         dist.all_gather(allc, torch.from_numpy(cnt))
         counts = torch.stack(allc).numpy()
         off, here = V.ep_rows(counts, owner, rank)
-        # dispatch: each pair's row goes to row off[e] + pos of its expert's
-        # owner (the peer stores of the device path, carried here by gloo)
+        # dispatch (the peer stores of the device path, carried here by gloo):
+        # a token's hidden row goes ONCE to each other rank holding one of its
+        # experts, into that rank's receive buffer at slot rank * max_tok + t;
+        # each pair's metadata (its row off[e] + pos on the owner, weight,
+        # pair, expert, receive slot or -1 when this rank placed the row
+        # itself) goes to the pair's owner
+        max_tok = n_tok
         dest = owner[flat]
+        tok_dest = sorted({(int(q), p // k) for p, q in enumerate(dest) if q != rank})
+        # tokens with several experts on one peer send their row once: fewer
+        # rows than remote pairs
+        assert len(tok_dest) < int((dest != rank).sum())
+        tsend = np.zeros((len(tok_dest), d + 1), dtype=np.float32)  # [hidden | receive slot]
+        for j, (q, t) in enumerate(tok_dest):
+            tsend[j, :d] = mine[t]
+            tsend[j, d] = rank * max_tok + t
+        tsendcnt = np.bincount(np.array([q for q, _ in tok_dest], dtype=np.int64), minlength=world)
+        tall = [torch.zeros(world, dtype=torch.int64) for _ in range(world)]
+        dist.all_gather(tall, torch.from_numpy(tsendcnt.astype(np.int64)))
+        trecvcnt = np.array([int(tall[q][rank]) for q in range(world)])
+        trecv = torch.zeros((int(trecvcnt.sum()), d + 1), dtype=torch.float32)
+        dist.all_to_all_single(trecv, torch.from_numpy(tsend), [int(c) for c in trecvcnt], [int(c) for c in tsendcnt])
+        xr = {}
+        for row in trecv.numpy():
+            slot = int(row[d])
+            assert slot not in xr  # one row per (source rank, token)
+            xr[slot] = row[:d]
         sendcnt = np.bincount(dest, minlength=world)
         recvcnt = np.array([counts[q][owner == rank].sum() for q in range(world)])
         order = np.argsort(dest, kind="stable")
-        send = np.zeros((T * k, d + 4), dtype=np.float32)  # [hidden | dest row | weight | pair | expert]
+        send = np.zeros((T * k, 5), dtype=np.float32)  # [dest row | weight | pair | expert | receive slot]
         for j, p in enumerate(order):
-            send[j, :d] = mine[p // k]
-            send[j, d] = off[flat[p]] + pos[p]
-            send[j, d + 1] = wts.reshape(-1)[p]
-            send[j, d + 2] = p
-            send[j, d + 3] = flat[p]
-        recv = torch.zeros((int(recvcnt.sum()), d + 4), dtype=torch.float32)
-        dist.all_to_all_single(recv, torch.from_numpy(send), [int(c) for c in recvcnt], [int(c) for c in sendcnt])
-        recv = recv.numpy()
-        # the owner's operand rows: every received row lands on its own row
+            send[j, 0] = off[flat[p]] + pos[p]
+            send[j, 1] = wts.reshape(-1)[p]
+            send[j, 2] = p
+            send[j, 3] = flat[p]
+            send[j, 4] = -1 if dest[p] == rank else rank * max_tok + p // k
+        meta = torch.zeros((int(recvcnt.sum()), 5), dtype=torch.float32)
+        dist.all_to_all_single(meta, torch.from_numpy(send), [int(c) for c in recvcnt], [int(c) for c in sendcnt])
+        meta = meta.numpy()
+        # the owner's operand rows: rows placed by this rank come from its own
+        # tokens, the others from the receive buffer (prefill_expand)
+        recv = np.zeros((len(meta), d + 4), dtype=np.float32)  # [hidden | dest row | weight | pair | expert]
+        recv[:, d:] = meta[:, :4]
+        src = np.repeat(np.arange(world), recvcnt)
+        for i in range(len(meta)):
+            slot = int(meta[i, 4])
+            assert (slot < 0) == (src[i] == rank)  # only the owner's own pairs skip the receive buffer
+            recv[i, :d] = mine[int(meta[i, 2]) // k] if slot < 0 else xr[slot]
         rows = np.full((max(int(recv[:, d].max()) + 1 if len(recv) else 0, 1),), -1, dtype=np.int64)
         for i in range(len(recv)):
             assert rows[int(recv[i, d])] == -1  # no two pairs share a row
