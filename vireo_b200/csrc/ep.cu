@@ -311,7 +311,6 @@ struct gguf_moe_ep {
   int32_t* d_owner = nullptr;
   int* d_own = nullptr;
   int* d_cnt = nullptr;     // [ne] local pairs per expert
-  int* d_cntall = nullptr;  // [G][ne]
   int* d_totals = nullptr;  // [ne]
   int* d_dstoff = nullptr;  // [ne]
   int* d_pos = nullptr;     // [max_tok * k]
@@ -482,7 +481,6 @@ int gguf_moe_ep_create(const gguf_moe_desc* desc, const int32_t* owner, int rank
   ep->rows_cap = prefill_row_capacity(pairs_cap * world, ne);
   if ((st = cuda_status(cudaMalloc(&ep->d_owner, ne * 4))) || (st = cuda_status(cudaMalloc(&ep->d_own, ne * 4))) ||
       (st = cuda_status(cudaMalloc(&ep->d_cnt, ne * 4))) ||
-      (st = cuda_status(cudaMalloc(&ep->d_cntall, (size_t)world * ne * 4))) ||
       (st = cuda_status(cudaMalloc(&ep->d_totals, ne * 4))) || (st = cuda_status(cudaMalloc(&ep->d_dstoff, ne * 4))) ||
       (st = cuda_status(cudaMalloc(&ep->d_pos, pairs_cap * 4))) || (st = cuda_status(cudaMalloc(&ep->d_bar, 16))) ||
       (st = cuda_status(cudaMalloc(&ep->xg, ep->rows_cap * Kx * 2))) ||
@@ -692,7 +690,7 @@ void gguf_moe_ep_destroy(gguf_moe_ep* ep) {
     }
     gguf_moe_destroy(ep->m);
   }
-  for (void* p : {(void*)ep->d_owner, (void*)ep->d_own, (void*)ep->d_cnt, (void*)ep->d_cntall, (void*)ep->d_totals, (void*)ep->d_dstoff,
+  for (void* p : {(void*)ep->d_owner, (void*)ep->d_own, (void*)ep->d_cnt, (void*)ep->d_totals, (void*)ep->d_dstoff,
                   (void*)ep->d_pos, (void*)ep->d_bar, (void*)ep->xg, (void*)ep->wrow, (void*)ep->ysrc,
                   (void*)ep->yret, (void*)ep->sig, (void*)ep->xr, (void*)ep->xsrc})
     if (p) cudaFree(p);
